@@ -1,0 +1,220 @@
+// comm.cpp -- several GPUs: each rank holds a leading-dimension shard; the
+// element-wise part needs no communication and the full sum combines per-rank
+// f64 partials with one NCCL all-reduce over NVLink.
+//
+// NCCL is loaded at run time (dlopen of libnccl.so.2), so a process that never
+// creates a communicator does not need it, and a process that already loaded
+// NCCL (e.g. through PyTorch) shares that copy.  Communicators are created
+// non-blocking and polled against a deadline; a rank that never joins makes
+// the others return TRS_ERR_TIMEOUT instead of hanging.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <chrono>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+
+#include "../../include/trs.h"
+#include "launch.h"
+#include "runtime.h"
+
+using namespace trs;
+
+struct trs_comm {
+  ncclComm_t comm = nullptr;
+  int nranks = 0;
+  int rank = 0;
+  int timeout_ms = 0;
+};
+
+namespace {
+
+struct Nccl {
+  bool loaded = false;
+  std::string why;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+Nccl& nccl() {
+  static Nccl n;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      const char* e = dlerror();
+      n.why = std::string("cannot load libnccl.so.2: ") + (e ? e : "");
+      return;
+    }
+#define TRS_SYM(field, name)                                              \
+  n.field = reinterpret_cast<decltype(n.field)>(dlsym(h, name));          \
+  if (!n.field) { n.why = std::string("missing NCCL symbol ") + name; return; }
+    TRS_SYM(GetUniqueId, "ncclGetUniqueId");
+    TRS_SYM(CommInitRankConfig, "ncclCommInitRankConfig");
+    TRS_SYM(CommGetAsyncError, "ncclCommGetAsyncError");
+    TRS_SYM(CommAbort, "ncclCommAbort");
+    TRS_SYM(CommDestroy, "ncclCommDestroy");
+    TRS_SYM(AllReduce, "ncclAllReduce");
+    TRS_SYM(GetErrorString, "ncclGetErrorString");
+#undef TRS_SYM
+    n.loaded = true;
+  });
+  return n;
+}
+
+trs_status finish(const Error& e) {
+  if (!e.ok()) set_last_error(e.msg);
+  return e.status;
+}
+
+Error nccl_error(ncclResult_t r, const char* what) {
+  Nccl& n = nccl();
+  return make_error(TRS_ERR_NCCL, std::string(what) + ": " +
+                                      (n.GetErrorString ? n.GetErrorString(r) : "nccl error"));
+}
+
+// Waits until a non-blocking communicator leaves ncclInProgress.
+Error wait_ready(trs_comm* c, const char* what) {
+  Nccl& n = nccl();
+  const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(c->timeout_ms);
+  for (;;) {
+    ncclResult_t st = ncclSuccess;
+    ncclResult_t r = n.CommGetAsyncError(c->comm, &st);
+    if (r != ncclSuccess) return nccl_error(r, "ncclCommGetAsyncError");
+    if (st == ncclSuccess) return Error{};
+    if (st != ncclInProgress) return nccl_error(st, what);
+    if (std::chrono::steady_clock::now() > deadline)
+      return make_error(TRS_ERR_TIMEOUT, std::string(what) + ": timed out");
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+  }
+}
+
+ncclDataType_t acc_type(int dtype) {
+  switch (dtype) {
+    case TRS_I32: return ncclUint32;
+    case TRS_I64: return ncclUint64;
+    default: return ncclFloat64;
+  }
+}
+
+Error sharded_sum(trs_comm* c, const trs_ew_program& prog, const trs_view* in, const trs_view* out,
+                  trs_view* sum_out, cudaStream_t stream) {
+  if (!c || !c->comm) return make_error(TRS_ERR_ARG, "null communicator");
+  Error e = validate_view(sum_out, "sum output");
+  if (!e.ok()) return e;
+  if (numel_of(sum_out->shape, sum_out->ndim) != 1) return make_error(TRS_ERR_SHAPE, "sum output must hold one element");
+  Scratch acc;
+  e = acc.alloc(8, stream);
+  if (!e.ok()) return e;
+  SumTarget t;
+  t.raw_acc = acc.get();
+  e = run_elementwise(prog, in, out, &t, stream);
+  if (!e.ok()) return e;
+  Nccl& n = nccl();
+  ncclResult_t r = n.AllReduce(acc.get(), acc.get(), 1, acc_type(in[0].dtype), ncclSum, c->comm, stream);
+  if (r == ncclInProgress) {
+    e = wait_ready(c, "ncclAllReduce");
+    if (!e.ok()) return e;
+  } else if (r != ncclSuccess) {
+    return nccl_error(r, "ncclAllReduce");
+  }
+  return run_acc_to_value(in[0].dtype, acc.get(), sum_out, stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+trs_status trs_comm_unique_id(uint8_t id[128]) {
+  Nccl& n = nccl();
+  if (!n.loaded) return finish(make_error(TRS_ERR_UNAVAILABLE, n.why));
+  ncclUniqueId u;
+  ncclResult_t r = n.GetUniqueId(&u);
+  if (r != ncclSuccess) return finish(nccl_error(r, "ncclGetUniqueId"));
+  static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId is 128 bytes");
+  std::memcpy(id, &u, 128);
+  return TRS_OK;
+}
+
+trs_status trs_comm_init_rank(const uint8_t id[128], int32_t nranks, int32_t rank, int32_t timeout_ms,
+                              trs_comm** comm) {
+  if (!id || !comm || nranks < 1 || rank < 0 || rank >= nranks || timeout_ms <= 0)
+    return finish(make_error(TRS_ERR_ARG, "bad communicator arguments"));
+  Nccl& n = nccl();
+  if (!n.loaded) return finish(make_error(TRS_ERR_UNAVAILABLE, n.why));
+  ncclUniqueId u;
+  std::memcpy(&u, id, 128);
+  trs_comm* c = new trs_comm;
+  c->nranks = nranks;
+  c->rank = rank;
+  c->timeout_ms = timeout_ms;
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  ncclResult_t r = n.CommInitRankConfig(&c->comm, nranks, u, rank, &cfg);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    delete c;
+    return finish(nccl_error(r, "ncclCommInitRankConfig"));
+  }
+  Error e = wait_ready(c, "ncclCommInitRankConfig");
+  if (!e.ok()) {
+    n.CommAbort(c->comm);
+    delete c;
+    return finish(e);
+  }
+  *comm = c;
+  return TRS_OK;
+}
+
+trs_status trs_comm_destroy(trs_comm* comm) {
+  if (!comm) return TRS_OK;
+  Nccl& n = nccl();
+  ncclResult_t r = n.CommDestroy(comm->comm);
+  delete comm;
+  if (r != ncclSuccess && r != ncclInProgress) return finish(nccl_error(r, "ncclCommDestroy"));
+  return TRS_OK;
+}
+
+trs_status trs_comm_abort(trs_comm* comm) {
+  if (!comm) return TRS_OK;
+  Nccl& n = nccl();
+  ncclResult_t r = n.CommAbort(comm->comm);
+  delete comm;
+  if (r != ncclSuccess) return finish(nccl_error(r, "ncclCommAbort"));
+  return TRS_OK;
+}
+
+trs_status trs_sharded_sum(trs_comm* comm, const trs_view* shard, trs_view* out, trs_stream stream) {
+  if (!shard || !out) return finish(make_error(TRS_ERR_ARG, "null view"));
+  trs_ew_program p;
+  std::memset(&p, 0, sizeof(p));
+  p.n_in = 1;
+  return finish(sharded_sum(comm, p, shard, nullptr, out, static_cast<cudaStream_t>(stream)));
+}
+
+trs_status trs_sharded_elementwise_sum(trs_comm* comm, const trs_ew_program* prog, const trs_view* in,
+                                       trs_view* out, trs_view* sum_out, trs_stream stream) {
+  if (!prog || !in || !sum_out) return finish(make_error(TRS_ERR_ARG, "null argument"));
+  return finish(sharded_sum(comm, *prog, in, out, sum_out, static_cast<cudaStream_t>(stream)));
+}
+
+trs_status trs_sharded_sum_axis0(trs_comm*, const trs_view*, trs_view*, trs_stream) {
+  return finish(make_error(TRS_ERR_UNAVAILABLE, "trs_sharded_sum_axis0 is not built yet"));
+}
+trs_status trs_sharded_max_axis0(trs_comm*, const trs_view*, trs_view*, trs_stream) {
+  return finish(make_error(TRS_ERR_UNAVAILABLE, "trs_sharded_max_axis0 is not built yet"));
+}
+trs_status trs_sharded_argmax_axis0(trs_comm*, const trs_view*, trs_view*, trs_stream) {
+  return finish(make_error(TRS_ERR_UNAVAILABLE, "trs_sharded_argmax_axis0 is not built yet"));
+}
+
+}  // extern "C"

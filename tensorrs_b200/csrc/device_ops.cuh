@@ -1,0 +1,276 @@
+// device_ops.cuh -- element arithmetic with the reference's rounding.
+//
+// Every f32/f64 operation goes through an explicitly rounded intrinsic
+// (__fadd_rn, __fmul_rn, __fdiv_rn, ... ), which the compiler never fuses
+// into an FMA, so each step rounds exactly once as the reference's separate
+// Rust operations do.  The library is also built with -fmad=false.
+//
+// Transcendentals are out-of-line calls so the unrolled element-wise kernels
+// carry one copy of each (pow_e_inline is the inlined form for the softmax
+// kernel, where it is the whole inner loop).
+//
+// Transcendentals: the reference calls glibc (expf, tanhf, powf, logf and the
+// f64 forms).  For f32 the kernels evaluate the function in f64 with CUDA's
+// double-precision math library and round once to f32, which lands within one
+// ulp of a correctly rounded result; glibc's f32 functions are themselves
+// within about one ulp, so the two agree to a couple of ulp at most (measured
+// by the parity tests).  For f64 the kernels call CUDA's f64 functions.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/trs.h"
+
+namespace trs {
+
+template <class T> struct Arith;
+
+template <> struct Arith<float> {
+  using Acc = double;  // accumulator type of sums
+  static __device__ __forceinline__ float add(float a, float b) { return __fadd_rn(a, b); }
+  static __device__ __forceinline__ float sub(float a, float b) { return __fsub_rn(a, b); }
+  static __device__ __forceinline__ float mul(float a, float b) { return __fmul_rn(a, b); }
+  static __device__ __forceinline__ float div(float a, float b, int*) { return __fdiv_rn(a, b); }
+  static __device__ __forceinline__ float neg(float a) { return -a; }
+  static __device__ __forceinline__ float abs(float a) { return fabsf(a); }
+  static __device__ __noinline__ float pow(float a, float b) {
+    return (float)::pow((double)a, (double)b);
+  }
+  // powf(E_f32, x) as exp(x * ln(E_f32)) in f64; `ln_e` is ln of the f32 E.
+  static __device__ __forceinline__ float pow_e_inline(float x, double ln_e) {
+    return (float)::exp(__dmul_rn((double)x, ln_e));
+  }
+  static __device__ __noinline__ float pow_e(float x, double ln_e) { return pow_e_inline(x, ln_e); }
+  static __device__ __noinline__ float exp(float a) { return (float)::exp((double)a); }
+  static __device__ __noinline__ float tanh(float a) { return (float)::tanh((double)a); }
+  static __device__ __noinline__ float ln(float a) { return (float)::log((double)a); }
+  static __device__ __forceinline__ float from(const trs_scalar& s) { return (float)s.f; }
+  static __device__ __forceinline__ double to_acc(float a) { return (double)a; }
+  static __device__ __forceinline__ float from_acc(double a) { return (float)a; }
+};
+
+template <> struct Arith<double> {
+  using Acc = double;
+  static __device__ __forceinline__ double add(double a, double b) { return __dadd_rn(a, b); }
+  static __device__ __forceinline__ double sub(double a, double b) { return __dsub_rn(a, b); }
+  static __device__ __forceinline__ double mul(double a, double b) { return __dmul_rn(a, b); }
+  static __device__ __forceinline__ double div(double a, double b, int*) { return __ddiv_rn(a, b); }
+  static __device__ __forceinline__ double neg(double a) { return -a; }
+  static __device__ __forceinline__ double abs(double a) { return fabs(a); }
+  static __device__ __noinline__ double pow(double a, double b) { return ::pow(a, b); }
+  // powf(E_f64, x): f64 has no wider type to hide the rounding of x*ln(E),
+  // so this calls pow with the f64 E itself.
+  static __device__ __forceinline__ double pow_e_inline(double x, double e) { return ::pow(e, x); }
+  static __device__ __noinline__ double pow_e(double x, double e) { return pow_e_inline(x, e); }
+  static __device__ __noinline__ double exp(double a) { return ::exp(a); }
+  static __device__ __noinline__ double tanh(double a) { return ::tanh(a); }
+  static __device__ __noinline__ double ln(double a) { return ::log(a); }
+  static __device__ __forceinline__ double from(const trs_scalar& s) { return s.f; }
+  static __device__ __forceinline__ double to_acc(double a) { return a; }
+  static __device__ __forceinline__ double from_acc(double a) { return a; }
+};
+
+// Integers: add/sub/mul wrap (the reference's release build); division by
+// zero and MIN / -1 set a flag the host turns into TRS_ERR_DIV_ZERO (the
+// reference panics on both) and produce 0.
+template <class I, class U>
+struct IntArith {
+  using Acc = U;  // sums wrap; unsigned keeps the wrap well defined
+  static __device__ __forceinline__ I add(I a, I b) { return (I)((U)a + (U)b); }
+  static __device__ __forceinline__ I sub(I a, I b) { return (I)((U)a - (U)b); }
+  static __device__ __forceinline__ I mul(I a, I b) { return (I)((U)a * (U)b); }
+  static __device__ __forceinline__ I div(I a, I b, int* flag) {
+    if (b == 0) { if (flag) atomicOr(flag, 1); return 0; }
+    if (b == (I)-1 && a == (I)((U)1 << (sizeof(I) * 8 - 1))) { if (flag) atomicOr(flag, 2); return 0; }
+    return a / b;
+  }
+  static __device__ __forceinline__ I neg(I a) { return (I)((U)0 - (U)a); }
+  static __device__ __forceinline__ I abs(I a) { return a < 0 ? neg(a) : a; }
+  static __device__ __forceinline__ I pow(I, I) { return 0; }
+  static __device__ __forceinline__ I pow_e(I, double) { return 0; }
+  static __device__ __forceinline__ I pow_e_inline(I, double) { return 0; }
+  static __device__ __forceinline__ I exp(I) { return 0; }
+  static __device__ __forceinline__ I tanh(I) { return 0; }
+  static __device__ __forceinline__ I ln(I) { return 0; }
+  static __device__ __forceinline__ I from(const trs_scalar& s) { return (I)s.i; }
+  static __device__ __forceinline__ U to_acc(I a) { return (U)a; }
+  static __device__ __forceinline__ I from_acc(U a) { return (I)a; }
+};
+template <> struct Arith<int32_t> : IntArith<int32_t, uint32_t> {};
+template <> struct Arith<int64_t> : IntArith<int64_t, uint64_t> {};
+
+template <class T> struct IsFloat { static constexpr bool value = false; };
+template <> struct IsFloat<float> { static constexpr bool value = true; };
+template <> struct IsFloat<double> { static constexpr bool value = true; };
+
+// Parameters every element-wise kernel needs beyond its operands.
+struct EwParams {
+  int n_in;
+  int op1, op2, epi;
+  trs_scalar p0, p1;
+  double e_const;  // ln(E_f32) for f32, E_f64 for f64 (see Arith::pow_e)
+  int* div_flag;
+};
+
+template <class T>
+__device__ __forceinline__ T apply_binop(int op, T a, T b, int* flag) {
+  using A = Arith<T>;
+  switch (op) {
+    case TRS_ADD: return A::add(a, b);
+    case TRS_SUB: return A::sub(a, b);
+    case TRS_MUL: return A::mul(a, b);
+    case TRS_DIV: return A::div(a, b, flag);
+    default: return A::pow(a, b);
+  }
+}
+
+// The unary maps of trs_unop, each in the order of operations of the
+// reference code cited in include/trs.h.
+template <class T>
+__device__ __forceinline__ T apply_unop(const EwParams& p, T v) {
+  using A = Arith<T>;
+  const T one = T(1), zero = T(0);
+  switch (p.epi) {
+    case TRS_UN_NONE: return v;
+    case TRS_UN_NEG: return A::neg(v);
+    case TRS_UN_RELU: {  // x & map(x > 0 ? 1 : 0)
+      return A::mul(v, v > zero ? one : zero);
+    }
+    case TRS_UN_SIGMOID: {  // autodiff/ops.rs:586-593
+      if (v >= zero) return A::div(one, A::add(one, A::exp(A::neg(v))), nullptr);
+      T e = A::exp(v);
+      return A::div(e, A::add(one, e), nullptr);
+    }
+    case TRS_UN_TANH: return A::tanh(v);
+    case TRS_UN_ELU: {  // elu.rs:47-63
+      T pos = A::mul(v, v > zero ? one : zero);
+      T ex = A::pow_e(v, p.e_const);
+      T neg = A::mul(A::mul(A::sub(ex, one), A::from(p.p0)), v <= zero ? one : zero);
+      return A::add(pos, neg);
+    }
+    case TRS_UN_LEAKY_RELU: {  // leaky_relu.rs:39-52
+      T pos = A::mul(v, v > zero ? one : zero);
+      T neg = A::mul(A::mul(v, A::from(p.p0)), v <= zero ? one : zero);
+      return A::add(pos, neg);
+    }
+    case TRS_UN_SELU: {  // selu.rs:52-70; p0 = alpha, p1 = lambda
+      T lambda = A::from(p.p1), alpha = A::from(p.p0);
+      T pos = A::mul(A::mul(v, lambda), v > zero ? one : zero);
+      T ex = A::pow_e(v, p.e_const);
+      T scale = A::mul(lambda, alpha);
+      T neg = A::mul(A::mul(A::sub(ex, one), scale), v <= zero ? one : zero);
+      return A::add(pos, neg);
+    }
+    case TRS_UN_EXP: return A::pow_e(v, p.e_const);
+    case TRS_UN_LN: return A::ln(v);
+    case TRS_UN_ABS: return A::abs(v);
+    case TRS_UN_SIGN: return v > zero ? one : (v == zero ? zero : A::neg(one));
+    case TRS_UN_CLAMP: {
+      T lo = A::from(p.p0), hi = A::from(p.p1);
+      return v < lo ? lo : (v > hi ? hi : v);
+    }
+    case TRS_UN_ADD_SCALAR: return A::add(v, A::from(p.p0));
+    case TRS_UN_SUB_SCALAR: return A::sub(v, A::from(p.p0));
+    case TRS_UN_RSUB_SCALAR: return A::sub(A::from(p.p0), v);
+    case TRS_UN_MUL_SCALAR: return A::mul(v, A::from(p.p0));
+    case TRS_UN_DIV_SCALAR: return A::div(v, A::from(p.p0), p.div_flag);
+    case TRS_UN_POW_SCALAR: return A::pow(v, A::from(p.p0));
+    case TRS_UN_RPOW_SCALAR: return A::pow(A::from(p.p0), v);
+  }
+  return v;
+}
+
+// The whole fused program on one element.
+template <class T>
+__device__ __forceinline__ T apply_program(const EwParams& p, T a, T b, T c) {
+  T v = a;
+  if (p.n_in >= 2) v = apply_binop<T>(p.op1, v, b, p.div_flag);
+  if (p.n_in >= 3) v = apply_binop<T>(p.op2, v, c, p.div_flag);
+  return apply_unop<T>(p, v);
+}
+
+// ---- reductions ------------------------------------------------------------
+
+// Sum of one f64 (or wrapping integer) value per thread over a block whose
+// size is a multiple of 32; the result is valid in thread 0.  The order of the
+// additions is fixed, so the result is deterministic.
+template <class Acc>
+__device__ __forceinline__ Acc block_sum(Acc v, Acc* smem /* >= 32 */) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int o = 16; o > 0; o >>= 1) v = v + __shfl_down_sync(0xffffffffu, v, o);
+  __syncthreads();  // smem may be reused from a previous call
+  if (lane == 0) smem[warp] = v;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  if (warp == 0) {
+    v = lane < nw ? smem[lane] : Acc(0);
+    for (int o = 16; o > 0; o >>= 1) v = v + __shfl_down_sync(0xffffffffu, v, o);
+  }
+  return v;
+}
+
+// Running maximum with the reference's semantics (max_axis, base.rs:1404-1411;
+// argmax_axis, base.rs:1467-1478): strict `>` from the first element, so a NaN
+// never replaces a value and ties keep the lowest index.  A partial state
+// covers a subset of the axis: `idx` < 0 means it holds no candidate yet.
+// NaNs are skipped here; a NaN at index 0 (which the reference keeps) is
+// applied by the caller after the reduction.
+template <class T>
+struct MaxState {
+  T val;
+  int64_t idx;
+};
+
+template <class T>
+__device__ __forceinline__ bool is_nan_val(T v) { return v != v; }
+
+template <class T>
+__device__ __forceinline__ void max_push(MaxState<T>& s, T v, int64_t k) {
+  if (is_nan_val(v)) return;
+  if (s.idx < 0 || v > s.val) { s.val = v; s.idx = k; }
+}
+
+// Combine two partial states; ties go to the lower index.
+template <class T>
+__device__ __forceinline__ MaxState<T> max_combine(MaxState<T> a, MaxState<T> b) {
+  if (a.idx < 0) return b;
+  if (b.idx < 0) return a;
+  if (b.val > a.val) return b;
+  if (a.val > b.val) return a;
+  return b.idx < a.idx ? b : a;
+}
+
+template <class T>
+__device__ __forceinline__ MaxState<T> shfl_down_max(MaxState<T> s, int o) {
+  MaxState<T> r;
+  r.val = __shfl_down_sync(0xffffffffu, s.val, o);
+  r.idx = __shfl_down_sync(0xffffffffu, s.idx, o);
+  return r;
+}
+
+template <class T>
+__device__ __forceinline__ MaxState<T> warp_max(MaxState<T> s) {
+  for (int o = 16; o > 0; o >>= 1) s = max_combine(s, shfl_down_max(s, o));
+  return s;
+}
+
+template <class T>
+__device__ __forceinline__ MaxState<T> block_max(MaxState<T> s, MaxState<T>* smem) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  s = warp_max(s);
+  __syncthreads();
+  if (lane == 0) smem[warp] = s;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  if (warp == 0) {
+    MaxState<T> e;
+    e.val = T(0);
+    e.idx = -1;
+    s = lane < nw ? smem[lane] : e;
+    s = warp_max(s);
+  }
+  return s;
+}
+
+}  // namespace trs

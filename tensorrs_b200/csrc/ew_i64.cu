@@ -1,0 +1,7 @@
+// ew_i64.cu -- element-wise kernels instantiated for int64_t.
+#include "ew_kernels.cuh"
+
+namespace trs {
+template Error ew_launch<int64_t>(const trs_ew_program&, const trs_view*, const trs_view*,
+                              const SumTarget*, const EwPrepared&, cudaStream_t);
+}  // namespace trs

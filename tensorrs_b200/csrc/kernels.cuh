@@ -1,0 +1,53 @@
+// kernels.cuh -- launch descriptors and launcher declarations shared by the
+// .cu files and the C ABI layer.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "device_ops.cuh"
+#include "launch.h"
+#include "plan.h"
+#include "runtime.h"
+
+namespace trs {
+
+constexpr int kThreads = 256;
+
+// Unsigned 32-bit division by a divisor fixed at launch (the round-up method
+// of Granlund and Montgomery, "Division by invariant integers using
+// multiplication", PLDI 1994): q = (umulhi(n, m) + n) >> s.
+struct FastDiv {
+  uint32_t d = 1, m = 1, s = 0;
+};
+FastDiv make_fastdiv(uint32_t d);
+
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
+  return (uint32_t)(((uint64_t)__umulhi(n, f.m) + n) >> f.s);
+}
+
+// Element-wise launch descriptor (passed by value as a kernel parameter).
+struct EwDev {
+  int nd;
+  int64_t shape[kMaxDims];
+  int64_t st[kMaxOperands][kMaxDims];
+  int64_t off[kMaxOperands];
+  const void* in[3];
+  void* out;
+  int64_t n;
+  // vector kernel
+  int vec;
+  uint64_t n_chunks;
+  uint64_t cpr;                // chunks per row
+  FastDiv f_cpr;
+  FastDiv f_dim[kMaxDims];     // shape[d] of the outer dimensions
+  // tile kernel
+  int ti;                      // tiled dimension i (unit stride in the transposed inputs)
+  int transposed[3];           // input k is read through shared memory
+  int n_batch;                 // dimensions other than i and j
+  int batch_dim[kMaxDims];
+  uint64_t tiles_i, tiles_j, n_tiles;
+};
+
+}  // namespace trs

@@ -1,0 +1,47 @@
+// launch.h -- host-side declarations of the element-wise launchers (ew*.cu),
+// usable from plain C++ translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "plan.h"
+#include "runtime.h"
+
+namespace trs {
+
+// Where a fused sum goes: a one-element view of the input dtype, or (for the
+// sharded path) a raw f64/u32/u64 accumulator written without rounding.
+struct SumTarget {
+  const trs_view* view = nullptr;  // rounded result
+  void* raw_acc = nullptr;         // accumulator before rounding
+};
+
+// Element-wise program over `in`; writes `out` unless it is null, and the sum
+// of the results to `sum` when it is non-null.
+Error run_elementwise(const trs_ew_program& prog, const trs_view* in,
+                      const trs_view* out, const SumTarget* sum, cudaStream_t stream);
+
+// Plan only (trs_plan_elementwise).
+Error plan_elementwise(const trs_ew_program& prog, const trs_view* in,
+                       const trs_view* out, EwFold* fold, EwChoice* choice);
+
+// Writes a raw accumulator (f64 for floats, wrapping unsigned for integers)
+// into a one-element view of `dtype`, rounding once.
+Error run_acc_to_value(int dtype, const void* acc, const trs_view* out, cudaStream_t stream);
+
+Error run_fill(trs_view* out, uint64_t seed, uint64_t first, double lo, double hi, bool normal,
+               cudaStream_t stream);
+
+// Per-dtype launch of a prepared element-wise op (ew_<dtype>.cu).
+struct EwPrepared {
+  EwFold fold;
+  EwChoice choice;
+  int dtype = TRS_F32;
+};
+template <class T>
+Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* out,
+                const SumTarget* sum, const EwPrepared& pr, cudaStream_t stream);
+
+}  // namespace trs

@@ -1,0 +1,200 @@
+// reduce.cu -- K-RED: reductions over one or more axes of a strided view.
+//
+// Serves sum_axis / sum_axis_keepdim (base.rs:1051-1107, 1534-1594), the
+// mean its callers build (nn/layer_norm.rs:26), max_axis / argmax_axis
+// (base.rs:1396-1505), reduce_broadcast_grad (base.rs:1651-1686) and the
+// fused un-broadcast of a Mul backward (autodiff/core.rs:206-227).
+//
+// The reference walks each output's axis serially (and leaves outputs < 8192
+// on one thread).  Here the reduced and kept dimensions are folded separately
+// on the host and one of three kernels is chosen:
+//   red_row_kernel  the innermost reduced dimension is contiguous: one warp
+//                   per output for short reductions, otherwise one CTA -- or a
+//                   thread-block cluster of up to 8 CTAs whose partials meet
+//                   in distributed shared memory -- per output; 16-byte loads.
+//   red_col_kernel  a kept dimension is contiguous (e.g. sum over axis 0):
+//                   lanes run along the kept dimension, the 8 warps of a CTA
+//                   and the CTAs of a cluster split the reduced rows, and the
+//                   partials meet in shared / distributed shared memory.
+//   red_generic_kernel one thread per output, any layout.
+// Float sums accumulate in f64 and round once; integer sums wrap.  Max and
+// argmax follow the reference's strict `>` scan exactly (see MaxState).
+// Every combine happens in a fixed order, so results are deterministic.
+#include <cstring>
+
+#include "kernels.cuh"
+#include "reduce.h"
+
+namespace trs {
+
+Error plan_reduce(const RedRequest& q, RedDev* d, RedChoice* c) {
+  std::memset(d, 0, sizeof(*d));
+  const trs_view* x = q.in[0];
+  const int nd = x->ndim;
+  d->mode = q.mode;
+  d->has_gate = q.in[1] != nullptr && q.mode == kRedSum3;
+  d->has_mul = q.in[2] != nullptr && q.mode == kRedSum3;
+  for (int k = 0; k < kRedOperands; ++k) {
+    d->in[k] = q.in[k] ? q.in[k]->data : x->data;
+    d->off[k] = q.in[k] ? q.in[k]->offset : 0;
+  }
+  for (int m = 0; m < 2; ++m) {
+    d->out[m] = q.out[m] ? q.out[m]->data : nullptr;
+    d->out_off[m] = q.out[m] ? q.out[m]->offset : 0;
+  }
+  // split the dimensions into kept and reduced, dropping size-1 dims
+  int64_t ksh[kMaxDims], kst[kRedOperands + 2][kMaxDims];
+  int64_t rsh[kMaxDims], rst[kRedOperands][kMaxDims];
+  int nk = 0, nr = 0;
+  d->total = 1;
+  d->n_out = 1;
+  for (int i = 0; i < nd; ++i) {
+    const int64_t s = x->shape[i];
+    if (q.reduce_mask & (1u << i)) {
+      d->total *= s;
+      if (s == 1) continue;
+      rsh[nr] = s;
+      for (int k = 0; k < kRedOperands; ++k) rst[k][nr] = q.in[k] ? q.op_strides[k][i] : 0;
+      ++nr;
+    } else {
+      d->n_out *= s;
+      if (s == 1) continue;
+      ksh[nk] = s;
+      for (int k = 0; k < kRedOperands; ++k) kst[k][nk] = q.in[k] ? q.op_strides[k][i] : 0;
+      kst[kRedOperands][nk] = q.out_strides[0][i];
+      kst[kRedOperands + 1][nk] = q.out_strides[1][i];
+      ++nk;
+    }
+  }
+  // fold adjacent dims of each group when every array steps through them as one run
+  auto fold = [](int64_t* sh, int64_t (*st)[kMaxDims], int n_arr, int& n) {
+    if (n == 0) return;
+    int w = 0;
+    for (int i = 1; i < n; ++i) {
+      bool merge = true;
+      for (int k = 0; k < n_arr; ++k)
+        if (st[k][w] != st[k][i] * sh[i]) { merge = false; break; }
+      if (merge) {
+        sh[w] *= sh[i];
+        for (int k = 0; k < n_arr; ++k) st[k][w] = st[k][i];
+      } else {
+        ++w;
+        sh[w] = sh[i];
+        for (int k = 0; k < n_arr; ++k) st[k][w] = st[k][i];
+      }
+    }
+    n = w + 1;
+  };
+  const bool single_axis = q.mode == kRedMax || q.mode == kRedArgmax;
+  fold(ksh, kst, kRedOperands + 2, nk);
+  if (!single_axis) fold(rsh, rst, kRedOperands, nr);
+  const int es = dtype_size(x->dtype);
+  const int VW = 16 / es;
+  c->variant = kRedGeneric;
+  c->vec = 1;
+  c->warp_mode = false;
+  c->cluster = 1;
+  // unit-stride operand classes
+  auto inner_ok = [&](int64_t s0, const int64_t* ss) {
+    if (s0 != 1) return false;
+    for (int k = 1; k < kRedOperands; ++k)
+      if (q.in[k] && ss[k] != 0 && ss[k] != 1) return false;
+    return true;
+  };
+  // row variant: the innermost reduced dim is contiguous in operand 0
+  int64_t rs_last[kRedOperands] = {0, 0, 0, 0};
+  if (nr > 0)
+    for (int k = 0; k < kRedOperands; ++k) rs_last[k] = rst[k][nr - 1];
+  const bool row_ok = nr > 0 && inner_ok(rs_last[0], rs_last);
+  // column variant: the innermost kept dim is contiguous in operand 0
+  int64_t ks_last[kRedOperands] = {0, 0, 0, 0};
+  if (nk > 0)
+    for (int k = 0; k < kRedOperands; ++k) ks_last[k] = kst[k][nk - 1];
+  const bool col_ok = nk > 0 && !row_ok && q.mode != kRedAffineRelu && inner_ok(ks_last[0], ks_last);
+  // copy the folded dims into the descriptor
+  d->nk = nk;
+  for (int i = 0; i < nk; ++i) {
+    d->kshape[i] = ksh[i];
+    for (int k = 0; k < kRedOperands; ++k) d->kst[k][i] = kst[k][i];
+    d->kout[0][i] = kst[kRedOperands][i];
+    d->kout[1][i] = kst[kRedOperands + 1][i];
+  }
+  d->nr = nr;
+  for (int i = 0; i < nr; ++i) {
+    d->rshape[i] = rsh[i];
+    for (int k = 0; k < kRedOperands; ++k) d->rst[k][i] = rst[k][i];
+  }
+  if (row_ok) {
+    c->variant = kRedRow;
+    d->L = rsh[nr - 1];
+    d->RO = d->total / d->L;
+    for (int k = 0; k < kRedOperands; ++k) d->inner_bcast[k] = rs_last[k] == 0 ? 1 : 0;
+    // the row kernel walks reduced dims 0..nr-2 as "outer rows"
+    bool vec = (d->L % VW) == 0;
+    for (int k = 0; k < kRedOperands && vec; ++k) {
+      // the operands the row kernel reads with vector loads
+      const bool vector_read =
+          q.in[k] && !d->inner_bcast[k] &&
+          (k == 0 || (k == 1 && (q.mode == kRedAffineRelu || d->has_gate)) ||
+           (k == 2 && q.mode == kRedSum3 && d->has_mul));
+      if (!vector_read) continue;
+      if (((uintptr_t)q.in[k]->data + (uintptr_t)(q.in[k]->offset * es)) % 16) vec = false;
+      for (int i = 0; i < nk; ++i) if (kst[k][i] % VW) vec = false;
+      for (int i = 0; i + 1 < nr; ++i) if (rst[k][i] % VW) vec = false;
+    }
+    c->vec = vec ? VW : 1;
+    if (d->total <= 4096 && q.mode != kRedAffineRelu) {
+      c->warp_mode = true;
+    } else {
+      // enough CTAs to fill the GPU: up to 8 per output in a cluster
+      const DeviceInfo& dev = current_device_info();
+      int cl = 1;
+      while (cl < 8 && (uint64_t)d->n_out * cl < (uint64_t)dev.sm_count * 4 &&
+             (uint64_t)d->total / (uint64_t)(cl * 2) >= 8192)
+        cl *= 2;
+      c->cluster = cl;
+    }
+    return Error{};
+  }
+  if (col_ok) {
+    c->variant = kRedCol;
+    d->W = ksh[nk - 1];
+    for (int k = 0; k < kRedOperands; ++k) d->wst[k] = ks_last[k];
+    d->wout[0] = kst[kRedOperands][nk - 1];
+    d->wout[1] = kst[kRedOperands + 1][nk - 1];
+    d->nk = nk - 1;  // the column kernel walks the remaining kept dims as "outer"
+    d->n_out_outer = d->n_out / d->W;
+    bool vec = (d->W % VW) == 0;
+    for (int k = 0; k < kRedOperands && vec; ++k) {
+      if (!q.in[k] || k > 0) continue;
+      if (((uintptr_t)q.in[k]->data + (uintptr_t)(q.in[k]->offset * es)) % 16) vec = false;
+      for (int i = 0; i + 1 < nk; ++i) if (kst[k][i] % VW) vec = false;
+      for (int i = 0; i < nr; ++i) if (rst[k][i] % VW) vec = false;
+    }
+    c->vec = vec ? VW : 1;
+    const DeviceInfo& dev = current_device_info();
+    const uint64_t blocks = (uint64_t)((d->W + 32 * c->vec - 1) / (32 * c->vec)) * (uint64_t)d->n_out_outer;
+    int cl = 1;
+    while (cl < 8 && blocks * cl < (uint64_t)dev.sm_count * 4 && (uint64_t)d->total / (uint64_t)(cl * 2) >= 64)
+      cl *= 2;
+    c->cluster = cl;
+    return Error{};
+  }
+  return Error{};
+}
+
+Error run_reduce(const RedRequest& q, cudaStream_t stream) {
+  RedDev d;
+  RedChoice c;
+  Error e = plan_reduce(q, &d, &c);
+  if (!e.ok()) return e;
+  switch (q.in[0]->dtype) {
+    case TRS_F32: return red_launch<float>(d, c, stream);
+    case TRS_F64: return red_launch<double>(d, c, stream);
+    case TRS_I32: return red_launch<int32_t>(d, c, stream);
+    case TRS_I64: return red_launch<int64_t>(d, c, stream);
+  }
+  return make_error(TRS_ERR_DTYPE, "unknown dtype");
+}
+
+}  // namespace trs

@@ -1,0 +1,78 @@
+// reduce.h -- reduction launch descriptors (see reduce.cu).
+#pragma once
+
+#include <cstdint>
+
+#include "plan.h"
+#include "runtime.h"
+
+namespace trs {
+
+enum RedMode {
+  kRedSum = 0,        // sum over the reduced dims
+  kRedMean = 1,       // sum / (number of reduced elements), IEEE division in T
+  kRedMax = 2,        // max_axis
+  kRedArgmax = 3,     // argmax_axis (i64 output)
+  kRedSum3 = 4,       // sum of g & map(gate > 0 ? 1 : 0) & mul (gate, mul optional)
+  kRedAffineRelu = 5  // ReLU(x & s + b) backward: out0 = sum (g&m)&x, out1 = sum g&m
+};
+
+constexpr int kRedOperands = 4;
+
+// What to reduce, in the input's own dimensions: operand k (0 = the tensor
+// being reduced, 1..3 = auxiliary inputs of the fused modes) has strides
+// op_strides[k][i] along input dimension i (already broadcast to the input's
+// shape); outputs m = 0, 1 have strides out_strides[m][i] along every kept
+// input dimension i.
+struct RedRequest {
+  int mode = kRedSum;
+  uint32_t reduce_mask = 0;  // bit i set: input dimension i is reduced
+  const trs_view* in[kRedOperands] = {nullptr, nullptr, nullptr, nullptr};
+  int64_t op_strides[kRedOperands][kMaxDims] = {};
+  const trs_view* out[2] = {nullptr, nullptr};
+  int64_t out_strides[2][kMaxDims] = {};
+};
+
+struct RedDev {
+  int mode;
+  int has_gate, has_mul;
+  const void* in[kRedOperands];
+  int64_t off[kRedOperands];
+  void* out[2];
+  int64_t out_off[2];
+  // kept dims (folded)
+  int nk;
+  int64_t kshape[kMaxDims];
+  int64_t kst[kRedOperands][kMaxDims];
+  int64_t kout[2][kMaxDims];
+  // reduced dims (folded)
+  int nr;
+  int64_t rshape[kMaxDims];
+  int64_t rst[kRedOperands][kMaxDims];
+  int64_t total;   // reduced elements per output
+  int64_t n_out;   // outputs
+  // row kernel
+  int64_t L, RO;
+  int inner_bcast[kRedOperands];
+  // column kernel
+  int64_t W;
+  int64_t wst[kRedOperands];
+  int64_t wout[2];
+  int64_t n_out_outer;
+};
+
+enum RedVariant { kRedRow = 0, kRedCol = 1, kRedGeneric = 2 };
+
+struct RedChoice {
+  int variant = kRedGeneric;
+  int vec = 1;
+  bool warp_mode = false;
+  unsigned cluster = 1;
+};
+
+Error plan_reduce(const RedRequest& q, RedDev* d, RedChoice* c);
+template <class T>
+Error red_launch(RedDev& d, const RedChoice& c, cudaStream_t stream);
+Error run_reduce(const RedRequest& q, cudaStream_t stream);
+
+}  // namespace trs

@@ -1,0 +1,6 @@
+// reduce_f32.cu -- reduction kernels instantiated for float.
+#include "reduce_kernels.cuh"
+
+namespace trs {
+template Error red_launch<float>(RedDev&, const RedChoice&, cudaStream_t);
+}  // namespace trs

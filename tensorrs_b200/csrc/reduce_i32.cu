@@ -1,0 +1,6 @@
+// reduce_i32.cu -- reduction kernels instantiated for int32_t.
+#include "reduce_kernels.cuh"
+
+namespace trs {
+template Error red_launch<int32_t>(RedDev&, const RedChoice&, cudaStream_t);
+}  // namespace trs

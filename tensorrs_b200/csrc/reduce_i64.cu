@@ -1,0 +1,6 @@
+// reduce_i64.cu -- reduction kernels instantiated for int64_t.
+#include "reduce_kernels.cuh"
+
+namespace trs {
+template Error red_launch<int64_t>(RedDev&, const RedChoice&, cudaStream_t);
+}  // namespace trs

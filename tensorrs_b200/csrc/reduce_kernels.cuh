@@ -1,0 +1,505 @@
+// reduce_kernels.cuh -- reduction kernel templates and their per-dtype
+// launcher (instantiated in reduce_f32.cu, reduce_f64.cu, reduce_i32.cu and
+// reduce_i64.cu).
+//
+// The reference walks each output's axis serially (and leaves outputs < 8192
+// on one thread).  Here the reduced and kept dimensions are folded separately
+// on the host and one of three kernels is chosen:
+//   red_row_kernel  the innermost reduced dimension is contiguous: one warp
+//                   per output for short reductions, otherwise one CTA -- or a
+//                   thread-block cluster of up to 8 CTAs whose partials meet
+//                   in distributed shared memory -- per output; 16-byte loads.
+//   red_col_kernel  a kept dimension is contiguous (e.g. sum over axis 0):
+//                   lanes run along the kept dimension, the 8 warps of a CTA
+//                   and the CTAs of a cluster split the reduced rows, and the
+//                   partials meet in shared / distributed shared memory.
+//   red_generic_kernel one thread per output, any layout.
+// Float sums accumulate in f64 and round once; integer sums wrap.  Max and
+// argmax follow the reference's strict `>` scan exactly (see MaxState).
+// Every combine happens in a fixed order, so results are deterministic.
+#pragma once
+
+#include <cooperative_groups.h>
+
+#include <cmath>
+#include <cstring>
+
+#include "kernels.cuh"
+#include "reduce.h"
+
+namespace cg = cooperative_groups;
+
+namespace trs {
+namespace rk {
+
+constexpr int kRowThreads = 256;
+constexpr int kWarpModeThreads = 128;
+
+template <class T, int V>
+struct alignas(sizeof(T) * V) RVec {
+  T v[V];
+};
+
+template <class T, int V>
+__device__ __forceinline__ RVec<T, V> rload(const T* p) {
+  RVec<T, V> r;
+  if constexpr (sizeof(T) * V == 16) {
+    int4 x = __ldg(reinterpret_cast<const int4*>(p));
+    memcpy(&r, &x, 16);
+  } else {
+#pragma unroll
+    for (int i = 0; i < V; ++i) r.v[i] = __ldg(p + i);
+  }
+  return r;
+}
+
+// Accumulator state of one reduction, for every mode.
+template <class T>
+struct RedAcc {
+  using Acc = typename Arith<T>::Acc;
+  Acc s0, s1;         // sums (s1: the second output of the affine mode)
+  MaxState<T> m;
+};
+
+template <class T>
+__device__ __forceinline__ RedAcc<T> red_init() {
+  RedAcc<T> a;
+  a.s0 = 0;
+  a.s1 = 0;
+  a.m.val = T(0);
+  a.m.idx = -1;
+  return a;
+}
+
+template <class T>
+__device__ __forceinline__ RedAcc<T> red_combine(int mode, RedAcc<T> a, const RedAcc<T>& b) {
+  if (mode == kRedMax || mode == kRedArgmax) {
+    a.m = max_combine(a.m, b.m);
+  } else {
+    a.s0 = a.s0 + b.s0;
+    a.s1 = a.s1 + b.s1;
+  }
+  return a;
+}
+
+template <class T>
+__device__ __forceinline__ RedAcc<T> red_shfl_down(const RedAcc<T>& a, int o) {
+  RedAcc<T> r;
+  r.s0 = __shfl_down_sync(0xffffffffu, a.s0, o);
+  r.s1 = __shfl_down_sync(0xffffffffu, a.s1, o);
+  r.m = shfl_down_max(a.m, o);
+  return r;
+}
+
+template <class T>
+__device__ __forceinline__ RedAcc<T> red_warp(int mode, RedAcc<T> a) {
+  for (int o = 16; o > 0; o >>= 1) a = red_combine(mode, a, red_shfl_down(a, o));
+  return a;
+}
+
+// Block reduction of RedAcc; valid in thread 0.
+template <class T>
+__device__ __forceinline__ RedAcc<T> red_block(int mode, RedAcc<T> a, RedAcc<T>* smem) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  a = red_warp(mode, a);
+  __syncthreads();
+  if (lane == 0) smem[warp] = a;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  if (warp == 0) {
+    a = lane < nw ? smem[lane] : red_init<T>();
+    a = red_warp(mode, a);
+  }
+  return a;
+}
+
+// One element folded into the accumulator.  `k` is the position along the
+// reduced axis (used by max/argmax, which reduce one axis only).
+template <class T>
+__device__ __forceinline__ void red_push(int mode, RedAcc<T>& a, T v, T g2, T g3, int64_t k) {
+  using A = Arith<T>;
+  switch (mode) {
+    case kRedSum:
+    case kRedMean:
+      a.s0 = a.s0 + A::to_acc(v);
+      break;
+    case kRedMax:
+    case kRedArgmax:
+      max_push(a.m, v, k);
+      break;
+  }
+  (void)g2;
+  (void)g3;
+}
+
+// The fused modes evaluate the product the separate reference calls would
+// have materialised, with the same roundings.
+template <class T>
+__device__ __forceinline__ void red_push_fused(const RedDev& d, RedAcc<T>& a, T g, T x1, T x2,
+                                               T x3, T s_c, T b_c) {
+  using A = Arith<T>;
+  const T one = T(1), zero = T(0);
+  if (d.mode == kRedSum3) {
+    T v = g;
+    if (d.has_gate) v = A::mul(v, x1 > zero ? one : zero);  // g & map(gate > 0 ? 1 : 0)
+    if (d.has_mul) v = A::mul(v, x2);                        // ... & mul
+    a.s0 = a.s0 + A::to_acc(v);
+  } else {  // kRedAffineRelu: x1 = x, with scale s_c and bias b_c of this channel
+    const T z = A::add(A::mul(x1, s_c), b_c);
+    const T gm = A::mul(g, z > zero ? one : zero);           // grad of z
+    a.s0 = a.s0 + A::to_acc(A::mul(gm, x1));                 // scale grad: (g & m) & x
+    a.s1 = a.s1 + A::to_acc(gm);                             // bias grad:   g & m
+  }
+  (void)x3;
+}
+
+// Offsets of output number `o` for every operand and output.
+__device__ __forceinline__ void kept_offsets(const RedDev& d, uint64_t o, int64_t* in_off,
+                                             int64_t* out_off) {
+#pragma unroll
+  for (int k = 0; k < kRedOperands; ++k) in_off[k] = d.off[k];
+  out_off[0] = d.out_off[0];
+  out_off[1] = d.out_off[1];
+  for (int q = d.nk - 1; q >= 0; --q) {
+    const uint64_t nq = q > 0 ? o / (uint64_t)d.kshape[q] : 0;
+    const int64_t c = (int64_t)(q > 0 ? o - nq * (uint64_t)d.kshape[q] : o);
+    o = nq;
+#pragma unroll
+    for (int k = 0; k < kRedOperands; ++k) in_off[k] += c * d.kst[k][q];
+    out_off[0] += c * d.kout[0][q];
+    out_off[1] += c * d.kout[1][q];
+  }
+}
+
+// Offsets of reduced index r (row-major over the reduced dimensions).
+__device__ __forceinline__ void red_offsets(const RedDev& d, uint64_t r, int64_t* off) {
+#pragma unroll
+  for (int k = 0; k < kRedOperands; ++k) off[k] = 0;
+  for (int q = d.nr - 1; q >= 0; --q) {
+    const uint64_t nq = q > 0 ? r / (uint64_t)d.rshape[q] : 0;
+    const int64_t c = (int64_t)(q > 0 ? r - nq * (uint64_t)d.rshape[q] : r);
+    r = nq;
+#pragma unroll
+    for (int k = 0; k < kRedOperands; ++k) off[k] += c * d.rst[k][q];
+  }
+}
+
+template <class T>
+__device__ __forceinline__ void red_write(const RedDev& d, const RedAcc<T>& a, const int64_t* out_off,
+                                          const T* x0, int64_t x_first) {
+  using A = Arith<T>;
+  switch (d.mode) {
+    case kRedSum:
+    case kRedSum3:
+      static_cast<T*>(d.out[0])[out_off[0]] = A::from_acc(a.s0);
+      break;
+    case kRedMean: {
+      const T s = A::from_acc(a.s0);
+      static_cast<T*>(d.out[0])[out_off[0]] = A::div(s, (T)d.total, nullptr);
+      break;
+    }
+    case kRedAffineRelu:
+      if (d.out[0]) static_cast<T*>(d.out[0])[out_off[0]] = A::from_acc(a.s0);
+      if (d.out[1]) static_cast<T*>(d.out[1])[out_off[1]] = A::from_acc(a.s1);
+      break;
+    case kRedMax:
+    case kRedArgmax: {
+      // the reference keeps a NaN found at index 0 (base.rs:1404-1411)
+      const T first = x0[x_first];
+      MaxState<T> m = a.m;
+      if (is_nan_val(first) || m.idx < 0) { m.val = first; m.idx = 0; }
+      if (d.mode == kRedMax)
+        static_cast<T*>(d.out[0])[out_off[0]] = m.val;
+      else
+        static_cast<int64_t*>(d.out[0])[out_off[0]] = m.idx;
+      break;
+    }
+  }
+}
+
+// --------------------------------------------------------------------------
+// Row kernel.  Group = one warp (WARP) or one CTA of a cluster of CS CTAs.
+// The reduced space of an output is [RO outer rows] x [L contiguous].
+template <class T, int V, bool WARP>
+__global__ void __launch_bounds__(WARP ? kWarpModeThreads : kRowThreads)
+red_row_kernel(const RedDev d) {
+  using A = Arith<T>;
+  __shared__ RedAcc<T> smem[32];
+  const T* x0 = static_cast<const T*>(d.in[0]);
+  const T* x1 = static_cast<const T*>(d.in[1]);
+  const T* x2 = static_cast<const T*>(d.in[2]);
+  const T* x3 = static_cast<const T*>(d.in[3]);
+  const bool fused = d.mode == kRedSum3 || d.mode == kRedAffineRelu;
+  uint64_t o;
+  uint32_t worker, n_workers;
+  unsigned crank = 0, csize = 1;
+  if constexpr (WARP) {
+    o = (uint64_t)blockIdx.x * (kWarpModeThreads / 32) + (threadIdx.x >> 5);
+    worker = threadIdx.x & 31;
+    n_workers = 32;
+  } else {
+    cg::cluster_group cluster = cg::this_cluster();
+    crank = cluster.block_rank();
+    csize = cluster.num_blocks();
+    o = blockIdx.x / csize;
+    worker = crank * kRowThreads + threadIdx.x;
+    n_workers = csize * kRowThreads;
+  }
+  const bool live = o < (uint64_t)d.n_out;
+  int64_t koff[kRedOperands], ooff[2];
+  kept_offsets(d, live ? o : 0, koff, ooff);
+  RedAcc<T> acc = red_init<T>();
+  T s_c = T(0), b_c = T(0);
+  if (d.mode == kRedAffineRelu) {
+    s_c = __ldg(x2 + koff[2]);
+    b_c = __ldg(x3 + koff[3]);
+  }
+  if (live) {
+    const uint64_t cpr = (uint64_t)(d.L / V);
+    const uint64_t total = (uint64_t)d.RO * cpr;
+    const int nr = d.nr;
+    for (uint64_t idx = worker; idx < total; idx += n_workers) {
+      const uint64_t ro = idx / cpr;
+      const int64_t c = (int64_t)(idx - ro * cpr) * V;
+      int64_t roff[kRedOperands];
+#pragma unroll
+      for (int k = 0; k < kRedOperands; ++k) roff[k] = 0;
+      if (nr > 1) {
+        uint64_t r = ro;
+        for (int q = nr - 2; q >= 0; --q) {
+          const uint64_t nq = q > 0 ? r / (uint64_t)d.rshape[q] : 0;
+          const int64_t cc = (int64_t)(q > 0 ? r - nq * (uint64_t)d.rshape[q] : r);
+          r = nq;
+#pragma unroll
+          for (int k = 0; k < kRedOperands; ++k) roff[k] += cc * d.rst[k][q];
+        }
+      }
+      const RVec<T, V> g = rload<T, V>(x0 + koff[0] + roff[0] + c);
+      if (!fused) {
+#pragma unroll
+        for (int i = 0; i < V; ++i) red_push<T>(d.mode, acc, g.v[i], T(0), T(0), c + i);
+      } else {
+        RVec<T, V> a1, a2;
+        if (d.mode == kRedAffineRelu || d.has_gate) {
+          if (d.inner_bcast[1]) { T s = __ldg(x1 + koff[1] + roff[1]);
+#pragma unroll
+            for (int i = 0; i < V; ++i) a1.v[i] = s; }
+          else a1 = rload<T, V>(x1 + koff[1] + roff[1] + c);
+        }
+        if (d.mode == kRedSum3 && d.has_mul) {
+          if (d.inner_bcast[2]) { T s = __ldg(x2 + koff[2] + roff[2]);
+#pragma unroll
+            for (int i = 0; i < V; ++i) a2.v[i] = s; }
+          else a2 = rload<T, V>(x2 + koff[2] + roff[2] + c);
+        }
+#pragma unroll
+        for (int i = 0; i < V; ++i) red_push_fused<T>(d, acc, g.v[i], a1.v[i], a2.v[i], T(0), s_c, b_c);
+      }
+    }
+  }
+  if constexpr (WARP) {
+    acc = red_warp(d.mode, acc);
+    if (live && (threadIdx.x & 31) == 0) red_write<T>(d, acc, ooff, x0, koff[0]);
+  } else {
+    acc = red_block(d.mode, acc, smem);
+    if (csize == 1) {
+      if (threadIdx.x == 0 && live) red_write<T>(d, acc, ooff, x0, koff[0]);
+      return;
+    }
+    // cluster: rank 0 combines the partials of ranks 0..csize-1 in order
+    cg::cluster_group cluster = cg::this_cluster();
+    if (threadIdx.x == 0) smem[0] = acc;
+    cluster.sync();
+    if (crank == 0 && threadIdx.x == 0) {
+      RedAcc<T> tot = smem[0];
+      for (unsigned r = 1; r < csize; ++r) {
+        const RedAcc<T>* peer = cluster.map_shared_rank(&smem[0], r);
+        tot = red_combine(d.mode, tot, *peer);
+      }
+      if (live) red_write<T>(d, tot, ooff, x0, koff[0]);
+    }
+    cluster.sync();
+  }
+}
+
+// --------------------------------------------------------------------------
+// Column kernel: lanes along the contiguous kept dimension w (32*V columns
+// per CTA), warps and cluster ranks over the reduced rows.
+template <class T, int V>
+__global__ void __launch_bounds__(kRowThreads) red_col_kernel(const RedDev d) {
+  using A = Arith<T>;
+  __shared__ RedAcc<T> part[kRowThreads / 32][32 * V];
+  cg::cluster_group cluster = cg::this_cluster();
+  const unsigned crank = cluster.block_rank(), csize = cluster.num_blocks();
+  const T* x0 = static_cast<const T*>(d.in[0]);
+  const T* x1 = static_cast<const T*>(d.in[1]);
+  const T* x2 = static_cast<const T*>(d.in[2]);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint64_t cb = blockIdx.x / csize;         // column block (and outer kept index)
+  const uint64_t col_blocks = (uint64_t)((d.W + 32 * V - 1) / (32 * V));
+  const uint64_t outer = cb / col_blocks;
+  const int64_t w0 = (int64_t)(cb - outer * col_blocks) * 32 * V + lane * V;
+  // kept offsets of the outer kept dims (all kept dims except w)
+  int64_t koff[kRedOperands], ooff[2];
+  kept_offsets(d, outer, koff, ooff);
+  RedAcc<T> acc[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) acc[i] = red_init<T>();
+  const bool full = w0 + V <= d.W;
+  const bool any = w0 < d.W;
+  const uint64_t rows = (uint64_t)d.total;
+  const bool fused = d.mode == kRedSum3;
+  if (any) {
+    for (uint64_t r = (uint64_t)crank * (kRowThreads / 32) + warp; r < rows;
+         r += (uint64_t)csize * (kRowThreads / 32)) {
+      int64_t roff[kRedOperands];
+      red_offsets(d, r, roff);
+      RVec<T, V> g, a1, a2;
+      const int64_t b0 = koff[0] + roff[0] + w0 * d.wst[0];
+      if (full && V > 1) {
+        g = rload<T, V>(x0 + b0);
+      } else {
+#pragma unroll
+        for (int i = 0; i < V; ++i) g.v[i] = w0 + i < d.W ? __ldg(x0 + b0 + i * d.wst[0]) : T(0);
+      }
+      if (fused) {
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+          const bool in = w0 + i < d.W;
+          a1.v[i] = (d.has_gate && in) ? __ldg(x1 + koff[1] + roff[1] + (w0 + i) * d.wst[1]) : T(0);
+          a2.v[i] = (d.has_mul && in) ? __ldg(x2 + koff[2] + roff[2] + (w0 + i) * d.wst[2]) : T(0);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        if (w0 + i >= d.W) continue;
+        if (fused)
+          red_push_fused<T>(d, acc[i], g.v[i], a1.v[i], a2.v[i], T(0), T(0), T(0));
+        else
+          red_push<T>(d.mode, acc[i], g.v[i], T(0), T(0), (int64_t)r);
+      }
+    }
+  }
+  // warps -> shared memory, combined in warp order by warp 0
+#pragma unroll
+  for (int i = 0; i < V; ++i) part[warp][lane * V + i] = acc[i];
+  __syncthreads();
+  if (warp == 0) {
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      RedAcc<T> t = part[0][lane * V + i];
+      for (int w = 1; w < kRowThreads / 32; ++w) t = red_combine(d.mode, t, part[w][lane * V + i]);
+      part[0][lane * V + i] = t;
+    }
+  }
+  cluster.sync();
+  if (crank == 0 && warp == 0) {
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      RedAcc<T> t = part[0][lane * V + i];
+      for (unsigned r = 1; r < csize; ++r) {
+        const RedAcc<T>* peer = cluster.map_shared_rank(&part[0][lane * V + i], r);
+        t = red_combine(d.mode, t, *peer);
+      }
+      const int64_t w = w0 + i;
+      if (w < d.W) {
+        int64_t oo[2] = {ooff[0] + w * d.wout[0], ooff[1] + w * d.wout[1]};
+        red_write<T>(d, t, oo, x0, koff[0] + w * d.wst[0]);
+      }
+    }
+  }
+  cluster.sync();
+}
+
+// --------------------------------------------------------------------------
+template <class T>
+__global__ void __launch_bounds__(kRowThreads) red_generic_kernel(const RedDev d) {
+  const T* x0 = static_cast<const T*>(d.in[0]);
+  const T* x1 = static_cast<const T*>(d.in[1]);
+  const T* x2 = static_cast<const T*>(d.in[2]);
+  const T* x3 = static_cast<const T*>(d.in[3]);
+  const bool fused = d.mode == kRedSum3 || d.mode == kRedAffineRelu;
+  for (uint64_t o = (uint64_t)blockIdx.x * kRowThreads + threadIdx.x; o < (uint64_t)d.n_out;
+       o += (uint64_t)gridDim.x * kRowThreads) {
+    int64_t koff[kRedOperands], ooff[2];
+    kept_offsets(d, o, koff, ooff);
+    RedAcc<T> acc = red_init<T>();
+    T s_c = T(0), b_c = T(0);
+    if (d.mode == kRedAffineRelu) {
+      s_c = x2[koff[2]];
+      b_c = x3[koff[3]];
+    }
+    for (uint64_t r = 0; r < (uint64_t)d.total; ++r) {
+      int64_t roff[kRedOperands];
+      red_offsets(d, r, roff);
+      const T g = x0[koff[0] + roff[0]];
+      if (!fused) {
+        red_push<T>(d.mode, acc, g, T(0), T(0), (int64_t)r);
+      } else {
+        const T a1 = (d.mode == kRedAffineRelu || d.has_gate) ? x1[koff[1] + roff[1]] : T(0);
+        const T a2 = (d.mode == kRedSum3 && d.has_mul) ? x2[koff[2] + roff[2]] : T(0);
+        red_push_fused<T>(d, acc, g, a1, a2, T(0), s_c, b_c);
+      }
+    }
+    red_write<T>(d, acc, ooff, x0, koff[0]);
+  }
+}
+
+// ---- host ------------------------------------------------------------------
+
+template <class K>
+Error launch_cluster(K kernel, unsigned grid, unsigned threads, unsigned cluster,
+                     cudaStream_t stream, const RedDev& d) {
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, d);
+  if (e != cudaSuccess) return cuda_error(e, "cluster launch");
+  return check_launch("reduction kernel");
+}
+
+}  // namespace rk
+
+template <class T>
+Error red_launch(RedDev& d, const RedChoice& c, cudaStream_t stream) {
+  using namespace rk;
+  const DeviceInfo& dev = current_device_info();
+  if (d.n_out == 0) return Error{};
+  constexpr int VW = 16 / sizeof(T);
+  if (c.variant == kRedRow) {
+    if (c.warp_mode) {
+      const unsigned grid = (unsigned)((d.n_out + kWarpModeThreads / 32 - 1) / (kWarpModeThreads / 32));
+      if (c.vec == VW) red_row_kernel<T, VW, true><<<grid, kWarpModeThreads, 0, stream>>>(d);
+      else red_row_kernel<T, 1, true><<<grid, kWarpModeThreads, 0, stream>>>(d);
+      return check_launch("row reduction kernel");
+    }
+    const unsigned grid = (unsigned)(d.n_out * c.cluster);
+    if (c.vec == VW) return launch_cluster(red_row_kernel<T, VW, false>, grid, kRowThreads, c.cluster, stream, d);
+    return launch_cluster(red_row_kernel<T, 1, false>, grid, kRowThreads, c.cluster, stream, d);
+  }
+  if (c.variant == kRedCol) {
+    const int V = c.vec;
+    const uint64_t col_blocks = (uint64_t)((d.W + 32 * V - 1) / (32 * V));
+    const unsigned grid = (unsigned)(col_blocks * (uint64_t)d.n_out_outer * c.cluster);
+    if (V == VW) return launch_cluster(red_col_kernel<T, VW>, grid, kRowThreads, c.cluster, stream, d);
+    return launch_cluster(red_col_kernel<T, 1>, grid, kRowThreads, c.cluster, stream, d);
+  }
+  uint64_t blocks = ((uint64_t)d.n_out + kRowThreads - 1) / kRowThreads;
+  const uint64_t cap = (uint64_t)dev.sm_count * 16;
+  if (blocks > cap) blocks = cap;
+  red_generic_kernel<T><<<(unsigned)blocks, kRowThreads, 0, stream>>>(d);
+  return check_launch("generic reduction kernel");
+}
+
+
+}  // namespace trs

@@ -1,0 +1,61 @@
+// runtime.cpp -- see runtime.h.
+#include "runtime.h"
+
+#include <mutex>
+
+namespace trs {
+
+std::atomic<uint64_t> g_launch_count{0};
+
+namespace {
+thread_local std::string t_last_error;
+}
+
+void set_last_error(const std::string& msg) { t_last_error = msg; }
+const std::string& last_error() { return t_last_error; }
+
+Error cuda_error(cudaError_t e, const char* what) {
+  return make_error(TRS_ERR_CUDA, std::string(what) + ": " + cudaGetErrorName(e) + ": " +
+                                      cudaGetErrorString(e));
+}
+
+const DeviceInfo& current_device_info() {
+  static DeviceInfo infos[64];
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    static DeviceInfo fallback;
+    return fallback;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  DeviceInfo& d = infos[dev];
+  if (d.device != dev) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess) d.sm_count = v;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) == cudaSuccess)
+      d.max_smem_optin = v;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrClusterLaunch, dev) == cudaSuccess) d.cluster_launch = v;
+    d.device = dev;
+  }
+  return d;
+}
+
+Scratch::~Scratch() {
+  if (ptr_) cudaFreeAsync(ptr_, stream_);
+}
+
+Error Scratch::alloc(size_t bytes, cudaStream_t stream) {
+  stream_ = stream;
+  if (bytes == 0) bytes = 16;
+  cudaError_t e = cudaMallocAsync(&ptr_, bytes, stream);
+  if (e != cudaSuccess) {
+    ptr_ = nullptr;
+    cudaGetLastError();
+    return make_error(e == cudaErrorMemoryAllocation ? TRS_ERR_OOM : TRS_ERR_CUDA,
+                      std::string("scratch allocation of ") + std::to_string(bytes) +
+                          " bytes: " + cudaGetErrorString(e));
+  }
+  return Error{};
+}
+
+}  // namespace trs

@@ -1,0 +1,134 @@
+"""trs_views over PyTorch CUDA tensors, and thin callers of the C ABI that
+allocate their outputs with PyTorch.
+
+PyTorch only provides device memory and the current stream here; every
+computation is a libtrs_b200.so kernel.  Views are described over a tensor's
+underlying storage, so any strides the reference can express (including the
+negative strides of step_slice, which PyTorch views cannot hold) are passed as
+explicit (shape, strides, offset) triples.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import abi
+
+TORCH_TO_TRS = {torch.float32: abi.F32, torch.float64: abi.F64, torch.int32: abi.I32, torch.int64: abi.I64}
+
+
+def stream_handle() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def view_of(t: torch.Tensor, shape=None, strides=None, offset=None) -> abi.View:
+    """A trs_view into t's storage.  Without overrides it describes t itself."""
+    if t.device.type != "cuda":
+        raise ValueError("view_of needs a CUDA tensor")
+    st = t.untyped_storage()
+    es = t.element_size()
+    base = st.data_ptr()
+    storage_len = st.nbytes() // es
+    if shape is None:
+        shape = list(t.shape)
+    if strides is None:
+        strides = list(t.stride()) if shape is not None and list(shape) == list(t.shape) else None
+    if offset is None:
+        offset = t.storage_offset()
+    return abi.make_view(base, TORCH_TO_TRS[t.dtype], shape, strides, offset, storage_len)
+
+
+def _call(name: str, *args) -> int:
+    lib = abi.load()
+    return abi.check(getattr(lib, name)(*args))
+
+
+def binary(op: str, a: abi.View, b: abi.View, out: torch.Tensor) -> torch.Tensor:
+    _call("trs_binary", abi.BINOPS[op], ctypes.byref(a), ctypes.byref(b), ctypes.byref(view_of(out)),
+          stream_handle())
+    return out
+
+
+def unary(op: str, x: abi.View, out: torch.Tensor, p0=0.0, p1=0.0) -> torch.Tensor:
+    params = (abi.Scalar * 2)(abi.scalar(p0), abi.scalar(p1))
+    _call("trs_unary", abi.UNOPS[op], ctypes.byref(x), params, ctypes.byref(view_of(out)), stream_handle())
+    return out
+
+
+def elementwise(prog: abi.Program, ins: list[abi.View], out: torch.Tensor | None,
+                sum_out: torch.Tensor | None = None) -> None:
+    arr = abi.views_array(ins)
+    ov = ctypes.byref(view_of(out)) if out is not None else None
+    if sum_out is None:
+        _call("trs_elementwise", ctypes.byref(prog), arr, ov, stream_handle())
+    else:
+        _call("trs_elementwise_sum", ctypes.byref(prog), arr, ov, ctypes.byref(view_of(sum_out)),
+              stream_handle())
+
+
+def pack(x: abi.View, out: torch.Tensor) -> torch.Tensor:
+    _call("trs_pack", ctypes.byref(x), ctypes.byref(view_of(out)), stream_handle())
+    return out
+
+
+def sum_all(x: abi.View, out: torch.Tensor) -> torch.Tensor:
+    _call("trs_sum", ctypes.byref(x), ctypes.byref(view_of(out)), stream_handle())
+    return out
+
+
+def sum_axis(x: abi.View, axis: int, keepdim: bool, out: torch.Tensor) -> torch.Tensor:
+    _call("trs_sum_axis", ctypes.byref(x), axis, int(keepdim), ctypes.byref(view_of(out)), stream_handle())
+    return out
+
+
+def mean_axis(x: abi.View, axis: int, keepdim: bool, out: torch.Tensor) -> torch.Tensor:
+    _call("trs_mean_axis", ctypes.byref(x), axis, int(keepdim), ctypes.byref(view_of(out)), stream_handle())
+    return out
+
+
+def max_axis(x: abi.View, axis: int, out: torch.Tensor) -> torch.Tensor:
+    _call("trs_max_axis", ctypes.byref(x), axis, ctypes.byref(view_of(out)), stream_handle())
+    return out
+
+
+def argmax_axis(x: abi.View, axis: int, out: torch.Tensor) -> torch.Tensor:
+    _call("trs_argmax_axis", ctypes.byref(x), axis, ctypes.byref(view_of(out)), stream_handle())
+    return out
+
+
+def reduce_broadcast_grad(g: abi.View, target: list[int], out: torch.Tensor) -> int:
+    """Returns abi.OK, or abi.NONE where the reference returns None."""
+    t = (ctypes.c_int64 * max(1, len(target)))(*target)
+    return _call("trs_reduce_broadcast_grad", ctypes.byref(g), t, len(target), ctypes.byref(view_of(out)),
+                 stream_handle())
+
+
+def sum_to_shape_fused(g: abi.View, gate: abi.View | None, mul: abi.View | None, target: list[int],
+                       out: torch.Tensor) -> int:
+    t = (ctypes.c_int64 * max(1, len(target)))(*target)
+    return _call("trs_sum_to_shape_fused", ctypes.byref(g), ctypes.byref(gate) if gate is not None else None,
+                 ctypes.byref(mul) if mul is not None else None, t, len(target), ctypes.byref(view_of(out)),
+                 stream_handle())
+
+
+def affine_relu_backward(g: abi.View, x: abi.View, scale: abi.View, bias: abi.View,
+                         grad_scale: torch.Tensor | None, grad_bias: torch.Tensor | None) -> None:
+    _call("trs_affine_relu_backward", ctypes.byref(g), ctypes.byref(x), ctypes.byref(scale), ctypes.byref(bias),
+          ctypes.byref(view_of(grad_scale)) if grad_scale is not None else None,
+          ctypes.byref(view_of(grad_bias)) if grad_bias is not None else None, stream_handle())
+
+
+def softmax_lastdim(x: abi.View, out: torch.Tensor) -> torch.Tensor:
+    _call("trs_softmax_lastdim", ctypes.byref(x), ctypes.byref(view_of(out)), stream_handle())
+    return out
+
+
+def fill_uniform(out: torch.Tensor, seed: int, lo: float = -1.0, hi: float = 1.0, first: int = 0) -> torch.Tensor:
+    _call("trs_fill_uniform", ctypes.byref(view_of(out)), seed, first, lo, hi, stream_handle())
+    return out
+
+
+def fill_normal(out: torch.Tensor, seed: int, first: int = 0) -> torch.Tensor:
+    _call("trs_fill_normal", ctypes.byref(view_of(out)), seed, first, stream_handle())
+    return out
