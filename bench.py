@@ -1,7 +1,7 @@
 """Benchmark of the broadcast-elementwise / full-reduction hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl trs|reference]
-                    [--workload fma_sum|bias_add|mul_transposed_sigmoid|rowcol_reduce|nchw_affine_relu]
+    python bench.py --suite      # every kernel of the path on its configuration
 
 Default workload (the sharded configuration, run at 1/2/4/8 GPUs):
     Y = A & B + c, s = sum(Y)  with A, B f32 [65536, 32768] ~ U(-1,1) (8 GiB
@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--suite", action="store_true",
+                    help="time every kernel of the path on its configuration (one JSON line each)")
     return ap.parse_args()
 
 
@@ -377,10 +379,157 @@ def run_trs(args) -> None:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# --suite: every kernel of the path on its configuration, one JSON line each
+# ---------------------------------------------------------------------------
+def run_suite(args) -> None:
+    """Times each hot-path kernel on the configuration it serves (SURVEY
+    configs 1-5), with CUDA events around each launch, an L2 flush (a 256 MiB
+    write) before every rep of the L2-resident config 1, and reports achieved
+    GB/s of algorithmic bytes against the measured HBM peak."""
+    import torch
+
+    from tensorrs_b200 import abi, device
+
+    torch.cuda.set_device(0)
+    lib = abi.load()
+    peak, peak_kind = measured_peaks()
+    sh = torch.cuda.current_stream().cuda_stream
+    flush_buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    f32 = torch.float32
+
+    def t(*shape):
+        return torch.empty(shape, dtype=f32, device="cuda")
+
+    def timed(fn, reps, flush):
+        # the 256 MiB flush write also keeps the GPU busy while the host
+        # enqueues the timed launch, so host overhead stays outside the events
+        times = []
+        for i in range(reps + 3):
+            flush_buf.fill_(float(i))
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            if i >= 3:
+                times.append(e0.elapsed_time(e1))
+        return float(np.median(times))
+
+    def report(cfg, name, nbytes, ms, flush=False, extra=None):
+        gbps = nbytes / (ms * 1e-3) / 1e9
+        line = {"suite": cfg, "kernel": name, "bytes": int(nbytes), "ms": round(ms, 4), "GBps": round(gbps, 1),
+                "frac_of_peak": round(gbps / peak, 4), "peak": peak, "peak_source": peak_kind,
+                "l2": "flushed before each rep (256 MiB write)" + ("" if flush else "; inputs exceed L2 anyway")}
+        if extra:
+            line.update(extra)
+        print(json.dumps(line), flush=True)
+
+    def C(st):
+        abi.check(st)
+
+    V = device.view_of
+    reps = max(5, args.steps)
+    # config 1: A[1024,1024] + b[1024]; sum_axis(1); sum()
+    A = device.fill_uniform(t(1024, 1024), 0)
+    b = device.fill_uniform(t(1024), 0, first=1 << 20)
+    Y = t(1024, 1024)
+    r = t(1024)
+    s = t(1)
+    va, vb, vy, vr, vs = V(A), V(b), V(Y), V(r), V(s)
+    p2 = abi.program(2, abi.ADD)
+    ins = abi.views_array([va, vb])
+    ms = timed(lambda: C(lib.trs_elementwise(ctypes.byref(p2), ins, ctypes.byref(vy), sh)), reps, True)
+    report("config1", "bias add A[1024,1024] + b[1024]", 8392704, ms, True)
+    ms = timed(lambda: C(lib.trs_sum_axis(ctypes.byref(va), 1, 0, ctypes.byref(vr), sh)), reps, True)
+    report("config1", "sum_axis(1) of A[1024,1024]", 4194304 + 4096, ms, True)
+    ms = timed(lambda: C(lib.trs_sum(ctypes.byref(va), ctypes.byref(vs), sh)), reps, True)
+    report("config1", "sum() of A[1024,1024]", 4194304 + 4, ms, True)
+    del A, b, Y
+    # config 2: C = A & B^T, sigmoid
+    n = 4096
+    A = device.fill_normal(t(n, n), 1)
+    B = device.fill_normal(t(n, n), 1, first=n * n)
+    Y = t(n, n)
+    vbt = V(B, [n, n], [1, n], 0)
+    nb = n * n * 4
+    pm = abi.program(2, abi.MUL)
+    pms = abi.program(2, abi.MUL, epilogue="sigmoid")
+    ins = abi.views_array([V(A), vbt])
+    ms = timed(lambda: C(lib.trs_elementwise(ctypes.byref(pm), ins, ctypes.byref(V(Y)), sh)), reps, False)
+    report("config2", "A & B^T (B^T strided view)", 3 * nb, ms)
+    ms = timed(lambda: C(lib.trs_elementwise(ctypes.byref(pms), ins, ctypes.byref(V(Y)), sh)), reps, False)
+    report("config2", "sigmoid(A & B^T) fused", 3 * nb, ms)
+    params = (abi.Scalar * 2)()
+    ms = timed(lambda: C(lib.trs_unary(abi.UNOPS["sigmoid"], ctypes.byref(V(A)), params, ctypes.byref(V(Y)), sh)),
+               reps, False)
+    report("config2", "sigmoid standalone [4096,4096]", 2 * nb, ms)
+    del A, B, Y
+    # config 3: X[8192,16384] axis reductions and softmax
+    R, Cc = 8192, 16384
+    X = device.fill_normal(t(R, Cc), 2)
+    vx = V(X)
+    xb = R * Cc * 4
+    r1, r0 = t(R), t(Cc)
+    i1, i0 = torch.empty(R, dtype=torch.int64, device="cuda"), torch.empty(Cc, dtype=torch.int64, device="cuda")
+    for axis, out_f, out_i, nout in [(1, r1, i1, R), (0, r0, i0, Cc)]:
+        vo, vi = V(out_f), V(out_i)
+        ms = timed(lambda: C(lib.trs_sum_axis(ctypes.byref(vx), axis, 0, ctypes.byref(vo), sh)), reps, False)
+        report("config3", f"sum_axis({axis}) of X[8192,16384]", xb + 4 * nout, ms)
+        ms = timed(lambda: C(lib.trs_mean_axis(ctypes.byref(vx), axis, 0, ctypes.byref(vo), sh)), reps, False)
+        report("config3", f"mean over axis {axis}", xb + 4 * nout, ms)
+        ms = timed(lambda: C(lib.trs_max_axis(ctypes.byref(vx), axis, ctypes.byref(vo), sh)), reps, False)
+        report("config3", f"max_axis({axis})", xb + 4 * nout, ms)
+        ms = timed(lambda: C(lib.trs_argmax_axis(ctypes.byref(vx), axis, ctypes.byref(vi), sh)), reps, False)
+        report("config3", f"argmax_axis({axis})", xb + 8 * nout, ms)
+    Ys = t(R, Cc)
+    ms = timed(lambda: C(lib.trs_softmax_lastdim(ctypes.byref(vx), ctypes.byref(V(Ys)), sh)), reps, False)
+    report("config3", "softmax over axis 1", 2 * xb, ms)
+    del X, Ys
+    # config 4: relu(X & s + b) forward; scale/bias gradients backward
+    N, Ch, H, W = 64, 256, 56, 56
+    X = device.fill_normal(t(N, Ch, H, W), 3)
+    G = device.fill_normal(t(N, Ch, H, W), 3, first=N * Ch * H * W)
+    sc = device.fill_uniform(t(1, Ch, 1, 1), 3, 0.5, 1.5)
+    bi = device.fill_uniform(t(1, Ch, 1, 1), 3, -0.1, 0.1, first=Ch)
+    Y = t(N, Ch, H, W)
+    gs, gb = t(1, Ch, 1, 1), t(1, Ch, 1, 1)
+    xb = N * Ch * H * W * 4
+    pf = abi.program(3, abi.MUL, abi.ADD, "relu")
+    ins = abi.views_array([V(X), V(sc), V(bi)])
+    ms = timed(lambda: C(lib.trs_elementwise(ctypes.byref(pf), ins, ctypes.byref(V(Y)), sh)), reps, False)
+    report("config4", "relu(X & s + b) fused forward", 2 * xb + 2 * 4 * Ch, ms)
+    ms = timed(lambda: C(lib.trs_affine_relu_backward(ctypes.byref(V(G)), ctypes.byref(V(X)), ctypes.byref(V(sc)),
+                                                      ctypes.byref(V(bi)), ctypes.byref(V(gs)), ctypes.byref(V(gb)),
+                                                      sh)), reps, False)
+    report("config4", "scale+bias grads of relu(X & s + b), fused", 2 * xb + 4 * 4 * Ch, ms)
+    tgt = (ctypes.c_int64 * 4)(1, Ch, 1, 1)
+    ms = timed(lambda: C(lib.trs_reduce_broadcast_grad(ctypes.byref(V(G)), tgt, 4, ctypes.byref(V(gb)), sh)),
+               reps, False)
+    report("config4", "reduce_broadcast_grad g -> [1,256,1,1]", xb + 4 * Ch, ms)
+    del X, G, Y
+    # config 5 (one GPU): the headline step
+    rows = ROWS
+    A = device.fill_uniform(t(rows, COLS), SEED_A)
+    B = device.fill_uniform(t(rows, COLS), SEED_B)
+    c = device.fill_uniform(t(COLS), SEED_C)
+    Y = t(rows, COLS)
+    p3 = abi.program(3, abi.MUL, abi.ADD)
+    ins = abi.views_array([V(A), V(B), V(c)])
+    ms = timed(lambda: C(lib.trs_elementwise_sum(ctypes.byref(p3), ins, ctypes.byref(V(Y)), ctypes.byref(V(s)), sh)),
+               reps, False)
+    report("config5", "Y = A & B + c and sum(Y) fused", workload_bytes(rows, COLS, 1), ms)
+    ms = timed(lambda: C(lib.trs_sum(ctypes.byref(V(Y)), ctypes.byref(V(s)), sh)), reps, False)
+    report("config5", "sum(Y) alone [65536,32768]", rows * COLS * 4 + 4, ms)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.suite:
+        run_suite(args)
     else:
         run_trs(args)
 

@@ -160,6 +160,13 @@ const char* trs_status_string(int32_t status);
  * Used by benchmarks to report how many GPU launches a timed region made. */
 uint64_t trs_launch_count(void);
 
+/* Reads and clears the current device's async-error word.  A kernel that
+ * waits on its own bulk copies gives up after a bounded number of polls,
+ * sets this word and returns instead of hanging; *code receives the word
+ * (0 = none).  Synchronises the device.  Returns TRS_ERR_TIMEOUT when the
+ * word was set. */
+trs_status trs_async_error(int32_t* code);
+
 /* ------------------------------------------------------------------ */
 /* Host planning (no GPU needed)                                        */
 /* ------------------------------------------------------------------ */

@@ -327,8 +327,12 @@ int binary_op(int op, const Tensor<T>& a, const Tensor<T>& b, Tensor<T>* out) {
   std::vector<int64_t> shape;
   if (!broadcast_shape(a.shape, b.shape, &shape)) { g_msg = bin_msg(op); return ERR_SHAPE; }
   Tensor<T> av, bv;
-  broadcast_to(a, shape, &av);
-  broadcast_to(b, shape, &bv);
+  // broadcast_shape maps a (0, 1) pair to 1, after which broadcast_to fails and
+  // the reference panics with this message (ops.rs:271-272)
+  if (!broadcast_to(a, shape, &av) || !broadcast_to(b, shape, &bv)) {
+    g_msg = "broadcast_to failed (bug)";
+    return ERR_SHAPE;
+  }
   std::vector<int64_t> ai = storage_indices(av);
   std::vector<int64_t> bi = storage_indices(bv);
   int64_t n = 1;
@@ -564,7 +568,8 @@ int reduce_broadcast_grad(const Tensor<T>& g, const std::vector<int64_t>& target
       return NONE;
     }
   }
-  *out = make_tensor(packed_data(cur), cur.shape);
+  // a rank-0 result holds one element (see write_out)
+  *out = make_tensor(cur.shape.empty() ? std::vector<T>{cur.data[cur.offset]} : packed_data(cur), cur.shape);
   return OK;
 }
 
@@ -585,9 +590,13 @@ int softmax_lastdim(const Tensor<T>& x, Tensor<T>* out) {
   return bin(DIV, ex, s, out);
 }
 
+// Copies a result out in row-major order.  A rank-0 result (what summing
+// every axis away leaves) is written as its one element; the reference's
+// storage_indices would list no element for it (base.rs:406-408).
 template <class T>
 void write_out(const Tensor<T>& t, void* out, int64_t* out_shape, int32_t* out_ndim) {
-  std::vector<T> d = is_contiguous(t) && t.offset == 0 && t.owned.size() == (size_t)t.numel()
+  std::vector<T> d = t.shape.empty() ? std::vector<T>{t.data[t.offset]}
+                     : is_contiguous(t) && t.offset == 0 && t.owned.size() == (size_t)t.numel()
                          ? t.owned : packed_data(t);
   std::memcpy(out, d.data(), d.size() * sizeof(T));
   if (out_shape) for (size_t i = 0; i < t.shape.size(); ++i) out_shape[i] = t.shape[i];

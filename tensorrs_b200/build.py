@@ -47,12 +47,13 @@ def _headers() -> list[Path]:
     return sorted(list(CSRC.glob("*.h")) + list(CSRC.glob("*.cuh")) + list((ROOT / "include").glob("*.h")))
 
 
-def _compile(src: Path, verbose: bool) -> Path:
-    obj = BUILD / (src.name + ".o")
+def _compile(src: Path, verbose: bool, build_dir: Path = BUILD, defines: tuple = ()) -> Path:
+    obj = build_dir / (src.name + ".o")
     newest_dep = max([src.stat().st_mtime] + [h.stat().st_mtime for h in _headers()])
     if obj.exists() and obj.stat().st_mtime >= newest_dep:
         return obj
     inc = ["-I", str(CSRC), "-I", str(ROOT / "include"), "-I", str(CUDA_HOME / "include")]
+    inc += [f"-D{d}" for d in defines]
     if src.suffix == ".cu":
         cmd = [str(CUDA_HOME / "bin" / "nvcc"), *ARCH, *NVCC_FLAGS, *inc, "-c", str(src), "-o", str(obj)]
     else:
@@ -67,24 +68,28 @@ def _compile(src: Path, verbose: bool) -> Path:
     return obj
 
 
-def build(clean: bool = False, verbose: bool = False) -> Path:
-    if clean and BUILD.exists():
-        shutil.rmtree(BUILD)
-    BUILD.mkdir(exist_ok=True)
+def build(clean: bool = False, verbose: bool = False, build_dir: Path = BUILD, lib: Path = LIB,
+          defines: tuple = ()) -> Path:
+    """Compiles every source into build_dir and links `lib`.  `defines` are
+    extra -D macros (tuning knobs of the kernels; the defaults are the
+    shipped configuration)."""
+    if clean and build_dir.exists():
+        shutil.rmtree(build_dir)
+    build_dir.mkdir(parents=True, exist_ok=True)
     srcs = _sources()
     with concurrent.futures.ThreadPoolExecutor(max_workers=os.cpu_count() or 4) as ex:
-        objs = list(ex.map(lambda s: _compile(s, verbose), srcs))
+        objs = list(ex.map(lambda s: _compile(s, verbose, build_dir, defines), srcs))
     newest = max(o.stat().st_mtime for o in objs)
-    if not LIB.exists() or LIB.stat().st_mtime < newest:
-        cmd = [str(CUDA_HOME / "bin" / "nvcc"), *ARCH, "-shared", "-o", str(LIB), *map(str, objs),
+    if not lib.exists() or lib.stat().st_mtime < newest:
+        cmd = [str(CUDA_HOME / "bin" / "nvcc"), *ARCH, "-shared", "-o", str(lib), *map(str, objs),
                "-cudart", "static", "-ldl", "-lpthread", "-lrt",
                "-Xlinker", "--version-script=" + str(CSRC / "exports.map")]
         if verbose:
             print(" ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
-            raise RuntimeError(f"linking libtrs_b200.so failed:\n{r.stdout}\n{r.stderr}")
-    return LIB
+            raise RuntimeError(f"linking {lib.name} failed:\n{r.stdout}\n{r.stderr}")
+    return lib
 
 
 def main() -> None:

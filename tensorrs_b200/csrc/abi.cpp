@@ -138,6 +138,20 @@ const char* trs_status_string(int32_t status) {
 
 uint64_t trs_launch_count(void) { return g_launch_count.load(); }
 
+trs_status trs_async_error(int32_t* code) {
+  int* word = async_error_word();
+  if (!word) return finish(make_error(TRS_ERR_CUDA, "the async-error word is not available"));
+  cudaError_t e = cudaDeviceSynchronize();
+  int v = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&v, word, sizeof(int), cudaMemcpyDeviceToHost);
+  const int zero = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(word, &zero, sizeof(int), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return finish(cuda_error(e, "reading the async-error word"));
+  if (code) *code = v;
+  if (v) return finish(make_error(TRS_ERR_TIMEOUT, "a kernel gave up waiting for its own bulk copies"));
+  return TRS_OK;
+}
+
 trs_status trs_broadcast_shape(const int64_t* a, int32_t a_ndim, const int64_t* b, int32_t b_ndim,
                                int64_t* out_shape, int32_t* out_ndim) {
   if (!a || !b || !out_shape || !out_ndim || a_ndim < 0 || b_ndim < 0 || a_ndim > TRS_MAX_DIMS ||
@@ -271,7 +285,13 @@ trs_status trs_reduce_broadcast_grad(const trs_view* g, const int64_t* target, i
       trs_ew_program p;
       std::memset(&p, 0, sizeof(p));
       p.n_in = 1;
-      return finish(run_elementwise(p, &gv, out, nullptr, s));
+      trs_view one = gv;  // the single element, seen with the target's shape
+      one.ndim = target_ndim;
+      for (int i = 0; i < target_ndim; ++i) {
+        one.shape[i] = target[i];
+        one.strides[i] = 0;
+      }
+      return finish(run_elementwise(p, &one, out, nullptr, s));
     }
     // prepend size-1 dimensions until the ranks match
     const int add = target_ndim - gv.ndim;

@@ -16,9 +16,11 @@
 #include <mutex>
 #include <string>
 #include <thread>
+#include <vector>
 
 #include "../../include/trs.h"
 #include "launch.h"
+#include "reduce.h"
 #include "runtime.h"
 
 using namespace trs;
@@ -42,6 +44,7 @@ struct Nccl {
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
   ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                             cudaStream_t) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
 };
 
@@ -65,6 +68,7 @@ Nccl& nccl() {
     TRS_SYM(CommAbort, "ncclCommAbort");
     TRS_SYM(CommDestroy, "ncclCommDestroy");
     TRS_SYM(AllReduce, "ncclAllReduce");
+    TRS_SYM(AllGather, "ncclAllGather");
     TRS_SYM(GetErrorString, "ncclGetErrorString");
 #undef TRS_SYM
     n.loaded = true;
@@ -129,6 +133,97 @@ Error sharded_sum(trs_comm* c, const trs_ew_program& prog, const trs_view* in, c
     return nccl_error(r, "ncclAllReduce");
   }
   return run_acc_to_value(in[0].dtype, acc.get(), sum_out, stream);
+}
+
+// A collective call on a non-blocking communicator.
+Error nccl_call(trs_comm* c, ncclResult_t r, const char* what) {
+  if (r == ncclInProgress) return wait_ready(c, what);
+  if (r != ncclSuccess) return nccl_error(r, what);
+  return Error{};
+}
+
+enum Axis0Op { kAxis0Sum, kAxis0Max, kAxis0Argmax };
+
+// sum_axis(0) / max_axis(0) / argmax_axis(0) of a tensor split on axis 0.
+Error sharded_axis0(trs_comm* c, int op, const trs_view* shard, const trs_view* out, cudaStream_t stream) {
+  if (!c || !c->comm) return make_error(TRS_ERR_ARG, "null communicator");
+  Error e = validate_view(shard, "shard");
+  if (!e.ok()) return e;
+  e = validate_view(out, "output");
+  if (!e.ok()) return e;
+  if (shard->ndim < 1) return make_error(TRS_ERR_AXIS, "!!!Axis index out of range!!!");
+  const int dt = shard->dtype;
+  if (out->dtype != (op == kAxis0Argmax ? (int)TRS_I64 : dt))
+    return make_error(TRS_ERR_DTYPE, op == kAxis0Argmax ? "argmax output must be i64" : "output dtype differs");
+  bool ok = out->ndim == shard->ndim - 1;
+  for (int i = 1; ok && i < shard->ndim; ++i) ok = out->shape[i - 1] == shard->shape[i];
+  if (!ok) return make_error(TRS_ERR_SHAPE, "output shape must be the shard shape without axis 0");
+  Nccl& n = nccl();
+  const int R = c->nranks;
+  // every rank's row count: the global index offset of this shard, and the
+  // empty-axis check of max/argmax
+  Scratch counts;
+  e = counts.alloc(sizeof(int64_t) * (R + 1), stream);
+  if (!e.ok()) return e;
+  int64_t* cnt = counts.as<int64_t>();
+  const int64_t mine = shard->shape[0];
+  cudaError_t ce = cudaMemcpyAsync(cnt + R, &mine, sizeof(int64_t), cudaMemcpyHostToDevice, stream);
+  if (ce != cudaSuccess) return cuda_error(ce, "cudaMemcpyAsync");
+  e = nccl_call(c, n.AllGather(cnt + R, cnt, 1, ncclInt64, c->comm, stream), "ncclAllGather (row counts)");
+  if (!e.ok()) return e;
+  std::vector<int64_t> all(R);
+  ce = cudaMemcpyAsync(all.data(), cnt, sizeof(int64_t) * R, cudaMemcpyDeviceToHost, stream);
+  if (ce == cudaSuccess) ce = cudaStreamSynchronize(stream);
+  if (ce != cudaSuccess) return cuda_error(ce, "reading the row counts");
+  int64_t total = 0, base = 0;
+  for (int r = 0; r < R; ++r) {
+    if (r < c->rank) base += all[r];
+    total += all[r];
+  }
+  if (op != kAxis0Sum && total == 0) return make_error(TRS_ERR_EMPTY_AXIS, "!!!Cannot reduce an empty axis!!!");
+  const int64_t nout = numel_of(out->shape, out->ndim);
+  // local partials, unrounded, into a contiguous scratch buffer
+  const size_t rec = op == kAxis0Sum ? (dt == TRS_I32 ? 4 : 8) : max_record_size(dt);
+  const size_t slots = op == kAxis0Sum ? 1 : (size_t)R;
+  Scratch part;
+  e = part.alloc(rec * (size_t)(nout > 0 ? nout : 1) * slots, stream);
+  if (!e.ok()) return e;
+  char* mine_at = part.as<char>() + (op == kAxis0Sum ? 0 : rec * (size_t)nout * (size_t)c->rank);
+  trs_view pv;
+  std::memset(&pv, 0, sizeof(pv));
+  pv.data = mine_at;
+  pv.dtype = dt;
+  pv.ndim = out->ndim;
+  pv.storage_len = nout > 0 ? nout : 1;
+  int64_t step = 1;
+  for (int i = out->ndim - 1; i >= 0; --i) {
+    pv.shape[i] = out->shape[i];
+    pv.strides[i] = step;
+    step *= out->shape[i];
+  }
+  RedRequest q;
+  q.mode = op == kAxis0Sum ? kRedSum : (op == kAxis0Max ? kRedMax : kRedArgmax);
+  q.raw = true;
+  q.idx_base = base;
+  q.reduce_mask = 1u;
+  q.in[0] = shard;
+  for (int i = 0; i < shard->ndim; ++i) q.op_strides[0][i] = shard->strides[i];
+  q.out[0] = &pv;
+  for (int i = 1; i < shard->ndim; ++i) q.out_strides[0][i] = pv.strides[i - 1];
+  if (nout > 0) {
+    e = run_reduce(q, stream);
+    if (!e.ok()) return e;
+  }
+  if (op == kAxis0Sum) {
+    e = nccl_call(c, n.AllReduce(part.get(), part.get(), (size_t)nout, acc_type(dt), ncclSum, c->comm, stream),
+                  "ncclAllReduce (partial sums)");
+    if (!e.ok()) return e;
+    return run_accs_to_view(dt, part.get(), out, stream);
+  }
+  e = nccl_call(c, n.AllGather(mine_at, part.get(), rec * (size_t)nout, ncclUint8, c->comm, stream),
+                "ncclAllGather (max records)");
+  if (!e.ok()) return e;
+  return run_max_records(dt, part.get(), R, out, op == kAxis0Argmax, stream);
 }
 
 }  // namespace
@@ -207,14 +302,19 @@ trs_status trs_sharded_elementwise_sum(trs_comm* comm, const trs_ew_program* pro
   return finish(sharded_sum(comm, *prog, in, out, sum_out, static_cast<cudaStream_t>(stream)));
 }
 
-trs_status trs_sharded_sum_axis0(trs_comm*, const trs_view*, trs_view*, trs_stream) {
-  return finish(make_error(TRS_ERR_UNAVAILABLE, "trs_sharded_sum_axis0 is not built yet"));
+trs_status trs_sharded_sum_axis0(trs_comm* comm, const trs_view* shard, trs_view* out, trs_stream stream) {
+  if (!shard || !out) return finish(make_error(TRS_ERR_ARG, "null view"));
+  return finish(sharded_axis0(comm, kAxis0Sum, shard, out, static_cast<cudaStream_t>(stream)));
 }
-trs_status trs_sharded_max_axis0(trs_comm*, const trs_view*, trs_view*, trs_stream) {
-  return finish(make_error(TRS_ERR_UNAVAILABLE, "trs_sharded_max_axis0 is not built yet"));
+
+trs_status trs_sharded_max_axis0(trs_comm* comm, const trs_view* shard, trs_view* out, trs_stream stream) {
+  if (!shard || !out) return finish(make_error(TRS_ERR_ARG, "null view"));
+  return finish(sharded_axis0(comm, kAxis0Max, shard, out, static_cast<cudaStream_t>(stream)));
 }
-trs_status trs_sharded_argmax_axis0(trs_comm*, const trs_view*, trs_view*, trs_stream) {
-  return finish(make_error(TRS_ERR_UNAVAILABLE, "trs_sharded_argmax_axis0 is not built yet"));
+
+trs_status trs_sharded_argmax_axis0(trs_comm* comm, const trs_view* shard, trs_view* out, trs_stream stream) {
+  if (!shard || !out) return finish(make_error(TRS_ERR_ARG, "null view"));
+  return finish(sharded_axis0(comm, kAxis0Argmax, shard, out, static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

@@ -43,7 +43,22 @@ template <> struct Arith<float> {
   }
   static __device__ __noinline__ float pow_e(float x, double ln_e) { return pow_e_inline(x, ln_e); }
   static __device__ __noinline__ float exp(float a) { return (float)::exp((double)a); }
-  static __device__ __noinline__ float tanh(float a) { return (float)::tanh((double)a); }
+  // tanh: for |x| >= 1 through expm1 in f32 steps, 1 - 2/(expm1(2|x|) + 2),
+  // the classical formulation (the one glibc's f32 tanh evaluates), with
+  // expm1 rounded once from f64; below 1 the f64 tanh rounded once, because
+  // there the formulation's -t/(t+2) amplifies a one-ulp difference in t.
+  static __device__ __noinline__ float tanh(float a) {
+    const float ax = fabsf(a);
+    if (!(ax >= 1.0f)) return (float)::tanh((double)a);  // |x| < 1, and NaN
+    float z;
+    if (ax >= 22.0f) {
+      z = 1.0f;
+    } else {
+      const float t = (float)::expm1((double)__fmul_rn(2.0f, ax));
+      z = __fsub_rn(1.0f, __fdiv_rn(2.0f, __fadd_rn(t, 2.0f)));
+    }
+    return a < 0.0f ? -z : z;
+  }
   static __device__ __noinline__ float ln(float a) { return (float)::log((double)a); }
   static __device__ __forceinline__ float from(const trs_scalar& s) { return (float)s.f; }
   static __device__ __forceinline__ double to_acc(float a) { return (double)a; }
@@ -188,6 +203,118 @@ __device__ __forceinline__ T apply_program(const EwParams& p, T a, T b, T c) {
   if (p.n_in >= 2) v = apply_binop<T>(p.op1, v, b, p.div_flag);
   if (p.n_in >= 3) v = apply_binop<T>(p.op2, v, c, p.div_flag);
   return apply_unop<T>(p, v);
+}
+
+// Programs without transcendentals (the host checks with is_simple_program):
+// the same arithmetic as apply_program with no out-of-line calls, so the
+// streaming kernels keep their registers for loads in flight.
+template <class T>
+__device__ __forceinline__ T apply_binop_simple(int op, T a, T b, int* flag) {
+  using A = Arith<T>;
+  switch (op) {
+    case TRS_ADD: return A::add(a, b);
+    case TRS_SUB: return A::sub(a, b);
+    case TRS_MUL: return A::mul(a, b);
+    default: return A::div(a, b, flag);
+  }
+}
+
+template <class T>
+__device__ __forceinline__ T apply_unop_simple(const EwParams& p, T v) {
+  using A = Arith<T>;
+  const T one = T(1), zero = T(0);
+  switch (p.epi) {
+    case TRS_UN_NEG: return A::neg(v);
+    case TRS_UN_RELU: return A::mul(v, v > zero ? one : zero);
+    case TRS_UN_LEAKY_RELU: {
+      T pos = A::mul(v, v > zero ? one : zero);
+      T neg = A::mul(A::mul(v, A::from(p.p0)), v <= zero ? one : zero);
+      return A::add(pos, neg);
+    }
+    case TRS_UN_ABS: return A::abs(v);
+    case TRS_UN_SIGN: return v > zero ? one : (v == zero ? zero : A::neg(one));
+    case TRS_UN_CLAMP: {
+      T lo = A::from(p.p0), hi = A::from(p.p1);
+      return v < lo ? lo : (v > hi ? hi : v);
+    }
+    case TRS_UN_ADD_SCALAR: return A::add(v, A::from(p.p0));
+    case TRS_UN_SUB_SCALAR: return A::sub(v, A::from(p.p0));
+    case TRS_UN_RSUB_SCALAR: return A::sub(A::from(p.p0), v);
+    case TRS_UN_MUL_SCALAR: return A::mul(v, A::from(p.p0));
+    case TRS_UN_DIV_SCALAR: return A::div(v, A::from(p.p0), p.div_flag);
+    default: return v;
+  }
+}
+
+template <class T>
+__device__ __forceinline__ T apply_program_simple(const EwParams& p, T a, T b, T c) {
+  T v = a;
+  if (p.n_in >= 2) v = apply_binop_simple<T>(p.op1, v, b, p.div_flag);
+  if (p.n_in >= 3) v = apply_binop_simple<T>(p.op2, v, c, p.div_flag);
+  return apply_unop_simple<T>(p, v);
+}
+
+// ---- programs known at compile time ---------------------------------------
+// The hot fused patterns get their own kernel instantiations, so the element
+// loop carries no op-code switch: PROG is a code from this list, or one of
+// the kRun* codes (op codes read at run time, for every other program).
+enum ProgCode {
+  kRunSimple1 = 0, kRunSimple2, kRunSimple3,  // runtime ops, no transcendental
+  kRunFull1, kRunFull2, kRunFull3,            // runtime ops, any
+  kPack,          // x
+  kAdd, kSub, kMul, kDiv,                     // a op b
+  kMulAdd,        // (a & b) + c
+  kMulAddRelu,    // ReLU((a & b) + c)
+  kMulSigmoid,    // sigmoid(a & b)
+  kSigmoid, kTanh, kRelu,                     // f(x)
+  kNumProgs
+};
+
+__host__ __device__ constexpr int prog_inputs(int code) {
+  return code == kRunSimple1 || code == kRunFull1 || code == kPack || code == kSigmoid || code == kTanh ||
+                 code == kRelu
+             ? 1
+             : (code == kRunSimple3 || code == kRunFull3 || code == kMulAdd || code == kMulAddRelu ? 3 : 2);
+}
+__host__ __device__ constexpr bool prog_is_runtime(int code) { return code <= kRunFull3; }
+__host__ __device__ constexpr bool prog_is_full_runtime(int code) { return code >= kRunFull1 && code <= kRunFull3; }
+
+template <class T, int PROG>
+__device__ __forceinline__ T apply_prog(const EwParams& p, T a, T b, T c) {
+  using A = Arith<T>;
+  const T one = T(1), zero = T(0);
+  if constexpr (PROG <= kRunSimple3) {
+    return apply_program_simple<T>(p, a, b, c);
+  } else if constexpr (PROG <= kRunFull3) {
+    return apply_program<T>(p, a, b, c);
+  } else if constexpr (PROG == kPack) {
+    return a;
+  } else if constexpr (PROG == kAdd) {
+    return A::add(a, b);
+  } else if constexpr (PROG == kSub) {
+    return A::sub(a, b);
+  } else if constexpr (PROG == kMul) {
+    return A::mul(a, b);
+  } else if constexpr (PROG == kDiv) {
+    return A::div(a, b, p.div_flag);
+  } else if constexpr (PROG == kMulAdd) {
+    return A::add(A::mul(a, b), c);
+  } else if constexpr (PROG == kMulAddRelu) {
+    const T v = A::add(A::mul(a, b), c);
+    return A::mul(v, v > zero ? one : zero);
+  } else if constexpr (PROG == kMulSigmoid) {
+    EwParams q = p;
+    q.epi = TRS_UN_SIGMOID;
+    return apply_unop<T>(q, A::mul(a, b));
+  } else if constexpr (PROG == kSigmoid) {
+    EwParams q = p;
+    q.epi = TRS_UN_SIGMOID;
+    return apply_unop<T>(q, a);
+  } else if constexpr (PROG == kTanh) {
+    return A::tanh(a);
+  } else {  // kRelu
+    return A::mul(a, a > zero ? one : zero);
+  }
 }
 
 // ---- reductions ------------------------------------------------------------

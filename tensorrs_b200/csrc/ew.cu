@@ -18,10 +18,54 @@
 // block; sum_finalize_kernel adds the partials in a fixed order and rounds once.
 #include <cmath>
 #include <cstring>
+#include <mutex>
 
 #include "kernels.cuh"
 
 namespace trs {
+
+// Set by a kernel that gave up waiting for its own bulk copies (bulk.cuh).
+__device__ int g_trs_async_error;
+
+int* async_error_word() {
+  static std::mutex mu;
+  static int* words[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!words[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_trs_async_error) == cudaSuccess)
+      words[dev] = static_cast<int*>(p);
+    else
+      cudaGetLastError();
+  }
+  return words[dev];
+}
+
+int program_code(const trs_ew_program& p, bool fl) {
+  const int n = p.n_in, o1 = p.op1, o2 = p.op2, e = p.epilogue;
+  if (n == 1 && e == TRS_UN_NONE) return kPack;
+  if (n == 2 && e == TRS_UN_NONE) {
+    if (o1 == TRS_ADD) return kAdd;
+    if (o1 == TRS_SUB) return kSub;
+    if (o1 == TRS_MUL) return kMul;
+    if (o1 == TRS_DIV) return kDiv;
+  }
+  if (n == 3 && o1 == TRS_MUL && o2 == TRS_ADD && e == TRS_UN_NONE) return kMulAdd;
+  if (fl) {
+    if (n == 3 && o1 == TRS_MUL && o2 == TRS_ADD && e == TRS_UN_RELU) return kMulAddRelu;
+    if (n == 2 && o1 == TRS_MUL && e == TRS_UN_SIGMOID) return kMulSigmoid;
+    if (n == 1 && e == TRS_UN_SIGMOID) return kSigmoid;
+    if (n == 1 && e == TRS_UN_TANH) return kTanh;
+    if (n == 1 && e == TRS_UN_RELU) return kRelu;
+  }
+  const bool simple = is_simple_program(p) || !fl;
+  return (simple ? kRunSimple1 : kRunFull1) + (n - 1);
+}
 
 FastDiv make_fastdiv(uint32_t d) {
   FastDiv f;
@@ -137,6 +181,14 @@ Error prepare(const trs_ew_program& prog, const trs_view* in, const trs_view* ou
   int64_t strides[kMaxOperands][kMaxDims] = {};
   int64_t offs[kMaxOperands] = {};
   const void* bases[kMaxOperands] = {nullptr, nullptr, nullptr, nullptr};
+  for (int k = 0; k < prog.n_in; ++k) {
+    // broadcast_shape maps a (0, 1) pair to 1, after which broadcast_to fails
+    // and the reference panics with this message (ops.rs:271-272)
+    if (!broadcast_strides(&in[k], shape, nd, strides[k + 1]))
+      return make_error(TRS_ERR_SHAPE, "broadcast_to failed (bug)");
+    offs[k + 1] = in[k].offset;
+    bases[k + 1] = in[k].data;
+  }
   if (out) {
     Error e = validate_view(out, "output");
     if (!e.ok()) return e;
@@ -151,12 +203,6 @@ Error prepare(const trs_ew_program& prog, const trs_view* in, const trs_view* ou
     // no output: fold as if writing a contiguous tensor
     int64_t s = 1;
     for (int i = nd - 1; i >= 0; --i) { strides[0][i] = s; s *= shape[i]; }
-  }
-  for (int k = 0; k < prog.n_in; ++k) {
-    if (!broadcast_strides(&in[k], shape, nd, strides[k + 1]))
-      return make_error(TRS_ERR_SHAPE, shape_msg(prog.op1));
-    offs[k + 1] = in[k].offset;
-    bases[k + 1] = in[k].data;
   }
   const int64_t n = numel_of(shape, nd);
   // an output may be an input only through the identical layout

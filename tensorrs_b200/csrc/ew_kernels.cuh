@@ -25,6 +25,17 @@
 
 #include "kernels.cuh"
 
+// Tuning knobs (the defaults are the shipped configuration):
+//   TRS_STREAM_ENABLE  1: rows >= 4 KiB take the bulk-copy pipeline
+//   TRS_VEC_PERSISTENT 1: the vec kernel runs a grid of resident CTAs that
+//                      loop; 0: one CTA per block of work (no loop)
+#ifndef TRS_STREAM_ENABLE
+#define TRS_STREAM_ENABLE 1
+#endif
+#ifndef TRS_VEC_PERSISTENT
+#define TRS_VEC_PERSISTENT 1
+#endif
+
 namespace trs {
 namespace ewk {
 
@@ -44,6 +55,33 @@ __device__ __forceinline__ VecT<T, V> load_vec(const T* p) {
     for (int i = 0; i < V; ++i) r.v[i] = __ldg(p + i);
   }
   return r;
+}
+
+// Streaming forms for operands touched once (evict-first in L1 and L2), so
+// the broadcast operands that are reused stay cached.
+template <class T, int V>
+__device__ __forceinline__ VecT<T, V> load_vec_stream(const T* p) {
+  VecT<T, V> r;
+  if constexpr (sizeof(T) * V == 16) {
+    int4 x = __ldcs(reinterpret_cast<const int4*>(p));
+    memcpy(&r, &x, 16);
+  } else {
+#pragma unroll
+    for (int i = 0; i < V; ++i) r.v[i] = __ldcs(p + i);
+  }
+  return r;
+}
+
+template <class T, int V>
+__device__ __forceinline__ void store_vec_stream(T* p, const VecT<T, V>& r) {
+  if constexpr (sizeof(T) * V == 16) {
+    int4 x;
+    memcpy(&x, &r, 16);
+    __stcs(reinterpret_cast<int4*>(p), x);
+  } else {
+#pragma unroll
+    for (int i = 0; i < V; ++i) __stcs(p + i, r.v[i]);
+  }
 }
 
 template <class T, int V>
@@ -68,83 +106,64 @@ __device__ __forceinline__ void write_partial(Acc acc, Acc* partials) {
 // --------------------------------------------------------------------------
 // ew_vec_kernel: chunk g covers V consecutive elements of one row of the
 // innermost folded dimension; chunks are numbered row-major, so consecutive
-// threads touch consecutive addresses.  Each thread handles U chunks per
-// iteration, issuing all loads before any arithmetic.
-template <class T, int V, int U, bool WRITE, bool SUM, bool BIG>
-__global__ void __launch_bounds__(kThreads)
+// threads touch consecutive addresses.  Each thread handles two chunks per
+// iteration, issuing every load before any arithmetic.  Chunk indices are
+// 32-bit within a launch; the host splits larger tensors into launches over
+// row ranges (row0).  The kernel is templated on the input count so no
+// offset of an absent operand is computed, which keeps it at <= 64
+// registers and 4 CTAs (1024 threads) per SM.
+template <class T, int V, int PROG, bool WRITE, bool SUM>
+__global__ void __launch_bounds__(kThreads, 4)
 ew_vec_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials) {
   using A = Arith<T>;
   using Acc = typename A::Acc;
-  Acc acc = Acc(0);
+  constexpr int NIN = prog_inputs(PROG);
+  constexpr int U = NIN == 1 ? 4 : 2;
+  Acc acc[V];  // one accumulator per lane: independent add chains
+#pragma unroll
+  for (int i = 0; i < V; ++i) acc[i] = Acc(0);
   const int nd = d.nd, j = nd - 1;
-  const int n_ops = p.n_in + 1;
-  const T* in0 = static_cast<const T*>(d.in[0]);
-  const T* in1 = static_cast<const T*>(d.in[1]);
-  const T* in2 = static_cast<const T*>(d.in[2]);
-  T* out = static_cast<T*>(d.out);
-  const bool b0 = d.st[1][j] == 0, b1 = d.st[2][j] == 0, b2 = d.st[3][j] == 0;
-  const uint64_t step = (uint64_t)gridDim.x * kThreads * U;
-  for (uint64_t base = (uint64_t)blockIdx.x * kThreads * U + threadIdx.x; base < d.n_chunks;
-       base += step) {
-    VecT<T, V> va[U], vb[U], vc[U];
+  const uint32_t n_chunks = (uint32_t)d.n_chunks;
+  const uint32_t cpr = d.f_cpr.d;
+  for (uint32_t base = blockIdx.x * (kThreads * U) + threadIdx.x; base < n_chunks;
+       base += gridDim.x * (kThreads * U)) {
+    VecT<T, V> v[U][3];
     int64_t oo[U];
     bool ok[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      uint64_t g = base + (uint64_t)u * kThreads;
-      ok[u] = g < d.n_chunks;
+      uint32_t g = base + (uint32_t)u * kThreads;
+      ok[u] = g < n_chunks;
       if (!ok[u]) g = 0;
-      uint64_t row, col;
-      if constexpr (BIG) {
-        row = g / d.cpr;
-        col = g - row * d.cpr;
-      } else {
-        uint32_t r32 = fdiv((uint32_t)g, d.f_cpr);
-        row = r32;
-        col = (uint32_t)g - r32 * d.f_cpr.d;
-      }
-      int64_t o[kMaxOperands];
+      const uint32_t row32 = fdiv(g, d.f_cpr);
+      const int64_t e = (int64_t)(g - row32 * cpr) * V;
+      int64_t o[NIN + 1];
 #pragma unroll
-      for (int k = 0; k < kMaxOperands; ++k) o[k] = d.off[k];
-      uint64_t r = row;
+      for (int k = 0; k <= NIN; ++k) o[k] = d.off[k];
+      uint32_t r = (uint32_t)d.row0 + row32;
       for (int dd = nd - 2; dd > 0; --dd) {
-        uint64_t q;
-        if constexpr (BIG) q = r / (uint64_t)d.shape[dd];
-        else q = fdiv((uint32_t)r, d.f_dim[dd]);
-        const int64_t c = (int64_t)(r - q * (uint64_t)d.shape[dd]);
+        const uint32_t q = fdiv(r, d.f_dim[dd]);
+        const int64_t c = (int64_t)(r - q * d.f_dim[dd].d);
         r = q;
 #pragma unroll
-        for (int k = 0; k < kMaxOperands; ++k) o[k] += c * d.st[k][dd];
+        for (int k = 0; k <= NIN; ++k) o[k] += c * d.st[k][dd];
       }
       if (nd >= 2) {
 #pragma unroll
-        for (int k = 0; k < kMaxOperands; ++k) o[k] += (int64_t)r * d.st[k][0];
+        for (int k = 0; k <= NIN; ++k) o[k] += (int64_t)r * d.st[k][0];
       }
-      const int64_t e = (int64_t)col * V;
       oo[u] = o[0] + e;
-      if (b0) {
-        T s = __ldg(in0 + o[1]);
 #pragma unroll
-        for (int i = 0; i < V; ++i) va[u].v[i] = s;
-      } else {
-        va[u] = load_vec<T, V>(in0 + o[1] + e);
-      }
-      if (n_ops > 2) {
-        if (b1) {
-          T s = __ldg(in1 + o[2]);
+      for (int k = 0; k < NIN; ++k) {
+        const T* src = static_cast<const T*>(d.in[k]) + o[k + 1];
+        if (d.st[k + 1][j] == 0) {
+          const T sv = __ldg(src);
 #pragma unroll
-          for (int i = 0; i < V; ++i) vb[u].v[i] = s;
+          for (int i = 0; i < V; ++i) v[u][k].v[i] = sv;
+        } else if (d.stream[k]) {
+          v[u][k] = load_vec_stream<T, V>(src + e);
         } else {
-          vb[u] = load_vec<T, V>(in1 + o[2] + e);
-        }
-      }
-      if (n_ops > 3) {
-        if (b2) {
-          T s = __ldg(in2 + o[3]);
-#pragma unroll
-          for (int i = 0; i < V; ++i) vc[u].v[i] = s;
-        } else {
-          vc[u] = load_vec<T, V>(in2 + o[3] + e);
+          v[u][k] = load_vec<T, V>(src + e);
         }
       }
     }
@@ -153,13 +172,202 @@ ew_vec_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials)
       VecT<T, V> r;
 #pragma unroll
       for (int i = 0; i < V; ++i) {
-        r.v[i] = apply_program<T>(p, va[u].v[i], vb[u].v[i], vc[u].v[i]);
-        if (SUM && ok[u]) acc = acc + A::to_acc(r.v[i]);
+        const T a = v[u][0].v[i];
+        const T b = NIN >= 2 ? v[u][NIN >= 2 ? 1 : 0].v[i] : T(0);
+        const T c = NIN >= 3 ? v[u][NIN >= 3 ? 2 : 0].v[i] : T(0);
+        r.v[i] = apply_prog<T, PROG>(p, a, b, c);
+        if (SUM && ok[u]) acc[i] = acc[i] + A::to_acc(r.v[i]);
       }
-      if (WRITE && ok[u]) store_vec<T, V>(out + oo[u], r);
+      if (WRITE && ok[u]) store_vec_stream<T, V>(static_cast<T*>(d.out) + oo[u], r);
     }
   }
-  if constexpr (SUM) write_partial<Acc>(acc, partials);
+  if constexpr (SUM) {
+    Acc t = acc[0];
+#pragma unroll
+    for (int i = 1; i < V; ++i) t = t + acc[i];
+    write_partial<Acc>(t, partials);
+  }
+}
+
+// --------------------------------------------------------------------------
+// ew_stream_kernel: the bulk-copy pipeline, warp-specialised.  Work is split
+// into tiles of up to kTileBytes of one row; each CTA walks its tiles
+// (t = blockIdx.x + k * gridDim.x) through a ring of `stages` shared-memory
+// stages.  Warp 0 is the producer: per tile it waits until the stage is free
+// (the stage's `empty` mbarrier), stores the tile's per-row scalar operands
+// into the stage, arms the stage's `full` mbarrier with the byte count and
+// issues one cp.async.bulk per unit-stride input.  Warps 1..8 consume: wait on
+// `full`, combine the tile from shared memory, stream the result out, and
+// release the stage with one arrive per warp on `empty`.  No CTA-wide barrier
+// runs inside the loop, and up to `stages` tiles are in flight per CTA.
+constexpr int kConsumerWarps = 8;
+constexpr int kStreamThreads = 32 * (1 + kConsumerWarps);
+constexpr int kTileBytes = 16384;
+constexpr int kStageBudget = 100 * 1024;  // shared memory per CTA: two CTAs per SM
+
+__host__ __device__ constexpr int stream_stage_bytes(int nb) { return nb * kTileBytes; }
+__host__ __device__ constexpr int stream_stages(int nb) {
+  return kStageBudget / stream_stage_bytes(nb) > 8 ? 8 : kStageBudget / stream_stage_bytes(nb);
+}
+
+template <class T, int NIN>
+__device__ __forceinline__ void stream_tile_geometry(const EwDev& d, uint32_t t, int64_t* off,
+                                                     int64_t& col0, uint32_t& len) {
+  constexpr int TILE = kTileBytes / (int)sizeof(T);
+  const uint32_t row32 = fdiv(t, d.f_tpr);
+  col0 = (int64_t)(t - row32 * d.f_tpr.d) * TILE;
+  const int64_t rem = d.inner - col0;
+  len = (uint32_t)(rem < TILE ? rem : TILE);
+#pragma unroll
+  for (int k = 0; k <= NIN; ++k) off[k] = d.off[k];
+  uint32_t r = (uint32_t)d.row0 + row32;
+  for (int dd = d.nd - 2; dd > 0; --dd) {
+    const uint32_t q = fdiv(r, d.f_dim[dd]);
+    const int64_t c = (int64_t)(r - q * d.f_dim[dd].d);
+    r = q;
+#pragma unroll
+    for (int k = 0; k <= NIN; ++k) off[k] += c * d.st[k][dd];
+  }
+  if (d.nd >= 2) {
+#pragma unroll
+    for (int k = 0; k <= NIN; ++k) off[k] += (int64_t)r * d.st[k][0];
+  }
+}
+
+template <class T, int PROG, int NB, bool WRITE, bool SUM>
+__global__ void __launch_bounds__(kStreamThreads)
+ew_stream_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials) {
+  using A = Arith<T>;
+  using Acc = typename A::Acc;
+  constexpr int NIN = prog_inputs(PROG);
+  constexpr int V = 16 / (int)sizeof(T);
+  constexpr int S = stream_stages(NB);
+  constexpr int SB = stream_stage_bytes(NB);
+  extern __shared__ __align__(128) unsigned char smem[];
+  // stage s: NB tiles; after the stages, the barriers
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * SB);
+  uint64_t* empty = full + S;
+  __shared__ Acc red[32];
+  const int j = d.nd - 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t n_tiles = (uint32_t)d.n_tiles_s;
+  const uint32_t first = blockIdx.x, stride = gridDim.x;
+  const uint32_t my_tiles = first < n_tiles ? (n_tiles - first + stride - 1) / stride : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  bool failed = false;
+  uint32_t issued = 0;  // producer: tiles whose copies were issued
+  Acc acc[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) acc[i] = Acc(0);
+
+  if (warp == 0) {
+    // ---- producer ----
+    if (lane == 0) {
+      for (uint32_t k = 0; k < my_tiles; ++k) {
+        const int s = (int)(k % S);
+        if (k >= (uint32_t)S && !mbar_wait(&empty[s], ((k / S) - 1) & 1u)) {
+          failed = true;
+          break;
+        }
+        fence_proxy_async();
+        int64_t off[NIN + 1];
+        int64_t col0;
+        uint32_t len;
+        stream_tile_geometry<T, NIN>(d, first + k * stride, off, col0, len);
+        unsigned char* stage = smem + s * SB;
+        const uint32_t bytes = len * (uint32_t)sizeof(T);
+        mbar_arrive_expect_tx(&full[s], bytes * NB);
+#pragma unroll
+        for (int kk = 0; kk < NIN; ++kk) {
+          const int slot = d.bulk_slot[kk];
+          if (slot >= 0)
+            bulk_g2s(stage + slot * kTileBytes, static_cast<const T*>(d.in[kk]) + off[kk + 1] + col0, bytes,
+                     &full[s]);
+        }
+        issued = k + 1;
+      }
+      if (failed) atomicOr(d.err, kAsyncWaitTimeout);
+    }
+  } else {
+    // ---- consumers ----
+    const int ct = threadIdx.x - 32;  // 0 .. 32*kConsumerWarps-1
+    for (uint32_t k = 0; k < my_tiles; ++k) {
+      const int s = (int)(k % S);
+      // geometry and the per-row scalar operands first, so their latency
+      // overlaps the wait for the tile
+      int64_t off[NIN + 1];
+      int64_t col0;
+      uint32_t len;
+      stream_tile_geometry<T, NIN>(d, first + k * stride, off, col0, len);
+      T scalars[3];
+#pragma unroll
+      for (int kk = 0; kk < NIN; ++kk)
+        scalars[kk] = d.bulk_slot[kk] < 0 ? __ldg(static_cast<const T*>(d.in[kk]) + off[kk + 1]) : T(0);
+      // the warp leaves together, so the __syncwarp below never waits on a
+      // lane that gave up
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (k / S) & 1u))) {
+        failed = true;
+        break;
+      }
+      const unsigned char* stage = smem + s * SB;
+      const uint32_t chunks = len / V;
+      for (uint32_t c = ct; c < chunks; c += 32 * kConsumerWarps) {
+        VecT<T, V> in[3];
+#pragma unroll
+        for (int kk = 0; kk < NIN; ++kk) {
+          const int slot = d.bulk_slot[kk];
+          if (slot >= 0) {
+            in[kk] = *reinterpret_cast<const VecT<T, V>*>(stage + slot * kTileBytes + c * 16);
+          } else {
+            const T sv = scalars[kk];
+#pragma unroll
+            for (int i = 0; i < V; ++i) in[kk].v[i] = sv;
+          }
+        }
+        VecT<T, V> r;
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+          const T a = in[0].v[i];
+          const T b = NIN >= 2 ? in[NIN >= 2 ? 1 : 0].v[i] : T(0);
+          const T cc = NIN >= 3 ? in[NIN >= 3 ? 2 : 0].v[i] : T(0);
+          r.v[i] = apply_prog<T, PROG>(p, a, b, cc);
+          if (SUM) acc[i] = acc[i] + A::to_acc(r.v[i]);
+        }
+        if (WRITE) store_vec_stream<T, V>(static_cast<T*>(d.out) + off[0] + col0 + (int64_t)c * V, r);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (failed && lane == 0) atomicOr(d.err, kAsyncWaitTimeout);
+  }
+  // Before the CTA exits every copy it issued must have landed: the consumers
+  // waited on every tile's `full` barrier unless they gave up, in which case
+  // the producer drains the stages still in flight (bounded).
+  const bool any_failed = __syncthreads_or(failed);
+  if (any_failed) {
+    if (threadIdx.x == 0) {
+      const uint32_t start = issued > (uint32_t)S ? issued - S : 0;
+      for (uint32_t k = start; k < issued; ++k) mbar_wait(&full[k % S], (k / S) & 1u);
+    }
+    __syncthreads();
+    return;
+  }
+  if constexpr (SUM) {
+    Acc t = acc[0];
+#pragma unroll
+    for (int i = 1; i < V; ++i) t = t + acc[i];
+    t = block_sum<Acc>(t, red);
+    if (threadIdx.x == 0) partials[blockIdx.x] = t;
+  }
 }
 
 // --------------------------------------------------------------------------
@@ -287,20 +495,150 @@ sum_finalize_kernel(const typename Arith<T>::Acc* partials, int n, T* out,
 }
 
 // Blocks per SM a kernel can keep resident (cached per kernel).
-template <class K>
-int resident_blocks(K kernel, int threads) {
+inline int resident_blocks(const void* kernel, int threads) {
   static std::mutex mu;
   static std::unordered_map<const void*, int> cache;
   std::lock_guard<std::mutex> lock(mu);
-  auto it = cache.find((const void*)kernel);
+  auto it = cache.find(kernel);
   if (it != cache.end()) return it->second;
   int b = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, threads, 0) != cudaSuccess || b < 1) {
     cudaGetLastError();
     b = 1;
   }
-  cache[(const void*)kernel] = b;
+  cache[kernel] = b;
   return b;
+}
+
+template <class K>
+int resident_blocks(K kernel, int threads) {
+  return resident_blocks((const void*)kernel, threads);
+}
+
+inline void allow_smem(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, int> done;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done[kernel] >= bytes) return;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess)
+    done[kernel] = bytes;
+  else
+    cudaGetLastError();
+}
+
+inline int resident_blocks_smem(const void* kernel, int threads, int smem) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(kernel);
+  if (it != cache.end()) return it->second;
+  int b = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, threads, smem) != cudaSuccess || b < 1) {
+    cudaGetLastError();
+    b = 1;
+  }
+  cache[kernel] = b;
+  return b;
+}
+
+// Which (write, sum) forms a program code is instantiated with: every code
+// writes; sums are instantiated for the runtime codes, Y = A & B + c, and
+// the plain sum of one input.
+template <class T, int PROG>
+const void* pick_vec_ws(int vw, bool write, bool want_sum) {
+  constexpr bool with_sum = prog_is_runtime(PROG) || PROG == kMulAdd;
+  constexpr bool sum_only = prog_is_runtime(PROG) || PROG == kPack;
+  constexpr int VW = 16 / (int)sizeof(T);
+  if (vw == VW) {
+    if (write && !want_sum) return (const void*)ew_vec_kernel<T, VW, PROG, true, false>;
+    if constexpr (with_sum)
+      if (write && want_sum) return (const void*)ew_vec_kernel<T, VW, PROG, true, true>;
+    if constexpr (sum_only)
+      if (!write && want_sum) return (const void*)ew_vec_kernel<T, VW, PROG, false, true>;
+    return nullptr;
+  }
+  if constexpr (prog_is_runtime(PROG)) {
+    if (write && !want_sum) return (const void*)ew_vec_kernel<T, 1, PROG, true, false>;
+    if (write && want_sum) return (const void*)ew_vec_kernel<T, 1, PROG, true, true>;
+    return (const void*)ew_vec_kernel<T, 1, PROG, false, true>;
+  }
+  return nullptr;
+}
+
+template <class T, int PROG, int NB>
+const void* pick_stream_ws(bool write, bool want_sum) {
+  constexpr bool with_sum = prog_is_runtime(PROG) || PROG == kMulAdd;
+  constexpr bool sum_only = prog_is_runtime(PROG) || PROG == kPack;
+  if (write && !want_sum) return (const void*)ew_stream_kernel<T, PROG, NB, true, false>;
+  if constexpr (with_sum)
+    if (write && want_sum) return (const void*)ew_stream_kernel<T, PROG, NB, true, true>;
+  if constexpr (sum_only)
+    if (!write && want_sum) return (const void*)ew_stream_kernel<T, PROG, NB, false, true>;
+  return nullptr;
+}
+
+// Bulk-input counts instantiated per code: the runtime codes take every
+// count, the specialised ones the layouts of their workloads.
+template <class T, int PROG>
+const void* pick_stream_nb(int nb, bool write, bool want_sum) {
+  constexpr int NIN = prog_inputs(PROG);
+  if constexpr (prog_is_runtime(PROG)) {
+    if (nb == 1) return pick_stream_ws<T, PROG, 1>(write, want_sum);
+    if constexpr (NIN >= 2)
+      if (nb == 2) return pick_stream_ws<T, PROG, 2>(write, want_sum);
+    if constexpr (NIN >= 3)
+      if (nb == 3) return pick_stream_ws<T, PROG, 3>(write, want_sum);
+    return nullptr;
+  } else {
+    if (nb == NIN) return pick_stream_ws<T, PROG, NIN>(write, want_sum);
+    if constexpr (PROG == kMulAddRelu || NIN == 2)
+      if (nb == 1) return pick_stream_ws<T, PROG, 1>(write, want_sum);
+    return nullptr;
+  }
+}
+
+template <class T, class F>
+const void* by_code(int code, F f) {
+  switch (code) {
+    case kRunSimple1: return f(std::integral_constant<int, kRunSimple1>{});
+    case kRunSimple2: return f(std::integral_constant<int, kRunSimple2>{});
+    case kRunSimple3: return f(std::integral_constant<int, kRunSimple3>{});
+    case kPack: return f(std::integral_constant<int, kPack>{});
+    case kAdd: return f(std::integral_constant<int, kAdd>{});
+    case kSub: return f(std::integral_constant<int, kSub>{});
+    case kMul: return f(std::integral_constant<int, kMul>{});
+    case kDiv: return f(std::integral_constant<int, kDiv>{});
+    case kMulAdd: return f(std::integral_constant<int, kMulAdd>{});
+  }
+  if constexpr (IsFloat<T>::value) {
+    switch (code) {
+      case kRunFull1: return f(std::integral_constant<int, kRunFull1>{});
+      case kRunFull2: return f(std::integral_constant<int, kRunFull2>{});
+      case kRunFull3: return f(std::integral_constant<int, kRunFull3>{});
+      case kMulAddRelu: return f(std::integral_constant<int, kMulAddRelu>{});
+      case kMulSigmoid: return f(std::integral_constant<int, kMulSigmoid>{});
+      case kSigmoid: return f(std::integral_constant<int, kSigmoid>{});
+      case kTanh: return f(std::integral_constant<int, kTanh>{});
+      case kRelu: return f(std::integral_constant<int, kRelu>{});
+    }
+  }
+  return nullptr;
+}
+
+// The vec kernel for a program code, falling back to the runtime code of the
+// same input count when the specialised form is not instantiated.
+template <class T>
+const void* pick_vec(int code, int fallback, int vw, bool write, bool want_sum) {
+  const void* k = by_code<T>(code, [&](auto c) { return pick_vec_ws<T, decltype(c)::value>(vw, write, want_sum); });
+  if (!k) k = by_code<T>(fallback, [&](auto c) { return pick_vec_ws<T, decltype(c)::value>(vw, write, want_sum); });
+  return k;
+}
+
+template <class T>
+const void* pick_stream(int code, int fallback, int nb, bool write, bool want_sum) {
+  const void* k = by_code<T>(code, [&](auto c) { return pick_stream_nb<T, decltype(c)::value>(nb, write, want_sum); });
+  if (!k) k = by_code<T>(fallback, [&](auto c) { return pick_stream_nb<T, decltype(c)::value>(nb, write, want_sum); });
+  return k;
 }
 
 }  // namespace ewk
@@ -349,48 +687,86 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
     p.div_flag = flag_mem.as<int>();
   }
 
-  // grid and kernel choice
+  // grid and kernel choice; the vec kernel may take several launches (row
+  // ranges of fewer than 2^31 chunks each)
   const void* kernel = nullptr;
   int blocks = 1;
+  int n_launch = 1;
+  uint64_t rows_per_launch = 0, total_rows = 0, stream_tpr = 0;
+  int stream_smem = 0;
+  constexpr int kEwStream = 100;  // internal variant: the bulk-copy pipeline
   auto grid_for = [&](const void* k, int per_sm, uint64_t work_blocks) {
     uint64_t cap = (uint64_t)dev.sm_count * (uint64_t)per_sm;
     uint64_t b = work_blocks < cap ? work_blocks : cap;
     kernel = k;
     blocks = (int)(b < 1 ? 1 : b);
   };
-  constexpr int U = 4;
-  if (pr.choice.variant == kEwVec) {
+  int variant = pr.choice.variant;
+  if (variant == kEwVec && f.n > 0) {
     const int V = pr.choice.vec;
     const int j = f.nd - 1;
-    d.vec = V;
-    d.n_chunks = (uint64_t)f.n / V;
-    d.cpr = (uint64_t)f.shape[j] / V;
-    bool big = d.n_chunks >= (1ull << 32) || d.cpr == 0;
+    const uint64_t cpr = (uint64_t)f.shape[j] / V;
+    total_rows = (uint64_t)f.n / (uint64_t)f.shape[j];
+    bool fits = cpr > 0 && cpr < (1ull << 31) && total_rows < (1ull << 32);
     for (int i = 0; i < f.nd; ++i)
-      if ((uint64_t)f.shape[i] >= (1ull << 32)) big = true;
-    if (!big) {
-      d.f_cpr = make_fastdiv((uint32_t)d.cpr);
-      for (int i = 0; i < f.nd; ++i) d.f_dim[i] = make_fastdiv((uint32_t)f.shape[i]);
+      if ((uint64_t)f.shape[i] >= (1ull << 32)) fits = false;
+    if (!fits) variant = kEwGeneric;  // index spaces beyond 32 bits take the generic kernel
+    // operands read once stream past the caches; broadcast ones stay cached
+    int nb = 0;
+    for (int k = 0; k < prog.n_in; ++k) {
+      bool reused = false;
+      for (int i = 0; i < f.nd; ++i)
+        if (f.st[k + 1][i] == 0 && f.shape[i] > 1) reused = true;
+      d.stream[k] = reused ? 0 : 1;
+      // the bulk pipeline copies every input that runs along the row; inputs
+      // constant along it (per-row scalars) go through the stage's scalar slots
+      d.bulk_slot[k] = f.st[k + 1][j] == 1 ? nb++ : -1;
     }
-    const uint64_t wb = (d.n_chunks + (uint64_t)kThreads * U - 1) / ((uint64_t)kThreads * U);
     constexpr int VW = 16 / sizeof(T);
-#define TRS_PICK_VEC(VV, W, S, B)                                                       \
-  {                                                                                     \
-    auto k = ewk::ew_vec_kernel<T, VV, U, W, S, B>;                                          \
-    grid_for((const void*)k, ewk::resident_blocks(k, kThreads), wb);                         \
-  }
-#define TRS_PICK_VEC_WS(VV, B)                                                          \
-  if (write && want_sum) TRS_PICK_VEC(VV, true, true, B)                                \
-  else if (write) TRS_PICK_VEC(VV, true, false, B)                                      \
-  else TRS_PICK_VEC(VV, false, true, B)
-    if (V == VW) {
-      if (big) TRS_PICK_VEC_WS(VW, true) else TRS_PICK_VEC_WS(VW, false)
-    } else {
-      if (big) TRS_PICK_VEC_WS(1, true) else TRS_PICK_VEC_WS(1, false)
+    const int code = program_code(prog, IsFloat<T>::value);
+    const bool simple = is_simple_program(prog) || !IsFloat<T>::value;
+    const int fallback = (simple ? kRunSimple1 : kRunFull1) + (prog.n_in - 1);
+    // rows of at least 4 KiB (every unit-stride input 16-byte aligned, which
+    // the vector width V == VW guarantees) take the bulk-copy pipeline
+    const void* sk = nullptr;
+    if (TRS_STREAM_ENABLE && fits && V == VW && nb > 0 && (uint64_t)f.shape[j] * sizeof(T) >= 4096)
+      sk = ewk::pick_stream<T>(code, fallback, nb, write, want_sum);
+    int* err = sk ? async_error_word() : nullptr;
+    if (sk && err) {
+      variant = kEwStream;
+      constexpr uint64_t TILE = ewk::kTileBytes / sizeof(T);
+      const uint64_t tpr = ((uint64_t)f.shape[j] + TILE - 1) / TILE;
+      d.inner = f.shape[j];
+      d.err = err;
+      d.f_tpr = make_fastdiv((uint32_t)tpr);
+      for (int i = 0; i < f.nd; ++i) d.f_dim[i] = make_fastdiv((uint32_t)f.shape[i]);
+      rows_per_launch = ((1ull << 31) - 1) / tpr;
+      if (rows_per_launch > total_rows) rows_per_launch = total_rows;
+      n_launch = (int)((total_rows + rows_per_launch - 1) / rows_per_launch);
+      stream_smem = ewk::stream_stages(nb) * (ewk::stream_stage_bytes(nb) + 16);
+      ewk::allow_smem(sk, stream_smem);
+      grid_for(sk, ewk::resident_blocks_smem(sk, ewk::kStreamThreads, stream_smem), rows_per_launch * tpr);
+      stream_tpr = tpr;
+    } else if (fits) {
+      d.vec = V;
+      d.f_cpr = make_fastdiv((uint32_t)cpr);
+      for (int i = 0; i < f.nd; ++i) d.f_dim[i] = make_fastdiv((uint32_t)f.shape[i]);
+      rows_per_launch = ((1ull << 31) - 1) / cpr;
+      if (rows_per_launch > total_rows) rows_per_launch = total_rows;
+      n_launch = (int)((total_rows + rows_per_launch - 1) / rows_per_launch);
+      const uint64_t chunks = rows_per_launch * cpr;
+      const uint64_t per_block = (uint64_t)kThreads * (prog.n_in == 1 ? 4 : 2);
+      const uint64_t wb = (chunks + per_block - 1) / per_block;
+      const void* k = ewk::pick_vec<T>(V == VW ? code : fallback, fallback, V, write, want_sum);
+      if (TRS_VEC_PERSISTENT) {
+        grid_for(k, ewk::resident_blocks(k, kThreads), wb);
+      } else {
+        kernel = k;
+        blocks = (int)(wb < 1 ? 1 : (wb > 0x7fffffffull ? 0x7fffffffull : wb));
+      }
     }
-#undef TRS_PICK_VEC_WS
-#undef TRS_PICK_VEC
-  } else if (pr.choice.variant == kEwTile) {
+  }
+  if (variant == kEwTile) {
     const int j = f.nd - 1, ti = pr.choice.tile_dim;
     d.ti = ti;
     for (int k = 0; k < prog.n_in; ++k) {
@@ -408,7 +784,7 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
     if (write && want_sum) { auto k = ewk::ew_tile_kernel<T, true, true>; grid_for((const void*)k, ewk::resident_blocks(k, kThreads), d.n_tiles); }
     else if (write) { auto k = ewk::ew_tile_kernel<T, true, false>; grid_for((const void*)k, ewk::resident_blocks(k, kThreads), d.n_tiles); }
     else { auto k = ewk::ew_tile_kernel<T, false, true>; grid_for((const void*)k, ewk::resident_blocks(k, kThreads), d.n_tiles); }
-  } else {
+  } else if (variant == kEwGeneric) {
     const uint64_t wb = ((uint64_t)f.n + kThreads - 1) / kThreads;
     if (write && want_sum) { auto k = ewk::ew_generic_kernel<T, true, true>; grid_for((const void*)k, ewk::resident_blocks(k, kThreads), wb); }
     else if (write) { auto k = ewk::ew_generic_kernel<T, true, false>; grid_for((const void*)k, ewk::resident_blocks(k, kThreads), wb); }
@@ -417,25 +793,37 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
 
   Scratch partials;
   Acc* part = nullptr;
+  const int n_part = blocks * n_launch;
   if (want_sum) {
-    Error e = partials.alloc(sizeof(Acc) * (size_t)blocks, stream);
+    Error e = partials.alloc(sizeof(Acc) * (size_t)n_part, stream);
     if (!e.ok()) return e;
     part = partials.as<Acc>();
   }
   if (f.n > 0) {
-    void* args[] = {(void*)&d, (void*)&p, (void*)&part};
-    cudaError_t ce = cudaLaunchKernel(kernel, dim3(blocks), dim3(kThreads), args, 0, stream);
-    if (ce != cudaSuccess) return cuda_error(ce, "element-wise kernel launch");
-    Error e = check_launch("element-wise kernel");
-    if (!e.ok()) return e;
+    for (int l = 0; l < n_launch; ++l) {
+      if (variant == kEwVec || variant == kEwStream) {
+        d.row0 = (uint64_t)l * rows_per_launch;
+        const uint64_t rows = total_rows - d.row0 < rows_per_launch ? total_rows - d.row0 : rows_per_launch;
+        d.n_chunks = rows * d.f_cpr.d;
+        d.n_tiles_s = rows * stream_tpr;
+      }
+      Acc* part_l = part ? part + (size_t)l * blocks : nullptr;
+      void* args[] = {(void*)&d, (void*)&p, (void*)&part_l};
+      const bool st = variant == kEwStream;
+      cudaError_t ce = cudaLaunchKernel(kernel, dim3(blocks), dim3(st ? ewk::kStreamThreads : kThreads), args,
+                                        st ? (size_t)stream_smem : 0, stream);
+      if (ce != cudaSuccess) return cuda_error(ce, "element-wise kernel launch");
+      Error e = check_launch("element-wise kernel");
+      if (!e.ok()) return e;
+    }
   } else if (want_sum) {
-    cudaError_t ce = cudaMemsetAsync(part, 0, sizeof(Acc) * (size_t)blocks, stream);
+    cudaError_t ce = cudaMemsetAsync(part, 0, sizeof(Acc) * (size_t)n_part, stream);
     if (ce != cudaSuccess) return cuda_error(ce, "cudaMemsetAsync");
   }
   if (want_sum) {
     T* sum_out = nullptr;
     if (sum->view) sum_out = static_cast<T*>(sum->view->data) + sum->view->offset;
-    ewk::sum_finalize_kernel<T><<<1, 1024, 0, stream>>>(part, blocks, sum_out,
+    ewk::sum_finalize_kernel<T><<<1, 1024, 0, stream>>>(part, n_part, sum_out,
                                                    static_cast<Acc*>(sum->raw_acc));
     Error e = check_launch("sum finalize kernel");
     if (!e.ok()) return e;

@@ -6,6 +6,7 @@
 
 #include <cstdint>
 
+#include "bulk.cuh"
 #include "device_ops.cuh"
 #include "launch.h"
 #include "plan.h"
@@ -38,10 +39,17 @@ struct EwDev {
   int64_t n;
   // vector kernel
   int vec;
-  uint64_t n_chunks;
-  uint64_t cpr;                // chunks per row
-  FastDiv f_cpr;
+  uint64_t n_chunks;           // chunks of this launch (< 2^31)
+  uint64_t row0;               // first row of this launch
+  FastDiv f_cpr;               // chunks per row
   FastDiv f_dim[kMaxDims];     // shape[d] of the outer dimensions
+  int stream[3];               // input k is read once: streaming loads
+  // bulk-copy stream kernel
+  uint64_t n_tiles_s;          // tiles of this launch
+  FastDiv f_tpr;               // tiles per row
+  int64_t inner;               // row length (innermost folded dimension)
+  int bulk_slot[3];            // shared-memory slot of input k, or -1
+  int* err;                    // async-error word of this device
   // tile kernel
   int ti;                      // tiled dimension i (unit stride in the transposed inputs)
   int transposed[3];           // input k is read through shared memory

@@ -34,6 +34,29 @@ Error run_acc_to_value(int dtype, const void* acc, const trs_view* out, cudaStre
 Error run_fill(trs_view* out, uint64_t seed, uint64_t first, double lo, double hi, bool normal,
                cudaStream_t stream);
 
+// Sharded axis-0 reductions (shard.cu): round `n = numel(out)` all-reduced
+// accumulators into `out`; fold `nranks` gathered max records per output.
+Error run_accs_to_view(int dtype, const void* acc, const trs_view* out, cudaStream_t stream);
+Error run_max_records(int dtype, const void* records, int nranks, const trs_view* out, bool argmax,
+                      cudaStream_t stream);
+size_t max_record_size(int dtype);
+
+// True when a program needs no transcendental (no powf, exp, tanh, ln).
+inline bool is_simple_program(const trs_ew_program& p) {
+  if (p.n_in >= 2 && p.op1 == TRS_POW) return false;
+  if (p.n_in >= 3 && p.op2 == TRS_POW) return false;
+  switch (p.epilogue) {
+    case TRS_UN_SIGMOID: case TRS_UN_TANH: case TRS_UN_ELU: case TRS_UN_SELU: case TRS_UN_EXP:
+    case TRS_UN_LN: case TRS_UN_POW_SCALAR: case TRS_UN_RPOW_SCALAR:
+      return false;
+  }
+  return true;
+}
+
+// The compile-time program code (ProgCode in device_ops.cuh) of a program:
+// a specialised code for the hot fused patterns, else a runtime code.
+int program_code(const trs_ew_program& p, bool is_float_dtype);
+
 // Per-dtype launch of a prepared element-wise op (ew_<dtype>.cu).
 struct EwPrepared {
   EwFold fold;

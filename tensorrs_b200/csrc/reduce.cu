@@ -32,6 +32,8 @@ Error plan_reduce(const RedRequest& q, RedDev* d, RedChoice* c) {
   const trs_view* x = q.in[0];
   const int nd = x->ndim;
   d->mode = q.mode;
+  d->raw = q.raw ? 1 : 0;
+  d->idx_base = q.idx_base;
   d->has_gate = q.in[1] != nullptr && q.mode == kRedSum3;
   d->has_mul = q.in[2] != nullptr && q.mode == kRedSum3;
   for (int k = 0; k < kRedOperands; ++k) {
@@ -105,12 +107,15 @@ Error plan_reduce(const RedRequest& q, RedDev* d, RedChoice* c) {
   int64_t rs_last[kRedOperands] = {0, 0, 0, 0};
   if (nr > 0)
     for (int k = 0; k < kRedOperands; ++k) rs_last[k] = rst[k][nr - 1];
-  const bool row_ok = nr > 0 && inner_ok(rs_last[0], rs_last);
+  // an empty reduction (some reduced dim is 0) takes the generic kernel,
+  // which writes the empty sum (0) or 0/0 for the mean
+  const bool row_ok = nr > 0 && d->total > 0 && inner_ok(rs_last[0], rs_last);
   // column variant: the innermost kept dim is contiguous in operand 0
   int64_t ks_last[kRedOperands] = {0, 0, 0, 0};
   if (nk > 0)
     for (int k = 0; k < kRedOperands; ++k) ks_last[k] = kst[k][nk - 1];
-  const bool col_ok = nk > 0 && !row_ok && q.mode != kRedAffineRelu && inner_ok(ks_last[0], ks_last);
+  const bool col_ok = nk > 0 && d->total > 0 && !row_ok && q.mode != kRedAffineRelu &&
+                      inner_ok(ks_last[0], ks_last);
   // copy the folded dims into the descriptor
   d->nk = nk;
   for (int i = 0; i < nk; ++i) {

@@ -26,6 +26,11 @@ constexpr int kRedOperands = 4;
 // input dimension i.
 struct RedRequest {
   int mode = kRedSum;
+  // raw outputs (for combining partials across ranks): sums are written as
+  // the unrounded accumulator, max/argmax as MaxRecord with indices offset by
+  // idx_base; out_strides then count records, not elements
+  bool raw = false;
+  int64_t idx_base = 0;
   uint32_t reduce_mask = 0;  // bit i set: input dimension i is reduced
   const trs_view* in[kRedOperands] = {nullptr, nullptr, nullptr, nullptr};
   int64_t op_strides[kRedOperands][kMaxDims] = {};
@@ -33,8 +38,20 @@ struct RedRequest {
   int64_t out_strides[2][kMaxDims] = {};
 };
 
+// One rank's max/argmax partial of one output: the largest non-NaN value
+// and its (global) index, idx < 0 when there is none; `first` is the element
+// at the rank's index 0 (the reference keeps a NaN found at global index 0).
+template <class T>
+struct MaxRecord {
+  T val;
+  T first;
+  int64_t idx;
+};
+
 struct RedDev {
   int mode;
+  int raw;
+  int64_t idx_base;
   int has_gate, has_mul;
   const void* in[kRedOperands];
   int64_t off[kRedOperands];

@@ -188,6 +188,18 @@ template <class T>
 __device__ __forceinline__ void red_write(const RedDev& d, const RedAcc<T>& a, const int64_t* out_off,
                                           const T* x0, int64_t x_first) {
   using A = Arith<T>;
+  if (d.raw) {
+    if (d.mode == kRedMax || d.mode == kRedArgmax) {
+      MaxRecord<T> r;
+      r.val = a.m.val;
+      r.idx = a.m.idx < 0 ? -1 : a.m.idx + d.idx_base;
+      r.first = d.total > 0 ? x0[x_first] : T(0);
+      static_cast<MaxRecord<T>*>(d.out[0])[out_off[0]] = r;
+    } else {
+      static_cast<typename A::Acc*>(d.out[0])[out_off[0]] = a.s0;
+    }
+    return;
+  }
   switch (d.mode) {
     case kRedSum:
     case kRedSum3:

@@ -35,6 +35,17 @@ const DeviceInfo& current_device_info() {
     if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) == cudaSuccess)
       d.max_smem_optin = v;
     if (cudaDeviceGetAttribute(&v, cudaDevAttrClusterLaunch, dev) == cudaSuccess) d.cluster_launch = v;
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    if (cudaMemPoolCreate(&d.pool, &props) == cudaSuccess) {
+      uint64_t keep = ~0ull;
+      cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    } else {
+      cudaGetLastError();
+      d.pool = nullptr;
+    }
     d.device = dev;
   }
   return d;
@@ -47,7 +58,9 @@ Scratch::~Scratch() {
 Error Scratch::alloc(size_t bytes, cudaStream_t stream) {
   stream_ = stream;
   if (bytes == 0) bytes = 16;
-  cudaError_t e = cudaMallocAsync(&ptr_, bytes, stream);
+  const DeviceInfo& dev = current_device_info();
+  cudaError_t e = dev.pool ? cudaMallocFromPoolAsync(&ptr_, bytes, dev.pool, stream)
+                           : cudaMallocAsync(&ptr_, bytes, stream);
   if (e != cudaSuccess) {
     ptr_ = nullptr;
     cudaGetLastError();

@@ -32,6 +32,7 @@ inline Error check_launch(const char* what) {
 
 struct DeviceInfo {
   int device = -1;
+  cudaMemPool_t pool = nullptr;
   int sm_count = 148;
   int max_smem_optin = 0;
   int cluster_launch = 0;
@@ -39,8 +40,10 @@ struct DeviceInfo {
 // Properties of the current device (cached per device).
 const DeviceInfo& current_device_info();
 
-// Scratch memory from the device's stream-ordered pool, released on the same
-// stream when the object goes out of scope (after the work that uses it).
+// Scratch memory from this library's stream-ordered pool on the current
+// device (created once per device with a release threshold that keeps freed
+// blocks cached across synchronisations), released on the same stream when
+// the object goes out of scope (after the work that uses it).
 class Scratch {
  public:
   Scratch() = default;
@@ -55,5 +58,9 @@ class Scratch {
   void* ptr_ = nullptr;
   cudaStream_t stream_ = nullptr;
 };
+
+// Address of the current device's async-error word (set by a kernel that gave
+// up waiting for its own bulk copies), or null if it cannot be found.
+int* async_error_word();
 
 }  // namespace trs

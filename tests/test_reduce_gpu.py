@@ -201,7 +201,6 @@ def test_sum_to_shape_fused_equals_the_mul_backward_chain():
     pre = rand(shape, np.float32, 22)
     x = rand(shape, np.float32, 23)
     dg, dp, dx = contiguous(g), contiguous(pre), contiguous(x)
-    mask = oracle.unary("sign", dp.host_view())  # sign > 0 gives the same 1/0 pattern for the test below
     mask = (pre > 0).astype(np.float32)
     gm = oracle.binary("mul", dg.host_view(), oracle.contiguous(mask))
     prod = oracle.binary("mul", oracle.contiguous(gm), dx.host_view())
@@ -233,7 +232,6 @@ def test_affine_relu_backward_equals_the_reference_chain(shape):
     b = oracle.fill_uniform(np.float32, c, 4, -0.1, 0.1).reshape(1, c, 1, 1)
     dg, dx, ds, db = contiguous(g), contiguous(x), contiguous(s), contiguous(b)
     z = oracle.program(3, "mul", "add", "none", [dx.host_view(), ds.host_view(), db.host_view()])
-    m = oracle.unary("relu", oracle.contiguous(z))  # only for the mask below
     mask = (z > 0).astype(np.float32)
     gm = oracle.binary("mul", dg.host_view(), oracle.contiguous(mask))
     gmx = oracle.binary("mul", oracle.contiguous(gm), dx.host_view())
@@ -247,7 +245,6 @@ def test_affine_relu_backward_equals_the_reference_chain(shape):
         exact = oracle.reduce_broadcast_grad(oracle.contiguous(pd), t)
         sabs = oracle.reduce_broadcast_grad(oracle.contiguous(np.abs(pd)), t)
         check_sum(got, ref, sabs, exact)
-    del m
 
 
 @pytest.mark.parametrize("dtype", [np.float32, np.int64], ids=lambda d: np.dtype(d).name)
