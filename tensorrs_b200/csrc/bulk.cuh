@@ -55,7 +55,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 // Tuning knob: the most time (ns) a try_wait may suspend the thread while the
 // phase is incomplete (0: the hardware's own limit).
 #ifndef TRS_WAIT_HINT_NS
-#define TRS_WAIT_HINT_NS 0
+#define TRS_WAIT_HINT_NS 2000
 #endif
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {

@@ -27,6 +27,75 @@
 
 namespace trs {
 
+namespace {
+
+bool stream_available(int dtype, int mode, int nb) {
+  switch (dtype) {
+    case TRS_F32: return red_stream_available<float>(mode, nb);
+    case TRS_F64: return red_stream_available<double>(mode, nb);
+    case TRS_I32: return red_stream_available<int32_t>(mode, nb);
+    case TRS_I64: return red_stream_available<int64_t>(mode, nb);
+  }
+  return false;
+}
+
+void set_fd(uint32_t* dst, uint64_t v) {
+  const FastDiv f = make_fastdiv((uint32_t)v);
+  dst[0] = f.d;
+  dst[1] = f.m;
+  dst[2] = f.s;
+}
+
+// The bulk-copy row reduction: every segment start 16-byte aligned, segments
+// of at least 2 KiB, 32-bit output / segment / tile counts.
+bool plan_row_stream(const RedRequest& q, RedDev* d, RedChoice* c, int nk, int nr, int es) {
+  const int VW = 16 / es;
+  if (q.raw || d->L * es < 2048 || d->L % VW) return false;
+  if ((uint64_t)d->n_out >= (1ull << 31) || (uint64_t)d->RO >= (1ull << 31)) return false;
+  int nb = 0;
+  for (int k = 0; k < kRedOperands; ++k) {
+    d->bulk_slot[k] = -1;
+    if (!q.in[k]) continue;
+    bool loaded = k == 0 || (q.mode == kRedSum3 && ((k == 1 && d->has_gate) || (k == 2 && d->has_mul))) ||
+                  (q.mode == kRedAffineRelu && k == 1);
+    if (!loaded) continue;
+    if (d->inner_bcast[k]) {
+      if (q.mode == kRedAffineRelu) return false;  // x must run along the segments
+      continue;
+    }
+    // every segment start of a bulk operand must be 16-byte aligned
+    if (((uintptr_t)q.in[k]->data + (uintptr_t)(q.in[k]->offset * es)) % 16) return false;
+    for (int i = 0; i < nk; ++i) if (d->kst[k][i] % VW) return false;
+    for (int i = 0; i + 1 < nr; ++i) if (d->rst[k][i] % VW) return false;
+    d->bulk_slot[k] = nb++;
+  }
+  if (d->bulk_slot[0] != 0 || (q.mode == kRedAffineRelu && d->bulk_slot[1] != 1)) return false;
+  if (!stream_available(q.in[0]->dtype, q.mode, nb)) return false;
+  d->err = async_error_word();
+  if (!d->err) return false;
+  const int64_t tile = 16384 / es;
+  d->tps = (d->L + tile - 1) / tile;
+  const uint64_t tiles_out = (uint64_t)d->RO * (uint64_t)d->tps;
+  if (tiles_out >= (1ull << 31)) return false;
+  const DeviceInfo& dev = current_device_info();
+  const uint64_t want = (uint64_t)dev.sm_count * 4;  // items to keep every CTA busy
+  uint64_t P = 1;
+  if ((uint64_t)d->n_out < want) {
+    P = (want + d->n_out - 1) / d->n_out;
+    if (P > tiles_out) P = tiles_out;
+  }
+  d->tpp = (int64_t)((tiles_out + P - 1) / P);
+  d->P = (int64_t)((tiles_out + d->tpp - 1) / d->tpp);
+  set_fd(d->f_tps, (uint64_t)d->tps);
+  for (int i = 0; i < nk; ++i) set_fd(d->fk[i], (uint64_t)d->kshape[i]);
+  for (int i = 0; i < nr; ++i) set_fd(d->fr[i], (uint64_t)d->rshape[i]);
+  c->variant = kRedRowStream;
+  c->nb = nb;
+  return true;
+}
+
+}  // namespace
+
 Error plan_reduce(const RedRequest& q, RedDev* d, RedChoice* c) {
   std::memset(d, 0, sizeof(*d));
   const trs_view* x = q.in[0];
@@ -134,6 +203,7 @@ Error plan_reduce(const RedRequest& q, RedDev* d, RedChoice* c) {
     d->L = rsh[nr - 1];
     d->RO = d->total / d->L;
     for (int k = 0; k < kRedOperands; ++k) d->inner_bcast[k] = rs_last[k] == 0 ? 1 : 0;
+    if (plan_row_stream(q, d, c, nk, nr, es)) return Error{};
     // the row kernel walks reduced dims 0..nr-2 as "outer rows"
     bool vec = (d->L % VW) == 0;
     for (int k = 0; k < kRedOperands && vec; ++k) {

@@ -71,6 +71,16 @@ struct RedDev {
   // row kernel
   int64_t L, RO;
   int inner_bcast[kRedOperands];
+  // row stream kernel (bulk-copy pipeline over contiguous segments)
+  int64_t tps;           // tiles per segment
+  int64_t P;             // parts per output (items = n_out * P)
+  int64_t tpp;           // tiles per part
+  int bulk_slot[kRedOperands];
+  uint32_t fk[kMaxDims][3];  // FastDiv (d, m, s) of kshape
+  uint32_t fr[kMaxDims][3];  // FastDiv of rshape
+  uint32_t f_tps[3];
+  void* parts;           // RedAcc partial per item when P > 1
+  int* err;
   // column kernel
   int64_t W;
   int64_t wst[kRedOperands];
@@ -78,10 +88,11 @@ struct RedDev {
   int64_t n_out_outer;
 };
 
-enum RedVariant { kRedRow = 0, kRedCol = 1, kRedGeneric = 2 };
+enum RedVariant { kRedRow = 0, kRedCol = 1, kRedGeneric = 2, kRedRowStream = 3 };
 
 struct RedChoice {
   int variant = kRedGeneric;
+  int nb = 0;  // bulk operands of the stream kernel
   int vec = 1;
   bool warp_mode = false;
   unsigned cluster = 1;
@@ -90,6 +101,8 @@ struct RedChoice {
 Error plan_reduce(const RedRequest& q, RedDev* d, RedChoice* c);
 template <class T>
 Error red_launch(RedDev& d, const RedChoice& c, cudaStream_t stream);
+template <class T>
+bool red_stream_available(int mode, int nb);
 Error run_reduce(const RedRequest& q, cudaStream_t stream);
 
 }  // namespace trs

@@ -3,4 +3,5 @@
 
 namespace trs {
 template Error red_launch<float>(RedDev&, const RedChoice&, cudaStream_t);
+template bool red_stream_available<float>(int, int);
 }  // namespace trs

@@ -3,4 +3,5 @@
 
 namespace trs {
 template Error red_launch<int64_t>(RedDev&, const RedChoice&, cudaStream_t);
+template bool red_stream_available<int64_t>(int, int);
 }  // namespace trs

@@ -23,6 +23,7 @@
 
 #include <cmath>
 #include <cstring>
+#include <mutex>
 
 #include "kernels.cuh"
 #include "reduce.h"
@@ -480,7 +481,314 @@ Error launch_cluster(K kernel, unsigned grid, unsigned threads, unsigned cluster
   return check_launch("reduction kernel");
 }
 
+// --------------------------------------------------------------------------
+// red_stream_kernel: reductions whose innermost reduced dimension is
+// contiguous, on the bulk-copy pipeline.  Output o reduces RO segments of L
+// contiguous elements; every segment is cut into tiles of up to
+// kRsTileBytes.  A work item is (output, part): with few outputs each one is
+// split into P parts whose partials a second kernel combines in order.
+// Warp 0 (lane 0) produces: per tile it waits for a free stage, arms the
+// stage's `full` mbarrier and issues one cp.async.bulk per unit-stride
+// operand.  Warps 1..8 consume: load the tile's per-segment scalars, wait,
+// accumulate with the compile-time MODE, release the stage; at the end of an
+// item they combine their states in a fixed order behind a named barrier (the
+// producer takes no part in it) and write the output or the partial.
+// A wait that runs out marks the CTA failed; the failed CTA keeps walking its
+// schedule without waiting or computing, so every barrier is still met, then
+// drains the copies it has in flight and reports through the error word.
+constexpr int kRsConsumerWarps = 8;
+constexpr int kRsThreads = 32 * (1 + kRsConsumerWarps);
+constexpr int kRsTileBytes = 16384;
+constexpr int kRsBudget = 100 * 1024;
+
+__host__ __device__ constexpr int rs_stages(int nb) {
+  return kRsBudget / (nb * kRsTileBytes) > 8 ? 8 : (kRsBudget / (nb * kRsTileBytes) < 2 ? 2 : kRsBudget / (nb * kRsTileBytes));
+}
+
+__device__ __forceinline__ FastDiv fd3(const uint32_t* v) {
+  FastDiv f;
+  f.d = v[0];
+  f.m = v[1];
+  f.s = v[2];
+  return f;
+}
+
+__device__ __forceinline__ void named_sync_consumers() {
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * kRsConsumerWarps) : "memory");
+}
+
+// Kept-dimension offsets of output o (32-bit index arithmetic).
+__device__ __forceinline__ void rs_kept(const RedDev& d, uint32_t o, int64_t* in_off, int64_t* out_off) {
+#pragma unroll
+  for (int k = 0; k < kRedOperands; ++k) in_off[k] = d.off[k];
+  out_off[0] = d.out_off[0];
+  out_off[1] = d.out_off[1];
+  for (int q = d.nk - 1; q >= 0; --q) {
+    uint32_t c = o;
+    if (q > 0) {
+      const FastDiv f = fd3(d.fk[q]);
+      const uint32_t nq = fdiv(o, f);
+      c = o - nq * f.d;
+      o = nq;
+    }
+#pragma unroll
+    for (int k = 0; k < kRedOperands; ++k) in_off[k] += (int64_t)c * d.kst[k][q];
+    out_off[0] += (int64_t)c * d.kout[0][q];
+    out_off[1] += (int64_t)c * d.kout[1][q];
+  }
+}
+
+// Offsets of segment r over the reduced dimensions other than the innermost.
+__device__ __forceinline__ void rs_seg(const RedDev& d, uint32_t r, int64_t* off) {
+#pragma unroll
+  for (int k = 0; k < kRedOperands; ++k) off[k] = 0;
+  for (int q = d.nr - 2; q >= 0; --q) {
+    uint32_t c = r;
+    if (q > 0) {
+      const FastDiv f = fd3(d.fr[q]);
+      const uint32_t nq = fdiv(r, f);
+      c = r - nq * f.d;
+      r = nq;
+    }
+#pragma unroll
+    for (int k = 0; k < kRedOperands; ++k) off[k] += (int64_t)c * d.rst[k][q];
+  }
+}
+
+template <class T, int MODE, int NB>
+__global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) {
+  using A = Arith<T>;
+  using Acc = typename A::Acc;
+  constexpr int V = 16 / (int)sizeof(T);
+  constexpr int TILE = kRsTileBytes / (int)sizeof(T);
+  constexpr int S = rs_stages(NB);
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * NB * kRsTileBytes);
+  uint64_t* empty = full + S;
+  __shared__ RedAcc<T> wred[kRsConsumerWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t n_items = (uint32_t)(d.n_out * d.P);
+  const uint32_t P = (uint32_t)d.P, tpp = (uint32_t)d.tpp;
+  const uint32_t tiles_out = (uint32_t)(d.RO * d.tps);
+  const FastDiv ftps = fd3(d.f_tps);
+  const T* x0 = static_cast<const T*>(d.in[0]);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kRsConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  bool failed = false;
+  uint32_t issued = 0;
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t qn = 0;
+      for (uint32_t it = blockIdx.x; it < n_items; it += gridDim.x) {
+        const uint32_t o = it / P, part = it - o * P;
+        int64_t koff[kRedOperands], ooff[2];
+        rs_kept(d, o, koff, ooff);
+        const uint32_t t0 = part * tpp;
+        const uint32_t nt = part + 1 < P ? tpp : tiles_out - t0;
+        for (uint32_t j = 0; j < nt; ++j, ++qn) {
+          const int s = (int)(qn % S);
+          if (!failed && qn >= (uint32_t)S && !mbar_wait(&empty[s], ((qn / S) - 1) & 1u)) failed = true;
+          if (failed) continue;
+          fence_proxy_async();
+          const uint32_t u = t0 + j;
+          const uint32_t r = fdiv(u, ftps);
+          const int64_t col0 = (int64_t)(u - r * ftps.d) * TILE;
+          const int64_t rem = d.L - col0;
+          const uint32_t len = (uint32_t)(rem < TILE ? rem : TILE);
+          int64_t roff[kRedOperands];
+          rs_seg(d, r, roff);
+          mbar_arrive_expect_tx(&full[s], len * (uint32_t)sizeof(T) * NB);
+#pragma unroll
+          for (int k = 0; k < kRedOperands; ++k) {
+            const int slot = d.bulk_slot[k];
+            if (slot >= 0)
+              bulk_g2s(smem + (s * NB + slot) * kRsTileBytes,
+                       static_cast<const T*>(d.in[k]) + koff[k] + roff[k] + col0, len * (uint32_t)sizeof(T),
+                       &full[s]);
+          }
+          issued = qn + 1;
+        }
+      }
+    }
+  } else {
+    const int ct = threadIdx.x - 32;
+    uint32_t qn = 0;
+    for (uint32_t it = blockIdx.x; it < n_items; it += gridDim.x) {
+      const uint32_t o = it / P, part = it - o * P;
+      int64_t koff[kRedOperands], ooff[2];
+      rs_kept(d, o, koff, ooff);
+      const uint32_t t0 = part * tpp;
+      const uint32_t nt = part + 1 < P ? tpp : tiles_out - t0;
+      Acc acc0[V], acc1[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc0[i] = acc1[i] = Acc(0);
+      MaxState<T> m;
+      m.val = T(0);
+      m.idx = -1;
+      T s_c = T(0), b_c = T(0);
+      if constexpr (MODE == kRedAffineRelu) {
+        s_c = __ldg(static_cast<const T*>(d.in[2]) + koff[2]);
+        b_c = __ldg(static_cast<const T*>(d.in[3]) + koff[3]);
+      }
+      for (uint32_t j = 0; j < nt; ++j, ++qn) {
+        const int s = (int)(qn % S);
+        const uint32_t u = t0 + j;
+        const uint32_t r = fdiv(u, ftps);
+        const int64_t col0 = (int64_t)(u - r * ftps.d) * TILE;
+        const int64_t rem = d.L - col0;
+        const uint32_t len = (uint32_t)(rem < TILE ? rem : TILE);
+        // per-segment scalars of the fused modes (gate / mul constant along L)
+        T sc1 = T(0), sc2 = T(0);
+        if constexpr (MODE == kRedSum3) {
+          int64_t roff[kRedOperands];
+          rs_seg(d, r, roff);
+          if (d.has_gate && d.bulk_slot[1] < 0) sc1 = __ldg(static_cast<const T*>(d.in[1]) + koff[1] + roff[1]);
+          if (d.has_mul && d.bulk_slot[2] < 0) sc2 = __ldg(static_cast<const T*>(d.in[2]) + koff[2] + roff[2]);
+        }
+        if (!failed && !__all_sync(0xffffffffu, mbar_wait(&full[s], (qn / S) & 1u))) failed = true;
+        if (!failed) {
+          const unsigned char* stage = smem + s * NB * kRsTileBytes;
+          const uint32_t chunks = len / V;
+          for (uint32_t c = ct; c < chunks; c += 32 * kRsConsumerWarps) {
+            const RVec<T, V> g = *reinterpret_cast<const RVec<T, V>*>(stage + c * 16);
+            if constexpr (MODE == kRedSum || MODE == kRedMean) {
+#pragma unroll
+              for (int i = 0; i < V; ++i) acc0[i] = acc0[i] + A::to_acc(g.v[i]);
+            } else if constexpr (MODE == kRedMax || MODE == kRedArgmax) {
+#pragma unroll
+              for (int i = 0; i < V; ++i) max_push(m, g.v[i], col0 + (int64_t)c * V + i);
+            } else if constexpr (MODE == kRedSum3) {
+              RVec<T, V> a1, a2;
+              const int s1 = d.bulk_slot[1], s2 = d.bulk_slot[2];
+              if (d.has_gate && s1 >= 0) a1 = *reinterpret_cast<const RVec<T, V>*>(stage + s1 * kRsTileBytes + c * 16);
+              if (d.has_mul && s2 >= 0) a2 = *reinterpret_cast<const RVec<T, V>*>(stage + s2 * kRsTileBytes + c * 16);
+#pragma unroll
+              for (int i = 0; i < V; ++i) {
+                T v = g.v[i];
+                if (d.has_gate) {
+                  const T gt = s1 >= 0 ? a1.v[i] : sc1;
+                  v = A::mul(v, gt > T(0) ? T(1) : T(0));
+                }
+                if (d.has_mul) v = A::mul(v, s2 >= 0 ? a2.v[i] : sc2);
+                acc0[i] = acc0[i] + A::to_acc(v);
+              }
+            } else {  // kRedAffineRelu: slot 1 holds x
+              const RVec<T, V> xv = *reinterpret_cast<const RVec<T, V>*>(stage + kRsTileBytes + c * 16);
+#pragma unroll
+              for (int i = 0; i < V; ++i) {
+                const T z = A::add(A::mul(xv.v[i], s_c), b_c);
+                const T gm = A::mul(g.v[i], z > T(0) ? T(1) : T(0));
+                acc0[i] = acc0[i] + A::to_acc(A::mul(gm, xv.v[i]));
+                acc1[i] = acc1[i] + A::to_acc(gm);
+              }
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+      // combine the item across the consumer warps, in a fixed order
+      RedAcc<T> a = red_init<T>();
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        a.s0 = a.s0 + acc0[i];
+        a.s1 = a.s1 + acc1[i];
+      }
+      a.m = m;
+      a = red_warp(MODE, a);
+      if (lane == 0) wred[warp - 1] = a;
+      named_sync_consumers();
+      if (ct == 0 && !failed) {
+        RedAcc<T> tot = wred[0];
+        for (int w = 1; w < kRsConsumerWarps; ++w) tot = red_combine(MODE, tot, wred[w]);
+        if (P == 1)
+          red_write<T>(d, tot, ooff, x0, koff[0]);
+        else
+          static_cast<RedAcc<T>*>(d.parts)[it] = tot;
+      }
+      named_sync_consumers();
+    }
+  }
+  if (__syncthreads_or(failed)) {
+    if (threadIdx.x == 0) {
+      atomicOr(d.err, kAsyncWaitTimeout);
+      const uint32_t start = issued > (uint32_t)S ? issued - S : 0;
+      for (uint32_t k = start; k < issued; ++k) mbar_wait(&full[k % S], (k / S) & 1u);
+    }
+    __syncthreads();
+  }
+}
+
+// Combines the P partials of every output in part order and writes it.
+template <class T, int MODE>
+__global__ void __launch_bounds__(256) red_parts_finalize(const RedDev d) {
+  const T* x0 = static_cast<const T*>(d.in[0]);
+  const RedAcc<T>* parts = static_cast<const RedAcc<T>*>(d.parts);
+  for (uint32_t o = blockIdx.x * 256 + threadIdx.x; o < (uint32_t)d.n_out; o += gridDim.x * 256) {
+    RedAcc<T> tot = parts[(uint64_t)o * d.P];
+    for (int64_t p = 1; p < d.P; ++p) tot = red_combine(MODE, tot, parts[(uint64_t)o * d.P + p]);
+    int64_t koff[kRedOperands], ooff[2];
+    rs_kept(d, o, koff, ooff);
+    red_write<T>(d, tot, ooff, x0, koff[0]);
+  }
+}
+
 }  // namespace rk
+
+namespace rk {
+
+template <class T, int MODE, int NB>
+const void* stream_kernel_nb() {
+  return (const void*)red_stream_kernel<T, MODE, NB>;
+}
+
+// The stream kernel for (mode, bulk operands), or null when not instantiated.
+template <class T>
+const void* pick_red_stream(int mode, int nb) {
+  if (mode == kRedSum && nb == 1) return stream_kernel_nb<T, kRedSum, 1>();
+  if (mode == kRedMax && nb == 1) return stream_kernel_nb<T, kRedMax, 1>();
+  if (mode == kRedArgmax && nb == 1) return stream_kernel_nb<T, kRedArgmax, 1>();
+  if constexpr (IsFloat<T>::value) {
+    if (mode == kRedMean && nb == 1) return stream_kernel_nb<T, kRedMean, 1>();
+    if (mode == kRedSum3 && nb == 1) return stream_kernel_nb<T, kRedSum3, 1>();
+    if (mode == kRedSum3 && nb == 2) return stream_kernel_nb<T, kRedSum3, 2>();
+    if (mode == kRedSum3 && nb == 3) return stream_kernel_nb<T, kRedSum3, 3>();
+    if (mode == kRedAffineRelu && nb == 2) return stream_kernel_nb<T, kRedAffineRelu, 2>();
+  }
+  return nullptr;
+}
+
+template <class T>
+const void* pick_red_finalize(int mode) {
+  switch (mode) {
+    case kRedSum: return (const void*)red_parts_finalize<T, kRedSum>;
+    case kRedMax: return (const void*)red_parts_finalize<T, kRedMax>;
+    case kRedArgmax: return (const void*)red_parts_finalize<T, kRedArgmax>;
+  }
+  if constexpr (IsFloat<T>::value) {
+    switch (mode) {
+      case kRedMean: return (const void*)red_parts_finalize<T, kRedMean>;
+      case kRedSum3: return (const void*)red_parts_finalize<T, kRedSum3>;
+      case kRedAffineRelu: return (const void*)red_parts_finalize<T, kRedAffineRelu>;
+    }
+  }
+  return nullptr;
+}
+
+}  // namespace rk
+
+template <class T>
+bool red_stream_available(int mode, int nb) {
+  return rk::pick_red_stream<T>(mode, nb) != nullptr;
+}
 
 template <class T>
 Error red_launch(RedDev& d, const RedChoice& c, cudaStream_t stream) {
@@ -488,6 +796,46 @@ Error red_launch(RedDev& d, const RedChoice& c, cudaStream_t stream) {
   const DeviceInfo& dev = current_device_info();
   if (d.n_out == 0) return Error{};
   constexpr int VW = 16 / sizeof(T);
+  if (c.variant == kRedRowStream) {
+    const void* k = pick_red_stream<T>(d.mode, c.nb);
+    if (!k) return make_error(TRS_ERR_ARG, "no stream reduction kernel for this mode");
+    const int S = rs_stages(c.nb);
+    const int smem = S * c.nb * kRsTileBytes + 2 * S * 8;
+    static std::mutex mu;
+    {
+      std::lock_guard<std::mutex> lock(mu);
+      if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        return cuda_error(cudaGetLastError(), "cudaFuncSetAttribute");
+    }
+    int per_sm = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kRsThreads, smem) != cudaSuccess || per_sm < 1) {
+      cudaGetLastError();
+      per_sm = 1;
+    }
+    const uint64_t items = (uint64_t)d.n_out * (uint64_t)d.P;
+    const uint64_t cap = (uint64_t)dev.sm_count * (uint64_t)per_sm;
+    const unsigned grid = (unsigned)(items < cap ? items : cap);
+    Scratch parts;
+    if (d.P > 1) {
+      Error e = parts.alloc(sizeof(RedAcc<T>) * items, stream);
+      if (!e.ok()) return e;
+      d.parts = parts.get();
+    }
+    void* args[] = {(void*)&d};
+    cudaError_t ce = cudaLaunchKernel(k, dim3(grid), dim3(kRsThreads), args, (size_t)smem, stream);
+    if (ce != cudaSuccess) return cuda_error(ce, "stream reduction launch");
+    Error e = check_launch("stream reduction kernel");
+    if (!e.ok()) return e;
+    if (d.P > 1) {
+      const void* fk = pick_red_finalize<T>(d.mode);
+      const uint64_t fb = ((uint64_t)d.n_out + 255) / 256;
+      const unsigned fg = (unsigned)(fb < (uint64_t)dev.sm_count * 8 ? fb : (uint64_t)dev.sm_count * 8);
+      ce = cudaLaunchKernel(fk, dim3(fg), dim3(256), args, 0, stream);
+      if (ce != cudaSuccess) return cuda_error(ce, "partials finalize launch");
+      return check_launch("reduction finalize kernel");
+    }
+    return Error{};
+  }
   if (c.variant == kRedRow) {
     if (c.warp_mode) {
       const unsigned grid = (unsigned)((d.n_out + kWarpModeThreads / 32 - 1) / (kWarpModeThreads / 32));
