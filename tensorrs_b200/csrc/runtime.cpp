@@ -35,20 +35,39 @@ const DeviceInfo& current_device_info() {
     if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) == cudaSuccess)
       d.max_smem_optin = v;
     if (cudaDeviceGetAttribute(&v, cudaDevAttrClusterLaunch, dev) == cudaSuccess) d.cluster_launch = v;
+    d.device = dev;
+  }
+  return d;
+}
+
+// This library's stream-ordered pool on the current device, created on first
+// use with a release threshold that keeps freed blocks cached across
+// synchronisations (null if it cannot be created).
+static cudaMemPool_t device_pool() {
+  static cudaMemPool_t pools[64] = {};
+  static bool tried[64] = {};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!tried[dev]) {
+    tried[dev] = true;
     cudaMemPoolProps props = {};
     props.allocType = cudaMemAllocationTypePinned;
     props.location.type = cudaMemLocationTypeDevice;
     props.location.id = dev;
-    if (cudaMemPoolCreate(&d.pool, &props) == cudaSuccess) {
+    if (cudaMemPoolCreate(&pools[dev], &props) == cudaSuccess) {
       uint64_t keep = ~0ull;
-      cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep);
+      cudaMemPoolSetAttribute(pools[dev], cudaMemPoolAttrReleaseThreshold, &keep);
     } else {
       cudaGetLastError();
-      d.pool = nullptr;
+      pools[dev] = nullptr;
     }
-    d.device = dev;
   }
-  return d;
+  return pools[dev];
 }
 
 Scratch::~Scratch() {
@@ -58,9 +77,8 @@ Scratch::~Scratch() {
 Error Scratch::alloc(size_t bytes, cudaStream_t stream) {
   stream_ = stream;
   if (bytes == 0) bytes = 16;
-  const DeviceInfo& dev = current_device_info();
-  cudaError_t e = dev.pool ? cudaMallocFromPoolAsync(&ptr_, bytes, dev.pool, stream)
-                           : cudaMallocAsync(&ptr_, bytes, stream);
+  cudaMemPool_t pool = device_pool();
+  cudaError_t e = pool ? cudaMallocFromPoolAsync(&ptr_, bytes, pool, stream) : cudaMallocAsync(&ptr_, bytes, stream);
   if (e != cudaSuccess) {
     ptr_ = nullptr;
     cudaGetLastError();

@@ -32,7 +32,6 @@ inline Error check_launch(const char* what) {
 
 struct DeviceInfo {
   int device = -1;
-  cudaMemPool_t pool = nullptr;
   int sm_count = 148;
   int max_smem_optin = 0;
   int cluster_launch = 0;
