@@ -230,6 +230,21 @@ trs_status trs_pack(const trs_view* x, trs_view* out, trs_stream stream);
  * reference's release build. */
 trs_status trs_sum(const trs_view* x, trs_view* out, trs_stream stream);
 
+/* sum() of x, like trs_sum, for callers that cannot allocate device memory
+ * while they run (a host that owns all device memory through its own arena,
+ * or a code path that must not enter the CUDA allocator).  No counterpart in
+ * the reference: it exists for those callers only.
+ *
+ * It calls no cudaMalloc, cudaFree or stream-ordered allocation: the
+ * per-block partial sums live in a static device array of 64 KiB (8192
+ * partials) that every GPU loading the library holds until the process exits.
+ * A sum that would need more partials than that is rejected with TRS_ERR_ARG.
+ * The first call on a device looks the array's address up (with that device
+ * current); make that first call before any stream capture.  All calls share
+ * the array and every call rewrites the partials it reads, but calls that
+ * overlap on the GPU (on different streams) race on it. */
+trs_status trs_sum_noalloc(const trs_view* x, trs_view* out, trs_stream stream);
+
 /* sum_axis (base.rs:1051-1107) with keepdim = 0, sum_axis_keepdim
  * (base.rs:1534-1594) with keepdim = 1. */
 trs_status trs_sum_axis(const trs_view* x, int32_t axis, int32_t keepdim,

@@ -90,6 +90,7 @@ _SIGNATURES = {
     "trs_elementwise_sum": (c_int32, [POINTER(Program), _V, _V, _V, c_void_p]),
     "trs_pack": (c_int32, [_V, _V, c_void_p]),
     "trs_sum": (c_int32, [_V, _V, c_void_p]),
+    "trs_sum_noalloc": (c_int32, [_V, _V, c_void_p]),
     "trs_sum_axis": (c_int32, [_V, c_int32, c_int32, _V, c_void_p]),
     "trs_mean_axis": (c_int32, [_V, c_int32, c_int32, _V, c_void_p]),
     "trs_max_axis": (c_int32, [_V, c_int32, _V, c_void_p]),

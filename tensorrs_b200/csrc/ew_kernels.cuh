@@ -794,7 +794,13 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
   Scratch partials;
   Acc* part = nullptr;
   const int n_part = blocks * n_launch;
-  if (want_sum) {
+  if (want_sum && sum->partials) {
+    if (sizeof(Acc) * (size_t)n_part > sum->partials_bytes)
+      return make_error(TRS_ERR_ARG, "the sum needs " + std::to_string(sizeof(Acc) * (size_t)n_part) +
+                                         " bytes of partials, more than the " +
+                                         std::to_string(sum->partials_bytes) + " provided");
+    part = static_cast<Acc*>(sum->partials);
+  } else if (want_sum) {
     Error e = partials.alloc(sizeof(Acc) * (size_t)n_part, stream);
     if (!e.ok()) return e;
     part = partials.as<Acc>();

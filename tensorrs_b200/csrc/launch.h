@@ -16,6 +16,10 @@ namespace trs {
 struct SumTarget {
   const trs_view* view = nullptr;  // rounded result
   void* raw_acc = nullptr;         // accumulator before rounding
+  // Caller-provided device memory for the per-block partial sums; when null
+  // they come from the scratch pool.
+  void* partials = nullptr;
+  size_t partials_bytes = 0;
 };
 
 // Element-wise program over `in`; writes `out` unless it is null, and the sum
