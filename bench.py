@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=ROWS,
+                    help="global rows of A and B (default 65536; smaller only for profiler captures)")
     ap.add_argument("--suite", action="store_true",
                     help="time every kernel of the path on its configuration (one JSON line each)")
     return ap.parse_args()
@@ -229,8 +231,9 @@ def run_trs(args) -> None:
         uid = (ctypes.c_uint8 * 128).from_buffer_copy(obj[0])
         abi.check(lib.trs_comm_init_rank(uid, world, rank, 120000, ctypes.byref(comm)))
 
-    assert ROWS % world == 0
-    rows = ROWS // world
+    total_rows = args.rows
+    assert total_rows % world == 0
+    rows = total_rows // world
     r0 = rank * rows
     f32 = torch.float32
     A = torch.empty((rows, COLS), dtype=f32, device="cuda")
@@ -293,7 +296,7 @@ def run_trs(args) -> None:
 
     s_val = float(S.cpu()[0])
 
-    total_bytes = workload_bytes(ROWS, COLS, world)
+    total_bytes = workload_bytes(total_rows, COLS, world)
     value = total_bytes / (ms_step * 1e-3) / 1e9
     # roofline of the dominant kernel on one GPU: bytes one launch moves / its duration
     bytes_per_launch = workload_bytes(rows, COLS, 1)
@@ -355,15 +358,16 @@ def run_trs(args) -> None:
             "warmup": max(3, args.warmup), "ms_per_step": round(ms_step, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded splitmix64 uniforms generated on device)",
-            "config": {"workload": "fma_sum: Y = A & B + c and sum(Y) (config 5); A,B f32 [65536,32768] ~U(-1,1) "
-                                   "split on dim 0, c f32 [32768], seed 4",
-                       "global_rows": ROWS, "cols": COLS, "rows_per_gpu": rows,
+            "config": {"workload": f"fma_sum: Y = A & B + c and sum(Y) (config 5); A,B f32 [{total_rows},32768] "
+                                   "~U(-1,1) split on dim 0, c f32 [32768], seed 4",
+                       "global_rows": total_rows, "cols": COLS, "rows_per_gpu": rows,
                        "bytes_per_step": total_bytes, "l2": "inputs 8 GiB/operand >> 126 MB L2, no flush",
                        "parallelism": f"dim-0 shards x{world}" + (", NCCL all-reduce of f64 partials" if world > 1 else "")},
-            "elements_per_s": round(ROWS * COLS / (ms_step * 1e-3), 1),
+            "elements_per_s": round(total_rows * COLS / (ms_step * 1e-3), 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": "ew_vec_kernel<float,4,4,write,sum> + sum_finalize_kernel (one trs_elementwise_sum call)",
+                         "kernel": "ew_stream_kernel<float, MulAdd, 3 bulk inputs, write, sum> + sum_finalize_kernel "
+                                   "(one trs_elementwise_sum call; the finalize is ~2 us of the step)",
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
             "clocks": clk,
             "gpu_launches": int(launches),
