@@ -221,15 +221,11 @@ def run_trs(args) -> None:
         import datetime
 
         import torch.distributed as dist
+        from tensorrs_b200 import sharding
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-        uid = (ctypes.c_uint8 * 128)()
-        if rank == 0:
-            abi.check(lib.trs_comm_unique_id(uid))
-        obj = [bytes(uid)]
-        dist.broadcast_object_list(obj, src=0)
-        uid = (ctypes.c_uint8 * 128).from_buffer_copy(obj[0])
-        abi.check(lib.trs_comm_init_rank(uid, world, rank, 120000, ctypes.byref(comm)))
+        communicator = sharding.Communicator(lib, rank, world, dist, timeout_ms=120000)
+        comm = communicator.handle
 
     total_rows = args.rows
     assert total_rows % world == 0
@@ -378,7 +374,7 @@ def run_trs(args) -> None:
         print(json.dumps(line), flush=True)
 
     if world > 1:
-        abi.check(lib.trs_comm_destroy(comm))
+        communicator.destroy()
         dist.barrier()
         dist.destroy_process_group()
 

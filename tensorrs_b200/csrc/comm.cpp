@@ -176,8 +176,10 @@ Error sharded_axis0(trs_comm* c, int op, const trs_view* shard, const trs_view* 
   if (ce == cudaSuccess) ce = cudaStreamSynchronize(stream);
   if (ce != cudaSuccess) return cuda_error(ce, "reading the row counts");
   int64_t total = 0, base = 0;
+  int first_rank = -1;
   for (int r = 0; r < R; ++r) {
     if (r < c->rank) base += all[r];
+    if (first_rank < 0 && all[r] > 0) first_rank = r;
     total += all[r];
   }
   if (op != kAxis0Sum && total == 0) return make_error(TRS_ERR_EMPTY_AXIS, "!!!Cannot reduce an empty axis!!!");
@@ -223,7 +225,7 @@ Error sharded_axis0(trs_comm* c, int op, const trs_view* shard, const trs_view* 
   e = nccl_call(c, n.AllGather(mine_at, part.get(), rec * (size_t)nout, ncclUint8, c->comm, stream),
                 "ncclAllGather (max records)");
   if (!e.ok()) return e;
-  return run_max_records(dt, part.get(), R, out, op == kAxis0Argmax, stream);
+  return run_max_records(dt, part.get(), R, first_rank, out, op == kAxis0Argmax, stream);
 }
 
 }  // namespace

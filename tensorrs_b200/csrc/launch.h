@@ -39,10 +39,12 @@ Error run_fill(trs_view* out, uint64_t seed, uint64_t first, double lo, double h
                cudaStream_t stream);
 
 // Sharded axis-0 reductions (shard.cu): round `n = numel(out)` all-reduced
-// accumulators into `out`; fold `nranks` gathered max records per output.
+// accumulators into `out`; fold `nranks` gathered max records per output
+// (`first_rank`: the lowest rank that holds rows, whose first row is global
+// row 0).
 Error run_accs_to_view(int dtype, const void* acc, const trs_view* out, cudaStream_t stream);
-Error run_max_records(int dtype, const void* records, int nranks, const trs_view* out, bool argmax,
-                      cudaStream_t stream);
+Error run_max_records(int dtype, const void* records, int nranks, int first_rank, const trs_view* out,
+                      bool argmax, cudaStream_t stream);
 size_t max_record_size(int dtype);
 
 // True when a program needs no transcendental (no powf, exp, tanh, ln).

@@ -36,10 +36,11 @@ accs_to_view_kernel(const typename Arith<T>::Acc* acc, OutDesc o, T* out) {
     out[out_offset(o, i)] = Arith<T>::from_acc(acc[i]);
 }
 
-// records: [nranks][n]; rank 0's `first` is the element at global index 0.
+// records: [nranks][n]; the `first` of rank `first_rank` (the lowest rank
+// holding rows) is the element at global index 0.
 template <class T>
 __global__ void __launch_bounds__(kThreads)
-max_records_kernel(const MaxRecord<T>* rec, int nranks, OutDesc o, void* out, int argmax) {
+max_records_kernel(const MaxRecord<T>* rec, int nranks, int first_rank, OutDesc o, void* out, int argmax) {
   for (uint64_t i = (uint64_t)blockIdx.x * kThreads + threadIdx.x; i < (uint64_t)o.n;
        i += (uint64_t)gridDim.x * kThreads) {
     MaxState<T> s;
@@ -52,7 +53,7 @@ max_records_kernel(const MaxRecord<T>* rec, int nranks, OutDesc o, void* out, in
       t.idx = p.idx;
       s = max_combine(s, t);
     }
-    const T first = rec[i].first;
+    const T first = rec[(uint64_t)first_rank * (uint64_t)o.n + i].first;
     if (is_nan_val(first) || s.idx < 0) { s.val = first; s.idx = 0; }
     if (argmax)
       static_cast<int64_t*>(out)[out_offset(o, i)] = s.idx;
@@ -96,17 +97,17 @@ Error run_accs_to_view(int dtype, const void* acc, const trs_view* out, cudaStre
   return check_launch("accumulator conversion kernel");
 }
 
-Error run_max_records(int dtype, const void* records, int nranks, const trs_view* out, bool argmax,
-                      cudaStream_t stream) {
+Error run_max_records(int dtype, const void* records, int nranks, int first_rank, const trs_view* out,
+                      bool argmax, cudaStream_t stream) {
   const OutDesc o = describe(out);
   if (o.n == 0) return Error{};
   const unsigned g = blocks_for(o.n);
   const int am = argmax ? 1 : 0;
   switch (dtype) {
-    case TRS_F32: max_records_kernel<float><<<g, kThreads, 0, stream>>>(static_cast<const MaxRecord<float>*>(records), nranks, o, out->data, am); break;
-    case TRS_F64: max_records_kernel<double><<<g, kThreads, 0, stream>>>(static_cast<const MaxRecord<double>*>(records), nranks, o, out->data, am); break;
-    case TRS_I32: max_records_kernel<int32_t><<<g, kThreads, 0, stream>>>(static_cast<const MaxRecord<int32_t>*>(records), nranks, o, out->data, am); break;
-    case TRS_I64: max_records_kernel<int64_t><<<g, kThreads, 0, stream>>>(static_cast<const MaxRecord<int64_t>*>(records), nranks, o, out->data, am); break;
+    case TRS_F32: max_records_kernel<float><<<g, kThreads, 0, stream>>>(static_cast<const MaxRecord<float>*>(records), nranks, first_rank, o, out->data, am); break;
+    case TRS_F64: max_records_kernel<double><<<g, kThreads, 0, stream>>>(static_cast<const MaxRecord<double>*>(records), nranks, first_rank, o, out->data, am); break;
+    case TRS_I32: max_records_kernel<int32_t><<<g, kThreads, 0, stream>>>(static_cast<const MaxRecord<int32_t>*>(records), nranks, first_rank, o, out->data, am); break;
+    case TRS_I64: max_records_kernel<int64_t><<<g, kThreads, 0, stream>>>(static_cast<const MaxRecord<int64_t>*>(records), nranks, first_rank, o, out->data, am); break;
     default: return make_error(TRS_ERR_DTYPE, "unknown dtype");
   }
   return check_launch("max record combine kernel");
