@@ -17,6 +17,8 @@
 //                   and the CTAs of a cluster split the reduced rows, and the
 //                   partials meet in shared / distributed shared memory.
 //   red_generic_kernel one thread per output, any layout.
+// Row and column reductions with enough data take the bulk-copy pipelines
+// instead (red_stream_kernel, red_cstream_kernel in reduce_kernels.cuh).
 // Float sums accumulate in f64 and round once; integer sums wrap.  Max and
 // argmax follow the reference's strict `>` scan exactly (see MaxState).
 // Every combine happens in a fixed order, so results are deterministic.
@@ -91,6 +93,85 @@ bool plan_row_stream(const RedRequest& q, RedDev* d, RedChoice* c, int nk, int n
   for (int i = 0; i < nr; ++i) set_fd(d->fr[i], (uint64_t)d->rshape[i]);
   c->variant = kRedRowStream;
   c->nb = nb;
+  return true;
+}
+
+bool cstream_available(int dtype, int mode, int nb) {
+  switch (dtype) {
+    case TRS_F32: return red_cstream_available<float>(mode, nb);
+    case TRS_F64: return red_cstream_available<double>(mode, nb);
+    case TRS_I32: return red_cstream_available<int32_t>(mode, nb);
+    case TRS_I64: return red_cstream_available<int64_t>(mode, nb);
+  }
+  return false;
+}
+
+// The bulk-copy column reduction: W (the contiguous kept dimension) at least
+// 512 bytes and a multiple of 16 bytes, every staged row segment 16-byte
+// aligned, at least 1 MiB of input, 32-bit row / output / item counts.
+// Chooses the column block width, the rows per stage and the split of the
+// reduced rows into parts so the work items fill the resident CTAs evenly.
+bool plan_col_stream(const RedRequest& q, RedDev* d, RedChoice* c, int nk_outer, int nr, int es) {
+  const int VW = 16 / es;
+  if (q.mode == kRedAffineRelu) return false;
+  if (d->W * es < 512 || (d->W * es) % 16) return false;
+  if ((uint64_t)d->total * (uint64_t)d->W * (uint64_t)es < (1ull << 20)) return false;
+  if ((uint64_t)d->total >= (1ull << 31) || (uint64_t)d->n_out >= (1ull << 31)) return false;
+  int nb = 0;
+  for (int k = 0; k < kRedOperands; ++k) {
+    d->bulk_slot[k] = -1;
+    if (!q.in[k]) continue;
+    const bool loaded = k == 0 || (q.mode == kRedSum3 && ((k == 1 && d->has_gate) || (k == 2 && d->has_mul)));
+    if (!loaded) continue;
+    if (d->wst[k] == 0 && k > 0) continue;  // constant along W: one scalar per row
+    if (d->wst[k] != 1) return false;
+    if (((uintptr_t)q.in[k]->data + (uintptr_t)(q.in[k]->offset * es)) % 16) return false;
+    for (int i = 0; i < nk_outer; ++i) if (d->kst[k][i] % VW) return false;
+    for (int i = 0; i < nr; ++i) if (d->rst[k][i] % VW) return false;
+    d->bulk_slot[k] = nb++;
+  }
+  if (d->bulk_slot[0] != 0) return false;
+  if (!cstream_available(q.in[0]->dtype, q.mode, nb)) return false;
+  d->err = async_error_word();
+  if (!d->err) return false;
+  const int64_t pitch = d->W * es < kCsMaxPitch ? d->W * es : kCsMaxPitch;
+  d->cs_pitch = (int32_t)pitch;
+  d->cs_wt = (int32_t)(pitch / es);
+  d->cs_rt = (int32_t)(kCsStageBytes / pitch < 32 ? kCsStageBytes / pitch : 32);
+  int cpad = 1;
+  while (cpad < d->cs_wt / VW) cpad *= 2;
+  d->cs_cpr_pad = cpad;
+  d->cs_ncb = (d->W + d->cs_wt - 1) / d->cs_wt;
+  const uint64_t base = (uint64_t)d->n_out_outer * (uint64_t)d->cs_ncb;
+  const DeviceInfo& dev = current_device_info();
+  int per_sm = kSmemPerSm / (cs_smem_bytes(nb) + 1024);
+  if (per_sm > 2) per_sm = 2;
+  if (per_sm < 1) per_sm = 1;
+  const uint64_t cap = (uint64_t)dev.sm_count * (uint64_t)per_sm;
+  // parts of at least 8 stages of rows keep the partials under ~6% of the input
+  uint64_t max_p = (uint64_t)d->total / (8ull * (uint64_t)d->cs_rt);
+  if (max_p < 1) max_p = 1;
+  if (max_p > 64) max_p = 64;
+  uint64_t best_p = 1;
+  double best_eff = -1.0;
+  for (uint64_t P = 1; P <= max_p; ++P) {
+    const uint64_t items = base * P;
+    const uint64_t waves = (items + cap - 1) / cap;
+    const double eff = (double)items / (double)(waves * cap);
+    if (eff > best_eff + 1e-9) { best_eff = eff; best_p = P; }
+    if (eff >= 0.9) break;
+  }
+  const uint64_t rt = (uint64_t)d->cs_rt;
+  uint64_t rp = ((uint64_t)d->total + best_p - 1) / best_p;
+  rp = (rp + rt - 1) / rt * rt;
+  d->cs_rp = (int64_t)rp;
+  d->P = (int64_t)(((uint64_t)d->total + rp - 1) / rp);
+  if (base * (uint64_t)d->P >= (1ull << 31)) return false;
+  for (int i = 0; i < nk_outer; ++i) set_fd(d->fk[i], (uint64_t)d->kshape[i]);
+  for (int i = 0; i < nr; ++i) set_fd(d->fr[i], (uint64_t)d->rshape[i]);
+  c->variant = kRedColStream;
+  c->nb = nb;
+  c->per_sm = per_sm;
   return true;
 }
 
@@ -239,6 +320,7 @@ Error plan_reduce(const RedRequest& q, RedDev* d, RedChoice* c) {
     d->wout[1] = kst[kRedOperands + 1][nk - 1];
     d->nk = nk - 1;  // the column kernel walks the remaining kept dims as "outer"
     d->n_out_outer = d->n_out / d->W;
+    if (plan_col_stream(q, d, c, nk - 1, nr, es)) return Error{};
     bool vec = (d->W % VW) == 0;
     for (int k = 0; k < kRedOperands && vec; ++k) {
       if (!q.in[k] || k > 0) continue;

@@ -86,9 +86,34 @@ struct RedDev {
   int64_t wst[kRedOperands];
   int64_t wout[2];
   int64_t n_out_outer;
+  // column stream kernel (bulk-copy pipeline over row segments of W)
+  int32_t cs_wt;       // columns per column block (its last block may be narrower)
+  int32_t cs_pitch;    // bytes between staged rows (cs_wt * element size)
+  int32_t cs_rt;       // rows per stage (<= 32)
+  int32_t cs_cpr_pad;  // 16-byte chunks per row, rounded up to a power of two
+  int64_t cs_ncb;      // column blocks
+  int64_t cs_rp;       // rows per part (a multiple of cs_rt)
 };
 
-enum RedVariant { kRedRow = 0, kRedCol = 1, kRedGeneric = 2, kRedRowStream = 3 };
+// Geometry of the column stream kernel, shared by the planner and the kernel:
+// 16 KiB stages (up to 32 staged rows of at most 2 KiB each), an 80 KiB stage
+// budget per CTA, and 16 KiB for combining the row groups' states.
+constexpr int kCsStageBytes = 16384;
+constexpr int kCsBudget = 80 * 1024;
+constexpr int kCsMaxPitch = 2048;
+constexpr int kCsCombBytes = 256 * 16 * 4;  // 256 threads x up to 4 columns x 16-byte states
+constexpr int kSmemPerSm = 228 * 1024;
+
+__host__ __device__ constexpr int cs_stages(int nb) {
+  return kCsBudget / (nb * kCsStageBytes) > 8 ? 8
+         : (kCsBudget / (nb * kCsStageBytes) < 2 ? 2 : kCsBudget / (nb * kCsStageBytes));
+}
+
+__host__ __device__ constexpr int cs_smem_bytes(int nb) {
+  return cs_stages(nb) * nb * kCsStageBytes + kCsCombBytes + 2 * cs_stages(nb) * 8;
+}
+
+enum RedVariant { kRedRow = 0, kRedCol = 1, kRedGeneric = 2, kRedRowStream = 3, kRedColStream = 4 };
 
 struct RedChoice {
   int variant = kRedGeneric;
@@ -96,6 +121,7 @@ struct RedChoice {
   int vec = 1;
   bool warp_mode = false;
   unsigned cluster = 1;
+  int per_sm = 1;  // resident CTAs per SM the planner assumed (stream kernels)
 };
 
 Error plan_reduce(const RedRequest& q, RedDev* d, RedChoice* c);
@@ -103,6 +129,8 @@ template <class T>
 Error red_launch(RedDev& d, const RedChoice& c, cudaStream_t stream);
 template <class T>
 bool red_stream_available(int mode, int nb);
+template <class T>
+bool red_cstream_available(int mode, int nb);
 Error run_reduce(const RedRequest& q, cudaStream_t stream);
 
 }  // namespace trs

@@ -4,4 +4,5 @@
 namespace trs {
 template Error red_launch<double>(RedDev&, const RedChoice&, cudaStream_t);
 template bool red_stream_available<double>(int, int);
+template bool red_cstream_available<double>(int, int);
 }  // namespace trs

@@ -4,4 +4,5 @@
 namespace trs {
 template Error red_launch<int64_t>(RedDev&, const RedChoice&, cudaStream_t);
 template bool red_stream_available<int64_t>(int, int);
+template bool red_cstream_available<int64_t>(int, int);
 }  // namespace trs

@@ -24,6 +24,7 @@
 #include <cmath>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "kernels.cuh"
 #include "reduce.h"
@@ -52,6 +53,17 @@ __device__ __forceinline__ RVec<T, V> rload(const T* p) {
     for (int i = 0; i < V; ++i) r.v[i] = __ldg(p + i);
   }
   return r;
+}
+
+// A value below every element of T (-inf, or the integer minimum): the start
+// of the strict `>` scans, which then need no "empty" test per element.  An
+// element equal to it never wins, so a scan that saw only such elements (and
+// NaNs) stays empty, and red_write resolves that as the reference does: the
+// element at index 0 (which is then that lowest value, or a NaN).
+template <class T>
+__device__ __forceinline__ T red_lowest() {
+  if constexpr (IsFloat<T>::value) return T(-INFINITY);
+  else return (T)((typename Arith<T>::Acc)1 << (sizeof(T) * 8 - 1));
 }
 
 // Accumulator state of one reduction, for every mode.
@@ -657,14 +669,51 @@ __global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) 
         if (!failed) {
           const unsigned char* stage = smem + s * NB * kRsTileBytes;
           const uint32_t chunks = len / V;
-          for (uint32_t c = ct; c < chunks; c += 32 * kRsConsumerWarps) {
+          if constexpr (MODE == kRedMax || MODE == kRedArgmax) {
+            // V independent strict `>` scans (element i of every chunk: one
+            // dependency chain each) from red_lowest, with the chunk index of
+            // the best; merged with the lower element index winning ties and
+            // folded into the item's state once per tile (tiles arrive in
+            // increasing order)
+            T tb[V];
+            uint32_t tc[V];
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+              tb[i] = red_lowest<T>();
+              tc[i] = 0xffffffffu;
+            }
+            for (uint32_t c = ct; c < chunks; c += 32 * kRsConsumerWarps) {
+              const RVec<T, V> g = *reinterpret_cast<const RVec<T, V>*>(stage + c * 16);
+#pragma unroll
+              for (int i = 0; i < V; ++i) {
+                const bool p = g.v[i] > tb[i];
+                tb[i] = p ? g.v[i] : tb[i];
+                tc[i] = p ? c : tc[i];
+              }
+            }
+            T bb = tb[0];
+            uint32_t bi = tc[0] == 0xffffffffu ? 0xffffffffu : tc[0] * V;
+#pragma unroll
+            for (int i = 1; i < V; ++i) {
+              if (tc[i] == 0xffffffffu) continue;
+              const uint32_t idx = tc[i] * V + i;
+              if (bi == 0xffffffffu || tb[i] > bb || (tb[i] == bb && idx < bi)) {
+                bb = tb[i];
+                bi = idx;
+              }
+            }
+            if (bi != 0xffffffffu && (m.idx < 0 || bb > m.val)) {
+              m.val = bb;
+              m.idx = col0 + (int64_t)bi;
+            }
+          }
+          for (uint32_t c = ct; c < chunks && MODE != kRedMax && MODE != kRedArgmax; c += 32 * kRsConsumerWarps) {
             const RVec<T, V> g = *reinterpret_cast<const RVec<T, V>*>(stage + c * 16);
             if constexpr (MODE == kRedSum || MODE == kRedMean) {
 #pragma unroll
               for (int i = 0; i < V; ++i) acc0[i] = acc0[i] + A::to_acc(g.v[i]);
             } else if constexpr (MODE == kRedMax || MODE == kRedArgmax) {
-#pragma unroll
-              for (int i = 0; i < V; ++i) max_push(m, g.v[i], col0 + (int64_t)c * V + i);
+              // handled above
             } else if constexpr (MODE == kRedSum3) {
               RVec<T, V> a1, a2;
               const int s1 = d.bulk_slot[1], s2 = d.bulk_slot[2];
@@ -741,6 +790,265 @@ __global__ void __launch_bounds__(256) red_parts_finalize(const RedDev d) {
   }
 }
 
+// --------------------------------------------------------------------------
+// red_cstream_kernel: reductions whose innermost KEPT dimension W is
+// contiguous (sum/max/argmax over axis 0 of a row-major matrix, and the
+// un-broadcast of a [rows, W] gradient), on the bulk-copy pipeline.
+// W is cut into column blocks of cs_wt columns (<= 2 KiB of a row); the
+// reduced rows of one (outer kept index, column block) are cut into parts of
+// cs_rp rows.  A work item is (outer, part, block).  Per stage the producer
+// warp arms the `full` mbarrier and its lanes issue one cp.async.bulk per
+// staged row (up to cs_rt <= 32 rows of one block) and bulk operand.  The 8
+// consumer warps own 16-byte column chunks (thread t: chunk t % cs_cpr_pad,
+// row group t / cs_cpr_pad) and fold the rows of their group in increasing
+// order; at the end of an item the row groups are combined in group order and
+// the outputs (or, with several parts, per-part partials that
+// red_cparts_finalize folds in part order) are written.  Failure handling is
+// the row pipeline's: bounded waits, a failed CTA walks its schedule without
+// waiting, drains its copies and sets the error word.
+
+// Offsets of reduced row r over every reduced dimension.
+__device__ __forceinline__ void cs_row(const RedDev& d, uint32_t r, int64_t* off) {
+#pragma unroll
+  for (int k = 0; k < kRedOperands; ++k) off[k] = 0;
+  for (int q = d.nr - 1; q >= 0; --q) {
+    uint32_t c = r;
+    if (q > 0) {
+      const FastDiv f = fd3(d.fr[q]);
+      const uint32_t nq = fdiv(r, f);
+      c = r - nq * f.d;
+      r = nq;
+    }
+#pragma unroll
+    for (int k = 0; k < kRedOperands; ++k) off[k] += (int64_t)c * d.rst[k][q];
+  }
+}
+
+template <int MODE>
+struct CsIsMax {
+  static constexpr bool value = MODE == kRedMax || MODE == kRedArgmax;
+};
+
+// The partial of one output of one part.
+template <class T, int MODE>
+using CsPart = typename std::conditional<CsIsMax<MODE>::value, MaxState<T>, typename Arith<T>::Acc>::type;
+
+template <class T, int MODE, int NB>
+__global__ void __launch_bounds__(kRsThreads) red_cstream_kernel(const RedDev d) {
+  using A = Arith<T>;
+  using Acc = typename A::Acc;
+  constexpr int V = 16 / (int)sizeof(T);
+  constexpr int S = cs_stages(NB);
+  constexpr bool kMax = CsIsMax<MODE>::value;
+  using Part = CsPart<T, MODE>;
+  extern __shared__ __align__(128) unsigned char smem[];
+  Part* comb = reinterpret_cast<Part*>(smem + S * NB * kCsStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * NB * kCsStageBytes + kCsCombBytes);
+  uint64_t* empty = full + S;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t ncb = (uint32_t)d.cs_ncb;
+  const uint32_t total = (uint32_t)d.total;
+  const uint32_t rp = (uint32_t)d.cs_rp, rt = (uint32_t)d.cs_rt;
+  const uint32_t P = (uint32_t)d.P;
+  const uint32_t n_items = (uint32_t)d.n_out_outer * P * ncb;
+  const int64_t W = d.W;
+  const int wt = d.cs_wt, pitch = d.cs_pitch;
+  const T* x0 = static_cast<const T*>(d.in[0]);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kRsConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  bool failed = false;
+  uint32_t issued = 0;
+  if (warp == 0) {
+    uint32_t qn = 0;
+    for (uint32_t it = blockIdx.x; it < n_items; it += gridDim.x) {
+      const uint32_t cb = it % ncb, op = it / ncb;
+      const uint32_t part = op % P, o = op / P;
+      int64_t koff[kRedOperands], ooff[2];
+      rs_kept(d, o, koff, ooff);
+      const int64_t col0 = (int64_t)cb * wt;
+      const int64_t wl = W - col0 < wt ? W - col0 : wt;
+      const uint32_t bytes = (uint32_t)wl * (uint32_t)sizeof(T);
+      const uint32_t r_end = part * rp + rp < total ? part * rp + rp : total;
+      for (uint32_t r0 = part * rp; r0 < r_end; r0 += rt, ++qn) {
+        const int s = (int)(qn % S);
+        if (!failed && qn >= (uint32_t)S) {
+          bool ok = true;
+          if (lane == 0) ok = mbar_wait(&empty[s], ((qn / S) - 1) & 1u);
+          if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) failed = true;
+        }
+        if (failed) continue;
+        const uint32_t nrows = r_end - r0 < rt ? r_end - r0 : rt;
+        if (lane == 0) {
+          fence_proxy_async();
+          mbar_arrive_expect_tx(&full[s], nrows * bytes * NB);
+        }
+        __syncwarp();
+        if ((uint32_t)lane < nrows) {
+          int64_t roff[kRedOperands];
+          cs_row(d, r0 + lane, roff);
+#pragma unroll
+          for (int k = 0; k < kRedOperands; ++k) {
+            const int slot = d.bulk_slot[k];
+            if (slot >= 0)
+              bulk_g2s(smem + (s * NB + slot) * kCsStageBytes + lane * pitch,
+                       static_cast<const T*>(d.in[k]) + koff[k] + roff[k] + col0, bytes, &full[s]);
+          }
+        }
+        issued = qn + 1;
+      }
+    }
+  } else {
+    const int ct = threadIdx.x - 32;
+    const int cpad = d.cs_cpr_pad;
+    const int c = ct & (cpad - 1), g = ct / cpad, G = (32 * kRsConsumerWarps) / cpad;
+    uint32_t qn = 0;
+    for (uint32_t it = blockIdx.x; it < n_items; it += gridDim.x) {
+      const uint32_t cb = it % ncb, op = it / ncb;
+      const uint32_t part = op % P, o = op / P;
+      int64_t koff[kRedOperands], ooff[2];
+      rs_kept(d, o, koff, ooff);
+      const int64_t col0 = (int64_t)cb * wt;
+      const int64_t wl = W - col0 < wt ? W - col0 : wt;
+      const bool mine = (int64_t)c * V < wl;
+      const uint32_t r_end = part * rp + rp < total ? part * rp + rp : total;
+      Acc acc[V];
+      T tb[V];          // strict `>` scan per column from red_lowest,
+      uint32_t tr[V];   // with the row of the best (~0: none yet)
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        acc[i] = Acc(0);
+        tb[i] = red_lowest<T>();
+        tr[i] = 0xffffffffu;
+      }
+      for (uint32_t r0 = part * rp; r0 < r_end; r0 += rt, ++qn) {
+        const int s = (int)(qn % S);
+        const uint32_t nrows = r_end - r0 < rt ? r_end - r0 : rt;
+        if (!failed && !__all_sync(0xffffffffu, mbar_wait(&full[s], (qn / S) & 1u))) failed = true;
+        if (!failed && mine) {
+          const unsigned char* stage = smem + s * NB * kCsStageBytes + c * 16;
+          for (uint32_t j = g; j < nrows; j += G) {
+            const RVec<T, V> v = *reinterpret_cast<const RVec<T, V>*>(stage + j * pitch);
+            if constexpr (MODE == kRedSum || MODE == kRedMean) {
+#pragma unroll
+              for (int i = 0; i < V; ++i) acc[i] = acc[i] + A::to_acc(v.v[i]);
+            } else if constexpr (kMax) {
+#pragma unroll
+              for (int i = 0; i < V; ++i) {
+                const bool p = v.v[i] > tb[i];
+                tb[i] = p ? v.v[i] : tb[i];
+                tr[i] = p ? r0 + j : tr[i];
+              }
+            } else {  // kRedSum3: gate / mul staged (slot >= 0) or constant along W
+              const int s1 = d.bulk_slot[1], s2 = d.bulk_slot[2];
+              T sc1 = T(0), sc2 = T(0);
+              RVec<T, V> a1, a2;
+              if (d.has_gate) {
+                if (s1 >= 0) a1 = *reinterpret_cast<const RVec<T, V>*>(stage + s1 * kCsStageBytes + j * pitch);
+                else { int64_t ro[kRedOperands]; cs_row(d, r0 + j, ro); sc1 = __ldg(static_cast<const T*>(d.in[1]) + koff[1] + ro[1]); }
+              }
+              if (d.has_mul) {
+                if (s2 >= 0) a2 = *reinterpret_cast<const RVec<T, V>*>(stage + s2 * kCsStageBytes + j * pitch);
+                else { int64_t ro[kRedOperands]; cs_row(d, r0 + j, ro); sc2 = __ldg(static_cast<const T*>(d.in[2]) + koff[2] + ro[2]); }
+              }
+#pragma unroll
+              for (int i = 0; i < V; ++i) {
+                T x = v.v[i];
+                if (d.has_gate) {
+                  const T gt = s1 >= 0 ? a1.v[i] : sc1;
+                  x = A::mul(x, gt > T(0) ? T(1) : T(0));
+                }
+                if (d.has_mul) x = A::mul(x, s2 >= 0 ? a2.v[i] : sc2);
+                acc[i] = acc[i] + A::to_acc(x);
+              }
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+      // row groups -> shared memory, folded in group order by group 0
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        if constexpr (kMax) {
+          MaxState<T> m;
+          m.val = tb[i];
+          m.idx = tr[i] == 0xffffffffu ? -1 : (int64_t)tr[i];
+          comb[ct * V + i] = m;
+        } else {
+          comb[ct * V + i] = acc[i];
+        }
+      }
+      named_sync_consumers();
+      if (g == 0 && mine && !failed) {
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+          const int64_t w = col0 + (int64_t)c * V + i;
+          if (w - col0 >= wl) break;
+          Part t = comb[c * V + i];
+          for (int gg = 1; gg < G; ++gg) {
+            const Part u = comb[(gg * cpad + c) * V + i];
+            if constexpr (kMax) t = max_combine(t, u);
+            else t = t + u;
+          }
+          const uint64_t u_out = (uint64_t)o * (uint64_t)W + (uint64_t)w;
+          if (P == 1) {
+            RedAcc<T> ra = red_init<T>();
+            if constexpr (kMax) ra.m = t;
+            else ra.s0 = t;
+            int64_t oo[2] = {ooff[0] + w * d.wout[0], ooff[1] + w * d.wout[1]};
+            red_write<T>(d, ra, oo, x0, koff[0] + w * d.wst[0]);
+          } else {
+            static_cast<Part*>(d.parts)[(uint64_t)part * (uint64_t)d.n_out + u_out] = t;
+          }
+        }
+      }
+      named_sync_consumers();
+    }
+  }
+  if (__syncthreads_or(failed)) {
+    if (threadIdx.x == 0) {
+      atomicOr(d.err, kAsyncWaitTimeout);
+      const uint32_t start = issued > (uint32_t)S ? issued - S : 0;
+      for (uint32_t k = start; k < issued; ++k) mbar_wait(&full[k % S], (k / S) & 1u);
+    }
+    __syncthreads();
+  }
+}
+
+// Folds the P per-part partials of every output in part order and writes it.
+template <class T, int MODE>
+__global__ void __launch_bounds__(256) red_cparts_finalize(const RedDev d) {
+  using Part = CsPart<T, MODE>;
+  const T* x0 = static_cast<const T*>(d.in[0]);
+  const Part* parts = static_cast<const Part*>(d.parts);
+  const uint64_t n = (uint64_t)d.n_out;
+  for (uint64_t u = (uint64_t)blockIdx.x * 256 + threadIdx.x; u < n; u += (uint64_t)gridDim.x * 256) {
+    Part t = parts[u];
+    for (int64_t p = 1; p < d.P; ++p) {
+      const Part v = parts[(uint64_t)p * n + u];
+      if constexpr (CsIsMax<MODE>::value) t = max_combine(t, v);
+      else t = t + v;
+    }
+    const uint64_t o = u / (uint64_t)d.W;
+    const int64_t w = (int64_t)(u - o * (uint64_t)d.W);
+    int64_t koff[kRedOperands], ooff[2];
+    kept_offsets(d, o, koff, ooff);
+    RedAcc<T> ra = red_init<T>();
+    if constexpr (CsIsMax<MODE>::value) ra.m = t;
+    else ra.s0 = t;
+    int64_t oo[2] = {ooff[0] + w * d.wout[0], ooff[1] + w * d.wout[1]};
+    red_write<T>(d, ra, oo, x0, koff[0] + w * d.wst[0]);
+  }
+}
+
 }  // namespace rk
 
 namespace rk {
@@ -762,6 +1070,42 @@ const void* pick_red_stream(int mode, int nb) {
     if (mode == kRedSum3 && nb == 2) return stream_kernel_nb<T, kRedSum3, 2>();
     if (mode == kRedSum3 && nb == 3) return stream_kernel_nb<T, kRedSum3, 3>();
     if (mode == kRedAffineRelu && nb == 2) return stream_kernel_nb<T, kRedAffineRelu, 2>();
+  }
+  return nullptr;
+}
+
+template <class T, int MODE, int NB>
+const void* cstream_kernel_nb() {
+  return (const void*)red_cstream_kernel<T, MODE, NB>;
+}
+
+// The column stream kernel for (mode, bulk operands), or null.
+template <class T>
+const void* pick_red_cstream(int mode, int nb) {
+  if (mode == kRedSum && nb == 1) return cstream_kernel_nb<T, kRedSum, 1>();
+  if (mode == kRedMax && nb == 1) return cstream_kernel_nb<T, kRedMax, 1>();
+  if (mode == kRedArgmax && nb == 1) return cstream_kernel_nb<T, kRedArgmax, 1>();
+  if constexpr (IsFloat<T>::value) {
+    if (mode == kRedMean && nb == 1) return cstream_kernel_nb<T, kRedMean, 1>();
+    if (mode == kRedSum3 && nb == 1) return cstream_kernel_nb<T, kRedSum3, 1>();
+    if (mode == kRedSum3 && nb == 2) return cstream_kernel_nb<T, kRedSum3, 2>();
+    if (mode == kRedSum3 && nb == 3) return cstream_kernel_nb<T, kRedSum3, 3>();
+  }
+  return nullptr;
+}
+
+template <class T>
+const void* pick_red_cfinalize(int mode) {
+  switch (mode) {
+    case kRedSum: return (const void*)red_cparts_finalize<T, kRedSum>;
+    case kRedMax: return (const void*)red_cparts_finalize<T, kRedMax>;
+    case kRedArgmax: return (const void*)red_cparts_finalize<T, kRedArgmax>;
+  }
+  if constexpr (IsFloat<T>::value) {
+    switch (mode) {
+      case kRedMean: return (const void*)red_cparts_finalize<T, kRedMean>;
+      case kRedSum3: return (const void*)red_cparts_finalize<T, kRedSum3>;
+    }
   }
   return nullptr;
 }
@@ -788,6 +1132,11 @@ const void* pick_red_finalize(int mode) {
 template <class T>
 bool red_stream_available(int mode, int nb) {
   return rk::pick_red_stream<T>(mode, nb) != nullptr;
+}
+
+template <class T>
+bool red_cstream_available(int mode, int nb) {
+  return rk::pick_red_cstream<T>(mode, nb) != nullptr;
 }
 
 template <class T>
@@ -833,6 +1182,42 @@ Error red_launch(RedDev& d, const RedChoice& c, cudaStream_t stream) {
       ce = cudaLaunchKernel(fk, dim3(fg), dim3(256), args, 0, stream);
       if (ce != cudaSuccess) return cuda_error(ce, "partials finalize launch");
       return check_launch("reduction finalize kernel");
+    }
+    return Error{};
+  }
+  if (c.variant == kRedColStream) {
+    const void* k = pick_red_cstream<T>(d.mode, c.nb);
+    if (!k) return make_error(TRS_ERR_ARG, "no column stream reduction kernel for this mode");
+    const int smem = cs_smem_bytes(c.nb);
+    static std::mutex mu;
+    {
+      std::lock_guard<std::mutex> lock(mu);
+      if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        return cuda_error(cudaGetLastError(), "cudaFuncSetAttribute");
+    }
+    const uint64_t items = (uint64_t)d.n_out_outer * (uint64_t)d.P * (uint64_t)d.cs_ncb;
+    const uint64_t cap = (uint64_t)dev.sm_count * (uint64_t)c.per_sm;
+    const unsigned grid = (unsigned)(items < cap ? items : cap);
+    Scratch parts;
+    if (d.P > 1) {
+      const size_t psz = (d.mode == kRedMax || d.mode == kRedArgmax) ? sizeof(MaxState<T>)
+                                                                      : sizeof(typename Arith<T>::Acc);
+      Error e = parts.alloc(psz * (size_t)d.n_out * (size_t)d.P, stream);
+      if (!e.ok()) return e;
+      d.parts = parts.get();
+    }
+    void* args[] = {(void*)&d};
+    cudaError_t ce = cudaLaunchKernel(k, dim3(grid), dim3(kRsThreads), args, (size_t)smem, stream);
+    if (ce != cudaSuccess) return cuda_error(ce, "column stream reduction launch");
+    Error e = check_launch("column stream reduction kernel");
+    if (!e.ok()) return e;
+    if (d.P > 1) {
+      const void* fk = pick_red_cfinalize<T>(d.mode);
+      const uint64_t fb = ((uint64_t)d.n_out + 255) / 256;
+      const unsigned fg = (unsigned)(fb < (uint64_t)dev.sm_count * 8 ? fb : (uint64_t)dev.sm_count * 8);
+      ce = cudaLaunchKernel(fk, dim3(fg), dim3(256), args, 0, stream);
+      if (ce != cudaSuccess) return cuda_error(ce, "column partials finalize launch");
+      return check_launch("column reduction finalize kernel");
     }
     return Error{};
   }
