@@ -56,6 +56,8 @@ def parse_args():
                     help="global rows of A and B (default 65536; smaller only for profiler captures)")
     ap.add_argument("--suite", action="store_true",
                     help="time every kernel of the path on its configuration (one JSON line each)")
+    ap.add_argument("--only", default=None,
+                    help="with --suite: only the entries whose 'config: kernel' name contains this text")
     return ap.parse_args()
 
 
@@ -384,9 +386,15 @@ def run_trs(args) -> None:
 # ---------------------------------------------------------------------------
 def run_suite(args) -> None:
     """Times each hot-path kernel on the configuration it serves (SURVEY
-    configs 1-5), with CUDA events around each launch, an L2 flush (a 256 MiB
-    write) before every rep of the L2-resident config 1, and reports achieved
-    GB/s of algorithmic bytes against the measured HBM peak."""
+    configs 1-5), with CUDA events around each launch, and reports achieved
+    GB/s of algorithmic bytes against the measured HBM peak.
+
+    Before every rep a 256 MiB buffer is written and then read: the write
+    evicts the inputs from L2 (so the L2-resident config 1 starts cold), the
+    read makes the flush's dirty lines drain to HBM before the timed launch
+    instead of inside it.  `--only TEXT` keeps the entries whose
+    "config: kernel" name contains TEXT (for profiler captures), `--warmup`
+    sets the untimed reps before the timed ones."""
     import torch
 
     from tensorrs_b200 import abi, device
@@ -397,34 +405,42 @@ def run_suite(args) -> None:
     sh = torch.cuda.current_stream().cuda_stream
     flush_buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
     f32 = torch.float32
+    only = args.only
+    warm = max(0, args.warmup)
+
+    def want(cfg, name):
+        return only is None or only in f"{cfg}: {name}"
 
     def t(*shape):
         return torch.empty(shape, dtype=f32, device="cuda")
 
-    def timed(fn, reps, flush):
-        # the 256 MiB flush write also keeps the GPU busy while the host
-        # enqueues the timed launch, so host overhead stays outside the events
+    def timed(fn, reps):
         times = []
-        for i in range(reps + 3):
+        for i in range(reps + warm):
             flush_buf.fill_(float(i))
+            flush_buf.sum()
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
             fn()
             e1.record()
             e1.synchronize()
-            if i >= 3:
+            if i >= warm:
                 times.append(e0.elapsed_time(e1))
         return float(np.median(times))
 
-    def report(cfg, name, nbytes, ms, flush=False, extra=None):
+    def run(cfg, name, nbytes, fn):
+        if not want(cfg, name):
+            return
+        ms = timed(fn, reps)
         gbps = nbytes / (ms * 1e-3) / 1e9
         line = {"suite": cfg, "kernel": name, "bytes": int(nbytes), "ms": round(ms, 4), "GBps": round(gbps, 1),
                 "frac_of_peak": round(gbps / peak, 4), "peak": peak, "peak_source": peak_kind,
-                "l2": "flushed before each rep (256 MiB write)" + ("" if flush else "; inputs exceed L2 anyway")}
-        if extra:
-            line.update(extra)
+                "l2": "256 MiB written then read before each rep"}
         print(json.dumps(line), flush=True)
+
+    def any_of(cfg, names):
+        return any(want(cfg, n) for n in names)
 
     def C(st):
         abi.check(st)
@@ -432,96 +448,104 @@ def run_suite(args) -> None:
     V = device.view_of
     reps = max(5, args.steps)
     # config 1: A[1024,1024] + b[1024]; sum_axis(1); sum()
-    A = device.fill_uniform(t(1024, 1024), 0)
-    b = device.fill_uniform(t(1024), 0, first=1 << 20)
-    Y = t(1024, 1024)
-    r = t(1024)
-    s = t(1)
-    va, vb, vy, vr, vs = V(A), V(b), V(Y), V(r), V(s)
-    p2 = abi.program(2, abi.ADD)
-    ins = abi.views_array([va, vb])
-    ms = timed(lambda: C(lib.trs_elementwise(ctypes.byref(p2), ins, ctypes.byref(vy), sh)), reps, True)
-    report("config1", "bias add A[1024,1024] + b[1024]", 8392704, ms, True)
-    ms = timed(lambda: C(lib.trs_sum_axis(ctypes.byref(va), 1, 0, ctypes.byref(vr), sh)), reps, True)
-    report("config1", "sum_axis(1) of A[1024,1024]", 4194304 + 4096, ms, True)
-    ms = timed(lambda: C(lib.trs_sum(ctypes.byref(va), ctypes.byref(vs), sh)), reps, True)
-    report("config1", "sum() of A[1024,1024]", 4194304 + 4, ms, True)
-    del A, b, Y
+    c1 = ["bias add A[1024,1024] + b[1024]", "sum_axis(1) of A[1024,1024]", "sum() of A[1024,1024]"]
+    if any_of("config1", c1):
+        A = device.fill_uniform(t(1024, 1024), 0)
+        b = device.fill_uniform(t(1024), 0, first=1 << 20)
+        Y = t(1024, 1024)
+        r = t(1024)
+        s = t(1)
+        va, vb, vy, vr, vs = V(A), V(b), V(Y), V(r), V(s)
+        p2 = abi.program(2, abi.ADD)
+        ins = abi.views_array([va, vb])
+        run("config1", c1[0], 8392704, lambda: C(lib.trs_elementwise(ctypes.byref(p2), ins, ctypes.byref(vy), sh)))
+        run("config1", c1[1], 4194304 + 4096, lambda: C(lib.trs_sum_axis(ctypes.byref(va), 1, 0, ctypes.byref(vr), sh)))
+        run("config1", c1[2], 4194304 + 4, lambda: C(lib.trs_sum(ctypes.byref(va), ctypes.byref(vs), sh)))
+        del A, b, Y
     # config 2: C = A & B^T, sigmoid
-    n = 4096
-    A = device.fill_normal(t(n, n), 1)
-    B = device.fill_normal(t(n, n), 1, first=n * n)
-    Y = t(n, n)
-    vbt = V(B, [n, n], [1, n], 0)
-    nb = n * n * 4
-    pm = abi.program(2, abi.MUL)
-    pms = abi.program(2, abi.MUL, epilogue="sigmoid")
-    ins = abi.views_array([V(A), vbt])
-    ms = timed(lambda: C(lib.trs_elementwise(ctypes.byref(pm), ins, ctypes.byref(V(Y)), sh)), reps, False)
-    report("config2", "A & B^T (B^T strided view)", 3 * nb, ms)
-    ms = timed(lambda: C(lib.trs_elementwise(ctypes.byref(pms), ins, ctypes.byref(V(Y)), sh)), reps, False)
-    report("config2", "sigmoid(A & B^T) fused", 3 * nb, ms)
-    params = (abi.Scalar * 2)()
-    ms = timed(lambda: C(lib.trs_unary(abi.UNOPS["sigmoid"], ctypes.byref(V(A)), params, ctypes.byref(V(Y)), sh)),
-               reps, False)
-    report("config2", "sigmoid standalone [4096,4096]", 2 * nb, ms)
-    del A, B, Y
+    c2 = ["A & B^T (B^T strided view)", "sigmoid(A & B^T) fused", "sigmoid standalone [4096,4096]"]
+    if any_of("config2", c2):
+        n = 4096
+        A = device.fill_normal(t(n, n), 1)
+        B = device.fill_normal(t(n, n), 1, first=n * n)
+        Y = t(n, n)
+        vbt = V(B, [n, n], [1, n], 0)
+        nb = n * n * 4
+        pm = abi.program(2, abi.MUL)
+        pms = abi.program(2, abi.MUL, epilogue="sigmoid")
+        ins = abi.views_array([V(A), vbt])
+        vy = V(Y)
+        run("config2", c2[0], 3 * nb, lambda: C(lib.trs_elementwise(ctypes.byref(pm), ins, ctypes.byref(vy), sh)))
+        run("config2", c2[1], 3 * nb, lambda: C(lib.trs_elementwise(ctypes.byref(pms), ins, ctypes.byref(vy), sh)))
+        params = (abi.Scalar * 2)()
+        va = V(A)
+        run("config2", c2[2], 2 * nb,
+            lambda: C(lib.trs_unary(abi.UNOPS["sigmoid"], ctypes.byref(va), params, ctypes.byref(vy), sh)))
+        del A, B, Y
     # config 3: X[8192,16384] axis reductions and softmax
     R, Cc = 8192, 16384
-    X = device.fill_normal(t(R, Cc), 2)
-    vx = V(X)
-    xb = R * Cc * 4
-    r1, r0 = t(R), t(Cc)
-    i1, i0 = torch.empty(R, dtype=torch.int64, device="cuda"), torch.empty(Cc, dtype=torch.int64, device="cuda")
-    for axis, out_f, out_i, nout in [(1, r1, i1, R), (0, r0, i0, Cc)]:
-        vo, vi = V(out_f), V(out_i)
-        ms = timed(lambda: C(lib.trs_sum_axis(ctypes.byref(vx), axis, 0, ctypes.byref(vo), sh)), reps, False)
-        report("config3", f"sum_axis({axis}) of X[8192,16384]", xb + 4 * nout, ms)
-        ms = timed(lambda: C(lib.trs_mean_axis(ctypes.byref(vx), axis, 0, ctypes.byref(vo), sh)), reps, False)
-        report("config3", f"mean over axis {axis}", xb + 4 * nout, ms)
-        ms = timed(lambda: C(lib.trs_max_axis(ctypes.byref(vx), axis, ctypes.byref(vo), sh)), reps, False)
-        report("config3", f"max_axis({axis})", xb + 4 * nout, ms)
-        ms = timed(lambda: C(lib.trs_argmax_axis(ctypes.byref(vx), axis, ctypes.byref(vi), sh)), reps, False)
-        report("config3", f"argmax_axis({axis})", xb + 8 * nout, ms)
-    Ys = t(R, Cc)
-    ms = timed(lambda: C(lib.trs_softmax_lastdim(ctypes.byref(vx), ctypes.byref(V(Ys)), sh)), reps, False)
-    report("config3", "softmax over axis 1", 2 * xb, ms)
-    del X, Ys
+    c3 = [k for axis in (1, 0) for k in (f"sum_axis({axis}) of X[8192,16384]", f"mean over axis {axis}",
+                                         f"max_axis({axis})", f"argmax_axis({axis})")] + ["softmax over axis 1"]
+    if any_of("config3", c3):
+        X = device.fill_normal(t(R, Cc), 2)
+        vx = V(X)
+        xb = R * Cc * 4
+        r1, r0 = t(R), t(Cc)
+        i1, i0 = torch.empty(R, dtype=torch.int64, device="cuda"), torch.empty(Cc, dtype=torch.int64, device="cuda")
+        for axis, out_f, out_i, nout in [(1, r1, i1, R), (0, r0, i0, Cc)]:
+            vo, vi = V(out_f), V(out_i)
+            run("config3", f"sum_axis({axis}) of X[8192,16384]", xb + 4 * nout,
+                lambda: C(lib.trs_sum_axis(ctypes.byref(vx), axis, 0, ctypes.byref(vo), sh)))
+            run("config3", f"mean over axis {axis}", xb + 4 * nout,
+                lambda: C(lib.trs_mean_axis(ctypes.byref(vx), axis, 0, ctypes.byref(vo), sh)))
+            run("config3", f"max_axis({axis})", xb + 4 * nout,
+                lambda: C(lib.trs_max_axis(ctypes.byref(vx), axis, ctypes.byref(vo), sh)))
+            run("config3", f"argmax_axis({axis})", xb + 8 * nout,
+                lambda: C(lib.trs_argmax_axis(ctypes.byref(vx), axis, ctypes.byref(vi), sh)))
+        Ys = t(R, Cc)
+        vys = V(Ys)
+        run("config3", "softmax over axis 1", 2 * xb,
+            lambda: C(lib.trs_softmax_lastdim(ctypes.byref(vx), ctypes.byref(vys), sh)))
+        del X, Ys
     # config 4: relu(X & s + b) forward; scale/bias gradients backward
-    N, Ch, H, W = 64, 256, 56, 56
-    X = device.fill_normal(t(N, Ch, H, W), 3)
-    G = device.fill_normal(t(N, Ch, H, W), 3, first=N * Ch * H * W)
-    sc = device.fill_uniform(t(1, Ch, 1, 1), 3, 0.5, 1.5)
-    bi = device.fill_uniform(t(1, Ch, 1, 1), 3, -0.1, 0.1, first=Ch)
-    Y = t(N, Ch, H, W)
-    gs, gb = t(1, Ch, 1, 1), t(1, Ch, 1, 1)
-    xb = N * Ch * H * W * 4
-    pf = abi.program(3, abi.MUL, abi.ADD, "relu")
-    ins = abi.views_array([V(X), V(sc), V(bi)])
-    ms = timed(lambda: C(lib.trs_elementwise(ctypes.byref(pf), ins, ctypes.byref(V(Y)), sh)), reps, False)
-    report("config4", "relu(X & s + b) fused forward", 2 * xb + 2 * 4 * Ch, ms)
-    ms = timed(lambda: C(lib.trs_affine_relu_backward(ctypes.byref(V(G)), ctypes.byref(V(X)), ctypes.byref(V(sc)),
-                                                      ctypes.byref(V(bi)), ctypes.byref(V(gs)), ctypes.byref(V(gb)),
-                                                      sh)), reps, False)
-    report("config4", "scale+bias grads of relu(X & s + b), fused", 2 * xb + 4 * 4 * Ch, ms)
-    tgt = (ctypes.c_int64 * 4)(1, Ch, 1, 1)
-    ms = timed(lambda: C(lib.trs_reduce_broadcast_grad(ctypes.byref(V(G)), tgt, 4, ctypes.byref(V(gb)), sh)),
-               reps, False)
-    report("config4", "reduce_broadcast_grad g -> [1,256,1,1]", xb + 4 * Ch, ms)
-    del X, G, Y
+    c4 = ["relu(X & s + b) fused forward", "scale+bias grads of relu(X & s + b), fused",
+          "reduce_broadcast_grad g -> [1,256,1,1]"]
+    if any_of("config4", c4):
+        N, Ch, H, W = 64, 256, 56, 56
+        X = device.fill_normal(t(N, Ch, H, W), 3)
+        G = device.fill_normal(t(N, Ch, H, W), 3, first=N * Ch * H * W)
+        sc = device.fill_uniform(t(1, Ch, 1, 1), 3, 0.5, 1.5)
+        bi = device.fill_uniform(t(1, Ch, 1, 1), 3, -0.1, 0.1, first=Ch)
+        Y = t(N, Ch, H, W)
+        gs, gb = t(1, Ch, 1, 1), t(1, Ch, 1, 1)
+        xb = N * Ch * H * W * 4
+        pf = abi.program(3, abi.MUL, abi.ADD, "relu")
+        ins = abi.views_array([V(X), V(sc), V(bi)])
+        vX, vG, vsc, vbi, vY, vgs, vgb = V(X), V(G), V(sc), V(bi), V(Y), V(gs), V(gb)
+        run("config4", c4[0], 2 * xb + 2 * 4 * Ch,
+            lambda: C(lib.trs_elementwise(ctypes.byref(pf), ins, ctypes.byref(vY), sh)))
+        run("config4", c4[1], 2 * xb + 4 * 4 * Ch,
+            lambda: C(lib.trs_affine_relu_backward(ctypes.byref(vG), ctypes.byref(vX), ctypes.byref(vsc),
+                                                   ctypes.byref(vbi), ctypes.byref(vgs), ctypes.byref(vgb), sh)))
+        tgt = (ctypes.c_int64 * 4)(1, Ch, 1, 1)
+        run("config4", c4[2], xb + 4 * Ch,
+            lambda: C(lib.trs_reduce_broadcast_grad(ctypes.byref(vG), tgt, 4, ctypes.byref(vgb), sh)))
+        del X, G, Y
     # config 5 (one GPU): the headline step
-    rows = ROWS
-    A = device.fill_uniform(t(rows, COLS), SEED_A)
-    B = device.fill_uniform(t(rows, COLS), SEED_B)
-    c = device.fill_uniform(t(COLS), SEED_C)
-    Y = t(rows, COLS)
-    p3 = abi.program(3, abi.MUL, abi.ADD)
-    ins = abi.views_array([V(A), V(B), V(c)])
-    ms = timed(lambda: C(lib.trs_elementwise_sum(ctypes.byref(p3), ins, ctypes.byref(V(Y)), ctypes.byref(V(s)), sh)),
-               reps, False)
-    report("config5", "Y = A & B + c and sum(Y) fused", workload_bytes(rows, COLS, 1), ms)
-    ms = timed(lambda: C(lib.trs_sum(ctypes.byref(V(Y)), ctypes.byref(V(s)), sh)), reps, False)
-    report("config5", "sum(Y) alone [65536,32768]", rows * COLS * 4 + 4, ms)
+    c5 = ["Y = A & B + c and sum(Y) fused", "sum(Y) alone [65536,32768]"]
+    if any_of("config5", c5):
+        rows = args.rows
+        A = device.fill_uniform(t(rows, COLS), SEED_A)
+        B = device.fill_uniform(t(rows, COLS), SEED_B)
+        c = device.fill_uniform(t(COLS), SEED_C)
+        Y = t(rows, COLS)
+        s = t(1)
+        p3 = abi.program(3, abi.MUL, abi.ADD)
+        ins = abi.views_array([V(A), V(B), V(c)])
+        vY, vs = V(Y), V(s)
+        run("config5", c5[0], workload_bytes(rows, COLS, 1),
+            lambda: C(lib.trs_elementwise_sum(ctypes.byref(p3), ins, ctypes.byref(vY), ctypes.byref(vs), sh)))
+        run("config5", c5[1], rows * COLS * 4 + 4, lambda: C(lib.trs_sum(ctypes.byref(vY), ctypes.byref(vs), sh)))
 
 
 def main():
