@@ -5,16 +5,14 @@
 // into an FMA, so each step rounds exactly once as the reference's separate
 // Rust operations do.  The library is also built with -fmad=false.
 //
-// Transcendentals are out-of-line calls so the unrolled element-wise kernels
-// carry one copy of each (pow_e_inline is the inlined form for the softmax
-// kernel, where it is the whole inner loop).
-//
 // Transcendentals: the reference calls glibc (expf, tanhf, powf, logf and the
-// f64 forms).  For f32 the kernels evaluate the function in f64 with CUDA's
-// double-precision math library and round once to f32, which lands within one
-// ulp of a correctly rounded result; glibc's f32 functions are themselves
-// within about one ulp, so the two agree to a couple of ulp at most (measured
-// by the parity tests).  For f64 the kernels call CUDA's f64 functions.
+// f64 forms).  For f32 the kernels evaluate the function in f64 and round once
+// to f32, which lands within one ulp of a correctly rounded result; glibc's
+// f32 functions are themselves within about one ulp, so the two agree to a
+// couple of ulp at most (measured by the parity tests).  The exponentials of
+// the hot paths (sigmoid, powf(E, x) in ELU / SELU / softmax) use exp2_scaled
+// below, inline; tanh, ln and the general powf call CUDA's f64 functions out
+// of line.  For f64 the kernels call CUDA's f64 functions.
 #pragma once
 
 #include <cstdint>
@@ -23,6 +21,47 @@
 #include "../../include/trs.h"
 
 namespace trs {
+
+// 2^(y * k2) for an f32 argument y, evaluated in f64 and returned unrounded
+// (the caller rounds it once to f32); k2 is log2 of a base near e (log2(e)
+// for expf, log2(2.7182817f) for powf(E, .)).
+//
+// Method: Cody and Waite's additive argument reduction followed by a minimax
+// polynomial (J.-M. Muller, "Elementary Functions: Algorithms and
+// Implementation", ch. 6 and 11).  k = round(y*k2) by adding 1.5*2^52, which
+// leaves k in the low word; f = y*k2 - k in [-1/2, 1/2] by one fused
+// multiply-add; 2^f by the degree-8 polynomial of least maximum relative
+// error on [-1/2, 1/2] (Remez exchange; error 7.8e-13); 2^k added to the
+// exponent field.  The result is within 1e-12 relative of 2^(y*k2): rounded
+// to f32 it is the correctly rounded value except within 1e-12 of a rounding
+// boundary, where it is one ulp away.  y is clamped to [-110, 90] first
+// (beyond it the f32 result is already 0 or +inf, and 2^k stays a normal
+// exponent); a NaN passes the clamps (the compares are false), keeps k = 0
+// and yields NaN.  NONPOS: the caller guarantees y <= 0 or NaN (softmax's
+// x - max), so the upper clamp is skipped.
+template <bool NONPOS = false>
+__device__ __forceinline__ double exp2_scaled(float y, double k2) {
+  y = y < -110.0f ? -110.0f : y;
+  if constexpr (!NONPOS) y = y > 90.0f ? 90.0f : y;
+  const double yd = (double)y;
+  const double kShift = 6755399441055744.0;  // 1.5 * 2^52
+  const double sh = __fma_rn(yd, k2, kShift);
+  const int k = y == y ? __double2loint(sh) : 0;
+  const double f = __fma_rn(yd, k2, -__dsub_rn(sh, kShift));
+  double q = 1.3175867143282797e-06;
+  q = __fma_rn(q, f, 1.5309737219754944e-05);
+  q = __fma_rn(q, f, 0.0001540385170493416);
+  q = __fma_rn(q, f, 0.00133334520632859);
+  q = __fma_rn(q, f, 0.009618128542934786);
+  q = __fma_rn(q, f, 0.05550410939340186);
+  q = __fma_rn(q, f, 0.2402265069887989);
+  q = __fma_rn(q, f, 0.6931471805465147);
+  q = __fma_rn(q, f, 0.9999999999997624);
+  // q in [0.70, 1.42] and |k| <= 159: the scaled value is a normal f64
+  return __hiloint2double(__double2hiint(q) + (int)((unsigned)k << 20), __double2loint(q));
+}
+
+constexpr double kLog2E = 1.4426950408889634;  // log2(e) rounded to f64
 
 template <class T> struct Arith;
 
@@ -37,12 +76,12 @@ template <> struct Arith<float> {
   static __device__ __noinline__ float pow(float a, float b) {
     return (float)::pow((double)a, (double)b);
   }
-  // powf(E_f32, x) as exp(x * ln(E_f32)) in f64; `ln_e` is ln of the f32 E.
-  static __device__ __forceinline__ float pow_e_inline(float x, double ln_e) {
-    return (float)::exp(__dmul_rn((double)x, ln_e));
+  // powf(E_f32, x) as 2^(x * log2(E_f32)) in f64; `log2_e` is log2 of the f32 E.
+  static __device__ __forceinline__ float pow_e_inline(float x, double log2_e) {
+    return (float)exp2_scaled(x, log2_e);
   }
-  static __device__ __noinline__ float pow_e(float x, double ln_e) { return pow_e_inline(x, ln_e); }
-  static __device__ __noinline__ float exp(float a) { return (float)::exp((double)a); }
+  static __device__ __forceinline__ float pow_e(float x, double log2_e) { return pow_e_inline(x, log2_e); }
+  static __device__ __forceinline__ float exp(float a) { return (float)exp2_scaled(a, kLog2E); }
   // tanh: for |x| >= 1 through expm1 in f32 steps, 1 - 2/(expm1(2|x|) + 2),
   // the classical formulation (the one glibc's f32 tanh evaluates), with
   // expm1 rounded once from f64; below 1 the f64 tanh rounded once, because
@@ -124,7 +163,7 @@ struct EwParams {
   int n_in;
   int op1, op2, epi;
   trs_scalar p0, p1;
-  double e_const;  // ln(E_f32) for f32, E_f64 for f64 (see Arith::pow_e)
+  double e_const;  // log2(E_f32) for f32, E_f64 for f64 (see Arith::pow_e)
   int* div_flag;
 };
 
@@ -153,9 +192,11 @@ __device__ __forceinline__ T apply_unop(const EwParams& p, T v) {
       return A::mul(v, v > zero ? one : zero);
     }
     case TRS_UN_SIGMOID: {  // autodiff/ops.rs:586-593
-      if (v >= zero) return A::div(one, A::add(one, A::exp(A::neg(v))), nullptr);
-      T e = A::exp(v);
-      return A::div(e, A::add(one, e), nullptr);
+      // x >= 0: 1 / (1 + exp(-x)); otherwise e / (1 + e) with e = exp(x).
+      // Both branches take exp(-|x|), so one exponential serves either
+      // (a NaN fails x >= 0 and gives exp(NaN) / ..., NaN, as the reference).
+      const T e = A::exp(A::neg(A::abs(v)));
+      return A::div(v >= zero ? one : e, A::add(one, e), nullptr);
     }
     case TRS_UN_TANH: return A::tanh(v);
     case TRS_UN_ELU: {  // elu.rs:47-63

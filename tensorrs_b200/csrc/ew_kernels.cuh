@@ -667,7 +667,7 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
   p.epi = prog.epilogue;
   p.p0 = prog.p0;
   p.p1 = prog.p1;
-  p.e_const = std::is_same<T, float>::value ? std::log((double)2.7182817f) : 2.718281828459045;
+  p.e_const = std::is_same<T, float>::value ? std::log2((double)2.7182817f) : 2.718281828459045;
   p.div_flag = nullptr;
 
   const bool want_sum = sum != nullptr;

@@ -1,15 +1,29 @@
 // softmax.cu -- K-SOFTMAX: SoftMax::forward over the last axis
 // (activation/softmax.rs:42-68).  The reference takes five passes over the
-// data (max_axis, x - max, powf(E, .), sum_axis_keepdim, e / sum); here one
-// warp or one CTA holds a row in registers and reads and writes it once:
-//   m = max_axis(row)          strict `>` scan semantics (MaxState)
+// data (max_axis, x - max, powf(E, .), sum_axis_keepdim, e / sum); here each
+// row is read and written once:
+//   m = max_axis(row)          the reference's max (a NaN at index 0 is kept)
 //   e = powf(E, x - m)         x - m rounded to T, then E^(x-m) rounded to T
 //   s = sum of e               accumulated in f64, rounded once to T
 //   out = e / s                IEEE division in T
-// Rows longer than a CTA can hold in registers take three passes over global
-// memory instead (max, sum, write).
+// Kernels:
+//   softmax_stream_kernel  rows of 4 KiB .. 96 KiB with 16-byte aligned rows:
+//                          one CTA per SM; a producer warp streams whole rows
+//                          into a ring of shared-memory stages with
+//                          cp.async.bulk, 16 consumer warps copy a row into
+//                          registers (releasing the stage at once), reduce the
+//                          max and the f64 sum across the CTA, and stream
+//                          e / s out with 16-byte stores.
+//   softmax_rows_kernel    other rows up to 16384: a warp or a CTA holds the
+//                          row in registers.
+//   softmax_long_kernel    longer rows: three passes over global memory.
+// The max only feeds x - m, where a -0 / +0 maximum gives the same
+// difference's exponential (E^0 = 1), so the stream kernel takes it with the
+// NaN-ignoring fmax and then applies the reference's NaN-at-index-0 rule.
 #include <cmath>
 #include <cstring>
+#include <mutex>
+#include <type_traits>
 
 #include "kernels.cuh"
 #include "softmax.h"
@@ -204,6 +218,217 @@ __global__ void __launch_bounds__(1024) softmax_long_kernel(const SmDev d) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// softmax_stream_kernel: the bulk-copy row pipeline (see the file comment).
+constexpr int kSmConsumerWarps = 16;
+constexpr int kSmConsumers = 32 * kSmConsumerWarps;
+constexpr int kSmThreads = 32 + kSmConsumers;
+constexpr int kSmStageBudget = 192 * 1024;
+constexpr int kSmMaxStages = 8;
+constexpr uint32_t kSmCopyBytes = 16384;  // one bulk copy per 16 KiB of a row
+
+__device__ __forceinline__ void sm_consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kSmConsumers) : "memory");
+}
+
+template <class T>
+__device__ __forceinline__ T fmax_t(T a, T b) {
+  if constexpr (sizeof(T) == 4) return fmaxf(a, b);
+  else return fmax(a, b);
+}
+
+template <class T, int V>
+__device__ __forceinline__ void sstore_stream(T* p, const SVec<T, V>& r) {
+  int4 x;
+  memcpy(&x, &r, 16);
+  __stcs(reinterpret_cast<int4*>(p), x);
+}
+
+// CPT: 16-byte chunks of a row per consumer thread (the row is at most
+// CPT * 512 chunks).
+template <class T, int CPT>
+__global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmDev d) {
+  using A = Arith<T>;
+  using Acc = typename A::Acc;
+  constexpr int V = 16 / (int)sizeof(T);
+  constexpr bool kF32 = std::is_same<T, float>::value;
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ uint64_t full[kSmMaxStages], empty[kSmMaxStages];
+  __shared__ T red_max[kSmConsumerWarps];
+  __shared__ Acc red_sum[kSmConsumerWarps];
+  __shared__ T first_elem;
+  const int S = d.stages;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t row_bytes = (uint32_t)d.C * (uint32_t)sizeof(T);
+  const uint32_t nchunk = row_bytes / 16;
+  const T* x = static_cast<const T*>(d.in);
+  T* out = static_cast<T*>(d.out);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kSmConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  bool failed = false;
+  uint32_t issued = 0;
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t qn = 0;
+      for (uint64_t row = blockIdx.x; row < (uint64_t)d.rows; row += gridDim.x, ++qn) {
+        const int s = (int)(qn % (uint32_t)S);
+        if (!failed && qn >= (uint32_t)S && !mbar_wait(&empty[s], ((qn / S) - 1) & 1u)) failed = true;
+        if (failed) continue;
+        int64_t bi, bo;
+        row_bases(d, row, &bi, &bo);
+        fence_proxy_async();
+        mbar_arrive_expect_tx(&full[s], row_bytes);
+        const unsigned char* src = reinterpret_cast<const unsigned char*>(x + bi);
+        unsigned char* dst = smem + (size_t)s * row_bytes;
+        for (uint32_t o = 0; o < row_bytes; o += kSmCopyBytes)
+          bulk_g2s(dst + o, src + o, row_bytes - o < kSmCopyBytes ? row_bytes - o : kSmCopyBytes, &full[s]);
+        issued = qn + 1;
+      }
+    }
+  } else {
+    const int ct = threadIdx.x - 32, cw = warp - 1;
+    uint32_t qn = 0;
+    for (uint64_t row = blockIdx.x; row < (uint64_t)d.rows; row += gridDim.x, ++qn) {
+      const int s = (int)(qn % (uint32_t)S);
+      if (!failed && !__all_sync(0xffffffffu, mbar_wait(&full[s], (qn / S) & 1u))) failed = true;
+      SVec<T, V> v[CPT];
+      T mx = -INFINITY;
+      if (!failed) {
+        const unsigned char* stage = smem + (size_t)s * row_bytes;
+#pragma unroll
+        for (int j = 0; j < CPT; ++j) {
+          const uint32_t k = (uint32_t)ct + (uint32_t)j * kSmConsumers;
+          if (k < nchunk) {
+            v[j] = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
+#pragma unroll
+            for (int i = 0; i < V; ++i) mx = fmax_t(mx, v[j].v[i]);
+          }
+        }
+        if (ct == 0) first_elem = v[0].v[0];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      // row maximum across the CTA (every consumer thread gets it)
+      for (int o = 16; o > 0; o >>= 1) mx = fmax_t(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (lane == 0) red_max[cw] = mx;
+      sm_consumer_sync();
+      T m = red_max[0];
+#pragma unroll
+      for (int w = 1; w < kSmConsumerWarps; ++w) m = fmax_t(m, red_max[w]);
+      if (is_nan_val(first_elem)) m = first_elem;
+      // e = powf(E, x - m), summed in f64 (x - m <= 0, or NaN)
+      Acc acc = Acc(0);
+      if (!failed) {
+#pragma unroll
+        for (int j = 0; j < CPT; ++j) {
+          const uint32_t k = (uint32_t)ct + (uint32_t)j * kSmConsumers;
+          if (k < nchunk) {
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+              T e;
+              if constexpr (kF32)
+                e = (float)exp2_scaled<true>(__fsub_rn(v[j].v[i], m), d.e_const);
+              else
+                e = A::pow_e_inline(A::sub(v[j].v[i], m), d.e_const);
+              v[j].v[i] = e;
+              acc = acc + A::to_acc(e);
+            }
+          }
+        }
+      }
+      for (int o = 16; o > 0; o >>= 1) acc = acc + __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) red_sum[cw] = acc;
+      sm_consumer_sync();
+      Acc tot = red_sum[0];
+#pragma unroll
+      for (int w = 1; w < kSmConsumerWarps; ++w) tot = tot + red_sum[w];
+      const T sum = A::from_acc(tot);
+      if (!failed) {
+        int64_t bi, bo;
+        row_bases(d, row, &bi, &bo);
+        T* orow = out + bo;
+        // f32: e / sum as e * (1/sum) in f64, rounded once.  For p-bit
+        // operands a quotient that is not a rounding midpoint lies at least
+        // 2^-(2p+1) (relative) from every midpoint and, for a normal result,
+        // is never exactly one; the f64 product is within 2^-52 of the
+        // quotient, so for p = 24 its rounding agrees with IEEE division.
+        // Results below 2^-125 take the IEEE division itself.
+        const double rs = kF32 ? __drcp_rn((double)sum) : 0.0;
+#pragma unroll
+        for (int j = 0; j < CPT; ++j) {
+          const uint32_t k = (uint32_t)ct + (uint32_t)j * kSmConsumers;
+          if (k < nchunk) {
+            SVec<T, V> r;
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+              if constexpr (kF32) {
+                float q = (float)__dmul_rn((double)v[j].v[i], rs);
+                if (fabsf(q) < 0x1p-125f) q = __fdiv_rn(v[j].v[i], sum);
+                r.v[i] = q;
+              } else {
+                r.v[i] = A::div(v[j].v[i], sum, nullptr);
+              }
+            }
+            sstore_stream<T, V>(orow + (size_t)k * V, r);
+          }
+        }
+      }
+    }
+  }
+  if (__syncthreads_or(failed)) {
+    if (threadIdx.x == 0) {
+      atomicOr(d.err, kAsyncWaitTimeout);
+      const uint32_t start = issued > (uint32_t)S ? issued - (uint32_t)S : 0;
+      for (uint32_t k = start; k < issued; ++k) mbar_wait(&full[k % S], (k / S) & 1u);
+    }
+    __syncthreads();
+  }
+}
+
+template <class T, int CPT>
+Error launch_softmax_stream(const SmDev& d, cudaStream_t stream) {
+  auto k = softmax_stream_kernel<T, CPT>;
+  const int smem = d.stages * (int)(d.C * (int64_t)sizeof(T));
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmStageBudget) != cudaSuccess)
+      return cuda_error(cudaGetLastError(), "cudaFuncSetAttribute");
+  }
+  const uint64_t sms = (uint64_t)current_device_info().sm_count;
+  const unsigned grid = (unsigned)((uint64_t)d.rows < sms ? (uint64_t)d.rows : sms);
+  k<<<grid, kSmThreads, smem, stream>>>(d);
+  return check_launch("softmax stream kernel");
+}
+
+// Whether the stream kernel takes these rows (else the register kernels run).
+template <class T>
+bool softmax_stream_fits(const SmDev& d, bool aligned) {
+  const int64_t row_bytes = d.C * (int64_t)sizeof(T);
+  return aligned && d.in_step == 1 && d.out_step == 1 && row_bytes % 16 == 0 && row_bytes >= 4096 &&
+         row_bytes * 2 <= kSmStageBudget && d.err != nullptr;
+}
+
+template <class T>
+Error launch_softmax_stream_typed(SmDev d, cudaStream_t stream) {
+  const int64_t row_bytes = d.C * (int64_t)sizeof(T);
+  int64_t st = kSmStageBudget / row_bytes;
+  d.stages = (int)(st > kSmMaxStages ? kSmMaxStages : st);
+  const int64_t chunks = row_bytes / 16;
+  if (chunks <= 2 * kSmConsumers) return launch_softmax_stream<T, 2>(d, stream);
+  if (chunks <= 4 * kSmConsumers) return launch_softmax_stream<T, 4>(d, stream);
+  if (chunks <= 8 * kSmConsumers) return launch_softmax_stream<T, 8>(d, stream);
+  return launch_softmax_stream<T, 12>(d, stream);
+}
+
 template <class K>
 unsigned grid_of(K kernel, int threads, uint64_t work) {
   const DeviceInfo& dev = current_device_info();
@@ -221,6 +446,7 @@ template <class T>
 Error launch_softmax_typed(const SmDev& d, int vec, cudaStream_t stream) {
   if (d.rows == 0 || d.C == 0) return Error{};
   constexpr int VW = 16 / sizeof(T);
+  if (softmax_stream_fits<T>(d, vec == VW)) return launch_softmax_stream_typed<T>(d, stream);
   const int64_t C = d.C;
   // warp per row
   if (C <= 32 * 32) {
@@ -310,8 +536,9 @@ Error run_softmax(const trs_view* x, const trs_view* out, cudaStream_t stream) {
   if (((uintptr_t)out->data + (uintptr_t)(out->offset * es)) % 16) vec = false;
   for (int i = 0; i < q; ++i)
     if (d.ist[i] % VW || d.ost[i] % VW) vec = false;
+  d.err = async_error_word();
   if (x->dtype == TRS_F32) {
-    d.e_const = std::log((double)2.7182817f);
+    d.e_const = std::log2((double)2.7182817f);
     return launch_softmax_typed<float>(d, vec ? VW : 1, stream);
   }
   d.e_const = 2.718281828459045;

@@ -19,7 +19,9 @@ struct SmDev {
   int64_t oshape[kMaxDims];
   int64_t ist[kMaxDims];
   int64_t ost[kMaxDims];
-  double e_const;            // ln(E_f32) for f32, E_f64 for f64
+  double e_const;            // log2(E_f32) for f32, E_f64 for f64
+  int stages;                // softmax_stream_kernel: rows staged in shared memory
+  int* err;                  // async-error word (bounded waits)
 };
 
 Error run_softmax(const trs_view* x, const trs_view* out, cudaStream_t stream);

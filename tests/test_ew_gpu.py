@@ -178,6 +178,29 @@ def test_transcendental_unary_maps_within_two_ulp(op, p0, p1, dtype):
     assert u <= (2 if dtype == np.float32 else F64_ULP), f"{op}: {u} ulp"
 
 
+@pytest.mark.parametrize("op", ["exp", "sigmoid"])
+def test_f32_exponentials_dense_sweep(op):
+    """powf(E, x) (elu.rs:58-60) and sigmoid (autodiff/ops.rs:586-593) on 2^22
+    points spanning every f32 result from overflow down through the
+    subnormals to 0, plus the specials.  The exponential is within 1 ulp of
+    glibc's; sigmoid divides two quantities that both carry it (e / (1 + e)),
+    so a one-ulp e can move it by 2 ulp, which happens for a few hundred of
+    the 2^22 points -- the rest are bit-identical."""
+    import oracle
+    from tensorrs_b200 import device
+    x = np.linspace(-110.0, 95.0, 1 << 22).astype(np.float32)
+    x = np.concatenate([x, np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 88.72283, 88.72284, -103.27893,
+                                     -103.97208, -87.33655, 1e-30, -1e-30], np.float32)])
+    dx = contiguous(x)
+    want = oracle.unary(op, dx.host_view())
+    got = to_host(device.unary(op, dx.view, empty(x.shape, np.float32)))
+    u = max_ulp(got, want)
+    exact = int((ulp_diff(got, want) == 0).sum())
+    print(f"{op}: max {u} ulp, {exact}/{x.size} bit-identical")
+    assert u <= (1 if op == "exp" else 2), f"{op}: {u} ulp"
+    assert exact >= 0.999 * x.size
+
+
 @pytest.mark.parametrize("op,p0,p1", CANCEL_UNARY, ids=lambda v: str(v))
 @pytest.mark.parametrize("dtype", [np.float32, np.float64], ids=lambda d: np.dtype(d).name)
 def test_elu_selu_within_the_propagated_bound(op, p0, p1, dtype):
