@@ -441,6 +441,133 @@ ew_tile_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials
 }
 
 // --------------------------------------------------------------------------
+// ew_tr_kernel: the same layouts as ew_tile_kernel (an input running along
+// another dimension i than the output's unit-stride dimension j, such as B^T)
+// when every row start is 16-byte aligned.  Tiles are TS x TS elements
+// (TS = 256 bytes: 64 f32 / 32 f64).  Each thread first issues all of its
+// loads of a tile: transposed inputs go from global to shared memory with
+// 16-byte cp.async (their rows are the tile's columns), the other inputs into
+// registers with 16-byte loads in the output's layout (or one scalar per row
+// when constant along j).  After one barrier each thread reads its transposed
+// values down the shared columns, applies the compile-time program and
+// stores 16 bytes of output.  The 16-byte chunks of a shared row are
+// XOR-swizzled by the row's chunk group, which keeps both the cp.async writes
+// and the column reads at most two-way bank conflicted.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+template <class T, int PROG, bool WRITE, bool SUM>
+__global__ void __launch_bounds__(kThreads, 3)
+ew_tr_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials) {
+  using A = Arith<T>;
+  using Acc = typename A::Acc;
+  constexpr int V = 16 / (int)sizeof(T);
+  constexpr int TS = 256 / (int)sizeof(T);
+  constexpr int CPR = TS / V;                 // 16-byte chunks per tile row
+  constexpr int VPT = TS * CPR / kThreads;    // chunks per thread per input
+  constexpr int NIN = prog_inputs(PROG);
+  extern __shared__ __align__(128) unsigned char tsm[];
+  Acc acc = Acc(0);
+  const int j = d.nd - 1, ti = d.ti;
+  const int64_t Ni = d.shape[ti], Nj = d.shape[j];
+  const T* ins[3] = {static_cast<const T*>(d.in[0]), static_cast<const T*>(d.in[1]),
+                     static_cast<const T*>(d.in[2])};
+  T* out = static_cast<T*>(d.out);
+  for (uint64_t t = blockIdx.x; t < d.n_tiles; t += gridDim.x) {
+    uint64_t rest = t / d.tiles_j;
+    const int64_t j0 = (int64_t)(t - rest * d.tiles_j) * TS;
+    uint64_t b = rest / d.tiles_i;
+    const int64_t i0 = (int64_t)(rest - b * d.tiles_i) * TS;
+    int64_t o[kMaxOperands];
+#pragma unroll
+    for (int k = 0; k < kMaxOperands; ++k) o[k] = d.off[k];
+    for (int q = d.n_batch - 1; q >= 0; --q) {
+      const int dd = d.batch_dim[q];
+      const uint64_t nb = b / (uint64_t)d.shape[dd];
+      const int64_t c = (int64_t)(b - nb * (uint64_t)d.shape[dd]);
+      b = nb;
+#pragma unroll
+      for (int k = 0; k < kMaxOperands; ++k) o[k] += c * d.st[k][dd];
+    }
+    // 1. transposed inputs: global -> shared, tile row = j offset
+#pragma unroll
+    for (int k = 0; k < NIN; ++k) {
+      const int slot = d.tslot[k];
+      if (slot < 0) continue;
+      unsigned char* base = tsm + slot * (TS * 256);
+      const int64_t sj = d.st[k + 1][j];
+#pragma unroll
+      for (int r = 0; r < VPT; ++r) {
+        const int v = threadIdx.x + r * kThreads;
+        const int row = v / CPR, ch = v % CPR;
+        const int64_t jj = j0 + row, ii = i0 + (int64_t)ch * V;
+        if (jj < Nj && ii < Ni)
+          cp_async16(base + row * 256 + ((ch ^ ((row / V) & 15)) * 16), ins[k] + o[k + 1] + ii + jj * sj);
+      }
+    }
+    cp_async_commit();
+    // 2. the other inputs: registers, in the output's layout (row = i offset)
+    VecT<T, V> rv[NIN][VPT];
+#pragma unroll
+    for (int k = 0; k < NIN; ++k) {
+      if (d.tslot[k] >= 0) continue;
+      const int64_t sj = d.st[k + 1][j], si = d.st[k + 1][ti];
+#pragma unroll
+      for (int r = 0; r < VPT; ++r) {
+        const int v = threadIdx.x + r * kThreads;
+        const int row = v / CPR, ch = v % CPR;
+        const int64_t ii = i0 + row, jj = j0 + (int64_t)ch * V;
+        if (ii < Ni && jj < Nj) {
+          const T* src = ins[k] + o[k + 1] + ii * si + jj * sj;
+          if (sj == 1) {
+            rv[k][r] = load_vec<T, V>(src);
+          } else {
+            const T sc = __ldg(src);
+#pragma unroll
+            for (int q = 0; q < V; ++q) rv[k][r].v[q] = sc;
+          }
+        }
+      }
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    // 3. combine, store 16 bytes per chunk
+#pragma unroll
+    for (int r = 0; r < VPT; ++r) {
+      const int v = threadIdx.x + r * kThreads;
+      const int row = v / CPR, ch = v % CPR;
+      const int64_t ii = i0 + row, jj = j0 + (int64_t)ch * V;
+      if (ii < Ni && jj < Nj) {
+        VecT<T, V> res;
+#pragma unroll
+        for (int q = 0; q < V; ++q) {
+          T a[3] = {T(0), T(0), T(0)};
+#pragma unroll
+          for (int k = 0; k < NIN; ++k) {
+            const int slot = d.tslot[k];
+            if (slot >= 0) {
+              const int jr = ch * V + q;  // the transposed input's tile row
+              a[k] = *reinterpret_cast<const T*>(tsm + slot * (TS * 256) + jr * 256 +
+                                                 (((row / V) ^ (ch & 15)) * 16) + (row % V) * (int)sizeof(T));
+            } else {
+              a[k] = rv[k][r].v[q];
+            }
+          }
+          res.v[q] = apply_prog<T, PROG>(p, a[0], a[1], a[2]);
+          if constexpr (SUM) acc = acc + A::to_acc(res.v[q]);
+        }
+        if constexpr (WRITE) store_vec_stream<T, V>(out + o[0] + ii * d.st[0][ti] + jj, res);
+      }
+    }
+    __syncthreads();
+  }
+  if constexpr (SUM) write_partial<Acc>(acc, partials);
+}
+
+// --------------------------------------------------------------------------
 // ew_generic_kernel: one element per thread, every operand's offset decoded
 // from the row-major element index.
 template <class T, bool WRITE, bool SUM>
@@ -597,6 +724,24 @@ const void* pick_stream_nb(int nb, bool write, bool want_sum) {
   }
 }
 
+template <class T, int PROG>
+const void* pick_tr_ws(bool write, bool want_sum) {
+  if (write && !want_sum) return (const void*)ew_tr_kernel<T, PROG, true, false>;
+  if constexpr (prog_is_runtime(PROG)) {
+    if (write && want_sum) return (const void*)ew_tr_kernel<T, PROG, true, true>;
+    return (const void*)ew_tr_kernel<T, PROG, false, true>;
+  }
+  return nullptr;
+}
+
+template <class T, int PROG>
+const void* pick_tr_code(bool write, bool want_sum) {
+  if constexpr (prog_is_runtime(PROG) || PROG == kPack || PROG == kAdd || PROG == kSub || PROG == kMul ||
+                PROG == kMulSigmoid)
+    return pick_tr_ws<T, PROG>(write, want_sum);
+  return nullptr;
+}
+
 template <class T, class F>
 const void* by_code(int code, F f) {
   switch (code) {
@@ -631,6 +776,13 @@ template <class T>
 const void* pick_vec(int code, int fallback, int vw, bool write, bool want_sum) {
   const void* k = by_code<T>(code, [&](auto c) { return pick_vec_ws<T, decltype(c)::value>(vw, write, want_sum); });
   if (!k) k = by_code<T>(fallback, [&](auto c) { return pick_vec_ws<T, decltype(c)::value>(vw, write, want_sum); });
+  return k;
+}
+
+template <class T>
+const void* pick_tr(int code, int fallback, bool write, bool want_sum) {
+  const void* k = by_code<T>(code, [&](auto c) { return pick_tr_code<T, decltype(c)::value>(write, want_sum); });
+  if (!k) k = by_code<T>(fallback, [&](auto c) { return pick_tr_code<T, decltype(c)::value>(write, want_sum); });
   return k;
 }
 
@@ -695,6 +847,7 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
   uint64_t rows_per_launch = 0, total_rows = 0, stream_tpr = 0;
   int stream_smem = 0;
   constexpr int kEwStream = 100;  // internal variant: the bulk-copy pipeline
+  constexpr int kEwTr = 101;      // internal variant: the vectorised tile kernel
   auto grid_for = [&](const void* k, int per_sm, uint64_t work_blocks) {
     uint64_t cap = (uint64_t)dev.sm_count * (uint64_t)per_sm;
     uint64_t b = work_blocks < cap ? work_blocks : cap;
@@ -766,6 +919,54 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
       }
     }
   }
+  int tr_smem = 0;
+  if (variant == kEwTile && f.n > 0) {
+    // the vectorised tile kernel when every row start is 16-byte aligned
+    constexpr int VW = 16 / sizeof(T);
+    const int j = f.nd - 1, ti = pr.choice.tile_dim;
+    bool ok = f.shape[ti] % VW == 0 && f.shape[j] % VW == 0;
+    auto aligned = [&](const void* base, int64_t off) {
+      return ((uintptr_t)base + (uintptr_t)(off * (int64_t)sizeof(T))) % 16 == 0;
+    };
+    int nt = 0;
+    for (int k = 0; k < prog.n_in && ok; ++k) {
+      const int64_t sj = f.st[k + 1][j], si = f.st[k + 1][ti];
+      d.tslot[k] = -1;
+      if (sj != 0 && sj != 1) {  // transposed: unit stride along i required
+        ok = si == 1 && sj % VW == 0 && aligned(in[k].data, f.off[k + 1]);
+        d.tslot[k] = nt++;
+      } else if (sj == 1) {
+        ok = si % VW == 0 && aligned(in[k].data, f.off[k + 1]);
+      }
+      for (int i = 0; i < f.nd && ok; ++i)
+        if (i != ti && i != j && f.st[k + 1][i] % VW) ok = false;
+    }
+    if (ok && write) {
+      ok = f.st[0][j] == 1 && f.st[0][ti] % VW == 0 && aligned(out->data, f.off[0]);
+      for (int i = 0; i < f.nd && ok; ++i)
+        if (i != ti && i != j && f.st[0][i] % VW) ok = false;
+    }
+    const int code = program_code(prog, IsFloat<T>::value);
+    const bool simple = is_simple_program(prog) || !IsFloat<T>::value;
+    const int fallback = (simple ? kRunSimple1 : kRunFull1) + (prog.n_in - 1);
+    const void* tk = ok && nt > 0 ? ewk::pick_tr<T>(code, fallback, write, want_sum) : nullptr;
+    if (tk) {
+      constexpr int TS = 256 / sizeof(T);
+      d.ti = ti;
+      d.n_batch = 0;
+      for (int i = 0; i < f.nd; ++i)
+        if (i != ti && i != j) d.batch_dim[d.n_batch++] = i;
+      d.tiles_i = ((uint64_t)f.shape[ti] + TS - 1) / TS;
+      d.tiles_j = ((uint64_t)f.shape[j] + TS - 1) / TS;
+      uint64_t nbt = 1;
+      for (int q = 0; q < d.n_batch; ++q) nbt *= (uint64_t)f.shape[d.batch_dim[q]];
+      d.n_tiles = d.tiles_i * d.tiles_j * nbt;
+      tr_smem = nt * TS * 256;
+      ewk::allow_smem(tk, tr_smem);
+      grid_for(tk, ewk::resident_blocks_smem(tk, kThreads, tr_smem), d.n_tiles);
+      variant = kEwTr;
+    }
+  }
   if (variant == kEwTile) {
     const int j = f.nd - 1, ti = pr.choice.tile_dim;
     d.ti = ti;
@@ -816,8 +1017,9 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
       Acc* part_l = part ? part + (size_t)l * blocks : nullptr;
       void* args[] = {(void*)&d, (void*)&p, (void*)&part_l};
       const bool st = variant == kEwStream;
+      const size_t dyn = st ? (size_t)stream_smem : (variant == kEwTr ? (size_t)tr_smem : 0);
       cudaError_t ce = cudaLaunchKernel(kernel, dim3(blocks), dim3(st ? ewk::kStreamThreads : kThreads), args,
-                                        st ? (size_t)stream_smem : 0, stream);
+                                        dyn, stream);
       if (ce != cudaSuccess) return cuda_error(ce, "element-wise kernel launch");
       Error e = check_launch("element-wise kernel");
       if (!e.ok()) return e;

@@ -102,6 +102,68 @@ def test_transposed_batched_operands():
     assert_bit_exact(gpu_binary("sub", da, dbt, np.float64), want)
 
 
+@pytest.mark.parametrize("dtype", [np.float32, np.float64, np.int32, np.int64], ids=lambda d: np.dtype(d).name)
+@pytest.mark.parametrize("n,m", [(4096, 4096), (300, 4100), (64, 64), (8, 1000), (1000, 8), (132, 68)],
+                         ids=lambda v: str(v))
+def test_transposed_vectorised_tiles(n, m, dtype):
+    """A op B^T on the vectorised tile path (row starts 16-byte aligned):
+    full and partial tiles, several ops, bit-exact."""
+    import oracle
+    a = rand([n, m], dtype, 31)
+    b = rand([m, n], dtype, 32)
+    da = contiguous(a)
+    dbt = DevView(b.reshape(-1), [n, m], [1, n], 0)
+    for op in ("mul", "add", "sub"):
+        want = oracle.binary(op, da.host_view(), dbt.host_view())
+        assert_bit_exact(gpu_binary(op, da, dbt, dtype), want, f"{op} {n}x{m}")
+    # B^T op A: the transposed input first
+    want = oracle.binary("mul", dbt.host_view(), da.host_view())
+    assert_bit_exact(gpu_binary("mul", dbt, da, dtype), want, "B^T & A")
+
+
+def test_transposed_pack_sigmoid_and_three_inputs():
+    """get_data of a transposed view (trs_pack), sigmoid(A & B^T) fused (the
+    config-2 program), and a 3-input program mixing two transposed inputs with
+    a per-row column vector plus the sum epilogue, on the vectorised tile path."""
+    import oracle
+    from tensorrs_b200 import abi, device
+    n = 1024
+    a = rand([n, n], np.float32, 41)
+    b = rand([n, n], np.float32, 42)
+    c = rand([n, 1], np.float32, 43)
+    da, dc = contiguous(a), contiguous(c)
+    dbt = DevView(b.reshape(-1), [n, n], [1, n], 0)
+    dat = DevView(a.reshape(-1), [n, n], [1, n], 0)
+    got = to_host(device.pack(dbt.view, empty([n, n], np.float32)))
+    assert_bit_exact(got, np.ascontiguousarray(b.T), "pack of B^T")
+    prog = abi.program(2, abi.MUL, epilogue="sigmoid")
+    out = empty([n, n], np.float32)
+    device.elementwise(prog, [da.view, dbt.view], out)
+    want = oracle.program(2, "mul", "add", "sigmoid", [da.host_view(), dbt.host_view()])
+    assert max_ulp(to_host(out), want) <= 2
+    prog3 = abi.program(3, abi.MUL, abi.ADD)
+    out3 = empty([n, n], np.float32)
+    s3 = empty([1], np.float32)
+    device.elementwise(prog3, [dat.view, dbt.view, dc.view], out3, s3)
+    want3 = oracle.program(3, "mul", "add", "none", [dat.host_view(), dbt.host_view(), dc.host_view()])
+    assert_bit_exact(to_host(out3), want3, "A^T & B^T + c")
+    ref_s = oracle.sum_all(oracle.contiguous(want3))
+    exact, sabs = oracle.sum_f64(oracle.contiguous(want3))
+    got_s = float(to_host(s3)[0])
+    assert abs(got_s - ref_s) <= 1e-5 * sabs and abs(got_s - exact) <= abs(exact) * 2.0**-23 + 2.0**-40 * sabs
+
+
+def test_transposed_batched_vectorised():
+    """[B, n, m] with a permuted view of a [B, m, n] storage, 16-byte aligned."""
+    import oracle
+    a = rand([3, 128, 72], np.float32, 51)
+    b = rand([3, 72, 128], np.float32, 52)
+    da = contiguous(a)
+    dbt = DevView(b.reshape(-1), [3, 128, 72], [72 * 128, 1, 128], 0)
+    want = oracle.binary("mul", da.host_view(), dbt.host_view())
+    assert_bit_exact(gpu_binary("mul", da, dbt, np.float32), want)
+
+
 @pytest.mark.parametrize("dtype", DTYPES, ids=lambda d: np.dtype(d).name)
 def test_reversed_offset_and_gapped_views(dtype):
     """step_slice views: negative steps, offsets and gaps (base.rs:369-398)."""
