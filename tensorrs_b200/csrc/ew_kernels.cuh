@@ -35,6 +35,11 @@
 #ifndef TRS_VEC_PERSISTENT
 #define TRS_VEC_PERSISTENT 1
 #endif
+//   TRS_STREAM_TRANSCENDENTAL 1: programs with transcendentals take the
+//                      bulk-copy pipeline too; 0: they take the vec kernel
+#ifndef TRS_STREAM_TRANSCENDENTAL
+#define TRS_STREAM_TRANSCENDENTAL 1
+#endif
 
 namespace trs {
 namespace ewk {
@@ -882,7 +887,8 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
     // rows of at least 4 KiB (every unit-stride input 16-byte aligned, which
     // the vector width V == VW guarantees) take the bulk-copy pipeline
     const void* sk = nullptr;
-    if (TRS_STREAM_ENABLE && fits && V == VW && nb > 0 && (uint64_t)f.shape[j] * sizeof(T) >= 4096)
+    if (TRS_STREAM_ENABLE && fits && V == VW && nb > 0 && (uint64_t)f.shape[j] * sizeof(T) >= 4096 &&
+        (TRS_STREAM_TRANSCENDENTAL || simple))
       sk = ewk::pick_stream<T>(code, fallback, nb, write, want_sum);
     int* err = sk ? async_error_word() : nullptr;
     if (sk && err) {

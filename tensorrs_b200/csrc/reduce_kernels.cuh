@@ -66,6 +66,14 @@ __device__ __forceinline__ T red_lowest() {
   else return (T)((typename Arith<T>::Acc)1 << (sizeof(T) * 8 - 1));
 }
 
+// max(a, b) ignoring a NaN operand (fmax for floats).
+template <class T>
+__device__ __forceinline__ T red_fmax(T a, T b) {
+  if constexpr (sizeof(T) == 4 && IsFloat<T>::value) return fmaxf(a, b);
+  else if constexpr (IsFloat<T>::value) return fmax(a, b);
+  else return a > b ? a : b;
+}
+
 // Accumulator state of one reduction, for every mode.
 template <class T>
 struct RedAcc {
@@ -670,41 +678,38 @@ __global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) 
           const unsigned char* stage = smem + s * NB * kRsTileBytes;
           const uint32_t chunks = len / V;
           if constexpr (MODE == kRedMax || MODE == kRedArgmax) {
-            // V independent strict `>` scans (element i of every chunk: one
-            // dependency chain each) from red_lowest, with the chunk index of
-            // the best; merged with the lower element index winning ties and
-            // folded into the item's state once per tile (tiles arrive in
-            // increasing order)
-            T tb[V];
-            uint32_t tc[V];
-#pragma unroll
-            for (int i = 0; i < V; ++i) {
-              tb[i] = red_lowest<T>();
-              tc[i] = 0xffffffffu;
-            }
+            // Per chunk: its NaN-ignoring maximum, compared strictly with
+            // the running best (so the earliest chunk holding the maximum
+            // wins).  Once per tile the winning chunk is read again and its
+            // first element equal to the best gives the index and the value
+            // (a -0 before a +0 stays, as in the reference's scan).  Tiles
+            // arrive in increasing order and fold into the item's state with
+            // the same strict rule.
+            T tb = red_lowest<T>();
+            uint32_t tc = 0xffffffffu;
             for (uint32_t c = ct; c < chunks; c += 32 * kRsConsumerWarps) {
               const RVec<T, V> g = *reinterpret_cast<const RVec<T, V>*>(stage + c * 16);
+              T cm = g.v[0];
 #pragma unroll
-              for (int i = 0; i < V; ++i) {
-                const bool p = g.v[i] > tb[i];
-                tb[i] = p ? g.v[i] : tb[i];
-                tc[i] = p ? c : tc[i];
-              }
+              for (int i = 1; i < V; ++i) cm = red_fmax(cm, g.v[i]);
+              const bool p = cm > tb;
+              tb = p ? cm : tb;
+              tc = p ? c : tc;
             }
-            T bb = tb[0];
-            uint32_t bi = tc[0] == 0xffffffffu ? 0xffffffffu : tc[0] * V;
+            if (tc != 0xffffffffu) {
+              const RVec<T, V> g = *reinterpret_cast<const RVec<T, V>*>(stage + tc * 16);
+              int first = V - 1;
+              T val = g.v[V - 1];
 #pragma unroll
-            for (int i = 1; i < V; ++i) {
-              if (tc[i] == 0xffffffffu) continue;
-              const uint32_t idx = tc[i] * V + i;
-              if (bi == 0xffffffffu || tb[i] > bb || (tb[i] == bb && idx < bi)) {
-                bb = tb[i];
-                bi = idx;
+              for (int i = V - 2; i >= 0; --i)
+                if (g.v[i] == tb) {
+                  first = i;
+                  val = g.v[i];
+                }
+              if (m.idx < 0 || val > m.val) {
+                m.val = val;
+                m.idx = col0 + (int64_t)(tc * V + first);
               }
-            }
-            if (bi != 0xffffffffu && (m.idx < 0 || bb > m.val)) {
-              m.val = bb;
-              m.idx = col0 + (int64_t)bi;
             }
           }
           for (uint32_t c = ct; c < chunks && MODE != kRedMax && MODE != kRedArgmax; c += 32 * kRsConsumerWarps) {
