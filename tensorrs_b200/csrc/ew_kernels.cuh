@@ -35,10 +35,13 @@
 #ifndef TRS_VEC_PERSISTENT
 #define TRS_VEC_PERSISTENT 1
 #endif
-//   TRS_STREAM_TRANSCENDENTAL 1: programs with transcendentals take the
-//                      bulk-copy pipeline too; 0: they take the vec kernel
+//   TRS_STREAM_TRANSCENDENTAL 0: programs with transcendentals take the vec
+//                      kernel, whose 32 warps per SM hide their arithmetic
+//                      latency better (measured: sigmoid over 64 MiB 0.50 of
+//                      the HBM peak against 0.40 on the pipeline); 1: the
+//                      bulk-copy pipeline
 #ifndef TRS_STREAM_TRANSCENDENTAL
-#define TRS_STREAM_TRANSCENDENTAL 1
+#define TRS_STREAM_TRANSCENDENTAL 0
 #endif
 
 namespace trs {

@@ -205,16 +205,18 @@ __device__ __forceinline__ void red_offsets(const RedDev& d, uint64_t r, int64_t
   }
 }
 
+// Writes one output.  `first` is the output's element at reduced index 0,
+// which the max modes need (callers read it ahead, off the critical path).
 template <class T>
-__device__ __forceinline__ void red_write(const RedDev& d, const RedAcc<T>& a, const int64_t* out_off,
-                                          const T* x0, int64_t x_first) {
+__device__ __forceinline__ void red_write_first(const RedDev& d, const RedAcc<T>& a, const int64_t* out_off,
+                                                T first) {
   using A = Arith<T>;
   if (d.raw) {
     if (d.mode == kRedMax || d.mode == kRedArgmax) {
       MaxRecord<T> r;
       r.val = a.m.val;
       r.idx = a.m.idx < 0 ? -1 : a.m.idx + d.idx_base;
-      r.first = d.total > 0 ? x0[x_first] : T(0);
+      r.first = d.total > 0 ? first : T(0);
       static_cast<MaxRecord<T>*>(d.out[0])[out_off[0]] = r;
     } else {
       static_cast<typename A::Acc*>(d.out[0])[out_off[0]] = a.s0;
@@ -238,7 +240,6 @@ __device__ __forceinline__ void red_write(const RedDev& d, const RedAcc<T>& a, c
     case kRedMax:
     case kRedArgmax: {
       // the reference keeps a NaN found at index 0 (base.rs:1404-1411)
-      const T first = x0[x_first];
       MaxState<T> m = a.m;
       if (is_nan_val(first) || m.idx < 0) { m.val = first; m.idx = 0; }
       if (d.mode == kRedMax)
@@ -248,6 +249,13 @@ __device__ __forceinline__ void red_write(const RedDev& d, const RedAcc<T>& a, c
       break;
     }
   }
+}
+
+template <class T>
+__device__ __forceinline__ void red_write(const RedDev& d, const RedAcc<T>& a, const int64_t* out_off,
+                                          const T* x0, int64_t x_first) {
+  const bool need = (d.mode == kRedMax || d.mode == kRedArgmax) && d.total > 0;
+  red_write_first<T>(d, a, out_off, need ? x0[x_first] : T(0));
 }
 
 // --------------------------------------------------------------------------
@@ -658,6 +666,11 @@ __global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) 
         s_c = __ldg(static_cast<const T*>(d.in[2]) + koff[2]);
         b_c = __ldg(static_cast<const T*>(d.in[3]) + koff[3]);
       }
+      // the element at index 0 for the max modes' rule, read ahead of the
+      // item's end so the write does not wait on it
+      T first_pref = T(0);
+      if constexpr (MODE == kRedMax || MODE == kRedArgmax)
+        if (ct == 0 && P == 1 && d.total > 0) first_pref = __ldg(x0 + koff[0]);
       for (uint32_t j = 0; j < nt; ++j, ++qn) {
         const int s = (int)(qn % S);
         const uint32_t u = t0 + j;
@@ -764,7 +777,7 @@ __global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) 
         RedAcc<T> tot = wred[0];
         for (int w = 1; w < kRsConsumerWarps; ++w) tot = red_combine(MODE, tot, wred[w]);
         if (P == 1)
-          red_write<T>(d, tot, ooff, x0, koff[0]);
+          red_write_first<T>(d, tot, ooff, first_pref);
         else
           static_cast<RedAcc<T>*>(d.parts)[it] = tot;
       }
@@ -924,6 +937,11 @@ __global__ void __launch_bounds__(kRsThreads) red_cstream_kernel(const RedDev d)
       const int64_t wl = W - col0 < wt ? W - col0 : wt;
       const bool mine = (int64_t)c * V < wl;
       const uint32_t r_end = part * rp + rp < total ? part * rp + rp : total;
+      // the columns' elements at reduced index 0 (max modes' rule), read
+      // ahead of the item's end
+      RVec<T, V> fv;
+      if constexpr (kMax)
+        if (g == 0 && mine && P == 1) fv = rload<T, V>(x0 + koff[0] + col0 + (int64_t)c * V);
       Acc acc[V];
       T tb[V];          // strict `>` scan per column from red_lowest,
       uint32_t tr[V];   // with the row of the best (~0: none yet)
@@ -1009,7 +1027,9 @@ __global__ void __launch_bounds__(kRsThreads) red_cstream_kernel(const RedDev d)
             if constexpr (kMax) ra.m = t;
             else ra.s0 = t;
             int64_t oo[2] = {ooff[0] + w * d.wout[0], ooff[1] + w * d.wout[1]};
-            red_write<T>(d, ra, oo, x0, koff[0] + w * d.wst[0]);
+            T first = T(0);
+            if constexpr (kMax) first = fv.v[i];
+            red_write_first<T>(d, ra, oo, first);
           } else {
             static_cast<Part*>(d.parts)[(uint64_t)part * (uint64_t)d.n_out + u_out] = t;
           }
