@@ -328,7 +328,12 @@ ew_stream_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partia
       }
       const unsigned char* stage = smem + s * SB;
       const uint32_t chunks = len / V;
-      for (uint32_t c = ct; c < chunks; c += 32 * kConsumerWarps) {
+      // the first chunk of each thread rotates by three warps per tile, so
+      // the leftover chunks of a tile that does not divide evenly fall on a
+      // different warp each time (a warp that finishes early moves on)
+      constexpr uint32_t kC = 32 * kConsumerWarps;
+      const uint32_t c0 = ((uint32_t)ct + kC - (k * 96u) % kC) % kC;
+      for (uint32_t c = c0; c < chunks; c += kC) {
         VecT<T, V> in[3];
 #pragma unroll
         for (int kk = 0; kk < NIN; ++kk) {

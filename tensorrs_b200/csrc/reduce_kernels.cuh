@@ -690,6 +690,11 @@ __global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) 
         if (!failed) {
           const unsigned char* stage = smem + s * NB * kRsTileBytes;
           const uint32_t chunks = len / V;
+          // the first chunk of each thread rotates by three warps per tile
+          // (leftover chunks of uneven tiles fall on a different warp each
+          // time; chunks stay in increasing order within a thread)
+          constexpr uint32_t kC = 32 * kRsConsumerWarps;
+          const uint32_t c0 = ((uint32_t)ct + kC - (qn * 96u) % kC) % kC;
           if constexpr (MODE == kRedMax || MODE == kRedArgmax) {
             // Per chunk: its NaN-ignoring maximum, compared strictly with
             // the running best (so the earliest chunk holding the maximum
@@ -700,7 +705,7 @@ __global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) 
             // the same strict rule.
             T tb = red_lowest<T>();
             uint32_t tc = 0xffffffffu;
-            for (uint32_t c = ct; c < chunks; c += 32 * kRsConsumerWarps) {
+            for (uint32_t c = c0; c < chunks; c += kC) {
               const RVec<T, V> g = *reinterpret_cast<const RVec<T, V>*>(stage + c * 16);
               T cm = g.v[0];
 #pragma unroll
@@ -725,7 +730,7 @@ __global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) 
               }
             }
           }
-          for (uint32_t c = ct; c < chunks && MODE != kRedMax && MODE != kRedArgmax; c += 32 * kRsConsumerWarps) {
+          for (uint32_t c = c0; c < chunks && MODE != kRedMax && MODE != kRedArgmax; c += kC) {
             const RVec<T, V> g = *reinterpret_cast<const RVec<T, V>*>(stage + c * 16);
             if constexpr (MODE == kRedSum || MODE == kRedMean) {
 #pragma unroll
