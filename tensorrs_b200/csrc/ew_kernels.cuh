@@ -333,6 +333,7 @@ ew_stream_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partia
       // different warp each time (a warp that finishes early moves on)
       constexpr uint32_t kC = 32 * kConsumerWarps;
       const uint32_t c0 = ((uint32_t)ct + kC - (k * 96u) % kC) % kC;
+#pragma unroll 4
       for (uint32_t c = c0; c < chunks; c += kC) {
         VecT<T, V> in[3];
 #pragma unroll

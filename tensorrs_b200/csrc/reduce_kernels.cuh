@@ -705,6 +705,7 @@ __global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) 
             // the same strict rule.
             T tb = red_lowest<T>();
             uint32_t tc = 0xffffffffu;
+#pragma unroll 4
             for (uint32_t c = c0; c < chunks; c += kC) {
               const RVec<T, V> g = *reinterpret_cast<const RVec<T, V>*>(stage + c * 16);
               T cm = g.v[0];
@@ -730,6 +731,7 @@ __global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) 
               }
             }
           }
+#pragma unroll 4
           for (uint32_t c = c0; c < chunks && MODE != kRedMax && MODE != kRedArgmax; c += kC) {
             const RVec<T, V> g = *reinterpret_cast<const RVec<T, V>*>(stage + c * 16);
             if constexpr (MODE == kRedSum || MODE == kRedMean) {
@@ -962,6 +964,7 @@ __global__ void __launch_bounds__(kRsThreads) red_cstream_kernel(const RedDev d)
         if (!failed && !__all_sync(0xffffffffu, mbar_wait(&full[s], (qn / S) & 1u))) failed = true;
         if (!failed && mine) {
           const unsigned char* stage = smem + s * NB * kCsStageBytes + c * 16;
+#pragma unroll 4
           for (uint32_t j = g; j < nrows; j += G) {
             const RVec<T, V> v = *reinterpret_cast<const RVec<T, V>*>(stage + j * pitch);
             if constexpr (MODE == kRedSum || MODE == kRedMean) {
