@@ -10,10 +10,10 @@
 //   softmax_stream_kernel  rows of 4 KiB .. 96 KiB with 16-byte aligned rows:
 //                          one CTA per SM; a producer warp streams whole rows
 //                          into a ring of shared-memory stages with
-//                          cp.async.bulk, 16 consumer warps copy a row into
-//                          registers (releasing the stage at once), reduce the
-//                          max and the f64 sum across the CTA, and stream
-//                          e / s out with 16-byte stores.
+//                          cp.async.bulk; the consumer warps take the max, the
+//                          exponentials (in place) with the f64 sum, and e / s
+//                          from the staged row, reduce across the CTA with two
+//                          named barriers, and store with 16-byte stores.
 //   softmax_rows_kernel    other rows up to 16384: a warp or a CTA holds the
 //                          row in registers.
 //   softmax_long_kernel    longer rows: three passes over global memory.
@@ -220,7 +220,15 @@ __global__ void __launch_bounds__(1024) softmax_long_kernel(const SmDev d) {
 
 // ---------------------------------------------------------------------------
 // softmax_stream_kernel: the bulk-copy row pipeline (see the file comment).
-constexpr int kSmConsumerWarps = 16;
+// Consumers work on the staged row in shared memory in three passes: the max;
+// e = E^(x - m) written back over x, with the f64 sum; e / sum streamed out.
+// Each thread reads back only the chunks it wrote, so the passes need no
+// barrier beyond the two CTA-wide reductions, and few registers stay live
+// per thread, which leaves room for many exponentials in flight.
+#ifndef TRS_SM_CONSUMER_WARPS
+#define TRS_SM_CONSUMER_WARPS 16
+#endif
+constexpr int kSmConsumerWarps = TRS_SM_CONSUMER_WARPS;
 constexpr int kSmConsumers = 32 * kSmConsumerWarps;
 constexpr int kSmThreads = 32 + kSmConsumers;
 constexpr int kSmStageBudget = 192 * 1024;
@@ -244,9 +252,7 @@ __device__ __forceinline__ void sstore_stream(T* p, const SVec<T, V>& r) {
   __stcs(reinterpret_cast<int4*>(p), x);
 }
 
-// CPT: 16-byte chunks of a row per consumer thread (the row is at most
-// CPT * 512 chunks).
-template <class T, int CPT>
+template <class T>
 __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmDev d) {
   using A = Arith<T>;
   using Acc = typename A::Acc;
@@ -256,7 +262,6 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
   __shared__ uint64_t full[kSmMaxStages], empty[kSmMaxStages];
   __shared__ T red_max[kSmConsumerWarps];
   __shared__ Acc red_sum[kSmConsumerWarps];
-  __shared__ T first_elem;
   const int S = d.stages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t row_bytes = (uint32_t)d.C * (uint32_t)sizeof(T);
@@ -299,49 +304,45 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
     for (uint64_t row = blockIdx.x; row < (uint64_t)d.rows; row += gridDim.x, ++qn) {
       const int s = (int)(qn % (uint32_t)S);
       if (!failed && !__all_sync(0xffffffffu, mbar_wait(&full[s], (qn / S) & 1u))) failed = true;
-      SVec<T, V> v[CPT];
+      unsigned char* stage = smem + (size_t)s * row_bytes;
+      // pass 1: the row maximum (NaN-ignoring), then the reference's rule:
+      // a NaN at index 0 is the maximum
       T mx = -INFINITY;
       if (!failed) {
-        const unsigned char* stage = smem + (size_t)s * row_bytes;
+#pragma unroll 4
+        for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmConsumers) {
+          const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
 #pragma unroll
-        for (int j = 0; j < CPT; ++j) {
-          const uint32_t k = (uint32_t)ct + (uint32_t)j * kSmConsumers;
-          if (k < nchunk) {
-            v[j] = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
-#pragma unroll
-            for (int i = 0; i < V; ++i) mx = fmax_t(mx, v[j].v[i]);
-          }
+          for (int i = 0; i < V; ++i) mx = fmax_t(mx, v.v[i]);
         }
-        if (ct == 0) first_elem = v[0].v[0];
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-      // row maximum across the CTA (every consumer thread gets it)
       for (int o = 16; o > 0; o >>= 1) mx = fmax_t(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       if (lane == 0) red_max[cw] = mx;
       sm_consumer_sync();
       T m = red_max[0];
 #pragma unroll
       for (int w = 1; w < kSmConsumerWarps; ++w) m = fmax_t(m, red_max[w]);
-      if (is_nan_val(first_elem)) m = first_elem;
-      // e = powf(E, x - m), summed in f64 (x - m <= 0, or NaN)
+      if (!failed) {
+        const T first = *reinterpret_cast<const T*>(stage);
+        if (is_nan_val(first)) m = first;
+      }
+      // pass 2: e = powf(E, x - m) over x in place, summed in f64
       Acc acc = Acc(0);
       if (!failed) {
+#pragma unroll 4
+        for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmConsumers) {
+          SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
 #pragma unroll
-        for (int j = 0; j < CPT; ++j) {
-          const uint32_t k = (uint32_t)ct + (uint32_t)j * kSmConsumers;
-          if (k < nchunk) {
-#pragma unroll
-            for (int i = 0; i < V; ++i) {
-              T e;
-              if constexpr (kF32)
-                e = (float)exp2_scaled<true>(__fsub_rn(v[j].v[i], m), d.e_const);
-              else
-                e = A::pow_e_inline(A::sub(v[j].v[i], m), d.e_const);
-              v[j].v[i] = e;
-              acc = acc + A::to_acc(e);
-            }
+          for (int i = 0; i < V; ++i) {
+            T e;
+            if constexpr (kF32)
+              e = (float)exp2_scaled<true>(__fsub_rn(v.v[i], m), d.e_const);
+            else
+              e = A::pow_e_inline(A::sub(v.v[i], m), d.e_const);
+            v.v[i] = e;
+            acc = acc + A::to_acc(e);
           }
+          *reinterpret_cast<SVec<T, V>*>(stage + k * 16) = v;
         }
       }
       for (int o = 16; o > 0; o >>= 1) acc = acc + __shfl_xor_sync(0xffffffffu, acc, o);
@@ -351,36 +352,39 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
 #pragma unroll
       for (int w = 1; w < kSmConsumerWarps; ++w) tot = tot + red_sum[w];
       const T sum = A::from_acc(tot);
+      // pass 3: e / sum.  f32: e * (1/sum) in f64, rounded once.  For p-bit
+      // operands a quotient that is not a rounding midpoint lies at least
+      // 2^-(2p+1) (relative) from every midpoint and, for a normal result,
+      // is never exactly one; the f64 product is within 2^-52 of the
+      // quotient, so for p = 24 its rounding agrees with IEEE division.
+      // Results below 2^-125 take the IEEE division itself.
       if (!failed) {
         int64_t bi, bo;
         row_bases(d, row, &bi, &bo);
         T* orow = out + bo;
-        // f32: e / sum as e * (1/sum) in f64, rounded once.  For p-bit
-        // operands a quotient that is not a rounding midpoint lies at least
-        // 2^-(2p+1) (relative) from every midpoint and, for a normal result,
-        // is never exactly one; the f64 product is within 2^-52 of the
-        // quotient, so for p = 24 its rounding agrees with IEEE division.
-        // Results below 2^-125 take the IEEE division itself.
         const double rs = kF32 ? __drcp_rn((double)sum) : 0.0;
+#pragma unroll 4
+        for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmConsumers) {
+          const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
+          SVec<T, V> r;
 #pragma unroll
-        for (int j = 0; j < CPT; ++j) {
-          const uint32_t k = (uint32_t)ct + (uint32_t)j * kSmConsumers;
-          if (k < nchunk) {
-            SVec<T, V> r;
-#pragma unroll
-            for (int i = 0; i < V; ++i) {
-              if constexpr (kF32) {
-                float q = (float)__dmul_rn((double)v[j].v[i], rs);
-                if (fabsf(q) < 0x1p-125f) q = __fdiv_rn(v[j].v[i], sum);
-                r.v[i] = q;
-              } else {
-                r.v[i] = A::div(v[j].v[i], sum, nullptr);
-              }
+          for (int i = 0; i < V; ++i) {
+            if constexpr (kF32) {
+              float q = (float)__dmul_rn((double)v.v[i], rs);
+              if (fabsf(q) < 0x1p-125f) q = __fdiv_rn(v.v[i], sum);
+              r.v[i] = q;
+            } else {
+              r.v[i] = A::div(v.v[i], sum, nullptr);
             }
-            sstore_stream<T, V>(orow + (size_t)k * V, r);
           }
+          sstore_stream<T, V>(orow + (size_t)k * V, r);
         }
       }
+      // the consumers wrote this stage; order those writes before the next
+      // bulk copy into it, then release it
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
     }
   }
   if (__syncthreads_or(failed)) {
@@ -393,9 +397,9 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
   }
 }
 
-template <class T, int CPT>
+template <class T>
 Error launch_softmax_stream(const SmDev& d, cudaStream_t stream) {
-  auto k = softmax_stream_kernel<T, CPT>;
+  auto k = softmax_stream_kernel<T>;
   const int smem = d.stages * (int)(d.C * (int64_t)sizeof(T));
   static std::mutex mu;
   {
@@ -422,11 +426,7 @@ Error launch_softmax_stream_typed(SmDev d, cudaStream_t stream) {
   const int64_t row_bytes = d.C * (int64_t)sizeof(T);
   int64_t st = kSmStageBudget / row_bytes;
   d.stages = (int)(st > kSmMaxStages ? kSmMaxStages : st);
-  const int64_t chunks = row_bytes / 16;
-  if (chunks <= 2 * kSmConsumers) return launch_softmax_stream<T, 2>(d, stream);
-  if (chunks <= 4 * kSmConsumers) return launch_softmax_stream<T, 4>(d, stream);
-  if (chunks <= 8 * kSmConsumers) return launch_softmax_stream<T, 8>(d, stream);
-  return launch_softmax_stream<T, 12>(d, stream);
+  return launch_softmax_stream<T>(d, stream);
 }
 
 template <class K>
