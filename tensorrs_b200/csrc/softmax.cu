@@ -252,6 +252,17 @@ __device__ __forceinline__ void sstore_stream(T* p, const SVec<T, V>& r) {
   __stcs(reinterpret_cast<int4*>(p), x);
 }
 
+// (double)(float)x for an f64 x >= 2^-126: the significand rounded to 24 bits
+// (to nearest, ties to even) in integer arithmetic.  Below 2^-126 the value
+// differs from the f32 rounding but stays below 2^-126, which leaves a row sum
+// of at least 1 (the maximum's own term) unchanged.
+__device__ __forceinline__ double f64_rounded_to_f32(double x) {
+  unsigned long long b = (unsigned long long)__double_as_longlong(x);
+  b += 0x0FFFFFFFull + ((b >> 29) & 1ull);
+  b &= ~0x1FFFFFFFull;
+  return __longlong_as_double((long long)b);
+}
+
 template <class T>
 __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmDev d) {
   using A = Arith<T>;
@@ -334,13 +345,15 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
           SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
 #pragma unroll
           for (int i = 0; i < V; ++i) {
-            T e;
-            if constexpr (kF32)
-              e = (float)exp2_scaled<true>(__fsub_rn(v.v[i], m), d.e_const);
-            else
-              e = A::pow_e_inline(A::sub(v.v[i], m), d.e_const);
-            v.v[i] = e;
-            acc = acc + A::to_acc(e);
+            if constexpr (kF32) {
+              const double e64 = exp2_scaled<true>(__fsub_rn(v.v[i], m), d.e_const);
+              v.v[i] = (float)e64;
+              acc = acc + f64_rounded_to_f32(e64);
+            } else {
+              const T e = A::pow_e_inline(A::sub(v.v[i], m), d.e_const);
+              v.v[i] = e;
+              acc = acc + A::to_acc(e);
+            }
           }
           *reinterpret_cast<SVec<T, V>*>(stage + k * 16) = v;
         }
@@ -352,17 +365,21 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
 #pragma unroll
       for (int w = 1; w < kSmConsumerWarps; ++w) tot = tot + red_sum[w];
       const T sum = A::from_acc(tot);
-      // pass 3: e / sum.  f32: e * (1/sum) in f64, rounded once.  For p-bit
-      // operands a quotient that is not a rounding midpoint lies at least
-      // 2^-(2p+1) (relative) from every midpoint and, for a normal result,
-      // is never exactly one; the f64 product is within 2^-52 of the
-      // quotient, so for p = 24 its rounding agrees with IEEE division.
-      // Results below 2^-125 take the IEEE division itself.
+      // pass 3: e / sum.  f32: with the reciprocal of the row sum as a pair
+      // yh + yl (yh = 1/sum rounded, yl the rounded rest), q0 = e*yh + e*yl
+      // is within one ulp of e/sum, so the remainder e - q0*sum is exact (one
+      // fused multiply-add) and q0 + rem*yh, rounded once, is the correctly
+      // rounded quotient (P. Markstein's correction step).  Results below
+      // 2^-125 take the IEEE division itself.
       if (!failed) {
         int64_t bi, bo;
         row_bases(d, row, &bi, &bo);
         T* orow = out + bo;
-        const double rs = kF32 ? __drcp_rn((double)sum) : 0.0;
+        float yh = 0.0f, yl = 0.0f;
+        if constexpr (kF32) {
+          yh = __frcp_rn(sum);
+          yl = (float)__dsub_rn(__drcp_rn((double)sum), (double)yh);
+        }
 #pragma unroll 4
         for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmConsumers) {
           const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
@@ -370,8 +387,11 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
 #pragma unroll
           for (int i = 0; i < V; ++i) {
             if constexpr (kF32) {
-              float q = (float)__dmul_rn((double)v.v[i], rs);
-              if (fabsf(q) < 0x1p-125f) q = __fdiv_rn(v.v[i], sum);
+              const float e = v.v[i];
+              const float q0 = __fmaf_rn(e, yh, __fmul_rn(e, yl));
+              const float rem = __fmaf_rn(-q0, sum, e);
+              float q = __fmaf_rn(rem, yh, q0);
+              if (fabsf(q) < 0x1p-125f) q = __fdiv_rn(e, sum);
               r.v[i] = q;
             } else {
               r.v[i] = A::div(v.v[i], sum, nullptr);

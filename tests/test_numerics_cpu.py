@@ -1,63 +1,75 @@
 """Host check of a numerical identity the softmax kernel relies on.
 
-The f32 row softmax divides every e by the same row sum s.  The kernel takes
-the quotient as e * (1/s) in f64 rounded once to f32 (a multiply instead of a
-division per element) and falls back to the IEEE division for results below
-2^-125.  The claim: for f32 e and s with a normal f32 quotient, that equals
-the IEEE f32 division e / s.  (A quotient of two 24-bit numbers that is not a
-rounding midpoint is at least 2^-49 relative away from every midpoint, and a
-normal one is never exactly a midpoint; the two f64 roundings stay within
-2^-52.)
+The f32 row softmax divides every e by the same row sum s.  Instead of an
+IEEE division per element the kernel takes, once per row, the reciprocal as a
+pair yh = RN(1/s), yl = RN(1/s - yh), and per element
 
-numpy's f64 arithmetic and its f64 -> f32 conversion are IEEE round-to-nearest
--even, as the GPU's __drcp_rn / __dmul_rn / cvt.rn.f32.f64 are, so the numpy
-restatement is bit-for-bit the kernel's computation.  The IEEE f32 quotient is
-the f64 quotient rounded once to f32 (exact because 53 >= 2 * 24 + 2; S. A.
-Figueroa, "When is double rounding innocuous?", SIGNUM Newsletter 30(3), 1995).
+    q0  = fma(e, yh, RN(e * yl))     within one ulp of e/s
+    rem = fma(-q0, s, e)             exact (q0 is within one ulp)
+    q   = fma(rem, yh, q0)           = RN(e / s)
+
+(the correction step of P. Markstein, "Computation of elementary functions on
+the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990), falling
+back to the IEEE division for results below 2^-125.  This test evaluates the
+same f32 operations with exact rational arithmetic, rounding each to f32 (ties
+to even) as the GPU's __fmaf_rn / __fmul_rn / __frcp_rn do, and checks the
+result against the correctly rounded quotient: random operands, quotients
+built next to rounding midpoints, and divisors with all-ones significands or
+powers of two.
 """
 from __future__ import annotations
+
+import random
+from fractions import Fraction as F
 
 import numpy as np
 
 
-def _check(e: np.ndarray, s: np.ndarray) -> int:
-    e = e.astype(np.float32)
-    s = s.astype(np.float32)
-    want = (e.astype(np.float64) / s.astype(np.float64)).astype(np.float32)
-    got = (e.astype(np.float64) * (1.0 / s.astype(np.float64))).astype(np.float32)
-    normal = np.abs(got) >= np.float32(2.0**-125)
-    bad = normal & (got.view(np.uint32) != want.view(np.uint32))
-    assert not bad.any(), (e[bad][:5], s[bad][:5], got[bad][:5], want[bad][:5])
-    return int(normal.sum())
+def _rn32(x: F) -> float:
+    """x rounded to the nearest f32, ties to even (normal range)."""
+    if x == 0:
+        return 0.0
+    c = np.float32(float(x))
+    cands = [np.nextafter(c, np.float32(-np.inf)), c, np.nextafter(c, np.float32(np.inf))]
+    return float(min(cands, key=lambda t: (abs(F(float(t)) - x), int(np.float32(t).view(np.uint32)) & 1)))
 
 
-def test_division_through_an_f64_reciprocal_equals_ieee_division_random():
-    rng = np.random.default_rng(2024)
-    n = 3_000_000
-    # softmax operands: e in (0, 1], s in [1, 2^24]
-    e = np.exp2(rng.uniform(-124.0, 0.0, n))
-    s = np.exp2(rng.uniform(0.0, 24.0, n))
-    assert _check(e, s) > 0.8 * n  # the rest fall below 2^-125 (IEEE division there)
-    # the general f32 range
-    e = np.exp2(rng.uniform(-100.0, 100.0, n)) * rng.choice([-1.0, 1.0], n)
-    s = np.exp2(rng.uniform(-20.0, 20.0, n))
-    assert _check(e, s) > 0.95 * n
+def _kernel_quotient(e: float, s: float) -> tuple[float, bool]:
+    yh = _rn32(F(1) / F(s))
+    yl = _rn32(F(1) / F(s) - F(yh))
+    q0 = _rn32(F(e) * F(yh) + F(_rn32(F(e) * F(yl))))
+    rem = F(e) - F(q0) * F(s)
+    exact = F(_rn32(rem)) == rem
+    return _rn32(F(q0) + F(_rn32(rem)) * F(yh)), exact
 
 
-def test_division_through_an_f64_reciprocal_equals_ieee_division_near_midpoints():
-    """Numerators built so that e / s lands next to an f32 rounding midpoint:
-    e = f32(m * s) for midpoints m, and its neighbours; plus divisors with
-    all-ones mantissas and powers of two."""
-    rng = np.random.default_rng(7)
-    n = 1_000_000
-    s = rng.integers(1 << 23, 1 << 24, n).astype(np.float64) * 2.0 ** rng.integers(-23, 1, n)
-    mid = (2 * rng.integers(1 << 23, 1 << 24, n) + 1).astype(np.float64) * 2.0**-25
-    e0 = (mid * s).astype(np.float32)
-    for step in (-1, 0, 1):
-        e = np.nextafter(e0, np.float32(np.inf) if step > 0 else np.float32(-np.inf)) if step else e0
-        _check(e, s)
-    ones = np.float32(2.0 - 2.0**-23) * np.exp2(np.arange(-10, 11)).astype(np.float32)
-    pows = np.exp2(np.arange(-10, 25)).astype(np.float32)
-    e = rng.uniform(0.0, 1.0, 200_000).astype(np.float32)
-    for d in np.concatenate([ones, pows]):
-        _check(e, np.full(e.shape, d, np.float32))
+def _check(e: float, s: float) -> bool:
+    e = float(np.float32(e))
+    s = float(np.float32(s))
+    want = _rn32(F(e) / F(s))
+    if e == 0 or abs(want) < 2.0**-125:
+        return False  # the kernel takes the IEEE division there
+    got, exact = _kernel_quotient(e, s)
+    assert exact, ("remainder not exact", e, s)
+    assert got == want, (e, s, got, want)
+    return True
+
+
+def test_row_division_equals_ieee_division_random():
+    rng = random.Random(2024)
+    checked = sum(_check(2.0 ** rng.uniform(-100.0, 0.0), 2.0 ** rng.uniform(0.0, 24.0)) for _ in range(12000))
+    assert checked > 10000
+
+
+def test_row_division_equals_ieee_division_near_midpoints():
+    rng = random.Random(7)
+    for _ in range(5000):
+        s = rng.randint(1 << 23, (1 << 24) - 1) * 2.0 ** rng.randint(-23, 0)
+        mid = (2 * rng.randint(1 << 23, (1 << 24) - 1) + 1) * 2.0**-25
+        e0 = np.float32(mid * s)
+        for e in (np.nextafter(e0, np.float32(-1)), e0, np.nextafter(e0, np.float32(2))):
+            _check(float(e), s)
+    for k in range(-4, 5):
+        for d in ((2.0 - 2.0**-23) * 2.0**k, 2.0**k, 3.0 * 2.0**k):
+            for _ in range(300):
+                _check(rng.uniform(0.0, 1.0), d)
