@@ -303,6 +303,46 @@ trs_status trs_softmax_lastdim(const trs_view* x, trs_view* out,
                                trs_stream stream);
 
 /* ------------------------------------------------------------------ */
+/* Callers of the path: LayerNorm and the optimiser steps               */
+/* ------------------------------------------------------------------ */
+
+/* LayerNorm::forward over the last axis (nn/layer_norm.rs:20-33) in one
+ * kernel: mean = sum_axis_keepdim(x) / F, sq = (x - mean) ^ 2,
+ * var = sum_axis_keepdim(sq) / F, denom = (var + eps) ^ 0.5,
+ * out = ((x - mean) / denom) & gamma + beta, with F the last dimension and
+ * gamma / beta of F elements each ([1, F] in the reference).  The sums
+ * accumulate in f64 and round once; every other step rounds as the separate
+ * reference calls do.  f32/f64. */
+trs_status trs_layer_norm_lastdim(const trs_view* x, const trs_view* gamma,
+                                  const trs_view* beta, double eps,
+                                  trs_view* out, trs_stream stream);
+
+/* One SGD step in place (optim/sgd.rs:29-37): param = param - grad * lr.
+ * `param` and `grad` contiguous, of one shape and dtype (f32/f64). */
+trs_status trs_sgd_step(trs_view* param, const trs_view* grad, double lr,
+                        trs_stream stream);
+
+/* One RMSprop step in place (optim/rmsprop.rs:30-46):
+ * v = v * alpha + (grad & grad) * (1 - alpha);
+ * param = param - (grad * lr) / map(v, sqrt(x) + eps).
+ * The reference's defaults are alpha = 0.99, eps = 1e-8.  Contiguous views
+ * of one shape. */
+trs_status trs_rmsprop_step(trs_view* param, const trs_view* grad, trs_view* v,
+                            double lr, double alpha, double eps,
+                            trs_stream stream);
+
+/* One Adam step in place (optim/adam.rs:119-144) for step number t >= 1:
+ * m = m * beta1 + grad * (1 - beta1); v = v * beta2 + (grad & grad) * (1 - beta2);
+ * m_hat = m / (1 - beta1^t); v_hat = v / (1 - beta2^t);
+ * param = param - (m_hat * lr) / map(v_hat, sqrt(x) + eps).
+ * beta^t is powf in the element type, computed on the host as the reference
+ * does; the reference's defaults are beta1 = 0.9, beta2 = 0.999, eps = 1e-8.
+ * Contiguous views of one shape. */
+trs_status trs_adam_step(trs_view* param, const trs_view* grad, trs_view* m,
+                         trs_view* v, double lr, double beta1, double beta2,
+                         double eps, int64_t t, trs_stream stream);
+
+/* ------------------------------------------------------------------ */
 /* Seeded synthetic inputs                                              */
 /* ------------------------------------------------------------------ */
 

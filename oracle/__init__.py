@@ -82,6 +82,8 @@ def load():
             "orc_fill_uniform": (c_int, [c_int, c_void_p, c_int64, c_uint64, c_double, c_double]),
             "orc_fill_uniform_at": (c_int, [c_int, c_void_p, c_int64, c_int64, c_uint64, c_double, c_double]),
             "orc_fill_normal": (c_int, [c_int, c_void_p, c_int64, c_uint64]),
+            "orc_opt_step": (c_int, [c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_double,
+                                     c_double, c_double, c_double, c_int64]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(lib, name)
@@ -238,6 +240,19 @@ def softmax_lastdim(x: HostView) -> np.ndarray:
     out = _out_buf(x.dtype, x.numel())
     _check(load().orc_softmax_lastdim(ctypes.byref(x.c()), out.ctypes.data))
     return out[: x.numel()].reshape(x.shape)
+
+
+def opt_step(kind: str, p: np.ndarray, g: np.ndarray, m: np.ndarray | None, v: np.ndarray | None, lr: float,
+             b1: float = 0.9, b2: float = 0.999, eps: float = 1e-8, t: int = 1) -> None:
+    """One SGD / RMSprop / Adam step in place on contiguous host arrays, as the
+    reference's chain of calls computes it (alpha goes in b2 for RMSprop)."""
+    k = {"sgd": 0, "rmsprop": 1, "adam": 2}[kind]
+    dt = {np.dtype(np.float32): 0, np.dtype(np.float64): 1}[p.dtype]
+    for a in (p, g, m, v):
+        assert a is None or (a.flags.c_contiguous and a.dtype == p.dtype and a.size == p.size)
+    nul = None
+    _check(load().orc_opt_step(k, dt, p.ctypes.data, g.ctypes.data, m.ctypes.data if m is not None else nul,
+                               v.ctypes.data if v is not None else nul, p.size, lr, b1, b2, eps, t))
 
 
 def sum_f64(x: HostView) -> tuple[float, float]:

@@ -626,6 +626,51 @@ inline uint64_t splitmix64(uint64_t seed, uint64_t i) {
     default: g_msg = "bad dtype"; return ERR_DTYPE;                 \
   }
 
+// One optimiser step for one parameter, element by element, as the
+// reference's chain of tensor calls computes it (each call rounds once):
+//   kind 0, SGD::step (optim/sgd.rs:29-37):     p = p - grad * lr
+//   kind 1, RMSprop::step (optim/rmsprop.rs:30-46):
+//     v = v * alpha + (grad & grad) * (1 - alpha)     [alpha in b2]
+//     p = p - (grad * lr) / map(v, |x| x.sqrt() + eps)
+//   kind 2, Adam::step (optim/adam.rs:119-144), step number t:
+//     m = m * b1 + grad * (1 - b1);  v = v * b2 + (grad & grad) * (1 - b2)
+//     m_hat = m / (1 - b1.powf(t));  v_hat = v / (1 - b2.powf(t))
+//     p = p - (m_hat * lr) / map(v_hat, |x| x.sqrt() + eps)
+// The scalars are the reference's: T::from_f64(..), T::one() - b and powf in T.
+template <class T>
+static void opt_step_t(int kind, T* p, const T* g, T* m, T* v, int64_t n, double lr_d, double b1_d,
+                       double b2_d, double eps_d, int64_t t) {
+  const T lr = (T)lr_d, b1 = (T)b1_d, b2 = (T)b2_d, eps = (T)eps_d, one = (T)1;
+  const T omb1 = one - b1, omb2 = one - b2;
+  const T tt = (T)t;
+  const T bc1 = one - std::pow(b1, tt), bc2 = one - std::pow(b2, tt);
+  for (int64_t i = 0; i < n; ++i) {
+    if (kind == 0) {
+      const T upd = g[i] * lr;
+      p[i] = p[i] - upd;
+    } else if (kind == 1) {
+      const T gsq = g[i] * g[i];
+      const T a = v[i] * b2, b = gsq * omb2;
+      v[i] = a + b;
+      const T vs = std::sqrt(v[i]) + eps;
+      const T gl = g[i] * lr;
+      const T upd = gl / vs;
+      p[i] = p[i] - upd;
+    } else {
+      const T a = m[i] * b1, b = g[i] * omb1;
+      m[i] = a + b;
+      const T gsq = g[i] * g[i];
+      const T c = v[i] * b2, d = gsq * omb2;
+      v[i] = c + d;
+      const T mh = m[i] / bc1, vh = v[i] / bc2;
+      const T vs = std::sqrt(vh) + eps;
+      const T ml = mh * lr;
+      const T upd = ml / vs;
+      p[i] = p[i] - upd;
+    }
+  }
+}
+
 extern "C" {
 
 int orc_fill_uniform_at(int dtype, void* out, int64_t first, int64_t n, uint64_t seed, double lo,
@@ -821,6 +866,18 @@ int orc_fill_normal(int dtype, void* out, int64_t n, uint64_t seed) {
     if (dtype == F32) ((float*)out)[i] = (float)z;
     else ((double*)out)[i] = z;
   }
+  return OK;
+}
+
+int orc_opt_step(int kind, int dtype, void* p, const void* g, void* m, void* v, int64_t n, double lr,
+                 double b1, double b2, double eps, int64_t t) {
+  if (kind < 0 || kind > 2 || n < 0) return ERR_ARG;
+  if (dtype == F32)
+    opt_step_t<float>(kind, (float*)p, (const float*)g, (float*)m, (float*)v, n, lr, b1, b2, eps, t);
+  else if (dtype == F64)
+    opt_step_t<double>(kind, (double*)p, (const double*)g, (double*)m, (double*)v, n, lr, b1, b2, eps, t);
+  else
+    return ERR_DTYPE;
   return OK;
 }
 

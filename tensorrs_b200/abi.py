@@ -99,6 +99,10 @@ _SIGNATURES = {
     "trs_sum_to_shape_fused": (c_int32, [_V, _V, _V, POINTER(c_int64), c_int32, _V, c_void_p]),
     "trs_affine_relu_backward": (c_int32, [_V, _V, _V, _V, _V, _V, c_void_p]),
     "trs_softmax_lastdim": (c_int32, [_V, _V, c_void_p]),
+    "trs_layer_norm_lastdim": (c_int32, [_V, _V, _V, c_double, _V, c_void_p]),
+    "trs_sgd_step": (c_int32, [_V, _V, c_double, c_void_p]),
+    "trs_rmsprop_step": (c_int32, [_V, _V, _V, c_double, c_double, c_double, c_void_p]),
+    "trs_adam_step": (c_int32, [_V, _V, _V, _V, c_double, c_double, c_double, c_double, c_int64, c_void_p]),
     "trs_fill_uniform": (c_int32, [_V, c_uint64, c_uint64, c_double, c_double, c_void_p]),
     "trs_fill_normal": (c_int32, [_V, c_uint64, c_uint64, c_void_p]),
     "trs_set_device": (c_int32, [c_int32]),

@@ -124,6 +124,32 @@ def softmax_lastdim(x: abi.View, out: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def layer_norm_lastdim(x: abi.View, gamma: abi.View, beta: abi.View, eps: float, out: torch.Tensor) -> torch.Tensor:
+    """LayerNorm::forward over the last axis (nn/layer_norm.rs:20-33)."""
+    _call("trs_layer_norm_lastdim", ctypes.byref(x), ctypes.byref(gamma), ctypes.byref(beta), float(eps),
+          ctypes.byref(view_of(out)), stream_handle())
+    return out
+
+
+def sgd_step(param: torch.Tensor, grad: torch.Tensor, lr: float) -> None:
+    """SGD::step for one parameter (optim/sgd.rs:29-37), in place."""
+    _call("trs_sgd_step", ctypes.byref(view_of(param)), ctypes.byref(view_of(grad)), float(lr), stream_handle())
+
+
+def rmsprop_step(param: torch.Tensor, grad: torch.Tensor, v: torch.Tensor, lr: float, alpha: float = 0.99,
+                 eps: float = 1e-8) -> None:
+    """RMSprop::step for one parameter (optim/rmsprop.rs:30-46), in place."""
+    _call("trs_rmsprop_step", ctypes.byref(view_of(param)), ctypes.byref(view_of(grad)), ctypes.byref(view_of(v)),
+          float(lr), float(alpha), float(eps), stream_handle())
+
+
+def adam_step(param: torch.Tensor, grad: torch.Tensor, m: torch.Tensor, v: torch.Tensor, lr: float, t: int,
+              beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8) -> None:
+    """Adam::step for one parameter at step t >= 1 (optim/adam.rs:119-144), in place."""
+    _call("trs_adam_step", ctypes.byref(view_of(param)), ctypes.byref(view_of(grad)), ctypes.byref(view_of(m)),
+          ctypes.byref(view_of(v)), float(lr), float(beta1), float(beta2), float(eps), int(t), stream_handle())
+
+
 def fill_uniform(out: torch.Tensor, seed: int, lo: float = -1.0, hi: float = 1.0, first: int = 0) -> torch.Tensor:
     _call("trs_fill_uniform", ctypes.byref(view_of(out)), seed, first, lo, hi, stream_handle())
     return out
