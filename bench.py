@@ -531,6 +531,34 @@ def run_suite(args) -> None:
         run("config4", c4[2], xb + 4 * Ch,
             lambda: C(lib.trs_reduce_broadcast_grad(ctypes.byref(vG), tgt, 4, ctypes.byref(vgb), sh)))
         del X, G, Y
+    # callers of the path: LayerNorm over config 3's X, one Adam step over 2^26 f32 parameters
+    cc = ["layer_norm over X[8192,16384]", "adam step, 2^26 f32 params", "sgd step, 2^26 f32 params"]
+    if any_of("callers", cc):
+        R, Cc = 8192, 16384
+        X = device.fill_normal(t(R, Cc), 2)
+        Yl = t(R, Cc)
+        gam = device.fill_uniform(t(1, Cc), 7, 0.5, 1.5)
+        bet = device.fill_uniform(t(1, Cc), 8, -0.5, 0.5)
+        vX, vY, vg, vb = V(X), V(Yl), V(gam), V(bet)
+        run("callers", cc[0], 2 * R * Cc * 4 + 2 * Cc * 4,
+            lambda: C(lib.trs_layer_norm_lastdim(ctypes.byref(vX), ctypes.byref(vg), ctypes.byref(vb), 1e-5,
+                                                 ctypes.byref(vY), sh)))
+        del X, Yl
+        n = 1 << 26
+        P = device.fill_normal(t(n), 9)
+        G = device.fill_normal(t(n), 10)
+        M = torch.zeros(n, dtype=f32, device="cuda")
+        W = torch.zeros(n, dtype=f32, device="cuda")
+        vP, vG, vM, vW = V(P), V(G), V(M), V(W)
+        step = [0]
+
+        def adam():
+            step[0] += 1
+            C(lib.trs_adam_step(ctypes.byref(vP), ctypes.byref(vG), ctypes.byref(vM), ctypes.byref(vW), 1e-3, 0.9,
+                                0.999, 1e-8, step[0], sh))
+        run("callers", cc[1], 7 * n * 4, adam)
+        run("callers", cc[2], 3 * n * 4, lambda: C(lib.trs_sgd_step(ctypes.byref(vP), ctypes.byref(vG), 1e-3, sh)))
+        del P, G, M, W
     # config 5 (one GPU): the headline step
     c5 = ["Y = A & B + c and sum(Y) fused", "sum(Y) alone [65536,32768]"]
     if any_of("config5", c5):

@@ -131,10 +131,16 @@ def test_layer_norm_fused(shape, dtype):
     got = to_host(device.layer_norm_lastdim(dx.view, dg.view, db.view, eps, empty(shape, dtype)))
     x2 = x.reshape(-1, F)
     ideal = _ideal_layer_norm(x2, gamma.reshape(-1), beta.reshape(-1), eps).reshape(shape)
-    same = got == ideal
-    rows_off = int((~same.reshape(-1, F)).any(axis=1).sum())
-    assert rows_off <= max(1, x2.shape[0] // 100), f"{rows_off} rows differ from the exactly-summed restatement"
-    assert np.allclose(got, ideal, rtol=1e-5, atol=1e-5 * float(np.abs(beta).max() + 1))
+    if dtype == np.float32:
+        # f64 sums rounded once: the exactly-summed restatement, bit for bit,
+        # except rows whose f64 sum rounds to the other f32 neighbour
+        same = got == ideal
+        rows_off = int((~same.reshape(-1, F)).any(axis=1).sum())
+        assert rows_off <= max(1, x2.shape[0] // 100), f"{rows_off} rows differ from the exactly-summed restatement"
+        assert np.allclose(got, ideal, rtol=1e-5, atol=1e-5 * float(np.abs(beta).max() + 1))
+    else:
+        # f64 sums in f64 (no wider type): F * 2^-53 relative on the sums
+        assert np.allclose(got, ideal, rtol=F * 2.0**-50, atol=F * 2.0**-50)
     # against the reference's chain: its f32 sequential sums carry up to
     # (F-1) * 2^-24 relative error, amplified by 1/denom in x_hat
     ref = _chain_layer_norm(oracle.contiguous(x), oracle.contiguous(gamma), oracle.contiguous(beta), eps)
