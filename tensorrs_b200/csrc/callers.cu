@@ -11,8 +11,12 @@
 //                         operation, so the result is the chain's, bit for bit
 //                         (the bias corrections beta^t are powf on the host,
 //                         as the reference computes them).
-//   layernorm_rows_kernel a warp or a CTA per row holds the row in registers:
-//                         mean, (x - mean), the sum of squares, the
+//   rows of 4 .. 96 KiB  the bulk-copy row pipeline of softmax.cu (LayerNorm
+//                         mode): rows staged in shared memory, three passes
+//                         (sum, sum of squares, normalise), one read and one
+//                         write per element.
+//   layernorm_rows_kernel other rows: a warp or a CTA per row holds the row
+//                         in registers: mean, (x - mean), the sum of squares, the
 //                         normalisation and gamma / beta in one read and one
 //                         write; sums in f64, rounded once.
 //   layernorm_long_kernel rows longer than a CTA holds: three passes.
@@ -21,6 +25,7 @@
 
 #include "../../include/trs.h"
 #include "kernels.cuh"
+#include "softmax.h"
 
 namespace trs {
 namespace {
@@ -519,6 +524,32 @@ Error run_layer_norm(const trs_view* x, const trs_view* gamma, const trs_view* b
   if (((uintptr_t)out->data + (uintptr_t)(out->offset * es)) % 16) vec = false;
   for (int i = 0; i < q; ++i)
     if (d.ist[i] % VW || d.ost[i] % VW) vec = false;
+  // rows of 4 KiB and more: the bulk-copy row pipeline
+  SmDev sd;
+  std::memset(&sd, 0, sizeof(sd));
+  sd.in = d.in;
+  sd.out = d.out;
+  sd.in_off = d.in_off;
+  sd.out_off = d.out_off;
+  sd.C = d.C;
+  sd.in_step = d.in_step;
+  sd.out_step = d.out_step;
+  sd.rows = d.rows;
+  sd.nouter = d.nouter;
+  for (int i = 0; i < q; ++i) {
+    sd.oshape[i] = d.oshape[i];
+    sd.ist[i] = d.ist[i];
+    sd.ost[i] = d.ost[i];
+  }
+  sd.gamma = d.gamma;
+  sd.beta = d.beta;
+  sd.g_off = d.g_off;
+  sd.b_off = d.b_off;
+  sd.g_st = d.g_st;
+  sd.b_st = d.b_st;
+  sd.ln_eps = d.eps;
+  e = run_layer_norm_stream(sd, x->dtype, stream);
+  if (e.status != TRS_NONE) return e;
   if (x->dtype == TRS_F32) return launch_ln<float>(d, vec, stream);
   return launch_ln<double>(d, vec, stream);
 }

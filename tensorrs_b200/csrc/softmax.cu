@@ -263,7 +263,97 @@ __device__ __forceinline__ double f64_rounded_to_f32(double x) {
   return __longlong_as_double((long long)b);
 }
 
+// Sum over the consumer warps (fixed order), returned to every consumer.
+template <class Acc>
+__device__ __forceinline__ Acc consumer_sum(Acc acc, Acc* red, int cw, int lane) {
+  for (int o = 16; o > 0; o >>= 1) acc = acc + __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) red[cw] = acc;
+  sm_consumer_sync();
+  Acc tot = red[0];
+#pragma unroll
+  for (int w = 1; w < kSmConsumerWarps; ++w) tot = tot + red[w];
+  sm_consumer_sync();  // red is reused by the next sum
+  return tot;
+}
+
+// LayerNorm::forward (nn/layer_norm.rs:20-33) of one staged row: mean =
+// sum / F; var = sum((x - mean)^2) / F with the square rounded once (the
+// correctly rounded powf(., 2)); denom = sqrt(var + eps) (the correctly
+// rounded powf(., 0.5)); out = ((x - mean) / denom) * gamma + beta.  Sums in
+// f64, rounded once.  f32 divides by denom through its reciprocal pair and
+// the correction step (results below 2^-125: IEEE division).
 template <class T>
+__device__ __forceinline__ void layer_norm_row(const SmDev& d, const unsigned char* stage, uint32_t nchunk,
+                                               uint64_t row, int ct, int cw, int lane, bool failed,
+                                               typename Arith<T>::Acc* red) {
+  using A = Arith<T>;
+  using Acc = typename A::Acc;
+  constexpr int V = 16 / (int)sizeof(T);
+  constexpr bool kF32 = std::is_same<T, float>::value;
+  const T fc = (T)d.C;
+  Acc acc = Acc(0);
+  if (!failed) {
+#pragma unroll 4
+    for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmConsumers) {
+      const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc = acc + A::to_acc(v.v[i]);
+    }
+  }
+  const T mean = A::div(A::from_acc(consumer_sum<Acc>(acc, red, cw, lane)), fc, nullptr);
+  acc = Acc(0);
+  if (!failed) {
+#pragma unroll 4
+    for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmConsumers) {
+      const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        const T xm = A::sub(v.v[i], mean);
+        acc = acc + A::to_acc(A::mul(xm, xm));
+      }
+    }
+  }
+  const T var = A::div(A::from_acc(consumer_sum<Acc>(acc, red, cw, lane)), fc, nullptr);
+  if (failed) return;
+  T denom;
+  if constexpr (kF32) denom = __fsqrt_rn(A::add(var, (T)d.ln_eps));
+  else denom = __dsqrt_rn(A::add(var, (T)d.ln_eps));
+  float yh = 0.0f, yl = 0.0f;
+  if constexpr (kF32) {
+    yh = __frcp_rn(denom);
+    yl = (float)__dsub_rn(__drcp_rn((double)denom), (double)yh);
+  }
+  int64_t bi, bo;
+  row_bases(d, row, &bi, &bo);
+  T* orow = static_cast<T*>(d.out) + bo;
+  const T* gm = static_cast<const T*>(d.gamma) + d.g_off;
+  const T* bt = static_cast<const T*>(d.beta) + d.b_off;
+#pragma unroll 4
+  for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmConsumers) {
+    const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
+    SVec<T, V> r;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int64_t j = (int64_t)k * V + i;
+      const T xm = A::sub(v.v[i], mean);
+      T q;
+      if constexpr (kF32) {
+        const float q0 = __fmaf_rn(xm, yh, __fmul_rn(xm, yl));
+        const float rem = __fmaf_rn(-q0, denom, xm);
+        q = __fmaf_rn(rem, yh, q0);
+        if (fabsf(q) < 0x1p-125f) q = __fdiv_rn(xm, denom);
+      } else {
+        q = A::div(xm, denom, nullptr);
+      }
+      r.v[i] = A::add(A::mul(q, __ldg(gm + j * d.g_st)), __ldg(bt + j * d.b_st));
+    }
+    sstore_stream<T, V>(orow + (size_t)k * V, r);
+  }
+}
+
+enum RowMode { kRowSoftmax = 0, kRowLayerNorm = 1 };
+
+template <class T, int MODE>
 __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmDev d) {
   using A = Arith<T>;
   using Acc = typename A::Acc;
@@ -316,6 +406,13 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
       const int s = (int)(qn % (uint32_t)S);
       if (!failed && !__all_sync(0xffffffffu, mbar_wait(&full[s], (qn / S) & 1u))) failed = true;
       unsigned char* stage = smem + (size_t)s * row_bytes;
+      if constexpr (MODE == kRowLayerNorm) {
+        layer_norm_row<T>(d, stage, nchunk, row, ct, cw, lane, failed, red_sum);
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        continue;
+      }
       // pass 1: the row maximum (NaN-ignoring), then the reference's rule:
       // a NaN at index 0 is the maximum
       T mx = -INFINITY;
@@ -417,9 +514,9 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
   }
 }
 
-template <class T>
+template <class T, int MODE = kRowSoftmax>
 Error launch_softmax_stream(const SmDev& d, cudaStream_t stream) {
-  auto k = softmax_stream_kernel<T>;
+  auto k = softmax_stream_kernel<T, MODE>;
   const int smem = d.stages * (int)(d.C * (int64_t)sizeof(T));
   static std::mutex mu;
   {
@@ -514,6 +611,23 @@ Error launch_softmax_typed(const SmDev& d, int vec, cudaStream_t stream) {
 }
 
 }  // namespace
+
+Error run_layer_norm_stream(SmDev d, int dtype, cudaStream_t stream) {
+  const int es = dtype_size(dtype);
+  const int64_t row_bytes = d.C * es;
+  bool ok = d.in_step == 1 && d.out_step == 1 && row_bytes % 16 == 0 && row_bytes >= 4096 &&
+            row_bytes * 2 <= kSmStageBudget;
+  if (((uintptr_t)d.in + (uintptr_t)(d.in_off * es)) % 16) ok = false;
+  if (((uintptr_t)d.out + (uintptr_t)(d.out_off * es)) % 16) ok = false;
+  for (int i = 0; i < d.nouter; ++i)
+    if ((d.ist[i] * es) % 16 || (d.ost[i] * es) % 16) ok = false;
+  d.err = async_error_word();
+  if (!ok || !d.err || d.rows == 0) return make_error(TRS_NONE, "rows do not suit the row pipeline");
+  int64_t st = kSmStageBudget / row_bytes;
+  d.stages = (int)(st > kSmMaxStages ? kSmMaxStages : st);
+  if (dtype == TRS_F32) return launch_softmax_stream<float, kRowLayerNorm>(d, stream);
+  return launch_softmax_stream<double, kRowLayerNorm>(d, stream);
+}
 
 Error run_softmax(const trs_view* x, const trs_view* out, cudaStream_t stream) {
   Error e = validate_view(x, "input");

@@ -20,10 +20,22 @@ struct SmDev {
   int64_t ist[kMaxDims];
   int64_t ost[kMaxDims];
   double e_const;            // log2(E_f32) for f32, E_f64 for f64
-  int stages;                // softmax_stream_kernel: rows staged in shared memory
+  int stages;                // row_stream_kernel: rows staged in shared memory
   int* err;                  // async-error word (bounded waits)
+  // LayerNorm: gamma / beta (F values each, stride g_st / b_st), epsilon
+  const void* gamma;
+  const void* beta;
+  int64_t g_off, b_off, g_st, b_st;
+  double ln_eps;
 };
 
 Error run_softmax(const trs_view* x, const trs_view* out, cudaStream_t stream);
+
+// LayerNorm over the last axis on the bulk-copy row pipeline, for rows of
+// 4 KiB .. 96 KiB whose starts (input and output) are 16-byte aligned and
+// whose step along the row is 1.  Returns TRS_NONE (nothing launched) when
+// the rows do not qualify; `d` describes x / out / gamma / beta as for the
+// row kernels.
+Error run_layer_norm_stream(SmDev d, int dtype, cudaStream_t stream);
 
 }  // namespace trs

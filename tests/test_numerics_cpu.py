@@ -1,8 +1,9 @@
-"""Host check of a numerical identity the softmax kernel relies on.
+"""Host check of a numerical identity the row kernels rely on.
 
-The f32 row softmax divides every e by the same row sum s.  Instead of an
-IEEE division per element the kernel takes, once per row, the reciprocal as a
-pair yh = RN(1/s), yl = RN(1/s - yh), and per element
+The f32 row kernels divide every element of a row by the same value s (the
+softmax's row sum, LayerNorm's sqrt(var + eps)).  Instead of an IEEE division
+per element they take, once per row, the reciprocal as a pair
+yh = RN(1/s), yl = RN(1/s - yh), and per element
 
     q0  = fma(e, yh, RN(e * yl))     within one ulp of e/s
     rem = fma(-q0, s, e)             exact (q0 is within one ulp)
@@ -57,8 +58,13 @@ def _check(e: float, s: float) -> bool:
 
 def test_row_division_equals_ieee_division_random():
     rng = random.Random(2024)
-    checked = sum(_check(2.0 ** rng.uniform(-100.0, 0.0), 2.0 ** rng.uniform(0.0, 24.0)) for _ in range(12000))
-    assert checked > 10000
+    # softmax: e in (0, 1], s in [1, 2^24]
+    checked = sum(_check(2.0 ** rng.uniform(-100.0, 0.0), 2.0 ** rng.uniform(0.0, 24.0)) for _ in range(8000))
+    assert checked > 6000
+    # LayerNorm: (x - mean) of either sign over denom = sqrt(var + eps)
+    checked = sum(_check(rng.choice([-1.0, 1.0]) * 2.0 ** rng.uniform(-60.0, 60.0), 2.0 ** rng.uniform(-30.0, 30.0))
+                  for _ in range(8000))
+    assert checked > 6000
 
 
 def test_row_division_equals_ieee_division_near_midpoints():
