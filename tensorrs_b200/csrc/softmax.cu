@@ -331,10 +331,19 @@ __device__ __forceinline__ void layer_norm_row(const SmDev& d, const unsigned ch
 #pragma unroll 4
   for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmConsumers) {
     const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
-    SVec<T, V> r;
+    SVec<T, V> gv, bv, r;
+    if (d.gb_vec) {
+      gv = sload<T, V>(gm + (int64_t)k * V);
+      bv = sload<T, V>(bt + (int64_t)k * V);
+    } else {
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        gv.v[i] = __ldg(gm + ((int64_t)k * V + i) * d.g_st);
+        bv.v[i] = __ldg(bt + ((int64_t)k * V + i) * d.b_st);
+      }
+    }
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      const int64_t j = (int64_t)k * V + i;
       const T xm = A::sub(v.v[i], mean);
       T q;
       if constexpr (kF32) {
@@ -345,7 +354,7 @@ __device__ __forceinline__ void layer_norm_row(const SmDev& d, const unsigned ch
       } else {
         q = A::div(xm, denom, nullptr);
       }
-      r.v[i] = A::add(A::mul(q, __ldg(gm + j * d.g_st)), __ldg(bt + j * d.b_st));
+      r.v[i] = A::add(A::mul(q, gv.v[i]), bv.v[i]);
     }
     sstore_stream<T, V>(orow + (size_t)k * V, r);
   }
@@ -623,6 +632,9 @@ Error run_layer_norm_stream(SmDev d, int dtype, cudaStream_t stream) {
     if ((d.ist[i] * es) % 16 || (d.ost[i] * es) % 16) ok = false;
   d.err = async_error_word();
   if (!ok || !d.err || d.rows == 0) return make_error(TRS_NONE, "rows do not suit the row pipeline");
+  d.gb_vec = d.g_st == 1 && d.b_st == 1 &&
+             ((uintptr_t)d.gamma + (uintptr_t)(d.g_off * es)) % 16 == 0 &&
+             ((uintptr_t)d.beta + (uintptr_t)(d.b_off * es)) % 16 == 0;
   int64_t st = kSmStageBudget / row_bytes;
   d.stages = (int)(st > kSmMaxStages ? kSmMaxStages : st);
   if (dtype == TRS_F32) return launch_softmax_stream<float, kRowLayerNorm>(d, stream);

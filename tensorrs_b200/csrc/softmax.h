@@ -27,6 +27,7 @@ struct SmDev {
   const void* beta;
   int64_t g_off, b_off, g_st, b_st;
   double ln_eps;
+  int gb_vec;                // gamma and beta unit-stride and 16-byte aligned
 };
 
 Error run_softmax(const trs_view* x, const trs_view* out, cudaStream_t stream);
