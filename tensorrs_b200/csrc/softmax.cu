@@ -235,8 +235,17 @@ constexpr int kSmStageBudget = 192 * 1024;
 constexpr int kSmMaxStages = 8;
 constexpr uint32_t kSmCopyBytes = 16384;  // one bulk copy per 16 KiB of a row
 
-__device__ __forceinline__ void sm_consumer_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kSmConsumers) : "memory");
+// The consumer warps form kSmGroups groups that take alternate rows, so one
+// group computes while the other waits at a barrier of its row.
+#ifndef TRS_SM_GROUPS
+#define TRS_SM_GROUPS 2
+#endif
+constexpr int kSmGroups = TRS_SM_GROUPS;
+constexpr int kSmGroupWarps = kSmConsumerWarps / kSmGroups;
+constexpr int kSmGroupThreads = 32 * kSmGroupWarps;
+
+__device__ __forceinline__ void sm_group_sync(int grp) {
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "n"(kSmGroupThreads) : "memory");
 }
 
 template <class T>
@@ -264,15 +273,16 @@ __device__ __forceinline__ double f64_rounded_to_f32(double x) {
 }
 
 // Sum over the consumer warps (fixed order), returned to every consumer.
+// `red` is the group's slice of kSmGroupWarps entries.
 template <class Acc>
-__device__ __forceinline__ Acc consumer_sum(Acc acc, Acc* red, int cw, int lane) {
+__device__ __forceinline__ Acc consumer_sum(Acc acc, Acc* red, int cw, int lane, int grp) {
   for (int o = 16; o > 0; o >>= 1) acc = acc + __shfl_xor_sync(0xffffffffu, acc, o);
   if (lane == 0) red[cw] = acc;
-  sm_consumer_sync();
+  sm_group_sync(grp);
   Acc tot = red[0];
 #pragma unroll
-  for (int w = 1; w < kSmConsumerWarps; ++w) tot = tot + red[w];
-  sm_consumer_sync();  // red is reused by the next sum
+  for (int w = 1; w < kSmGroupWarps; ++w) tot = tot + red[w];
+  sm_group_sync(grp);  // red is reused by the next sum
   return tot;
 }
 
@@ -284,7 +294,7 @@ __device__ __forceinline__ Acc consumer_sum(Acc acc, Acc* red, int cw, int lane)
 // the correction step (results below 2^-125: IEEE division).
 template <class T>
 __device__ __forceinline__ void layer_norm_row(const SmDev& d, const unsigned char* stage, uint32_t nchunk,
-                                               uint64_t row, int ct, int cw, int lane, bool failed,
+                                               uint64_t row, int ct, int cw, int lane, int grp, bool failed,
                                                typename Arith<T>::Acc* red) {
   using A = Arith<T>;
   using Acc = typename A::Acc;
@@ -294,17 +304,17 @@ __device__ __forceinline__ void layer_norm_row(const SmDev& d, const unsigned ch
   Acc acc = Acc(0);
   if (!failed) {
 #pragma unroll 4
-    for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmConsumers) {
+    for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmGroupThreads) {
       const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
 #pragma unroll
       for (int i = 0; i < V; ++i) acc = acc + A::to_acc(v.v[i]);
     }
   }
-  const T mean = A::div(A::from_acc(consumer_sum<Acc>(acc, red, cw, lane)), fc, nullptr);
+  const T mean = A::div(A::from_acc(consumer_sum<Acc>(acc, red, cw, lane, grp)), fc, nullptr);
   acc = Acc(0);
   if (!failed) {
 #pragma unroll 4
-    for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmConsumers) {
+    for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmGroupThreads) {
       const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
 #pragma unroll
       for (int i = 0; i < V; ++i) {
@@ -313,7 +323,7 @@ __device__ __forceinline__ void layer_norm_row(const SmDev& d, const unsigned ch
       }
     }
   }
-  const T var = A::div(A::from_acc(consumer_sum<Acc>(acc, red, cw, lane)), fc, nullptr);
+  const T var = A::div(A::from_acc(consumer_sum<Acc>(acc, red, cw, lane, grp)), fc, nullptr);
   if (failed) return;
   T denom;
   if constexpr (kF32) denom = __fsqrt_rn(A::add(var, (T)d.ln_eps));
@@ -329,7 +339,7 @@ __device__ __forceinline__ void layer_norm_row(const SmDev& d, const unsigned ch
   const T* gm = static_cast<const T*>(d.gamma) + d.g_off;
   const T* bt = static_cast<const T*>(d.beta) + d.b_off;
 #pragma unroll 4
-  for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmConsumers) {
+  for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmGroupThreads) {
     const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
     SVec<T, V> gv, bv, r;
     if (d.gb_vec) {
@@ -382,7 +392,7 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kSmConsumerWarps);
+      mbar_init(&empty[s], kSmGroupWarps);
     }
     fence_mbar_init();
   }
@@ -409,14 +419,19 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
       }
     }
   } else {
-    const int ct = threadIdx.x - 32, cw = warp - 1;
-    uint32_t qn = 0;
-    for (uint64_t row = blockIdx.x; row < (uint64_t)d.rows; row += gridDim.x, ++qn) {
+    const int grp = (warp - 1) / kSmGroupWarps;
+    const int cw = (warp - 1) % kSmGroupWarps;
+    const int ct = (threadIdx.x - 32) % kSmGroupThreads;
+    T* gred_max = red_max + grp * kSmGroupWarps;
+    Acc* gred_sum = red_sum + grp * kSmGroupWarps;
+    uint32_t qn = (uint32_t)grp;
+    for (uint64_t row = blockIdx.x + (uint64_t)grp * gridDim.x; row < (uint64_t)d.rows;
+         row += (uint64_t)kSmGroups * gridDim.x, qn += kSmGroups) {
       const int s = (int)(qn % (uint32_t)S);
       if (!failed && !__all_sync(0xffffffffu, mbar_wait(&full[s], (qn / S) & 1u))) failed = true;
       unsigned char* stage = smem + (size_t)s * row_bytes;
       if constexpr (MODE == kRowLayerNorm) {
-        layer_norm_row<T>(d, stage, nchunk, row, ct, cw, lane, failed, red_sum);
+        layer_norm_row<T>(d, stage, nchunk, row, ct, cw, lane, grp, failed, gred_sum);
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
@@ -427,18 +442,18 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
       T mx = -INFINITY;
       if (!failed) {
 #pragma unroll 4
-        for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmConsumers) {
+        for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmGroupThreads) {
           const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
 #pragma unroll
           for (int i = 0; i < V; ++i) mx = fmax_t(mx, v.v[i]);
         }
       }
       for (int o = 16; o > 0; o >>= 1) mx = fmax_t(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      if (lane == 0) red_max[cw] = mx;
-      sm_consumer_sync();
-      T m = red_max[0];
+      if (lane == 0) gred_max[cw] = mx;
+      sm_group_sync(grp);
+      T m = gred_max[0];
 #pragma unroll
-      for (int w = 1; w < kSmConsumerWarps; ++w) m = fmax_t(m, red_max[w]);
+      for (int w = 1; w < kSmGroupWarps; ++w) m = fmax_t(m, gred_max[w]);
       if (!failed) {
         const T first = *reinterpret_cast<const T*>(stage);
         if (is_nan_val(first)) m = first;
@@ -447,7 +462,7 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
       Acc acc = Acc(0);
       if (!failed) {
 #pragma unroll 4
-        for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmConsumers) {
+        for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmGroupThreads) {
           SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
 #pragma unroll
           for (int i = 0; i < V; ++i) {
@@ -465,11 +480,11 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
         }
       }
       for (int o = 16; o > 0; o >>= 1) acc = acc + __shfl_xor_sync(0xffffffffu, acc, o);
-      if (lane == 0) red_sum[cw] = acc;
-      sm_consumer_sync();
-      Acc tot = red_sum[0];
+      if (lane == 0) gred_sum[cw] = acc;
+      sm_group_sync(grp);
+      Acc tot = gred_sum[0];
 #pragma unroll
-      for (int w = 1; w < kSmConsumerWarps; ++w) tot = tot + red_sum[w];
+      for (int w = 1; w < kSmGroupWarps; ++w) tot = tot + gred_sum[w];
       const T sum = A::from_acc(tot);
       // pass 3: e / sum.  f32: with the reciprocal of the row sum as a pair
       // yh + yl (yh = 1/sum rounded, yl the rounded rest), q0 = e*yh + e*yl
@@ -487,7 +502,7 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
           yl = (float)__dsub_rn(__drcp_rn((double)sum), (double)yh);
         }
 #pragma unroll 4
-        for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmConsumers) {
+        for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmGroupThreads) {
           const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
           SVec<T, V> r;
 #pragma unroll
