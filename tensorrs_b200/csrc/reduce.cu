@@ -79,12 +79,24 @@ bool plan_row_stream(const RedRequest& q, RedDev* d, RedChoice* c, int nk, int n
   d->tps = (d->L + tile - 1) / tile;
   const uint64_t tiles_out = (uint64_t)d->RO * (uint64_t)d->tps;
   if (tiles_out >= (1ull << 31)) return false;
+  // Split each output's tiles into P parts so the items fill the resident
+  // CTAs (two per SM) in whole waves: the smallest P whose last wave is at
+  // least 95% full, parts of at least 4 tiles (at most 64 parts).
   const DeviceInfo& dev = current_device_info();
-  const uint64_t want = (uint64_t)dev.sm_count * 4;  // items to keep every CTA busy
+  const uint64_t cap = (uint64_t)dev.sm_count * 2;
+  uint64_t max_p = tiles_out / 4;
+  if (max_p < 1) max_p = 1;
+  if (max_p > 64) max_p = 64;
   uint64_t P = 1;
-  if ((uint64_t)d->n_out < want) {
-    P = (want + d->n_out - 1) / d->n_out;
-    if (P > tiles_out) P = tiles_out;
+  double best = -1.0;
+  for (uint64_t q = 1; q <= max_p; ++q) {
+    const uint64_t tpp = (tiles_out + q - 1) / q;
+    const uint64_t parts = (tiles_out + tpp - 1) / tpp;
+    const uint64_t items = (uint64_t)d->n_out * parts;
+    const uint64_t waves = (items + cap - 1) / cap;
+    const double eff = (double)items / (double)(waves * cap);
+    if (eff > best + 1e-9) { best = eff; P = q; }
+    if (eff >= 0.95) break;
   }
   d->tpp = (int64_t)((tiles_out + P - 1) / P);
   d->P = (int64_t)((tiles_out + d->tpp - 1) / d->tpp);
