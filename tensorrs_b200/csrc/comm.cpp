@@ -87,11 +87,14 @@ Error nccl_error(ncclResult_t r, const char* what) {
                                       (n.GetErrorString ? n.GetErrorString(r) : "nccl error"));
 }
 
-// Waits until a non-blocking communicator leaves ncclInProgress.
+// Waits until a non-blocking communicator leaves ncclInProgress: a few
+// thousand yielding polls first (an enqueue that is merely busy clears in
+// microseconds, and a sleep here would starve the GPU's queue), then polls
+// 200 us apart until the deadline.
 Error wait_ready(trs_comm* c, const char* what) {
   Nccl& n = nccl();
   const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(c->timeout_ms);
-  for (;;) {
+  for (int polls = 0;; ++polls) {
     ncclResult_t st = ncclSuccess;
     ncclResult_t r = n.CommGetAsyncError(c->comm, &st);
     if (r != ncclSuccess) return nccl_error(r, "ncclCommGetAsyncError");
@@ -99,7 +102,10 @@ Error wait_ready(trs_comm* c, const char* what) {
     if (st != ncclInProgress) return nccl_error(st, what);
     if (std::chrono::steady_clock::now() > deadline)
       return make_error(TRS_ERR_TIMEOUT, std::string(what) + ": timed out");
-    std::this_thread::sleep_for(std::chrono::microseconds(200));
+    if (polls < 4096)
+      std::this_thread::yield();
+    else
+      std::this_thread::sleep_for(std::chrono::microseconds(200));
   }
 }
 
