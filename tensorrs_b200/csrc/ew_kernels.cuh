@@ -43,6 +43,12 @@
 #ifndef TRS_STREAM_TRANSCENDENTAL
 #define TRS_STREAM_TRANSCENDENTAL 0
 #endif
+//   TRS_STREAM_MIN_BYTES  tensors with fewer elements x element size than this
+//                      take the vec kernel (the pipeline's set-up does not pay
+//                      off on a few tiles per CTA)
+#ifndef TRS_STREAM_MIN_BYTES
+#define TRS_STREAM_MIN_BYTES 0
+#endif
 
 namespace trs {
 namespace ewk {
@@ -897,6 +903,7 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
     // the vector width V == VW guarantees) take the bulk-copy pipeline
     const void* sk = nullptr;
     if (TRS_STREAM_ENABLE && fits && V == VW && nb > 0 && (uint64_t)f.shape[j] * sizeof(T) >= 4096 &&
+        (uint64_t)f.n * sizeof(T) >= (uint64_t)TRS_STREAM_MIN_BYTES &&
         (TRS_STREAM_TRANSCENDENTAL || simple))
       sk = ewk::pick_stream<T>(code, fallback, nb, write, want_sum);
     int* err = sk ? async_error_word() : nullptr;

@@ -50,9 +50,16 @@ void set_fd(uint32_t* dst, uint64_t v) {
 
 // The bulk-copy row reduction: every segment start 16-byte aligned, segments
 // of at least 2 KiB, 32-bit output / segment / tile counts.
+// Tuning knob: reductions reading fewer bytes than this keep the register
+// kernels (the pipeline's set-up does not pay off on a few tiles per CTA).
+#ifndef TRS_RSTREAM_MIN_BYTES
+#define TRS_RSTREAM_MIN_BYTES 0
+#endif
+
 bool plan_row_stream(const RedRequest& q, RedDev* d, RedChoice* c, int nk, int nr, int es) {
   const int VW = 16 / es;
   if (q.raw || d->L * es < 2048 || d->L % VW) return false;
+  if ((uint64_t)d->n_out * (uint64_t)d->total * (uint64_t)es < (uint64_t)TRS_RSTREAM_MIN_BYTES) return false;
   if ((uint64_t)d->n_out >= (1ull << 31) || (uint64_t)d->RO >= (1ull << 31)) return false;
   int nb = 0;
   for (int k = 0; k < kRedOperands; ++k) {
