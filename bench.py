@@ -531,6 +531,23 @@ def run_suite(args) -> None:
         run("config4", c4[2], xb + 4 * Ch,
             lambda: C(lib.trs_reduce_broadcast_grad(ctypes.byref(vG), tgt, 4, ctypes.byref(vgb), sh)))
         del X, G, Y
+    # callers of the path: the pooling layers over config 4's activation
+    cp = ["max_pool2d 2x2 over X[64,256,56,56]", "avg_pool2d 2x2 over X[64,256,56,56]",
+          "max_pool2d 3x3 stride 2 over X[64,256,56,56]", "max_pool2d 2x2 backward to X[64,256,56,56]"]
+    if any_of("callers", cp):
+        N, Ch, H, W = 64, 256, 56, 56
+        X = device.fill_normal(t(N, Ch, H, W), 3)
+        P2, P3, GX = t(N, Ch, 28, 28), t(N, Ch, 27, 27), t(N, Ch, H, W)
+        G2 = device.fill_normal(t(N, Ch, 28, 28), 11)
+        xb, ob2, ob3 = N * Ch * H * W * 4, N * Ch * 28 * 28 * 4, N * Ch * 27 * 27 * 4
+        vX, vP2, vP3, vG2, vGX = V(X), V(P2), V(P3), V(G2), V(GX)
+        run("callers", cp[0], xb + ob2, lambda: C(lib.trs_max_pool2d(ctypes.byref(vX), 2, 2, 2, 2, ctypes.byref(vP2), sh)))
+        run("callers", cp[1], xb + ob2, lambda: C(lib.trs_avg_pool2d(ctypes.byref(vX), 2, 2, 2, 2, ctypes.byref(vP2), sh)))
+        run("callers", cp[2], xb + ob3, lambda: C(lib.trs_max_pool2d(ctypes.byref(vX), 3, 3, 2, 2, ctypes.byref(vP3), sh)))
+        run("callers", cp[3], 2 * xb + ob2,
+            lambda: C(lib.trs_max_pool2d_backward(ctypes.byref(vX), ctypes.byref(vG2), 2, 2, 2, 2, 0,
+                                                  ctypes.byref(vGX), sh)))
+        del X, P2, P3, GX, G2
     # callers of the path: LayerNorm over config 3's X, one Adam step over 2^26 f32 parameters
     cc = ["layer_norm over X[8192,16384]", "adam step, 2^26 f32 params", "sgd step, 2^26 f32 params"]
     if any_of("callers", cc):

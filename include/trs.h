@@ -342,6 +342,41 @@ trs_status trs_adam_step(trs_view* param, const trs_view* grad, trs_view* m,
                          trs_view* v, double lr, double beta1, double beta2,
                          double eps, int64_t t, trs_stream stream);
 
+/* MaxPool2d::forward (nn/pool.rs:137-144), replacing its chain
+ * reshape -> unfold_2d (linalg/tensor/conv.rs:360-418) -> max_axis(1): x is
+ * [N, C, H, W] (any strides), windows kh x kw at strides sh x sw, no padding;
+ * `out` is [N, C, (H - kh) / sh + 1, (W - kw) / sw + 1].  Each output is the
+ * window's first element replaced only by a strictly greater one, in row-major
+ * window order (so a NaN first element stays).  f32/f64.
+ * Errors: x not 4-D, out of another shape, or H < kh / W < kw: TRS_ERR_SHAPE;
+ * a stride of 0: TRS_ERR_ARG; kh * kw == 0: TRS_ERR_EMPTY_AXIS; out
+ * overlapping x: TRS_ERR_ALIAS. */
+trs_status trs_max_pool2d(const trs_view* x, int64_t kh, int64_t kw,
+                          int64_t sh, int64_t sw, trs_view* out,
+                          trs_stream stream);
+
+/* AvgPool2d::forward (nn/pool.rs:223-233): unfold_2d -> sum_axis(1) ->
+ * divided by kh * kw.  Each window is summed in the element type in
+ * row-major order from 0, as sum_axis does (base.rs:1051-1107), then divided
+ * once, so the result is the reference's bit for bit.  Shapes and errors as
+ * trs_max_pool2d, except that an empty window (kh * kw == 0) gives 0 / 0. */
+trs_status trs_avg_pool2d(const trs_view* x, int64_t kh, int64_t kw,
+                          int64_t sh, int64_t sw, trs_view* out,
+                          trs_stream stream);
+
+/* The gradient MaxPool2d passes back to its input: max_axis's backward
+ * (autodiff/core.rs:352-375: each window's gradient to the first of its
+ * largest elements, argmax_axis base.rs:1458-1505), then unfold's backward
+ * fold_2d (conv.rs:434-488: a pixel sums, from 0 and in window order, the
+ * gradients of the windows that read it).  grad_out is [N, C, OH, OW] and
+ * grad_x [N, C, H, W]; with accumulate != 0, grad_x = grad_x + that sum (the
+ * accumulation `current + grad` of autodiff/traits.rs:141-150), else
+ * grad_x = the sum.  grad_x may not overlap x or grad_out (TRS_ERR_ALIAS). */
+trs_status trs_max_pool2d_backward(const trs_view* x, const trs_view* grad_out,
+                                   int64_t kh, int64_t kw, int64_t sh,
+                                   int64_t sw, int32_t accumulate,
+                                   trs_view* grad_x, trs_stream stream);
+
 /* ------------------------------------------------------------------ */
 /* Seeded synthetic inputs                                              */
 /* ------------------------------------------------------------------ */

@@ -84,6 +84,8 @@ def load():
             "orc_fill_normal": (c_int, [c_int, c_void_p, c_int64, c_uint64]),
             "orc_opt_step": (c_int, [c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_double,
                                      c_double, c_double, c_double, c_int64]),
+            "orc_pool2d": (c_int, [c_int, V, c_int64, c_int64, c_int64, c_int64, c_void_p, I64P]),
+            "orc_max_pool2d_backward": (c_int, [V, V, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(lib, name)
@@ -253,6 +255,37 @@ def opt_step(kind: str, p: np.ndarray, g: np.ndarray, m: np.ndarray | None, v: n
     nul = None
     _check(load().orc_opt_step(k, dt, p.ctypes.data, g.ctypes.data, m.ctypes.data if m is not None else nul,
                                v.ctypes.data if v is not None else nul, p.size, lr, b1, b2, eps, t))
+
+
+def pool2d(kind: str, x: HostView, kernel, stride=None) -> np.ndarray:
+    """MaxPool2d / AvgPool2d forward ("max" / "avg") of an [N, C, H, W] view, as
+    the reference computes it (reshape, unfold_2d, max_axis or sum_axis / k)."""
+    kh, kw = kernel
+    sh, sw = stride if stride is not None else kernel
+    n_out = 1
+    if len(x.shape) == 4 and sh > 0 and sw > 0 and x.shape[2] >= kh >= 0 and x.shape[3] >= kw >= 0:
+        N, C, H, W = x.shape
+        n_out = N * C * ((H - kh) // sh + 1) * ((W - kw) // sw + 1)
+    out = _out_buf(x.dtype, max(n_out, 1))
+    shp = (c_int64 * 4)()
+    _check(load().orc_pool2d(1 if kind == "max" else 0, ctypes.byref(x.c()), kh, kw, sh, sw, out.ctypes.data, shp))
+    shape = [shp[i] for i in range(4)]
+    return out[: int(np.prod(shape, dtype=np.int64))].reshape(shape)
+
+
+def max_pool2d_backward(x: HostView, g: HostView, kernel, stride=None, current: np.ndarray | None = None):
+    """The gradient MaxPool2d passes to x (max_axis backward, fold_2d), added to
+    `current` (same shape as x) when given."""
+    kh, kw = kernel
+    sh, sw = stride if stride is not None else kernel
+    out = _out_buf(x.dtype, max(x.numel(), 1))
+    cur = None
+    if current is not None:
+        cur = np.ascontiguousarray(current, dtype=x.dtype)
+        assert cur.size == x.numel()
+    _check(load().orc_max_pool2d_backward(ctypes.byref(x.c()), ctypes.byref(g.c()), kh, kw, sh, sw,
+                                          cur.ctypes.data if cur is not None else None, out.ctypes.data))
+    return out[: x.numel()].reshape(x.shape)
 
 
 def sum_f64(x: HostView) -> tuple[float, float]:

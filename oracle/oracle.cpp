@@ -615,6 +615,139 @@ inline uint64_t splitmix64(uint64_t seed, uint64_t i) {
   return z ^ (z >> 31);
 }
 
+// unfold_2d (linalg/tensor/conv.rs:360-418): every window of a packed
+// [batch, channels, height, width] image as a row of channels * kh * kw values
+// in (c, i, j) order, rows in (n, oh, ow) order; a window position inside the
+// padding stays 0.
+template <class T>
+std::vector<T> unfold_2d(const std::vector<T>& src, int64_t batch, int64_t channels, int64_t height,
+                         int64_t width, int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
+                         int64_t* out_h, int64_t* out_w) {
+  const int64_t oh_n = (height + 2 * ph - kh) / sh + 1, ow_n = (width + 2 * pw - kw) / sw + 1;
+  const int64_t patch = channels * kh * kw;
+  std::vector<T> data((size_t)(batch * oh_n * ow_n * patch), T(0));
+  for_outputs(batch * oh_n * ow_n, [&](int64_t row) {
+    const int64_t ow = row % ow_n, oh = (row / ow_n) % oh_n, n = row / (oh_n * ow_n);
+    T* out = data.data() + row * patch;
+    for (int64_t c = 0; c < channels; ++c)
+      for (int64_t i = 0; i < kh; ++i) {
+        const int64_t y = oh * sh + i - ph;
+        if (y < 0 || y >= height) continue;
+        for (int64_t j = 0; j < kw; ++j) {
+          const int64_t x = ow * sw + j - pw;
+          if (x < 0 || x >= width) continue;
+          out[c * kh * kw + i * kw + j] = src[(size_t)(((n * channels + c) * height + y) * width + x)];
+        }
+      }
+  });
+  *out_h = oh_n;
+  *out_w = ow_n;
+  return data;
+}
+
+// fold_2d (conv.rs:434-488): adds the rows of an unfold back into a zeroed
+// [batch, channels, height, width] image, image by image, rows in (oh, ow)
+// order, each row in (c, i, j) order.
+template <class T>
+std::vector<T> fold_2d(const std::vector<T>& src, int64_t batch, int64_t channels, int64_t height, int64_t width,
+                       int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw) {
+  const int64_t oh_n = (height + 2 * ph - kh) / sh + 1, ow_n = (width + 2 * pw - kw) / sw + 1;
+  const int64_t patch = channels * kh * kw;
+  std::vector<T> data((size_t)(batch * channels * height * width), T(0));
+  for_outputs(batch, [&](int64_t n) {
+    T* image = data.data() + n * channels * height * width;
+    for (int64_t oh = 0; oh < oh_n; ++oh)
+      for (int64_t ow = 0; ow < ow_n; ++ow) {
+        const int64_t row = (n * oh_n + oh) * ow_n + ow;
+        for (int64_t c = 0; c < channels; ++c)
+          for (int64_t i = 0; i < kh; ++i) {
+            const int64_t y = oh * sh + i - ph;
+            if (y < 0 || y >= height) continue;
+            for (int64_t j = 0; j < kw; ++j) {
+              const int64_t x = ow * sw + j - pw;
+              if (x < 0 || x >= width) continue;
+              T& px = image[(c * height + y) * width + x];
+              px = Arith<T>::add(px, src[(size_t)(row * patch + c * kh * kw + i * kw + j)]);
+            }
+          }
+      }
+  });
+  return data;
+}
+
+// The checks of pool_dims (nn/pool.rs:36-41), with_stride (pool.rs:115-118)
+// and unfold_dims (conv.rs:490-510).
+template <class T>
+int pool_dims(const Tensor<T>& x, int64_t kh, int64_t kw, int64_t sh, int64_t sw) {
+  if (x.shape.size() != 4) { g_msg = "!!!MaxPool2d expects [batch, channels, height, width]!!!"; return ERR_SHAPE; }
+  if (sh <= 0 || sw <= 0) { g_msg = "!!!MaxPool2d: stride must be positive!!!"; return ERR_ARG; }
+  if (kh < 0 || kw < 0 || x.shape[2] < kh || x.shape[3] < kw) { g_msg = "input smaller than the kernel"; return ERR_SHAPE; }
+  return OK;
+}
+
+// MaxPool2d::forward (pool.rs:137-144) and AvgPool2d::forward (pool.rs:223-233):
+// windows_per_channel (pool.rs:25-33: reshape to [N*C, 1, H, W], unfold), then
+// max_axis(1), or sum_axis(1) divided by kh*kw -- a VarRef divided by a scalar
+// leaf, i.e. binary_op's division (ops.rs:498) against a [1] tensor.
+template <class T>
+int pool2d(bool is_max, const Tensor<T>& x, int64_t kh, int64_t kw, int64_t sh, int64_t sw, std::vector<T>* out,
+           std::vector<int64_t>* out_shape) {
+  int st = pool_dims(x, kh, kw, sh, sw);
+  if (st) return st;
+  const int64_t N = x.shape[0], C = x.shape[1], H = x.shape[2], W = x.shape[3];
+  int64_t oh, ow;
+  std::vector<T> cols = unfold_2d(packed_data(x), N * C, 1, H, W, kh, kw, sh, sw, 0, 0, &oh, &ow);
+  Tensor<T> ct = make_tensor(std::move(cols), {N * C * oh * ow, kh * kw});
+  if (is_max) {
+    std::vector<T> v;
+    std::vector<int64_t> idx, os;
+    st = max_argmax_axis(ct, 1, &v, &idx, &os);
+    if (st) return st;
+    *out = std::move(v);
+  } else {
+    Tensor<T> summed, q;
+    st = sum_axis(ct, 1, false, &summed);
+    if (st) return st;
+    st = bin(DIV, summed, make_scalar<T>((T)(kh * kw)), &q);
+    if (st) return st;
+    *out = packed_data(q);
+  }
+  *out_shape = {N, C, oh, ow};
+  return OK;
+}
+
+// The gradient MaxPool2d passes to its input: reshape's backward (the same
+// elements), max_axis's backward (autodiff/core.rs:352-375: each row's gradient
+// to its argmax, 0 elsewhere), unfold's backward fold_2d (core.rs:397-405),
+// reshape back, and the accumulation `current + grad` (autodiff/traits.rs:
+// 141-150) when `current` is given.  The intermediate gradients the reference
+// also accumulates from 0 (0 + g) only turn -0 into +0, which fold_2d's sum
+// from 0 does anyway.
+template <class T>
+int max_pool2d_backward(const Tensor<T>& x, const Tensor<T>& g, int64_t kh, int64_t kw, int64_t sh, int64_t sw,
+                        const T* current, std::vector<T>* out) {
+  int st = pool_dims(x, kh, kw, sh, sw);
+  if (st) return st;
+  const int64_t N = x.shape[0], C = x.shape[1], H = x.shape[2], W = x.shape[3];
+  int64_t oh, ow;
+  std::vector<T> cols = unfold_2d(packed_data(x), N * C, 1, H, W, kh, kw, sh, sw, 0, 0, &oh, &ow);
+  const int64_t rows = N * C * oh * ow, patch = kh * kw;
+  if (g.shape != std::vector<int64_t>{N, C, oh, ow}) { g_msg = "grad_out shape"; return ERR_SHAPE; }
+  Tensor<T> ct = make_tensor(std::move(cols), {rows, patch});
+  std::vector<T> v;
+  std::vector<int64_t> winners, os;
+  st = max_argmax_axis(ct, 1, &v, &winners, &os);
+  if (st) return st;
+  std::vector<T> grad = packed_data(g);
+  std::vector<T> data((size_t)(rows * patch), T(0));
+  for (int64_t r = 0; r < rows; ++r) data[(size_t)(r * patch + winners[r])] = grad[(size_t)r];
+  std::vector<T> img = fold_2d(data, N * C, 1, H, W, kh, kw, sh, sw, 0, 0);
+  if (current)
+    for (size_t i = 0; i < img.size(); ++i) img[i] = Arith<T>::add(current[i], img[i]);
+  *out = std::move(img);
+  return OK;
+}
+
 }  // namespace
 
 #define DISPATCH(dt, ...)                                          \
@@ -878,6 +1011,38 @@ int orc_opt_step(int kind, int dtype, void* p, const void* g, void* m, void* v, 
     opt_step_t<double>(kind, (double*)p, (const double*)g, (double*)m, (double*)v, n, lr, b1, b2, eps, t);
   else
     return ERR_DTYPE;
+  return OK;
+}
+
+// MaxPool2d / AvgPool2d forward (is_max 1 / 0); `out` receives the packed
+// [N, C, OH, OW] result and out_shape its 4 dimensions.
+int orc_pool2d(int is_max, const View* x, int64_t kh, int64_t kw, int64_t sh, int64_t sw, void* out,
+               int64_t* out_shape) {
+  if (x->dtype != F32 && x->dtype != F64) return ERR_DTYPE;
+  DISPATCH(x->dtype, {
+    std::vector<T> r;
+    std::vector<int64_t> os;
+    int st = pool2d(is_max != 0, from_view<T>(x), kh, kw, sh, sw, &r, &os);
+    if (st) return st;
+    std::memcpy(out, r.data(), r.size() * sizeof(T));
+    for (int i = 0; i < 4; ++i) out_shape[i] = os[i];
+  });
+  return OK;
+}
+
+// MaxPool2d's gradient to x, packed [N, C, H, W]; `current` (packed, nullable)
+// is the gradient it is accumulated onto.
+int orc_max_pool2d_backward(const View* x, const View* g, int64_t kh, int64_t kw, int64_t sh, int64_t sw,
+                            const void* current, void* out) {
+  if (x->dtype != F32 && x->dtype != F64) return ERR_DTYPE;
+  if (g->dtype != x->dtype) return ERR_DTYPE;
+  DISPATCH(x->dtype, {
+    std::vector<T> r;
+    int st = max_pool2d_backward(from_view<T>(x), from_view<T>(g), kh, kw, sh, sw,
+                                 static_cast<const T*>(current), &r);
+    if (st) return st;
+    std::memcpy(out, r.data(), r.size() * sizeof(T));
+  });
   return OK;
 }
 

@@ -103,6 +103,9 @@ _SIGNATURES = {
     "trs_sgd_step": (c_int32, [_V, _V, c_double, c_void_p]),
     "trs_rmsprop_step": (c_int32, [_V, _V, _V, c_double, c_double, c_double, c_void_p]),
     "trs_adam_step": (c_int32, [_V, _V, _V, _V, c_double, c_double, c_double, c_double, c_int64, c_void_p]),
+    "trs_max_pool2d": (c_int32, [_V, c_int64, c_int64, c_int64, c_int64, _V, c_void_p]),
+    "trs_avg_pool2d": (c_int32, [_V, c_int64, c_int64, c_int64, c_int64, _V, c_void_p]),
+    "trs_max_pool2d_backward": (c_int32, [_V, _V, c_int64, c_int64, c_int64, c_int64, c_int32, _V, c_void_p]),
     "trs_fill_uniform": (c_int32, [_V, c_uint64, c_uint64, c_double, c_double, c_void_p]),
     "trs_fill_normal": (c_int32, [_V, c_uint64, c_uint64, c_void_p]),
     "trs_set_device": (c_int32, [c_int32]),

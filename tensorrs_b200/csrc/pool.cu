@@ -1,0 +1,403 @@
+// pool.cu -- the pooling layers of nn/pool.rs, each as one kernel.
+//
+// MaxPool2d::forward and AvgPool2d::forward (nn/pool.rs:137-144, 223-233)
+// fold the channels into the batch (windows_per_channel, pool.rs:25-33), lay
+// every window out as a row with unfold_2d (linalg/tensor/conv.rs:360-418: an
+// im2col copy holding kh*kw values per output), and reduce the rows with
+// max_axis (base.rs:1396-1436) or with sum_axis (base.rs:1051-1107) followed by
+// a division by kh*kw.  Without padding a window is a strided view of the
+// input, so each output here reads its window straight from the input: one
+// read of the input and one write of the output, no im2col buffer.
+//
+//   pool_fwd_kernel<T, MODE, KW>  KW > 0: kw == stride_w == KW, unit-stride
+//       rows aligned to 16 bytes; a thread loads one 16-byte strip per window
+//       row, which holds the windows of 16 / (KW * size) neighbouring outputs.
+//       KW == 0: any window; one thread per output, scalar loads (neighbouring
+//       threads share their rows through L1).
+//   pool_max_bwd_kernel<T>  the gradient MaxPool2d passes back to its input:
+//       max_axis's backward (autodiff/core.rs:352-375) gives each window's
+//       gradient to the first of its largest elements (argmax_axis,
+//       base.rs:1458-1505) and unfold's backward fold_2d (conv.rs:434-488)
+//       sums, per pixel, the gradients of the windows that read it, in window
+//       order from 0.  One thread per input pixel walks the windows covering
+//       it in that order and finds each window's winner again; with
+//       `accumulate` it adds the sum to the gradient already held (the
+//       `current + grad` of autodiff/traits.rs:141-150).
+//
+// Order of floating-point operations: max keeps the window's first element and
+// replaces it only by a strictly greater one (a NaN first element stays); the
+// average adds the window in row-major order in the element type, from +0,
+// then divides once by kh*kw -- the reference's f32 / f64 operations in its
+// order, so both are bit-exact.
+#include <cstring>
+
+#include "../../include/trs.h"
+#include "kernels.cuh"
+
+namespace trs {
+namespace {
+
+enum PoolMode { kPoolMax = 0, kPoolAvg = 1 };
+
+struct PoolDev {
+  const void* x;
+  const void* g;
+  void* out;
+  int64_t x_off, g_off, o_off;
+  int64_t xs[4], gs[4], os[4];  // strides of [N, C, H, W] / [N, C, OH, OW]
+  int64_t H, W, OH, OW;
+  int32_t kh, kw, sh, sw;
+  int64_t items;   // work items: outputs (or strips), or input pixels
+  int64_t inner;   // items along the last axis of one row
+  FastDiv f_inner, f_rows, f_c;  // items per row, rows per plane, channels
+  int32_t fast;    // items < 2^32: 32-bit index arithmetic
+  int32_t accumulate;
+};
+
+// items -> (n, c, row, col), the last one counted in items of the row.
+__device__ __forceinline__ void pool_coords(const PoolDev& d, uint64_t i, int64_t* n, int64_t* c, int64_t* r,
+                                            int64_t* q) {
+  if (d.fast) {
+    const uint32_t a = (uint32_t)i;
+    const uint32_t b = fdiv(a, d.f_inner);
+    const uint32_t e = fdiv(b, d.f_rows);
+    const uint32_t f = fdiv(e, d.f_c);
+    *q = a - b * d.f_inner.d;
+    *r = b - e * d.f_rows.d;
+    *c = e - f * d.f_c.d;
+    *n = f;
+  } else {
+    const uint64_t t = i / d.f_inner.d;
+    const uint64_t u = t / d.f_rows.d;
+    const uint64_t v = u / d.f_c.d;
+    *q = (int64_t)(i - t * d.f_inner.d);
+    *r = (int64_t)(t - u * d.f_rows.d);
+    *c = (int64_t)(u - v * d.f_c.d);
+    *n = (int64_t)v;
+  }
+}
+
+template <class T, int V>
+struct alignas(sizeof(T) * V) PVec {
+  T v[V];
+};
+
+// One window by scalar loads, in row-major order.
+template <class T, int MODE>
+__device__ __forceinline__ T pool_window(const T* __restrict__ x, int64_t base, const PoolDev& d) {
+  using A = Arith<T>;
+  if constexpr (MODE == kPoolMax) {
+    T best = __ldg(x + base);
+    for (int u = 0; u < d.kh; ++u)
+      for (int v = (u == 0 ? 1 : 0); v < d.kw; ++v) {
+        const T val = __ldg(x + base + u * d.xs[2] + v * d.xs[3]);
+        if (val > best) best = val;
+      }
+    return best;
+  } else {
+    T acc = T(0);
+    for (int u = 0; u < d.kh; ++u)
+      for (int v = 0; v < d.kw; ++v) acc = A::add(acc, __ldg(x + base + u * d.xs[2] + v * d.xs[3]));
+    return A::div(acc, (T)((int64_t)d.kh * d.kw), nullptr);
+  }
+}
+
+template <class T, int MODE, int KW>
+__global__ void __launch_bounds__(256) pool_fwd_kernel(const PoolDev d) {
+  constexpr int VW = 16 / sizeof(T);
+  constexpr int Q = KW > 0 ? VW / KW : 1;  // outputs per item
+  using A = Arith<T>;
+  const T* __restrict__ x = static_cast<const T*>(d.x);
+  T* __restrict__ out = static_cast<T*>(d.out);
+  for (uint64_t it = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; it < (uint64_t)d.items;
+       it += (uint64_t)gridDim.x * blockDim.x) {
+    int64_t n, c, i, q;
+    pool_coords(d, it, &n, &c, &i, &q);
+    const int64_t row0 = d.x_off + n * d.xs[0] + c * d.xs[1] + i * d.sh * d.xs[2];
+    const int64_t obase = d.o_off + n * d.os[0] + c * d.os[1] + i * d.os[2];
+    if constexpr (KW == 0) {
+      out[obase + q * d.os[3]] = pool_window<T, MODE>(x, row0 + q * d.sw * d.xs[3], d);
+    } else {
+      const int64_t col0 = q * VW;  // first input column of the strip
+      const int64_t j0 = q * Q;     // its first output
+      if (col0 + VW <= d.W) {
+        T r[Q];
+#pragma unroll
+        for (int o = 0; o < Q; ++o) r[o] = T(0);  // an empty window (kh == 0) averages to 0 / 0
+        const T scale = (T)((int64_t)d.kh * KW);
+        for (int u = 0; u < d.kh; ++u) {
+          const PVec<T, VW> s = *reinterpret_cast<const PVec<T, VW>*>(x + row0 + u * d.xs[2] + col0);
+#pragma unroll
+          for (int o = 0; o < Q; ++o) {
+#pragma unroll
+            for (int v = 0; v < KW; ++v) {
+              const T val = s.v[o * KW + v];
+              if constexpr (MODE == kPoolMax) {
+                if (u == 0 && v == 0) r[o] = val;
+                else if (val > r[o]) r[o] = val;
+              } else {
+                r[o] = A::add(u == 0 && v == 0 ? T(0) : r[o], val);
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int o = 0; o < Q; ++o) {
+          if (j0 + o < d.OW) {
+            T res = r[o];
+            if constexpr (MODE == kPoolAvg) res = A::div(res, scale, nullptr);
+            out[obase + (j0 + o) * d.os[3]] = res;
+          }
+        }
+      } else {
+        // the row's ragged end: windows one by one
+        for (int o = 0; o < Q; ++o)
+          if (j0 + o < d.OW) out[obase + (j0 + o) * d.os[3]] = pool_window<T, MODE>(x, row0 + (j0 + o) * KW, d);
+      }
+    }
+  }
+}
+
+template <class T>
+__global__ void __launch_bounds__(256) pool_max_bwd_kernel(const PoolDev d) {
+  using A = Arith<T>;
+  const T* __restrict__ x = static_cast<const T*>(d.x);
+  const T* __restrict__ g = static_cast<const T*>(d.g);
+  T* out = static_cast<T*>(d.out);
+  for (uint64_t it = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; it < (uint64_t)d.items;
+       it += (uint64_t)gridDim.x * blockDim.x) {
+    int64_t n, c, y, xc;
+    pool_coords(d, it, &n, &c, &y, &xc);
+    const int64_t plane = d.x_off + n * d.xs[0] + c * d.xs[1];
+    const int64_t gplane = d.g_off + n * d.gs[0] + c * d.gs[1];
+    // windows oh with oh*sh <= y <= oh*sh + kh - 1, likewise ow
+    const int64_t oh_lo = y >= d.kh ? (y - d.kh + d.sh) / d.sh : 0;
+    int64_t oh_hi = y / d.sh;
+    if (oh_hi > d.OH - 1) oh_hi = d.OH - 1;
+    const int64_t ow_lo = xc >= d.kw ? (xc - d.kw + d.sw) / d.sw : 0;
+    int64_t ow_hi = xc / d.sw;
+    if (ow_hi > d.OW - 1) ow_hi = d.OW - 1;
+    T acc = T(0);
+    for (int64_t oh = oh_lo; oh <= oh_hi; ++oh) {
+      for (int64_t ow = ow_lo; ow <= ow_hi; ++ow) {
+        const int64_t base = plane + oh * d.sh * d.xs[2] + ow * d.sw * d.xs[3];
+        T best = __ldg(x + base);
+        int bu = 0, bv = 0;
+        for (int u = 0; u < d.kh; ++u)
+          for (int v = (u == 0 ? 1 : 0); v < d.kw; ++v) {
+            const T val = __ldg(x + base + u * d.xs[2] + v * d.xs[3]);
+            if (val > best) { best = val; bu = u; bv = v; }
+          }
+        if (oh * d.sh + bu == y && ow * d.sw + bv == xc)
+          acc = A::add(acc, __ldg(g + gplane + oh * d.gs[2] + ow * d.gs[3]));
+      }
+    }
+    const int64_t o = d.o_off + n * d.os[0] + c * d.os[1] + y * d.os[2] + xc * d.os[3];
+    out[o] = d.accumulate ? A::add(out[o], acc) : acc;
+  }
+}
+
+// One wave of 256-thread CTAs (as many per SM as fit), each thread looping.
+template <class K>
+unsigned pool_grid(K kernel, uint64_t items) {
+  int per_sm = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, 0) != cudaSuccess || per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
+  const uint64_t cap = (uint64_t)current_device_info().sm_count * (uint64_t)per_sm;
+  const uint64_t need = (items + 255) / 256;
+  return (unsigned)(need < cap ? (need < 1 ? 1 : need) : cap);
+}
+
+// [lo, hi) byte range a view can touch.
+void byte_range(const trs_view* v, int64_t* lo, int64_t* hi) {
+  const int es = dtype_size(v->dtype);
+  int64_t a = v->offset, b = v->offset;
+  for (int i = 0; i < v->ndim; ++i) {
+    const int64_t span = (v->shape[i] - 1) * v->strides[i];
+    if (span > 0) b += span; else a += span;
+  }
+  *lo = (int64_t)(uintptr_t)v->data + a * es;
+  *hi = (int64_t)(uintptr_t)v->data + (b + 1) * es;
+}
+
+bool overlaps(const trs_view* a, const trs_view* b) {
+  if (numel_of(a->shape, a->ndim) == 0 || numel_of(b->shape, b->ndim) == 0) return false;
+  int64_t alo, ahi, blo, bhi;
+  byte_range(a, &alo, &ahi);
+  byte_range(b, &blo, &bhi);
+  return alo < bhi && blo < ahi;
+}
+
+Error check_4d(const trs_view* v, const char* what, int dt, const int64_t* want) {
+  Error e = validate_view(v, what);
+  if (!e.ok()) return e;
+  if (v->dtype != dt) return make_error(TRS_ERR_DTYPE, std::string(what) + ": dtype differs from x");
+  bool same = v->ndim == 4;
+  for (int i = 0; same && i < 4; ++i) same = v->shape[i] == want[i];
+  if (!same) return make_error(TRS_ERR_SHAPE, std::string(what) + ": wrong shape");
+  return Error{};
+}
+
+// Shape rules of pool_dims (pool.rs:36-41), with_stride (pool.rs:115-118) and
+// unfold_dims (conv.rs:490-510); fills the geometry of d.
+Error pool_setup(const char* layer, const trs_view* x, int64_t kh, int64_t kw, int64_t sh, int64_t sw, bool is_max,
+                 PoolDev* d) {
+  std::memset(d, 0, sizeof(*d));
+  if (!x) return make_error(TRS_ERR_ARG, "null view");
+  Error e = validate_view(x, "x");
+  if (!e.ok()) return e;
+  if (!is_float(x->dtype)) return make_error(TRS_ERR_DTYPE, std::string(layer) + " needs f32 or f64");
+  if (x->ndim != 4)
+    return make_error(TRS_ERR_SHAPE, std::string("!!!") + layer + " expects [batch, channels, height, width]!!!");
+  if (sh <= 0 || sw <= 0) return make_error(TRS_ERR_ARG, std::string("!!!") + layer + ": stride must be positive!!!");
+  if (kh < 0 || kw < 0 || kh > (1 << 20) || kw > (1 << 20) || sh > (1 << 30) || sw > (1 << 30))
+    return make_error(TRS_ERR_ARG, "window or stride out of range");
+  if (x->shape[2] < kh || x->shape[3] < kw)
+    return make_error(TRS_ERR_SHAPE, "!!!unfold_2d(): the input is smaller than the kernel!!!");
+  if (is_max && kh * kw == 0) return make_error(TRS_ERR_EMPTY_AXIS, "!!!Cannot reduce an empty axis!!!");
+  // the index arithmetic divides by W, H and C as 32-bit divisors
+  if (x->shape[1] >= (1ll << 32) || x->shape[2] >= (1ll << 32) || x->shape[3] >= (1ll << 32))
+    return make_error(TRS_ERR_ARG, "pool: a dimension of 2^32 or more");
+  d->H = x->shape[2];
+  d->W = x->shape[3];
+  d->OH = (d->H - kh) / sh + 1;
+  d->OW = (d->W - kw) / sw + 1;
+  d->kh = (int32_t)kh;
+  d->kw = (int32_t)kw;
+  d->sh = (int32_t)sh;
+  d->sw = (int32_t)sw;
+  d->x = x->data;
+  d->x_off = x->offset;
+  for (int i = 0; i < 4; ++i) d->xs[i] = x->strides[i];
+  return Error{};
+}
+
+void set_items(PoolDev* d, int64_t planes, int64_t C, int64_t rows, int64_t inner) {
+  d->inner = inner;
+  d->items = planes * rows * inner;
+  d->fast = (uint64_t)d->items < (1ull << 32) ? 1 : 0;
+  d->f_inner = make_fastdiv((uint32_t)(inner < 1 ? 1 : inner));
+  d->f_rows = make_fastdiv((uint32_t)(rows < 1 ? 1 : rows));
+  d->f_c = make_fastdiv((uint32_t)(C < 1 ? 1 : C));
+}
+
+template <class T>
+Error launch_pool_fwd(PoolDev d, int mode, int64_t N, int64_t C, cudaStream_t stream) {
+  constexpr int VW = 16 / sizeof(T);
+  // the strip path: kw == stride_w dividing 16 bytes, unit-stride rows whose
+  // starts are all 16-byte aligned
+  const int es = sizeof(T);
+  bool strip = d.kw == d.sw && d.kw > 0 && VW % d.kw == 0 && d.xs[3] == 1;
+  if (strip) {
+    if (((uintptr_t)d.x + (uintptr_t)(d.x_off * es)) % 16) strip = false;
+    for (int i = 0; i < 3; ++i)
+      if (d.xs[i] % VW) strip = false;
+  }
+  const int64_t rows = d.OH;
+  auto go = [&](auto kernel) {
+    kernel<<<pool_grid(kernel, (uint64_t)d.items), 256, 0, stream>>>(d);
+    return check_launch("pool kernel");
+  };
+  if (!strip) {
+    set_items(&d, N * C, C, rows, d.OW);
+    return mode == kPoolMax ? go(pool_fwd_kernel<T, kPoolMax, 0>) : go(pool_fwd_kernel<T, kPoolAvg, 0>);
+  }
+  const int Q = VW / d.kw;
+  set_items(&d, N * C, C, rows, (d.OW + Q - 1) / Q);
+#define TRS_POOL_LAUNCH(KWV) \
+  if (d.kw == KWV) return mode == kPoolMax ? go(pool_fwd_kernel<T, kPoolMax, KWV>) : go(pool_fwd_kernel<T, kPoolAvg, KWV>);
+  TRS_POOL_LAUNCH(1)
+  TRS_POOL_LAUNCH(2)
+  if constexpr (VW >= 4) {
+    TRS_POOL_LAUNCH(4)
+  }
+#undef TRS_POOL_LAUNCH
+  return make_error(TRS_ERR_ARG, "pool: no strip kernel for this window");
+}
+
+Error run_pool(int mode, const trs_view* x, int64_t kh, int64_t kw, int64_t sh, int64_t sw, const trs_view* out,
+               cudaStream_t stream) {
+  const char* layer = mode == kPoolMax ? "MaxPool2d" : "AvgPool2d";
+  PoolDev d;
+  Error e = pool_setup(layer, x, kh, kw, sh, sw, mode == kPoolMax, &d);
+  if (!e.ok()) return e;
+  if (!out) return make_error(TRS_ERR_ARG, "null view");
+  const int64_t N = x->shape[0], C = x->shape[1];
+  const int64_t want[4] = {N, C, d.OH, d.OW};
+  e = check_4d(out, "output", x->dtype, want);
+  if (!e.ok()) return e;
+  if (overlaps(x, out)) return make_error(TRS_ERR_ALIAS, "pool: the output overlaps the input");
+  if (N * C * d.OH * d.OW == 0) return Error{};
+  d.out = out->data;
+  d.o_off = out->offset;
+  for (int i = 0; i < 4; ++i) d.os[i] = out->strides[i];
+  if (x->dtype == TRS_F32) return launch_pool_fwd<float>(d, mode, N, C, stream);
+  return launch_pool_fwd<double>(d, mode, N, C, stream);
+}
+
+Error run_max_pool_backward(const trs_view* x, const trs_view* g, int64_t kh, int64_t kw, int64_t sh, int64_t sw,
+                            int accumulate, const trs_view* gx, cudaStream_t stream) {
+  PoolDev d;
+  Error e = pool_setup("MaxPool2d", x, kh, kw, sh, sw, true, &d);
+  if (!e.ok()) return e;
+  if (!g || !gx) return make_error(TRS_ERR_ARG, "null view");
+  const int64_t N = x->shape[0], C = x->shape[1];
+  const int64_t gshape[4] = {N, C, d.OH, d.OW};
+  e = check_4d(g, "grad_out", x->dtype, gshape);
+  if (!e.ok()) return e;
+  e = check_4d(gx, "grad_x", x->dtype, x->shape);
+  if (!e.ok()) return e;
+  if (overlaps(gx, x) || overlaps(gx, g))
+    return make_error(TRS_ERR_ALIAS, "pool backward: grad_x overlaps an input");
+  if (N * C * d.H * d.W == 0) return Error{};
+  d.g = g->data;
+  d.g_off = g->offset;
+  d.out = gx->data;
+  d.o_off = gx->offset;
+  for (int i = 0; i < 4; ++i) {
+    d.gs[i] = g->strides[i];
+    d.os[i] = gx->strides[i];
+  }
+  d.accumulate = accumulate ? 1 : 0;
+  set_items(&d, N * C, C, d.H, d.W);
+  if (x->dtype == TRS_F32) {
+    auto k = pool_max_bwd_kernel<float>;
+    k<<<pool_grid(k, (uint64_t)d.items), 256, 0, stream>>>(d);
+  } else {
+    auto k = pool_max_bwd_kernel<double>;
+    k<<<pool_grid(k, (uint64_t)d.items), 256, 0, stream>>>(d);
+  }
+  return check_launch("max pool backward kernel");
+}
+
+trs_status finish(const Error& e) {
+  if (!e.ok()) set_last_error(e.msg);
+  return e.status;
+}
+
+}  // namespace
+}  // namespace trs
+
+using namespace trs;
+
+extern "C" {
+
+trs_status trs_max_pool2d(const trs_view* x, int64_t kh, int64_t kw, int64_t sh, int64_t sw, trs_view* out,
+                          trs_stream stream) {
+  return finish(run_pool(kPoolMax, x, kh, kw, sh, sw, out, static_cast<cudaStream_t>(stream)));
+}
+
+trs_status trs_avg_pool2d(const trs_view* x, int64_t kh, int64_t kw, int64_t sh, int64_t sw, trs_view* out,
+                          trs_stream stream) {
+  return finish(run_pool(kPoolAvg, x, kh, kw, sh, sw, out, static_cast<cudaStream_t>(stream)));
+}
+
+trs_status trs_max_pool2d_backward(const trs_view* x, const trs_view* grad_out, int64_t kh, int64_t kw, int64_t sh,
+                                   int64_t sw, int32_t accumulate, trs_view* grad_x, trs_stream stream) {
+  return finish(run_max_pool_backward(x, grad_out, kh, kw, sh, sw, accumulate, grad_x,
+                                      static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

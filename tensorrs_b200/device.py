@@ -150,6 +150,46 @@ def adam_step(param: torch.Tensor, grad: torch.Tensor, m: torch.Tensor, v: torch
           ctypes.byref(view_of(v)), float(lr), float(beta1), float(beta2), float(eps), int(t), stream_handle())
 
 
+def pooled_size(size: tuple[int, int], kernel: tuple[int, int], stride: tuple[int, int]) -> tuple[int, int]:
+    """The spatial size a pooling layer turns `size` into (pooled_size, nn/pool.rs:8-17;
+    MaxPool2d::output_size / AvgPool2d::output_size).  No padding: a window that
+    would hang over the edge is not taken."""
+    if stride[0] <= 0 or stride[1] <= 0:
+        raise ValueError("!!!MaxPool2d: stride must be positive!!!")
+    if size[0] < kernel[0] or size[1] < kernel[1]:
+        raise ValueError("the input is smaller than one window")
+    return (size[0] - kernel[0]) // stride[0] + 1, (size[1] - kernel[1]) // stride[1] + 1
+
+
+def max_pool2d(x: abi.View, kernel: tuple[int, int], out: torch.Tensor,
+               stride: tuple[int, int] | None = None) -> torch.Tensor:
+    """MaxPool2d::forward (nn/pool.rs:137-144) of an [N, C, H, W] view; the stride
+    defaults to the kernel (MaxPool2d::new)."""
+    sh, sw = stride if stride is not None else kernel
+    _call("trs_max_pool2d", ctypes.byref(x), int(kernel[0]), int(kernel[1]), int(sh), int(sw),
+          ctypes.byref(view_of(out)), stream_handle())
+    return out
+
+
+def avg_pool2d(x: abi.View, kernel: tuple[int, int], out: torch.Tensor,
+               stride: tuple[int, int] | None = None) -> torch.Tensor:
+    """AvgPool2d::forward (nn/pool.rs:223-233)."""
+    sh, sw = stride if stride is not None else kernel
+    _call("trs_avg_pool2d", ctypes.byref(x), int(kernel[0]), int(kernel[1]), int(sh), int(sw),
+          ctypes.byref(view_of(out)), stream_handle())
+    return out
+
+
+def max_pool2d_backward(x: abi.View, grad_out: abi.View, kernel: tuple[int, int], grad_x: torch.Tensor,
+                        stride: tuple[int, int] | None = None, accumulate: bool = False) -> torch.Tensor:
+    """The gradient MaxPool2d passes back to x (max_axis backward, then fold_2d);
+    with accumulate, added to what grad_x holds."""
+    sh, sw = stride if stride is not None else kernel
+    _call("trs_max_pool2d_backward", ctypes.byref(x), ctypes.byref(grad_out), int(kernel[0]), int(kernel[1]),
+          int(sh), int(sw), int(bool(accumulate)), ctypes.byref(view_of(grad_x)), stream_handle())
+    return grad_x
+
+
 def fill_uniform(out: torch.Tensor, seed: int, lo: float = -1.0, hi: float = 1.0, first: int = 0) -> torch.Tensor:
     _call("trs_fill_uniform", ctypes.byref(view_of(out)), seed, first, lo, hi, stream_handle())
     return out

@@ -8,12 +8,20 @@ import numpy as np
 from conftest import NP_DTYPES
 
 
+def storage_of(inp, dt) -> np.ndarray:
+    """An input's storage: its listed values, or 1, 2, ..., n for a ramp
+    (nn/pool.rs:245-248)."""
+    if inp.get("ramp"):
+        return np.arange(1, int(np.prod(inp["shape"])) + 1).astype(dt)
+    return np.array(inp["storage"], dtype=dt)
+
+
 def _host_views(case):
     import oracle
     dt = NP_DTYPES[case["dtype"]]
     vs = []
     for inp in case["inputs"]:
-        st = np.array(inp["storage"], dtype=dt)
+        st = storage_of(inp, dt)
         vs.append(oracle.HostView(st, inp["shape"], inp.get("strides"), inp.get("offset", 0)))
     return vs
 
@@ -55,6 +63,10 @@ def run_oracle(case):
         return oracle.reduce_broadcast_grad(vs[0], case["target"])
     if op == "softmax":
         return oracle.softmax_lastdim(vs[0])
+    if op in ("max_pool2d", "avg_pool2d"):
+        return oracle.pool2d(op[:3], vs[0], case["kernel"], case["stride"])
+    if op == "max_pool2d_backward":
+        return oracle.max_pool2d_backward(vs[0], vs[1], case["kernel"], case["stride"])
     if op == "layer_norm":
         wrap = oracle.contiguous
         return _layer_norm(

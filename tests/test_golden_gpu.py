@@ -5,7 +5,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from _golden import check
+from _golden import check, storage_of
 from conftest import NP_DTYPES, golden_cases
 
 pytestmark = pytest.mark.gpu
@@ -15,8 +15,7 @@ def _run_gpu(case):
     from _gpu import DevView, empty, to_host
     from tensorrs_b200 import abi, device
     dt = NP_DTYPES[case["dtype"]]
-    dvs = [DevView(np.array(i["storage"], dtype=dt), i["shape"], i.get("strides"), i.get("offset", 0))
-           for i in case["inputs"]]
+    dvs = [DevView(storage_of(i, dt), i["shape"], i.get("strides"), i.get("offset", 0)) for i in case["inputs"]]
     op = case["op"]
     if op == "binary":
         shape = list(np.broadcast_shapes(tuple(dvs[0].shape), tuple(dvs[1].shape)))
@@ -58,6 +57,16 @@ def _run_gpu(case):
     if op == "softmax":
         out = empty(dvs[0].shape, dt)
         return to_host(device.softmax_lastdim(dvs[0].view, out))
+    if op in ("max_pool2d", "avg_pool2d", "max_pool2d_backward"):
+        kh, kw = case["kernel"]
+        sh, sw = case["stride"]
+        n, c, h, w = dvs[0].shape
+        if op == "max_pool2d_backward":
+            gx = empty([n, c, h, w], dt)
+            return to_host(device.max_pool2d_backward(dvs[0].view, dvs[1].view, (kh, kw), gx, (sh, sw)))
+        oh, ow = device.pooled_size((h, w), (kh, kw), (sh, sw))
+        fn = device.max_pool2d if op == "max_pool2d" else device.avg_pool2d
+        return to_host(fn(dvs[0].view, (kh, kw), empty([n, c, oh, ow], dt), (sh, sw)))
     if op == "layer_norm":
         return _layer_norm_gpu(dvs, case["epsilon"], dt)
     raise ValueError(op)
@@ -100,7 +109,8 @@ def test_gpu_matches_oracle_on_kat_inputs(case):
     from _util import assert_bit_exact, max_ulp
     got = np.asarray(_run_gpu(case))
     want = np.asarray(run_oracle(case))
-    if case["op"] in ("binary", "pack", "max_axis", "argmax_axis") or case["dtype"] in ("i32", "i64") \
+    if case["op"] in ("binary", "pack", "max_axis", "argmax_axis", "max_pool2d", "avg_pool2d",
+                      "max_pool2d_backward") or case["dtype"] in ("i32", "i64") \
             or (case["op"] == "unary" and case["unop"] in ("relu", "leaky_relu", "abs", "clamp", "mul_scalar")):
         assert_bit_exact(got, want, case["name"])
     elif case["op"] in ("sum", "sum_axis", "reduce_broadcast_grad"):
