@@ -50,6 +50,7 @@ struct PoolDev {
   int64_t items;   // work items: outputs (or strips), or input pixels
   int64_t inner;   // items along the last axis of one row
   FastDiv f_inner, f_rows, f_c;  // items per row, rows per plane, channels
+  FastDiv f_sh, f_sw;            // the window strides
   int32_t fast;    // items < 2^32: 32-bit index arithmetic
   int32_t accumulate;
 };
@@ -102,36 +103,70 @@ __device__ __forceinline__ T pool_window(const T* __restrict__ x, int64_t base, 
   }
 }
 
-template <class T, int MODE, int KW>
+constexpr int kPoolItems = 2;  // strips per thread per pass of the strip kernels
+
+// Any window: one thread per output, scalar loads.
+template <class T, int MODE>
 __global__ void __launch_bounds__(256) pool_fwd_kernel(const PoolDev d) {
-  constexpr int VW = 16 / sizeof(T);
-  constexpr int Q = KW > 0 ? VW / KW : 1;  // outputs per item
-  using A = Arith<T>;
   const T* __restrict__ x = static_cast<const T*>(d.x);
   T* __restrict__ out = static_cast<T*>(d.out);
   for (uint64_t it = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; it < (uint64_t)d.items;
        it += (uint64_t)gridDim.x * blockDim.x) {
-    int64_t n, c, i, q;
-    pool_coords(d, it, &n, &c, &i, &q);
-    const int64_t row0 = d.x_off + n * d.xs[0] + c * d.xs[1] + i * d.sh * d.xs[2];
-    const int64_t obase = d.o_off + n * d.os[0] + c * d.os[1] + i * d.os[2];
-    if constexpr (KW == 0) {
-      out[obase + q * d.os[3]] = pool_window<T, MODE>(x, row0 + q * d.sw * d.xs[3], d);
-    } else {
-      const int64_t col0 = q * VW;  // first input column of the strip
-      const int64_t j0 = q * Q;     // its first output
-      if (col0 + VW <= d.W) {
+    int64_t n, c, i, j;
+    pool_coords(d, it, &n, &c, &i, &j);
+    const int64_t base = d.x_off + n * d.xs[0] + c * d.xs[1] + i * d.sh * d.xs[2] + j * d.sw * d.xs[3];
+    out[d.o_off + n * d.os[0] + c * d.os[1] + i * d.os[2] + j * d.os[3]] = pool_window<T, MODE>(x, base, d);
+  }
+}
+
+// Windows KW wide at a stride of KW, at most KH high, over unit-stride rows
+// aligned to 16 bytes: an item is one 16-byte strip of one row of windows,
+// the windows of Q = 16 / (KW * size) neighbouring outputs.  Each thread takes
+// kPoolItems strips per pass and issues all their row loads before combining.
+template <class T, int MODE, int KW, int KH>
+__global__ void __launch_bounds__(256) pool_strip_kernel(const PoolDev d) {
+  constexpr int VW = 16 / sizeof(T);
+  constexpr int Q = VW / KW;
+  using A = Arith<T>;
+  const T* __restrict__ x = static_cast<const T*>(d.x);
+  T* __restrict__ out = static_cast<T*>(d.out);
+  const uint64_t step = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t it0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; it0 < (uint64_t)d.items;
+       it0 += kPoolItems * step) {
+    int64_t row0[kPoolItems], obase[kPoolItems], col0[kPoolItems];
+    bool live[kPoolItems], whole[kPoolItems];
+    PVec<T, VW> s[kPoolItems][KH];
+#pragma unroll
+    for (int k = 0; k < kPoolItems; ++k) {
+      const uint64_t it = it0 + (uint64_t)k * step;
+      live[k] = it < (uint64_t)d.items;
+      int64_t n = 0, c = 0, i = 0, q = 0;
+      if (live[k]) pool_coords(d, it, &n, &c, &i, &q);
+      row0[k] = d.x_off + n * d.xs[0] + c * d.xs[1] + i * d.sh * d.xs[2];
+      obase[k] = d.o_off + n * d.os[0] + c * d.os[1] + i * d.os[2];
+      col0[k] = q * VW;
+      whole[k] = live[k] && col0[k] + VW <= d.W;
+#pragma unroll
+      for (int u = 0; u < KH; ++u)
+        if (whole[k] && u < d.kh)
+          s[k][u] = *reinterpret_cast<const PVec<T, VW>*>(x + row0[k] + u * d.xs[2] + col0[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < kPoolItems; ++k) {
+      if (!live[k]) continue;
+      const int64_t j0 = col0[k] / KW;  // the strip's first output
+      if (whole[k]) {
         T r[Q];
 #pragma unroll
         for (int o = 0; o < Q; ++o) r[o] = T(0);  // an empty window (kh == 0) averages to 0 / 0
-        const T scale = (T)((int64_t)d.kh * KW);
-        for (int u = 0; u < d.kh; ++u) {
-          const PVec<T, VW> s = *reinterpret_cast<const PVec<T, VW>*>(x + row0 + u * d.xs[2] + col0);
+#pragma unroll
+        for (int u = 0; u < KH; ++u) {
+          if (u >= d.kh) break;
 #pragma unroll
           for (int o = 0; o < Q; ++o) {
 #pragma unroll
             for (int v = 0; v < KW; ++v) {
-              const T val = s.v[o * KW + v];
+              const T val = s[k][u].v[o * KW + v];
               if constexpr (MODE == kPoolMax) {
                 if (u == 0 && v == 0) r[o] = val;
                 else if (val > r[o]) r[o] = val;
@@ -145,19 +180,53 @@ __global__ void __launch_bounds__(256) pool_fwd_kernel(const PoolDev d) {
         for (int o = 0; o < Q; ++o) {
           if (j0 + o < d.OW) {
             T res = r[o];
-            if constexpr (MODE == kPoolAvg) res = A::div(res, scale, nullptr);
-            out[obase + (j0 + o) * d.os[3]] = res;
+            if constexpr (MODE == kPoolAvg) res = A::div(res, (T)((int64_t)d.kh * KW), nullptr);
+            out[obase[k] + (j0 + o) * d.os[3]] = res;
           }
         }
       } else {
         // the row's ragged end: windows one by one
         for (int o = 0; o < Q; ++o)
-          if (j0 + o < d.OW) out[obase + (j0 + o) * d.os[3]] = pool_window<T, MODE>(x, row0 + (j0 + o) * KW, d);
+          if (j0 + o < d.OW)
+            out[obase[k] + (j0 + o) * d.os[3]] = pool_window<T, MODE>(x, row0[k] + (j0 + o) * KW, d);
       }
     }
   }
 }
 
+// MaxPool2d's gradient at pixel (y, xc) of one plane: the sum, from 0 and in
+// window order, of the gradients of the windows that read the pixel and
+// whose winner (first of the largest, strict `>`) it is.
+template <class T>
+__device__ __forceinline__ T pixel_grad(const PoolDev& d, const T* __restrict__ x, const T* __restrict__ g,
+                                        int64_t plane, int64_t gplane, uint32_t y, uint32_t xc) {
+  using A = Arith<T>;
+  // windows oh with oh*sh <= y <= oh*sh + kh - 1, likewise ow
+  const uint32_t oh_lo = y >= (uint32_t)d.kh ? fdiv(y - d.kh + d.sh, d.f_sh) : 0u;
+  uint32_t oh_hi = fdiv(y, d.f_sh);
+  if (oh_hi > (uint32_t)d.OH - 1) oh_hi = (uint32_t)d.OH - 1;
+  const uint32_t ow_lo = xc >= (uint32_t)d.kw ? fdiv(xc - d.kw + d.sw, d.f_sw) : 0u;
+  uint32_t ow_hi = fdiv(xc, d.f_sw);
+  if (ow_hi > (uint32_t)d.OW - 1) ow_hi = (uint32_t)d.OW - 1;
+  T acc = T(0);
+  for (uint32_t oh = oh_lo; oh <= oh_hi; ++oh) {
+    for (uint32_t ow = ow_lo; ow <= ow_hi; ++ow) {
+      const int64_t base = plane + (int64_t)oh * d.sh * d.xs[2] + (int64_t)ow * d.sw * d.xs[3];
+      T best = __ldg(x + base);
+      int bu = 0, bv = 0;
+      for (int u = 0; u < d.kh; ++u)
+        for (int v = (u == 0 ? 1 : 0); v < d.kw; ++v) {
+          const T val = __ldg(x + base + u * d.xs[2] + v * d.xs[3]);
+          if (val > best) { best = val; bu = u; bv = v; }
+        }
+      if (oh * d.sh + bu == y && ow * d.sw + bv == xc)
+        acc = A::add(acc, __ldg(g + gplane + (int64_t)oh * d.gs[2] + (int64_t)ow * d.gs[3]));
+    }
+  }
+  return acc;
+}
+
+// Any window: one thread per input pixel.
 template <class T>
 __global__ void __launch_bounds__(256) pool_max_bwd_kernel(const PoolDev d) {
   using A = Arith<T>;
@@ -168,32 +237,109 @@ __global__ void __launch_bounds__(256) pool_max_bwd_kernel(const PoolDev d) {
        it += (uint64_t)gridDim.x * blockDim.x) {
     int64_t n, c, y, xc;
     pool_coords(d, it, &n, &c, &y, &xc);
-    const int64_t plane = d.x_off + n * d.xs[0] + c * d.xs[1];
-    const int64_t gplane = d.g_off + n * d.gs[0] + c * d.gs[1];
-    // windows oh with oh*sh <= y <= oh*sh + kh - 1, likewise ow
-    const int64_t oh_lo = y >= d.kh ? (y - d.kh + d.sh) / d.sh : 0;
-    int64_t oh_hi = y / d.sh;
-    if (oh_hi > d.OH - 1) oh_hi = d.OH - 1;
-    const int64_t ow_lo = xc >= d.kw ? (xc - d.kw + d.sw) / d.sw : 0;
-    int64_t ow_hi = xc / d.sw;
-    if (ow_hi > d.OW - 1) ow_hi = d.OW - 1;
-    T acc = T(0);
-    for (int64_t oh = oh_lo; oh <= oh_hi; ++oh) {
-      for (int64_t ow = ow_lo; ow <= ow_hi; ++ow) {
-        const int64_t base = plane + oh * d.sh * d.xs[2] + ow * d.sw * d.xs[3];
-        T best = __ldg(x + base);
-        int bu = 0, bv = 0;
-        for (int u = 0; u < d.kh; ++u)
-          for (int v = (u == 0 ? 1 : 0); v < d.kw; ++v) {
-            const T val = __ldg(x + base + u * d.xs[2] + v * d.xs[3]);
-            if (val > best) { best = val; bu = u; bv = v; }
-          }
-        if (oh * d.sh + bu == y && ow * d.sw + bv == xc)
-          acc = A::add(acc, __ldg(g + gplane + oh * d.gs[2] + ow * d.gs[3]));
-      }
-    }
+    const T acc = pixel_grad<T>(d, x, g, d.x_off + n * d.xs[0] + c * d.xs[1], d.g_off + n * d.gs[0] + c * d.gs[1],
+                                (uint32_t)y, (uint32_t)xc);
     const int64_t o = d.o_off + n * d.os[0] + c * d.os[1] + y * d.os[2] + xc * d.os[3];
     out[o] = d.accumulate ? A::add(out[o], acc) : acc;
+  }
+}
+
+// MaxPool2d's gradient where the stride equals the window (MaxPool2d::new),
+// KW wide and at most KH high, with x and grad_x in unit-stride rows aligned
+// to 16 bytes.  The windows tile the image, so a pixel is read by one window
+// at most.  An item is one 16-byte strip of one row of windows: the thread
+// loads the strip's window rows, finds the winner of each of its Q windows
+// once, and writes whole 16-byte rows of grad_x -- the window rows, and in
+// the last row of windows also the rows below that no window reads (0, or
+// grad_x + 0 when accumulating); columns past the last window get 0 too.
+template <class T, int KW, int KH>
+__global__ void __launch_bounds__(256) pool_max_bwd_strip_kernel(const PoolDev d) {
+  constexpr int VW = 16 / sizeof(T);
+  constexpr int Q = VW / KW;
+  using A = Arith<T>;
+  const T* __restrict__ x = static_cast<const T*>(d.x);
+  const T* __restrict__ g = static_cast<const T*>(d.g);
+  T* out = static_cast<T*>(d.out);
+  const uint64_t step = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t it0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; it0 < (uint64_t)d.items;
+       it0 += kPoolItems * step) {
+    int64_t plane[kPoolItems], gplane[kPoolItems], oplane[kPoolItems], col0[kPoolItems], y0[kPoolItems];
+    int64_t irow[kPoolItems];
+    bool live[kPoolItems], whole[kPoolItems];
+    PVec<T, VW> s[kPoolItems][KH];
+#pragma unroll
+    for (int k = 0; k < kPoolItems; ++k) {
+      const uint64_t it = it0 + (uint64_t)k * step;
+      live[k] = it < (uint64_t)d.items;
+      int64_t n = 0, c = 0, i = 0, q = 0;
+      if (live[k]) pool_coords(d, it, &n, &c, &i, &q);
+      plane[k] = d.x_off + n * d.xs[0] + c * d.xs[1];
+      gplane[k] = d.g_off + n * d.gs[0] + c * d.gs[1];
+      oplane[k] = d.o_off + n * d.os[0] + c * d.os[1];
+      irow[k] = i;
+      y0[k] = i * d.kh;
+      col0[k] = q * VW;
+      whole[k] = live[k] && col0[k] + VW <= d.W;
+#pragma unroll
+      for (int u = 0; u < KH; ++u)
+        if (whole[k] && u < d.kh)
+          s[k][u] = *reinterpret_cast<const PVec<T, VW>*>(x + plane[k] + (y0[k] + u) * d.xs[2] + col0[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < kPoolItems; ++k) {
+      if (!live[k]) continue;
+      // the cell's rows: its windows', and below the last row of windows the rest
+      const int64_t y_end = irow[k] == d.OH - 1 ? d.H : y0[k] + d.kh;
+      if (!whole[k]) {
+        // the row's ragged end: pixel by pixel
+        for (int64_t y = y0[k]; y < y_end; ++y)
+          for (int64_t xc = col0[k]; xc < d.W; ++xc) {
+            const T acc = pixel_grad<T>(d, x, g, plane[k], gplane[k], (uint32_t)y, (uint32_t)xc);
+            T* dst = out + oplane[k] + y * d.os[2] + xc * d.os[3];
+            *dst = d.accumulate ? A::add(*dst, acc) : acc;
+          }
+        continue;
+      }
+      const int64_t j0 = col0[k] / KW;
+      int bu[Q], bv[Q];
+      T gv[Q];
+#pragma unroll
+      for (int o = 0; o < Q; ++o) {
+        bu[o] = -1;
+        bv[o] = 0;
+        gv[o] = T(0);
+        if (j0 + o < d.OW) {
+          T best = s[k][0].v[o * KW];
+          bu[o] = 0;
+#pragma unroll
+          for (int u = 0; u < KH; ++u) {
+            if (u >= d.kh) break;
+#pragma unroll
+            for (int v = 0; v < KW; ++v) {
+              if (u == 0 && v == 0) continue;
+              const T val = s[k][u].v[o * KW + v];
+              if (val > best) { best = val; bu[o] = u; bv[o] = v; }
+            }
+          }
+          gv[o] = A::add(T(0), __ldg(g + gplane[k] + irow[k] * d.gs[2] + (j0 + o) * d.gs[3]));
+        }
+      }
+      for (int64_t y = y0[k]; y < y_end; ++y) {
+        const int u = (int)(y - y0[k]);
+        PVec<T, VW> w;
+#pragma unroll
+        for (int o = 0; o < Q; ++o)
+#pragma unroll
+          for (int v = 0; v < KW; ++v) w.v[o * KW + v] = (bu[o] == u && bv[o] == v) ? gv[o] : T(0);
+        PVec<T, VW>* dst = reinterpret_cast<PVec<T, VW>*>(out + oplane[k] + y * d.os[2] + col0[k]);
+        if (d.accumulate) {
+          const PVec<T, VW> cur = *dst;
+#pragma unroll
+          for (int e = 0; e < VW; ++e) w.v[e] = A::add(cur.v[e], w.v[e]);
+        }
+        *dst = w;
+      }
+    }
   }
 }
 
@@ -257,9 +403,10 @@ Error pool_setup(const char* layer, const trs_view* x, int64_t kh, int64_t kw, i
   if (x->shape[2] < kh || x->shape[3] < kw)
     return make_error(TRS_ERR_SHAPE, "!!!unfold_2d(): the input is smaller than the kernel!!!");
   if (is_max && kh * kw == 0) return make_error(TRS_ERR_EMPTY_AXIS, "!!!Cannot reduce an empty axis!!!");
-  // the index arithmetic divides by W, H and C as 32-bit divisors
-  if (x->shape[1] >= (1ll << 32) || x->shape[2] >= (1ll << 32) || x->shape[3] >= (1ll << 32))
-    return make_error(TRS_ERR_ARG, "pool: a dimension of 2^32 or more");
+  // the index arithmetic divides by W, H, C and the strides as 32-bit
+  // divisors, and y - kh + stride stays below 2^32
+  if (x->shape[1] >= (1ll << 31) || x->shape[2] >= (1ll << 31) || x->shape[3] >= (1ll << 31))
+    return make_error(TRS_ERR_ARG, "pool: a dimension of 2^31 or more");
   d->H = x->shape[2];
   d->W = x->shape[3];
   d->OH = (d->H - kh) / sh + 1;
@@ -268,6 +415,8 @@ Error pool_setup(const char* layer, const trs_view* x, int64_t kh, int64_t kw, i
   d->kw = (int32_t)kw;
   d->sh = (int32_t)sh;
   d->sw = (int32_t)sw;
+  d->f_sh = make_fastdiv((uint32_t)sh);
+  d->f_sw = make_fastdiv((uint32_t)sw);
   d->x = x->data;
   d->x_off = x->offset;
   for (int i = 0; i < 4; ++i) d->xs[i] = x->strides[i];
@@ -283,38 +432,77 @@ void set_items(PoolDev* d, int64_t planes, int64_t C, int64_t rows, int64_t inne
   d->f_c = make_fastdiv((uint32_t)(C < 1 ? 1 : C));
 }
 
+// x (and, for the backward, grad_x) in unit-stride rows whose starts are all
+// 16-byte aligned.
+bool rows_aligned(const void* base, int64_t off, const int64_t* st, int es) {
+  const int vw = 16 / es;
+  if (((uintptr_t)base + (uintptr_t)(off * es)) % 16 || st[3] != 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if (st[i] % vw) return false;
+  return true;
+}
+
+template <class K>
+Error pool_launch(K kernel, const PoolDev& d, cudaStream_t stream, const char* what) {
+  kernel<<<pool_grid(kernel, (uint64_t)d.items), 256, 0, stream>>>(d);
+  return check_launch(what);
+}
+
 template <class T>
 Error launch_pool_fwd(PoolDev d, int mode, int64_t N, int64_t C, cudaStream_t stream) {
   constexpr int VW = 16 / sizeof(T);
-  // the strip path: kw == stride_w dividing 16 bytes, unit-stride rows whose
-  // starts are all 16-byte aligned
-  const int es = sizeof(T);
-  bool strip = d.kw == d.sw && d.kw > 0 && VW % d.kw == 0 && d.xs[3] == 1;
-  if (strip) {
-    if (((uintptr_t)d.x + (uintptr_t)(d.x_off * es)) % 16) strip = false;
-    for (int i = 0; i < 3; ++i)
-      if (d.xs[i] % VW) strip = false;
-  }
-  const int64_t rows = d.OH;
-  auto go = [&](auto kernel) {
-    kernel<<<pool_grid(kernel, (uint64_t)d.items), 256, 0, stream>>>(d);
-    return check_launch("pool kernel");
-  };
+  // the strip kernel: kw == stride_w dividing 16 bytes, kh <= 4, aligned rows
+  const bool strip = d.kw == d.sw && d.kw > 0 && VW % d.kw == 0 && d.kh <= 4 &&
+                     rows_aligned(d.x, d.x_off, d.xs, sizeof(T));
   if (!strip) {
-    set_items(&d, N * C, C, rows, d.OW);
-    return mode == kPoolMax ? go(pool_fwd_kernel<T, kPoolMax, 0>) : go(pool_fwd_kernel<T, kPoolAvg, 0>);
+    set_items(&d, N * C, C, d.OH, d.OW);
+    return mode == kPoolMax ? pool_launch(pool_fwd_kernel<T, kPoolMax>, d, stream, "pool kernel")
+                            : pool_launch(pool_fwd_kernel<T, kPoolAvg>, d, stream, "pool kernel");
   }
   const int Q = VW / d.kw;
-  set_items(&d, N * C, C, rows, (d.OW + Q - 1) / Q);
-#define TRS_POOL_LAUNCH(KWV) \
-  if (d.kw == KWV) return mode == kPoolMax ? go(pool_fwd_kernel<T, kPoolMax, KWV>) : go(pool_fwd_kernel<T, kPoolAvg, KWV>);
-  TRS_POOL_LAUNCH(1)
-  TRS_POOL_LAUNCH(2)
-  if constexpr (VW >= 4) {
-    TRS_POOL_LAUNCH(4)
+  set_items(&d, N * C, C, d.OH, (d.OW + Q - 1) / Q);
+  const bool max = mode == kPoolMax;
+  const bool low = d.kh <= 2;
+#define TRS_POOL_STRIP(KWV)                                                                            \
+  if (d.kw == KWV) {                                                                                   \
+    if (low) return max ? pool_launch(pool_strip_kernel<T, kPoolMax, KWV, 2>, d, stream, "pool strips")  \
+                        : pool_launch(pool_strip_kernel<T, kPoolAvg, KWV, 2>, d, stream, "pool strips"); \
+    return max ? pool_launch(pool_strip_kernel<T, kPoolMax, KWV, 4>, d, stream, "pool strips")           \
+               : pool_launch(pool_strip_kernel<T, kPoolAvg, KWV, 4>, d, stream, "pool strips");          \
   }
-#undef TRS_POOL_LAUNCH
+  TRS_POOL_STRIP(1)
+  TRS_POOL_STRIP(2)
+  if constexpr (VW >= 4) {
+    TRS_POOL_STRIP(4)
+  }
+#undef TRS_POOL_STRIP
   return make_error(TRS_ERR_ARG, "pool: no strip kernel for this window");
+}
+
+template <class T>
+Error launch_pool_bwd(PoolDev d, int64_t N, int64_t C, cudaStream_t stream) {
+  constexpr int VW = 16 / sizeof(T);
+  // the strip kernel: stride == window (the windows tile the image), kw
+  // dividing 16 bytes, kh <= 4, x and grad_x in aligned rows
+  const bool strip = d.kw == d.sw && d.kh == d.sh && d.kw > 0 && VW % d.kw == 0 && d.kh <= 4 &&
+                     rows_aligned(d.x, d.x_off, d.xs, sizeof(T)) && rows_aligned(d.out, d.o_off, d.os, sizeof(T));
+  if (!strip) {
+    set_items(&d, N * C, C, d.H, d.W);
+    return pool_launch(pool_max_bwd_kernel<T>, d, stream, "max pool backward kernel");
+  }
+  set_items(&d, N * C, C, d.OH, (d.W + VW - 1) / VW);
+  const bool low = d.kh <= 2;
+#define TRS_POOL_BWD_STRIP(KWV)                                                                  \
+  if (d.kw == KWV)                                                                               \
+    return low ? pool_launch(pool_max_bwd_strip_kernel<T, KWV, 2>, d, stream, "max pool backward strips") \
+               : pool_launch(pool_max_bwd_strip_kernel<T, KWV, 4>, d, stream, "max pool backward strips");
+  TRS_POOL_BWD_STRIP(1)
+  TRS_POOL_BWD_STRIP(2)
+  if constexpr (VW >= 4) {
+    TRS_POOL_BWD_STRIP(4)
+  }
+#undef TRS_POOL_BWD_STRIP
+  return make_error(TRS_ERR_ARG, "pool backward: no strip kernel for this window");
 }
 
 Error run_pool(int mode, const trs_view* x, int64_t kh, int64_t kw, int64_t sh, int64_t sw, const trs_view* out,
@@ -361,15 +549,8 @@ Error run_max_pool_backward(const trs_view* x, const trs_view* g, int64_t kh, in
     d.os[i] = gx->strides[i];
   }
   d.accumulate = accumulate ? 1 : 0;
-  set_items(&d, N * C, C, d.H, d.W);
-  if (x->dtype == TRS_F32) {
-    auto k = pool_max_bwd_kernel<float>;
-    k<<<pool_grid(k, (uint64_t)d.items), 256, 0, stream>>>(d);
-  } else {
-    auto k = pool_max_bwd_kernel<double>;
-    k<<<pool_grid(k, (uint64_t)d.items), 256, 0, stream>>>(d);
-  }
-  return check_launch("max pool backward kernel");
+  if (x->dtype == TRS_F32) return launch_pool_bwd<float>(d, N, C, stream);
+  return launch_pool_bwd<double>(d, N, C, stream);
 }
 
 trs_status finish(const Error& e) {
