@@ -474,11 +474,6 @@ ew_tile_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials
 // stores 16 bytes of output.  The 16-byte chunks of a shared row are
 // XOR-swizzled by the row's chunk group, which keeps both the cp.async writes
 // and the column reads at most two-way bank conflicted.
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 template <class T, int PROG, bool WRITE, bool SUM>
 __global__ void __launch_bounds__(kThreads, 3)

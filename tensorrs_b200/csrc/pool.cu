@@ -51,6 +51,10 @@ struct PoolDev {
   int64_t inner;   // items along the last axis of one row
   FastDiv f_inner, f_rows, f_c;  // items per row, rows per plane, channels
   FastDiv f_sh, f_sw;            // the window strides
+  // tile kernels: blocks of R window rows per plane, input rows staged in
+  // shared memory at a pitch of P elements
+  int32_t R, P, nblk, full;          // full: whole 16-byte chunks per row
+  FastDiv f_blk, f_ow, f_w, f_full;  // blocks per plane, OW, W, full
   int32_t fast;    // items < 2^32: 32-bit index arithmetic
   int32_t accumulate;
 };
@@ -343,6 +347,148 @@ __global__ void __launch_bounds__(256) pool_max_bwd_strip_kernel(const PoolDev d
   }
 }
 
+// ---- shared-memory tiles (any window and stride) ---------------------------
+
+// Copies rows y0 .. y0 + nrows - 1 of one plane (unit-stride rows whose starts
+// are 16-byte aligned) into shared memory at a pitch of P elements: 16-byte
+// cp.async for the whole chunks of each row, plain loads for its last
+// W % (16 / size) elements; returns after the CTA's barrier.
+template <class T>
+__device__ __forceinline__ void stage_rows(const PoolDev& d, T* sm, const T* __restrict__ x, int64_t plane, int64_t y0,
+                                           uint32_t nrows) {
+  constexpr int VW = 16 / sizeof(T);
+  const uint32_t full = (uint32_t)d.full;
+  const uint32_t chunks = nrows * full;
+  for (uint32_t t = threadIdx.x; t < chunks; t += blockDim.x) {
+    const uint32_t r = fdiv(t, d.f_full), ch = t - r * full;
+    cp_async16(sm + r * d.P + ch * VW, x + plane + (y0 + r) * d.xs[2] + ch * VW);
+  }
+  const uint32_t tail = (uint32_t)(d.W - (int64_t)full * VW);
+  if (tail)
+    for (uint32_t t = threadIdx.x; t < nrows * tail; t += blockDim.x) {
+      const uint32_t r = t / tail, e = full * VW + (t - r * tail);
+      sm[r * d.P + e] = __ldg(x + plane + (y0 + r) * d.xs[2] + e);
+    }
+  cp_async_commit();
+  cp_async_wait_all();
+  __syncthreads();
+}
+
+__device__ __forceinline__ void tile_item(const PoolDev& d, uint64_t item, int64_t* n, int64_t* c, int64_t* i0) {
+  const uint32_t pl = fdiv((uint32_t)item, d.f_blk);
+  const uint32_t b = (uint32_t)item - pl * d.f_blk.d;
+  const uint32_t nn = fdiv(pl, d.f_c);
+  *n = nn;
+  *c = pl - nn * d.f_c.d;
+  *i0 = (int64_t)b * d.R;
+}
+
+// Forward: an item is a block of R output rows of one plane; its input rows
+// are staged once, then each output reads its window from shared memory.
+template <class T, int MODE>
+__global__ void __launch_bounds__(256) pool_tile_fwd_kernel(const PoolDev d) {
+  using A = Arith<T>;
+  extern __shared__ __align__(16) unsigned char pool_smem[];
+  T* sm = reinterpret_cast<T*>(pool_smem);
+  const T* __restrict__ x = static_cast<const T*>(d.x);
+  T* __restrict__ out = static_cast<T*>(d.out);
+  for (uint64_t item = blockIdx.x; item < (uint64_t)d.items; item += gridDim.x) {
+    int64_t n, c, i0;
+    tile_item(d, item, &n, &c, &i0);
+    const uint32_t rcnt = (uint32_t)(d.OH - i0 < d.R ? d.OH - i0 : d.R);
+    stage_rows<T>(d, sm, x, d.x_off + n * d.xs[0] + c * d.xs[1], i0 * d.sh, (rcnt - 1) * d.sh + d.kh);
+    const int64_t oplane = d.o_off + n * d.os[0] + c * d.os[1];
+    const uint32_t nout = rcnt * (uint32_t)d.OW;
+    for (uint32_t o = threadIdx.x; o < nout; o += blockDim.x) {
+      const uint32_t i = fdiv(o, d.f_ow), j = o - i * (uint32_t)d.OW;
+      const T* w = sm + i * d.sh * d.P + j * d.sw;
+      T r;
+      if constexpr (MODE == kPoolMax) {
+        r = w[0];
+        for (int u = 0; u < d.kh; ++u)
+          for (int v = (u == 0 ? 1 : 0); v < d.kw; ++v) {
+            const T val = w[u * d.P + v];
+            if (val > r) r = val;
+          }
+      } else {
+        r = T(0);
+        for (int u = 0; u < d.kh; ++u)
+          for (int v = 0; v < d.kw; ++v) r = A::add(r, w[u * d.P + v]);
+        r = A::div(r, (T)((int64_t)d.kh * d.kw), nullptr);
+      }
+      out[oplane + (i0 + i) * d.os[2] + (int64_t)j * d.os[3]] = r;
+    }
+    __syncthreads();
+  }
+}
+
+// MaxPool2d's gradient: an item is a block of R window rows of one plane and
+// owns the input rows from its first window row's start up to the next
+// block's (the last block: to the bottom).  The rows of every window reading
+// them are staged once, each window's winner is found once (an offset
+// u * kw + v in shared memory), then each owned pixel adds, in window order
+// from 0, the gradients of the covering windows that it wins.
+template <class T>
+__global__ void __launch_bounds__(256) pool_tile_bwd_kernel(const PoolDev d) {
+  using A = Arith<T>;
+  extern __shared__ __align__(16) unsigned char pool_smem[];
+  T* sm = reinterpret_cast<T*>(pool_smem);
+  const T* __restrict__ x = static_cast<const T*>(d.x);
+  const T* __restrict__ g = static_cast<const T*>(d.g);
+  T* out = static_cast<T*>(d.out);
+  for (uint64_t item = blockIdx.x; item < (uint64_t)d.items; item += gridDim.x) {
+    int64_t n, c, i0;
+    tile_item(d, item, &n, &c, &i0);
+    const int64_t i1 = d.OH - i0 < d.R ? d.OH : i0 + d.R;
+    const uint32_t y_lo = (uint32_t)(i0 * d.sh);
+    const uint32_t y_hi = (uint32_t)(i1 == d.OH ? d.H : i1 * d.sh);
+    const uint32_t oh_lo = y_lo >= (uint32_t)d.kh ? fdiv(y_lo - d.kh + d.sh, d.f_sh) : 0u;
+    uint32_t oh_hi = fdiv(y_hi - 1, d.f_sh);
+    if (oh_hi > (uint32_t)d.OH - 1) oh_hi = (uint32_t)d.OH - 1;
+    const int64_t plane = d.x_off + n * d.xs[0] + c * d.xs[1];
+    const int64_t gplane = d.g_off + n * d.gs[0] + c * d.gs[1];
+    const int64_t oplane = d.o_off + n * d.os[0] + c * d.os[1];
+    const uint32_t sy0 = oh_lo * d.sh;
+    const uint32_t srows = (uint32_t)((int64_t)oh_hi * d.sh + d.kh) - sy0;
+    // the winners after the staged rows, 16-byte aligned
+    int32_t* win = reinterpret_cast<int32_t*>(pool_smem + (((size_t)srows * d.P * sizeof(T) + 15) & ~(size_t)15));
+    stage_rows<T>(d, sm, x, plane, sy0, srows);
+    const uint32_t nwin = (oh_hi - oh_lo + 1) * (uint32_t)d.OW;
+    for (uint32_t t = threadIdx.x; t < nwin; t += blockDim.x) {
+      const uint32_t wr = fdiv(t, d.f_ow), ow = t - wr * (uint32_t)d.OW;
+      const T* w = sm + wr * d.sh * d.P + ow * d.sw;
+      T best = w[0];
+      int k = 0;
+      for (int u = 0; u < d.kh; ++u)
+        for (int v = (u == 0 ? 1 : 0); v < d.kw; ++v) {
+          const T val = w[u * d.P + v];
+          if (val > best) { best = val; k = u * d.kw + v; }
+        }
+      win[t] = k;
+    }
+    __syncthreads();
+    const uint32_t npx = (y_hi - y_lo) * (uint32_t)d.W;
+    for (uint32_t q = threadIdx.x; q < npx; q += blockDim.x) {
+      const uint32_t yr = fdiv(q, d.f_w), xc = q - yr * (uint32_t)d.W;
+      const uint32_t y = y_lo + yr;
+      uint32_t ohs = y >= (uint32_t)d.kh ? fdiv(y - d.kh + d.sh, d.f_sh) : 0u;
+      uint32_t ohe = fdiv(y, d.f_sh);
+      if (ohe > oh_hi) ohe = oh_hi;
+      const uint32_t ows = xc >= (uint32_t)d.kw ? fdiv(xc - d.kw + d.sw, d.f_sw) : 0u;
+      uint32_t owe = fdiv(xc, d.f_sw);
+      if (owe > (uint32_t)d.OW - 1) owe = (uint32_t)d.OW - 1;
+      T acc = T(0);
+      for (uint32_t oh = ohs; oh <= ohe; ++oh)
+        for (uint32_t ow = ows; ow <= owe; ++ow)
+          if (win[(oh - oh_lo) * (uint32_t)d.OW + ow] == (int)((y - oh * d.sh) * d.kw + (xc - ow * d.sw)))
+            acc = A::add(acc, __ldg(g + gplane + (int64_t)oh * d.gs[2] + (int64_t)ow * d.gs[3]));
+      T* dst = out + oplane + (int64_t)y * d.os[2] + (int64_t)xc * d.os[3];
+      *dst = d.accumulate ? A::add(*dst, acc) : acc;
+    }
+    __syncthreads();
+  }
+}
+
 // One wave of 256-thread CTAs (as many per SM as fit), each thread looping.
 template <class K>
 unsigned pool_grid(K kernel, uint64_t items) {
@@ -448,12 +594,69 @@ Error pool_launch(K kernel, const PoolDev& d, cudaStream_t stream, const char* w
   return check_launch(what);
 }
 
+// Shared memory a tile item may use: 8 CTAs of 256 threads fit on an SM.
+constexpr int64_t kPoolTileBytes = 24 << 10;
+
+// 1: the tile kernels take windows the strip kernels could also take.
+#ifndef TRS_POOL_TILE_FIRST
+#define TRS_POOL_TILE_FIRST 0
+#endif
+
+// Blocks of R window rows per plane for the tile kernels; false when one
+// window row does not fit or the items overflow 32-bit indexing.
+bool plan_tile(PoolDev* d, bool bwd, int es, int64_t N, int64_t C, size_t* smem) {
+  const int vw = 16 / es;
+  const int64_t P = (d->W + vw - 1) / vw * vw;
+  const int64_t e = bwd ? (d->kh - 1) / d->sh : 0;  // windows above a block reaching into it
+  auto bytes = [&](int64_t R) {
+    const int64_t rows = (R + e - 1) * d->sh + d->kh;
+    int64_t b = (rows * P * es + 15) / 16 * 16;
+    if (bwd) b += (R + e) * d->OW * 4;
+    return b;
+  };
+  if (d->kh < 1 || d->kw < 1 || bytes(1) > kPoolTileBytes) return false;
+  int64_t R = 1;
+  while (R < d->OH && bytes(R + 1) <= kPoolTileBytes) ++R;
+  const int64_t nblk = (d->OH + R - 1) / R;
+  const int64_t items = N * C * nblk;
+  if (items >= (1ll << 32) || (bwd && (R * d->sh + d->kh) * d->W >= (1ll << 32))) return false;
+  d->R = (int32_t)R;
+  d->P = (int32_t)P;
+  d->nblk = (int32_t)nblk;
+  d->full = (int32_t)(d->W / vw);
+  d->items = items;
+  d->f_blk = make_fastdiv((uint32_t)nblk);
+  d->f_ow = make_fastdiv((uint32_t)d->OW);
+  d->f_w = make_fastdiv((uint32_t)d->W);
+  d->f_full = make_fastdiv((uint32_t)(d->full < 1 ? 1 : d->full));
+  d->f_c = make_fastdiv((uint32_t)(C < 1 ? 1 : C));
+  *smem = (size_t)bytes(R);
+  return true;
+}
+
+template <class K>
+Error pool_tile_launch(K kernel, const PoolDev& d, size_t smem, cudaStream_t stream, const char* what) {
+  int per_sm = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, smem) != cudaSuccess || per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
+  const uint64_t cap = (uint64_t)current_device_info().sm_count * (uint64_t)per_sm;
+  const uint64_t grid = (uint64_t)d.items < cap ? (uint64_t)d.items : cap;
+  kernel<<<(unsigned)grid, 256, smem, stream>>>(d);
+  return check_launch(what);
+}
+
 template <class T>
 Error launch_pool_fwd(PoolDev d, int mode, int64_t N, int64_t C, cudaStream_t stream) {
   constexpr int VW = 16 / sizeof(T);
   // the strip kernel: kw == stride_w dividing 16 bytes, kh <= 4, aligned rows
-  const bool strip = d.kw == d.sw && d.kw > 0 && VW % d.kw == 0 && d.kh <= 4 &&
-                     rows_aligned(d.x, d.x_off, d.xs, sizeof(T));
+  const bool aligned = rows_aligned(d.x, d.x_off, d.xs, sizeof(T));
+  const bool strip = d.kw == d.sw && d.kw > 0 && VW % d.kw == 0 && d.kh <= 4 && aligned;
+  size_t smem = 0;
+  if ((!strip || TRS_POOL_TILE_FIRST) && aligned && plan_tile(&d, false, sizeof(T), N, C, &smem))
+    return mode == kPoolMax ? pool_tile_launch(pool_tile_fwd_kernel<T, kPoolMax>, d, smem, stream, "pool tiles")
+                            : pool_tile_launch(pool_tile_fwd_kernel<T, kPoolAvg>, d, smem, stream, "pool tiles");
   if (!strip) {
     set_items(&d, N * C, C, d.OH, d.OW);
     return mode == kPoolMax ? pool_launch(pool_fwd_kernel<T, kPoolMax>, d, stream, "pool kernel")
@@ -484,8 +687,12 @@ Error launch_pool_bwd(PoolDev d, int64_t N, int64_t C, cudaStream_t stream) {
   constexpr int VW = 16 / sizeof(T);
   // the strip kernel: stride == window (the windows tile the image), kw
   // dividing 16 bytes, kh <= 4, x and grad_x in aligned rows
-  const bool strip = d.kw == d.sw && d.kh == d.sh && d.kw > 0 && VW % d.kw == 0 && d.kh <= 4 &&
-                     rows_aligned(d.x, d.x_off, d.xs, sizeof(T)) && rows_aligned(d.out, d.o_off, d.os, sizeof(T));
+  const bool aligned = rows_aligned(d.x, d.x_off, d.xs, sizeof(T));
+  const bool strip = d.kw == d.sw && d.kh == d.sh && d.kw > 0 && VW % d.kw == 0 && d.kh <= 4 && aligned &&
+                     rows_aligned(d.out, d.o_off, d.os, sizeof(T));
+  size_t smem = 0;
+  if ((!strip || TRS_POOL_TILE_FIRST) && aligned && plan_tile(&d, true, sizeof(T), N, C, &smem))
+    return pool_tile_launch(pool_tile_bwd_kernel<T>, d, smem, stream, "max pool backward tiles");
   if (!strip) {
     set_items(&d, N * C, C, d.H, d.W);
     return pool_launch(pool_max_bwd_kernel<T>, d, stream, "max pool backward kernel");

@@ -2,13 +2,15 @@
 oracle's restatement of the reference (reshape -> unfold_2d -> max_axis, or
 sum_axis / (kh * kw); max_axis's backward -> fold_2d):
 
-* both forward kernels: the 16-byte strip kernel (kw == stride_w dividing 16
-  bytes, its ragged row ends) and the general one (overlapping windows,
-  strides other than the width, strided or misaligned views, strided outputs);
+* the forward kernels: the 16-byte strip kernel (kw == stride_w dividing 16
+  bytes, its ragged row ends), the shared-memory tile kernel (rows of a
+  multiple of 16 bytes, any window: overlapping, gapped, planes split into
+  several blocks of rows) and the general one (other views, strided outputs);
 * NaN as a window's first element and elsewhere, +-inf, -0 / +0 ties;
-* MaxPool2d's gradient with ties, overlapping windows (a pixel collecting from
-  several windows), uncovered edge pixels, and the accumulation onto a held
-  gradient;
+* MaxPool2d's gradient through the strip, tile and general kernels with
+  ties, overlapping windows (a pixel collecting from several windows, blocks
+  taking windows from the block above), uncovered edge pixels, and the
+  accumulation onto a held gradient;
 * the config-4 activation shape [64, 256, 56, 56] at full size;
 * the errors the reference panics with, aliasing and empty tensors.
 """
@@ -62,6 +64,14 @@ FWD = [
     ([1, 2, 5, 11], (1, 2), (1, 1)),
     ([2, 2, 11, 7], (3, 1), (2, 3)),
     ([1, 3, 32, 33], (5, 3), (3, 2)),
+    # shared-memory tiles: rows of a multiple of 16 bytes, any window
+    ([2, 3, 9, 12], (3, 3), (2, 2)),
+    ([2, 4, 56, 56], (3, 3), (2, 2)),
+    ([1, 2, 5, 8], (1, 2), (1, 1)),
+    ([2, 2, 11, 8], (3, 1), (2, 3)),
+    ([1, 3, 32, 36], (5, 3), (3, 2)),
+    ([1, 2, 64, 1024], (3, 3), (2, 2)),   # several blocks of rows per plane
+    ([1, 1, 4, 8192], (1, 3), (1, 2)),    # rows too wide for a tile: the general kernel
 ]
 
 
@@ -137,6 +147,13 @@ BWD = [
     ([2, 2, 7, 10], (2, 2), (1, 1)),
     ([1, 2, 4, 9], (1, 2), (1, 1)),
     ([2, 2, 11, 7], (2, 1), (3, 3)),     # gaps between windows
+    # shared-memory tiles
+    ([2, 3, 9, 12], (3, 3), (2, 2)),
+    ([2, 2, 7, 12], (2, 2), (1, 1)),
+    ([1, 2, 4, 8], (1, 2), (1, 1)),
+    ([2, 2, 11, 8], (2, 1), (3, 3)),
+    ([1, 2, 40, 1024], (3, 3), (2, 2)),  # blocks that take windows from the block above
+    ([1, 2, 13, 16], (5, 2), (1, 2)),    # windows five rows high at stride 1
 ]
 
 
