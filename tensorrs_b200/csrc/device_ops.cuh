@@ -6,19 +6,20 @@
 // Rust operations do.  The library is also built with -fmad=false.
 //
 // Transcendentals: the reference calls glibc (expf, tanhf, powf, logf and the
-// f64 forms).  For f32 the kernels evaluate the function in f64 and round once
-// to f32, which lands within one ulp of a correctly rounded result; glibc's
-// f32 functions are themselves within about one ulp, so the two agree to a
-// couple of ulp at most (measured by the parity tests).  The exponentials of
-// the hot paths (sigmoid, powf(E, x) in ELU / SELU / softmax) use exp2_scaled
-// below, inline; tanh, ln and the general powf call CUDA's f64 functions out
-// of line.  For f64 the kernels call CUDA's f64 functions.
+// f64 forms).  The exponentials of the f32 hot paths (expf in sigmoid,
+// powf(E, x) in ELU / SELU / softmax) are the f32 table-driven exponential of
+// exp_f32.h, at most one ulp from glibc; its rare inputs outside the normal
+// result range take exp2_scaled below (f64, rounded once).  tanh, ln and the
+// general powf evaluate CUDA's f64 functions and round once to f32, within one
+// ulp of the correctly rounded result.  For f64 the kernels call CUDA's f64
+// functions.
 #pragma once
 
 #include <cstdint>
 #include <cuda_runtime.h>
 
 #include "../../include/trs.h"
+#include "exp_f32.h"
 
 namespace trs {
 
@@ -63,6 +64,17 @@ __device__ __forceinline__ double exp2_scaled(float y, double k2) {
 
 constexpr double kLog2E = 1.4426950408889634;  // log2(e) rounded to f64
 
+// b^y in f32 for the bases of exp_f32.h: the table-driven fast path, or the
+// f64 evaluation (k2 = log2(b) in f64) for y outside it (results that are
+// subnormal, zero or infinite, and NaN).
+template <bool NONPOS = false>
+__device__ __forceinline__ float exp_tab(float y, expf32::Base b, double k2) {
+  float s;
+  int ex;
+  if (expf32::parts<NONPOS>(y, b, &s, &ex)) return expf32::scale(s, ex);
+  return (float)exp2_scaled<NONPOS>(y, k2);
+}
+
 template <class T> struct Arith;
 
 template <> struct Arith<float> {
@@ -76,12 +88,19 @@ template <> struct Arith<float> {
   static __device__ __noinline__ float pow(float a, float b) {
     return (float)::pow((double)a, (double)b);
   }
-  // powf(E_f32, x) as 2^(x * log2(E_f32)) in f64; `log2_e` is log2 of the f32 E.
+  // powf(E_f32, x); `log2_e` is log2 of the f32 E in f64 (for the inputs
+  // outside the table path).
   static __device__ __forceinline__ float pow_e_inline(float x, double log2_e) {
-    return (float)exp2_scaled(x, log2_e);
+    return exp_tab(x, expf32::kBaseEf32, log2_e);
   }
   static __device__ __forceinline__ float pow_e(float x, double log2_e) { return pow_e_inline(x, log2_e); }
-  static __device__ __forceinline__ float exp(float a) { return (float)exp2_scaled(a, kLog2E); }
+  static __device__ __forceinline__ float exp(float a) { return exp_tab(a, expf32::kBaseE, kLog2E); }
+  // expf and powf(E, .) for a <= 0 or NaN (sigmoid's exp(-|x|), softmax's
+  // E^(x - max)): the branch-free form
+  static __device__ __forceinline__ float exp_nonpos(float a) { return expf32::exp_nonpos(a, expf32::kBaseE); }
+  static __device__ __forceinline__ float pow_e_nonpos(float a, double) {
+    return expf32::exp_nonpos(a, expf32::kBaseEf32);
+  }
   // tanh: for |x| >= 1 through expm1 in f32 steps, 1 - 2/(expm1(2|x|) + 2),
   // the classical formulation (the one glibc's f32 tanh evaluates), with
   // expm1 rounded once from f64; below 1 the f64 tanh rounded once, because
@@ -118,6 +137,8 @@ template <> struct Arith<double> {
   static __device__ __forceinline__ double pow_e_inline(double x, double e) { return ::pow(e, x); }
   static __device__ __noinline__ double pow_e(double x, double e) { return pow_e_inline(x, e); }
   static __device__ __noinline__ double exp(double a) { return ::exp(a); }
+  static __device__ __forceinline__ double exp_nonpos(double a) { return exp(a); }
+  static __device__ __forceinline__ double pow_e_nonpos(double x, double e) { return pow_e(x, e); }
   static __device__ __noinline__ double tanh(double a) { return ::tanh(a); }
   static __device__ __noinline__ double ln(double a) { return ::log(a); }
   static __device__ __forceinline__ double from(const trs_scalar& s) { return s.f; }
@@ -145,6 +166,8 @@ struct IntArith {
   static __device__ __forceinline__ I pow_e(I, double) { return 0; }
   static __device__ __forceinline__ I pow_e_inline(I, double) { return 0; }
   static __device__ __forceinline__ I exp(I) { return 0; }
+  static __device__ __forceinline__ I exp_nonpos(I) { return 0; }
+  static __device__ __forceinline__ I pow_e_nonpos(I, double) { return 0; }
   static __device__ __forceinline__ I tanh(I) { return 0; }
   static __device__ __forceinline__ I ln(I) { return 0; }
   static __device__ __forceinline__ I from(const trs_scalar& s) { return (I)s.i; }
@@ -195,7 +218,7 @@ __device__ __forceinline__ T apply_unop(const EwParams& p, T v) {
       // x >= 0: 1 / (1 + exp(-x)); otherwise e / (1 + e) with e = exp(x).
       // Both branches take exp(-|x|), so one exponential serves either
       // (a NaN fails x >= 0 and gives exp(NaN) / ..., NaN, as the reference).
-      const T e = A::exp(A::neg(A::abs(v)));
+      const T e = A::exp_nonpos(A::neg(A::abs(v)));
       return A::div(v >= zero ? one : e, A::add(one, e), nullptr);
     }
     case TRS_UN_TANH: return A::tanh(v);

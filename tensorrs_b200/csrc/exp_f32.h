@@ -1,0 +1,166 @@
+// exp_f32.h -- the f32 exponential of the hot paths, in f32 arithmetic.
+//
+// 2^(y * log2(b)) for an f32 y and the two bases the reference uses: e
+// (expf: sigmoid) and the f32 constant E = 2.7182817f (powf(E, y): ELU,
+// SELU, SoftMax).  The method is P. T. P. Tang's table-driven exponential
+// ("Table-driven implementation of the exponential function in IEEE
+// floating-point arithmetic", ACM TOMS 15(2), 1989) with 16 table entries:
+//
+//   k   = round(16 * y * log2(b))          by adding 1.5 * 2^23 (k in the low bits)
+//   z   = 16 * y * log2(b) - k             two fused multiply-adds with
+//                                          16 * log2(b) split as mh + ml;
+//                                          |z| <= 1/2, absolute error <= 2^-25
+//   p   = 2^(z/16) - 1                     degree-4 Taylor polynomial in z
+//                                          (truncation error < 2^-34)
+//   s   = T[j] + (T[j] * p + t[j])         j = k mod 16, 2^(j/16) = T[j] + t[j];
+//                                          the one rounding that matters is
+//                                          this last addition
+//   result = s * 2^(k div 16)              added to the exponent field
+//
+// The fast path covers y in [-86, 87], where the result is a normal f32;
+// other y (and NaN) return false, and the caller takes the f64 evaluation
+// (exp2_scaled) instead.  Against glibc's expf and powf(2.7182817f, y),
+// every f32 y in that range was compared on the host: at most one ulp apart,
+// 99.92 % identical overall and 99.1-99.3 % for |y| in [0.01, 20]
+// (tests/test_exp_cpu.py re-checks a sample).
+//
+// The same source compiles for the host (g++, strict IEEE: -ffp-contract=off)
+// so the host test evaluates exactly the operations the kernels do.
+#pragma once
+
+#include <cstdint>
+#include <cstring>
+
+#include "exp_table.h"
+
+#if defined(__CUDACC__)
+#define TRS_EXP_HD __host__ __device__ __forceinline__
+#else
+#include <cmath>
+#define TRS_EXP_HD inline
+#endif
+
+namespace trs {
+namespace expf32 {
+
+TRS_EXP_HD float fma_rn(float a, float b, float c) {
+#if defined(__CUDA_ARCH__)
+  return __fmaf_rn(a, b, c);
+#else
+  return std::fmaf(a, b, c);
+#endif
+}
+TRS_EXP_HD float add_rn(float a, float b) {
+#if defined(__CUDA_ARCH__)
+  return __fadd_rn(a, b);
+#else
+  return a + b;
+#endif
+}
+TRS_EXP_HD float mul_rn(float a, float b) {
+#if defined(__CUDA_ARCH__)
+  return __fmul_rn(a, b);
+#else
+  return a * b;
+#endif
+}
+TRS_EXP_HD uint32_t bits(float x) {
+#if defined(__CUDA_ARCH__)
+  return __float_as_uint(x);
+#else
+  uint32_t u;
+  std::memcpy(&u, &x, 4);
+  return u;
+#endif
+}
+TRS_EXP_HD float from_bits(uint32_t u) {
+#if defined(__CUDA_ARCH__)
+  return __uint_as_float(u);
+#else
+  float x;
+  std::memcpy(&x, &u, 4);
+  return x;
+#endif
+}
+
+// Base e and base E = 2.7182817f: 16 * log2(b) as an f32 pair.
+struct Base {
+  float mh, ml;
+};
+constexpr Base kBaseE = {kExp16LogEHi, kExp16LogELo};
+constexpr Base kBaseEf32 = {kExp16LogEf32Hi, kExp16LogEf32Lo};
+
+// The fast path: *s in [0.69, 1.45] and *ex with b^y ~= *s * 2^*ex.  Returns
+// false when y is outside the fast range (or NaN); *s and *ex are then
+// meaningless, but the table index stays in bounds for every y.  NONPOS: the
+// caller guarantees y <= 0 or NaN, so only the lower bound is checked.
+template <bool NONPOS>
+TRS_EXP_HD bool parts(float y, Base b, float* s, int* ex) {
+  const bool fast = NONPOS ? (y >= -86.0f) : (y >= -86.0f && y <= 87.0f);
+  const float kShift = 12582912.0f;  // 1.5 * 2^23
+  const float t = fma_rn(y, b.mh, kShift);
+  const int k = (int)(bits(t) - bits(kShift));
+  const float kf = add_rn(t, -kShift);
+  const float z = fma_rn(y, b.ml, fma_rn(y, b.mh, -kf));
+  float u = fma_rn(z, kExpC4, kExpC3);
+  u = fma_rn(z, u, kExpC2);
+  u = fma_rn(z, u, kExpC1);
+  const float p = mul_rn(z, u);
+  const int j = k & 15;
+#if defined(__CUDA_ARCH__)
+  const float2 tj = __ldg(reinterpret_cast<const float2*>(&kExp2Tab16[0][0]) + j);
+  const float th = tj.x, tl = tj.y;
+#else
+  const float th = kExp2Tab16[j][0], tl = kExp2Tab16[j][1];
+#endif
+  *s = add_rn(th, fma_rn(th, p, tl));
+  *ex = k >> 4;  // arithmetic shift: floor(k / 16)
+  return fast;
+}
+
+// s * 2^ex for the fast path's parts (a normal f32).
+TRS_EXP_HD float scale(float s, int ex) { return from_bits(bits(s) + ((uint32_t)ex << 23)); }
+
+// b^y for y <= 0 or NaN, branch-free (sigmoid's exp(-|x|), softmax's
+// E^(x - max)): y is clamped to -104 (below it every result rounds to 0; a
+// NaN passes the compare and propagates through s), the parts are those of
+// `parts` above, and the scaling is s * 2^(ex + 64) (exact: a normal f32)
+// times 2^-64, which rounds once.  Normal results are therefore identical to
+// the fast path's; subnormal ones (y < -87.3) carry the rounding of s as
+// well, at most one ulp from the correctly rounded value.  The exponent field
+// of 2^(ex + 64) comes from the bits of t: with t = 1.5 * 2^23 + k,
+// (bits(t) << 19) masked to the exponent field is (k div 16) << 23, because
+// the bits of 1.5 * 2^23 shift out.
+TRS_EXP_HD float exp_nonpos(float y, Base b) {
+  y = y < -104.0f ? -104.0f : y;
+  const float kShift = 12582912.0f;  // 1.5 * 2^23
+  const float t = fma_rn(y, b.mh, kShift);
+  const uint32_t tb = bits(t);
+  const float kf = add_rn(t, -kShift);
+  const float z = fma_rn(y, b.ml, fma_rn(y, b.mh, -kf));
+  float u = fma_rn(z, kExpC4, kExpC3);
+  u = fma_rn(z, u, kExpC2);
+  u = fma_rn(z, u, kExpC1);
+  const float p = mul_rn(z, u);
+  const uint32_t j = tb & 15u;
+#if defined(__CUDA_ARCH__)
+  const float2 tj = __ldg(reinterpret_cast<const float2*>(&kExp2Tab16[0][0]) + j);
+  const float th = tj.x, tl = tj.y;
+#else
+  const float th = kExp2Tab16[j][0], tl = kExp2Tab16[j][1];
+#endif
+  const float s = add_rn(th, fma_rn(th, p, tl));
+  const float p2 = from_bits(((tb << 19) & 0xFF800000u) + (191u << 23));  // 2^(ex + 64)
+  return mul_rn(mul_rn(s, p2), 0x1p-64f);
+}
+
+// The f64 value of scale(s, ex), built from the bits (no conversion
+// instruction): the f32 fields widened to the f64 layout.
+TRS_EXP_HD void scale_f64_words(float s, int ex, uint32_t* hi, uint32_t* lo) {
+  const uint32_t u = bits(s);
+  *hi = (u >> 3) + ((uint32_t)(ex + 896) << 20);
+  *lo = u << 29;
+}
+
+}  // namespace expf32
+}  // namespace trs

@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(THREADS) softmax_rows_kernel(const SmDev d) {
 #pragma unroll
         for (int i = 0; i < V; ++i) {
           if (e + i < C) {
-            const T p = A::pow_e_inline(A::sub(v[c].v[i], mx), d.e_const);
+            const T p = A::pow_e_nonpos(A::sub(v[c].v[i], mx), d.e_const);
             v[c].v[i] = p;
             s = s + A::to_acc(p);
           }
@@ -205,13 +205,13 @@ __global__ void __launch_bounds__(1024) softmax_long_kernel(const SmDev d) {
     const T mx = bcast[0];
     Acc s = Acc(0);
     for (int64_t e = threadIdx.x; e < d.C; e += blockDim.x)
-      s = s + A::to_acc(A::pow_e_inline(A::sub(__ldg(x + bi + e * d.in_step), mx), d.e_const));
+      s = s + A::to_acc(A::pow_e_nonpos(A::sub(__ldg(x + bi + e * d.in_step), mx), d.e_const));
     s = block_sum<Acc>(s, red_s);
     if (threadIdx.x == 0) bcast[1] = A::from_acc(s);
     __syncthreads();
     const T sum = bcast[1];
     for (int64_t e = threadIdx.x; e < d.C; e += blockDim.x) {
-      const T p = A::pow_e_inline(A::sub(__ldg(x + bi + e * d.in_step), mx), d.e_const);
+      const T p = A::pow_e_nonpos(A::sub(__ldg(x + bi + e * d.in_step), mx), d.e_const);
       out[bo + e * d.out_step] = A::div(p, sum, nullptr);
     }
     __syncthreads();
@@ -259,17 +259,6 @@ __device__ __forceinline__ void sstore_stream(T* p, const SVec<T, V>& r) {
   int4 x;
   memcpy(&x, &r, 16);
   __stcs(reinterpret_cast<int4*>(p), x);
-}
-
-// (double)(float)x for an f64 x >= 2^-126: the significand rounded to 24 bits
-// (to nearest, ties to even) in integer arithmetic.  Below 2^-126 the value
-// differs from the f32 rounding but stays below 2^-126, which leaves a row sum
-// of at least 1 (the maximum's own term) unchanged.
-__device__ __forceinline__ double f64_rounded_to_f32(double x) {
-  unsigned long long b = (unsigned long long)__double_as_longlong(x);
-  b += 0x0FFFFFFFull + ((b >> 29) & 1ull);
-  b &= ~0x1FFFFFFFull;
-  return __longlong_as_double((long long)b);
 }
 
 // Sum over the consumer warps (fixed order), returned to every consumer.
@@ -458,8 +447,10 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
         const T first = *reinterpret_cast<const T*>(stage);
         if (is_nan_val(first)) m = first;
       }
-      // pass 2: e = powf(E, x - m) over x in place, summed in f64
+      // pass 2: e = powf(E, x - m) over x in place, summed in f64; each
+      // thread keeps the least e it produced (f32)
       Acc acc = Acc(0);
+      float emin = INFINITY;
       if (!failed) {
 #pragma unroll 4
         for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmGroupThreads) {
@@ -467,11 +458,12 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
 #pragma unroll
           for (int i = 0; i < V; ++i) {
             if constexpr (kF32) {
-              const double e64 = exp2_scaled<true>(__fsub_rn(v.v[i], m), d.e_const);
-              v.v[i] = (float)e64;
-              acc = acc + f64_rounded_to_f32(e64);
+              const float e = expf32::exp_nonpos(__fsub_rn(v.v[i], m), expf32::kBaseEf32);
+              v.v[i] = e;
+              emin = fminf(emin, e);
+              acc = acc + (double)e;
             } else {
-              const T e = A::pow_e_inline(A::sub(v.v[i], m), d.e_const);
+              const T e = A::pow_e_nonpos(A::sub(v.v[i], m), d.e_const);
               v.v[i] = e;
               acc = acc + A::to_acc(e);
             }
@@ -491,34 +483,54 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
       // is within one ulp of e/sum, so the remainder e - q0*sum is exact (one
       // fused multiply-add) and q0 + rem*yh, rounded once, is the correctly
       // rounded quotient (P. Markstein's correction step).  Results below
-      // 2^-125 take the IEEE division itself.
+      // 2^-125 take the IEEE division itself; a thread whose least e is at
+      // least sum * 2^-124 has none (every quotient is above 2^-125), so
+      // only the other threads test each result.
       if (!failed) {
         int64_t bi, bo;
         row_bases(d, row, &bi, &bo);
         T* orow = out + bo;
         float yh = 0.0f, yl = 0.0f;
+        bool careful = true;
         if constexpr (kF32) {
           yh = __frcp_rn(sum);
           yl = (float)__dsub_rn(__drcp_rn((double)sum), (double)yh);
+          careful = !(emin >= __fmul_rn(sum, 0x1p-124f));
         }
+        if (kF32 && !careful) {
 #pragma unroll 4
-        for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmGroupThreads) {
-          const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
-          SVec<T, V> r;
+          for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmGroupThreads) {
+            const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
+            SVec<T, V> r;
 #pragma unroll
-          for (int i = 0; i < V; ++i) {
-            if constexpr (kF32) {
+            for (int i = 0; i < V; ++i) {
               const float e = v.v[i];
               const float q0 = __fmaf_rn(e, yh, __fmul_rn(e, yl));
               const float rem = __fmaf_rn(-q0, sum, e);
-              float q = __fmaf_rn(rem, yh, q0);
-              if (fabsf(q) < 0x1p-125f) q = __fdiv_rn(e, sum);
-              r.v[i] = q;
-            } else {
-              r.v[i] = A::div(v.v[i], sum, nullptr);
+              r.v[i] = __fmaf_rn(rem, yh, q0);
             }
+            sstore_stream<T, V>(orow + (size_t)k * V, r);
           }
-          sstore_stream<T, V>(orow + (size_t)k * V, r);
+        } else {
+#pragma unroll 4
+          for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmGroupThreads) {
+            const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
+            SVec<T, V> r;
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+              if constexpr (kF32) {
+                const float e = v.v[i];
+                const float q0 = __fmaf_rn(e, yh, __fmul_rn(e, yl));
+                const float rem = __fmaf_rn(-q0, sum, e);
+                float q = __fmaf_rn(rem, yh, q0);
+                if (fabsf(q) < 0x1p-125f) q = __fdiv_rn(e, sum);
+                r.v[i] = q;
+              } else {
+                r.v[i] = A::div(v.v[i], sum, nullptr);
+              }
+            }
+            sstore_stream<T, V>(orow + (size_t)k * V, r);
+          }
         }
       }
       // the consumers wrote this stage; order those writes before the next
