@@ -16,6 +16,7 @@
 #pragma once
 
 #include <cstdint>
+#include <type_traits>
 #include <cuda_runtime.h>
 
 #include "../../include/trs.h"
@@ -218,8 +219,12 @@ __device__ __forceinline__ T apply_unop(const EwParams& p, T v) {
       // x >= 0: 1 / (1 + exp(-x)); otherwise e / (1 + e) with e = exp(x).
       // Both branches take exp(-|x|), so one exponential serves either
       // (a NaN fails x >= 0 and gives exp(NaN) / ..., NaN, as the reference).
-      const T e = A::exp_nonpos(A::neg(A::abs(v)));
-      return A::div(v >= zero ? one : e, A::add(one, e), nullptr);
+      if constexpr (std::is_same<T, float>::value) {
+        return expf32::sigmoid(v);  // the same steps, with Markstein's division
+      } else {
+        const T e = A::exp_nonpos(A::neg(A::abs(v)));
+        return A::div(v >= zero ? one : e, A::add(one, e), nullptr);
+      }
     }
     case TRS_UN_TANH: return A::tanh(v);
     case TRS_UN_ELU: {  // elu.rs:47-63

@@ -154,13 +154,39 @@ TRS_EXP_HD float exp_nonpos(float y, Base b) {
   return mul_rn(mul_rn(s, p2), 0x1p-64f);
 }
 
-// The f64 value of scale(s, ex), built from the bits (no conversion
-// instruction): the f32 fields widened to the f64 layout.
-TRS_EXP_HD void scale_f64_words(float s, int ex, uint32_t* hi, uint32_t* lo) {
-  const uint32_t u = bits(s);
-  *hi = (u >> 3) + ((uint32_t)(ex + 896) << 20);
-  *lo = u << 29;
+// num / (1 + e) for the two quotients of the reference's sigmoid
+// (autodiff/ops.rs:586-593): num = 1 (x >= 0) or num = e (x < 0), where
+// e = exp(-|x|) in [0, 1], so the denominator d = RN(1 + e) lies in [1, 2].
+// P. Markstein's division ("Computation of elementary functions on the IBM
+// RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990): a reciprocal
+// seed y0 within one ulp of 1/d, one Newton step y1 = y0 + y0 (1 - d y0),
+// q0 = num y1, the exact remainder r = num - q0 d, and q = q0 + r y1 rounded
+// once.  The Newton step can land on 1/2 for d = 2 - 2^-23 (an exact tie at
+// the binade boundary), where the correction then rounds the wrong way;
+// 1/d >= 1/2 + 2^-24 for every d < 2, so y1 is floored there (for d = 2 the
+// floored y1 still corrects to 1/2).  With that floor the result equals the
+// IEEE quotient num / d for every f32 e in [0, 1] and both numerators, for
+// each seed within one ulp of 1/d: tests/test_exp_cpu.py checks all of them.
+// NaN in e propagates (the floor's compare is false).
+TRS_EXP_HD float sigmoid_div(float num, float d, float y0) {
+  float y1 = fma_rn(y0, fma_rn(-d, y0, 1.0f), y0);
+  y1 = y1 < 0x1.000002p-1f ? 0x1.000002p-1f : y1;
+  const float q0 = mul_rn(num, y1);
+  return fma_rn(fma_rn(-q0, d, num), y1, q0);
 }
+
+#if defined(__CUDACC__)
+// The reference's sigmoid, x >= 0 ? 1 / (1 + e) : e / (1 + e) with
+// e = exp(-|x|): both branches take the same e, and the seed of the division
+// is the hardware's approximate reciprocal (at most one ulp from 1/d).
+__device__ __forceinline__ float sigmoid(float x) {
+  const float e = exp_nonpos(-fabsf(x), kBaseE);
+  const float d = add_rn(1.0f, e);
+  float y0;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y0) : "f"(d));
+  return sigmoid_div(x >= 0.0f ? 1.0f : e, d, y0);
+}
+#endif
 
 }  // namespace expf32
 }  // namespace trs

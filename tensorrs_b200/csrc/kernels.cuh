@@ -53,10 +53,15 @@ struct EwDev {
   // tile kernel
   int ti;                      // tiled dimension i (unit stride in the transposed inputs)
   int transposed[3];           // input k is read through shared memory
-  int tslot[3];                // ew_tr_kernel: shared-memory tile of transposed input k, or -1
+  int tslot[3];                // ew_tr_kernel: shared-memory tile of input k, or -1 (constant along j)
+  int n_slots;                 // ew_tr_kernel: inputs staged in shared memory
   int n_batch;                 // dimensions other than i and j
   int batch_dim[kMaxDims];
   uint64_t tiles_i, tiles_j, n_tiles;
+  // ew_tr_kernel: 32-bit tile decode when n_tiles < 2^32 and every batch
+  // dimension is below 2^32 (f_dim then holds the batch dimensions' sizes)
+  int tile32;
+  FastDiv f_tj, f_ti;
 };
 
 }  // namespace trs

@@ -96,6 +96,10 @@ bool plan_row_stream(const RedRequest& q, RedDev* d, RedChoice* c, int nk, int n
   if (max_p > 64) max_p = 64;
   uint64_t P = 1;
   double best = -1.0;
+  // Outputs that fit one wave and occupy at least half the resident CTAs
+  // keep P = 1: every item then runs from the start, more than enough copies
+  // are in flight to hold HBM busy, and no partials need a second kernel.
+  if ((uint64_t)d->n_out <= cap && 2 * (uint64_t)d->n_out >= cap) max_p = 1;
   for (uint64_t q = 1; q <= max_p; ++q) {
     const uint64_t tpp = (tiles_out + q - 1) / q;
     const uint64_t parts = (tiles_out + tpp - 1) / tpp;

@@ -593,7 +593,10 @@ __global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) 
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * NB * kRsTileBytes);
   uint64_t* empty = full + S;
-  __shared__ RedAcc<T> wred[kRsConsumerWarps];
+  // per-warp states of an item, double-buffered by the item's parity (one
+  // barrier per item: a buffer is rewritten two items later, after the next
+  // barrier, which thread 0 reaches only once it has read this one)
+  __shared__ RedAcc<T> wred[2][kRsConsumerWarps];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t n_items = (uint32_t)(d.n_out * d.P);
   const uint32_t P = (uint32_t)d.P, tpp = (uint32_t)d.tpp;
@@ -648,8 +651,8 @@ __global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) 
     }
   } else {
     const int ct = threadIdx.x - 32;
-    uint32_t qn = 0;
-    for (uint32_t it = blockIdx.x; it < n_items; it += gridDim.x) {
+    uint32_t qn = 0, qi = 0;
+    for (uint32_t it = blockIdx.x; it < n_items; it += gridDim.x, ++qi) {
       const uint32_t o = it / P, part = it - o * P;
       int64_t koff[kRedOperands], ooff[2];
       rs_kept(d, o, koff, ooff);
@@ -778,17 +781,17 @@ __global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) 
       }
       a.m = m;
       a = red_warp(MODE, a);
-      if (lane == 0) wred[warp - 1] = a;
+      RedAcc<T>* wb = wred[qi & 1u];
+      if (lane == 0) wb[warp - 1] = a;
       named_sync_consumers();
       if (ct == 0 && !failed) {
-        RedAcc<T> tot = wred[0];
-        for (int w = 1; w < kRsConsumerWarps; ++w) tot = red_combine(MODE, tot, wred[w]);
+        RedAcc<T> tot = wb[0];
+        for (int w = 1; w < kRsConsumerWarps; ++w) tot = red_combine(MODE, tot, wb[w]);
         if (P == 1)
           red_write_first<T>(d, tot, ooff, first_pref);
         else
           static_cast<RedAcc<T>*>(d.parts)[it] = tot;
       }
-      named_sync_consumers();
     }
   }
   if (__syncthreads_or(failed)) {

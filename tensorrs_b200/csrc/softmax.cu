@@ -261,6 +261,15 @@ __device__ __forceinline__ void sstore_stream(T* p, const SVec<T, V>& r) {
   __stcs(reinterpret_cast<int4*>(p), x);
 }
 
+// The V per-lane accumulators of a thread, added in a fixed order.
+template <class Acc, int V>
+__device__ __forceinline__ Acc lanes_sum(const Acc (&a)[V]) {
+  Acc t = a[0];
+#pragma unroll
+  for (int i = 1; i < V; ++i) t = t + a[i];
+  return t;
+}
+
 // Sum over the consumer warps (fixed order), returned to every consumer.
 // `red` is the group's slice of kSmGroupWarps entries.
 template <class Acc>
@@ -290,17 +299,21 @@ __device__ __forceinline__ void layer_norm_row(const SmDev& d, const unsigned ch
   constexpr int V = 16 / (int)sizeof(T);
   constexpr bool kF32 = std::is_same<T, float>::value;
   const T fc = (T)d.C;
-  Acc acc = Acc(0);
+  // one f64 accumulator per vector lane: V independent add chains
+  Acc acc[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) acc[i] = Acc(0);
   if (!failed) {
 #pragma unroll 4
     for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmGroupThreads) {
       const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
 #pragma unroll
-      for (int i = 0; i < V; ++i) acc = acc + A::to_acc(v.v[i]);
+      for (int i = 0; i < V; ++i) acc[i] = acc[i] + A::to_acc(v.v[i]);
     }
   }
-  const T mean = A::div(A::from_acc(consumer_sum<Acc>(acc, red, cw, lane, grp)), fc, nullptr);
-  acc = Acc(0);
+  const T mean = A::div(A::from_acc(consumer_sum<Acc>(lanes_sum<Acc, V>(acc), red, cw, lane, grp)), fc, nullptr);
+#pragma unroll
+  for (int i = 0; i < V; ++i) acc[i] = Acc(0);
   if (!failed) {
 #pragma unroll 4
     for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmGroupThreads) {
@@ -308,11 +321,11 @@ __device__ __forceinline__ void layer_norm_row(const SmDev& d, const unsigned ch
 #pragma unroll
       for (int i = 0; i < V; ++i) {
         const T xm = A::sub(v.v[i], mean);
-        acc = acc + A::to_acc(A::mul(xm, xm));
+        acc[i] = acc[i] + A::to_acc(A::mul(xm, xm));
       }
     }
   }
-  const T var = A::div(A::from_acc(consumer_sum<Acc>(acc, red, cw, lane, grp)), fc, nullptr);
+  const T var = A::div(A::from_acc(consumer_sum<Acc>(lanes_sum<Acc, V>(acc), red, cw, lane, grp)), fc, nullptr);
   if (failed) return;
   T denom;
   if constexpr (kF32) denom = __fsqrt_rn(A::add(var, (T)d.ln_eps));
@@ -449,7 +462,9 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
       }
       // pass 2: e = powf(E, x - m) over x in place, summed in f64; each
       // thread keeps the least e it produced (f32)
-      Acc acc = Acc(0);
+      Acc accs[V];  // one per vector lane: V independent add chains
+#pragma unroll
+      for (int i = 0; i < V; ++i) accs[i] = Acc(0);
       float emin = INFINITY;
       if (!failed) {
 #pragma unroll 4
@@ -461,16 +476,17 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
               const float e = expf32::exp_nonpos(__fsub_rn(v.v[i], m), expf32::kBaseEf32);
               v.v[i] = e;
               emin = fminf(emin, e);
-              acc = acc + (double)e;
+              accs[i] = accs[i] + (double)e;
             } else {
               const T e = A::pow_e_nonpos(A::sub(v.v[i], m), d.e_const);
               v.v[i] = e;
-              acc = acc + A::to_acc(e);
+              accs[i] = accs[i] + A::to_acc(e);
             }
           }
           *reinterpret_cast<SVec<T, V>*>(stage + k * 16) = v;
         }
       }
+      Acc acc = lanes_sum<Acc, V>(accs);
       for (int o = 16; o > 0; o >>= 1) acc = acc + __shfl_xor_sync(0xffffffffu, acc, o);
       if (lane == 0) gred_sum[cw] = acc;
       sm_group_sync(grp);

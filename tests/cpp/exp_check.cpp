@@ -82,6 +82,60 @@ static void sweep_nonpos(const char* name, bool pow_e, uint32_t stride) {
               (long long)mismatch);
 }
 
+// sigmoid_div against the IEEE quotient, for every f32 e in [0, 1] (d = 1 + e),
+// both numerators (1 and e) and the seeds RN(1/d) and its two neighbours
+// (every f32 within one ulp of 1/d): prints the count and the mismatches.
+static void check_sigmoid_div() {
+  int64_t count = 0, bad = 0;
+#pragma omp parallel for reduction(+ : count, bad) schedule(static)
+  for (int64_t u = 0; u <= (int64_t)bits(1.0f); ++u) {
+    const float e = from_bits((uint32_t)u);
+    const float d = 1.0f + e;
+    const float rn = 1.0f / d;
+    const float seeds[3] = {std::nextafter(rn, 0.0f), rn, std::nextafter(rn, 2.0f)};
+    for (int n = 0; n < 2; ++n) {
+      const float num = n ? e : 1.0f;
+      const float want = num / d;
+      for (float y0 : seeds) {
+        ++count;
+        if (bits(sigmoid_div(num, d, y0)) != bits(want)) ++bad;
+      }
+    }
+  }
+  std::printf("sigmoid_div 0 1 %lld %lld 0 %lld\n", (long long)count, (long long)(count - bad), (long long)bad);
+}
+
+// The whole sigmoid (exp_nonpos, then sigmoid_div with the seed RN(1/d))
+// against the reference's two branches on glibc's expf, every stride-th f32.
+static void sweep_sigmoid(uint32_t stride) {
+  int64_t count = 0, same = 0, worst = 0, mismatch = 0;
+  const int64_t n = (int64_t)(0xFFFFFFFFull / stride) + 1;
+#pragma omp parallel for reduction(+ : count, same, mismatch) reduction(max : worst) schedule(static)
+  for (int64_t i = 0; i < n; ++i) {
+    const float x = from_bits((uint32_t)(i * stride));
+    const float e = exp_nonpos(-std::fabs(x), kBaseE);
+    const float d = 1.0f + e;
+    const float got = sigmoid_div(x >= 0.0f ? 1.0f : e, d, 1.0f / d);
+    float want;
+    if (x >= 0.0f) {
+      want = 1.0f / (1.0f + expf(-x));
+    } else {
+      const float ee = expf(x);
+      want = ee / (1.0f + ee);
+    }
+    if (want != want || got != got) {
+      if ((want != want) != (got != got)) ++mismatch;
+      continue;
+    }
+    const int64_t dist = ulp_distance(got, want);
+    ++count;
+    if (dist == 0) ++same;
+    if (dist > worst) worst = dist;
+  }
+  std::printf("sigmoid -inf inf %lld %lld %lld %lld\n", (long long)count, (long long)same, (long long)worst,
+              (long long)mismatch);
+}
+
 int main(int argc, char** argv) {
   const uint32_t stride = argc > 1 ? (uint32_t)std::strtoul(argv[1], nullptr, 10) : 1;
   for (int f = 0; f < 2; ++f) {
@@ -93,5 +147,7 @@ int main(int argc, char** argv) {
     sweep(name, f, 1.0f, 20.0f, stride > 16 ? stride / 16 : 1);
     sweep_nonpos(name, f, stride);
   }
+  check_sigmoid_div();
+  sweep_sigmoid(stride);
   return 0;
 }
