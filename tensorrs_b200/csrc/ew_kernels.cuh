@@ -465,18 +465,19 @@ ew_tile_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials
 // ew_tr_kernel: the same layouts as ew_tile_kernel (an input running along
 // another dimension i than the output's unit-stride dimension j, such as B^T)
 // when every row start is 16-byte aligned.  Tiles are TS x TS elements
-// (TS = 256 bytes: 64 f32 / 32 f64).  Every input that is not constant along
-// j goes from global to shared memory with 16-byte cp.async: transposed inputs
-// with the tile's columns as their shared rows, the others in the output's
-// layout; an input constant along j is one scalar per row.  The copies of the
-// CTA's next tile are issued into the second of two buffers before the
-// current tile is combined, so they overlap its arithmetic.  After a barrier
-// each thread reads its transposed values down the shared columns, applies
-// the compile-time program and stores 16 bytes of output.  The 16-byte chunks
-// of a transposed shared row are XOR-swizzled by the row's chunk group, which
-// keeps both the cp.async writes and the column reads at most two-way bank
-// conflicted.  Tile indices are decoded with 32-bit fast division when they
-// fit, and interior tiles skip the bounds checks.
+// (TS = 256 bytes: 64 f32 / 32 f64).  Each thread first issues all of its
+// loads of a tile: transposed inputs go from global to shared memory with
+// 16-byte cp.async (their rows are the tile's columns), the other inputs into
+// registers with 16-byte loads in the output's layout (or one scalar per row
+// when constant along j).  After one barrier each thread reads its transposed
+// values down the shared columns, applies the compile-time program and
+// stores 16 bytes of output.  The 16-byte chunks of a shared row are
+// XOR-swizzled by the row's chunk group, which keeps both the cp.async writes
+// and the column reads at most two-way bank conflicted.  Tile indices are
+// decoded with 32-bit fast division when they fit, and interior tiles skip
+// the bounds checks.  (Staging every input in shared memory with the next
+// tile's copies in flight measured slower: the extra shared-memory traffic
+// and instructions outweighed the overlap.)
 
 template <class T, int PROG, bool WRITE, bool SUM>
 __global__ void __launch_bounds__(kThreads, 3)
@@ -488,120 +489,96 @@ ew_tr_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials) 
   constexpr int CPR = TS / V;                 // 16-byte chunks per tile row
   constexpr int VPT = TS * CPR / kThreads;    // chunks per thread per input
   constexpr int NIN = prog_inputs(PROG);
-  constexpr int kSlotBytes = TS * 256;
   extern __shared__ __align__(128) unsigned char tsm[];
   Acc acc = Acc(0);
   const int j = d.nd - 1, ti = d.ti;
   const int64_t Ni = d.shape[ti], Nj = d.shape[j];
-  const int nslots = d.n_slots;
   const T* ins[3] = {static_cast<const T*>(d.in[0]), static_cast<const T*>(d.in[1]),
                      static_cast<const T*>(d.in[2])};
   T* out = static_cast<T*>(d.out);
-
-  struct Tile {
+  for (uint64_t t = blockIdx.x; t < d.n_tiles; t += gridDim.x) {
     int64_t i0, j0;
     int64_t o[kMaxOperands];
-    bool full;  // interior: no bounds checks
-  };
-  auto decode = [&](uint64_t t) {
-    Tile c;
 #pragma unroll
-    for (int k = 0; k < kMaxOperands; ++k) c.o[k] = d.off[k];
+    for (int k = 0; k < kMaxOperands; ++k) o[k] = d.off[k];
     if (d.tile32) {  // 32-bit decode by fast division
       const uint32_t t32 = (uint32_t)t;
       const uint32_t rest = fdiv(t32, d.f_tj);
-      c.j0 = (int64_t)(t32 - rest * d.f_tj.d) * TS;
+      j0 = (int64_t)(t32 - rest * d.f_tj.d) * TS;
       uint32_t b = fdiv(rest, d.f_ti);
-      c.i0 = (int64_t)(rest - b * d.f_ti.d) * TS;
+      i0 = (int64_t)(rest - b * d.f_ti.d) * TS;
       for (int q = d.n_batch - 1; q >= 0; --q) {
         const int dd = d.batch_dim[q];
         const uint32_t nb = fdiv(b, d.f_dim[dd]);
-        const int64_t cc = (int64_t)(b - nb * d.f_dim[dd].d);
+        const int64_t c = (int64_t)(b - nb * d.f_dim[dd].d);
         b = nb;
 #pragma unroll
-        for (int k = 0; k < kMaxOperands; ++k) c.o[k] += cc * d.st[k][dd];
+        for (int k = 0; k < kMaxOperands; ++k) o[k] += c * d.st[k][dd];
       }
     } else {
       uint64_t rest = t / d.tiles_j;
-      c.j0 = (int64_t)(t - rest * d.tiles_j) * TS;
+      j0 = (int64_t)(t - rest * d.tiles_j) * TS;
       uint64_t b = rest / d.tiles_i;
-      c.i0 = (int64_t)(rest - b * d.tiles_i) * TS;
+      i0 = (int64_t)(rest - b * d.tiles_i) * TS;
       for (int q = d.n_batch - 1; q >= 0; --q) {
         const int dd = d.batch_dim[q];
         const uint64_t nb = b / (uint64_t)d.shape[dd];
-        const int64_t cc = (int64_t)(b - nb * (uint64_t)d.shape[dd]);
+        const int64_t c = (int64_t)(b - nb * (uint64_t)d.shape[dd]);
         b = nb;
 #pragma unroll
-        for (int k = 0; k < kMaxOperands; ++k) c.o[k] += cc * d.st[k][dd];
+        for (int k = 0; k < kMaxOperands; ++k) o[k] += c * d.st[k][dd];
       }
     }
-    c.full = c.i0 + TS <= Ni && c.j0 + TS <= Nj;
-    return c;
-  };
-  // global -> shared with 16-byte cp.async: transposed inputs with their
-  // tile rows along j (XOR-swizzled chunks), the others in the output's layout
-  auto issue = [&](const Tile& c, int buf) {
+    const bool full = i0 + TS <= Ni && j0 + TS <= Nj;  // interior: no bounds checks
+    // 1. transposed inputs: global -> shared, tile row = j offset
 #pragma unroll
     for (int k = 0; k < NIN; ++k) {
       const int slot = d.tslot[k];
       if (slot < 0) continue;
-      unsigned char* base = tsm + (buf * nslots + slot) * kSlotBytes;
-      const int64_t sj = d.st[k + 1][j], si = d.st[k + 1][ti];
-      const bool tr = d.transposed[k] != 0;
+      unsigned char* base = tsm + slot * (TS * 256);
+      const int64_t sj = d.st[k + 1][j];
 #pragma unroll
       for (int r = 0; r < VPT; ++r) {
         const int v = threadIdx.x + r * kThreads;
         const int row = v / CPR, ch = v % CPR;
-        if (tr) {
-          const int64_t jj = c.j0 + row, ii = c.i0 + (int64_t)ch * V;
-          if (c.full || (jj < Nj && ii < Ni))
-            cp_async16(base + row * 256 + ((ch ^ ((row / V) & 15)) * 16), ins[k] + c.o[k + 1] + ii + jj * sj);
-        } else {
-          const int64_t ii = c.i0 + row, jj = c.j0 + (int64_t)ch * V;
-          if (c.full || (ii < Ni && jj < Nj))
-            cp_async16(base + row * 256 + ch * 16, ins[k] + c.o[k + 1] + ii * si + jj);
+        const int64_t jj = j0 + row, ii = i0 + (int64_t)ch * V;
+        if (full || (jj < Nj && ii < Ni))
+          cp_async16(base + row * 256 + ((ch ^ ((row / V) & 15)) * 16), ins[k] + o[k + 1] + ii + jj * sj);
+      }
+    }
+    cp_async_commit();
+    // 2. the other inputs: registers, in the output's layout (row = i offset)
+    VecT<T, V> rv[NIN][VPT];
+#pragma unroll
+    for (int k = 0; k < NIN; ++k) {
+      if (d.tslot[k] >= 0) continue;
+      const int64_t sj = d.st[k + 1][j], si = d.st[k + 1][ti];
+#pragma unroll
+      for (int r = 0; r < VPT; ++r) {
+        const int v = threadIdx.x + r * kThreads;
+        const int row = v / CPR, ch = v % CPR;
+        const int64_t ii = i0 + row, jj = j0 + (int64_t)ch * V;
+        if (full || (ii < Ni && jj < Nj)) {
+          const T* src = ins[k] + o[k + 1] + ii * si + jj * sj;
+          if (sj == 1) {
+            rv[k][r] = load_vec<T, V>(src);
+          } else {
+            const T sc = __ldg(src);
+#pragma unroll
+            for (int q = 0; q < V; ++q) rv[k][r].v[q] = sc;
+          }
         }
       }
     }
-  };
-
-  // Software pipeline: the copies of the next tile are in flight while the
-  // current one is combined (two shared-memory buffers per input).
-  uint64_t t = blockIdx.x;
-  Tile cur = decode(t < d.n_tiles ? t : 0);
-  if (t < d.n_tiles) issue(cur, 0);
-  cp_async_commit();
-  int buf = 0;
-  for (; t < d.n_tiles; t += gridDim.x, buf ^= 1) {
-    const uint64_t tn = t + gridDim.x;
-    Tile nxt = cur;
-    if (tn < d.n_tiles) {
-      nxt = decode(tn);
-      issue(nxt, buf ^ 1);
-    }
-    cp_async_commit();
-    cp_async_wait_prev();
+    cp_async_wait_all();
     __syncthreads();
-    // combine, store 16 bytes per chunk
+    // 3. combine, store 16 bytes per chunk
 #pragma unroll
     for (int r = 0; r < VPT; ++r) {
       const int v = threadIdx.x + r * kThreads;
       const int row = v / CPR, ch = v % CPR;
-      const int64_t ii = cur.i0 + row, jj = cur.j0 + (int64_t)ch * V;
-      if (cur.full || (ii < Ni && jj < Nj)) {
-        VecT<T, V> sv[NIN];
-#pragma unroll
-        for (int k = 0; k < NIN; ++k) {
-          const int slot = d.tslot[k];
-          if (slot >= 0 && !d.transposed[k]) {
-            sv[k] = *reinterpret_cast<const VecT<T, V>*>(tsm + (buf * nslots + slot) * kSlotBytes + row * 256 +
-                                                         ch * 16);
-          } else if (slot < 0) {  // constant along j: one value per row
-            const T sc = __ldg(ins[k] + cur.o[k + 1] + ii * d.st[k + 1][ti]);
-#pragma unroll
-            for (int q = 0; q < V; ++q) sv[k].v[q] = sc;
-          }
-        }
+      const int64_t ii = i0 + row, jj = j0 + (int64_t)ch * V;
+      if (full || (ii < Ni && jj < Nj)) {
         VecT<T, V> res;
 #pragma unroll
         for (int q = 0; q < V; ++q) {
@@ -609,25 +586,22 @@ ew_tr_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials) 
 #pragma unroll
           for (int k = 0; k < NIN; ++k) {
             const int slot = d.tslot[k];
-            if (slot >= 0 && d.transposed[k]) {
+            if (slot >= 0) {
               const int jr = ch * V + q;  // the transposed input's tile row
-              a[k] = *reinterpret_cast<const T*>(tsm + (buf * nslots + slot) * kSlotBytes + jr * 256 +
+              a[k] = *reinterpret_cast<const T*>(tsm + slot * (TS * 256) + jr * 256 +
                                                  (((row / V) ^ (ch & 15)) * 16) + (row % V) * (int)sizeof(T));
             } else {
-              a[k] = sv[k].v[q];
+              a[k] = rv[k][r].v[q];
             }
           }
           res.v[q] = apply_prog<T, PROG>(p, a[0], a[1], a[2]);
           if constexpr (SUM) acc = acc + A::to_acc(res.v[q]);
         }
-        if constexpr (WRITE) store_vec_stream<T, V>(out + cur.o[0] + ii * d.st[0][ti] + jj, res);
+        if constexpr (WRITE) store_vec_stream<T, V>(out + o[0] + ii * d.st[0][ti] + jj, res);
       }
     }
-    // this buffer is refilled by the next iteration's copies
     __syncthreads();
-    cur = nxt;
   }
-  cp_async_wait_all();
   if constexpr (SUM) write_partial<Acc>(acc, partials);
 }
 
@@ -994,19 +968,15 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
     auto aligned = [&](const void* base, int64_t off) {
       return ((uintptr_t)base + (uintptr_t)(off * (int64_t)sizeof(T))) % 16 == 0;
     };
-    int nt = 0, ns = 0;  // transposed inputs, staged inputs
+    int nt = 0;
     for (int k = 0; k < prog.n_in && ok; ++k) {
       const int64_t sj = f.st[k + 1][j], si = f.st[k + 1][ti];
       d.tslot[k] = -1;
-      d.transposed[k] = 0;
       if (sj != 0 && sj != 1) {  // transposed: unit stride along i required
         ok = si == 1 && sj % VW == 0 && aligned(in[k].data, f.off[k + 1]);
-        d.tslot[k] = ns++;
-        d.transposed[k] = 1;
-        ++nt;
+        d.tslot[k] = nt++;
       } else if (sj == 1) {
         ok = si % VW == 0 && aligned(in[k].data, f.off[k + 1]);
-        d.tslot[k] = ns++;
       }
       for (int i = 0; i < f.nd && ok; ++i)
         if (i != ti && i != j && f.st[k + 1][i] % VW) ok = false;
@@ -1040,8 +1010,7 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
         for (int q = 0; q < d.n_batch; ++q)
           d.f_dim[d.batch_dim[q]] = make_fastdiv((uint32_t)f.shape[d.batch_dim[q]]);
       }
-      d.n_slots = ns;
-      tr_smem = 2 * ns * TS * 256;  // two buffers per staged input
+      tr_smem = nt * TS * 256;
       ewk::allow_smem(tk, tr_smem);
       grid_for(tk, ewk::resident_blocks_smem(tk, kThreads, tr_smem), d.n_tiles);
       variant = kEwTr;

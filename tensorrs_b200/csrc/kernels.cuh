@@ -53,8 +53,7 @@ struct EwDev {
   // tile kernel
   int ti;                      // tiled dimension i (unit stride in the transposed inputs)
   int transposed[3];           // input k is read through shared memory
-  int tslot[3];                // ew_tr_kernel: shared-memory tile of input k, or -1 (constant along j)
-  int n_slots;                 // ew_tr_kernel: inputs staged in shared memory
+  int tslot[3];                // ew_tr_kernel: shared-memory tile of transposed input k, or -1
   int n_batch;                 // dimensions other than i and j
   int batch_dim[kMaxDims];
   uint64_t tiles_i, tiles_j, n_tiles;

@@ -718,7 +718,9 @@ __global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) 
               tb = p ? cm : tb;
               tc = p ? c : tc;
             }
-            if (tc != 0xffffffffu) {
+            // the recovered value equals tb, so the strict test against the
+            // running best comes first and most tiles skip the re-read
+            if (tc != 0xffffffffu && (m.idx < 0 || tb > m.val)) {
               const RVec<T, V> g = *reinterpret_cast<const RVec<T, V>*>(stage + tc * 16);
               int first = V - 1;
               T val = g.v[V - 1];
@@ -728,10 +730,8 @@ __global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) 
                   first = i;
                   val = g.v[i];
                 }
-              if (m.idx < 0 || val > m.val) {
-                m.val = val;
-                m.idx = col0 + (int64_t)(tc * V + first);
-              }
+              m.val = val;
+              m.idx = col0 + (int64_t)(tc * V + first);
             }
           }
 #pragma unroll 4

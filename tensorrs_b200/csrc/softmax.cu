@@ -299,21 +299,17 @@ __device__ __forceinline__ void layer_norm_row(const SmDev& d, const unsigned ch
   constexpr int V = 16 / (int)sizeof(T);
   constexpr bool kF32 = std::is_same<T, float>::value;
   const T fc = (T)d.C;
-  // one f64 accumulator per vector lane: V independent add chains
-  Acc acc[V];
-#pragma unroll
-  for (int i = 0; i < V; ++i) acc[i] = Acc(0);
+  Acc acc = Acc(0);
   if (!failed) {
 #pragma unroll 4
     for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmGroupThreads) {
       const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
 #pragma unroll
-      for (int i = 0; i < V; ++i) acc[i] = acc[i] + A::to_acc(v.v[i]);
+      for (int i = 0; i < V; ++i) acc = acc + A::to_acc(v.v[i]);
     }
   }
-  const T mean = A::div(A::from_acc(consumer_sum<Acc>(lanes_sum<Acc, V>(acc), red, cw, lane, grp)), fc, nullptr);
-#pragma unroll
-  for (int i = 0; i < V; ++i) acc[i] = Acc(0);
+  const T mean = A::div(A::from_acc(consumer_sum<Acc>(acc, red, cw, lane, grp)), fc, nullptr);
+  acc = Acc(0);
   if (!failed) {
 #pragma unroll 4
     for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmGroupThreads) {
@@ -321,11 +317,11 @@ __device__ __forceinline__ void layer_norm_row(const SmDev& d, const unsigned ch
 #pragma unroll
       for (int i = 0; i < V; ++i) {
         const T xm = A::sub(v.v[i], mean);
-        acc[i] = acc[i] + A::to_acc(A::mul(xm, xm));
+        acc = acc + A::to_acc(A::mul(xm, xm));
       }
     }
   }
-  const T var = A::div(A::from_acc(consumer_sum<Acc>(lanes_sum<Acc, V>(acc), red, cw, lane, grp)), fc, nullptr);
+  const T var = A::div(A::from_acc(consumer_sum<Acc>(acc, red, cw, lane, grp)), fc, nullptr);
   if (failed) return;
   T denom;
   if constexpr (kF32) denom = __fsqrt_rn(A::add(var, (T)d.ln_eps));
