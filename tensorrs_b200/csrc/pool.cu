@@ -9,11 +9,15 @@
 // input, so each output here reads its window straight from the input: one
 // read of the input and one write of the output, no im2col buffer.
 //
-//   pool_fwd_kernel<T, MODE, KW>  KW > 0: kw == stride_w == KW, unit-stride
-//       rows aligned to 16 bytes; a thread loads one 16-byte strip per window
-//       row, which holds the windows of 16 / (KW * size) neighbouring outputs.
-//       KW == 0: any window; one thread per output, scalar loads (neighbouring
-//       threads share their rows through L1).
+//   pool_strip_kernel  kw == stride_w dividing 16 bytes, kh <= 4, unit-stride
+//       rows aligned to 16 bytes: a thread loads one 16-byte strip per window
+//       row, which holds the windows of 16 / (kw * size) neighbouring outputs.
+//   pool_tile_fwd_kernel  any window and stride, rows aligned to 16 bytes: an
+//       item is a block of window rows of one plane whose input rows are
+//       staged once in shared memory (16-byte cp.async), then each output
+//       reads its window from there.
+//   pool_fwd_kernel  any other layout: one thread per output, scalar loads
+//       (neighbouring threads share their rows through L1).
 //   pool_max_bwd_kernel<T>  the gradient MaxPool2d passes back to its input:
 //       max_axis's backward (autodiff/core.rs:352-375) gives each window's
 //       gradient to the first of its largest elements (argmax_axis,
@@ -23,6 +27,11 @@
 //       it in that order and finds each window's winner again; with
 //       `accumulate` it adds the sum to the gradient already held (the
 //       `current + grad` of autodiff/traits.rs:141-150).
+//       pool_max_bwd_strip_kernel serves windows that tile the image (stride
+//       == window, kw dividing 16 bytes) with 16-byte strips;
+//       pool_tile_bwd_kernel stages the rows of a block of window rows in
+//       shared memory, finds each window's winner once, then lets each owned
+//       pixel add the gradients of the covering windows it wins.
 //
 // Order of floating-point operations: max keeps the window's first element and
 // replaces it only by a strictly greater one (a NaN first element stays); the
