@@ -103,18 +103,30 @@ __device__ __forceinline__ RedAcc<T> red_combine(int mode, RedAcc<T> a, const Re
   return a;
 }
 
+// Only the fields the mode uses move (a constant mode drops the others).
 template <class T>
-__device__ __forceinline__ RedAcc<T> red_shfl_down(const RedAcc<T>& a, int o) {
-  RedAcc<T> r;
-  r.s0 = __shfl_down_sync(0xffffffffu, a.s0, o);
-  r.s1 = __shfl_down_sync(0xffffffffu, a.s1, o);
-  r.m = shfl_down_max(a.m, o);
+__device__ __forceinline__ RedAcc<T> red_shfl_down(int mode, const RedAcc<T>& a, int o) {
+  RedAcc<T> r = a;
+  if (mode == kRedMax || mode == kRedArgmax) {
+    r.m = shfl_down_max(a.m, o);
+  } else {
+    r.s0 = __shfl_down_sync(0xffffffffu, a.s0, o);
+    if (mode == kRedAffineRelu) r.s1 = __shfl_down_sync(0xffffffffu, a.s1, o);
+  }
   return r;
 }
 
 template <class T>
 __device__ __forceinline__ RedAcc<T> red_warp(int mode, RedAcc<T> a) {
-  for (int o = 16; o > 0; o >>= 1) a = red_combine(mode, a, red_shfl_down(a, o));
+  for (int o = 16; o > 0; o >>= 1) a = red_combine(mode, a, red_shfl_down(mode, a, o));
+  return a;
+}
+
+// The first n (a power of two, <= 32) lanes' states combined as a tree in a
+// fixed order; the result is valid in lane 0.
+template <class T>
+__device__ __forceinline__ RedAcc<T> red_lanes(int mode, RedAcc<T> a, int n) {
+  for (int o = n >> 1; o > 0; o >>= 1) a = red_combine(mode, a, red_shfl_down(mode, a, o));
   return a;
 }
 
@@ -784,13 +796,16 @@ __global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) 
       RedAcc<T>* wb = wred[qi & 1u];
       if (lane == 0) wb[warp - 1] = a;
       named_sync_consumers();
-      if (ct == 0 && !failed) {
-        RedAcc<T> tot = wb[0];
-        for (int w = 1; w < kRsConsumerWarps; ++w) tot = red_combine(MODE, tot, wb[w]);
-        if (P == 1)
-          red_write_first<T>(d, tot, ooff, first_pref);
-        else
-          static_cast<RedAcc<T>*>(d.parts)[it] = tot;
+      // the first consumer warp folds the warps' states as a lane tree
+      if (warp == 1) {
+        RedAcc<T> tot = lane < kRsConsumerWarps ? wb[lane] : red_init<T>();
+        tot = red_lanes(MODE, tot, kRsConsumerWarps);
+        if (ct == 0 && !failed) {
+          if (P == 1)
+            red_write_first<T>(d, tot, ooff, first_pref);
+          else
+            static_cast<RedAcc<T>*>(d.parts)[it] = tot;
+        }
       }
     }
   }
