@@ -479,7 +479,17 @@ ew_tile_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials
 // tile's copies in flight measured slower: the extra shared-memory traffic
 // and instructions outweighed the overlap.)
 
-template <class T, int PROG, bool WRITE, bool SUM>
+// Shared-memory tile of input k: from the launch descriptor (TM < 0), or
+// known at compile time from the mask TM of transposed inputs (bit k set: input
+// k is transposed; its tile follows those of the lower transposed inputs).
+constexpr int popc_c(int x) { return x ? (x & 1) + popc_c(x >> 1) : 0; }
+template <int TM>
+__device__ __forceinline__ int tr_slot(const EwDev& d, int k) {
+  if constexpr (TM < 0) return d.tslot[k];
+  else return ((TM >> k) & 1) ? popc_c(TM & ((1 << k) - 1)) : -1;
+}
+
+template <class T, int PROG, bool WRITE, bool SUM, int TM = -1>
 __global__ void __launch_bounds__(kThreads, 3)
 ew_tr_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials) {
   using A = Arith<T>;
@@ -533,7 +543,7 @@ ew_tr_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials) 
     // 1. transposed inputs: global -> shared, tile row = j offset
 #pragma unroll
     for (int k = 0; k < NIN; ++k) {
-      const int slot = d.tslot[k];
+      const int slot = tr_slot<TM>(d, k);
       if (slot < 0) continue;
       unsigned char* base = tsm + slot * (TS * 256);
       const int64_t sj = d.st[k + 1][j];
@@ -551,7 +561,7 @@ ew_tr_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials) 
     VecT<T, V> rv[NIN][VPT];
 #pragma unroll
     for (int k = 0; k < NIN; ++k) {
-      if (d.tslot[k] >= 0) continue;
+      if (tr_slot<TM>(d, k) >= 0) continue;
       const int64_t sj = d.st[k + 1][j], si = d.st[k + 1][ti];
 #pragma unroll
       for (int r = 0; r < VPT; ++r) {
@@ -585,7 +595,7 @@ ew_tr_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials) 
           T a[3] = {T(0), T(0), T(0)};
 #pragma unroll
           for (int k = 0; k < NIN; ++k) {
-            const int slot = d.tslot[k];
+            const int slot = tr_slot<TM>(d, k);
             if (slot >= 0) {
               const int jr = ch * V + q;  // the transposed input's tile row
               a[k] = *reinterpret_cast<const T*>(tsm + slot * (TS * 256) + jr * 256 +
@@ -763,8 +773,19 @@ const void* pick_stream_nb(int nb, bool write, bool want_sum) {
 }
 
 template <class T, int PROG>
-const void* pick_tr_ws(bool write, bool want_sum) {
-  if (write && !want_sum) return (const void*)ew_tr_kernel<T, PROG, true, false>;
+const void* pick_tr_ws(bool write, bool want_sum, int tmask) {
+  if (write && !want_sum) {
+    // the fused programs of the transposed layouts get kernels specialised on
+    // which inputs are transposed
+    if constexpr (PROG == kMul || PROG == kMulSigmoid) {
+      switch (tmask) {
+        case 1: return (const void*)ew_tr_kernel<T, PROG, true, false, 1>;
+        case 2: return (const void*)ew_tr_kernel<T, PROG, true, false, 2>;
+        case 3: return (const void*)ew_tr_kernel<T, PROG, true, false, 3>;
+      }
+    }
+    return (const void*)ew_tr_kernel<T, PROG, true, false>;
+  }
   if constexpr (prog_is_runtime(PROG)) {
     if (write && want_sum) return (const void*)ew_tr_kernel<T, PROG, true, true>;
     return (const void*)ew_tr_kernel<T, PROG, false, true>;
@@ -773,10 +794,10 @@ const void* pick_tr_ws(bool write, bool want_sum) {
 }
 
 template <class T, int PROG>
-const void* pick_tr_code(bool write, bool want_sum) {
+const void* pick_tr_code(bool write, bool want_sum, int tmask) {
   if constexpr (prog_is_runtime(PROG) || PROG == kPack || PROG == kAdd || PROG == kSub || PROG == kMul ||
                 PROG == kMulSigmoid)
-    return pick_tr_ws<T, PROG>(write, want_sum);
+    return pick_tr_ws<T, PROG>(write, want_sum, tmask);
   return nullptr;
 }
 
@@ -818,9 +839,11 @@ const void* pick_vec(int code, int fallback, int vw, bool write, bool want_sum) 
 }
 
 template <class T>
-const void* pick_tr(int code, int fallback, bool write, bool want_sum) {
-  const void* k = by_code<T>(code, [&](auto c) { return pick_tr_code<T, decltype(c)::value>(write, want_sum); });
-  if (!k) k = by_code<T>(fallback, [&](auto c) { return pick_tr_code<T, decltype(c)::value>(write, want_sum); });
+const void* pick_tr(int code, int fallback, bool write, bool want_sum, int tmask) {
+  const void* k =
+      by_code<T>(code, [&](auto c) { return pick_tr_code<T, decltype(c)::value>(write, want_sum, tmask); });
+  if (!k)
+    k = by_code<T>(fallback, [&](auto c) { return pick_tr_code<T, decltype(c)::value>(write, want_sum, -1); });
   return k;
 }
 
@@ -989,7 +1012,10 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
     const int code = program_code(prog, IsFloat<T>::value);
     const bool simple = is_simple_program(prog) || !IsFloat<T>::value;
     const int fallback = (simple ? kRunSimple1 : kRunFull1) + (prog.n_in - 1);
-    const void* tk = ok && nt > 0 ? ewk::pick_tr<T>(code, fallback, write, want_sum) : nullptr;
+    int tmask = 0;  // inputs read through shared-memory tiles
+    for (int k = 0; k < prog.n_in; ++k)
+      if (d.tslot[k] >= 0) tmask |= 1 << k;
+    const void* tk = ok && nt > 0 ? ewk::pick_tr<T>(code, fallback, write, want_sum, tmask) : nullptr;
     if (tk) {
       constexpr int TS = 256 / sizeof(T);
       d.ti = ti;
