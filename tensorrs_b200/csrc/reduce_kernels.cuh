@@ -825,8 +825,18 @@ __global__ void __launch_bounds__(256) red_parts_finalize(const RedDev d) {
   const T* x0 = static_cast<const T*>(d.in[0]);
   const RedAcc<T>* parts = static_cast<const RedAcc<T>*>(d.parts);
   for (uint32_t o = blockIdx.x * 256 + threadIdx.x; o < (uint32_t)d.n_out; o += gridDim.x * 256) {
-    RedAcc<T> tot = parts[(uint64_t)o * d.P];
-    for (int64_t p = 1; p < d.P; ++p) tot = red_combine(MODE, tot, parts[(uint64_t)o * d.P + p]);
+    // the parts in order, loaded eight at a time so their loads overlap
+    const RedAcc<T>* po = parts + (uint64_t)o * d.P;
+    RedAcc<T> tot = po[0];
+    int64_t p = 1;
+    for (; p + 8 <= d.P; p += 8) {
+      RedAcc<T> v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = po[p + i];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) tot = red_combine(MODE, tot, v[i]);
+    }
+    for (; p < d.P; ++p) tot = red_combine(MODE, tot, po[p]);
     int64_t koff[kRedOperands], ooff[2];
     rs_kept(d, o, koff, ooff);
     red_write<T>(d, tot, ooff, x0, koff[0]);
@@ -1082,8 +1092,20 @@ __global__ void __launch_bounds__(256) red_cparts_finalize(const RedDev d) {
   const Part* parts = static_cast<const Part*>(d.parts);
   const uint64_t n = (uint64_t)d.n_out;
   for (uint64_t u = (uint64_t)blockIdx.x * 256 + threadIdx.x; u < n; u += (uint64_t)gridDim.x * 256) {
+    // the parts in order, loaded eight at a time so their loads overlap
     Part t = parts[u];
-    for (int64_t p = 1; p < d.P; ++p) {
+    int64_t p = 1;
+    for (; p + 8 <= d.P; p += 8) {
+      Part v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = parts[(uint64_t)(p + i) * n + u];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if constexpr (CsIsMax<MODE>::value) t = max_combine(t, v[i]);
+        else t = t + v[i];
+      }
+    }
+    for (; p < d.P; ++p) {
       const Part v = parts[(uint64_t)p * n + u];
       if constexpr (CsIsMax<MODE>::value) t = max_combine(t, v);
       else t = t + v;
