@@ -394,7 +394,9 @@ __device__ __forceinline__ void tile_item(const PoolDev& d, uint64_t item, int64
 
 // Forward: an item is a block of R output rows of one plane; its input rows
 // are staged once, then each output reads its window from shared memory.
-template <class T, int MODE>
+// KH, KW > 0: the window's size at compile time (its loops unroll); 0: the
+// launch descriptor's.
+template <class T, int MODE, int KH = 0, int KW = 0>
 __global__ void __launch_bounds__(256) pool_tile_fwd_kernel(const PoolDev d) {
   using A = Arith<T>;
   extern __shared__ __align__(16) unsigned char pool_smem[];
@@ -411,19 +413,25 @@ __global__ void __launch_bounds__(256) pool_tile_fwd_kernel(const PoolDev d) {
     for (uint32_t o = threadIdx.x; o < nout; o += blockDim.x) {
       const uint32_t i = fdiv(o, d.f_ow), j = o - i * (uint32_t)d.OW;
       const T* w = sm + i * d.sh * d.P + j * d.sw;
+      const int kh = KH > 0 ? KH : d.kh, kw = KW > 0 ? KW : d.kw;
       T r;
       if constexpr (MODE == kPoolMax) {
         r = w[0];
-        for (int u = 0; u < d.kh; ++u)
-          for (int v = (u == 0 ? 1 : 0); v < d.kw; ++v) {
+#pragma unroll
+        for (int u = 0; u < kh; ++u)
+#pragma unroll
+          for (int v = 0; v < kw; ++v) {
+            if (u == 0 && v == 0) continue;
             const T val = w[u * d.P + v];
             if (val > r) r = val;
           }
       } else {
         r = T(0);
-        for (int u = 0; u < d.kh; ++u)
-          for (int v = 0; v < d.kw; ++v) r = A::add(r, w[u * d.P + v]);
-        r = A::div(r, (T)((int64_t)d.kh * d.kw), nullptr);
+#pragma unroll
+        for (int u = 0; u < kh; ++u)
+#pragma unroll
+          for (int v = 0; v < kw; ++v) r = A::add(r, w[u * d.P + v]);
+        r = A::div(r, (T)((int64_t)kh * kw), nullptr);
       }
       out[oplane + (i0 + i) * d.os[2] + (int64_t)j * d.os[3]] = r;
     }
@@ -663,9 +671,17 @@ Error launch_pool_fwd(PoolDev d, int mode, int64_t N, int64_t C, cudaStream_t st
   const bool aligned = rows_aligned(d.x, d.x_off, d.xs, sizeof(T));
   const bool strip = d.kw == d.sw && d.kw > 0 && VW % d.kw == 0 && d.kh <= 4 && aligned;
   size_t smem = 0;
-  if ((!strip || TRS_POOL_TILE_FIRST) && aligned && plan_tile(&d, false, sizeof(T), N, C, &smem))
+  if ((!strip || TRS_POOL_TILE_FIRST) && aligned && plan_tile(&d, false, sizeof(T), N, C, &smem)) {
+    // the common square windows with their loops unrolled
+    if (d.kh == 3 && d.kw == 3)
+      return mode == kPoolMax ? pool_tile_launch(pool_tile_fwd_kernel<T, kPoolMax, 3, 3>, d, smem, stream, "pool tiles")
+                              : pool_tile_launch(pool_tile_fwd_kernel<T, kPoolAvg, 3, 3>, d, smem, stream, "pool tiles");
+    if (d.kh == 2 && d.kw == 2)
+      return mode == kPoolMax ? pool_tile_launch(pool_tile_fwd_kernel<T, kPoolMax, 2, 2>, d, smem, stream, "pool tiles")
+                              : pool_tile_launch(pool_tile_fwd_kernel<T, kPoolAvg, 2, 2>, d, smem, stream, "pool tiles");
     return mode == kPoolMax ? pool_tile_launch(pool_tile_fwd_kernel<T, kPoolMax>, d, smem, stream, "pool tiles")
                             : pool_tile_launch(pool_tile_fwd_kernel<T, kPoolAvg>, d, smem, stream, "pool tiles");
+  }
   if (!strip) {
     set_items(&d, N * C, C, d.OH, d.OW);
     return mode == kPoolMax ? pool_launch(pool_fwd_kernel<T, kPoolMax>, d, stream, "pool kernel")
