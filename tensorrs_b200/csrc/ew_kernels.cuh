@@ -489,8 +489,10 @@ __device__ __forceinline__ int tr_slot(const EwDev& d, int k) {
   else return ((TM >> k) & 1) ? popc_c(TM & ((1 << k) - 1)) : -1;
 }
 
+// The sigmoid epilogue's long arithmetic phase overlaps other CTAs' loads:
+// its kernels are held to 64 registers so four CTAs fit on an SM.
 template <class T, int PROG, bool WRITE, bool SUM, int TM = -1>
-__global__ void __launch_bounds__(kThreads, 3)
+__global__ void __launch_bounds__(kThreads, PROG == kMulSigmoid ? 4 : 3)
 ew_tr_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials) {
   using A = Arith<T>;
   using Acc = typename A::Acc;

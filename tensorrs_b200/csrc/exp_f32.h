@@ -167,10 +167,11 @@ TRS_EXP_HD float exp_nonpos(float y, Base b) {
 // floored y1 still corrects to 1/2).  With that floor the result equals the
 // IEEE quotient num / d for every f32 e in [0, 1] and both numerators, for
 // each seed within one ulp of 1/d: tests/test_exp_cpu.py checks all of them.
-// NaN in e propagates (the floor's compare is false).
+// NaN in e propagates through num.
 TRS_EXP_HD float sigmoid_div(float num, float d, float y0) {
-  float y1 = fma_rn(y0, fma_rn(-d, y0, 1.0f), y0);
-  y1 = y1 < 0x1.000002p-1f ? 0x1.000002p-1f : y1;
+  // the floor as a maximum: a NaN y1 (only for a NaN d, where num is NaN as
+  // well) becomes the floor, and num carries the NaN on
+  const float y1 = fmaxf(fma_rn(y0, fma_rn(-d, y0, 1.0f), y0), 0x1.000002p-1f);
   const float q0 = mul_rn(num, y1);
   return fma_rn(fma_rn(-q0, d, num), y1, q0);
 }
