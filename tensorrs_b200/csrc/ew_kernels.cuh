@@ -18,6 +18,7 @@
 #pragma once
 
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <type_traits>
@@ -617,6 +618,96 @@ ew_tr_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials) 
   if constexpr (SUM) write_partial<Acc>(acc, partials);
 }
 
+// ew_tr2d_kernel: ew_tr_kernel for the fused multiply programs on two
+// folded dimensions (i = 0, j = 1), with the mask TM of transposed inputs
+// fixed at compile time and every offset within 2^31 elements of its
+// operand's base: the tile's offsets are 32-bit, and each thread's chunk
+// coordinates inside a tile, with their shared-memory addresses, are
+// computed once.  Same data flow as ew_tr_kernel.
+template <class T, int PROG, int TM>
+__global__ void __launch_bounds__(kThreads, PROG == kMulSigmoid ? 4 : 3)
+ew_tr2d_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc*) {
+  constexpr int V = 16 / (int)sizeof(T);
+  constexpr int TS = 256 / (int)sizeof(T);
+  constexpr int CPR = TS / V;
+  constexpr int VPT = TS * CPR / kThreads;
+  constexpr int NIN = 2;
+  extern __shared__ __align__(128) unsigned char tsm[];
+  const int32_t Ni = (int32_t)d.shape[0], Nj = (int32_t)d.shape[1];
+  const T* in0 = static_cast<const T*>(d.in[0]) + d.off[1];
+  const T* in1 = static_cast<const T*>(d.in[1]) + d.off[2];
+  T* out = static_cast<T*>(d.out) + d.off[0];
+  const int32_t si[2] = {(int32_t)d.st[1][0], (int32_t)d.st[2][0]};
+  const int32_t sj[2] = {(int32_t)d.st[1][1], (int32_t)d.st[2][1]};
+  const int32_t so = (int32_t)d.st[0][0];
+  // this thread's chunks: tile row and 16-byte column chunk
+  int row[VPT], ch[VPT];
+#pragma unroll
+  for (int r = 0; r < VPT; ++r) {
+    const int v = threadIdx.x + r * kThreads;
+    row[r] = v / CPR;
+    ch[r] = v % CPR;
+  }
+  const uint32_t n_tiles = (uint32_t)d.n_tiles;
+  for (uint32_t t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+    const uint32_t ti = fdiv(t, d.f_tj);
+    const int32_t j0 = (int32_t)(t - ti * d.f_tj.d) * TS, i0 = (int32_t)ti * TS;
+    const bool full = i0 + TS <= Ni && j0 + TS <= Nj;
+    // transposed inputs: global -> shared (tile row = j offset), swizzled
+#pragma unroll
+    for (int k = 0; k < NIN; ++k) {
+      if (!((TM >> k) & 1)) continue;
+      unsigned char* base = tsm + popc_c(TM & ((1 << k) - 1)) * (TS * 256);
+      const T* src = k == 0 ? in0 : in1;
+#pragma unroll
+      for (int r = 0; r < VPT; ++r) {
+        const int32_t jj = j0 + row[r], ii = i0 + ch[r] * V;
+        if (full || (jj < Nj && ii < Ni))
+          cp_async16(base + row[r] * 256 + ((ch[r] ^ ((row[r] / V) & 15)) * 16), src + ii + jj * sj[k]);
+      }
+    }
+    cp_async_commit();
+    // the other inputs: registers, in the output's layout
+    VecT<T, V> rv[NIN][VPT];
+#pragma unroll
+    for (int k = 0; k < NIN; ++k) {
+      if ((TM >> k) & 1) continue;
+      const T* src = k == 0 ? in0 : in1;
+#pragma unroll
+      for (int r = 0; r < VPT; ++r) {
+        const int32_t ii = i0 + row[r], jj = j0 + ch[r] * V;
+        if (full || (ii < Ni && jj < Nj)) rv[k][r] = load_vec<T, V>(src + ii * si[k] + jj);
+      }
+    }
+    cp_async_wait_all();
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < VPT; ++r) {
+      const int32_t ii = i0 + row[r], jj = j0 + ch[r] * V;
+      if (full || (ii < Ni && jj < Nj)) {
+        VecT<T, V> res;
+#pragma unroll
+        for (int q = 0; q < V; ++q) {
+          T a[2];
+#pragma unroll
+          for (int k = 0; k < NIN; ++k) {
+            if ((TM >> k) & 1) {
+              a[k] = *reinterpret_cast<const T*>(tsm + popc_c(TM & ((1 << k) - 1)) * (TS * 256) +
+                                                 (ch[r] * V + q) * 256 + (((row[r] / V) ^ (ch[r] & 15)) * 16) +
+                                                 (row[r] % V) * (int)sizeof(T));
+            } else {
+              a[k] = rv[k][r].v[q];
+            }
+          }
+          res.v[q] = apply_prog<T, PROG>(p, a[0], a[1], T(0));
+        }
+        store_vec_stream<T, V>(out + ii * so + jj, res);
+      }
+    }
+    __syncthreads();
+  }
+}
+
 // --------------------------------------------------------------------------
 // ew_generic_kernel: one element per thread, every operand's offset decoded
 // from the row-major element index.
@@ -1018,6 +1109,28 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
     for (int k = 0; k < prog.n_in; ++k)
       if (d.tslot[k] >= 0) tmask |= 1 << k;
     const void* tk = ok && nt > 0 ? ewk::pick_tr<T>(code, fallback, write, want_sum, tmask) : nullptr;
+    // two folded dimensions, a fused multiply program, 32-bit offsets: the
+    // 2-D kernel
+    bool two_d = tk && f.nd == 2 && ti == 0 && j == 1 && write && !want_sum && tmask >= 1 && tmask <= 3 &&
+                 prog.n_in == 2 && (code == kMul || code == kMulSigmoid);
+    for (int k = 0; k <= prog.n_in && two_d; ++k) {
+      const uint64_t span = (uint64_t)(f.shape[0] - 1) * (uint64_t)std::llabs(f.st[k][0]) +
+                            (uint64_t)(f.shape[1] - 1) * (uint64_t)std::llabs(f.st[k][1]);
+      if (span >= (1ull << 31)) two_d = false;
+    }
+    if (two_d) {
+      const void* k2 = nullptr;
+      if (code == kMul) {
+        k2 = tmask == 1 ? (const void*)ewk::ew_tr2d_kernel<T, kMul, 1>
+             : tmask == 2 ? (const void*)ewk::ew_tr2d_kernel<T, kMul, 2>
+                          : (const void*)ewk::ew_tr2d_kernel<T, kMul, 3>;
+      } else {
+        k2 = tmask == 1 ? (const void*)ewk::ew_tr2d_kernel<T, kMulSigmoid, 1>
+             : tmask == 2 ? (const void*)ewk::ew_tr2d_kernel<T, kMulSigmoid, 2>
+                          : (const void*)ewk::ew_tr2d_kernel<T, kMulSigmoid, 3>;
+      }
+      tk = k2;
+    }
     if (tk) {
       constexpr int TS = 256 / sizeof(T);
       d.ti = ti;
@@ -1029,7 +1142,7 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
       uint64_t nbt = 1;
       for (int q = 0; q < d.n_batch; ++q) nbt *= (uint64_t)f.shape[d.batch_dim[q]];
       d.n_tiles = d.tiles_i * d.tiles_j * nbt;
-      d.tile32 = d.n_tiles < (1ull << 32) ? 1 : 0;
+      d.tile32 = d.n_tiles < (1ull << 32) ? 1 : 0;  // always, for the 2-D kernel (offsets < 2^31)
       for (int q = 0; q < d.n_batch; ++q)
         if ((uint64_t)f.shape[d.batch_dim[q]] >= (1ull << 32)) d.tile32 = 0;
       if (d.tile32) {

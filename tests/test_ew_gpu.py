@@ -153,6 +153,25 @@ def test_transposed_pack_sigmoid_and_three_inputs():
     assert abs(got_s - ref_s) <= 1e-5 * sabs and abs(got_s - exact) <= abs(exact) * 2.0**-23 + 2.0**-40 * sabs
 
 
+@pytest.mark.parametrize("n,m", [(512, 512), (136, 200)], ids=lambda v: str(v))
+def test_both_operands_transposed(n, m):
+    """A^T & B^T and sigmoid(A^T & B^T): both inputs read through shared-memory
+    tiles (full and partial tiles), bit-exact for the product and within
+    2 ulp for the sigmoid."""
+    import oracle
+    from tensorrs_b200 import abi, device
+    a = rand([m, n], np.float32, 61)
+    b = rand([m, n], np.float32, 62)
+    dat = DevView(a.reshape(-1), [n, m], [1, n], 0)
+    dbt = DevView(b.reshape(-1), [n, m], [1, n], 0)
+    want = oracle.binary("mul", dat.host_view(), dbt.host_view())
+    assert_bit_exact(gpu_binary("mul", dat, dbt, np.float32), want, "A^T & B^T")
+    out = empty([n, m], np.float32)
+    device.elementwise(abi.program(2, abi.MUL, epilogue="sigmoid"), [dat.view, dbt.view], out)
+    want = oracle.program(2, "mul", "add", "sigmoid", [dat.host_view(), dbt.host_view()])
+    assert max_ulp(to_host(out), want) <= 2
+
+
 def test_transposed_batched_vectorised():
     """[B, n, m] with a permuted view of a [B, m, n] storage, 16-byte aligned."""
     import oracle
