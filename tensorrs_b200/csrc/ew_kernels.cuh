@@ -708,6 +708,39 @@ ew_tr2d_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc*) {
   }
 }
 
+// ew_flat1_kernel: a one-input map with a transcendental program (sigmoid,
+// tanh) over a contiguous 1-D range of fewer than 2^31 16-byte chunks: the
+// vector kernel's data flow (four chunks per thread loaded, then mapped)
+// with plain chunk indices instead of the strided row decode.
+template <class T, int PROG>
+__global__ void __launch_bounds__(kThreads, 4)
+ew_flat1_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc*) {
+  constexpr int V = 16 / (int)sizeof(T);
+  constexpr int U = 4;
+  const T* in = static_cast<const T*>(d.in[0]) + d.off[1];
+  T* out = static_cast<T*>(d.out) + d.off[0];
+  const uint32_t n = (uint32_t)d.n_chunks;
+  const bool stream = d.stream[0] != 0;
+  for (uint32_t base = blockIdx.x * (kThreads * U) + threadIdx.x; base < n; base += gridDim.x * (kThreads * U)) {
+    VecT<T, V> v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t g = base + (uint32_t)u * kThreads;
+      if (g < n) v[u] = stream ? load_vec_stream<T, V>(in + (size_t)g * V) : load_vec<T, V>(in + (size_t)g * V);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t g = base + (uint32_t)u * kThreads;
+      if (g < n) {
+        VecT<T, V> r;
+#pragma unroll
+        for (int i = 0; i < V; ++i) r.v[i] = apply_prog<T, PROG>(p, v[u].v[i], T(0), T(0));
+        store_vec_stream<T, V>(out + (size_t)g * V, r);
+      }
+    }
+  }
+}
+
 // --------------------------------------------------------------------------
 // ew_generic_kernel: one element per thread, every operand's offset decoded
 // from the row-major element index.
@@ -932,6 +965,15 @@ const void* pick_vec(int code, int fallback, int vw, bool write, bool want_sum) 
 }
 
 template <class T>
+const void* pick_flat1(int code) {
+  if constexpr (IsFloat<T>::value) {
+    if (code == kSigmoid) return (const void*)ew_flat1_kernel<T, kSigmoid>;
+    if (code == kTanh) return (const void*)ew_flat1_kernel<T, kTanh>;
+  }
+  return nullptr;
+}
+
+template <class T>
 const void* pick_tr(int code, int fallback, bool write, bool want_sum, int tmask) {
   const void* k =
       by_code<T>(code, [&](auto c) { return pick_tr_code<T, decltype(c)::value>(write, want_sum, tmask); });
@@ -1067,6 +1109,11 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
       const uint64_t per_block = (uint64_t)kThreads * (prog.n_in == 1 ? 4 : 2);
       const uint64_t wb = (chunks + per_block - 1) / per_block;
       const void* k = ewk::pick_vec<T>(V == VW ? code : fallback, fallback, V, write, want_sum);
+      // a contiguous 1-D transcendental map: plain chunk indices
+      if (f.nd == 1 && prog.n_in == 1 && V == VW && write && !want_sum && f.st[0][0] == 1 && f.st[1][0] == 1) {
+        const void* k1 = ewk::pick_flat1<T>(code);
+        if (k1) k = k1;
+      }
       if (TRS_VEC_PERSISTENT) {
         grid_for(k, ewk::resident_blocks(k, kThreads), wb);
       } else {
