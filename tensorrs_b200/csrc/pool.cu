@@ -97,6 +97,16 @@ struct alignas(sizeof(T) * V) PVec {
 };
 
 // One window by scalar loads, in row-major order.
+// The average's division by the window size n.  For a power of two the
+// quotient x / n equals x * (1/n) exactly before rounding (1/n is exact), so
+// the product rounds to the IEEE quotient bit for bit, zeros, infinities,
+// NaN and subnormals included; other sizes divide.
+template <class T>
+__device__ __forceinline__ T pool_mean(T acc, int64_t n) {
+  if ((n & (n - 1)) == 0) return Arith<T>::mul(acc, (T)(1.0 / (double)n));
+  return Arith<T>::div(acc, (T)n, nullptr);
+}
+
 template <class T, int MODE>
 __device__ __forceinline__ T pool_window(const T* __restrict__ x, int64_t base, const PoolDev& d) {
   using A = Arith<T>;
@@ -112,7 +122,7 @@ __device__ __forceinline__ T pool_window(const T* __restrict__ x, int64_t base, 
     T acc = T(0);
     for (int u = 0; u < d.kh; ++u)
       for (int v = 0; v < d.kw; ++v) acc = A::add(acc, __ldg(x + base + u * d.xs[2] + v * d.xs[3]));
-    return A::div(acc, (T)((int64_t)d.kh * d.kw), nullptr);
+    return pool_mean<T>(acc, (int64_t)d.kh * d.kw);
   }
 }
 
@@ -193,7 +203,7 @@ __global__ void __launch_bounds__(256) pool_strip_kernel(const PoolDev d) {
         for (int o = 0; o < Q; ++o) {
           if (j0 + o < d.OW) {
             T res = r[o];
-            if constexpr (MODE == kPoolAvg) res = A::div(res, (T)((int64_t)d.kh * KW), nullptr);
+            if constexpr (MODE == kPoolAvg) res = pool_mean<T>(res, (int64_t)d.kh * KW);
             out[obase[k] + (j0 + o) * d.os[3]] = res;
           }
         }
@@ -431,7 +441,7 @@ __global__ void __launch_bounds__(256) pool_tile_fwd_kernel(const PoolDev d) {
         for (int u = 0; u < kh; ++u)
 #pragma unroll
           for (int v = 0; v < kw; ++v) r = A::add(r, w[u * d.P + v]);
-        r = A::div(r, (T)((int64_t)kh * kw), nullptr);
+        r = pool_mean<T>(r, (int64_t)kh * kw);
       }
       out[oplane + (i0 + i) * d.os[2] + (int64_t)j * d.os[3]] = r;
     }
