@@ -100,6 +100,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+// Programmatic dependent launch.  launch_dependents: the next grid on the
+// stream, if launched with programmatic stream serialization, may be
+// scheduled now; wait: in that grid, blocks until the previous grid has
+// completed and its memory operations are visible (returns at once when the
+// grid was launched without the attribute).
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Error codes in the async-error word.
 constexpr int kAsyncWaitTimeout = 1;
 

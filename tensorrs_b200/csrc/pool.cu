@@ -276,7 +276,7 @@ __global__ void __launch_bounds__(256) pool_max_bwd_kernel(const PoolDev d) {
 // the last row of windows also the rows below that no window reads (0, or
 // grad_x + 0 when accumulating); columns past the last window get 0 too.
 template <class T, int KW, int KH>
-__global__ void __launch_bounds__(256) pool_max_bwd_strip_kernel(const PoolDev d) {
+__global__ void __launch_bounds__(256, 3) pool_max_bwd_strip_kernel(const PoolDev d) {
   constexpr int VW = 16 / sizeof(T);
   constexpr int Q = VW / KW;
   using A = Arith<T>;

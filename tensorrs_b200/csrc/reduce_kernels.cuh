@@ -597,6 +597,8 @@ __device__ __forceinline__ void rs_seg(const RedDev& d, uint32_t r, int64_t* off
 
 template <class T, int MODE, int NB>
 __global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) {
+  // the partials' fold kernel, launched after this one, may be scheduled now
+  pdl_launch_dependents();
   using A = Arith<T>;
   using Acc = typename A::Acc;
   constexpr int V = 16 / (int)sizeof(T);
@@ -822,6 +824,7 @@ __global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) 
 // Combines the P partials of every output in part order and writes it.
 template <class T, int MODE>
 __global__ void __launch_bounds__(256) red_parts_finalize(const RedDev d) {
+  pdl_wait();  // the partials of the kernel before it
   const T* x0 = static_cast<const T*>(d.in[0]);
   const RedAcc<T>* parts = static_cast<const RedAcc<T>*>(d.parts);
   for (uint32_t o = blockIdx.x * 256 + threadIdx.x; o < (uint32_t)d.n_out; o += gridDim.x * 256) {
@@ -888,6 +891,8 @@ using CsPart = typename std::conditional<CsIsMax<MODE>::value, MaxState<T>, type
 
 template <class T, int MODE, int NB>
 __global__ void __launch_bounds__(kRsThreads) red_cstream_kernel(const RedDev d) {
+  // the partials' fold kernel, launched after this one, may be scheduled now
+  pdl_launch_dependents();
   using A = Arith<T>;
   using Acc = typename A::Acc;
   constexpr int V = 16 / (int)sizeof(T);
@@ -1087,6 +1092,7 @@ __global__ void __launch_bounds__(kRsThreads) red_cstream_kernel(const RedDev d)
 // Folds the P per-part partials of every output in part order and writes it.
 template <class T, int MODE>
 __global__ void __launch_bounds__(256) red_cparts_finalize(const RedDev d) {
+  pdl_wait();  // the partials of the kernel before it
   using Part = CsPart<T, MODE>;
   const T* x0 = static_cast<const T*>(d.in[0]);
   const Part* parts = static_cast<const Part*>(d.parts);
@@ -1212,6 +1218,23 @@ bool red_cstream_available(int mode, int nb) {
   return rk::pick_red_cstream<T>(mode, nb) != nullptr;
 }
 
+// A fold kernel launched with programmatic stream serialization: it is
+// scheduled while the reduction before it finishes and waits (pdl_wait) for
+// that grid's completion, which removes the gap between the two launches.
+inline cudaError_t launch_fold(const void* k, unsigned grid, void** args, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, k, args);
+}
+
 template <class T>
 Error red_launch(RedDev& d, const RedChoice& c, cudaStream_t stream) {
   using namespace rk;
@@ -1252,7 +1275,7 @@ Error red_launch(RedDev& d, const RedChoice& c, cudaStream_t stream) {
       const void* fk = pick_red_finalize<T>(d.mode);
       const uint64_t fb = ((uint64_t)d.n_out + 255) / 256;
       const unsigned fg = (unsigned)(fb < (uint64_t)dev.sm_count * 8 ? fb : (uint64_t)dev.sm_count * 8);
-      ce = cudaLaunchKernel(fk, dim3(fg), dim3(256), args, 0, stream);
+      ce = launch_fold(fk, fg, args, stream);
       if (ce != cudaSuccess) return cuda_error(ce, "partials finalize launch");
       return check_launch("reduction finalize kernel");
     }
@@ -1288,7 +1311,7 @@ Error red_launch(RedDev& d, const RedChoice& c, cudaStream_t stream) {
       const void* fk = pick_red_cfinalize<T>(d.mode);
       const uint64_t fb = ((uint64_t)d.n_out + 255) / 256;
       const unsigned fg = (unsigned)(fb < (uint64_t)dev.sm_count * 8 ? fb : (uint64_t)dev.sm_count * 8);
-      ce = cudaLaunchKernel(fk, dim3(fg), dim3(256), args, 0, stream);
+      ce = launch_fold(fk, fg, args, stream);
       if (ce != cudaSuccess) return cuda_error(ce, "column partials finalize launch");
       return check_launch("column reduction finalize kernel");
     }
