@@ -131,6 +131,7 @@ __device__ __forceinline__ void write_partial(Acc acc, Acc* partials) {
 template <class T, int V, int PROG, bool WRITE, bool SUM>
 __global__ void __launch_bounds__(kThreads, 4)
 ew_vec_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials) {
+  if constexpr (SUM) pdl_launch_dependents();  // sum_finalize_kernel may be scheduled now
   using A = Arith<T>;
   using Acc = typename A::Acc;
   constexpr int NIN = prog_inputs(PROG);
@@ -253,6 +254,7 @@ __device__ __forceinline__ void stream_tile_geometry(const EwDev& d, uint32_t t,
 template <class T, int PROG, int NB, bool WRITE, bool SUM>
 __global__ void __launch_bounds__(kStreamThreads)
 ew_stream_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials) {
+  if constexpr (SUM) pdl_launch_dependents();  // sum_finalize_kernel may be scheduled now
   using A = Arith<T>;
   using Acc = typename A::Acc;
   constexpr int NIN = prog_inputs(PROG);
@@ -401,6 +403,7 @@ ew_stream_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partia
 template <class T, bool WRITE, bool SUM>
 __global__ void __launch_bounds__(kThreads)
 ew_tile_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials) {
+  if constexpr (SUM) pdl_launch_dependents();  // sum_finalize_kernel may be scheduled now
   using A = Arith<T>;
   using Acc = typename A::Acc;
   __shared__ T tile[3][32][33];
@@ -495,6 +498,7 @@ __device__ __forceinline__ int tr_slot(const EwDev& d, int k) {
 template <class T, int PROG, bool WRITE, bool SUM, int TM = -1>
 __global__ void __launch_bounds__(kThreads, PROG == kMulSigmoid ? 4 : 3)
 ew_tr_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials) {
+  if constexpr (SUM) pdl_launch_dependents();  // sum_finalize_kernel may be scheduled now
   using A = Arith<T>;
   using Acc = typename A::Acc;
   constexpr int V = 16 / (int)sizeof(T);
@@ -747,6 +751,7 @@ ew_flat1_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc*) {
 template <class T, bool WRITE, bool SUM>
 __global__ void __launch_bounds__(kThreads)
 ew_generic_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials) {
+  if constexpr (SUM) pdl_launch_dependents();  // sum_finalize_kernel may be scheduled now
   using A = Arith<T>;
   using Acc = typename A::Acc;
   Acc acc = Acc(0);
@@ -784,6 +789,7 @@ template <class T>
 __global__ void __launch_bounds__(1024)
 sum_finalize_kernel(const typename Arith<T>::Acc* partials, int n, T* out,
                     typename Arith<T>::Acc* raw_out) {
+  pdl_wait();  // the partials of the kernel before it
   using Acc = typename Arith<T>::Acc;
   __shared__ Acc red[32];
   Acc s = Acc(0);
@@ -1268,8 +1274,22 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
   if (want_sum) {
     T* sum_out = nullptr;
     if (sum->view) sum_out = static_cast<T*>(sum->view->data) + sum->view->offset;
-    ewk::sum_finalize_kernel<T><<<1, 1024, 0, stream>>>(part, n_part, sum_out,
-                                                   static_cast<Acc*>(sum->raw_acc));
+    // launched with programmatic stream serialization: scheduled while the
+    // element-wise kernel finishes, it waits for that grid in pdl_wait
+    Acc* raw = static_cast<Acc*>(sum->raw_acc);
+    void* fargs[] = {(void*)&part, (void*)&n_part, (void*)&sum_out, (void*)&raw};
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(1024);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t fe = cudaLaunchKernelExC(&cfg, (const void*)ewk::sum_finalize_kernel<T>, fargs);
+    if (fe != cudaSuccess) return cuda_error(fe, "sum finalize launch");
     Error e = check_launch("sum finalize kernel");
     if (!e.ok()) return e;
   }
