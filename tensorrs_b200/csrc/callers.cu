@@ -169,12 +169,8 @@ Error launch_opt(const trs_view* p, const trs_view* g, const trs_view* m, const 
   const int64_t n = numel_of(p->shape, p->ndim);
   if (n == 0) return Error{};
   auto at = [](const trs_view* w) -> T* { return w ? static_cast<T*>(w->data) + w->offset : nullptr; };
-  int per_sm = 1;
   auto k = optim_kernel<T, KIND>;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kOptThreads, 0) != cudaSuccess || per_sm < 1) {
-    cudaGetLastError();
-    per_sm = 1;
-  }
+  const int per_sm = resident_blocks_smem((const void*)k, kOptThreads, 0);
   constexpr int V = 16 / sizeof(T);
   const uint64_t want = ((uint64_t)n / V + kOptThreads - 1) / kOptThreads + 1;
   const uint64_t cap = (uint64_t)current_device_info().sm_count * (uint64_t)per_sm;
@@ -412,11 +408,7 @@ __global__ void __launch_bounds__(1024) layernorm_long_kernel(const LnDev d) {
 
 template <class K>
 unsigned ln_grid(K kernel, int threads, uint64_t work) {
-  int per_sm = 1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) != cudaSuccess || per_sm < 1) {
-    cudaGetLastError();
-    per_sm = 1;
-  }
+  const int per_sm = resident_blocks_smem((const void*)kernel, threads, 0);
   const uint64_t cap = (uint64_t)current_device_info().sm_count * (uint64_t)per_sm;
   const uint64_t g = work < cap ? work : cap;
   return (unsigned)(g < 1 ? 1 : g);

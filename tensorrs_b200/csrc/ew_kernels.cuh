@@ -822,31 +822,8 @@ int resident_blocks(K kernel, int threads) {
   return resident_blocks((const void*)kernel, threads);
 }
 
-inline void allow_smem(const void* kernel, int bytes) {
-  static std::mutex mu;
-  static std::unordered_map<const void*, int> done;
-  std::lock_guard<std::mutex> lock(mu);
-  if (done[kernel] >= bytes) return;
-  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess)
-    done[kernel] = bytes;
-  else
-    cudaGetLastError();
-}
-
-inline int resident_blocks_smem(const void* kernel, int threads, int smem) {
-  static std::mutex mu;
-  static std::unordered_map<const void*, int> cache;
-  std::lock_guard<std::mutex> lock(mu);
-  auto it = cache.find(kernel);
-  if (it != cache.end()) return it->second;
-  int b = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, threads, smem) != cudaSuccess || b < 1) {
-    cudaGetLastError();
-    b = 1;
-  }
-  cache[kernel] = b;
-  return b;
-}
+using trs::allow_smem;
+using trs::resident_blocks_smem;
 
 // Which (write, sum) forms a program code is instantiated with: every code
 // writes; sums are instantiated for the runtime codes, Y = A & B + c, and

@@ -5,6 +5,10 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <map>
+#include <mutex>
+#include <unordered_map>
+#include <utility>
 
 #include "bulk.cuh"
 #include "device_ops.cuh"
@@ -26,6 +30,37 @@ FastDiv make_fastdiv(uint32_t d);
 
 __device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
   return (uint32_t)(((uint64_t)__umulhi(n, f.m) + n) >> f.s);
+}
+
+// Per-kernel launch set-up done once per process: the dynamic shared memory
+// a kernel may use (raised only upward), and the CTAs of it an SM keeps
+// resident with a given dynamic shared memory (each kernel here has one block
+// size), queried once per pair.
+inline void allow_smem(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, int> done;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done[kernel] >= bytes) return;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess)
+    done[kernel] = bytes;
+  else
+    cudaGetLastError();
+}
+
+inline int resident_blocks_smem(const void* kernel, int threads, int smem) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> cache;  // (kernel, shared bytes)
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(kernel, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int b = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, threads, smem) != cudaSuccess || b < 1) {
+    cudaGetLastError();
+    b = 1;
+  }
+  cache[key] = b;
+  return b;
 }
 
 // Element-wise launch descriptor (passed by value as a kernel parameter).

@@ -519,11 +519,7 @@ __global__ void __launch_bounds__(256) pool_tile_bwd_kernel(const PoolDev d) {
 // One wave of 256-thread CTAs (as many per SM as fit), each thread looping.
 template <class K>
 unsigned pool_grid(K kernel, uint64_t items) {
-  int per_sm = 1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, 0) != cudaSuccess || per_sm < 1) {
-    cudaGetLastError();
-    per_sm = 1;
-  }
+  const int per_sm = resident_blocks_smem((const void*)kernel, 256, 0);
   const uint64_t cap = (uint64_t)current_device_info().sm_count * (uint64_t)per_sm;
   const uint64_t need = (items + 255) / 256;
   return (unsigned)(need < cap ? (need < 1 ? 1 : need) : cap);
@@ -663,11 +659,7 @@ bool plan_tile(PoolDev* d, bool bwd, int es, int64_t N, int64_t C, size_t* smem)
 
 template <class K>
 Error pool_tile_launch(K kernel, const PoolDev& d, size_t smem, cudaStream_t stream, const char* what) {
-  int per_sm = 1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, smem) != cudaSuccess || per_sm < 1) {
-    cudaGetLastError();
-    per_sm = 1;
-  }
+  const int per_sm = resident_blocks_smem((const void*)kernel, 256, (int)smem);
   const uint64_t cap = (uint64_t)current_device_info().sm_count * (uint64_t)per_sm;
   const uint64_t grid = (uint64_t)d.items < cap ? (uint64_t)d.items : cap;
   kernel<<<(unsigned)grid, 256, smem, stream>>>(d);

@@ -1246,17 +1246,8 @@ Error red_launch(RedDev& d, const RedChoice& c, cudaStream_t stream) {
     if (!k) return make_error(TRS_ERR_ARG, "no stream reduction kernel for this mode");
     const int S = rs_stages(c.nb);
     const int smem = S * c.nb * kRsTileBytes + 2 * S * 8;
-    static std::mutex mu;
-    {
-      std::lock_guard<std::mutex> lock(mu);
-      if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-        return cuda_error(cudaGetLastError(), "cudaFuncSetAttribute");
-    }
-    int per_sm = 1;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kRsThreads, smem) != cudaSuccess || per_sm < 1) {
-      cudaGetLastError();
-      per_sm = 1;
-    }
+    allow_smem(k, smem);  // once per kernel
+    const int per_sm = resident_blocks_smem(k, kRsThreads, smem);
     const uint64_t items = (uint64_t)d.n_out * (uint64_t)d.P;
     const uint64_t cap = (uint64_t)dev.sm_count * (uint64_t)per_sm;
     const unsigned grid = (unsigned)(items < cap ? items : cap);
@@ -1285,12 +1276,7 @@ Error red_launch(RedDev& d, const RedChoice& c, cudaStream_t stream) {
     const void* k = pick_red_cstream<T>(d.mode, c.nb);
     if (!k) return make_error(TRS_ERR_ARG, "no column stream reduction kernel for this mode");
     const int smem = cs_smem_bytes(c.nb);
-    static std::mutex mu;
-    {
-      std::lock_guard<std::mutex> lock(mu);
-      if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-        return cuda_error(cudaGetLastError(), "cudaFuncSetAttribute");
-    }
+    allow_smem(k, smem);  // once per kernel
     const uint64_t items = (uint64_t)d.n_out_outer * (uint64_t)d.P * (uint64_t)d.cs_ncb;
     const uint64_t cap = (uint64_t)dev.sm_count * (uint64_t)c.per_sm;
     const unsigned grid = (unsigned)(items < cap ? items : cap);

@@ -566,12 +566,7 @@ template <class T, int MODE = kRowSoftmax>
 Error launch_softmax_stream(const SmDev& d, cudaStream_t stream) {
   auto k = softmax_stream_kernel<T, MODE>;
   const int smem = d.stages * (int)(d.C * (int64_t)sizeof(T));
-  static std::mutex mu;
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmStageBudget) != cudaSuccess)
-      return cuda_error(cudaGetLastError(), "cudaFuncSetAttribute");
-  }
+  allow_smem((const void*)k, kSmStageBudget);  // once per kernel
   const uint64_t sms = (uint64_t)current_device_info().sm_count;
   const unsigned grid = (unsigned)((uint64_t)d.rows < sms ? (uint64_t)d.rows : sms);
   k<<<grid, kSmThreads, smem, stream>>>(d);
@@ -597,11 +592,7 @@ Error launch_softmax_stream_typed(SmDev d, cudaStream_t stream) {
 template <class K>
 unsigned grid_of(K kernel, int threads, uint64_t work) {
   const DeviceInfo& dev = current_device_info();
-  int per_sm = 1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) != cudaSuccess || per_sm < 1) {
-    cudaGetLastError();
-    per_sm = 1;
-  }
+  const int per_sm = resident_blocks_smem((const void*)kernel, threads, 0);
   const uint64_t cap = (uint64_t)dev.sm_count * (uint64_t)per_sm;
   const uint64_t g = work < cap ? work : cap;
   return (unsigned)(g < 1 ? 1 : g);
