@@ -626,25 +626,26 @@ ew_tr_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc* partials) 
 // folded dimensions (i = 0, j = 1), with the mask TM of transposed inputs
 // fixed at compile time and every offset within 2^31 elements of its
 // operand's base: the tile's offsets are 32-bit, and each thread's chunk
-// coordinates inside a tile, with their shared-memory addresses, are
-// computed once.  Same data flow as ew_tr_kernel.
+// coordinates inside a tile are computed once.  Software-pipelined: the
+// copies of the CTA's next tile (into the second of two shared buffers) and
+// its register loads are issued before the current tile is combined.
 template <class T, int PROG, int TM>
-__global__ void __launch_bounds__(kThreads, PROG == kMulSigmoid ? 4 : 3)
+__global__ void __launch_bounds__(kThreads, 3)
 ew_tr2d_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc*) {
   constexpr int V = 16 / (int)sizeof(T);
   constexpr int TS = 256 / (int)sizeof(T);
   constexpr int CPR = TS / V;
   constexpr int VPT = TS * CPR / kThreads;
   constexpr int NIN = 2;
+  constexpr int NT = popc_c(TM);          // transposed inputs (shared tiles)
+  constexpr int kBuf = NT * TS * 256;     // bytes of one buffer
   extern __shared__ __align__(128) unsigned char tsm[];
   const int32_t Ni = (int32_t)d.shape[0], Nj = (int32_t)d.shape[1];
-  const T* in0 = static_cast<const T*>(d.in[0]) + d.off[1];
-  const T* in1 = static_cast<const T*>(d.in[1]) + d.off[2];
+  const T* ins[2] = {static_cast<const T*>(d.in[0]) + d.off[1], static_cast<const T*>(d.in[1]) + d.off[2]};
   T* out = static_cast<T*>(d.out) + d.off[0];
   const int32_t si[2] = {(int32_t)d.st[1][0], (int32_t)d.st[2][0]};
   const int32_t sj[2] = {(int32_t)d.st[1][1], (int32_t)d.st[2][1]};
   const int32_t so = (int32_t)d.st[0][0];
-  // this thread's chunks: tile row and 16-byte column chunk
   int row[VPT], ch[VPT];
 #pragma unroll
   for (int r = 0; r < VPT; ++r) {
@@ -653,38 +654,53 @@ ew_tr2d_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc*) {
     ch[r] = v % CPR;
   }
   const uint32_t n_tiles = (uint32_t)d.n_tiles;
-  for (uint32_t t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+  auto origin = [&](uint32_t t, int32_t* i0, int32_t* j0) {
     const uint32_t ti = fdiv(t, d.f_tj);
-    const int32_t j0 = (int32_t)(t - ti * d.f_tj.d) * TS, i0 = (int32_t)ti * TS;
+    *j0 = (int32_t)(t - ti * d.f_tj.d) * TS;
+    *i0 = (int32_t)ti * TS;
+  };
+  // the tile's transposed inputs -> buffer `buf`, its other inputs -> rv
+  auto fetch = [&](int32_t i0, int32_t j0, int buf, VecT<T, V> (&rv)[NIN][VPT]) {
     const bool full = i0 + TS <= Ni && j0 + TS <= Nj;
-    // transposed inputs: global -> shared (tile row = j offset), swizzled
 #pragma unroll
     for (int k = 0; k < NIN; ++k) {
-      if (!((TM >> k) & 1)) continue;
-      unsigned char* base = tsm + popc_c(TM & ((1 << k) - 1)) * (TS * 256);
-      const T* src = k == 0 ? in0 : in1;
+      if ((TM >> k) & 1) {
+        unsigned char* base = tsm + buf * kBuf + popc_c(TM & ((1 << k) - 1)) * (TS * 256);
 #pragma unroll
-      for (int r = 0; r < VPT; ++r) {
-        const int32_t jj = j0 + row[r], ii = i0 + ch[r] * V;
-        if (full || (jj < Nj && ii < Ni))
-          cp_async16(base + row[r] * 256 + ((ch[r] ^ ((row[r] / V) & 15)) * 16), src + ii + jj * sj[k]);
+        for (int r = 0; r < VPT; ++r) {
+          const int32_t jj = j0 + row[r], ii = i0 + ch[r] * V;
+          if (full || (jj < Nj && ii < Ni))
+            cp_async16(base + row[r] * 256 + ((ch[r] ^ ((row[r] / V) & 15)) * 16), ins[k] + ii + jj * sj[k]);
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < VPT; ++r) {
+          const int32_t ii = i0 + row[r], jj = j0 + ch[r] * V;
+          if (full || (ii < Ni && jj < Nj)) rv[k][r] = load_vec<T, V>(ins[k] + ii * si[k] + jj);
+        }
       }
+    }
+  };
+  VecT<T, V> rcur[NIN][VPT], rnxt[NIN][VPT];
+  uint32_t t = blockIdx.x;
+  int32_t i0 = 0, j0 = 0;
+  if (t < n_tiles) {
+    origin(t, &i0, &j0);
+    fetch(i0, j0, 0, rcur);
+  }
+  cp_async_commit();
+  int buf = 0;
+  for (; t < n_tiles; t += gridDim.x, buf ^= 1) {
+    const uint32_t tn = t + gridDim.x;
+    int32_t ni0 = 0, nj0 = 0;
+    if (tn < n_tiles) {
+      origin(tn, &ni0, &nj0);
+      fetch(ni0, nj0, buf ^ 1, rnxt);
     }
     cp_async_commit();
-    // the other inputs: registers, in the output's layout
-    VecT<T, V> rv[NIN][VPT];
-#pragma unroll
-    for (int k = 0; k < NIN; ++k) {
-      if ((TM >> k) & 1) continue;
-      const T* src = k == 0 ? in0 : in1;
-#pragma unroll
-      for (int r = 0; r < VPT; ++r) {
-        const int32_t ii = i0 + row[r], jj = j0 + ch[r] * V;
-        if (full || (ii < Ni && jj < Nj)) rv[k][r] = load_vec<T, V>(src + ii * si[k] + jj);
-      }
-    }
-    cp_async_wait_all();
+    cp_async_wait_prev();  // this tile's copies (the next tile's stay in flight)
     __syncthreads();
+    const bool full = i0 + TS <= Ni && j0 + TS <= Nj;
 #pragma unroll
     for (int r = 0; r < VPT; ++r) {
       const int32_t ii = i0 + row[r], jj = j0 + ch[r] * V;
@@ -696,11 +712,11 @@ ew_tr2d_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc*) {
 #pragma unroll
           for (int k = 0; k < NIN; ++k) {
             if ((TM >> k) & 1) {
-              a[k] = *reinterpret_cast<const T*>(tsm + popc_c(TM & ((1 << k) - 1)) * (TS * 256) +
+              a[k] = *reinterpret_cast<const T*>(tsm + buf * kBuf + popc_c(TM & ((1 << k) - 1)) * (TS * 256) +
                                                  (ch[r] * V + q) * 256 + (((row[r] / V) ^ (ch[r] & 15)) * 16) +
                                                  (row[r] % V) * (int)sizeof(T));
             } else {
-              a[k] = rv[k][r].v[q];
+              a[k] = rcur[k][r].v[q];
             }
           }
           res.v[q] = apply_prog<T, PROG>(p, a[0], a[1], T(0));
@@ -708,8 +724,15 @@ ew_tr2d_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc*) {
         store_vec_stream<T, V>(out + ii * so + jj, res);
       }
     }
-    __syncthreads();
+    __syncthreads();  // the next iteration's copies go into this buffer
+#pragma unroll
+    for (int k = 0; k < NIN; ++k)
+#pragma unroll
+      for (int r = 0; r < VPT; ++r) rcur[k][r] = rnxt[k][r];
+    i0 = ni0;
+    j0 = nj0;
   }
+  cp_async_wait_all();
 }
 
 // ew_flat1_kernel: a one-input map with a transcendental program (sigmoid,
@@ -1181,7 +1204,7 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
         for (int q = 0; q < d.n_batch; ++q)
           d.f_dim[d.batch_dim[q]] = make_fastdiv((uint32_t)f.shape[d.batch_dim[q]]);
       }
-      tr_smem = nt * TS * 256;
+      tr_smem = (two_d ? 2 : 1) * nt * TS * 256;  // the 2-D kernel double-buffers its tiles
       ewk::allow_smem(tk, tr_smem);
       grid_for(tk, ewk::resident_blocks_smem(tk, kThreads, tr_smem), d.n_tiles);
       variant = kEwTr;
