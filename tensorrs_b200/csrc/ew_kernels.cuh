@@ -738,9 +738,10 @@ ew_tr2d_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc*) {
 // ew_flat1_kernel: a one-input map with a transcendental program (sigmoid,
 // tanh) over a contiguous 1-D range of fewer than 2^31 16-byte chunks: the
 // vector kernel's data flow (four chunks per thread loaded, then mapped)
-// with plain chunk indices instead of the strided row decode.
+// with plain chunk indices instead of the strided row decode; held to 40
+// registers so six CTAs fit on an SM (more warps to cover the loads).
 template <class T, int PROG>
-__global__ void __launch_bounds__(kThreads, 4)
+__global__ void __launch_bounds__(kThreads, 6)
 ew_flat1_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc*) {
   constexpr int V = 16 / (int)sizeof(T);
   constexpr int U = 4;
