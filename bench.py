@@ -18,8 +18,11 @@ once at its stored size, every output written once) / time, whole job.
 and c and the device->host read of the sum inside the timed region.  Inputs
 (8 GiB per operand) exceed the 126 MB L2, so no flush is needed.
 
+At N = 1 the line also carries `suite`: every other kernel of the path timed
+on its own configuration (see run_suite_entries).
+
 --impl reference times the reference's own CPU algorithm (its restatement in
-oracle/, with all host threads) on a bounded row sample of the same workload.
+oracle/, with all host threads) on one dim-0 shard of the same workload.
 """
 from __future__ import annotations
 
@@ -58,6 +61,10 @@ def parse_args():
                     help="time every kernel of the path on its configuration (one JSON line each)")
     ap.add_argument("--only", default=None,
                     help="with --suite: only the entries whose 'config: kernel' name contains this text")
+    ap.add_argument("--no-steady", action="store_true",
+                    help="with --suite: one flushed launch per kernel only (for profiler captures)")
+    ap.add_argument("--no-suite", action="store_true",
+                    help="leave the per-kernel suite out of the headline line")
     return ap.parse_args()
 
 
@@ -80,10 +87,14 @@ def workload_bytes(rows: int, cols: int, ranks: int) -> int:
 def cpu_reference_sample(seconds: float, threads: int) -> dict:
     """Times `&(&a & &b) + &c` then `.sum()` exactly as the reference runs them
     (binary_op fast path for a & b, broadcast path with storage_indices for
-    + c, packed_data + serial fold for sum) on a row sample of the workload."""
+    + c, packed_data + serial fold for sum) on one dim-0 shard of the
+    workload, [8192, 32768]: 1/8 of the rows, which the full configuration's
+    index vectors (about 72 GiB) need not fit in host memory.  At least two
+    passes, and as many as fit in `seconds`; the full workload's time is 8x a
+    pass, its GB/s the same."""
     import oracle
     oracle.set_threads(threads)
-    rows = 512
+    rows = ROWS // 8
     a = oracle.fill_uniform(np.float32, rows * COLS, SEED_A)
     b = oracle.fill_uniform(np.float32, rows * COLS, SEED_B)
     c = oracle.fill_uniform(np.float32, COLS, SEED_C)
@@ -96,7 +107,9 @@ def cpu_reference_sample(seconds: float, threads: int) -> dict:
         t0 = time.perf_counter()
         t = oracle.binary("mul", av, bv)
         y = oracle.binary("add", oracle.HostView(t.reshape(-1), [rows, COLS]), cv)
+        del t
         oracle.sum_all(oracle.HostView(y.reshape(-1), [rows, COLS]))
+        del y
         times.append(time.perf_counter() - t0)
         if time.perf_counter() > t_end and len(times) >= 2:
             break
@@ -105,9 +118,10 @@ def cpu_reference_sample(seconds: float, threads: int) -> dict:
     return {
         "value": round(nbytes / sec / 1e9, 3), "unit": "GB/s", "cores": threads,
         "kind": "port",
-        "sample": f"{rows} of {ROWS} rows ([{rows},{COLS}] f32), {len(times)} timed passes, median "
-                  f"{sec * 1e3:.1f} ms/pass; C++ restatement of binary_op/storage_indices/sum "
-                  f"(oracle/oracle.cpp) on {threads} OpenMP threads",
+        "sample": f"one dim-0 shard, {rows} of {ROWS} rows ([{rows},{COLS}] f32, 1/8 of the workload), "
+                  f"{len(times)} timed passes, median {sec * 1e3:.0f} ms/pass (the full workload: 8x that); "
+                  f"C++ restatement of binary_op/storage_indices/sum (oracle/oracle.cpp) on {threads} "
+                  f"OpenMP threads",
         "ms_per_pass": round(sec * 1e3, 3),
     }
 
@@ -124,7 +138,7 @@ def run_reference(args) -> None:
         "ms_per_step": base["ms_per_pass"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (seeded splitmix64 uniforms)",
         "config": {"workload": "fma_sum: Y = A & B + c, sum(Y); A,B f32 [65536,32768], c [32768]; seed 4",
-                   "timed": "row sample on host cores"},
+                   "timed": "one [8192,32768] dim-0 shard per pass on the host cores"},
         "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -344,6 +358,12 @@ def run_trs(args) -> None:
                        "PCIe-bound"}
         del hA, hB
 
+    suite = None
+    if rank == 0 and world == 1 and not args.no_suite:
+        del A, B, Y
+        torch.cuda.empty_cache()
+        suite, _, _ = run_suite_entries(args)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_reference_sample(args.cpu_seconds, os.cpu_count() or 1)
@@ -372,6 +392,12 @@ def run_trs(args) -> None:
             "e2e": e2e,
             "cpu_baseline": cpu,
             "sum": s_val,
+            "suite": suite,
+            "suite_about": "every other kernel of the path on its configuration (configs 1-4 and the callers), "
+                           "one GPU: us_flushed = one launch after an L2 flush; us_steady = back-to-back "
+                           "launches over rotating buffer sets >= 4x L2, so each pays its outputs' write-back; "
+                           "frac = steady algorithmic GB/s / peak; dram_ratio = ncu DRAM bytes / algorithmic "
+                           "bytes of one cold launch (profiles/traffic.json)" if suite else None,
         }
         print(json.dumps(line), flush=True)
 
@@ -382,215 +408,329 @@ def run_trs(args) -> None:
 
 
 # ---------------------------------------------------------------------------
-# --suite: every kernel of the path on its configuration, one JSON line each
+# the kernel suite: every kernel of the path on the configuration it serves
 # ---------------------------------------------------------------------------
-def run_suite(args) -> None:
-    """Times each hot-path kernel on the configuration it serves (SURVEY
-    configs 1-5), with CUDA events around each launch, and reports achieved
-    GB/s of algorithmic bytes against the measured HBM peak.
+L2_BYTES = 126 * 1024 * 1024
+ROTATE_BYTES = 4 * L2_BYTES  # the buffer sets one steady-state run cycles through
 
-    Before every rep a 256 MiB buffer is written and then read: the write
-    evicts the inputs from L2 (so the L2-resident config 1 starts cold), the
-    read makes the flush's dirty lines drain to HBM before the timed launch
-    instead of inside it.  `--only TEXT` keeps the entries whose
-    "config: kernel" name contains TEXT (for profiler captures), `--warmup`
-    sets the untimed reps before the timed ones."""
+
+class SuiteGroup:
+    """Kernels that share one set of input and output buffers.  `make()`
+    allocates and fills one set (a dict of tensors); each entry is
+    (name, algorithmic bytes, launch(set))."""
+
+    def __init__(self, cfg, make, entries):
+        self.cfg, self.make, self.entries = cfg, make, entries
+
+
+def suite_groups(lib, abi, device, torch):
+    """The hot-path kernels on their benchmark configurations (inputs drawn
+    from the same seeded streams the parity tests use)."""
+    f32 = torch.float32
+    sh = torch.cuda.current_stream().cuda_stream
+    V = device.view_of
+
+    def t(*shape, dtype=f32):
+        return torch.empty(shape, dtype=dtype, device="cuda")
+
+    def C(st):
+        abi.check(st)
+
+    def ref(x):
+        return ctypes.byref(x)
+
+    groups = []
+
+    # config 1: A[1024,1024] + b[1024]; sum_axis(1); sum()
+    def make1():
+        A = device.fill_uniform(t(1024, 1024), 0)
+        b = device.fill_uniform(t(1024), 0, first=1 << 20)
+        s = {"A": A, "b": b, "Y": t(1024, 1024), "r": t(1024), "s": t(1)}
+        s["v"] = {k: V(x) for k, x in s.items() if isinstance(x, torch.Tensor)}
+        s["ins"] = abi.views_array([s["v"]["A"], s["v"]["b"]])
+        s["p"] = abi.program(2, abi.ADD)
+        return s
+    groups.append(SuiteGroup("config1", make1, [
+        ("bias add A[1024,1024] + b[1024]", 8392704,
+         lambda s: C(lib.trs_elementwise(ref(s["p"]), s["ins"], ref(s["v"]["Y"]), sh))),
+        ("sum_axis(1) of A[1024,1024]", 4194304 + 4096,
+         lambda s: C(lib.trs_sum_axis(ref(s["v"]["A"]), 1, 0, ref(s["v"]["r"]), sh))),
+        ("sum() of A[1024,1024]", 4194304 + 4,
+         lambda s: C(lib.trs_sum(ref(s["v"]["A"]), ref(s["v"]["s"]), sh))),
+    ]))
+
+    # config 2: C = A & B^T (B^T a strided view), sigmoid
+    n = 4096
+    nb = n * n * 4
+
+    def make2():
+        A = device.fill_normal(t(n, n), 1)
+        B = device.fill_normal(t(n, n), 1, first=n * n)
+        s = {"A": A, "B": B, "Y": t(n, n)}
+        s["va"], s["vy"] = V(A), V(s["Y"])
+        s["ins"] = abi.views_array([s["va"], V(B, [n, n], [1, n], 0)])
+        s["pm"] = abi.program(2, abi.MUL)
+        s["pms"] = abi.program(2, abi.MUL, epilogue="sigmoid")
+        s["par"] = (abi.Scalar * 2)()
+        return s
+    groups.append(SuiteGroup("config2", make2, [
+        ("A & B^T (B^T strided view)", 3 * nb,
+         lambda s: C(lib.trs_elementwise(ref(s["pm"]), s["ins"], ref(s["vy"]), sh))),
+        ("sigmoid(A & B^T) fused", 3 * nb,
+         lambda s: C(lib.trs_elementwise(ref(s["pms"]), s["ins"], ref(s["vy"]), sh))),
+        ("sigmoid standalone [4096,4096]", 2 * nb,
+         lambda s: C(lib.trs_unary(abi.UNOPS["sigmoid"], ref(s["va"]), s["par"], ref(s["vy"]), sh))),
+    ]))
+
+    # config 3: X[8192,16384] axis reductions and softmax
+    R, Cc = 8192, 16384
+    xb = R * Cc * 4
+
+    def make3():
+        X = device.fill_normal(t(R, Cc), 2)
+        s = {"X": X, "r1": t(R), "r0": t(Cc), "i1": t(R, dtype=torch.int64), "i0": t(Cc, dtype=torch.int64),
+             "Y": t(R, Cc)}
+        s["v"] = {k: V(x) for k, x in s.items()}
+        return s
+    e3 = []
+    for axis, nout, of, oi in [(1, R, "r1", "i1"), (0, Cc, "r0", "i0")]:
+        e3 += [
+            (f"sum_axis({axis}) of X[8192,16384]", xb + 4 * nout,
+             lambda s, a=axis, o=of: C(lib.trs_sum_axis(ref(s["v"]["X"]), a, 0, ref(s["v"][o]), sh))),
+            (f"mean over axis {axis}", xb + 4 * nout,
+             lambda s, a=axis, o=of: C(lib.trs_mean_axis(ref(s["v"]["X"]), a, 0, ref(s["v"][o]), sh))),
+            (f"max_axis({axis})", xb + 4 * nout,
+             lambda s, a=axis, o=of: C(lib.trs_max_axis(ref(s["v"]["X"]), a, ref(s["v"][o]), sh))),
+            (f"argmax_axis({axis})", xb + 8 * nout,
+             lambda s, a=axis, o=oi: C(lib.trs_argmax_axis(ref(s["v"]["X"]), a, ref(s["v"][o]), sh))),
+        ]
+    e3.append(("softmax over axis 1", 2 * xb,
+               lambda s: C(lib.trs_softmax_lastdim(ref(s["v"]["X"]), ref(s["v"]["Y"]), sh))))
+    groups.append(SuiteGroup("config3", make3, e3))
+
+    # config 4: relu(X & s + b) forward; scale/bias gradients backward
+    N, Ch, H, W = 64, 256, 56, 56
+    x4 = N * Ch * H * W * 4
+
+    def make4():
+        X = device.fill_normal(t(N, Ch, H, W), 3)
+        G = device.fill_normal(t(N, Ch, H, W), 3, first=N * Ch * H * W)
+        sc = device.fill_uniform(t(1, Ch, 1, 1), 3, 0.5, 1.5)
+        bi = device.fill_uniform(t(1, Ch, 1, 1), 3, -0.1, 0.1, first=Ch)
+        s = {"X": X, "G": G, "sc": sc, "bi": bi, "Y": t(N, Ch, H, W), "gs": t(1, Ch, 1, 1), "gb": t(1, Ch, 1, 1)}
+        s["v"] = {k: V(x) for k, x in s.items()}
+        s["ins"] = abi.views_array([s["v"]["X"], s["v"]["sc"], s["v"]["bi"]])
+        s["pf"] = abi.program(3, abi.MUL, abi.ADD, "relu")
+        s["tgt"] = (ctypes.c_int64 * 4)(1, Ch, 1, 1)
+        return s
+    groups.append(SuiteGroup("config4", make4, [
+        ("relu(X & s + b) fused forward", 2 * x4 + 2 * 4 * Ch,
+         lambda s: C(lib.trs_elementwise(ref(s["pf"]), s["ins"], ref(s["v"]["Y"]), sh))),
+        ("scale+bias grads of relu(X & s + b), fused", 2 * x4 + 4 * 4 * Ch,
+         lambda s: C(lib.trs_affine_relu_backward(ref(s["v"]["G"]), ref(s["v"]["X"]), ref(s["v"]["sc"]),
+                                                  ref(s["v"]["bi"]), ref(s["v"]["gs"]), ref(s["v"]["gb"]), sh))),
+        ("reduce_broadcast_grad g -> [1,256,1,1]", x4 + 4 * Ch,
+         lambda s: C(lib.trs_reduce_broadcast_grad(ref(s["v"]["G"]), s["tgt"], 4, ref(s["v"]["gb"]), sh))),
+    ]))
+
+    # callers of the path: pooling over config 4's activation
+    o2, o3 = N * Ch * 28 * 28 * 4, N * Ch * 27 * 27 * 4
+
+    def make_pool():
+        X = device.fill_normal(t(N, Ch, H, W), 3)
+        s = {"X": X, "P2": t(N, Ch, 28, 28), "P3": t(N, Ch, 27, 27), "GX": t(N, Ch, H, W),
+             "G2": device.fill_normal(t(N, Ch, 28, 28), 11)}
+        s["v"] = {k: V(x) for k, x in s.items()}
+        return s
+    groups.append(SuiteGroup("callers", make_pool, [
+        ("max_pool2d 2x2 over X[64,256,56,56]", x4 + o2,
+         lambda s: C(lib.trs_max_pool2d(ref(s["v"]["X"]), 2, 2, 2, 2, ref(s["v"]["P2"]), sh))),
+        ("avg_pool2d 2x2 over X[64,256,56,56]", x4 + o2,
+         lambda s: C(lib.trs_avg_pool2d(ref(s["v"]["X"]), 2, 2, 2, 2, ref(s["v"]["P2"]), sh))),
+        ("max_pool2d 3x3 stride 2 over X[64,256,56,56]", x4 + o3,
+         lambda s: C(lib.trs_max_pool2d(ref(s["v"]["X"]), 3, 3, 2, 2, ref(s["v"]["P3"]), sh))),
+        ("max_pool2d 2x2 backward to X[64,256,56,56]", 2 * x4 + o2,
+         lambda s: C(lib.trs_max_pool2d_backward(ref(s["v"]["X"]), ref(s["v"]["G2"]), 2, 2, 2, 2, 0,
+                                                 ref(s["v"]["GX"]), sh))),
+    ]))
+
+    # callers of the path: LayerNorm over config 3's X; optimiser steps
+    def make_ln():
+        X = device.fill_normal(t(R, Cc), 2)
+        s = {"X": X, "Y": t(R, Cc), "g": device.fill_uniform(t(1, Cc), 7, 0.5, 1.5),
+             "b": device.fill_uniform(t(1, Cc), 8, -0.5, 0.5)}
+        s["v"] = {k: V(x) for k, x in s.items()}
+        return s
+    groups.append(SuiteGroup("callers", make_ln, [
+        ("layer_norm over X[8192,16384]", 2 * R * Cc * 4 + 2 * Cc * 4,
+         lambda s: C(lib.trs_layer_norm_lastdim(ref(s["v"]["X"]), ref(s["v"]["g"]), ref(s["v"]["b"]), 1e-5,
+                                                ref(s["v"]["Y"]), sh))),
+    ]))
+    npar = 1 << 26
+
+    def make_opt():
+        s = {"P": device.fill_normal(t(npar), 9), "G": device.fill_normal(t(npar), 10),
+             "M": torch.zeros(npar, dtype=f32, device="cuda"), "W": torch.zeros(npar, dtype=f32, device="cuda")}
+        s["v"] = {k: V(x) for k, x in s.items()}
+        s["step"] = [0]
+        return s
+
+    def adam(s):
+        s["step"][0] += 1
+        C(lib.trs_adam_step(ref(s["v"]["P"]), ref(s["v"]["G"]), ref(s["v"]["M"]), ref(s["v"]["W"]), 1e-3, 0.9,
+                            0.999, 1e-8, s["step"][0], sh))
+    groups.append(SuiteGroup("callers", make_opt, [
+        ("adam step, 2^26 f32 params", 7 * npar * 4, adam),
+        ("sgd step, 2^26 f32 params", 3 * npar * 4,
+         lambda s: C(lib.trs_sgd_step(ref(s["v"]["P"]), ref(s["v"]["G"]), 1e-3, sh))),
+    ]))
+    return groups
+
+
+def set_bytes(s) -> int:
+    import torch
+    return sum(x.numel() * x.element_size() for x in s.values() if isinstance(x, torch.Tensor))
+
+
+def suite_traffic() -> dict:
+    """DRAM bytes per launch of each suite kernel (read + write, one cold
+    launch under ncu), from profiles/traffic.json."""
+    p = ROOT / "profiles" / "traffic.json"
+    try:
+        return json.loads(p.read_text()).get("suite", {})
+    except (OSError, ValueError):
+        return {}
+
+
+def run_suite_entries(args, only=None, steady=True, flushed_reps=5, warm=2):
+    """Times every suite kernel two ways, with CUDA events on the launching
+    stream, and returns one record per kernel:
+      * flushed: one launch after a 256 MiB buffer was written and then read
+        (the write evicts the inputs from L2, the read drains the flush's
+        dirty lines to HBM before the timed launch rather than inside it) --
+        a cold start, launch latency included, but the output may still sit
+        in the 126 MB L2 when the kernel ends;
+      * steady: launches back to back over rotating copies of the inputs and
+        outputs totalling at least 4x L2 (504 MiB), timed as a whole and
+        divided by the launch count -- each launch pays for the write-back of
+        the outputs before it, so algorithmic bytes / this time is what HBM
+        sustains.
+    `frac` is steady algorithmic GB/s over the measured copy peak; `dram_ratio`
+    is the kernel's DRAM traffic under ncu over its algorithmic bytes."""
+    import torch
+
+    from tensorrs_b200 import abi, device
+
+    lib = abi.load()
+    peak, peak_kind = measured_peaks()
+    stream = torch.cuda.current_stream()
+    flush_buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    traffic = suite_traffic()
+    out = []
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    for g in suite_groups(lib, abi, device, torch):
+        names = [e for e in g.entries if only is None or only in f"{g.cfg}: {e[0]}"]
+        if not names:
+            continue
+        sets = [g.make()]
+        sb = set_bytes(sets[0])
+        if steady:
+            n_sets = min(64, max(2, -(-ROTATE_BYTES // max(sb, 1))))
+            sets += [g.make() for _ in range(n_sets - 1)]
+        torch.cuda.synchronize()
+        for name, nbytes, launch in names:
+            times = []
+            for i in range(flushed_reps + warm):
+                flush_buf.fill_(float(i))
+                flush_buf.sum()
+                e0, e1 = ev(), ev()
+                e0.record(stream)
+                launch(sets[0])
+                e1.record(stream)
+                e1.synchronize()
+                if i >= warm:
+                    times.append(e0.elapsed_time(e1))
+            ms_f = float(np.median(times))
+            rec = {"suite": g.cfg, "kernel": name, "bytes": int(nbytes), "us_flushed": round(ms_f * 1e3, 2),
+                   "frac_flushed": round(nbytes / (ms_f * 1e-3) / 1e9 / peak, 4)}
+            if steady:
+                k = len(sets)
+                n_launch = max(2 * k, 20)
+                for i in range(k):
+                    launch(sets[i])
+                e0, e1 = ev(), ev()
+                e0.record(stream)
+                for i in range(n_launch):
+                    launch(sets[i % k])
+                e1.record(stream)
+                e1.synchronize()
+                ms_s = e0.elapsed_time(e1) / n_launch
+                gbps = nbytes / (ms_s * 1e-3) / 1e9
+                rec.update({"us_steady": round(ms_s * 1e3, 2), "GBps": round(gbps, 1), "frac": round(gbps / peak, 4),
+                            "rotation": f"{k} buffer sets x {sb / 2**20:.0f} MiB"})
+            tr = traffic.get(name)
+            rec["dram_ratio"] = round(tr / nbytes, 3) if tr else None
+            out.append(rec)
+        del sets
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    return out, peak, peak_kind
+
+
+def run_suite(args) -> None:
+    """--suite: one JSON line per kernel of the path (run_suite_entries), plus
+    the headline configuration's fused step and its sum alone."""
     import torch
 
     from tensorrs_b200 import abi, device
 
     torch.cuda.set_device(0)
-    lib = abi.load()
-    peak, peak_kind = measured_peaks()
-    sh = torch.cuda.current_stream().cuda_stream
-    flush_buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
-    f32 = torch.float32
-    only = args.only
-    warm = max(0, args.warmup)
-
-    def want(cfg, name):
-        return only is None or only in f"{cfg}: {name}"
-
-    def t(*shape):
-        return torch.empty(shape, dtype=f32, device="cuda")
-
-    def timed(fn, reps):
-        times = []
-        for i in range(reps + warm):
-            flush_buf.fill_(float(i))
-            flush_buf.sum()
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record()
-            fn()
-            e1.record()
-            e1.synchronize()
-            if i >= warm:
-                times.append(e0.elapsed_time(e1))
-        return float(np.median(times))
-
-    def run(cfg, name, nbytes, fn):
-        if not want(cfg, name):
-            return
-        ms = timed(fn, reps)
-        gbps = nbytes / (ms * 1e-3) / 1e9
-        line = {"suite": cfg, "kernel": name, "bytes": int(nbytes), "ms": round(ms, 4), "GBps": round(gbps, 1),
-                "frac_of_peak": round(gbps / peak, 4), "peak": peak, "peak_source": peak_kind,
-                "l2": "256 MiB written then read before each rep"}
-        print(json.dumps(line), flush=True)
-
-    def any_of(cfg, names):
-        return any(want(cfg, n) for n in names)
-
-    def C(st):
-        abi.check(st)
-
-    V = device.view_of
-    reps = max(5, args.steps)
-    # config 1: A[1024,1024] + b[1024]; sum_axis(1); sum()
-    c1 = ["bias add A[1024,1024] + b[1024]", "sum_axis(1) of A[1024,1024]", "sum() of A[1024,1024]"]
-    if any_of("config1", c1):
-        A = device.fill_uniform(t(1024, 1024), 0)
-        b = device.fill_uniform(t(1024), 0, first=1 << 20)
-        Y = t(1024, 1024)
-        r = t(1024)
-        s = t(1)
-        va, vb, vy, vr, vs = V(A), V(b), V(Y), V(r), V(s)
-        p2 = abi.program(2, abi.ADD)
-        ins = abi.views_array([va, vb])
-        run("config1", c1[0], 8392704, lambda: C(lib.trs_elementwise(ctypes.byref(p2), ins, ctypes.byref(vy), sh)))
-        run("config1", c1[1], 4194304 + 4096, lambda: C(lib.trs_sum_axis(ctypes.byref(va), 1, 0, ctypes.byref(vr), sh)))
-        run("config1", c1[2], 4194304 + 4, lambda: C(lib.trs_sum(ctypes.byref(va), ctypes.byref(vs), sh)))
-        del A, b, Y
-    # config 2: C = A & B^T, sigmoid
-    c2 = ["A & B^T (B^T strided view)", "sigmoid(A & B^T) fused", "sigmoid standalone [4096,4096]"]
-    if any_of("config2", c2):
-        n = 4096
-        A = device.fill_normal(t(n, n), 1)
-        B = device.fill_normal(t(n, n), 1, first=n * n)
-        Y = t(n, n)
-        vbt = V(B, [n, n], [1, n], 0)
-        nb = n * n * 4
-        pm = abi.program(2, abi.MUL)
-        pms = abi.program(2, abi.MUL, epilogue="sigmoid")
-        ins = abi.views_array([V(A), vbt])
-        vy = V(Y)
-        run("config2", c2[0], 3 * nb, lambda: C(lib.trs_elementwise(ctypes.byref(pm), ins, ctypes.byref(vy), sh)))
-        run("config2", c2[1], 3 * nb, lambda: C(lib.trs_elementwise(ctypes.byref(pms), ins, ctypes.byref(vy), sh)))
-        params = (abi.Scalar * 2)()
-        va = V(A)
-        run("config2", c2[2], 2 * nb,
-            lambda: C(lib.trs_unary(abi.UNOPS["sigmoid"], ctypes.byref(va), params, ctypes.byref(vy), sh)))
-        del A, B, Y
-    # config 3: X[8192,16384] axis reductions and softmax
-    R, Cc = 8192, 16384
-    c3 = [k for axis in (1, 0) for k in (f"sum_axis({axis}) of X[8192,16384]", f"mean over axis {axis}",
-                                         f"max_axis({axis})", f"argmax_axis({axis})")] + ["softmax over axis 1"]
-    if any_of("config3", c3):
-        X = device.fill_normal(t(R, Cc), 2)
-        vx = V(X)
-        xb = R * Cc * 4
-        r1, r0 = t(R), t(Cc)
-        i1, i0 = torch.empty(R, dtype=torch.int64, device="cuda"), torch.empty(Cc, dtype=torch.int64, device="cuda")
-        for axis, out_f, out_i, nout in [(1, r1, i1, R), (0, r0, i0, Cc)]:
-            vo, vi = V(out_f), V(out_i)
-            run("config3", f"sum_axis({axis}) of X[8192,16384]", xb + 4 * nout,
-                lambda: C(lib.trs_sum_axis(ctypes.byref(vx), axis, 0, ctypes.byref(vo), sh)))
-            run("config3", f"mean over axis {axis}", xb + 4 * nout,
-                lambda: C(lib.trs_mean_axis(ctypes.byref(vx), axis, 0, ctypes.byref(vo), sh)))
-            run("config3", f"max_axis({axis})", xb + 4 * nout,
-                lambda: C(lib.trs_max_axis(ctypes.byref(vx), axis, ctypes.byref(vo), sh)))
-            run("config3", f"argmax_axis({axis})", xb + 8 * nout,
-                lambda: C(lib.trs_argmax_axis(ctypes.byref(vx), axis, ctypes.byref(vi), sh)))
-        Ys = t(R, Cc)
-        vys = V(Ys)
-        run("config3", "softmax over axis 1", 2 * xb,
-            lambda: C(lib.trs_softmax_lastdim(ctypes.byref(vx), ctypes.byref(vys), sh)))
-        del X, Ys
-    # config 4: relu(X & s + b) forward; scale/bias gradients backward
-    c4 = ["relu(X & s + b) fused forward", "scale+bias grads of relu(X & s + b), fused",
-          "reduce_broadcast_grad g -> [1,256,1,1]"]
-    if any_of("config4", c4):
-        N, Ch, H, W = 64, 256, 56, 56
-        X = device.fill_normal(t(N, Ch, H, W), 3)
-        G = device.fill_normal(t(N, Ch, H, W), 3, first=N * Ch * H * W)
-        sc = device.fill_uniform(t(1, Ch, 1, 1), 3, 0.5, 1.5)
-        bi = device.fill_uniform(t(1, Ch, 1, 1), 3, -0.1, 0.1, first=Ch)
-        Y = t(N, Ch, H, W)
-        gs, gb = t(1, Ch, 1, 1), t(1, Ch, 1, 1)
-        xb = N * Ch * H * W * 4
-        pf = abi.program(3, abi.MUL, abi.ADD, "relu")
-        ins = abi.views_array([V(X), V(sc), V(bi)])
-        vX, vG, vsc, vbi, vY, vgs, vgb = V(X), V(G), V(sc), V(bi), V(Y), V(gs), V(gb)
-        run("config4", c4[0], 2 * xb + 2 * 4 * Ch,
-            lambda: C(lib.trs_elementwise(ctypes.byref(pf), ins, ctypes.byref(vY), sh)))
-        run("config4", c4[1], 2 * xb + 4 * 4 * Ch,
-            lambda: C(lib.trs_affine_relu_backward(ctypes.byref(vG), ctypes.byref(vX), ctypes.byref(vsc),
-                                                   ctypes.byref(vbi), ctypes.byref(vgs), ctypes.byref(vgb), sh)))
-        tgt = (ctypes.c_int64 * 4)(1, Ch, 1, 1)
-        run("config4", c4[2], xb + 4 * Ch,
-            lambda: C(lib.trs_reduce_broadcast_grad(ctypes.byref(vG), tgt, 4, ctypes.byref(vgb), sh)))
-        del X, G, Y
-    # callers of the path: the pooling layers over config 4's activation
-    cp = ["max_pool2d 2x2 over X[64,256,56,56]", "avg_pool2d 2x2 over X[64,256,56,56]",
-          "max_pool2d 3x3 stride 2 over X[64,256,56,56]", "max_pool2d 2x2 backward to X[64,256,56,56]"]
-    if any_of("callers", cp):
-        N, Ch, H, W = 64, 256, 56, 56
-        X = device.fill_normal(t(N, Ch, H, W), 3)
-        P2, P3, GX = t(N, Ch, 28, 28), t(N, Ch, 27, 27), t(N, Ch, H, W)
-        G2 = device.fill_normal(t(N, Ch, 28, 28), 11)
-        xb, ob2, ob3 = N * Ch * H * W * 4, N * Ch * 28 * 28 * 4, N * Ch * 27 * 27 * 4
-        vX, vP2, vP3, vG2, vGX = V(X), V(P2), V(P3), V(G2), V(GX)
-        run("callers", cp[0], xb + ob2, lambda: C(lib.trs_max_pool2d(ctypes.byref(vX), 2, 2, 2, 2, ctypes.byref(vP2), sh)))
-        run("callers", cp[1], xb + ob2, lambda: C(lib.trs_avg_pool2d(ctypes.byref(vX), 2, 2, 2, 2, ctypes.byref(vP2), sh)))
-        run("callers", cp[2], xb + ob3, lambda: C(lib.trs_max_pool2d(ctypes.byref(vX), 3, 3, 2, 2, ctypes.byref(vP3), sh)))
-        run("callers", cp[3], 2 * xb + ob2,
-            lambda: C(lib.trs_max_pool2d_backward(ctypes.byref(vX), ctypes.byref(vG2), 2, 2, 2, 2, 0,
-                                                  ctypes.byref(vGX), sh)))
-        del X, P2, P3, GX, G2
-    # callers of the path: LayerNorm over config 3's X, one Adam step over 2^26 f32 parameters
-    cc = ["layer_norm over X[8192,16384]", "adam step, 2^26 f32 params", "sgd step, 2^26 f32 params"]
-    if any_of("callers", cc):
-        R, Cc = 8192, 16384
-        X = device.fill_normal(t(R, Cc), 2)
-        Yl = t(R, Cc)
-        gam = device.fill_uniform(t(1, Cc), 7, 0.5, 1.5)
-        bet = device.fill_uniform(t(1, Cc), 8, -0.5, 0.5)
-        vX, vY, vg, vb = V(X), V(Yl), V(gam), V(bet)
-        run("callers", cc[0], 2 * R * Cc * 4 + 2 * Cc * 4,
-            lambda: C(lib.trs_layer_norm_lastdim(ctypes.byref(vX), ctypes.byref(vg), ctypes.byref(vb), 1e-5,
-                                                 ctypes.byref(vY), sh)))
-        del X, Yl
-        n = 1 << 26
-        P = device.fill_normal(t(n), 9)
-        G = device.fill_normal(t(n), 10)
-        M = torch.zeros(n, dtype=f32, device="cuda")
-        W = torch.zeros(n, dtype=f32, device="cuda")
-        vP, vG, vM, vW = V(P), V(G), V(M), V(W)
-        step = [0]
-
-        def adam():
-            step[0] += 1
-            C(lib.trs_adam_step(ctypes.byref(vP), ctypes.byref(vG), ctypes.byref(vM), ctypes.byref(vW), 1e-3, 0.9,
-                                0.999, 1e-8, step[0], sh))
-        run("callers", cc[1], 7 * n * 4, adam)
-        run("callers", cc[2], 3 * n * 4, lambda: C(lib.trs_sgd_step(ctypes.byref(vP), ctypes.byref(vG), 1e-3, sh)))
-        del P, G, M, W
-    # config 5 (one GPU): the headline step
+    recs, peak, peak_kind = run_suite_entries(
+        args, only=args.only, steady=not args.no_steady,
+        flushed_reps=max(1, args.steps) if args.no_steady else max(5, args.steps), warm=max(0, args.warmup))
+    for r in recs:
+        r.update({"peak": peak, "peak_source": peak_kind})
+        print(json.dumps(r), flush=True)
+    # the headline configuration (24 GiB on the device): only in timing runs,
+    # never in a single-launch profiler pass
     c5 = ["Y = A & B + c and sum(Y) fused", "sum(Y) alone [65536,32768]"]
-    if any_of("config5", c5):
-        rows = args.rows
-        A = device.fill_uniform(t(rows, COLS), SEED_A)
-        B = device.fill_uniform(t(rows, COLS), SEED_B)
-        c = device.fill_uniform(t(COLS), SEED_C)
-        Y = t(rows, COLS)
-        s = t(1)
-        p3 = abi.program(3, abi.MUL, abi.ADD)
-        ins = abi.views_array([V(A), V(B), V(c)])
-        vY, vs = V(Y), V(s)
-        run("config5", c5[0], workload_bytes(rows, COLS, 1),
-            lambda: C(lib.trs_elementwise_sum(ctypes.byref(p3), ins, ctypes.byref(vY), ctypes.byref(vs), sh)))
-        run("config5", c5[1], rows * COLS * 4 + 4, lambda: C(lib.trs_sum(ctypes.byref(vY), ctypes.byref(vs), sh)))
+    if args.no_steady or (args.only is not None and not any(args.only in f"config5: {n}" for n in c5)):
+        return
+    lib = abi.load()
+    sh = torch.cuda.current_stream().cuda_stream
+    f32 = torch.float32
+    rows = args.rows
+    A = device.fill_uniform(torch.empty((rows, COLS), dtype=f32, device="cuda"), SEED_A)
+    B = device.fill_uniform(torch.empty((rows, COLS), dtype=f32, device="cuda"), SEED_B)
+    c = device.fill_uniform(torch.empty((COLS,), dtype=f32, device="cuda"), SEED_C)
+    Y = torch.empty((rows, COLS), dtype=f32, device="cuda")
+    s = torch.empty((1,), dtype=f32, device="cuda")
+    p3 = abi.program(3, abi.MUL, abi.ADD)
+    ins = abi.views_array([device.view_of(A), device.view_of(B), device.view_of(c)])
+    vY, vs = device.view_of(Y), device.view_of(s)
+    for name, nbytes, fn in [
+            (c5[0], workload_bytes(rows, COLS, 1),
+             lambda: abi.check(lib.trs_elementwise_sum(ctypes.byref(p3), ins, ctypes.byref(vY), ctypes.byref(vs), sh))),
+            (c5[1], rows * COLS * 4 + 4, lambda: abi.check(lib.trs_sum(ctypes.byref(vY), ctypes.byref(vs), sh)))]:
+        if args.only is not None and args.only not in f"config5: {name}":
+            continue
+        for _ in range(max(1, args.warmup)):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(5, args.steps)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        gbps = nbytes / (ms * 1e-3) / 1e9
+        print(json.dumps({"suite": "config5", "kernel": name, "bytes": int(nbytes), "us_steady": round(ms * 1e3, 1),
+                          "GBps": round(gbps, 1), "frac": round(gbps / peak, 4), "peak": peak,
+                          "peak_source": peak_kind, "l2": "inputs 8 GiB per operand >> L2"}), flush=True)
 
 
 def main():

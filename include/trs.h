@@ -160,6 +160,12 @@ const char* trs_status_string(int32_t status);
  * Used by benchmarks to report how many GPU launches a timed region made. */
 uint64_t trs_launch_count(void);
 
+/* Number of scratch allocations (per-block partials, flags, per-rank
+ * buffers) this library has made from its stream-ordered pool in this
+ * process (all devices).  Used by tests to show that a call allocated
+ * nothing. */
+uint64_t trs_scratch_alloc_count(void);
+
 /* Reads and clears the current device's async-error word.  A kernel that
  * waits on its own bulk copies gives up after a bounded number of polls,
  * sets this word and returns instead of hanging; *code receives the word
@@ -240,9 +246,12 @@ trs_status trs_sum(const trs_view* x, trs_view* out, trs_stream stream);
  * partials) that every GPU loading the library holds until the process exits.
  * A sum that would need more partials than that is rejected with TRS_ERR_ARG.
  * The first call on a device looks the array's address up (with that device
- * current); make that first call before any stream capture.  All calls share
- * the array and every call rewrites the partials it reads, but calls that
- * overlap on the GPU (on different streams) race on it. */
+ * current), which also loads the library's device code on that device if
+ * nothing has yet (CUDA loads modules lazily) and so commits the array's
+ * memory then: make that first call at start-up, before the host's arena
+ * reserves the device's memory and before any stream capture.  All calls
+ * share the array and every call rewrites the partials it reads, but calls
+ * that overlap on the GPU (on different streams) race on it. */
 trs_status trs_sum_noalloc(const trs_view* x, trs_view* out, trs_stream stream);
 
 /* sum_axis (base.rs:1051-1107) with keepdim = 0, sum_axis_keepdim

@@ -82,6 +82,9 @@ def load():
             "orc_fill_uniform": (c_int, [c_int, c_void_p, c_int64, c_uint64, c_double, c_double]),
             "orc_fill_uniform_at": (c_int, [c_int, c_void_p, c_int64, c_int64, c_uint64, c_double, c_double]),
             "orc_fill_normal": (c_int, [c_int, c_void_p, c_int64, c_uint64]),
+            "orc_fill_normal_at": (c_int, [c_int, c_void_p, c_int64, c_int64, c_uint64]),
+            "orc_fma_sum_stream": (c_int, [c_int64, c_int64, c_uint64, c_uint64, c_uint64, POINTER(c_double),
+                                           POINTER(c_double), POINTER(ctypes.c_float), c_void_p]),
             "orc_opt_step": (c_int, [c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_double,
                                      c_double, c_double, c_double, c_int64]),
             "orc_pool2d": (c_int, [c_int, V, c_int64, c_int64, c_int64, c_int64, c_void_p, I64P]),
@@ -301,7 +304,20 @@ def fill_uniform(dtype, n: int, seed: int, lo: float = -1.0, hi: float = 1.0, fi
     return out
 
 
-def fill_normal(dtype, n: int, seed: int) -> np.ndarray:
+def fill_normal(dtype, n: int, seed: int, first: int = 0) -> np.ndarray:
+    """Elements first .. first + n - 1 of the seeded N(0, 1) stream."""
     out = np.empty(n, dtype=dtype)
-    _check(load().orc_fill_normal(NP_TO_DT[np.dtype(dtype)], out.ctypes.data, n, seed))
+    _check(load().orc_fill_normal_at(NP_TO_DT[np.dtype(dtype)], out.ctypes.data, first, n, seed))
     return out
+
+
+def fma_sum_stream(rows: int, cols: int, seed_a: int, seed_b: int, seed_c: int, row_bits: bool = False):
+    """The sharded workload Y = A & B + c, sum(Y) (A, B [rows, cols], c [cols],
+    U(-1, 1) from the three seeds) checked by regenerating every element:
+    returns (reference's sequential f32 fold of Y, exact sum, sum of |y|,
+    per-row int64 sums of y's int32 bit patterns or None)."""
+    ex, sa, fold = c_double(), c_double(), ctypes.c_float()
+    bits = np.zeros(rows, dtype=np.int64) if row_bits else None
+    _check(load().orc_fma_sum_stream(rows, cols, seed_a, seed_b, seed_c, ctypes.byref(ex), ctypes.byref(sa),
+                                     ctypes.byref(fold), bits.ctypes.data if bits is not None else None))
+    return np.float32(fold.value), ex.value, sa.value, bits

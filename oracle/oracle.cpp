@@ -25,6 +25,7 @@
 #include <cstdint>
 #include <cstring>
 #include <limits>
+#include <thread>
 #include <type_traits>
 #include <vector>
 #include <omp.h>
@@ -987,18 +988,97 @@ int orc_fill_uniform_at(int dtype, void* out, int64_t first, int64_t n, uint64_t
 }
 
 // Normal: Box-Muller over uniforms 2i and 2i+1, u1 in (0, 1], in f64 with
-// glibc's log/cos/sqrt, rounded once.
-int orc_fill_normal(int dtype, void* out, int64_t n, uint64_t seed) {
+// glibc's log/cos/sqrt, rounded once.  orc_fill_normal_at writes elements
+// first .. first + n - 1 of the stream (a second tensor drawn from the same
+// seed continues where the first ended).
+int orc_fill_normal_at(int dtype, void* out, int64_t first, int64_t n, uint64_t seed) {
+  if (dtype != F32 && dtype != F64) return ERR_DTYPE;
   const double scale = 1.0 / 16777216.0;
   const double two_pi = 6.283185307179586;
 #pragma omp parallel for schedule(static)
   for (int64_t i = 0; i < n; ++i) {
-    double u1 = (double)((splitmix64(seed, 2 * (uint64_t)i) >> 40) + 1) * scale;
-    double u2 = (double)(splitmix64(seed, 2 * (uint64_t)i + 1) >> 40) * scale;
+    const uint64_t k = (uint64_t)(first + i);
+    double u1 = (double)((splitmix64(seed, 2 * k) >> 40) + 1) * scale;
+    double u2 = (double)(splitmix64(seed, 2 * k + 1) >> 40) * scale;
     double z = std::sqrt(-2.0 * std::log(u1)) * std::cos(two_pi * u2);
     if (dtype == F32) ((float*)out)[i] = (float)z;
     else ((double*)out)[i] = z;
   }
+  return OK;
+}
+
+int orc_fill_normal(int dtype, void* out, int64_t n, uint64_t seed) {
+  return orc_fill_normal_at(dtype, out, 0, n, seed);
+}
+
+// The sharded workload Y = A & B + c, sum(Y) with A, B f32 [rows, cols] and c
+// f32 [cols] drawn as U(-1, 1) from seeds sa, sb, sc (element (i, j) of A is
+// element i * cols + j of its stream), checked without holding any of it:
+// every y is regenerated from the seeds.
+//  * ref_fold: the reference's `sum` (base.rs:1024-1030): packed data folded
+//    left to right in f32 from 0, each y = fl(fl(a * b) + c) as binary_op
+//    computes `&(&a & &b) + &c` (ops.rs:240-300);
+//  * exact / sum_abs: the sum and the sum of |y| in long double with Neumaier
+//    compensation (per row, then over rows in order);
+//  * row_bits (nullable, `rows` entries): per row, the sum of the int32 bit
+//    patterns of its y as int64 -- a checksum that any single differing
+//    element changes.
+// The fold runs on its own thread beside the parallel pass.
+int orc_fma_sum_stream(int64_t rows, int64_t cols, uint64_t sa, uint64_t sb, uint64_t sc, double* exact,
+                       double* sum_abs, float* ref_fold, int64_t* row_bits) {
+  if (rows < 0 || cols < 0) return ERR_ARG;
+  const double scale = 1.0 / 16777216.0;
+  auto uni = [scale](uint64_t seed, uint64_t i) -> float {
+    double u = (double)(splitmix64(seed, i) >> 40) * scale;
+    return (float)(-1.0 + 2.0 * u);
+  };
+  std::vector<float> c((size_t)cols);
+  for (int64_t j = 0; j < cols; ++j) c[(size_t)j] = uni(sc, (uint64_t)j);
+  auto y_at = [&](int64_t i, int64_t j) -> float {
+    const uint64_t k = (uint64_t)(i * cols + j);
+    volatile float t = uni(sa, k) * uni(sb, k);  // rounded to f32 before the add
+    return t + c[(size_t)j];
+  };
+  float fold = 0.0f;
+  std::thread folder([&]() {
+    float acc = 0.0f;
+    for (int64_t i = 0; i < rows; ++i)
+      for (int64_t j = 0; j < cols; ++j) acc = acc + y_at(i, j);
+    fold = acc;
+  });
+  std::vector<long double> rs((size_t)rows), rc((size_t)rows), ra((size_t)rows);
+#pragma omp parallel for schedule(dynamic, 16)
+  for (int64_t i = 0; i < rows; ++i) {
+    long double s = 0, cmp = 0, a = 0;
+    int64_t bits = 0;
+    for (int64_t j = 0; j < cols; ++j) {
+      const float y = y_at(i, j);
+      int32_t b;
+      std::memcpy(&b, &y, 4);
+      bits += b;
+      const long double v = (long double)y;
+      const long double u = s + v;
+      if (fabsl(s) >= fabsl(v)) cmp += (s - u) + v; else cmp += (v - u) + s;
+      s = u;
+      a += fabsl(v);
+    }
+    rs[(size_t)i] = s;
+    rc[(size_t)i] = cmp;
+    ra[(size_t)i] = a;
+    if (row_bits) row_bits[i] = bits;
+  }
+  long double s = 0, cmp = 0, a = 0;
+  for (int64_t i = 0; i < rows; ++i) {
+    const long double v = rs[(size_t)i] + rc[(size_t)i];
+    const long double u = s + v;
+    if (fabsl(s) >= fabsl(v)) cmp += (s - u) + v; else cmp += (v - u) + s;
+    s = u;
+    a += ra[(size_t)i];
+  }
+  folder.join();
+  *exact = (double)(s + cmp);
+  *sum_abs = (double)a;
+  *ref_fold = fold;
   return OK;
 }
 

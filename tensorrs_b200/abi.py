@@ -79,6 +79,7 @@ _SIGNATURES = {
     "trs_last_error": (c_size_t, [ctypes.c_char_p, c_size_t]),
     "trs_status_string": (ctypes.c_char_p, [c_int32]),
     "trs_launch_count": (c_uint64, []),
+    "trs_scratch_alloc_count": (c_uint64, []),
     "trs_async_error": (c_int32, [POINTER(c_int32)]),
     "trs_broadcast_shape": (c_int32, [POINTER(c_int64), c_int32, POINTER(c_int64), c_int32,
                                       POINTER(c_int64), POINTER(c_int32)]),

@@ -138,6 +138,8 @@ const char* trs_status_string(int32_t status) {
 
 uint64_t trs_launch_count(void) { return g_launch_count.load(); }
 
+uint64_t trs_scratch_alloc_count(void) { return g_scratch_alloc_count.load(); }
+
 trs_status trs_async_error(int32_t* code) {
   int* word = async_error_word();
   if (!word) return finish(make_error(TRS_ERR_CUDA, "the async-error word is not available"));

@@ -13,8 +13,12 @@
 // In host code `g_noalloc_scratch` only names a host-side stand-in for the
 // array, not a device address; its device address is looked up once per
 // device with cudaGetSymbolAddress (on the first call on that device, with
-// that device current) and passed to the kernels.  Every call shares the one
-// array, so calls that overlap on the GPU (on different streams) race on it.
+// that device current) and passed to the kernels.  CUDA loads a library's
+// device code lazily, so that first lookup may be what loads this module and
+// commits the array's memory: a host that reserves all device memory for its
+// own arena makes its first call at start-up, before the reservation (and
+// before any stream capture).  Every call shares the one array, so calls that
+// overlap on the GPU (on different streams) race on it.
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -42,6 +46,7 @@ void* noalloc_scratch(Error* err) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();  // leave no stale error for a later launch check
     *err = cuda_error(e != cudaSuccess ? e : cudaErrorInvalidDevice, "cudaGetDevice");
     return nullptr;
   }
@@ -50,6 +55,7 @@ void* noalloc_scratch(Error* err) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) {
+      cudaGetLastError();
       *err = cuda_error(e, "cudaGetSymbolAddress of the no-alloc scratch");
       return nullptr;
     }

@@ -6,6 +6,7 @@
 namespace trs {
 
 std::atomic<uint64_t> g_launch_count{0};
+std::atomic<uint64_t> g_scratch_alloc_count{0};
 
 namespace {
 thread_local std::string t_last_error;
@@ -86,6 +87,7 @@ Error Scratch::alloc(size_t bytes, cudaStream_t stream) {
                       std::string("scratch allocation of ") + std::to_string(bytes) +
                           " bytes: " + cudaGetErrorString(e));
   }
+  g_scratch_alloc_count.fetch_add(1, std::memory_order_relaxed);
   return Error{};
 }
 

@@ -20,6 +20,9 @@ const std::string& last_error();
 extern std::atomic<uint64_t> g_launch_count;
 inline void count_launch(uint64_t n = 1) { g_launch_count.fetch_add(n, std::memory_order_relaxed); }
 
+// Successful Scratch::alloc calls (trs_scratch_alloc_count).
+extern std::atomic<uint64_t> g_scratch_alloc_count;
+
 Error cuda_error(cudaError_t e, const char* what);
 
 // Checks the launch that was just issued.
