@@ -7,9 +7,10 @@
 //
 // Transcendentals: the reference calls glibc (expf, tanhf, powf, logf and the
 // f64 forms).  The exponentials of the f32 hot paths (expf in sigmoid,
-// powf(E, x) in ELU / SELU / softmax) are the f32 table-driven exponential of
-// exp_f32.h, at most one ulp from glibc; its rare inputs outside the normal
-// result range take exp2_scaled below (f64, rounded once).  tanh, ln and the
+// powf(E, x) in softmax) are the f32 table-driven exponential of exp_f32.h,
+// at most one ulp from glibc; its rare inputs outside the normal result range
+// take exp2_scaled below (f64, rounded once).  ELU and SELU, which subtract 1
+// from E^x, take exp2_scaled for every input (the correctly rounded E^x).  tanh, ln and the
 // general powf evaluate CUDA's f64 functions and round once to f32, within one
 // ulp of the correctly rounded result.  For f64 the kernels call CUDA's f64
 // functions.
@@ -95,6 +96,13 @@ template <> struct Arith<float> {
     return exp_tab(x, expf32::kBaseEf32, log2_e);
   }
   static __device__ __forceinline__ float pow_e(float x, double log2_e) { return pow_e_inline(x, log2_e); }
+  // E^x rounded once from the f64 evaluation: ELU and SELU subtract 1 from
+  // it, which turns a one-ulp difference near x = 0 into many ulps of the
+  // result, so there the value has to be the correctly rounded one (as
+  // glibc's powf gives it, to within its hard cases)
+  static __device__ __forceinline__ float pow_e_rounded_once(float x, double log2_e) {
+    return (float)exp2_scaled<false>(x, log2_e);
+  }
   static __device__ __forceinline__ float exp(float a) { return exp_tab(a, expf32::kBaseE, kLog2E); }
   // expf and powf(E, .) for a <= 0 or NaN (sigmoid's exp(-|x|), softmax's
   // E^(x - max)): the branch-free form
@@ -140,6 +148,7 @@ template <> struct Arith<double> {
   static __device__ __noinline__ double exp(double a) { return ::exp(a); }
   static __device__ __forceinline__ double exp_nonpos(double a) { return exp(a); }
   static __device__ __forceinline__ double pow_e_nonpos(double x, double e) { return pow_e(x, e); }
+  static __device__ __forceinline__ double pow_e_rounded_once(double x, double e) { return pow_e(x, e); }
   static __device__ __noinline__ double tanh(double a) { return ::tanh(a); }
   static __device__ __noinline__ double ln(double a) { return ::log(a); }
   static __device__ __forceinline__ double from(const trs_scalar& s) { return s.f; }
@@ -165,6 +174,7 @@ struct IntArith {
   static __device__ __forceinline__ I abs(I a) { return a < 0 ? neg(a) : a; }
   static __device__ __forceinline__ I pow(I, I) { return 0; }
   static __device__ __forceinline__ I pow_e(I, double) { return 0; }
+  static __device__ __forceinline__ I pow_e_rounded_once(I, double) { return 0; }
   static __device__ __forceinline__ I pow_e_inline(I, double) { return 0; }
   static __device__ __forceinline__ I exp(I) { return 0; }
   static __device__ __forceinline__ I exp_nonpos(I) { return 0; }
@@ -229,7 +239,7 @@ __device__ __forceinline__ T apply_unop(const EwParams& p, T v) {
     case TRS_UN_TANH: return A::tanh(v);
     case TRS_UN_ELU: {  // elu.rs:47-63
       T pos = A::mul(v, v > zero ? one : zero);
-      T ex = A::pow_e(v, p.e_const);
+      T ex = A::pow_e_rounded_once(v, p.e_const);
       T neg = A::mul(A::mul(A::sub(ex, one), A::from(p.p0)), v <= zero ? one : zero);
       return A::add(pos, neg);
     }
@@ -241,7 +251,7 @@ __device__ __forceinline__ T apply_unop(const EwParams& p, T v) {
     case TRS_UN_SELU: {  // selu.rs:52-70; p0 = alpha, p1 = lambda
       T lambda = A::from(p.p1), alpha = A::from(p.p0);
       T pos = A::mul(A::mul(v, lambda), v > zero ? one : zero);
-      T ex = A::pow_e(v, p.e_const);
+      T ex = A::pow_e_rounded_once(v, p.e_const);
       T scale = A::mul(lambda, alpha);
       T neg = A::mul(A::mul(A::sub(ex, one), scale), v <= zero ? one : zero);
       return A::add(pos, neg);

@@ -100,6 +100,30 @@ __device__ __forceinline__ void store_vec_stream(T* p, const VecT<T, V>& r) {
   }
 }
 
+// A compile-time program over one chunk of V elements of each input: the
+// sigmoid programs on f32 take the packed sigmoid two elements at a time
+// (bit-identical to the scalar form), every other program goes element by
+// element.
+template <class T, int PROG, int V>
+__device__ __forceinline__ VecT<T, V> apply_prog_vec(const EwParams& p, const VecT<T, V>& a,
+                                                     const VecT<T, V>& b) {
+  VecT<T, V> r;
+  if constexpr (std::is_same<T, float>::value && V % 2 == 0 && (PROG == kSigmoid || PROG == kMulSigmoid)) {
+#pragma unroll
+    for (int i = 0; i < V; i += 2) {
+      float2 x = make_float2(a.v[i], a.v[i + 1]);
+      if constexpr (PROG == kMulSigmoid) x = __fmul2_rn(x, make_float2(b.v[i], b.v[i + 1]));
+      const float2 s = expf32::sigmoid2(x);
+      r.v[i] = s.x;
+      r.v[i + 1] = s.y;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < V; ++i) r.v[i] = apply_prog<T, PROG>(p, a.v[i], b.v[i], T(0));
+  }
+  return r;
+}
+
 template <class T, int V>
 __device__ __forceinline__ void store_vec(T* p, const VecT<T, V>& r) {
   if constexpr (sizeof(T) * V == 16) {
@@ -705,23 +729,21 @@ ew_tr2d_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc*) {
     for (int r = 0; r < VPT; ++r) {
       const int32_t ii = i0 + row[r], jj = j0 + ch[r] * V;
       if (full || (ii < Ni && jj < Nj)) {
-        VecT<T, V> res;
+        VecT<T, V> a[2];
 #pragma unroll
         for (int q = 0; q < V; ++q) {
-          T a[2];
 #pragma unroll
           for (int k = 0; k < NIN; ++k) {
             if ((TM >> k) & 1) {
-              a[k] = *reinterpret_cast<const T*>(tsm + buf * kBuf + popc_c(TM & ((1 << k) - 1)) * (TS * 256) +
-                                                 (ch[r] * V + q) * 256 + (((row[r] / V) ^ (ch[r] & 15)) * 16) +
-                                                 (row[r] % V) * (int)sizeof(T));
+              a[k].v[q] = *reinterpret_cast<const T*>(tsm + buf * kBuf + popc_c(TM & ((1 << k) - 1)) * (TS * 256) +
+                                                      (ch[r] * V + q) * 256 + (((row[r] / V) ^ (ch[r] & 15)) * 16) +
+                                                      (row[r] % V) * (int)sizeof(T));
             } else {
-              a[k] = rcur[k][r].v[q];
+              a[k].v[q] = rcur[k][r].v[q];
             }
           }
-          res.v[q] = apply_prog<T, PROG>(p, a[0], a[1], T(0));
         }
-        store_vec_stream<T, V>(out + ii * so + jj, res);
+        store_vec_stream<T, V>(out + ii * so + jj, apply_prog_vec<T, PROG, V>(p, a[0], a[NIN - 1]));
       }
     }
     __syncthreads();  // the next iteration's copies go into this buffer
@@ -760,10 +782,7 @@ ew_flat1_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc*) {
     for (int u = 0; u < U; ++u) {
       const uint32_t g = base + (uint32_t)u * kThreads;
       if (g < n) {
-        VecT<T, V> r;
-#pragma unroll
-        for (int i = 0; i < V; ++i) r.v[i] = apply_prog<T, PROG>(p, v[u].v[i], T(0), T(0));
-        store_vec_stream<T, V>(out + (size_t)g * V, r);
+        store_vec_stream<T, V>(out + (size_t)g * V, apply_prog_vec<T, PROG, V>(p, v[u], v[u]));
       }
     }
   }

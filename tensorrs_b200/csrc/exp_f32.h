@@ -187,6 +187,55 @@ __device__ __forceinline__ float sigmoid(float x) {
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y0) : "f"(d));
   return sigmoid_div(x >= 0.0f ? 1.0f : e, d, y0);
 }
+
+// sigmoid of two values at once on sm_100's packed f32x2 add / multiply /
+// fused multiply-add (each lane rounded to nearest exactly as the scalar
+// instruction rounds, subnormals kept), so each pair costs one issue slot
+// where `sigmoid` above takes two.  The operations are those of `sigmoid` and
+// `exp_nonpos`, step for step, with every negated operand folded into an
+// exact product by -1 or a sign-symmetric rounding:
+//   shift - t        = fma(t, -1, shift)  (exact: both integers in [2^23, 2^24))
+//   -RN(1 + e)       = fma(e, -1, -1)
+//   RN(1 - d y0)     = fma(-d, y0, 1)
+//   RN(num - q0 d)   = fma(q0, -d, num)
+// so each lane's result is bit-identical to `sigmoid` of that lane.  The
+// clamp at -104 is max.NaN (a NaN passes through, as the scalar compare
+// lets it); the table loads, the exponent scaling, the reciprocal seed, the
+// reciprocal floor and the numerator choice stay per lane.
+__device__ __forceinline__ float2 sigmoid2(float2 x) {
+  float2 y;
+  asm("max.NaN.f32 %0, %1, 0fC2D00000;" : "=f"(y.x) : "f"(-fabsf(x.x)));  // max(-|x|, -104)
+  asm("max.NaN.f32 %0, %1, 0fC2D00000;" : "=f"(y.y) : "f"(-fabsf(x.y)));
+  const float2 mh = make_float2(kBaseE.mh, kBaseE.mh), ml = make_float2(kBaseE.ml, kBaseE.ml);
+  const float2 shift = make_float2(12582912.0f, 12582912.0f);  // 1.5 * 2^23
+  const float2 m1 = make_float2(-1.0f, -1.0f), one = make_float2(1.0f, 1.0f);
+  const float2 t = __ffma2_rn(y, mh, shift);
+  const uint32_t tbx = __float_as_uint(t.x), tby = __float_as_uint(t.y);
+  const float2 nkf = __ffma2_rn(t, m1, shift);  // -(t - shift)
+  const float2 z = __ffma2_rn(y, ml, __ffma2_rn(y, mh, nkf));
+  float2 u = __ffma2_rn(z, make_float2(kExpC4, kExpC4), make_float2(kExpC3, kExpC3));
+  u = __ffma2_rn(z, u, make_float2(kExpC2, kExpC2));
+  u = __ffma2_rn(z, u, make_float2(kExpC1, kExpC1));
+  const float2 p = __fmul2_rn(z, u);
+  const float2* tab = reinterpret_cast<const float2*>(&kExp2Tab16[0][0]);
+  const float2 tjx = __ldg(tab + (tbx & 15u)), tjy = __ldg(tab + (tby & 15u));
+  const float2 th = make_float2(tjx.x, tjy.x), tl = make_float2(tjx.y, tjy.y);
+  const float2 s = __fadd2_rn(th, __ffma2_rn(th, p, tl));
+  const float2 p2 = make_float2(__uint_as_float(((tbx << 19) & 0xFF800000u) + (191u << 23)),
+                                __uint_as_float(((tby << 19) & 0xFF800000u) + (191u << 23)));  // 2^(ex + 64)
+  const float2 e = __fmul2_rn(__fmul2_rn(s, p2), make_float2(0x1p-64f, 0x1p-64f));
+  const float2 d = __fadd2_rn(one, e);
+  const float2 nd = __ffma2_rn(e, m1, m1);  // -d
+  float2 y0;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y0.x) : "f"(d.x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y0.y) : "f"(d.y));
+  float2 y1 = __ffma2_rn(y0, __ffma2_rn(nd, y0, one), y0);
+  y1.x = fmaxf(y1.x, 0x1.000002p-1f);
+  y1.y = fmaxf(y1.y, 0x1.000002p-1f);
+  const float2 num = make_float2(x.x >= 0.0f ? 1.0f : e.x, x.y >= 0.0f ? 1.0f : e.y);
+  const float2 q0 = __fmul2_rn(num, y1);
+  return __ffma2_rn(__ffma2_rn(q0, nd, num), y1, q0);
+}
 #endif
 
 }  // namespace expf32

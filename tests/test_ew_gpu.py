@@ -284,28 +284,44 @@ def test_f32_exponentials_dense_sweep(op):
 
 @pytest.mark.parametrize("op,p0,p1", CANCEL_UNARY, ids=lambda v: str(v))
 @pytest.mark.parametrize("dtype", [np.float32, np.float64], ids=lambda d: np.dtype(d).name)
-def test_elu_selu_within_the_propagated_bound(op, p0, p1, dtype):
+def test_elu_selu(op, p0, p1, dtype):
+    """ELU / SELU compose (E^x - 1) * alpha (* lambda) under masks (elu.rs:43-64,
+    selu.rs:48-71).  The transcendental in them, E^x, is within one ulp of the
+    reference's: for f32 it is the f64 evaluation rounded once (correctly
+    rounded), and glibc's powf is within 0.82 ulp, so the two differ by at
+    most one ulp and agree for almost every input; for f64 it is CUDA's pow,
+    within 2 ulp of glibc's pow.  Subtracting 1 turns that ulp of E^x into
+    many ulps of a result near 0, the reference's own rounding included, so
+    the composed result is held to the bound this implies: K ulp of E^x times
+    alpha (times lambda), plus 2 ulp of the result (K = 1 for f32, F64_ULP for
+    f64).  f32 is checked over the specials and a dense sweep of the band
+    x in [-4, 0] where E^x - 1 cancels, and must be bit-identical for at
+    least 99.9 % of them."""
     import oracle
     from tensorrs_b200 import device
     x = special_f32(200003, 13).astype(dtype)
+    if dtype == np.float32:
+        band = np.linspace(-4.0, 0.0, 1 << 22, dtype=np.float32)
+        tiny = -np.logspace(-38, -1, 1 << 16).astype(np.float32)
+        x = np.concatenate([x, band, tiny])
     dx = contiguous(x)
     want = oracle.unary(op, dx.host_view(), p0, p1)
     got = to_host(device.unary(op, dx.view, empty(x.shape, dtype), p0, p1))
     ex = oracle.unary("exp", dx.host_view())  # E^x as the reference computes it
     scale = abs(p0) * (p1 if op == "selu" else 1.0)
-    k = 2 if dtype == np.float32 else F64_ULP
+    k = 1 if dtype == np.float32 else F64_ULP
     with np.errstate(invalid="ignore", over="ignore"):
-        bound = k * scale * np.spacing(np.abs(ex)).astype(np.float64) + k * np.spacing(np.abs(want)).astype(np.float64)
+        bound = k * scale * np.spacing(np.abs(ex)).astype(np.float64) + 2 * np.spacing(np.abs(want)).astype(np.float64)
         diff = np.abs(got.astype(np.float64) - want.astype(np.float64))
-    both_nan = np.isnan(got) & np.isnan(want)
-    same = got == want
-    ok = both_nan | same | (diff <= bound)
+    ok = (np.isnan(got) & np.isnan(want)) | (got == want) | (diff <= bound)
     assert ok.all(), f"{op}: {(~ok).sum()} outside the bound, e.g. x={x[~ok][:3]}"
+    same = float((ulp_diff(got, want) == 0).mean())
+    print(f"{op} {np.dtype(dtype).name}: {same:.5%} bit-identical, max {max_ulp(got, want)} ulp of the result")
+    if dtype == np.float32:
+        assert same >= 0.999
     # x > 0 takes the exact branch: the value itself (NaN once E^x overflows)
     pos = (x > 0) & np.isfinite(want)
     assert_bit_exact(got[pos], want[pos], op + " positive branch")
-    print(f"{op} {np.dtype(dtype).name}: max {max_ulp(got, want)} ulp of the result, "
-          f"{int((ulp_diff(got, want) == 0).sum())}/{x.size} bit-identical")
 
 
 def test_relu_keeps_negative_zero_and_nan():
@@ -443,3 +459,38 @@ def test_zero_dim_broadcast_fails_like_the_reference():
     with pytest.raises(abi.TrsError) as ge:
         gpu_binary("add", a, b, np.float32)
     assert oe.value.message == ge.value.message == "broadcast_to failed (bug)"
+
+
+def test_packed_sigmoid_equals_the_scalar_form():
+    """The contiguous 1-D map and the transposed-tile multiply take sigmoid two
+    elements at a time on packed f32x2 operations; a strided layout takes the
+    scalar form.  The two perform the same roundings, so they agree bit for bit."""
+    import oracle
+    from tensorrs_b200 import abi, device
+    x = np.concatenate([special_f32(100003, 21), np.linspace(-110.0, 95.0, 1 << 20).astype(np.float32)])
+    n = x.size
+    flat = contiguous(x)
+    packed = to_host(device.unary("sigmoid", flat.view, empty([n], np.float32)))
+    spread = np.zeros(2 * n, np.float32)
+    spread[::2] = x
+    strided = DevView(spread, [n], [2], 0)
+    scalar = to_host(device.unary("sigmoid", strided.view, empty([n], np.float32)))
+    assert_bit_exact(packed, scalar, "packed vs scalar sigmoid")
+    assert max_ulp(packed, oracle.unary("sigmoid", flat.host_view())) <= 2
+    # sigmoid(A & B^T): the 2-D tile kernel (packed) against a gapped B^T view
+    # (scalar, one element per thread)
+    m = 512
+    a = special_f32(m * m, 22).reshape(m, m)
+    b = special_f32(m * m, 23).reshape(m, m)
+    da = contiguous(a)
+    db = contiguous(b)
+    db.shape, db.strides = [m, m], [1, m]
+    prog = abi.program(2, abi.MUL, epilogue="sigmoid")
+    y1 = empty([m, m], np.float32)
+    device.elementwise(prog, [da.view, db.view], y1)
+    gap = np.zeros((m, m + 3), np.float32)
+    gap[:, :m] = b
+    dg = DevView(gap, [m, m], [1, m + 3], 0)
+    y2 = empty([m, m], np.float32)
+    device.elementwise(prog, [da.view, dg.view], y2)
+    assert_bit_exact(to_host(y1), to_host(y2), "packed vs scalar sigmoid(A & B^T)")
