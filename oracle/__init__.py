@@ -88,6 +88,9 @@ def load():
             "orc_opt_step": (c_int, [c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_double,
                                      c_double, c_double, c_double, c_int64]),
             "orc_pool2d": (c_int, [c_int, V, c_int64, c_int64, c_int64, c_int64, c_void_p, I64P]),
+            "orc_matmul": (c_int, [V, V, c_void_p, I64P, POINTER(c_int32)]),
+            "orc_unfold_2d": (c_int, [V, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, I64P]),
+            "orc_fold_2d": (c_int, [V, I64P, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p]),
             "orc_max_pool2d_backward": (c_int, [V, V, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
         }
         for name, (res, args) in sig.items():
@@ -289,6 +292,43 @@ def max_pool2d_backward(x: HostView, g: HostView, kernel, stride=None, current: 
     _check(load().orc_max_pool2d_backward(ctypes.byref(x.c()), ctypes.byref(g.c()), kh, kw, sh, sw,
                                           cur.ctypes.data if cur is not None else None, out.ctypes.data))
     return out[: x.numel()].reshape(x.shape)
+
+
+def matmul(a: HostView, b: HostView) -> np.ndarray:
+    """Tensor::matmul (linalg/tensor/base.rs:896-1013)."""
+    batch = list(np.broadcast_shapes(tuple(a.shape[:-2]), tuple(b.shape[:-2]))) if len(a.shape) >= 2 and \
+        len(b.shape) >= 2 else []
+    n = int(np.prod(batch, dtype=np.int64)) * (a.shape[-2] if len(a.shape) >= 2 else 1) * \
+        (b.shape[-1] if len(b.shape) >= 2 else 1)
+    out = _out_buf(a.dtype, max(n, 1))
+    shp = (c_int64 * (MAX_DIMS + 2))()
+    nd = c_int32()
+    _check(load().orc_matmul(ctypes.byref(a.c()), ctypes.byref(b.c()), out.ctypes.data, shp, ctypes.byref(nd)))
+    shape = [shp[i] for i in range(nd.value)]
+    return out[: int(np.prod(shape, dtype=np.int64))].reshape(shape)
+
+
+def unfold_2d(x: HostView, kernel, stride, padding=(0, 0)) -> np.ndarray:
+    """Tensor::unfold_2d (linalg/tensor/conv.rs:360-418)."""
+    (kh, kw), (sh, sw), (ph, pw) = kernel, stride, padding
+    n = 1
+    if len(x.shape) == 4 and sh > 0 and sw > 0 and x.shape[2] + 2 * ph >= kh and x.shape[3] + 2 * pw >= kw:
+        N, C, H, W = x.shape
+        n = N * ((H + 2 * ph - kh) // sh + 1) * ((W + 2 * pw - kw) // sw + 1) * C * kh * kw
+    out = _out_buf(x.dtype, max(n, 1))
+    shp = (c_int64 * 2)()
+    _check(load().orc_unfold_2d(ctypes.byref(x.c()), kh, kw, sh, sw, ph, pw, out.ctypes.data, shp))
+    return out[: shp[0] * shp[1]].reshape(shp[0], shp[1])
+
+
+def fold_2d(cols: HostView, shape, kernel, stride, padding=(0, 0)) -> np.ndarray:
+    """Tensor::fold_2d (linalg/tensor/conv.rs:434-488) into [batch, channels, height, width]."""
+    (kh, kw), (sh, sw), (ph, pw) = kernel, stride, padding
+    n = int(np.prod(shape, dtype=np.int64))
+    out = _out_buf(cols.dtype, max(n, 1))
+    _check(load().orc_fold_2d(ctypes.byref(cols.c()), (c_int64 * 4)(*shape), kh, kw, sh, sw, ph, pw,
+                              out.ctypes.data))
+    return out[:n].reshape(shape)
 
 
 def sum_f64(x: HostView) -> tuple[float, float]:

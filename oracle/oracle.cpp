@@ -25,6 +25,7 @@
 #include <cstdint>
 #include <cstring>
 #include <limits>
+#include <string>
 #include <thread>
 #include <type_traits>
 #include <vector>
@@ -308,6 +309,13 @@ const char* bin_msg(int op) {
 }
 
 thread_local const char* g_msg = "";
+thread_local std::string g_msg_buf;  // formatted panic texts (g_msg points here)
+
+std::string shape_text(const std::vector<int64_t>& s) {
+  std::string r = "[";
+  for (size_t i = 0; i < s.size(); ++i) r += (i ? ", " : "") + std::to_string(s[i]);
+  return r + "]";
+}
 
 // binary_op (ops.rs:240-300), fast path and broadcast path.
 template <class T>
@@ -674,6 +682,81 @@ std::vector<T> fold_2d(const std::vector<T>& src, int64_t batch, int64_t channel
       }
   });
   return data;
+}
+
+// Tensor::matmul (linalg/tensor/base.rs:896-1013): A [..., M, K] times
+// B [..., K, N], the batch dimensions broadcast against each other (1 against
+// anything; a 0 against a 1 gives 1, as in broadcast_shape); every output is
+// `acc = acc + a * b` over k = 0 .. K-1 from acc = 0 in the element type, both
+// operands read through their strides.
+template <class T>
+int matmul(const Tensor<T>& a, const Tensor<T>& b, std::vector<T>* out, std::vector<int64_t>* out_shape) {
+  const size_t an = a.shape.size(), bn = b.shape.size();
+  if (an < 2 || bn < 2) { g_msg = "matmul: both tensors must be at least 2D"; return ERR_SHAPE; }
+  const int64_t m = a.shape[an - 2], k = a.shape[an - 1], n = b.shape[bn - 1];
+  if (k != b.shape[bn - 2]) {
+    g_msg = "matmul: inner dimensions must match (A.shape[-1] == B.shape[-2])";
+    return ERR_SHAPE;
+  }
+  std::vector<int64_t> ab(a.shape.begin(), a.shape.end() - 2), bb(b.shape.begin(), b.shape.end() - 2), batch;
+  if (!broadcast_shape(ab, bb, &batch)) { g_msg = "matmul: batch shapes not broadcastable"; return ERR_SHAPE; }
+  std::vector<int64_t> os = batch;
+  os.push_back(m);
+  os.push_back(n);
+  int64_t len = 1;
+  for (int64_t d : os) len *= d;
+  const size_t on = os.size();
+  std::vector<int64_t> suffix(on, 1);
+  for (int i = (int)on - 2; i >= 0; --i) suffix[i] = suffix[i + 1] * os[i + 1];
+  auto batch_offset = [&](const Tensor<T>& t, const int64_t* coords) {
+    const size_t tn = t.shape.size();
+    int64_t off = t.offset;
+    for (size_t ax = 0; ax + 2 < tn; ++ax) {
+      const size_t oax = on - tn + ax;
+      const int64_t c = t.shape[ax] == 1 ? 0 : coords[oax];
+      off += t.strides[ax] * c;
+    }
+    return off;
+  };
+  out->assign((size_t)len, T(0));
+  T* o = out->data();
+  for_outputs(len, [&](int64_t idx) {
+    int64_t coords[kMaxDims + 2];
+    int64_t rem = idx;
+    for (size_t ax = 0; ax < on; ++ax) {
+      coords[ax] = rem / suffix[ax];
+      rem %= suffix[ax];
+    }
+    const int64_t i = coords[on - 2], j = coords[on - 1];
+    const int64_t a_base = batch_offset(a, coords) + a.strides[an - 2] * i;
+    const int64_t b_base = batch_offset(b, coords) + b.strides[bn - 1] * j;
+    const int64_t a_step = a.strides[an - 1], b_step = b.strides[bn - 2];
+    T acc = T(0);
+    for (int64_t kk = 0; kk < k; ++kk)
+      acc = Arith<T>::add(acc, Arith<T>::mul(a.data[a_base + a_step * kk], b.data[b_base + b_step * kk]));
+    o[idx] = acc;
+  });
+  *out_shape = os;
+  return OK;
+}
+
+// unfold_dims (linalg/tensor/conv.rs:490-510): the checks of unfold_2d.
+template <class T>
+int unfold_dims(const Tensor<T>& x, int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw) {
+  if (x.shape.size() != 4) {
+    g_msg_buf = "!!!unfold_2d() expects [batch, channels, height, width], got " + shape_text(x.shape) + "!!!";
+    g_msg = g_msg_buf.c_str();
+    return ERR_SHAPE;
+  }
+  if (sh <= 0 || sw <= 0) { g_msg = "!!!unfold_2d(): stride must be positive!!!"; return ERR_ARG; }
+  if (kh < 0 || kw < 0 || ph < 0 || pw < 0 || x.shape[2] + 2 * ph < kh || x.shape[3] + 2 * pw < kw) {
+    g_msg_buf = "!!!unfold_2d(): a (" + std::to_string(kh) + ", " + std::to_string(kw) +
+                ") kernel does not fit a " + std::to_string(x.shape[2]) + "x" + std::to_string(x.shape[3]) +
+                " input padded by (" + std::to_string(ph) + ", " + std::to_string(pw) + ")!!!";
+    g_msg = g_msg_buf.c_str();
+    return ERR_SHAPE;
+  }
+  return OK;
 }
 
 // The checks of pool_dims (nn/pool.rs:36-41), with_stride (pool.rs:115-118)
@@ -1121,6 +1204,67 @@ int orc_max_pool2d_backward(const View* x, const View* g, int64_t kh, int64_t kw
     int st = max_pool2d_backward(from_view<T>(x), from_view<T>(g), kh, kw, sh, sw,
                                  static_cast<const T*>(current), &r);
     if (st) return st;
+    std::memcpy(out, r.data(), r.size() * sizeof(T));
+  });
+  return OK;
+}
+
+// Tensor::matmul; out_shape receives the result's ndim dimensions.
+int orc_matmul(const View* a, const View* b, void* out, int64_t* out_shape, int32_t* out_ndim) {
+  if (a->dtype != b->dtype) { g_msg = "dtype mismatch"; return ERR_DTYPE; }
+  DISPATCH(a->dtype, {
+    std::vector<T> r;
+    std::vector<int64_t> os;
+    int st = matmul(from_view<T>(a), from_view<T>(b), &r, &os);
+    if (st) return st;
+    std::memcpy(out, r.data(), r.size() * sizeof(T));
+    for (size_t d = 0; d < os.size(); ++d) out_shape[d] = os[d];
+    *out_ndim = (int32_t)os.size();
+  });
+  return OK;
+}
+
+// Tensor::unfold_2d (conv.rs:360-418) of a [batch, channels, height, width]
+// view; out_shape receives [batch * out_h * out_w, channels * kh * kw].
+int orc_unfold_2d(const View* x, int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw, void* out,
+                  int64_t* out_shape) {
+  DISPATCH(x->dtype, {
+    Tensor<T> t = from_view<T>(x);
+    int st = unfold_dims(t, kh, kw, sh, sw, ph, pw);
+    if (st) return st;
+    int64_t oh, ow;
+    std::vector<T> r = unfold_2d(packed_data(t), t.shape[0], t.shape[1], t.shape[2], t.shape[3], kh, kw, sh, sw,
+                                 ph, pw, &oh, &ow);
+    std::memcpy(out, r.data(), r.size() * sizeof(T));
+    out_shape[0] = t.shape[0] * oh * ow;
+    out_shape[1] = t.shape[1] * kh * kw;
+  });
+  return OK;
+}
+
+// Tensor::fold_2d (conv.rs:434-488) of a 2-D view into [batch, channels,
+// height, width] = shape.
+int orc_fold_2d(const View* cols, const int64_t* shape, int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph,
+                int64_t pw, void* out) {
+  DISPATCH(cols->dtype, {
+    Tensor<T> t = from_view<T>(cols);
+    if (sh <= 0 || sw <= 0) { g_msg = "!!!fold_2d(): stride must be positive!!!"; return ERR_ARG; }
+    const int64_t B = shape[0], C = shape[1], H = shape[2], W = shape[3];
+    bool ok = kh >= 0 && kw >= 0 && ph >= 0 && pw >= 0 && H + 2 * ph >= kh && W + 2 * pw >= kw;
+    int64_t oh = 0, ow = 0;
+    if (ok) {
+      oh = (H + 2 * ph - kh) / sh + 1;
+      ow = (W + 2 * pw - kw) / sw + 1;
+      ok = t.shape == std::vector<int64_t>{B * oh * ow, C * kh * kw};
+    }
+    if (!ok) {
+      g_msg_buf = "!!!fold_2d(): shape " + shape_text(t.shape) + " does not match an unfold of [" +
+                  std::to_string(B) + ", " + std::to_string(C) + ", " + std::to_string(H) + ", " + std::to_string(W) +
+                  "]!!!";
+      g_msg = g_msg_buf.c_str();
+      return ERR_SHAPE;
+    }
+    std::vector<T> r = fold_2d(packed_data(t), B, C, H, W, kh, kw, sh, sw, ph, pw);
     std::memcpy(out, r.data(), r.size() * sizeof(T));
   });
   return OK;

@@ -67,6 +67,13 @@ def run_oracle(case):
         return oracle.pool2d(op[:3], vs[0], case["kernel"], case["stride"])
     if op == "max_pool2d_backward":
         return oracle.max_pool2d_backward(vs[0], vs[1], case["kernel"], case["stride"])
+    if op == "matmul":
+        return oracle.matmul(vs[0], vs[1])
+    if op == "unfold_2d":
+        return oracle.unfold_2d(vs[0], case["kernel"], case["stride"], case["padding"])
+    if op == "unfold_fold_2d":  # the fold doctest folds the unfold of its input back
+        cols = oracle.unfold_2d(vs[0], case["kernel"], case["stride"], case["padding"])
+        return oracle.fold_2d(oracle.contiguous(cols), vs[0].shape, case["kernel"], case["stride"], case["padding"])
     if op == "layer_norm":
         wrap = oracle.contiguous
         return _layer_norm(
