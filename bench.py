@@ -6,8 +6,9 @@
 Default workload (the sharded configuration, run at 1/2/4/8 GPUs):
     Y = A & B + c, s = sum(Y)  with A, B f32 [65536, 32768] ~ U(-1,1) (8 GiB
     each), c f32 [32768] ~ U(-1,1), seed 4; A and B split on dim 0 across the
-    ranks (strong scaling: the total problem is fixed), the sum combined with
-    one NCCL all-reduce of f64 partials.
+    ranks (strong scaling: the total problem is fixed), the ranks' f64
+    partial sums combined over NVLink peer memory by the kernel that folds
+    them (ncclAllReduce where peer mapping is unavailable).
 A step is one fused pass through the C ABI (trs_elementwise_sum, or
 trs_sharded_elementwise_sum for N > 1): Y written, sum(Y) returned.
 
@@ -242,6 +243,7 @@ def run_trs(args) -> None:
                                 device_id=torch.device("cuda", local))
         communicator = sharding.Communicator(lib, rank, world, dist, timeout_ms=120000)
         comm = communicator.handle
+    exchange = world > 1 and communicator.peer_exchange
 
     total_rows = args.rows
     assert total_rows % world == 0
@@ -380,7 +382,9 @@ def run_trs(args) -> None:
                                    "~U(-1,1) split on dim 0, c f32 [32768], seed 4",
                        "global_rows": total_rows, "cols": COLS, "rows_per_gpu": rows,
                        "bytes_per_step": total_bytes, "l2": "inputs 8 GiB/operand >> 126 MB L2, no flush",
-                       "parallelism": f"dim-0 shards x{world}" + (", NCCL all-reduce of f64 partials" if world > 1 else "")},
+                       "parallelism": f"dim-0 shards x{world}" + (
+                           (", f64 partials combined over NVLink peer memory inside the fold kernel"
+                            if exchange else ", f64 partials combined by ncclAllReduce") if world > 1 else "")},
             "elements_per_s": round(total_rows * COLS / (ms_step * 1e-3), 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
@@ -584,7 +588,47 @@ def suite_groups(lib, abi, device, torch):
         ("sgd step, 2^26 f32 params", 3 * npar * 4,
          lambda s: C(lib.trs_sgd_step(ref(s["v"]["P"]), ref(s["v"]["G"]), 1e-3, sh))),
     ]))
+
+    # callers of the path: matmul (Linear, Conv2d) and the im2col pair
+    mm = 4096
+
+    def make_mm():
+        s = {"A": device.fill_normal(t(mm, mm), 14), "B": device.fill_normal(t(mm, mm), 15), "C": t(mm, mm)}
+        s["v"] = {k: V(x) for k, x in s.items()}
+        return s
+    groups.append(SuiteGroup("callers", make_mm, [
+        ("matmul [4096,4096] x [4096,4096] f32, reference order", 3 * mm * mm * 4,
+         lambda s: C(lib.trs_matmul(ref(s["v"]["A"]), ref(s["v"]["B"]), ref(s["v"]["C"]), sh)), 2 * mm ** 3),
+    ]))
+    cN, cC, cH, cW = 32, 64, 56, 56
+    crow, cpatch = cN * cH * cW, cC * 9
+    xb_c, cb_c = cN * cC * cH * cW * 4, crow * cpatch * 4
+
+    def make_cols():
+        s = {"X": device.fill_normal(t(cN, cC, cH, cW), 16), "K": t(crow, cpatch), "Y": t(cN, cC, cH, cW)}
+        s["v"] = {k: V(x) for k, x in s.items()}
+        return s
+    groups.append(SuiteGroup("callers", make_cols, [
+        ("unfold_2d 3x3 pad 1 of X[32,64,56,56]", xb_c + cb_c,
+         lambda s: C(lib.trs_unfold_2d(ref(s["v"]["X"]), 3, 3, 1, 1, 1, 1, ref(s["v"]["K"]), sh))),
+        ("fold_2d 3x3 pad 1 into X[32,64,56,56]", xb_c + cb_c,
+         lambda s: C(lib.trs_fold_2d(ref(s["v"]["K"]), 3, 3, 1, 1, 1, 1, ref(s["v"]["Y"]), sh))),
+    ]))
     return groups
+
+
+def fp32_lane_peak() -> float:
+    """FP32 lane operations per second of the CUDA cores at the measured
+    maximum SM clock: 148 SMs x 128 lanes x clock.  matmul in the reference's
+    order spends two of them per multiply-add (a separately rounded product
+    and sum), so 2 M N K flops against this figure is its compute roofline."""
+    mhz = 1965.0
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        mhz = float(json.loads(p.read_text()).get("sm_max_mhz", mhz))
+    except (OSError, ValueError):
+        pass
+    return 148 * 128 * mhz * 1e6
 
 
 def set_bytes(s) -> int:
@@ -641,7 +685,9 @@ def run_suite_entries(args, only=None, steady=True, flushed_reps=5, warm=2):
             n_sets = min(64, max(2, -(-ROTATE_BYTES // max(sb, 1))))
             sets += [g.make() for _ in range(n_sets - 1)]
         torch.cuda.synchronize()
-        for name, nbytes, launch in names:
+        for entry in names:
+            name, nbytes, launch = entry[:3]
+            flops = entry[3] if len(entry) > 3 else None
             times = []
             for i in range(flushed_reps + warm):
                 flush_buf.fill_(float(i))
@@ -671,6 +717,13 @@ def run_suite_entries(args, only=None, steady=True, flushed_reps=5, warm=2):
                 gbps = nbytes / (ms_s * 1e-3) / 1e9
                 rec.update({"us_steady": round(ms_s * 1e3, 2), "GBps": round(gbps, 1), "frac": round(gbps / peak, 4),
                             "rotation": f"{k} buffer sets x {sb / 2**20:.0f} MiB"})
+            if flops:  # a contraction: its roofline is compute, not HBM
+                ms = rec.get("us_steady", rec["us_flushed"]) / 1e3
+                tf = flops / (ms * 1e-3) / 1e12
+                rec.update({"flops": int(flops), "TFLOPs": round(tf, 2), "frac": round(tf * 1e12 / fp32_lane_peak(), 4),
+                            "bound": "fp32 CUDA cores (separately rounded multiply and add)"})
+                rec.pop("GBps", None)
+                rec["frac_flushed"] = round(flops / (ms_f * 1e-3) / fp32_lane_peak(), 4)
             tr = traffic.get(name)
             rec["dram_ratio"] = round(tr / nbytes, 3) if tr else None
             out.append(rec)

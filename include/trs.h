@@ -167,10 +167,11 @@ uint64_t trs_launch_count(void);
 uint64_t trs_scratch_alloc_count(void);
 
 /* Reads and clears the current device's async-error word.  A kernel that
- * waits on its own bulk copies gives up after a bounded number of polls,
- * sets this word and returns instead of hanging; *code receives the word
- * (0 = none).  Synchronises the device.  Returns TRS_ERR_TIMEOUT when the
- * word was set. */
+ * waits gives up after a bounded number of polls, sets a bit of this word and
+ * returns instead of hanging: bit 0 (1) when it waited on its own bulk
+ * copies, bit 1 (2) when a sharded sum waited on a peer rank's partial;
+ * *code receives the word (0 = none).  Synchronises the device.  Returns
+ * TRS_ERR_TIMEOUT when the word was set. */
 trs_status trs_async_error(int32_t* code);
 
 /* ------------------------------------------------------------------ */
@@ -387,6 +388,44 @@ trs_status trs_max_pool2d_backward(const trs_view* x, const trs_view* grad_out,
                                    trs_view* grad_x, trs_stream stream);
 
 /* ------------------------------------------------------------------ */
+/* Contraction and the im2col pair (callers of the path: Linear,       */
+/* Conv2d, MultiHeadAttention)                                          */
+/* ------------------------------------------------------------------ */
+
+/* Tensor::matmul (linalg/tensor/base.rs:896-1013): a [..., M, K] times
+ * b [..., K, N] into out [batch..., M, N], where the batch dimensions of a
+ * and b broadcast against each other (a dimension of 1 is reused).  Both
+ * operands are read through their strides.  Every output is the reference's
+ * chain acc = acc + a[i, k] * b[k, j] over k = 0 .. K-1 from acc = 0, each
+ * step rounded once in the element type (integers wrap), so results are
+ * bit-identical to the reference's.  Panics of the reference map to
+ * TRS_ERR_SHAPE with its text ("matmul: both tensors must be at least 2D",
+ * "matmul: inner dimensions must match (A.shape[-1] == B.shape[-2])",
+ * "matmul: batch shapes not broadcastable"); out may not overlap a or b
+ * (TRS_ERR_ALIAS). */
+trs_status trs_matmul(const trs_view* a, const trs_view* b, trs_view* out,
+                      trs_stream stream);
+
+/* Tensor::unfold_2d (linalg/tensor/conv.rs:360-418): every (kh, kw) window of
+ * x [B, C, H, W] (stride (sh, sw), zero padding (ph, pw) on each side) as one
+ * row of out [B * OH * OW, C * kh * kw], rows in (b, oh, ow) order, each row
+ * in (c, i, j) order; OH = (H + 2 ph - kh) / sh + 1, likewise OW.  Panics of
+ * unfold_dims (conv.rs:490-510) map to TRS_ERR_SHAPE / TRS_ERR_ARG. */
+trs_status trs_unfold_2d(const trs_view* x, int64_t kh, int64_t kw, int64_t sh,
+                         int64_t sw, int64_t ph, int64_t pw, trs_view* out,
+                         trs_stream stream);
+
+/* Tensor::fold_2d (linalg/tensor/conv.rs:434-488): the rows of an unfold,
+ * cols [B * OH * OW, C * kh * kw], added back into out [B, C, H, W] (its
+ * shape is the reference's output_shape) wherever windows overlap; each
+ * pixel adds its windows' values in increasing (oh, ow) order from +0, as the
+ * reference's loop does, so results are bit-identical.  A cols shape that is
+ * not an unfold of out is TRS_ERR_SHAPE with the reference's text. */
+trs_status trs_fold_2d(const trs_view* cols, int64_t kh, int64_t kw, int64_t sh,
+                       int64_t sw, int64_t ph, int64_t pw, trs_view* out,
+                       trs_stream stream);
+
+/* ------------------------------------------------------------------ */
 /* Seeded synthetic inputs                                              */
 /* ------------------------------------------------------------------ */
 
@@ -432,14 +471,29 @@ trs_status trs_comm_init_rank(const uint8_t id[128], int32_t nranks,
 trs_status trs_comm_destroy(trs_comm* comm);
 trs_status trs_comm_abort(trs_comm* comm);
 
+/* *active = 1 when this communicator's sharded sums combine over NVLink peer
+ * memory (every rank mapped every peer's slot buffer at creation), 0 when
+ * they combine with ncclAllReduce. */
+trs_status trs_comm_peer_exchange(const trs_comm* comm, int32_t* active);
+
 /* sum() of a tensor whose leading dimension is split across the ranks:
  * every rank passes its shard; every rank receives the global sum (f64
- * partials all-reduced, rounded once). */
+ * partials combined in rank order, rounded once).  The combine is done by the
+ * kernel that folds this rank's partials: it writes its accumulator into
+ * every peer's slot buffer over NVLink and reads theirs (mapped at
+ * communicator creation with CUDA IPC), so no collective is launched; where
+ * that mapping could not be made on every rank, an ncclAllReduce combines
+ * instead.  Calls on one communicator must be made by every rank in the same
+ * order and, per rank, on one stream (their slots are reused call after
+ * call).  A peer that does not make the call leaves this rank's kernel
+ * waiting about 2 s, after which it gives up: the sum is NaN (0 for
+ * integers) and trs_async_error() reports bit 1. */
 trs_status trs_sharded_sum(trs_comm* comm, const trs_view* shard,
                            trs_view* out, trs_stream stream);
 
 /* trs_elementwise_sum over leading-dimension shards: each rank writes its
- * shard of the element-wise result and every rank receives the global sum. */
+ * shard of the element-wise result and every rank receives the global sum,
+ * combined as in trs_sharded_sum. */
 trs_status trs_sharded_elementwise_sum(trs_comm* comm,
                                        const trs_ew_program* prog,
                                        const trs_view* in, trs_view* out,

@@ -107,6 +107,9 @@ _SIGNATURES = {
     "trs_max_pool2d": (c_int32, [_V, c_int64, c_int64, c_int64, c_int64, _V, c_void_p]),
     "trs_avg_pool2d": (c_int32, [_V, c_int64, c_int64, c_int64, c_int64, _V, c_void_p]),
     "trs_max_pool2d_backward": (c_int32, [_V, _V, c_int64, c_int64, c_int64, c_int64, c_int32, _V, c_void_p]),
+    "trs_matmul": (c_int32, [_V, _V, _V, c_void_p]),
+    "trs_unfold_2d": (c_int32, [_V, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, _V, c_void_p]),
+    "trs_fold_2d": (c_int32, [_V, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, _V, c_void_p]),
     "trs_fill_uniform": (c_int32, [_V, c_uint64, c_uint64, c_double, c_double, c_void_p]),
     "trs_fill_normal": (c_int32, [_V, c_uint64, c_uint64, c_void_p]),
     "trs_set_device": (c_int32, [c_int32]),
@@ -118,6 +121,7 @@ _SIGNATURES = {
     "trs_comm_unique_id": (c_int32, [POINTER(c_uint8)]),
     "trs_comm_init_rank": (c_int32, [POINTER(c_uint8), c_int32, c_int32, c_int32, POINTER(c_void_p)]),
     "trs_comm_destroy": (c_int32, [c_void_p]),
+    "trs_comm_peer_exchange": (c_int32, [c_void_p, POINTER(c_int32)]),
     "trs_comm_abort": (c_int32, [c_void_p]),
     "trs_sharded_sum": (c_int32, [c_void_p, _V, _V, c_void_p]),
     "trs_sharded_elementwise_sum": (c_int32, [c_void_p, POINTER(Program), _V, _V, _V, c_void_p]),

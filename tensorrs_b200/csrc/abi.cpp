@@ -150,7 +150,10 @@ trs_status trs_async_error(int32_t* code) {
   if (e == cudaSuccess) e = cudaMemcpy(word, &zero, sizeof(int), cudaMemcpyHostToDevice);
   if (e != cudaSuccess) return finish(cuda_error(e, "reading the async-error word"));
   if (code) *code = v;
-  if (v) return finish(make_error(TRS_ERR_TIMEOUT, "a kernel gave up waiting for its own bulk copies"));
+  if (v)
+    return finish(make_error(TRS_ERR_TIMEOUT, std::string("a kernel gave up waiting: ") +
+                                                  ((v & 1) ? "for its own bulk copies " : "") +
+                                                  ((v & 2) ? "for a peer rank's partial sum" : "")));
   return TRS_OK;
 }
 

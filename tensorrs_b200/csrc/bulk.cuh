@@ -112,7 +112,8 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
-// Error codes in the async-error word.
-constexpr int kAsyncWaitTimeout = 1;
+// Error codes in the async-error word (bits).
+constexpr int kAsyncWaitTimeout = 1;   // a CTA gave up waiting for its own bulk copies
+constexpr int kAsyncPeerTimeout = 2;   // the sum exchange gave up waiting for a peer rank
 
 }  // namespace trs

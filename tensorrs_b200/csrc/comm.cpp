@@ -1,6 +1,17 @@
 // comm.cpp -- several GPUs: each rank holds a leading-dimension shard; the
 // element-wise part needs no communication and the full sum combines per-rank
-// f64 partials with one NCCL all-reduce over NVLink.
+// f64 partials over NVLink.
+//
+// The full sum's combine is fused into the kernel that folds this rank's
+// partials (sum_exchange_kernel): at communicator creation every rank
+// allocates a small slot buffer, exports it as a CUDA IPC handle, the handles
+// travel by one NCCL all-gather, and every rank maps its peers' buffers; a
+// sharded sum then writes its accumulator straight into every peer's buffer
+// and reads the others' from its own, with no collective launch.  When the
+// mapping cannot be made on some rank (peers not visible to the process, no
+// peer access), every rank agrees (an all-reduce of a flag) to combine with
+// ncclAllReduce instead; TRS_PEER_EXCHANGE=0 in the environment forces that.
+// Axis-0 reductions (many values) keep NCCL.
 //
 // NCCL is loaded at run time (dlopen of libnccl.so.2), so a process that never
 // creates a communicator does not need it, and a process that already loaded
@@ -12,6 +23,7 @@
 #include <nccl.h>
 
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -30,6 +42,11 @@ struct trs_comm {
   int nranks = 0;
   int rank = 0;
   int timeout_ms = 0;
+  // peer exchange of the sharded sums (xpeers null: combine through NCCL)
+  unsigned long long* xbuf = nullptr;    // this rank's slot buffer
+  unsigned long long** xpeers = nullptr; // device array: every rank's buffer, mapped here
+  std::vector<void*> xopened;            // IPC mappings of the peers' buffers
+  unsigned long long xseq = 0;           // sequence number of the last sharded sum
 };
 
 namespace {
@@ -109,6 +126,107 @@ Error wait_ready(trs_comm* c, const char* what) {
   }
 }
 
+// ---- the peer exchange ------------------------------------------------------
+
+Error nccl_call(trs_comm* c, ncclResult_t r, const char* what);
+
+// Unmaps the peers' buffers and frees this rank's, after this device's work
+// has finished (an exchange kernel of this rank may still be writing into a
+// peer's buffer).  A peer writes into this rank's buffer only inside calls
+// this rank also makes, before this rank's kernel of that call can finish.
+void teardown_exchange(trs_comm* c) {
+  if (c->xbuf || c->xpeers || !c->xopened.empty()) cudaDeviceSynchronize();
+  for (void* p : c->xopened) cudaIpcCloseMemHandle(p);
+  c->xopened.clear();
+  if (c->xpeers) cudaFree(c->xpeers);
+  if (c->xbuf) cudaFree(c->xbuf);
+  c->xpeers = nullptr;
+  c->xbuf = nullptr;
+  cudaGetLastError();
+}
+
+// Called by every rank of a new communicator (a collective: one all-gather
+// and one all-reduce).  Leaves c->xpeers set when every rank mapped every
+// peer's slot buffer, null (NCCL combine) otherwise.
+Error setup_exchange(trs_comm* c) {
+  const int R = c->nranks;
+  const char* env = std::getenv("TRS_PEER_EXCHANGE");
+  const bool wanted = !(env && env[0] == '0');
+  if (R < 2 || R > kMaxExchangeRanks) return Error{};
+  Nccl& n = nccl();
+  cudaStream_t s = nullptr;
+  cudaError_t ce = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+  if (ce != cudaSuccess) return cuda_error(ce, "cudaStreamCreateWithFlags");
+  int ok = wanted ? 1 : 0;
+  const size_t bytes = (size_t)2 * R * 2 * sizeof(unsigned long long);
+  if (ok && cudaMalloc(&c->xbuf, bytes) != cudaSuccess) ok = 0;
+  if (ok && cudaMemset(c->xbuf, 0, bytes) != cudaSuccess) ok = 0;
+  cudaIpcMemHandle_t mine;
+  std::memset(&mine, 0, sizeof(mine));
+  if (ok && cudaIpcGetMemHandle(&mine, c->xbuf) != cudaSuccess) ok = 0;
+  cudaGetLastError();
+  // every rank's handle (an all-gather every rank takes part in, ok or not),
+  // then the agreement flag
+  const size_t hs = sizeof(cudaIpcMemHandle_t);
+  char* dev = nullptr;
+  ce = cudaMalloc(&dev, hs * (size_t)(R + 1) + 16);
+  if (ce != cudaSuccess) {
+    cudaStreamDestroy(s);
+    teardown_exchange(c);
+    return cuda_error(ce, "cudaMalloc (exchange set-up)");
+  }
+  std::vector<char> all(hs * (size_t)R);
+  Error e;
+  ce = cudaMemcpy(dev + hs * R, &mine, hs, cudaMemcpyHostToDevice);
+  if (ce != cudaSuccess) e = cuda_error(ce, "cudaMemcpy");
+  if (e.ok()) e = nccl_call(c, n.AllGather(dev + hs * R, dev, hs, ncclUint8, c->comm, s), "ncclAllGather (handles)");
+  if (e.ok()) {
+    ce = cudaMemcpyAsync(all.data(), dev, hs * R, cudaMemcpyDeviceToHost, s);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
+    if (ce != cudaSuccess) e = cuda_error(ce, "reading the handles");
+  }
+  std::vector<unsigned long long*> table(R, nullptr);
+  if (e.ok() && ok) {
+    table[c->rank] = c->xbuf;
+    for (int r = 0; r < R && ok; ++r) {
+      if (r == c->rank) continue;
+      cudaIpcMemHandle_t h;
+      std::memcpy(&h, all.data() + hs * r, hs);
+      void* p = nullptr;
+      if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        ok = 0;
+        break;
+      }
+      c->xopened.push_back(p);
+      table[r] = static_cast<unsigned long long*>(p);
+    }
+  }
+  // agreement: the exchange is used only if every rank mapped every peer
+  int32_t* flag = reinterpret_cast<int32_t*>(dev + hs * (R + 1));
+  int32_t agreed = 0;
+  if (e.ok()) {
+    ce = cudaMemcpy(flag, &ok, sizeof(int32_t), cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) e = cuda_error(ce, "cudaMemcpy");
+  }
+  if (e.ok()) e = nccl_call(c, n.AllReduce(flag, flag, 1, ncclInt32, ncclMin, c->comm, s), "ncclAllReduce (agreement)");
+  if (e.ok()) {
+    ce = cudaMemcpyAsync(&agreed, flag, sizeof(int32_t), cudaMemcpyDeviceToHost, s);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
+    if (ce != cudaSuccess) e = cuda_error(ce, "reading the agreement");
+  }
+  if (e.ok() && agreed) {
+    ce = cudaMalloc(&c->xpeers, sizeof(unsigned long long*) * R);
+    if (ce == cudaSuccess)
+      ce = cudaMemcpy(c->xpeers, table.data(), sizeof(unsigned long long*) * R, cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) e = cuda_error(ce, "the peer table");
+  }
+  cudaFree(dev);
+  cudaStreamDestroy(s);
+  if (!e.ok() || !agreed) teardown_exchange(c);
+  return e;
+}
+
 ncclDataType_t acc_type(int dtype) {
   switch (dtype) {
     case TRS_I32: return ncclUint32;
@@ -123,6 +241,18 @@ Error sharded_sum(trs_comm* c, const trs_ew_program& prog, const trs_view* in, c
   Error e = validate_view(sum_out, "sum output");
   if (!e.ok()) return e;
   if (numel_of(sum_out->shape, sum_out->ndim) != 1) return make_error(TRS_ERR_SHAPE, "sum output must hold one element");
+  if (c->xpeers) {  // the combine fused into the partials' fold, over NVLink
+    PeerExchange x;
+    x.peers = c->xpeers;
+    x.world = c->nranks;
+    x.rank = c->rank;
+    x.seq = ++c->xseq;
+    x.err = async_error_word();
+    SumTarget t;
+    t.view = sum_out;
+    t.exchange = &x;
+    return run_elementwise(prog, in, out, &t, stream);
+  }
   Scratch acc;
   e = acc.alloc(8, stream);
   if (!e.ok()) return e;
@@ -269,7 +399,9 @@ trs_status trs_comm_init_rank(const uint8_t id[128], int32_t nranks, int32_t ran
     return finish(nccl_error(r, "ncclCommInitRankConfig"));
   }
   Error e = wait_ready(c, "ncclCommInitRankConfig");
+  if (e.ok()) e = setup_exchange(c);
   if (!e.ok()) {
+    teardown_exchange(c);
     n.CommAbort(c->comm);
     delete c;
     return finish(e);
@@ -281,6 +413,7 @@ trs_status trs_comm_init_rank(const uint8_t id[128], int32_t nranks, int32_t ran
 trs_status trs_comm_destroy(trs_comm* comm) {
   if (!comm) return TRS_OK;
   Nccl& n = nccl();
+  teardown_exchange(comm);
   ncclResult_t r = n.CommDestroy(comm->comm);
   delete comm;
   if (r != ncclSuccess && r != ncclInProgress) return finish(nccl_error(r, "ncclCommDestroy"));
@@ -290,9 +423,16 @@ trs_status trs_comm_destroy(trs_comm* comm) {
 trs_status trs_comm_abort(trs_comm* comm) {
   if (!comm) return TRS_OK;
   Nccl& n = nccl();
+  teardown_exchange(comm);
   ncclResult_t r = n.CommAbort(comm->comm);
   delete comm;
   if (r != ncclSuccess) return finish(nccl_error(r, "ncclCommAbort"));
+  return TRS_OK;
+}
+
+trs_status trs_comm_peer_exchange(const trs_comm* comm, int32_t* active) {
+  if (!comm || !active) return finish(make_error(TRS_ERR_ARG, "null argument"));
+  *active = comm->xpeers ? 1 : 0;
   return TRS_OK;
 }
 

@@ -844,6 +844,114 @@ sum_finalize_kernel(const typename Arith<T>::Acc* partials, int n, T* out,
   }
 }
 
+// sum_finalize_kernel for a tensor split on axis 0 across ranks: the
+// partials of this rank fold in a fixed order as above, then the ranks
+// exchange their accumulators over NVLink peer memory instead of through a
+// collective library call -- thread r stores this rank's accumulator and the
+// call's sequence number into rank r's slot buffer (release: the value
+// before the number), threads r < world wait for rank r's number to reach
+// this call's in this rank's own buffer (acquire), and thread 0 adds the
+// world accumulators in rank order and rounds once.  Every rank adds the same
+// values in the same order, so all ranks get the same result.  The slot set
+// alternates with the parity of the sequence number: a rank can be at most
+// one call ahead of a peer still reading (it cannot finish a call before
+// every peer has written that call's value), so the value a reader needs is
+// never overwritten.  Each wait polls at most kPeerPolls times, sleeping in
+// between (about 2 s in all); a wait that runs out sets kAsyncPeerTimeout in
+// the async-error word and the result is NaN (floats) or 0 (integers).
+constexpr unsigned kPeerPolls = 1u << 23;
+
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <class Acc>
+__device__ __forceinline__ unsigned long long acc_bits(Acc a) {
+  if constexpr (sizeof(Acc) == 8) {
+    unsigned long long u;
+    memcpy(&u, &a, 8);
+    return u;
+  } else {
+    return (unsigned long long)a;
+  }
+}
+template <class Acc>
+__device__ __forceinline__ Acc acc_from_bits(unsigned long long u) {
+  if constexpr (sizeof(Acc) == 8) {
+    Acc a;
+    memcpy(&a, &u, 8);
+    return a;
+  } else {
+    return (Acc)u;
+  }
+}
+
+template <class T>
+__global__ void __launch_bounds__(1024)
+sum_exchange_kernel(const typename Arith<T>::Acc* partials, int n, T* out, const PeerExchange x) {
+  pdl_wait();  // the partials of the kernel before it
+  using Acc = typename Arith<T>::Acc;
+  __shared__ Acc red[32];
+  __shared__ unsigned long long vals[kMaxExchangeRanks];
+  __shared__ int failed;
+  Acc s = Acc(0);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s = s + partials[i];
+  s = block_sum<Acc>(s, red);
+  if (threadIdx.x == 0) {
+    red[0] = s;
+    failed = 0;
+  }
+  __syncthreads();
+  const int t = threadIdx.x;
+  const unsigned long long set = (x.seq & 1ull) * (unsigned long long)x.world;
+  if (t < x.world) {
+    unsigned long long* slot = x.peers[t] + 2 * (set + (unsigned long long)x.rank);
+    st_relaxed_sys(slot, acc_bits<Acc>(red[0]));
+    st_release_sys(slot + 1, x.seq);
+  }
+  if (t < x.world) {
+    const unsigned long long* mine = x.peers[x.rank] + 2 * (set + (unsigned long long)t);
+    unsigned polls = 0;
+    while (ld_acquire_sys(mine + 1) < x.seq) {
+      if (++polls > kPeerPolls) {
+        atomicOr(&failed, 1);
+        break;
+      }
+      __nanosleep(256);
+    }
+    vals[t] = ld_relaxed_sys(mine);
+  }
+  __syncthreads();
+  if (t == 0) {
+    if (failed) {
+      if (x.err) atomicOr(x.err, kAsyncPeerTimeout);
+      if (out) {
+        if constexpr (IsFloat<T>::value)
+          *out = Arith<T>::from_acc(Acc(NAN));
+        else
+          *out = T(0);
+      }
+    } else {
+      Acc total = Acc(0);
+      for (int r = 0; r < x.world; ++r) total = total + acc_from_bits<Acc>(vals[r]);
+      if (out) *out = Arith<T>::from_acc(total);
+    }
+  }
+}
+
 // Blocks per SM a kernel can keep resident (cached per kernel).
 inline int resident_blocks(const void* kernel, int threads) {
   static std::mutex mu;
@@ -1297,7 +1405,9 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
     // launched with programmatic stream serialization: scheduled while the
     // element-wise kernel finishes, it waits for that grid in pdl_wait
     Acc* raw = static_cast<Acc*>(sum->raw_acc);
+    const PeerExchange* xc = sum->exchange;
     void* fargs[] = {(void*)&part, (void*)&n_part, (void*)&sum_out, (void*)&raw};
+    void* xargs[] = {(void*)&part, (void*)&n_part, (void*)&sum_out, (void*)xc};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1);
     cfg.blockDim = dim3(1024);
@@ -1308,7 +1418,9 @@ Error ew_launch(const trs_ew_program& prog, const trs_view* in, const trs_view* 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t fe = cudaLaunchKernelExC(&cfg, (const void*)ewk::sum_finalize_kernel<T>, fargs);
+    const cudaError_t fe =
+        xc ? cudaLaunchKernelExC(&cfg, (const void*)ewk::sum_exchange_kernel<T>, xargs)
+           : cudaLaunchKernelExC(&cfg, (const void*)ewk::sum_finalize_kernel<T>, fargs);
     if (fe != cudaSuccess) return cuda_error(fe, "sum finalize launch");
     Error e = check_launch("sum finalize kernel");
     if (!e.ok()) return e;

@@ -41,6 +41,7 @@
 #endif
 
 namespace trs {
+
 namespace expf32 {
 
 TRS_EXP_HD float fma_rn(float a, float b, float c) {
@@ -191,7 +192,11 @@ __device__ __forceinline__ float sigmoid(float x) {
 // sigmoid of two values at once on sm_100's packed f32x2 add / multiply /
 // fused multiply-add (each lane rounded to nearest exactly as the scalar
 // instruction rounds, subnormals kept), so each pair costs one issue slot
-// where `sigmoid` above takes two.  The operations are those of `sigmoid` and
+// where `sigmoid` above takes two.  Unlike the scalar __fmul_rn / __fadd_rn,
+// a packed multiply whose result feeds a packed add may be fused into one
+// multiply-add by the compiler; the only such pair here is e = (s * 2^(ex+64))
+// * 2^-64 feeding d = 1 + e, where the scaling is exact (or e < 2^-126, and
+// 1 + e rounds to 1 either way), so a fused form gives the same d.  The operations are those of `sigmoid` and
 // `exp_nonpos`, step for step, with every negated operand folded into an
 // exact product by -1 or a sign-symmetric rounding:
 //   shift - t        = fma(t, -1, shift)  (exact: both integers in [2^23, 2^24))

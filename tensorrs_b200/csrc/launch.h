@@ -11,8 +11,22 @@
 
 namespace trs {
 
+// The cross-rank combine of a sharded sum, done by the kernel that folds the
+// per-block partials (sum_exchange_kernel): every rank's slot buffer mapped
+// into this process over NVLink (comm.cpp sets it up).  A rank's buffer holds
+// two sets (by the parity of the call's sequence number) of `world` slots of
+// {accumulator bits, sequence number}; slot r of a set is written by rank r.
+struct PeerExchange {
+  unsigned long long* const* peers = nullptr;  // device array: rank r's slot buffer
+  int world = 0;
+  int rank = 0;
+  unsigned long long seq = 0;                  // this call's number, the same on every rank
+  int* err = nullptr;                          // async-error word of this device
+};
+
 // Where a fused sum goes: a one-element view of the input dtype, or (for the
-// sharded path) a raw f64/u32/u64 accumulator written without rounding.
+// sharded path) a raw f64/u32/u64 accumulator written without rounding, or
+// the view after the cross-rank combine of `exchange`.
 struct SumTarget {
   const trs_view* view = nullptr;  // rounded result
   void* raw_acc = nullptr;         // accumulator before rounding
@@ -20,7 +34,11 @@ struct SumTarget {
   // they come from the scratch pool.
   void* partials = nullptr;
   size_t partials_bytes = 0;
+  const PeerExchange* exchange = nullptr;  // sum over the ranks before rounding
 };
+
+// Largest communicator the peer exchange serves (one slot per rank).
+constexpr int kMaxExchangeRanks = 64;
 
 // Element-wise program over `in`; writes `out` unless it is null, and the sum
 // of the results to `sum` when it is non-null.

@@ -190,6 +190,34 @@ def max_pool2d_backward(x: abi.View, grad_out: abi.View, kernel: tuple[int, int]
     return grad_x
 
 
+def matmul_shape(a: abi.View, b: abi.View) -> list[int]:
+    """The shape Tensor::matmul returns for a [..., M, K] and b [..., K, N]."""
+    sa = [a.shape[i] for i in range(a.ndim)]
+    sb = [b.shape[i] for i in range(b.ndim)]
+    batch = [max(x, y) for x, y in zip([1] * (len(sb) - len(sa)) + sa[:-2], [1] * (len(sa) - len(sb)) + sb[:-2])]
+    return batch + [sa[-2], sb[-1]]
+
+
+def matmul(a: abi.View, b: abi.View, out: torch.Tensor) -> torch.Tensor:
+    """Tensor::matmul (linalg/tensor/base.rs:896-1013), bit-identical to the reference."""
+    _call("trs_matmul", ctypes.byref(a), ctypes.byref(b), ctypes.byref(view_of(out)), stream_handle())
+    return out
+
+
+def unfold_2d(x: abi.View, kernel, stride, padding, out: torch.Tensor) -> torch.Tensor:
+    """Tensor::unfold_2d (linalg/tensor/conv.rs:360-418) into out [B*OH*OW, C*kh*kw]."""
+    (kh, kw), (sh, sw), (ph, pw) = kernel, stride, padding
+    _call("trs_unfold_2d", ctypes.byref(x), kh, kw, sh, sw, ph, pw, ctypes.byref(view_of(out)), stream_handle())
+    return out
+
+
+def fold_2d(cols: abi.View, kernel, stride, padding, out: torch.Tensor) -> torch.Tensor:
+    """Tensor::fold_2d (linalg/tensor/conv.rs:434-488) into out [B, C, H, W]."""
+    (kh, kw), (sh, sw), (ph, pw) = kernel, stride, padding
+    _call("trs_fold_2d", ctypes.byref(cols), kh, kw, sh, sw, ph, pw, ctypes.byref(view_of(out)), stream_handle())
+    return out
+
+
 def fill_uniform(out: torch.Tensor, seed: int, lo: float = -1.0, hi: float = 1.0, first: int = 0) -> torch.Tensor:
     _call("trs_fill_uniform", ctypes.byref(view_of(out)), seed, first, lo, hi, stream_handle())
     return out

@@ -76,6 +76,13 @@ class Communicator:
         self.handle = ctypes.c_void_p()
         abi.check(lib.trs_comm_init_rank(arr, world, rank, int(timeout_ms), ctypes.byref(self.handle)))
 
+    @property
+    def peer_exchange(self) -> bool:
+        """True when the sharded sums combine over NVLink peer memory."""
+        v = ctypes.c_int32(0)
+        abi.check(self.lib.trs_comm_peer_exchange(self.handle, ctypes.byref(v)))
+        return bool(v.value)
+
     def destroy(self) -> None:
         if self.handle:
             abi.check(self.lib.trs_comm_destroy(self.handle))

@@ -189,13 +189,89 @@ def main(outdir: str) -> int:
 
     run("elementwise_sum fma", case_fma)
 
+    # the combine of the full sums: over NVLink peer memory when every rank
+    # mapped every peer's slot buffer; many calls in a row (the slot sets
+    # alternate with the call's parity), then the same sums through a
+    # communicator forced onto ncclAllReduce, which must agree
+    exchange = comm.peer_exchange
+    xs = [rand((257 + 31 * i, 129), np.float32 if i % 2 else np.int64, 500 + i) for i in range(40)]
+
+    def sums_through(c):
+        got = []
+        for x in xs:
+            counts = counts_for("ragged", x.shape[0])
+            offs = sharding.row_offsets(counts)
+            t = dev(x[offs[rank]:offs[rank] + counts[rank]])
+            out = torch.empty((1,), dtype=t.dtype, device="cuda")
+            c.sum(device.view_of(t), device.view_of(out), sh)
+            got.append(out)
+        torch.cuda.synchronize()
+        return [o.cpu().numpy() for o in got]
+
+    def case_many():
+        got = sums_through(comm)
+        for x, g in zip(xs, got):
+            ref = np.asarray(oracle.sum_all(oracle.contiguous(x))).reshape(1)
+            if x.dtype.kind == "i":
+                assert_bit_exact(g, ref.astype(x.dtype), "sum in a row of calls")
+            else:
+                xd = x.astype(np.float64)
+                check_sum(g, ref, np.abs(xd).sum(), np.array([xd.sum()]))
+        os.environ["TRS_PEER_EXCHANGE"] = "0"
+        try:
+            nc = sharding.Communicator(lib, rank, world, dist, timeout_ms=60000)
+        finally:
+            del os.environ["TRS_PEER_EXCHANGE"]
+        try:
+            assert not nc.peer_exchange
+            via_nccl = sums_through(nc)
+        finally:
+            nc.destroy()
+        for x, g, h in zip(xs, got, via_nccl):
+            if x.dtype.kind == "i":
+                assert_bit_exact(g, h, "exchange vs NCCL")
+            else:  # both f64 sums of `world` partials rounded once
+                assert abs(float(g[0]) - float(h[0])) <= float(np.spacing(np.float32(abs(h[0]))))
+
+    run("sums in a row, exchange vs NCCL", case_many)
+
+    def case_peer_timeout():
+        """Rank 0 makes a sharded sum that rank 1 skips: its kernel's wait for
+        rank 1's partial runs out (about 2 s), it reports bit 1 of the
+        async-error word and writes NaN; rank 1 keeps its buffers alive until
+        rank 0's kernel has ended (the barrier), then both destroy the
+        communicator, whose calls are no longer matched."""
+        import time
+        tc = sharding.Communicator(lib, rank, world, dist, timeout_ms=60000)
+        try:
+            if not tc.peer_exchange:
+                return
+            if rank == 0:
+                t = dev(np.ones((8, 8), np.float32))
+                out = torch.zeros((1,), dtype=torch.float32, device="cuda")
+                t0 = time.monotonic()
+                tc.sum(device.view_of(t), device.view_of(out), sh)
+                torch.cuda.synchronize()
+                waited = time.monotonic() - t0
+                code = ctypes_async_error(lib)
+                assert code & 2, f"async-error word {code}, waited {waited:.2f} s"
+                assert np.isnan(out.cpu().numpy()[0])
+                assert 0.5 <= waited <= 60, waited
+            dist.barrier()
+        finally:
+            tc.destroy()
+
+    if world == 2:
+        run("peer exchange wait runs out", case_peer_timeout)
+
     err = ctypes_async_error(lib)
     if err:
         failures.append(f"async error word {err}")
     comm.destroy()
     dist.barrier()
     dist.destroy_process_group()
-    Path(outdir, f"rank{rank}.json").write_text(json.dumps({"rank": rank, "world": world, "failures": failures}))
+    Path(outdir, f"rank{rank}.json").write_text(json.dumps({"rank": rank, "world": world, "failures": failures,
+                                                           "peer_exchange": exchange}))
     return 1 if failures else 0
 
 

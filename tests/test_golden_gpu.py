@@ -69,6 +69,18 @@ def _run_gpu(case):
         return to_host(fn(dvs[0].view, (kh, kw), empty([n, c, oh, ow], dt), (sh, sw)))
     if op == "layer_norm":
         return _layer_norm_gpu(dvs, case["epsilon"], dt)
+    if op == "matmul":
+        out = empty(device.matmul_shape(dvs[0].view, dvs[1].view), dt)
+        return to_host(device.matmul(dvs[0].view, dvs[1].view, out))
+    if op in ("unfold_2d", "unfold_fold_2d"):
+        (kh, kw), (sh, sw), (ph, pw) = case["kernel"], case["stride"], case["padding"]
+        n, c, h, w = dvs[0].shape
+        oh, ow = (h + 2 * ph - kh) // sh + 1, (w + 2 * pw - kw) // sw + 1
+        cols = device.unfold_2d(dvs[0].view, (kh, kw), (sh, sw), (ph, pw), empty([n * oh * ow, c * kh * kw], dt))
+        if op == "unfold_2d":
+            return to_host(cols)
+        back = device.fold_2d(device.view_of(cols), (kh, kw), (sh, sw), (ph, pw), empty([n, c, h, w], dt))
+        return to_host(back)
     raise ValueError(op)
 
 

@@ -6,7 +6,11 @@ failing with TRS_ERR_TIMEOUT when a rank never joins.
 These launch child processes: a failure ends a child with an error, never a
 GPU kernel that waits on a rank that is gone (every collective here runs
 between ranks that are all alive; the timeout case never gets as far as a
-collective).  NCCL's NVLink SHARP path is switched off in the children."""
+collective).  The one wait made to run out on purpose is the sharded sum's
+peer exchange, where rank 1 skips a call while staying alive: rank 0's kernel
+gives up after its bounded wait (about 2 s) and reports it in the async-error
+word.  The exchange uses plain peer stores and loads (no multicast); NCCL's
+NVLink SHARP path is switched off in the children."""
 from __future__ import annotations
 
 import json
@@ -56,6 +60,9 @@ def test_sharded_entry_points_on_two_ranks(tmp_path):
     assert r.returncode == 0 and len(reports) == world, (r.returncode, r.stdout[-3000:], r.stderr[-3000:], reports)
     for k, rep in reports.items():
         assert rep["failures"] == [], (k, rep["failures"][:5])
+        # B200s under NVSwitch map each other's memory: the full sums combine
+        # over NVLink peer memory, not through NCCL
+        assert rep["peer_exchange"], k
 
 
 TIMEOUT_CHILD = r"""
