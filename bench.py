@@ -310,6 +310,31 @@ def run_trs(args) -> None:
 
     s_val = float(S.cpu()[0])
 
+    # where a sharded step goes: each rank's own element-wise + sum pass with
+    # no cross-rank combine, timed the same way; the sharded step above minus
+    # the slowest rank's local pass is the combine plus the wait for the
+    # slowest rank
+    breakdown = None
+    if world > 1:
+        def local_step():
+            abi.check(lib.trs_elementwise_sum(ctypes.byref(prog), ins, ctypes.byref(yv), ctypes.byref(sv), sh))
+        for _ in range(2):
+            local_step()
+        barrier()
+        l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        l0.record(stream)
+        for _ in range(args.steps):
+            local_step()
+        l1.record(stream)
+        barrier()
+        mine_ms = torch.tensor([l0.elapsed_time(l1) / args.steps], dtype=torch.float64, device="cuda")
+        every = [torch.zeros_like(mine_ms) for _ in range(world)]
+        dist.all_gather(every, mine_ms)
+        local = [round(float(t[0]), 4) for t in every]
+        breakdown = {"local_pass_ms_per_rank": local, "sharded_step_ms": round(ms_step, 4),
+                     "combine_and_skew_ms": round(ms_step - max(local), 4),
+                     "skew_ms": round(max(local) - min(local), 4)}
+
     total_bytes = workload_bytes(total_rows, COLS, world)
     value = total_bytes / (ms_step * 1e-3) / 1e9
     # roofline of the dominant kernel on one GPU: bytes one launch moves / its duration
@@ -396,6 +421,7 @@ def run_trs(args) -> None:
             "e2e": e2e,
             "cpu_baseline": cpu,
             "sum": s_val,
+            "step_breakdown": breakdown,
             "suite": suite,
             "suite_about": "every other kernel of the path on its configuration (configs 1-4 and the callers), "
                            "one GPU: us_flushed = one launch after an L2 flush; us_steady = back-to-back "
