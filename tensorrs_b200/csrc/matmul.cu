@@ -10,10 +10,11 @@
 // everything around that chain:
 //   * a CTA of 256 threads owns a BM x BN output tile; each thread owns a
 //     TM x TN block of it (8 x 8 for 4-byte types, 8 x 4 for 8-byte ones);
-//   * K advances in BK-deep slabs; the next slab of A and B is loaded from
-//     global memory into registers while the current one is multiplied out of
-//     shared memory (two buffers), with coalesced loads chosen by which
-//     dimension of each operand is unit-stride;
+//   * K advances in BK-deep slabs; the next slab of A and B is copied from
+//     global to shared memory asynchronously (cp.async, zero-filled beyond
+//     the matrix) while the current one is multiplied (two buffers), with
+//     coalesced reads chosen by which dimension of each operand is
+//     unit-stride;
 //   * the arithmetic is the scalar multiply and add, rounded separately:
 //     the FP32 lanes (32 per SM sub-partition per clock) bind a multiply and
 //     an add per output either way, and sm_100's packed f32x2 forms, which
@@ -35,6 +36,12 @@
 #include <string>
 
 #include "kernels.cuh"
+
+// Tuning knob: CTAs of the matmul kernel an SM keeps resident (its register
+// budget per thread follows); the default is the shipped configuration.
+#ifndef TRS_MM_MINB
+#define TRS_MM_MINB 2
+#endif
 
 namespace trs {
 namespace {
@@ -78,12 +85,41 @@ struct AccTile {
   __device__ __forceinline__ T get(int i, int j) const { return v[i][j]; }
 };
 
+// Asynchronous global -> shared copy of one element (4 or 8 bytes); src_bytes
+// 0 writes zeros without reading (the slab's padding beyond M, N or K).
+template <int BYTES>
+__device__ __forceinline__ void cp_async_elem(void* smem_dst, const void* gsrc, int src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], %2, %3;" ::"r"(smem_u32(smem_dst)), "l"(gsrc), "n"(BYTES),
+               "r"(src_bytes)
+               : "memory");
+}
+
+// Four consecutive elements of a shared row (16-byte aligned) in registers.
 template <class T>
-__global__ void __launch_bounds__(kThreads, std::is_same<T, double>::value ? 2 : 1) matmul_kernel(const MmDev d) {
+__device__ __forceinline__ void lds4(const T* p, T (&v)[4]) {
+  if constexpr (sizeof(T) == 4) {
+    const int4 x = *reinterpret_cast<const int4*>(p);
+    memcpy(v, &x, 16);
+  } else {
+    const int4 x = *reinterpret_cast<const int4*>(p);
+    const int4 y = *reinterpret_cast<const int4*>(p + 2);
+    memcpy(v, &x, 16);
+    memcpy(v + 2, &y, 16);
+  }
+}
+
+// Each thread owns rows {g * 64 + ty * 4 + i} and columns {h * 64 + tx * 4 + j}
+// of the tile (i, j < 4; g < TM / 4, h < TN / 4): its fragment reads are 4
+// consecutive elements, and the 16 threads of a row of the warp read one
+// contiguous run, so the shared-memory reads are conflict-free.
+template <class T>
+__global__ void __launch_bounds__(kThreads, TRS_MM_MINB) matmul_kernel(const MmDev d) {
   constexpr int TM = MmTile<T>::TM, TN = MmTile<T>::TN, BK = MmTile<T>::BK;
   constexpr int BM = 16 * TM, BN = 16 * TN;
+  constexpr int GM = TM / 4, GN = TN / 4;
   constexpr int LA = BM * BK / kThreads, LB = BN * BK / kThreads;
   constexpr int PAD = 16 / (int)sizeof(T);  // keeps each shared row 16-byte aligned
+  constexpr int ES = (int)sizeof(T);
   __shared__ __align__(16) T As[2][BK][BM + PAD];
   __shared__ __align__(16) T Bs[2][BK][BN + PAD];
   const T* ga = static_cast<const T*>(d.a);
@@ -91,12 +127,6 @@ __global__ void __launch_bounds__(kThreads, std::is_same<T, double>::value ? 2 :
   T* go = static_cast<T*>(d.out);
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
   const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
-  // slot q of this thread in a slab: element e = tid + q * 256, laid out so
-  // consecutive threads read consecutive addresses of the unit-stride dimension
-  auto a_row = [&](int q) { const int e = threadIdx.x + q * kThreads; return d.a_kfast ? e / BK : e % BM; };
-  auto a_kk = [&](int q) { const int e = threadIdx.x + q * kThreads; return d.a_kfast ? e % BK : e / BM; };
-  auto b_col = [&](int q) { const int e = threadIdx.x + q * kThreads; return d.b_nfast ? e % BN : e / BK; };
-  auto b_kk = [&](int q) { const int e = threadIdx.x + q * kThreads; return d.b_nfast ? e / BN : e % BK; };
 
   for (int64_t z = blockIdx.z; z < d.batches; z += gridDim.z) {
     int64_t ao = d.a_off, bo = d.b_off, oo = d.o_off;
@@ -110,60 +140,74 @@ __global__ void __launch_bounds__(kThreads, std::is_same<T, double>::value ? 2 :
         oo += c * d.o_bst[i];
       }
     }
-    T ra[LA], rb[LB];
-    auto fetch = [&](int64_t k0) {
+    // slab k0 of A and B into shared buffer `buf`: slot q of this thread is
+    // element e = tid + q * 256, laid out so consecutive threads read
+    // consecutive addresses of the unit-stride dimension
+    auto issue = [&](int64_t k0, int buf) {
 #pragma unroll
       for (int q = 0; q < LA; ++q) {
-        const int64_t row = m0 + a_row(q), k = k0 + a_kk(q);
-        ra[q] = (row < d.M && k < d.K) ? ga[ao + row * d.sam + k * d.sak] : T(0);
+        const int e = threadIdx.x + q * kThreads;
+        const int rr = d.a_kfast ? e / BK : e % BM, kk = d.a_kfast ? e % BK : e / BM;
+        const int64_t row = m0 + rr, k = k0 + kk;
+        const bool in = row < d.M && k < d.K;
+        cp_async_elem<ES>(&As[buf][kk][rr], in ? ga + ao + row * d.sam + k * d.sak : ga + d.a_off, in ? ES : 0);
       }
 #pragma unroll
       for (int q = 0; q < LB; ++q) {
-        const int64_t col = n0 + b_col(q), k = k0 + b_kk(q);
-        rb[q] = (col < d.N && k < d.K) ? gb[bo + k * d.sbk + col * d.sbn] : T(0);
+        const int e = threadIdx.x + q * kThreads;
+        const int cc = d.b_nfast ? e % BN : e / BK, kk = d.b_nfast ? e / BN : e % BK;
+        const int64_t col = n0 + cc, k = k0 + kk;
+        const bool in = col < d.N && k < d.K;
+        cp_async_elem<ES>(&Bs[buf][kk][cc], in ? gb + bo + k * d.sbk + col * d.sbn : gb + d.b_off, in ? ES : 0);
       }
-    };
-    auto stash = [&](int buf) {
-#pragma unroll
-      for (int q = 0; q < LA; ++q) As[buf][a_kk(q)][a_row(q)] = ra[q];
-#pragma unroll
-      for (int q = 0; q < LB; ++q) Bs[buf][b_kk(q)][b_col(q)] = rb[q];
+      cp_async_commit();
     };
 
     AccTile<T, TM, TN> acc;  // +0: T::default() of the reference
     acc.zero();
-    fetch(0);
     __syncthreads();  // the previous batch's last slab has been read
-    stash(0);
-    __syncthreads();
+    issue(0, 0);
     int buf = 0;
     for (int64_t k0 = 0; k0 < d.K; k0 += BK, buf ^= 1) {
       const bool more = k0 + BK < d.K;
-      if (more) fetch(k0 + BK);  // in flight while this slab is multiplied
+      if (more) {
+        issue(k0 + BK, buf ^ 1);  // in flight while this slab is multiplied
+        cp_async_wait_prev();
+      } else {
+        cp_async_wait_all();
+      }
+      __syncthreads();  // slab k0 is in shared memory for every thread
       const int kmax = d.K - k0 < BK ? (int)(d.K - k0) : BK;
 #pragma unroll
       for (int kk = 0; kk < BK; ++kk) {
         if (kk < kmax) {  // k walks 0 .. K-1 in order, one step per kk
           T av[TM], bv[TN];
 #pragma unroll
-          for (int i = 0; i < TM; ++i) av[i] = As[buf][kk][ty * TM + i];
+          for (int g = 0; g < GM; ++g) {
+            T v[4];
+            lds4<T>(&As[buf][kk][g * 64 + ty * 4], v);
 #pragma unroll
-          for (int j = 0; j < TN; ++j) bv[j] = Bs[buf][kk][tx * TN + j];
+            for (int i = 0; i < 4; ++i) av[g * 4 + i] = v[i];
+          }
+#pragma unroll
+          for (int h = 0; h < GN; ++h) {
+            T v[4];
+            lds4<T>(&Bs[buf][kk][h * 64 + tx * 4], v);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) bv[h * 4 + j] = v[j];
+          }
           acc.step(av, bv);
         }
       }
-      if (more) {
-        stash(buf ^ 1);
-        __syncthreads();
-      }
+      __syncthreads();  // every thread is done with `buf` before it is refilled
     }
 #pragma unroll
     for (int i = 0; i < TM; ++i) {
-      const int64_t row = m0 + ty * TM + i;
+      const int64_t row = m0 + (i / 4) * 64 + ty * 4 + (i % 4);
       if (row >= d.M) continue;
 #pragma unroll
       for (int j = 0; j < TN; ++j) {
-        const int64_t col = n0 + tx * TN + j;
+        const int64_t col = n0 + (j / 4) * 64 + tx * 4 + (j % 4);
         if (col < d.N) go[oo + row * d.som + col * d.son] = acc.get(i, j);
       }
     }
@@ -179,59 +223,113 @@ struct ColsDev {
   int64_t x_off, xs[4];   // the image ([B, C, H, W] view): unfold's input, fold's output
   int64_t c_off, cs[2];   // the columns ([B*OH*OW, C*kh*kw] view): unfold's output, fold's input
   int64_t patch, rows;
+  // 32-bit index decode (every index below 2^32): divisors of the decode
+  FastDiv f_patch, f_kk, f_kw, f_ow, f_oh, f_w, f_h, f_c, f_sh, f_sw;
 };
 
-// one thread per element of the columns, row-major
+// Columns elements (unfold) or image pixels (fold) per thread per iteration:
+// their loads are all issued before the first result is used, so each thread
+// keeps that many gathered loads in flight.
+constexpr int kColsU = 8;
+
+// Elements idx .. of the columns, row-major: row = (b, oh, ow), col = (c, i,
+// j); 32-bit decode with divisors fixed at launch.  Thread t of a block takes
+// elements base + u * kThreads (u < kColsU): coalesced stores.
 template <class T>
 __global__ void __launch_bounds__(kThreads) unfold_kernel(const ColsDev d) {
   const T* x = static_cast<const T*>(d.src);
   T* out = static_cast<T*>(d.dst);
-  const uint64_t n = (uint64_t)d.rows * (uint64_t)d.patch;
-  const uint64_t step = (uint64_t)gridDim.x * kThreads;
-  for (uint64_t idx = (uint64_t)blockIdx.x * kThreads + threadIdx.x; idx < n; idx += step) {
-    const int64_t row = (int64_t)(idx / (uint64_t)d.patch), col = (int64_t)(idx - (uint64_t)row * d.patch);
-    const int64_t ow = row % d.OW, oh = (row / d.OW) % d.OH, b = row / (d.OW * d.OH);
-    const int64_t kk = d.kh * d.kw;
-    const int64_t c = col / kk, r = col - c * kk, i = r / d.kw, j = r - (r / d.kw) * d.kw;
-    const int64_t y = oh * d.sh + i - d.ph, xx = ow * d.sw + j - d.pw;
-    T v = T(0);
-    if (y >= 0 && y < d.H && xx >= 0 && xx < d.W)
-      v = x[d.x_off + b * d.xs[0] + c * d.xs[1] + y * d.xs[2] + xx * d.xs[3]];
-    out[d.c_off + row * d.cs[0] + col * d.cs[1]] = v;
+  const uint32_t n = (uint32_t)(d.rows * d.patch);
+  const int32_t H = (int32_t)d.H, W = (int32_t)d.W;
+  const uint32_t step = gridDim.x * (kThreads * kColsU);
+  for (uint32_t base = blockIdx.x * (kThreads * kColsU) + threadIdx.x; base < n; base += step) {
+    T v[kColsU];
+    uint32_t at[kColsU];
+#pragma unroll
+    for (int u = 0; u < kColsU; ++u) {
+      const uint32_t idx = base + (uint32_t)u * kThreads;
+      at[u] = idx;
+      v[u] = T(0);
+      if (idx < n) {
+        const uint32_t row = fdiv(idx, d.f_patch), col = idx - row * d.f_patch.d;
+        const uint32_t r1 = fdiv(row, d.f_ow), ow = row - r1 * d.f_ow.d;
+        const uint32_t b = fdiv(r1, d.f_oh), oh = r1 - b * d.f_oh.d;
+        const uint32_t c = fdiv(col, d.f_kk), r = col - c * d.f_kk.d;
+        const uint32_t i = fdiv(r, d.f_kw), j = r - i * d.f_kw.d;
+        const int32_t y = (int32_t)(oh * (uint32_t)d.sh + i) - (int32_t)d.ph;
+        const int32_t xx = (int32_t)(ow * (uint32_t)d.sw + j) - (int32_t)d.pw;
+        if (y >= 0 && y < H && xx >= 0 && xx < W)
+          v[u] = x[d.x_off + (int64_t)b * d.xs[0] + (int64_t)c * d.xs[1] + (int64_t)y * d.xs[2] +
+                   (int64_t)xx * d.xs[3]];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kColsU; ++u) {
+      if (at[u] < n) {
+        const uint32_t row = fdiv(at[u], d.f_patch), col = at[u] - row * d.f_patch.d;
+        out[d.c_off + (int64_t)row * d.cs[0] + (int64_t)col * d.cs[1]] = v[u];
+      }
+    }
   }
 }
 
-// one thread per output pixel (b, c, y, x), row-major
-template <class T>
+// One thread per output pixel (b, c, y, x), row-major: adds the values of the
+// windows covering the pixel, windows by increasing (oh, ow), from +0.  When
+// at most kFoldRegs windows can cover a pixel (ceil(kh / sh) * ceil(kw / sw),
+// every usual convolution), the values are all loaded before the first
+// addition; otherwise they are added as they are loaded.
+constexpr int kFoldRegs = 16;
+
+template <class T, bool REGS>
 __global__ void __launch_bounds__(kThreads) fold_kernel(const ColsDev d) {
   using A = Arith<T>;
   const T* cols = static_cast<const T*>(d.src);
   T* out = static_cast<T*>(d.dst);
-  const uint64_t n = (uint64_t)(d.B * d.C * d.H * d.W);
-  const uint64_t step = (uint64_t)gridDim.x * kThreads;
-  for (uint64_t idx = (uint64_t)blockIdx.x * kThreads + threadIdx.x; idx < n; idx += step) {
-    const int64_t xx = (int64_t)(idx % (uint64_t)d.W);
-    const int64_t y = (int64_t)((idx / (uint64_t)d.W) % (uint64_t)d.H);
-    const int64_t c = (int64_t)((idx / (uint64_t)(d.W * d.H)) % (uint64_t)d.C);
-    const int64_t b = (int64_t)(idx / (uint64_t)(d.W * d.H * d.C));
-    // windows whose row range holds y: oh * sh <= y + ph <= oh * sh + kh - 1
-    const int64_t yp = y + d.ph, xp = xx + d.pw;
-    int64_t oh_lo = yp - d.kh + 1 <= 0 ? 0 : (yp - d.kh + d.sh) / d.sh;
-    int64_t oh_hi = yp / d.sh;
-    if (oh_hi > d.OH - 1) oh_hi = d.OH - 1;
-    int64_t ow_lo = xp - d.kw + 1 <= 0 ? 0 : (xp - d.kw + d.sw) / d.sw;
-    int64_t ow_hi = xp / d.sw;
-    if (ow_hi > d.OW - 1) ow_hi = d.OW - 1;
+  const uint32_t n = (uint32_t)(d.B * d.C * d.H * d.W);
+  const int32_t kh = (int32_t)d.kh, kw = (int32_t)d.kw, sh = (int32_t)d.sh, sw = (int32_t)d.sw;
+  const int32_t OH = (int32_t)d.OH, OW = (int32_t)d.OW;
+  for (uint32_t idx = blockIdx.x * kThreads + threadIdx.x; idx < n; idx += gridDim.x * kThreads) {
+    const uint32_t q1 = fdiv(idx, d.f_w), xx = idx - q1 * d.f_w.d;
+    const uint32_t q2 = fdiv(q1, d.f_h), y = q1 - q2 * d.f_h.d;
+    const uint32_t b = fdiv(q2, d.f_c), c = q2 - b * d.f_c.d;
+    // windows whose rows hold y: oh * sh <= y + ph <= oh * sh + kh - 1
+    const int32_t yp = (int32_t)y + (int32_t)d.ph, xp = (int32_t)xx + (int32_t)d.pw;
+    const int32_t oh_lo = yp - kh + 1 <= 0 ? 0 : (int32_t)fdiv((uint32_t)(yp - kh + sh), d.f_sh);
+    int32_t oh_hi = (int32_t)fdiv((uint32_t)yp, d.f_sh);
+    if (oh_hi > OH - 1) oh_hi = OH - 1;
+    const int32_t ow_lo = xp - kw + 1 <= 0 ? 0 : (int32_t)fdiv((uint32_t)(xp - kw + sw), d.f_sw);
+    int32_t ow_hi = (int32_t)fdiv((uint32_t)xp, d.f_sw);
+    if (ow_hi > OW - 1) ow_hi = OW - 1;
+    const int32_t nw = ow_hi - ow_lo + 1;
+    auto at = [&](int32_t oh, int32_t ow) {
+      const int32_t i = yp - oh * sh, j = xp - ow * sw;
+      const int64_t row = ((int64_t)b * OH + oh) * OW + ow, col = ((int64_t)c * kh + i) * kw + j;
+      return d.c_off + row * d.cs[0] + col * d.cs[1];
+    };
     T acc = T(0);
-    for (int64_t oh = oh_lo; oh <= oh_hi; ++oh) {
-      const int64_t i = yp - oh * d.sh;
-      for (int64_t ow = ow_lo; ow <= ow_hi; ++ow) {
-        const int64_t j = xp - ow * d.sw;
-        const int64_t row = (b * d.OH + oh) * d.OW + ow, col = (c * d.kh + i) * d.kw + j;
-        acc = A::add(acc, cols[d.c_off + row * d.cs[0] + col * d.cs[1]]);
+    if constexpr (REGS) {
+      const int32_t cnt = (oh_hi >= oh_lo && nw > 0) ? (oh_hi - oh_lo + 1) * nw : 0;
+      T v[kFoldRegs];
+      int32_t oh = oh_lo, ow = ow_lo;  // window w = (oh, ow), row-major over the covering range
+#pragma unroll
+      for (int w = 0; w < kFoldRegs; ++w) {
+        v[w] = T(0);
+        if (w < cnt) {
+          v[w] = cols[at(oh, ow)];
+          if (++ow > ow_hi) {
+            ow = ow_lo;
+            ++oh;
+          }
+        }
       }
+#pragma unroll
+      for (int w = 0; w < kFoldRegs; ++w)
+        if (w < cnt) acc = A::add(acc, v[w]);  // windows in (oh, ow) order
+    } else {
+      for (int32_t oh = oh_lo; oh <= oh_hi; ++oh)
+        for (int32_t ow = ow_lo; ow <= ow_hi; ++ow) acc = A::add(acc, cols[at(oh, ow)]);
     }
-    out[d.x_off + b * d.xs[0] + c * d.xs[1] + y * d.xs[2] + xx * d.xs[3]] = acc;
+    out[d.x_off + (int64_t)b * d.xs[0] + (int64_t)c * d.xs[1] + (int64_t)y * d.xs[2] + (int64_t)xx * d.xs[3]] = acc;
   }
 }
 
@@ -373,6 +471,25 @@ Error cols_setup(const char* fn, const trs_view* img, int64_t kh, int64_t kw, in
   d->rows = d->B * d->OH * d->OW;
   d->x_off = img->offset;
   for (int i = 0; i < 4; ++i) d->xs[i] = img->strides[i];
+  // the kernels decode indices in 32 bits
+  const uint64_t lim = 1ull << 32;
+  if ((uint64_t)d->rows * (uint64_t)d->patch >= lim || (uint64_t)(d->B * d->C * H * W) >= lim ||
+      (uint64_t)(H + 2 * ph) >= lim || (uint64_t)(W + 2 * pw) >= lim)
+    return make_error(TRS_ERR_SHAPE, "!!!" + f + "(): more than 2^32 - 1 elements!!!");
+  if (d->patch > 0 && d->rows > 0) {
+    d->f_patch = make_fastdiv((uint32_t)d->patch);
+    d->f_kk = make_fastdiv((uint32_t)(kh * kw > 0 ? kh * kw : 1));
+    d->f_kw = make_fastdiv((uint32_t)(kw > 0 ? kw : 1));
+    d->f_ow = make_fastdiv((uint32_t)d->OW);
+    d->f_oh = make_fastdiv((uint32_t)d->OH);
+  }
+  if (H > 0 && W > 0 && d->C > 0) {
+    d->f_w = make_fastdiv((uint32_t)W);
+    d->f_h = make_fastdiv((uint32_t)H);
+    d->f_c = make_fastdiv((uint32_t)d->C);
+  }
+  d->f_sh = make_fastdiv((uint32_t)sh);
+  d->f_sw = make_fastdiv((uint32_t)sw);
   return Error{};
 }
 
@@ -384,14 +501,21 @@ unsigned cols_grid(const void* kernel, uint64_t items) {
 
 template <class T>
 Error launch_cols(bool unfold, const ColsDev& d, cudaStream_t stream) {
-  const void* k = unfold ? (const void*)unfold_kernel<T> : (const void*)fold_kernel<T>;
-  const uint64_t items = unfold ? (uint64_t)d.rows * (uint64_t)d.patch : (uint64_t)(d.B * d.C * d.H * d.W);
+  // windows that can cover one pixel: ceil(kh / sh) * ceil(kw / sw)
+  const int64_t cover = ((d.kh + d.sh - 1) / d.sh) * ((d.kw + d.sw - 1) / d.sw);
+  const bool regs = cover <= kFoldRegs;
+  const void* k = unfold ? (const void*)unfold_kernel<T>
+                         : (regs ? (const void*)fold_kernel<T, true> : (const void*)fold_kernel<T, false>);
+  const uint64_t items = unfold ? ((uint64_t)d.rows * (uint64_t)d.patch + kColsU - 1) / kColsU
+                                : (uint64_t)(d.B * d.C * d.H * d.W);
   if (items == 0) return Error{};
   const unsigned g = cols_grid(k, items);
   if (unfold)
     unfold_kernel<T><<<g, kThreads, 0, stream>>>(d);
+  else if (regs)
+    fold_kernel<T, true><<<g, kThreads, 0, stream>>>(d);
   else
-    fold_kernel<T><<<g, kThreads, 0, stream>>>(d);
+    fold_kernel<T, false><<<g, kThreads, 0, stream>>>(d);
   return check_launch(unfold ? "unfold_2d kernel" : "fold_2d kernel");
 }
 

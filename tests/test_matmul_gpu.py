@@ -129,6 +129,8 @@ COL_CASES = [  # shape, kernel, stride, padding
     ([2, 3, 9, 11], (3, 2), (2, 3), (0, 1)), ([1, 4, 8, 8], (1, 1), (1, 1), (0, 0)),
     ([3, 2, 7, 5], (5, 5), (2, 2), (2, 2)), ([2, 16, 14, 14], (3, 3), (2, 2), (1, 1)),
     ([1, 1, 4, 4], (4, 4), (3, 3), (0, 0)), ([1, 2, 5, 6], (2, 3), (1, 1), (3, 2)),
+    # more than 16 windows cover a pixel: fold adds them as it loads them
+    ([1, 2, 9, 9], (5, 5), (1, 1), (2, 2)), ([2, 1, 12, 7], (7, 3), (1, 1), (3, 1)),
 ]
 
 
