@@ -625,6 +625,9 @@ def suite_groups(lib, abi, device, torch):
     groups.append(SuiteGroup("callers", make_mm, [
         ("matmul [4096,4096] x [4096,4096] f32, reference order", 3 * mm * mm * 4,
          lambda s: C(lib.trs_matmul(ref(s["v"]["A"]), ref(s["v"]["B"]), ref(s["v"]["C"]), sh)), 2 * mm ** 3),
+        ("matmul_tf32x3 [4096,4096] x [4096,4096] f32, tensor cores", 3 * mm * mm * 4,
+         lambda s: C(lib.trs_matmul_tf32x3(ref(s["v"]["A"]), ref(s["v"]["B"]), ref(s["v"]["C"]), sh)),
+         2 * mm ** 3, "tc"),
     ]))
     cN, cC, cH, cW = 32, 64, 56, 56
     crow, cpatch = cN * cH * cW, cC * 9
@@ -641,6 +644,18 @@ def suite_groups(lib, abi, device, torch):
          lambda s: C(lib.trs_fold_2d(ref(s["v"]["K"]), 3, 3, 1, 1, 1, 1, ref(s["v"]["Y"]), sh))),
     ]))
     return groups
+
+
+def tf32_tensor_peak() -> float:
+    """Dense TF32 tensor-core operations per second: half the measured bf16
+    rate (MEASURED_PEAKS.json bf16_tflops; TF32 runs at half the bf16 rate)."""
+    tf = 1679.4
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        tf = float(json.loads(p.read_text()).get("bf16_tflops", tf))
+    except (OSError, ValueError):
+        pass
+    return tf * 1e12 / 2
 
 
 def fp32_lane_peak() -> float:
@@ -746,10 +761,17 @@ def run_suite_entries(args, only=None, steady=True, flushed_reps=5, warm=2):
             if flops:  # a contraction: its roofline is compute, not HBM
                 ms = rec.get("us_steady", rec["us_flushed"]) / 1e3
                 tf = flops / (ms * 1e-3) / 1e12
-                rec.update({"flops": int(flops), "TFLOPs": round(tf, 2), "frac": round(tf * 1e12 / fp32_lane_peak(), 4),
-                            "bound": "fp32 CUDA cores (separately rounded multiply and add)"})
+                if len(entry) > 4 and entry[4] == "tc":
+                    # three TF32 products per multiply-add (hi*hi, hi*lo, lo*hi)
+                    peak_ops, hw = tf32_tensor_peak(), 3.0
+                    bound = "tensor cores (tcgen05 kind::tf32, three products per multiply-add)"
+                else:
+                    peak_ops, hw = fp32_lane_peak(), 1.0
+                    bound = "fp32 CUDA cores (separately rounded multiply and add)"
+                rec.update({"flops": int(flops), "TFLOPs": round(tf, 2), "frac": round(hw * tf * 1e12 / peak_ops, 4),
+                            "bound": bound})
                 rec.pop("GBps", None)
-                rec["frac_flushed"] = round(flops / (ms_f * 1e-3) / fp32_lane_peak(), 4)
+                rec["frac_flushed"] = round(hw * flops / (ms_f * 1e-3) / peak_ops, 4)
             tr = traffic.get(name)
             rec["dram_ratio"] = round(tr / nbytes, 3) if tr else None
             out.append(rec)

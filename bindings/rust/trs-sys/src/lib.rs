@@ -143,6 +143,7 @@ extern "C" {
     pub fn trs_avg_pool2d(x: *const trs_view, kh: i64, kw: i64, sh: i64, sw: i64, out_: *mut trs_view, stream: trs_stream) -> trs_status;
     pub fn trs_max_pool2d_backward(x: *const trs_view, grad_out: *const trs_view, kh: i64, kw: i64, sh: i64, sw: i64, accumulate: i32, grad_x: *mut trs_view, stream: trs_stream) -> trs_status;
     pub fn trs_matmul(a: *const trs_view, b: *const trs_view, out_: *mut trs_view, stream: trs_stream) -> trs_status;
+    pub fn trs_matmul_tf32x3(a: *const trs_view, b: *const trs_view, out_: *mut trs_view, stream: trs_stream) -> trs_status;
     pub fn trs_unfold_2d(x: *const trs_view, kh: i64, kw: i64, sh: i64, sw: i64, ph: i64, pw: i64, out_: *mut trs_view, stream: trs_stream) -> trs_status;
     pub fn trs_fold_2d(cols: *const trs_view, kh: i64, kw: i64, sh: i64, sw: i64, ph: i64, pw: i64, out_: *mut trs_view, stream: trs_stream) -> trs_status;
     pub fn trs_fill_uniform(out_: *mut trs_view, seed: u64, first: u64, lo: f64, hi: f64, stream: trs_stream) -> trs_status;

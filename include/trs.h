@@ -406,6 +406,19 @@ trs_status trs_max_pool2d_backward(const trs_view* x, const trs_view* grad_out,
 trs_status trs_matmul(const trs_view* a, const trs_view* b, trs_view* out,
                       trs_stream stream);
 
+/* Tensor::matmul (linalg/tensor/base.rs:896-1013) for f32 on the tensor cores
+ * (tcgen05, TF32 inputs): shapes, broadcasting, views and panics as
+ * trs_matmul, but not bit-identical.  Each operand is split into two TF32
+ * parts (hi = x with its 13 low mantissa bits cleared, lo = x - hi) and every
+ * product taken as hi*hi + hi*lo + lo*hi, accumulated in f32 by the tensor
+ * cores in their own order: finite results are within about the rounding
+ * error of an f32 sum of the products (the tests hold them to
+ * 1e-5 * sum_k |a_ik b_kj| of the reference's).  Infinities and NaNs
+ * propagate, without the reference's exact special-value rules.  Scratch for
+ * the split operands comes from the stream-ordered pool. */
+trs_status trs_matmul_tf32x3(const trs_view* a, const trs_view* b, trs_view* out,
+                             trs_stream stream);
+
 /* Tensor::unfold_2d (linalg/tensor/conv.rs:360-418): every (kh, kw) window of
  * x [B, C, H, W] (stride (sh, sw), zero padding (ph, pw) on each side) as one
  * row of out [B * OH * OW, C * kh * kw], rows in (b, oh, ow) order, each row

@@ -108,6 +108,7 @@ _SIGNATURES = {
     "trs_avg_pool2d": (c_int32, [_V, c_int64, c_int64, c_int64, c_int64, _V, c_void_p]),
     "trs_max_pool2d_backward": (c_int32, [_V, _V, c_int64, c_int64, c_int64, c_int64, c_int32, _V, c_void_p]),
     "trs_matmul": (c_int32, [_V, _V, _V, c_void_p]),
+    "trs_matmul_tf32x3": (c_int32, [_V, _V, _V, c_void_p]),
     "trs_unfold_2d": (c_int32, [_V, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, _V, c_void_p]),
     "trs_fold_2d": (c_int32, [_V, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, _V, c_void_p]),
     "trs_fill_uniform": (c_int32, [_V, c_uint64, c_uint64, c_double, c_double, c_void_p]),

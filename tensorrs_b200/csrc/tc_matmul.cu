@@ -1,0 +1,514 @@
+// tc_matmul.cu -- trs_matmul_tf32x3: Tensor::matmul (linalg/tensor/base.rs:
+// 896-1013) for f32 on the 5th-generation tensor cores, within the sum
+// tolerance instead of bit-identical.
+//
+// trs_matmul keeps the reference's per-output chain of separately rounded
+// multiplies and adds on the CUDA cores.  This variant trades that for the
+// tensor cores' rate: each f32 operand x is split into two TF32 values,
+// hi = x with its 13 low mantissa bits cleared and lo = x - hi (exact in f32;
+// the tensor core reads its top 19 bits), and every product is taken as
+// hi*hi + hi*lo + lo*hi (the lo*lo term, below 2^-21 of the product, is
+// dropped), accumulated in f32 in tensor memory.  Products keep about 21 bits;
+// the accumulation order and rounding are the tensor core's, so a result
+// differs from the reference's sequential chain by about the rounding error of
+// an f32 sum: the tests hold it to |gpu - ref| <= 1e-5 * sum_k |a_ik b_kj|.
+//
+// Data flow:
+//   1. tf32_split_kernel packs A into hi/lo arrays [A batches][Mp][Kp] and B
+//      into [B batches][Np][Kp] (K contiguous: both operands K-major for the
+//      MMA), zero-padded to multiples of 128 rows and 32 k, through 32 x 32
+//      shared-memory tiles so that both the strided reads and the writes are
+//      coalesced (scratch from the stream-ordered pool);
+//   2. tc_gemm_kernel: one CTA of 4 warps per 128 x 128 output tile.  Thread 0
+//      streams 32-deep k slabs of the four operand tiles (16 KiB each) into a
+//      3-stage ring with TMA (cp.async.bulk.tensor.2d, 128-byte swizzle, no
+//      multicast), completing on a `full` mbarrier; thread 32 waits for a slab
+//      and issues, for each of its 4 k-steps of 8, the three tcgen05.mma
+//      kind::tf32 (M 128, N 128) into one f32 accumulator of 128 TMEM columns,
+//      then tcgen05.commit frees the slab through its `empty` mbarrier; a final
+//      commit signals `done`, and all 4 warps read their 32 accumulator rows
+//      with tcgen05.ld and write them through the output view.
+// Every mbarrier wait is bounded (kWaitIters polls); a wait that runs out
+// sets the async-error word and the CTA skips ahead to free its tensor
+// memory and return.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "kernels.cuh"
+
+namespace trs {
+namespace {
+
+constexpr int kTcBM = 128, kTcBN = 128, kTcBK = 32, kTcStages = 3;
+constexpr uint32_t kTcTile = kTcBM * kTcBK * 4;      // one operand tile of a slab: 16 KiB
+constexpr uint32_t kTcStage = 4 * kTcTile;           // A hi, A lo, B hi, B lo
+constexpr uint32_t kTcSmem = kTcStages * kTcStage + 1024 + 256;  // + alignment slack + barriers
+constexpr uint32_t kTcCols = 128;                    // TMEM columns of the f32 accumulator
+
+// ---- the split / pack kernel -------------------------------------------------
+
+struct SplitDev {
+  const float* src;
+  float* hi;
+  float* lo;
+  int64_t rows, K;       // logical rows (M for A, N for B) and depth
+  int64_t rows_p, Kp;    // padded
+  int64_t s_row, s_k;    // source strides of a row and of k
+  int64_t off;           // source offset
+  int nb;                // batch dimensions of this operand
+  int64_t bshape[kMaxDims], bst[kMaxDims];
+  int k_fast;            // the source is unit-stride along k
+};
+
+__device__ __forceinline__ void tf32_split(float x, float* h, float* l) {
+  if (!isfinite(x)) {  // inf / NaN carried by hi alone
+    *h = x;
+    *l = 0.0f;
+    return;
+  }
+  const float hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+  *h = hi;
+  *l = __fsub_rn(x, hi);  // exact
+}
+
+// grid: (Kp / 32, rows_p / 32, batches); block 32 x 8
+__global__ void __launch_bounds__(256) tf32_split_kernel(const SplitDev d) {
+  __shared__ float tile[32][33];
+  const int64_t bt = blockIdx.z;
+  int64_t off = d.off;
+  {
+    int64_t r = bt;
+    for (int i = d.nb - 1; i >= 0; --i) {
+      off += (r % d.bshape[i]) * d.bst[i];
+      r /= d.bshape[i];
+    }
+  }
+  const int64_t k0 = (int64_t)blockIdx.x * 32, r0 = (int64_t)blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  for (int q = ty; q < 32; q += 8) {
+    // read along the source's unit-stride dimension
+    const int64_t r = d.k_fast ? r0 + q : r0 + tx, k = d.k_fast ? k0 + tx : k0 + q;
+    float v = 0.0f;
+    if (r < d.rows && k < d.K) v = d.src[off + r * d.s_row + k * d.s_k];
+    if (d.k_fast)
+      tile[q][tx] = v;
+    else
+      tile[tx][q] = v;
+  }
+  __syncthreads();
+  for (int q = ty; q < 32; q += 8) {
+    const int64_t r = r0 + q, k = k0 + tx;
+    float h, l;
+    tf32_split(tile[q][tx], &h, &l);
+    const int64_t at = (bt * d.rows_p + r) * d.Kp + k;
+    d.hi[at] = h;
+    d.lo[at] = l;
+  }
+}
+
+// +0 into every element of a view (row-major over its shape).
+__global__ void __launch_bounds__(256) zero_view_kernel(const trs_view v, int64_t n) {
+  float* o = static_cast<float*>(v.data);
+  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (int64_t)gridDim.x * 256) {
+    int64_t r = i, at = v.offset;
+    for (int dd = v.ndim - 1; dd >= 0; --dd) {
+      at += (r % v.shape[dd]) * v.strides[dd];
+      r /= v.shape[dd];
+    }
+    o[at] = 0.0f;
+  }
+}
+
+// ---- tcgen05 / TMA primitives ---------------------------------------------------
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem, K-major] * B[smem, K-major]^T, M 128, N 128, K 8 (tf32).
+__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+
+// Arrives on `bar` once every tcgen05.mma this thread issued before has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 consecutive accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile with 128-byte swizzle:
+// rows of 128 bytes, 8-row groups 1024 bytes apart (SBO), leading offset
+// unused (1), descriptor version 1, layout SWIZZLE_128B (2); the tile starts
+// on a 1024-byte boundary, so the base offset is 0.
+__device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
+  const uint64_t a = (uint64_t)(smem_u32(tile) >> 4) & 0x3FFFull;
+  return a | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor: D f32, A and B tf32, both K-major, N 128, M 128.
+constexpr uint32_t kTf32Idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(kTcBN >> 3) << 17) |
+                                ((uint32_t)(kTcBM >> 4) << 24);
+
+struct TcDev {
+  int64_t M, N, Kp, Mp, Np;
+  void* out;
+  int64_t o_off, som, son;
+  int nb;  // output batch dimensions
+  int64_t bshape[kMaxDims], o_bst[kMaxDims];
+  int64_t a_bidx[kMaxDims], b_bidx[kMaxDims];  // per output batch dim: stride in the operand's packed batch index
+  int* err;
+};
+
+__global__ void __launch_bounds__(128, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap t_ahi, const __grid_constant__ CUtensorMap t_alo,
+               const __grid_constant__ CUtensorMap t_bhi, const __grid_constant__ CUtensorMap t_blo,
+               const TcDev d) {
+  extern __shared__ unsigned char tc_smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTcStages * kTcStage);
+  uint64_t* empty = full + kTcStages;
+  uint64_t* done = empty + kTcStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  int* failed = reinterpret_cast<int*>(tmem_slot + 1);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    *failed = 0;
+    fence_mbar_init();
+  }
+  __syncwarp();  // warp 0 converged for the warp-collective allocation
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, kTcCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // this CTA's rows in the packed operands: batch index of A and of B
+  int64_t abt = 0, bbt = 0, oo = d.o_off;
+  {
+    int64_t r = blockIdx.z;
+    for (int i = d.nb - 1; i >= 0; --i) {
+      const int64_t c = r % d.bshape[i];
+      r /= d.bshape[i];
+      abt += c * d.a_bidx[i];
+      bbt += c * d.b_bidx[i];
+      oo += c * d.o_bst[i];
+    }
+  }
+  const int32_t a_row = (int32_t)(abt * d.Mp + (int64_t)blockIdx.y * kTcBM);
+  const int32_t b_row = (int32_t)(bbt * d.Np + (int64_t)blockIdx.x * kTcBN);
+  const int nk = (int)(d.Kp / kTcBK);
+
+  if (threadIdx.x == 0) {  // TMA producer
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % kTcStages;
+      const uint32_t ph = (uint32_t)(kb / kTcStages) & 1u;
+      if (kb >= kTcStages && !mbar_wait(&empty[s], ph ^ 1u)) {
+        atomicExch(failed, 1);
+        break;
+      }
+      if (*(volatile int*)failed) break;
+      unsigned char* st = smem + s * kTcStage;
+      mbar_arrive_expect_tx(&full[s], kTcStage);
+      const int32_t kx = kb * kTcBK;
+      tma_load_2d(st, &t_ahi, kx, a_row, &full[s]);
+      tma_load_2d(st + kTcTile, &t_alo, kx, a_row, &full[s]);
+      tma_load_2d(st + 2 * kTcTile, &t_bhi, kx, b_row, &full[s]);
+      tma_load_2d(st + 3 * kTcTile, &t_blo, kx, b_row, &full[s]);
+    }
+  } else if (threadIdx.x == 32) {  // MMA issuer
+    bool ok = true;
+    for (int kb = 0; kb < nk && ok; ++kb) {
+      const int s = kb % kTcStages;
+      const uint32_t ph = (uint32_t)(kb / kTcStages) & 1u;
+      if (!mbar_wait(&full[s], ph)) {
+        atomicExch(failed, 1);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      unsigned char* st = smem + s * kTcStage;
+      const uint64_t ahi = sw128_desc(st), alo = sw128_desc(st + kTcTile);
+      const uint64_t bhi = sw128_desc(st + 2 * kTcTile), blo = sw128_desc(st + 3 * kTcTile);
+#pragma unroll
+      for (int k = 0; k < kTcBK / 8; ++k) {
+        const uint64_t dk = (uint64_t)(k * 2);  // 8 tf32 = 32 bytes, in 16-byte units
+        umma_tf32(tmem, ahi + dk, bhi + dk, kTf32Idesc, (kb > 0 || k > 0) ? 1u : 0u);
+        umma_tf32(tmem, ahi + dk, blo + dk, kTf32Idesc, 1u);
+        umma_tf32(tmem, alo + dk, bhi + dk, kTf32Idesc, 1u);
+      }
+      umma_commit(&empty[s]);  // the slab is free once these have read it
+    }
+    umma_commit(done);  // every MMA issued above has completed
+  }
+
+  // epilogue: warp w reads accumulator rows 32w .. 32w + 31 (its TMEM lanes)
+  const bool ready = mbar_wait(done, 0);
+  // tcgen05.ld is warp-collective: the whole warp takes one branch
+  const bool go = __all_sync(0xffffffffu, ready && !*(volatile int*)failed);
+  tc_fence_after();
+  if (!go) {
+    if (lane == 0 && d.err) atomicOr(d.err, kAsyncWaitTimeout);
+  } else {
+    float* out = static_cast<float*>(d.out);
+    const int64_t row = (int64_t)blockIdx.y * kTcBM + warp * 32 + lane;
+#pragma unroll 1
+    for (int c = 0; c < kTcBN / 32; ++c) {
+      uint32_t v[32];
+      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(c * 32), v);
+      if (row < d.M) {
+        const int64_t col0 = (int64_t)blockIdx.x * kTcBN + c * 32;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < d.N) out[oo + row * d.som + (col0 + j) * d.son] = __uint_as_float(v[j]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kTcCols);
+}
+
+// ---- host side -------------------------------------------------------------------
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn(Error* err) {
+  static std::once_flag once;
+  static EncodeTiled fn = nullptr;
+  static std::string why;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+    else
+      why = "cuTensorMapEncodeTiled is not available from the driver";
+    cudaGetLastError();
+  });
+  if (!fn) *err = make_error(TRS_ERR_UNAVAILABLE, why);
+  return fn;
+}
+
+// [batches * rows_p, Kp] f32, K contiguous, 32 x 128 boxes with 128-byte swizzle.
+Error make_map(EncodeTiled enc, CUtensorMap* map, float* base, int64_t rows_total, int64_t Kp) {
+  const cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)rows_total};
+  const cuuint64_t strides[1] = {(cuuint64_t)Kp * 4};
+  const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)kTcBM};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return make_error(TRS_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return Error{};
+}
+
+bool views_overlap(const trs_view* a, const trs_view* b) {
+  if (numel_of(a->shape, a->ndim) == 0 || numel_of(b->shape, b->ndim) == 0) return false;
+  auto range = [](const trs_view* v, int64_t* lo, int64_t* hi) {
+    int64_t l = v->offset, h = v->offset;
+    for (int i = 0; i < v->ndim; ++i) {
+      const int64_t span = (v->shape[i] - 1) * v->strides[i];
+      if (span > 0) h += span; else l += span;
+    }
+    *lo = (int64_t)(uintptr_t)v->data + l * 4;
+    *hi = (int64_t)(uintptr_t)v->data + (h + 1) * 4;
+  };
+  int64_t alo, ahi, blo, bhi;
+  range(a, &alo, &ahi);
+  range(b, &blo, &bhi);
+  return alo < bhi && blo < ahi;
+}
+
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+Error run_tc_matmul(const trs_view* a, const trs_view* b, const trs_view* out, cudaStream_t stream) {
+  Error e = validate_view(a, "a");
+  if (!e.ok()) return e;
+  e = validate_view(b, "b");
+  if (!e.ok()) return e;
+  e = validate_view(out, "output");
+  if (!e.ok()) return e;
+  if (a->dtype != TRS_F32 || b->dtype != TRS_F32 || out->dtype != TRS_F32)
+    return make_error(TRS_ERR_DTYPE, "matmul_tf32x3: f32 operands and output only");
+  const int an = a->ndim, bn = b->ndim;
+  if (an < 2 || bn < 2) return make_error(TRS_ERR_SHAPE, "matmul: both tensors must be at least 2D");
+  const int64_t M = a->shape[an - 2], K = a->shape[an - 1], N = b->shape[bn - 1];
+  if (K != b->shape[bn - 2])
+    return make_error(TRS_ERR_SHAPE, "matmul: inner dimensions must match (A.shape[-1] == B.shape[-2])");
+  int64_t batch[kMaxDims];
+  int nb = 0;
+  if (!broadcast_shapes(a->shape, an - 2, b->shape, bn - 2, batch, &nb))
+    return make_error(TRS_ERR_SHAPE, "matmul: batch shapes not broadcastable");
+  bool same = out->ndim == nb + 2 && out->shape[nb] == M && out->shape[nb + 1] == N;
+  for (int i = 0; same && i < nb; ++i) same = out->shape[i] == batch[i];
+  if (!same) return make_error(TRS_ERR_SHAPE, "matmul_tf32x3: the output must have the shape [batch..., M, N]");
+  if (views_overlap(out, a) || views_overlap(out, b))
+    return make_error(TRS_ERR_ALIAS, "matmul_tf32x3: the output overlaps an input");
+  int64_t batches = 1;
+  for (int i = 0; i < nb; ++i) batches *= batch[i];
+  if (M == 0 || N == 0 || batches == 0) return Error{};
+  const int64_t Mp = round_up(M, kTcBM), Np = round_up(N, kTcBN), Kp = round_up(K, kTcBK);
+  // each operand packed over its own batch dimensions
+  SplitDev sa, sb;
+  std::memset(&sa, 0, sizeof(sa));
+  std::memset(&sb, 0, sizeof(sb));
+  int64_t a_batches = 1, b_batches = 1;
+  for (int i = 0; i < an - 2; ++i) a_batches *= a->shape[i];
+  for (int i = 0; i < bn - 2; ++i) b_batches *= b->shape[i];
+  if (K == 0) {  // every output is the empty chain's +0
+    zero_view_kernel<<<(unsigned)((batches * M * N + 255) / 256 < 65535 ? (batches * M * N + 255) / 256 : 65535), 256,
+                       0, stream>>>(*out, batches * M * N);
+    return check_launch("matmul zero fill");
+  }
+  if (Kp >= (1ll << 31) || a_batches * Mp >= (1ll << 31) || b_batches * Np >= (1ll << 31) || Mp / 32 > 65535 ||
+      Np / 32 > 65535)
+    return make_error(TRS_ERR_SHAPE, "matmul_tf32x3: operands beyond 2^31 packed rows or 2 M rows per batch");
+  TcDev td;
+  std::memset(&td, 0, sizeof(td));
+  td.M = M;
+  td.N = N;
+  td.Kp = Kp;
+  td.Mp = Mp;
+  td.Np = Np;
+  td.out = out->data;
+  td.o_off = out->offset;
+  td.som = out->strides[nb];
+  td.son = out->strides[nb + 1];
+  td.nb = nb;
+  td.err = async_error_word();
+  {
+    // strides of each output batch dimension in A's and B's packed batch index
+    int64_t sa_step = 1, sb_step = 1;
+    int64_t a_step[kMaxDims] = {}, b_step[kMaxDims] = {};
+    for (int i = an - 3; i >= 0; --i) { a_step[i] = sa_step; sa_step *= a->shape[i]; }
+    for (int i = bn - 3; i >= 0; --i) { b_step[i] = sb_step; sb_step *= b->shape[i]; }
+    for (int i = 0; i < nb; ++i) {
+      td.bshape[i] = batch[i];
+      td.o_bst[i] = out->strides[i];
+      const int ia = i - (nb - (an - 2)), ib = i - (nb - (bn - 2));
+      td.a_bidx[i] = (ia >= 0 && a->shape[ia] != 1) ? a_step[ia] : 0;
+      td.b_bidx[i] = (ib >= 0 && b->shape[ib] != 1) ? b_step[ib] : 0;
+    }
+  }
+  EncodeTiled enc = encode_fn(&e);
+  if (!enc) return e;
+  Scratch buf;
+  const size_t na = (size_t)(a_batches * Mp * Kp), nbb = (size_t)(b_batches * Np * Kp);
+  e = buf.alloc(sizeof(float) * 2 * (na + nbb), stream);
+  if (!e.ok()) return e;
+  float* ahi = buf.as<float>();
+  float* alo = ahi + na;
+  float* bhi = alo + na;
+  float* blo = bhi + nbb;
+  // split / pack
+  sa.src = static_cast<const float*>(a->data);
+  sa.hi = ahi;
+  sa.lo = alo;
+  sa.rows = M;
+  sa.K = K;
+  sa.rows_p = Mp;
+  sa.Kp = Kp;
+  sa.s_row = a->strides[an - 2];
+  sa.s_k = a->strides[an - 1];
+  sa.off = a->offset;
+  sa.nb = an - 2;
+  for (int i = 0; i < an - 2; ++i) { sa.bshape[i] = a->shape[i]; sa.bst[i] = a->strides[i]; }
+  sa.k_fast = sa.s_k == 1 || sa.s_row != 1;
+  sb.src = static_cast<const float*>(b->data);
+  sb.hi = bhi;
+  sb.lo = blo;
+  sb.rows = N;
+  sb.K = K;
+  sb.rows_p = Np;
+  sb.Kp = Kp;
+  sb.s_row = b->strides[bn - 1];
+  sb.s_k = b->strides[bn - 2];
+  sb.off = b->offset;
+  sb.nb = bn - 2;
+  for (int i = 0; i < bn - 2; ++i) { sb.bshape[i] = b->shape[i]; sb.bst[i] = b->strides[i]; }
+  sb.k_fast = sb.s_k == 1 || sb.s_row != 1;
+  if (a_batches > 65535 || b_batches > 65535 || batches > 65535)
+    return make_error(TRS_ERR_SHAPE, "matmul_tf32x3: more than 65535 batches");
+  tf32_split_kernel<<<dim3((unsigned)(Kp / 32), (unsigned)(Mp / 32), (unsigned)a_batches), dim3(32, 8), 0, stream>>>(sa);
+  e = check_launch("tf32 split kernel (A)");
+  if (!e.ok()) return e;
+  tf32_split_kernel<<<dim3((unsigned)(Kp / 32), (unsigned)(Np / 32), (unsigned)b_batches), dim3(32, 8), 0, stream>>>(sb);
+  e = check_launch("tf32 split kernel (B)");
+  if (!e.ok()) return e;
+  CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
+  e = make_map(enc, &m_ahi, ahi, a_batches * Mp, Kp);
+  if (e.ok()) e = make_map(enc, &m_alo, alo, a_batches * Mp, Kp);
+  if (e.ok()) e = make_map(enc, &m_bhi, bhi, b_batches * Np, Kp);
+  if (e.ok()) e = make_map(enc, &m_blo, blo, b_batches * Np, Kp);
+  if (!e.ok()) return e;
+  allow_smem((const void*)tc_gemm_kernel, (int)kTcSmem);
+  tc_gemm_kernel<<<dim3((unsigned)(Np / kTcBN), (unsigned)(Mp / kTcBM), (unsigned)batches), 128, kTcSmem, stream>>>(
+      m_ahi, m_alo, m_bhi, m_blo, td);
+  return check_launch("tcgen05 tf32x3 matmul kernel");
+}
+
+trs_status finish(const Error& e) {
+  if (!e.ok()) set_last_error(e.msg);
+  return e.status;
+}
+
+}  // namespace
+}  // namespace trs
+
+extern "C" trs_status trs_matmul_tf32x3(const trs_view* a, const trs_view* b, trs_view* out, trs_stream stream) {
+  if (!a || !b || !out) return trs::finish(trs::make_error(TRS_ERR_ARG, "null view"));
+  return trs::finish(trs::run_tc_matmul(a, b, out, static_cast<cudaStream_t>(stream)));
+}

@@ -204,6 +204,12 @@ def matmul(a: abi.View, b: abi.View, out: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def matmul_tf32x3(a: abi.View, b: abi.View, out: torch.Tensor) -> torch.Tensor:
+    """Tensor::matmul for f32 on the tensor cores (split-TF32, within the sum tolerance)."""
+    _call("trs_matmul_tf32x3", ctypes.byref(a), ctypes.byref(b), ctypes.byref(view_of(out)), stream_handle())
+    return out
+
+
 def unfold_2d(x: abi.View, kernel, stride, padding, out: torch.Tensor) -> torch.Tensor:
     """Tensor::unfold_2d (linalg/tensor/conv.rs:360-418) into out [B*OH*OW, C*kh*kw]."""
     (kh, kw), (sh, sw), (ph, pw) = kernel, stride, padding

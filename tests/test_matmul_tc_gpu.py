@@ -1,0 +1,89 @@
+"""trs_matmul_tf32x3: Tensor::matmul (linalg/tensor/base.rs:896-1013) for f32
+on the tensor cores (tcgen05, split TF32), through the C ABI.
+
+Not bit-identical by design (the tensor cores add the products in their own
+order and precision): every output is held to
+    |gpu - ref| <= 1e-5 * sum_k |a_ik b_kj|
+against the reference's sequential f32 chain (the oracle), and to
+    |gpu - exact| <= 2^-18 * sum_k |a_ik b_kj|
+against the exact product (f64), which the split into hi/lo TF32 parts
+(products kept to about 2^-21) and an f32 accumulation of K terms allow with
+margin.  Shapes cover the padding of every tile edge (M, N not multiples of
+128, K not a multiple of 32), batches with broadcasting, transposed and
+offset views, K = 1 and K = 0."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from _gpu import DevView, contiguous, empty, to_host
+
+pytestmark = pytest.mark.gpu
+
+
+def rand(shape, seed):
+    return np.random.default_rng(seed).standard_normal(size=shape).astype(np.float32)
+
+
+def check(da: DevView, db: DevView):
+    import oracle
+    from tensorrs_b200 import device
+    out = empty(device.matmul_shape(da.view, db.view), np.float32)
+    got = to_host(device.matmul_tf32x3(da.view, db.view, out)).astype(np.float64)
+    ref = oracle.matmul(da.host_view(), db.host_view()).astype(np.float64)
+    a = np.array(oracle.unary("none", da.host_view()), np.float64)
+    b = np.array(oracle.unary("none", db.host_view()), np.float64)
+    exact = np.matmul(a, b)
+    mag = np.matmul(np.abs(a), np.abs(b))
+    assert got.shape == ref.shape
+    worst = float(np.max(np.abs(got - ref) / np.maximum(mag, 1e-300))) if got.size else 0.0
+    assert np.all(np.abs(got - ref) <= 1e-5 * mag + 1e-30), worst
+    assert np.all(np.abs(got - exact) <= 2.0**-18 * mag + 1e-30)
+    return worst
+
+
+SHAPES = [
+    ([128, 32], [32, 128]), ([256, 256], [256, 256]), ([129, 77], [77, 300]), ([1, 5], [5, 1]),
+    ([300, 1], [1, 200]), ([2, 1, 70, 40], [3, 40, 50]), ([4, 64, 96], [96, 33]), ([1000, 513], [513, 257]),
+]
+
+
+@pytest.mark.parametrize("sa,sb", SHAPES, ids=lambda v: str(v))
+def test_tf32x3_within_the_sum_tolerance(sa, sb):
+    worst = check(contiguous(rand(sa, sum(sa))), contiguous(rand(sb, sum(sb) + 1)))
+    print(f"{sa} x {sb}: worst |gpu - ref| / sum|ab| = {worst:.2e}")
+
+
+def test_tf32x3_through_views_and_long_k():
+    m, k, n = 200, 1500, 150
+    a_t = rand([k, m], 3)
+    b_t = rand([n, k], 4)
+    check(DevView(a_t, [m, k], [1, m], 0), DevView(b_t, [k, n], [1, k], 0))  # A^T x B^T
+    store = rand([m * (k + 3) + 7], 5)
+    check(DevView(store, [m, k], [k + 3, 1], 7), contiguous(rand([k, n], 6)))
+    check(contiguous(rand([512, 4096], 8)), contiguous(rand([4096, 384], 9)))
+
+
+def test_tf32x3_empty_depth_gives_zeros_and_errors():
+    from tensorrs_b200 import abi, device
+    out = empty([3, 4], np.float32)
+    got = to_host(device.matmul_tf32x3(contiguous(np.ones([3, 0], np.float32)).view,
+                                       contiguous(np.ones([0, 4], np.float32)).view, out))
+    assert np.array_equal(got, np.zeros([3, 4], np.float32)) and not np.signbit(got).any()
+    with pytest.raises(abi.TrsError) as e:
+        device.matmul_tf32x3(contiguous(np.ones([2, 3], np.float32)).view,
+                             contiguous(np.ones([2, 3], np.float32)).view, empty([2, 3], np.float32))
+    assert "matmul: inner dimensions must match (A.shape[-1] == B.shape[-2])" in e.value.message
+    with pytest.raises(abi.TrsError) as e:
+        device.matmul_tf32x3(contiguous(np.ones([2, 3], np.int32)).view,
+                             contiguous(np.ones([3, 2], np.int32)).view, empty([2, 2], np.int32))
+    assert e.value.status == abi.ERR_DTYPE
+
+
+def test_tf32x3_no_kernel_gave_up_waiting():
+    import ctypes
+
+    from tensorrs_b200 import abi
+    code = ctypes.c_int32(-1)
+    abi.check(abi.load().trs_async_error(ctypes.byref(code)))
+    assert code.value == 0
