@@ -487,6 +487,14 @@ def suite_groups(lib, abi, device, torch):
          lambda s: C(lib.trs_sum_axis(ref(s["v"]["A"]), 1, 0, ref(s["v"]["r"]), sh))),
         ("sum() of A[1024,1024]", 4194304 + 4,
          lambda s: C(lib.trs_sum(ref(s["v"]["A"]), ref(s["v"]["s"]), sh))),
+        # the chain the configuration names: y = A + b, y.sum_axis(1), y.sum()
+        ("chain y = A + b, y.sum_axis(1), y.sum() as three calls", 8392704 + 4194304 + 4096 + 4194304 + 4,
+         lambda s: (C(lib.trs_elementwise(ref(s["p"]), s["ins"], ref(s["v"]["Y"]), sh)),
+                    C(lib.trs_sum_axis(ref(s["v"]["Y"]), 1, 0, ref(s["v"]["r"]), sh)),
+                    C(lib.trs_sum(ref(s["v"]["Y"]), ref(s["v"]["s"]), sh)))),
+        ("chain y = A + b, y.sum_axis(1), y.sum() in one pass", 8392704 + 4096 + 4,
+         lambda s: C(lib.trs_elementwise_row_sums(ref(s["p"]), s["ins"], ref(s["v"]["Y"]), ref(s["v"]["r"]),
+                                                  ref(s["v"]["s"]), sh))),
     ]))
 
     # config 2: C = A & B^T (B^T a strided view), sigmoid

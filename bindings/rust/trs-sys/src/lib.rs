@@ -124,6 +124,7 @@ extern "C" {
     pub fn trs_unary(op: i32, x: *const trs_view, params: *const trs_scalar, out_: *mut trs_view, stream: trs_stream) -> trs_status;
     pub fn trs_elementwise(prog: *const trs_ew_program, in_: *const trs_view, out_: *mut trs_view, stream: trs_stream) -> trs_status;
     pub fn trs_elementwise_sum(prog: *const trs_ew_program, in_: *const trs_view, out_: *mut trs_view, sum_out: *mut trs_view, stream: trs_stream) -> trs_status;
+    pub fn trs_elementwise_row_sums(prog: *const trs_ew_program, in_: *const trs_view, out_: *mut trs_view, row_sums: *mut trs_view, total: *mut trs_view, stream: trs_stream) -> trs_status;
     pub fn trs_pack(x: *const trs_view, out_: *mut trs_view, stream: trs_stream) -> trs_status;
     pub fn trs_sum(x: *const trs_view, out_: *mut trs_view, stream: trs_stream) -> trs_status;
     pub fn trs_sum_noalloc(x: *const trs_view, out_: *mut trs_view, stream: trs_stream) -> trs_status;

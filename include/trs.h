@@ -224,6 +224,21 @@ trs_status trs_elementwise_sum(const trs_ew_program* prog, const trs_view* in,
                                trs_view* out, trs_view* sum_out,
                                trs_stream stream);
 
+/* The chain `y = prog(in); y.sum_axis(last); y.sum()` (binary_op,
+ * ops.rs:240-300; sum_axis, base.rs:1051-1107; sum, base.rs:1024-1030) in
+ * one pass: `out` receives y (shape: the inputs' broadcast shape, rank >= 1),
+ * `row_sums` its sums along the last axis (the reduced shape, with or without
+ * the axis kept as size 1) and `total` (one element) the sum of all of y.
+ * Either sum may be NULL, not both.  Sums accumulate in f64 (wrapping
+ * integers) and round once, as trs_sum_axis and trs_sum do.  A contiguous
+ * `out` of at least 256 rows whose inputs run along the last axis with unit
+ * stride (or are constant along it) takes one kernel plus a one-CTA fold;
+ * other layouts run the three passes.  The sums may overlap no other
+ * operand (TRS_ERR_ALIAS). */
+trs_status trs_elementwise_row_sums(const trs_ew_program* prog, const trs_view* in,
+                                    trs_view* out, trs_view* row_sums, trs_view* total,
+                                    trs_stream stream);
+
 /* packed_data / get_data / Clone (base.rs:430-434, 252, 1934-1945):
  * copy any view into the layout of `out` (normally contiguous). */
 trs_status trs_pack(const trs_view* x, trs_view* out, trs_stream stream);

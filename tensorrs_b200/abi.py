@@ -89,6 +89,7 @@ _SIGNATURES = {
     "trs_unary": (c_int32, [c_int32, _V, POINTER(Scalar), _V, c_void_p]),
     "trs_elementwise": (c_int32, [POINTER(Program), _V, _V, c_void_p]),
     "trs_elementwise_sum": (c_int32, [POINTER(Program), _V, _V, _V, c_void_p]),
+    "trs_elementwise_row_sums": (c_int32, [POINTER(Program), _V, _V, _V, _V, c_void_p]),
     "trs_pack": (c_int32, [_V, _V, c_void_p]),
     "trs_sum": (c_int32, [_V, _V, c_void_p]),
     "trs_sum_noalloc": (c_int32, [_V, _V, c_void_p]),

@@ -79,6 +79,25 @@ Error axis_reduce(int mode, const trs_view* x, int32_t axis, bool keepdim, const
   return run_reduce(q, stream);
 }
 
+// Whether two views can reach a common byte of memory.
+bool views_overlap(const trs_view* a, const trs_view* b) {
+  if (numel_of(a->shape, a->ndim) == 0 || numel_of(b->shape, b->ndim) == 0) return false;
+  auto range = [](const trs_view* v, int64_t* lo, int64_t* hi) {
+    const int es = dtype_size(v->dtype);
+    int64_t l = v->offset, h = v->offset;
+    for (int i = 0; i < v->ndim; ++i) {
+      const int64_t span = (v->shape[i] - 1) * v->strides[i];
+      if (span > 0) h += span; else l += span;
+    }
+    *lo = (int64_t)(uintptr_t)v->data + l * es;
+    *hi = (int64_t)(uintptr_t)v->data + (h + 1) * es;
+  };
+  int64_t alo, ahi, blo, bhi;
+  range(a, &alo, &ahi);
+  range(b, &blo, &bhi);
+  return alo < bhi && blo < ahi;
+}
+
 // Shared planning of reduce_broadcast_grad (base.rs:1651-1686): which
 // dimensions of g are summed, or TRS_NONE where the reference returns None.
 Error plan_to_shape(const trs_view* g, const int64_t* target, int tn, const trs_view* out,
@@ -229,6 +248,65 @@ trs_status trs_elementwise_sum(const trs_ew_program* prog, const trs_view* in, t
   SumTarget t;
   t.view = sum_out;
   return finish(run_elementwise(*prog, in, out, &t, as_stream(stream)));
+}
+
+trs_status trs_elementwise_row_sums(const trs_ew_program* prog, const trs_view* in, trs_view* out,
+                                    trs_view* row_sums, trs_view* total, trs_stream stream) {
+  if (!prog || !in || !out) return finish(make_error(TRS_ERR_ARG, "null argument"));
+  if (!row_sums && !total) return finish(make_error(TRS_ERR_ARG, "neither row sums nor a total requested"));
+  cudaStream_t s = as_stream(stream);
+  EwFold fold;
+  EwChoice choice;
+  Error e = plan_elementwise(*prog, in, out, &fold, &choice);  // inputs, output, shapes, aliasing
+  if (!e.ok()) return finish(e);
+  const int axis = out->ndim - 1;
+  e = check_axis(out, axis);
+  if (!e.ok()) return finish(e);
+  int64_t rs_strides[TRS_MAX_DIMS];
+  bool keepdim = false;
+  if (row_sums) {
+    e = validate_view(row_sums, "row sums");
+    if (!e.ok()) return finish(e);
+    if (row_sums->dtype != out->dtype) return finish(make_error(TRS_ERR_DTYPE, "row sums dtype differs"));
+    keepdim = row_sums->ndim == out->ndim;
+    e = map_axis_output(out, axis, keepdim, row_sums, rs_strides);
+    if (!e.ok()) return finish(e);
+  }
+  if (total) {
+    e = validate_view(total, "total");
+    if (!e.ok()) return finish(e);
+    if (total->dtype != out->dtype) return finish(make_error(TRS_ERR_DTYPE, "total dtype differs"));
+    if (numel_of(total->shape, total->ndim) != 1)
+      return finish(make_error(TRS_ERR_SHAPE, "total must hold one element"));
+  }
+  // the sums are fresh tensors in the reference: they may overlap nothing
+  const trs_view* sums[2] = {row_sums, total};
+  for (int i = 0; i < 2; ++i) {
+    if (!sums[i]) continue;
+    bool clash = views_overlap(sums[i], out) || (i == 1 && row_sums && views_overlap(total, row_sums));
+    for (int k = 0; k < prog->n_in && !clash; ++k) clash = views_overlap(sums[i], &in[k]);
+    if (clash) return finish(make_error(TRS_ERR_ALIAS, "a sum output overlaps another operand"));
+  }
+  bool taken = false;
+  e = run_row_sums_fused(*prog, in, out, row_sums, total, s, &taken);
+  if (taken || !e.ok()) return finish(e);
+  // the three passes: Y, then its sums along the last axis, then its total
+  e = run_elementwise(*prog, in, out, nullptr, s);
+  if (!e.ok()) return finish(e);
+  if (row_sums) {
+    e = axis_reduce(kRedSum, out, axis, keepdim, row_sums, s);
+    if (!e.ok()) return finish(e);
+  }
+  if (total) {
+    trs_ew_program p;
+    std::memset(&p, 0, sizeof(p));
+    p.n_in = 1;
+    p.epilogue = TRS_UN_NONE;
+    SumTarget t;
+    t.view = total;
+    e = run_elementwise(p, out, nullptr, &t, s);
+  }
+  return finish(e);
 }
 
 trs_status trs_pack(const trs_view* x, trs_view* out, trs_stream stream) {

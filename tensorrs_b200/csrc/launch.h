@@ -45,6 +45,15 @@ constexpr int kMaxExchangeRanks = 64;
 Error run_elementwise(const trs_ew_program& prog, const trs_view* in,
                       const trs_view* out, const SumTarget* sum, cudaStream_t stream);
 
+// trs_elementwise_row_sums in one pass (rowsum.cu): Y = prog(in) into the
+// contiguous `out`, its sums along the last axis into `rows_out` (contiguous,
+// or null) and its total into `total` (or null).  Views are validated by the
+// caller.  *taken is false, with nothing launched, when the layout is not one
+// the fused kernel serves (fewer than 256 rows, a strided or transposed
+// operand, integer division); the caller then runs the three passes.
+Error run_row_sums_fused(const trs_ew_program& prog, const trs_view* in, const trs_view* out,
+                         const trs_view* rows_out, const trs_view* total, cudaStream_t stream, bool* taken);
+
 // Plan only (trs_plan_elementwise).
 Error plan_elementwise(const trs_ew_program& prog, const trs_view* in,
                        const trs_view* out, EwFold* fold, EwChoice* choice);

@@ -32,6 +32,7 @@
 // values of the windows covering it in the reference's order -- windows by
 // increasing (oh, ow) -- starting from +0, so its sums round exactly as the
 // reference's `image[..] += src[..]` loop does.
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -223,6 +224,10 @@ struct ColsDev {
   int64_t x_off, xs[4];   // the image ([B, C, H, W] view): unfold's input, fold's output
   int64_t c_off, cs[2];   // the columns ([B*OH*OW, C*kh*kw] view): unfold's output, fold's input
   int64_t patch, rows;
+  // fold: the columns offset of window (oh, ow) for a fixed pixel is linear,
+  // base + oh * step_oh + ow * step_ow, with
+  // step_oh = OW * cs0 - sh * kw * cs1 and step_ow = cs0 - sw * cs1
+  int64_t step_oh, step_ow;
   // 32-bit index decode (every index below 2^32): divisors of the decode
   FastDiv f_patch, f_kk, f_kw, f_ow, f_oh, f_w, f_h, f_c, f_sh, f_sw;
 };
@@ -273,6 +278,128 @@ __global__ void __launch_bounds__(kThreads) unfold_kernel(const ColsDev d) {
   }
 }
 
+// unfold with a column table.  Each CTA first writes, for every column
+// col = (c, i, j) of a row, the image offset c * xs1 + i * xs2 + j * xs3 and
+// (i, j) into shared memory (patch <= kUnfoldTab columns).  Then it takes
+// groups of `group` rows (b, oh, ow): a pass decodes each row of the group
+// once into shared memory (its image base, top-left corner and output base)
+// and walks the group's group * patch elements flat, so every thread has
+// work whatever the patch.
+//   VEC (contiguous columns, patch a multiple of the 16-byte width EV, table
+//   offsets within 31 bits): a thread takes EV consecutive elements at a
+//   time -- always of one row, since patch % EV == 0 -- with one division,
+//   16-byte reads of the table, unsigned bounds checks, EV gathered loads and
+//   one 16-byte store; kUnfoldVecU such chunks per thread are in flight.
+//   Otherwise: one element at a time, kColsU loads in flight, any strides.
+constexpr int kUnfoldTab = 2048;
+constexpr int kUnfoldGroup = 64;
+constexpr int kUnfoldVecU = 4;
+
+struct UnfoldRow {
+  int64_t base, obase;  // image offset of (b, c=0, y0, x0); output offset of the row
+  int32_t y0, x0;       // top-left corner of the window (may be negative: padding)
+};
+
+template <class T, int N>
+struct alignas(sizeof(T) * N) Pack {
+  T v[N];
+};
+
+template <class T, bool VEC>
+__global__ void __launch_bounds__(kThreads) unfold_tab_kernel(const ColsDev d, const uint32_t group) {
+  constexpr int EV = VEC ? 16 / (int)sizeof(T) : 1;
+  __shared__ __align__(16) unsigned char toff_raw[kUnfoldTab * 8];
+  __shared__ __align__(16) uint32_t tij[kUnfoldTab];
+  __shared__ UnfoldRow rinfo[kUnfoldGroup];
+  int64_t* toff64 = reinterpret_cast<int64_t*>(toff_raw);
+  int32_t* toff32 = reinterpret_cast<int32_t*>(toff_raw);
+  const T* x = static_cast<const T*>(d.src);
+  T* out = static_cast<T*>(d.dst);
+  const uint32_t patch = (uint32_t)d.patch;
+  for (uint32_t col = threadIdx.x; col < patch; col += kThreads) {
+    const uint32_t c = fdiv(col, d.f_kk), r = col - c * d.f_kk.d;
+    const uint32_t i = fdiv(r, d.f_kw), j = r - i * d.f_kw.d;
+    const int64_t off = (int64_t)c * d.xs[1] + (int64_t)i * d.xs[2] + (int64_t)j * d.xs[3];
+    if (VEC)
+      toff32[col] = (int32_t)off;
+    else
+      toff64[col] = off;
+    tij[col] = (i << 16) | j;
+  }
+  const uint64_t rows = (uint64_t)d.rows;
+  const uint32_t H = (uint32_t)d.H, W = (uint32_t)d.W;
+  for (uint64_t r0 = (uint64_t)blockIdx.x * group; r0 < rows; r0 += (uint64_t)gridDim.x * group) {
+    const uint32_t nr = rows - r0 < group ? (uint32_t)(rows - r0) : group;
+    if (threadIdx.x < nr) {
+      const uint32_t row = (uint32_t)r0 + threadIdx.x;
+      const uint32_t r1 = fdiv(row, d.f_ow), ow = row - r1 * d.f_ow.d;
+      const uint32_t b = fdiv(r1, d.f_oh), oh = r1 - b * d.f_oh.d;
+      UnfoldRow ri;
+      ri.y0 = (int32_t)(oh * (uint32_t)d.sh) - (int32_t)d.ph;
+      ri.x0 = (int32_t)(ow * (uint32_t)d.sw) - (int32_t)d.pw;
+      ri.base = d.x_off + (int64_t)b * d.xs[0] + (int64_t)ri.y0 * d.xs[2] + (int64_t)ri.x0 * d.xs[3];
+      ri.obase = d.c_off + (int64_t)row * d.cs[0];
+      rinfo[threadIdx.x] = ri;
+    }
+    __syncthreads();  // the table (first pass) and this group's rows are written
+    if constexpr (VEC) {
+      // the group's columns are one contiguous run of nr * patch elements
+      T* gout = out + d.c_off + (int64_t)r0 * (int64_t)patch;
+      const uint32_t nv = nr * (patch / EV);
+      for (uint32_t e0 = threadIdx.x; e0 < nv; e0 += kThreads * kUnfoldVecU) {
+        Pack<T, EV> v[kUnfoldVecU];
+#pragma unroll
+        for (int u = 0; u < kUnfoldVecU; ++u) {
+          const uint32_t ev = e0 + (uint32_t)u * kThreads;
+          if (ev < nv) {
+            const uint32_t e = ev * EV;
+            const uint32_t q = fdiv(e, d.f_patch), col = e - q * patch;
+            const UnfoldRow& ri = rinfo[q];
+            const Pack<uint32_t, EV> ij = *reinterpret_cast<const Pack<uint32_t, EV>*>(&tij[col]);
+            const Pack<int32_t, EV> of = *reinterpret_cast<const Pack<int32_t, EV>*>(&toff32[col]);
+#pragma unroll
+            for (int t = 0; t < EV; ++t) {
+              const uint32_t y = (uint32_t)(ri.y0 + (int32_t)(ij.v[t] >> 16));
+              const uint32_t xx = (uint32_t)(ri.x0 + (int32_t)(ij.v[t] & 0xFFFFu));
+              v[u].v[t] = (y < H && xx < W) ? x[ri.base + of.v[t]] : T(0);
+            }
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kUnfoldVecU; ++u) {
+          const uint32_t ev = e0 + (uint32_t)u * kThreads;
+          if (ev < nv) *reinterpret_cast<Pack<T, EV>*>(gout + (size_t)ev * EV) = v[u];
+        }
+      }
+    } else {
+      const uint32_t n = nr * patch;  // < 2^32: rows * patch < 2^32
+      for (uint32_t e0 = threadIdx.x; e0 < n; e0 += kThreads * kColsU) {
+        T v[kColsU];
+        int64_t at[kColsU];
+#pragma unroll
+        for (int u = 0; u < kColsU; ++u) {
+          const uint32_t e = e0 + (uint32_t)u * kThreads;
+          v[u] = T(0);
+          at[u] = -1;
+          if (e < n) {
+            const uint32_t q = fdiv(e, d.f_patch), col = e - q * patch;
+            const UnfoldRow& ri = rinfo[q];
+            const uint32_t ij = tij[col];
+            const uint32_t y = (uint32_t)(ri.y0 + (int32_t)(ij >> 16));
+            const uint32_t xx = (uint32_t)(ri.x0 + (int32_t)(ij & 0xFFFFu));
+            if (y < H && xx < W) v[u] = x[ri.base + toff64[col]];
+            at[u] = ri.obase + (int64_t)col * d.cs[1];
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kColsU; ++u)
+          if (at[u] >= 0) out[at[u]] = v[u];
+      }
+    }
+    __syncthreads();  // every thread is done with this group's rows
+  }
+}
+
 // One thread per output pixel (b, c, y, x), row-major: adds the values of the
 // windows covering the pixel, windows by increasing (oh, ow), from +0.  When
 // at most kFoldRegs windows can cover a pixel (ceil(kh / sh) * ceil(kw / sw),
@@ -301,24 +428,28 @@ __global__ void __launch_bounds__(kThreads) fold_kernel(const ColsDev d) {
     int32_t ow_hi = (int32_t)fdiv((uint32_t)xp, d.f_sw);
     if (ow_hi > OW - 1) ow_hi = OW - 1;
     const int32_t nw = ow_hi - ow_lo + 1;
-    auto at = [&](int32_t oh, int32_t ow) {
-      const int32_t i = yp - oh * sh, j = xp - ow * sw;
-      const int64_t row = ((int64_t)b * OH + oh) * OW + ow, col = ((int64_t)c * kh + i) * kw + j;
-      return d.c_off + row * d.cs[0] + col * d.cs[1];
-    };
+    // window (oh, ow) is column (c, i, j) = (c, yp - oh * sh, xp - ow * sw) of
+    // row (b, oh, ow); its offset steps by step_oh / step_ow per window
+    const int64_t first = d.c_off + (int64_t)b * OH * OW * d.cs[0] +
+                          (((int64_t)c * kh + yp) * kw + xp) * d.cs[1] + (int64_t)oh_lo * d.step_oh +
+                          (int64_t)ow_lo * d.step_ow;
     T acc = T(0);
     if constexpr (REGS) {
       const int32_t cnt = (oh_hi >= oh_lo && nw > 0) ? (oh_hi - oh_lo + 1) * nw : 0;
       T v[kFoldRegs];
-      int32_t oh = oh_lo, ow = ow_lo;  // window w = (oh, ow), row-major over the covering range
+      int64_t row_at = first, at = first;
+      int32_t ow = ow_lo;  // window w = (oh, ow), row-major over the covering range
 #pragma unroll
       for (int w = 0; w < kFoldRegs; ++w) {
         v[w] = T(0);
         if (w < cnt) {
-          v[w] = cols[at(oh, ow)];
+          v[w] = cols[at];
           if (++ow > ow_hi) {
             ow = ow_lo;
-            ++oh;
+            row_at += d.step_oh;
+            at = row_at;
+          } else {
+            at += d.step_ow;
           }
         }
       }
@@ -326,10 +457,94 @@ __global__ void __launch_bounds__(kThreads) fold_kernel(const ColsDev d) {
       for (int w = 0; w < kFoldRegs; ++w)
         if (w < cnt) acc = A::add(acc, v[w]);  // windows in (oh, ow) order
     } else {
-      for (int32_t oh = oh_lo; oh <= oh_hi; ++oh)
-        for (int32_t ow = ow_lo; ow <= ow_hi; ++ow) acc = A::add(acc, cols[at(oh, ow)]);
+      int64_t row_at = first;
+      for (int32_t oh = oh_lo; oh <= oh_hi; ++oh, row_at += d.step_oh) {
+        int64_t at = row_at;
+        for (int32_t ow = ow_lo; ow <= ow_hi; ++ow, at += d.step_ow) acc = A::add(acc, cols[at]);
+      }
     }
     out[d.x_off + (int64_t)b * d.xs[0] + (int64_t)c * d.xs[1] + (int64_t)y * d.xs[2] + (int64_t)xx * d.xs[3]] = acc;
+  }
+}
+
+// fold through shared memory.  A tile is (b, a block of CB channels, a band
+// of TY output rows, every column x).  The windows that can cover the band
+// are the rows (b, oh, ow) for oh in [oh_a, oh_b] and every ow: consecutive
+// rows of the columns matrix, of which the tile needs the CB * kh * kw
+// consecutive entries of its channels.  The CTA copies those into shared
+// memory with coalesced 4- or 8-byte cp.async (entry t of window row r at
+// r * segp + t, segp odd so that neighbouring windows fall in different
+// banks), then each thread adds, for its pixels, the covering windows by
+// increasing (oh, ow) from +0 -- the reference's order -- reading them from
+// shared memory with the same linear stepping as fold_kernel.  Window rows at
+// a band's edges are copied by both neighbouring tiles; tiles are numbered
+// band-fastest, so the second copy usually comes from L2.
+struct FoldTile {
+  int32_t CB, TY, noh, seg, segp;  // channels, output rows, window rows, entries per window row (and padded)
+  int32_t n_cb, n_yb;              // channel blocks, bands
+  int64_t tiles;
+  FastDiv f_seg, f_ty, f_yb, f_cb;
+};
+
+template <class T>
+__global__ void __launch_bounds__(kThreads) fold_smem_kernel(const ColsDev d, const FoldTile t) {
+  using A = Arith<T>;
+  extern __shared__ __align__(16) unsigned char fold_raw[];
+  T* sm = reinterpret_cast<T*>(fold_raw);
+  const T* cols = static_cast<const T*>(d.src);
+  T* out = static_cast<T*>(d.dst);
+  const int32_t kh = (int32_t)d.kh, kw = (int32_t)d.kw, sh = (int32_t)d.sh, sw = (int32_t)d.sw;
+  const int32_t OH = (int32_t)d.OH, OW = (int32_t)d.OW, H = (int32_t)d.H, W = (int32_t)d.W;
+  const int32_t C = (int32_t)d.C, kk = kh * kw;
+  const int32_t step_ow = t.segp - sw, step_oh = OW * t.segp - sh * kw;
+  for (int64_t tile = blockIdx.x; tile < t.tiles; tile += gridDim.x) {
+    // tile = (b * n_cb + cb) * n_yb + yb
+    const uint32_t q1 = fdiv((uint32_t)tile, t.f_yb), yb = (uint32_t)tile - q1 * t.f_yb.d;
+    const uint32_t b = fdiv(q1, t.f_cb), cb = q1 - b * t.f_cb.d;
+    const int32_t y0 = (int32_t)yb * t.TY, c0 = (int32_t)cb * t.CB;
+    const int32_t ty = H - y0 < t.TY ? H - y0 : t.TY, ncb = C - c0 < t.CB ? C - c0 : t.CB;
+    // window rows covering output rows y0 .. y0 + ty - 1
+    const int32_t lo = y0 + (int32_t)d.ph - kh + 1, hi = y0 + ty - 1 + (int32_t)d.ph;
+    const int32_t oh_a = lo <= 0 ? 0 : (lo + sh - 1) / sh;
+    const int32_t oh_b = hi / sh < OH - 1 ? hi / sh : OH - 1;
+    const int32_t noh = oh_b - oh_a + 1;
+    const int32_t seg_eff = ncb * kk;
+    if (noh > 0) {
+      const int64_t row0 = ((int64_t)b * OH + oh_a) * OW;  // first window row of the tile
+      const int64_t src0 = d.c_off + row0 * d.cs[0] + (int64_t)c0 * kk * d.cs[1];
+      const uint32_t n_load = (uint32_t)(noh * OW) * (uint32_t)t.seg;
+      for (uint32_t i = threadIdx.x; i < n_load; i += kThreads) {
+        const uint32_t r = fdiv(i, t.f_seg), e = i - r * t.f_seg.d;
+        if ((int32_t)e < seg_eff)
+          cp_async_elem<(int)sizeof(T)>(sm + (size_t)r * t.segp + e, cols + src0 + (int64_t)r * d.cs[0] + (int64_t)e * d.cs[1],
+                                        (int)sizeof(T));
+      }
+      cp_async_commit();
+      cp_async_wait_all();
+    }
+    __syncthreads();  // the tile's windows are in shared memory
+    const uint32_t n_pix = (uint32_t)(ncb * t.TY * W);  // rows yr >= ty (last band) are skipped
+    for (uint32_t pidx = threadIdx.x; pidx < n_pix; pidx += kThreads) {
+      const uint32_t q = fdiv(pidx, d.f_w), x = pidx - q * d.f_w.d;
+      const uint32_t cr = fdiv(q, t.f_ty), yr = q - cr * t.f_ty.d;
+      if ((int32_t)yr >= ty) continue;
+      const int32_t y = y0 + (int32_t)yr, c = c0 + (int32_t)cr;
+      const int32_t yp = y + (int32_t)d.ph, xp = (int32_t)x + (int32_t)d.pw;
+      const int32_t ohl = yp - kh + 1 <= 0 ? 0 : (yp - kh + sh) / sh;
+      int32_t ohh = yp / sh;
+      if (ohh > OH - 1) ohh = OH - 1;
+      const int32_t owl = xp - kw + 1 <= 0 ? 0 : (xp - kw + sw) / sw;
+      int32_t owh = xp / sw;
+      if (owh > OW - 1) owh = OW - 1;
+      T acc = T(0);
+      int32_t row_at = ((ohl - oh_a) * OW + owl) * t.segp + (int32_t)cr * kk + (yp - ohl * sh) * kw + (xp - owl * sw);
+      for (int32_t oh = ohl; oh <= ohh; ++oh, row_at += step_oh) {
+        int32_t at = row_at;
+        for (int32_t ow = owl; ow <= owh; ++ow, at += step_ow) acc = A::add(acc, sm[at]);
+      }
+      out[d.x_off + (int64_t)b * d.xs[0] + (int64_t)c * d.xs[1] + (int64_t)y * d.xs[2] + (int64_t)x * d.xs[3]] = acc;
+    }
+    __syncthreads();  // every thread is done with the tile's windows
   }
 }
 
@@ -499,18 +714,84 @@ unsigned cols_grid(const void* kernel, uint64_t items) {
   return (unsigned)(need < cap ? (need < 1 ? 1 : need) : cap);
 }
 
+// Shared memory a fold tile may take: five CTAs per SM.
+constexpr int64_t kFoldSmemBudget = 44 * 1024;
+
+// The largest band of output rows (8, 4, 2 or 1), then the most channels (up
+// to 4), whose windows fit kFoldSmemBudget; false if none does.
+bool pick_fold_tile(const ColsDev& d, int es, FoldTile* t) {
+  if (d.B <= 0 || d.C <= 0 || d.H <= 0 || d.W <= 0 || d.OH <= 0 || d.OW <= 0) return false;
+  for (int ty = 8; ty >= 1; ty /= 2) {
+    if (ty > 1 && ty >= 2 * d.H) continue;
+    for (int cb = 4; cb >= 1; cb /= 2) {
+      if (cb > 1 && cb >= 2 * d.C) continue;
+      const int64_t noh = (ty + d.kh - 1 + d.sh - 1) / d.sh;
+      const int64_t seg = cb * d.kh * d.kw, segp = seg | 1;
+      if (noh * d.OW * segp * es > kFoldSmemBudget) continue;
+      t->CB = cb;
+      t->TY = ty;
+      t->noh = (int32_t)noh;
+      t->seg = (int32_t)seg;
+      t->segp = (int32_t)segp;
+      t->n_cb = (int32_t)((d.C + cb - 1) / cb);
+      t->n_yb = (int32_t)((d.H + ty - 1) / ty);
+      t->tiles = d.B * t->n_cb * t->n_yb;
+      if (t->tiles >= (1ll << 32) || (uint64_t)d.C * (uint64_t)ty * (uint64_t)d.W >= (1ull << 31)) return false;
+      t->f_seg = make_fastdiv((uint32_t)seg);
+      t->f_ty = make_fastdiv((uint32_t)ty);
+      t->f_yb = make_fastdiv((uint32_t)t->n_yb);
+      t->f_cb = make_fastdiv((uint32_t)t->n_cb);
+      return true;
+    }
+  }
+  return false;
+}
+
 template <class T>
 Error launch_cols(bool unfold, const ColsDev& d, cudaStream_t stream) {
+  if (!unfold) {
+    FoldTile ft;
+    if (pick_fold_tile(d, (int)sizeof(T), &ft)) {
+      const int smem = (int)((int64_t)ft.noh * d.OW * ft.segp * (int64_t)sizeof(T));
+      const void* k = (const void*)fold_smem_kernel<T>;
+      const uint64_t cap =
+          (uint64_t)current_device_info().sm_count * (uint64_t)resident_blocks_smem(k, kThreads, smem);
+      const unsigned g = (unsigned)((uint64_t)ft.tiles < cap ? (uint64_t)ft.tiles : cap);
+      fold_smem_kernel<T><<<g, kThreads, smem, stream>>>(d, ft);
+      return check_launch("fold_2d kernel");
+    }
+  }
   // windows that can cover one pixel: ceil(kh / sh) * ceil(kw / sw)
   const int64_t cover = ((d.kh + d.sh - 1) / d.sh) * ((d.kw + d.sw - 1) / d.sw);
   const bool regs = cover <= kFoldRegs;
-  const void* k = unfold ? (const void*)unfold_kernel<T>
+  // the table form when a row's columns fit its table (and i, j fit 16 bits)
+  const bool tab = unfold && d.patch <= kUnfoldTab && d.kh < 65536 && d.kw < 65536;
+  // the vector form: contiguous columns, patch % EV == 0, 16-byte aligned
+  // start, every table offset within 31 bits
+  constexpr int EV = 16 / (int)sizeof(T);
+  const uint64_t max_off = (uint64_t)std::llabs(d.xs[1]) * (uint64_t)(d.C > 0 ? d.C - 1 : 0) +
+                           (uint64_t)std::llabs(d.xs[2]) * (uint64_t)(d.kh > 0 ? d.kh - 1 : 0) +
+                           (uint64_t)std::llabs(d.xs[3]) * (uint64_t)(d.kw > 0 ? d.kw - 1 : 0);
+  const bool vec = tab && d.cs[1] == 1 && d.cs[0] == d.patch && d.patch % EV == 0 && d.c_off % EV == 0 &&
+                   ((uintptr_t)d.dst + (uintptr_t)d.c_off * sizeof(T)) % 16 == 0 && max_off < (1ull << 31);
+  const void* k = unfold ? (tab ? (vec ? (const void*)unfold_tab_kernel<T, true> : (const void*)unfold_tab_kernel<T, false>)
+                                : (const void*)unfold_kernel<T>)
                          : (regs ? (const void*)fold_kernel<T, true> : (const void*)fold_kernel<T, false>);
-  const uint64_t items = unfold ? ((uint64_t)d.rows * (uint64_t)d.patch + kColsU - 1) / kColsU
+  // rows per pass of the table form: about kThreads * kColsU elements; the
+  // vector form, at most one chunk of EV elements per thread and unroll step
+  const uint64_t pt = (uint64_t)(d.patch > 0 ? d.patch : 1);
+  const uint64_t want = vec ? (uint64_t)kThreads * kUnfoldVecU * EV / pt : ((uint64_t)kThreads * kColsU + pt - 1) / pt;
+  const uint32_t group = (uint32_t)(want < 1 ? 1 : (want > (uint64_t)kUnfoldGroup ? kUnfoldGroup : want));
+  const uint64_t items = unfold ? (tab ? ((uint64_t)d.rows + group - 1) / group * kThreads
+                                       : ((uint64_t)d.rows * (uint64_t)d.patch + kColsU - 1) / kColsU)
                                 : (uint64_t)(d.B * d.C * d.H * d.W);
-  if (items == 0) return Error{};
+  if (items == 0 || (unfold && d.patch == 0)) return Error{};
   const unsigned g = cols_grid(k, items);
-  if (unfold)
+  if (unfold && vec)
+    unfold_tab_kernel<T, true><<<g, kThreads, 0, stream>>>(d, group);
+  else if (unfold && tab)
+    unfold_tab_kernel<T, false><<<g, kThreads, 0, stream>>>(d, group);
+  else if (unfold)
     unfold_kernel<T><<<g, kThreads, 0, stream>>>(d);
   else if (regs)
     fold_kernel<T, true><<<g, kThreads, 0, stream>>>(d);
@@ -576,6 +857,8 @@ Error run_fold(const trs_view* cols, int64_t kh, int64_t kw, int64_t sh, int64_t
   d.c_off = cols->offset;
   d.cs[0] = cols->strides[0];
   d.cs[1] = cols->strides[1];
+  d.step_oh = d.OW * d.cs[0] - d.sh * d.kw * d.cs[1];
+  d.step_ow = d.cs[0] - d.sw * d.cs[1];
   return dispatch_cols(false, cols->dtype, d, stream);
 }
 

@@ -67,6 +67,17 @@ def elementwise(prog: abi.Program, ins: list[abi.View], out: torch.Tensor | None
               stream_handle())
 
 
+def elementwise_row_sums(prog: abi.Program, ins: list[abi.View], out: torch.Tensor,
+                         row_sums: torch.Tensor | None, total: torch.Tensor | None) -> None:
+    """Y = prog(ins) into `out`, its sums along the last axis into `row_sums`
+    and its total into `total`, in one pass (trs_elementwise_row_sums)."""
+    arr = abi.views_array(ins)
+    rv = ctypes.byref(view_of(row_sums)) if row_sums is not None else None
+    tv = ctypes.byref(view_of(total)) if total is not None else None
+    _call("trs_elementwise_row_sums", ctypes.byref(prog), arr, ctypes.byref(view_of(out)), rv, tv,
+          stream_handle())
+
+
 def pack(x: abi.View, out: torch.Tensor) -> torch.Tensor:
     _call("trs_pack", ctypes.byref(x), ctypes.byref(view_of(out)), stream_handle())
     return out

@@ -78,6 +78,12 @@ def test_config1_bias_add_row_sums_and_sum():
     device.elementwise(abi.program(2, abi.ADD), [da.view, db.view], y2, s2)
     assert_bit_exact(to_host(y2), want, "A + b (fused with its sum)")
     check_sum(to_host(s2), [oracle.sum_all(dy.host_view())], [sabs], [exact])
+    # the whole chain (A + b, its row sums, its sum) in one pass
+    y3, r3, s3 = empty([n, n], np.float32), empty([n], np.float32), empty([1], np.float32)
+    device.elementwise_row_sums(abi.program(2, abi.ADD), [da.view, db.view], y3, r3, s3)
+    assert_bit_exact(to_host(y3), want, "A + b (one pass with its sums)")
+    check_sum(to_host(r3), ref_rows, np.abs(yd).sum(axis=1), yd.sum(axis=1))
+    check_sum(to_host(s3), [oracle.sum_all(dy.host_view())], [sabs], [exact])
 
 
 # ---------------------------------------------------------------------------

@@ -131,6 +131,10 @@ COL_CASES = [  # shape, kernel, stride, padding
     ([1, 1, 4, 4], (4, 4), (3, 3), (0, 0)), ([1, 2, 5, 6], (2, 3), (1, 1), (3, 2)),
     # more than 16 windows cover a pixel: fold adds them as it loads them
     ([1, 2, 9, 9], (5, 5), (1, 1), (2, 2)), ([2, 1, 12, 7], (7, 3), (1, 1), (3, 1)),
+    # a row of exactly 2048 columns (the largest column table) and one of 2160 (past it)
+    ([1, 128, 5, 6], (4, 4), (1, 1), (1, 1)), ([1, 240, 6, 7], (3, 3), (1, 1), (1, 1)),
+    # fold windows too wide for a shared-memory tile: the per-pixel kernels
+    ([1, 1, 6, 1200], (4, 4), (1, 1), (0, 0)), ([1, 1, 12, 20], (11, 11), (1, 1), (0, 0)),
 ]
 
 
@@ -149,6 +153,24 @@ def test_unfold_and_fold_bit_exact(shape, kernel, stride, padding, dtype):
     dc = contiguous(c)
     back = to_host(device.fold_2d(dc.view, kernel, stride, padding, empty(shape, dtype)))
     assert_bit_exact(back, oracle.fold_2d(dc.host_view(), shape, kernel, stride, padding), "fold_2d")
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64], ids=lambda d: np.dtype(d).name)
+def test_unfold_into_a_transposed_output(dtype):
+    """Columns written through a transposed view (column stride = rows)."""
+    import torch
+
+    import oracle
+    from tensorrs_b200 import device
+    x = rand([2, 3, 9, 11], dtype, 14)
+    dx = contiguous(x)
+    want = oracle.unfold_2d(dx.host_view(), (3, 3), (1, 1), (1, 1))
+    rows, patch = want.shape
+    out = empty([patch, rows], dtype).t()
+    assert out.stride() == (1, rows)
+    got = device.unfold_2d(dx.view, (3, 3), (1, 1), (1, 1), out)
+    assert_bit_exact(to_host(got.contiguous()), want, "unfold into a transposed view")
+    assert isinstance(got, torch.Tensor)
 
 
 def test_unfold_of_a_strided_image_and_fold_errors():
