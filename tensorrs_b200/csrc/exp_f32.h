@@ -226,8 +226,10 @@ __device__ __forceinline__ float2 sigmoid2(float2 x) {
   const float2 tjx = __ldg(tab + (tbx & 15u)), tjy = __ldg(tab + (tby & 15u));
   const float2 th = make_float2(tjx.x, tjy.x), tl = make_float2(tjx.y, tjy.y);
   const float2 s = __fadd2_rn(th, __ffma2_rn(th, p, tl));
-  const float2 p2 = make_float2(__uint_as_float(((tbx << 19) & 0xFF800000u) + (191u << 23)),
-                                __uint_as_float(((tby << 19) & 0xFF800000u) + (191u << 23)));  // 2^(ex + 64)
+  // 2^(ex + 64): bits 4..12 of t are ex (two's complement), so
+  // ((t >> 4) << 23) + (191 << 23) modulo 2^32 is its f32 bit pattern
+  const float2 p2 = make_float2(__uint_as_float((tbx >> 4) * (1u << 23) + (191u << 23)),
+                                __uint_as_float((tby >> 4) * (1u << 23) + (191u << 23)));
   const float2 e = __fmul2_rn(__fmul2_rn(s, p2), make_float2(0x1p-64f, 0x1p-64f));
   const float2 d = __fadd2_rn(one, e);
   const float2 nd = __ffma2_rn(e, m1, m1);  // -d
