@@ -505,8 +505,9 @@ __global__ void __launch_bounds__(kThreads) fold_smem_kernel(const ColsDev d, co
     const int32_t ty = H - y0 < t.TY ? H - y0 : t.TY, ncb = C - c0 < t.CB ? C - c0 : t.CB;
     // window rows covering output rows y0 .. y0 + ty - 1
     const int32_t lo = y0 + (int32_t)d.ph - kh + 1, hi = y0 + ty - 1 + (int32_t)d.ph;
-    const int32_t oh_a = lo <= 0 ? 0 : (lo + sh - 1) / sh;
-    const int32_t oh_b = hi / sh < OH - 1 ? hi / sh : OH - 1;
+    const int32_t oh_a = lo <= 0 ? 0 : (int32_t)fdiv((uint32_t)(lo + sh - 1), d.f_sh);
+    const int32_t hq = (int32_t)fdiv((uint32_t)hi, d.f_sh);
+    const int32_t oh_b = hq < OH - 1 ? hq : OH - 1;
     const int32_t noh = oh_b - oh_a + 1;
     const int32_t seg_eff = ncb * kk;
     if (noh > 0) {
@@ -530,11 +531,12 @@ __global__ void __launch_bounds__(kThreads) fold_smem_kernel(const ColsDev d, co
       if ((int32_t)yr >= ty) continue;
       const int32_t y = y0 + (int32_t)yr, c = c0 + (int32_t)cr;
       const int32_t yp = y + (int32_t)d.ph, xp = (int32_t)x + (int32_t)d.pw;
-      const int32_t ohl = yp - kh + 1 <= 0 ? 0 : (yp - kh + sh) / sh;
-      int32_t ohh = yp / sh;
+      // window ranges by the fast divisions (every dividend here is >= 0)
+      const int32_t ohl = yp - kh + 1 <= 0 ? 0 : (int32_t)fdiv((uint32_t)(yp - kh + sh), d.f_sh);
+      int32_t ohh = (int32_t)fdiv((uint32_t)yp, d.f_sh);
       if (ohh > OH - 1) ohh = OH - 1;
-      const int32_t owl = xp - kw + 1 <= 0 ? 0 : (xp - kw + sw) / sw;
-      int32_t owh = xp / sw;
+      const int32_t owl = xp - kw + 1 <= 0 ? 0 : (int32_t)fdiv((uint32_t)(xp - kw + sw), d.f_sw);
+      int32_t owh = (int32_t)fdiv((uint32_t)xp, d.f_sw);
       if (owh > OW - 1) owh = OW - 1;
       T acc = T(0);
       int32_t row_at = ((ohl - oh_a) * OW + owl) * t.segp + (int32_t)cr * kk + (yp - ohl * sh) * kw + (xp - owl * sw);

@@ -48,6 +48,10 @@ constexpr uint32_t kTcTile = kTcBM * kTcBK * 4;      // one operand tile of a sl
 constexpr uint32_t kTcStage = 4 * kTcTile;           // A hi, A lo, B hi, B lo
 constexpr uint32_t kTcSmem = kTcStages * kTcStage + 1024 + 256;  // + alignment slack + barriers
 constexpr uint32_t kTcCols = 128;                    // TMEM columns of the f32 accumulator
+#ifndef TRS_TC_GROUP
+#define TRS_TC_GROUP 8
+#endif
+constexpr int kTcGroup = TRS_TC_GROUP;               // row blocks of tiles per group of the tile order
 
 // ---- the split / pack kernel -------------------------------------------------
 
@@ -243,8 +247,22 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap t_ahi, const __grid_constant_
       oo += c * d.o_bst[i];
     }
   }
-  const int32_t a_row = (int32_t)(abt * d.Mp + (int64_t)blockIdx.y * kTcBM);
-  const int32_t b_row = (int32_t)(bbt * d.Np + (int64_t)blockIdx.x * kTcBN);
+  // grouped tile order: CTAs launch in blockIdx order, and consecutive ones
+  // take the tiles of kTcGroup row blocks column by column, so a wave's A and
+  // B tiles are few enough to stay in L2 while the wave walks K
+  int64_t tile_m, tile_n;
+  {
+    const int64_t gx = gridDim.x, gy = gridDim.y;
+    const int64_t pid = (int64_t)blockIdx.y * gx + blockIdx.x;
+    const int64_t per_group = (int64_t)kTcGroup * gx;
+    const int64_t first = pid / per_group * kTcGroup;
+    const int64_t rows = gy - first < kTcGroup ? gy - first : kTcGroup;
+    const int64_t local = pid % per_group;
+    tile_m = first + local % rows;
+    tile_n = local / rows;
+  }
+  const int32_t a_row = (int32_t)(abt * d.Mp + tile_m * kTcBM);
+  const int32_t b_row = (int32_t)(bbt * d.Np + tile_n * kTcBN);
   const int nk = (int)(d.Kp / kTcBK);
 
   if (threadIdx.x == 0) {  // TMA producer
@@ -299,13 +317,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap t_ahi, const __grid_constant_
     if (lane == 0 && d.err) atomicOr(d.err, kAsyncWaitTimeout);
   } else {
     float* out = static_cast<float*>(d.out);
-    const int64_t row = (int64_t)blockIdx.y * kTcBM + warp * 32 + lane;
+    const int64_t row = tile_m * kTcBM + warp * 32 + lane;
 #pragma unroll 1
     for (int c = 0; c < kTcBN / 32; ++c) {
       uint32_t v[32];
       tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(c * 32), v);
       if (row < d.M) {
-        const int64_t col0 = (int64_t)blockIdx.x * kTcBN + c * 32;
+        const int64_t col0 = tile_n * kTcBN + c * 32;
 #pragma unroll
         for (int j = 0; j < 32; ++j)
           if (col0 + j < d.N) out[oo + row * d.som + (col0 + j) * d.son] = __uint_as_float(v[j]);
