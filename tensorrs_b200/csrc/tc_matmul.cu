@@ -24,10 +24,14 @@
 //      3-stage ring with TMA (cp.async.bulk.tensor.2d, 128-byte swizzle, no
 //      multicast), completing on a `full` mbarrier; thread 32 waits for a slab
 //      and issues, for each of its 4 k-steps of 8, the three tcgen05.mma
-//      kind::tf32 (M 128, N 128) into one f32 accumulator of 128 TMEM columns,
+//      kind::tf32 (M 128, N 128) into one f32 accumulator of 128 TMEM columns
+//      (the first two share A, which the collector buffer keeps between them),
 //      then tcgen05.commit frees the slab through its `empty` mbarrier; a final
 //      commit signals `done`, and all 4 warps read their 32 accumulator rows
 //      with tcgen05.ld and write them through the output view.
+// A call whose inputs hold an infinity or NaN (the split kernels raise a flag)
+// takes the reference's exact chain on the CUDA cores in every CTA instead: a
+// split product inf * (a zero lo part) would turn an infinite result into NaN.
 // Every mbarrier wait is bounded (kWaitIters polls); a wait that runs out
 // sets the async-error word and the CTA skips ahead to free its tensor
 // memory and return.
@@ -59,6 +63,7 @@ struct SplitDev {
   const float* src;
   float* hi;
   float* lo;
+  int* nonfinite;        // set to 1 when some element is an infinity or NaN
   int64_t rows, K;       // logical rows (M for A, N for B) and depth
   int64_t rows_p, Kp;    // padded
   int64_t s_row, s_k;    // source strides of a row and of k
@@ -98,6 +103,8 @@ __global__ void __launch_bounds__(256) tf32_split_kernel(const SplitDev d) {
     const int64_t r = d.k_fast ? r0 + q : r0 + tx, k = d.k_fast ? k0 + tx : k0 + q;
     float v = 0.0f;
     if (r < d.rows && k < d.K) v = d.src[off + r * d.s_row + k * d.s_k];
+    if (__any_sync(0xffffffffu, (__float_as_uint(v) & 0x7F800000u) == 0x7F800000u) && tx == 0)
+      atomicOr(d.nonfinite, 1);
     if (d.k_fast)
       tile[q][tx] = v;
     else
@@ -160,6 +167,30 @@ __device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t da, uint64_t
       : "memory");
 }
 
+#ifndef TRS_TC_COLLECTOR
+#define TRS_TC_COLLECTOR 1
+#endif
+// The same MMA with its A operand kept in the collector buffer for the next
+// MMA (fill), or taken from it and released (lastuse).
+__device__ __forceinline__ void umma_tf32_fill(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32.collector::a::fill [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+__device__ __forceinline__ void umma_tf32_lastuse(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                                  uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32.collector::a::lastuse [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
+          tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+
 // Arrives on `bar` once every tcgen05.mma this thread issued before has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -200,7 +231,30 @@ struct TcDev {
   int64_t bshape[kMaxDims], o_bst[kMaxDims];
   int64_t a_bidx[kMaxDims], b_bidx[kMaxDims];  // per output batch dim: stride in the operand's packed batch index
   int* err;
+  const float *ahi, *alo, *bhi, *blo;  // the packed planes (for the exact path)
+  int64_t K;
+  const int* nonfinite;  // set by the split kernels: some input is an infinity or NaN
 };
+
+// The reference's chain acc = acc + a * b over k from +0, each step rounded
+// once, for this CTA's tile: used instead of the tensor cores when an input
+// holds an infinity or NaN, where a split product (inf times a zero lo part)
+// would turn an infinite result into NaN.  x = hi + lo exactly (hi = x, lo = 0
+// for a non-finite x), so the result is bit-identical to trs_matmul's.
+__device__ void tc_exact_tile(const TcDev& d, int64_t abt, int64_t bbt, int64_t oo, int64_t tile_m, int64_t tile_n) {
+  const int t = threadIdx.x;
+  const int64_t col = tile_n * kTcBN + (t % kTcBN);
+  if (col >= d.N) return;
+  const int64_t bo = (bbt * d.Np + col) * d.Kp;
+  float* out = static_cast<float*>(d.out);
+  for (int64_t r = tile_m * kTcBM + t / kTcBN; r < tile_m * kTcBM + kTcBM && r < d.M; r += blockDim.x / kTcBN) {
+    const int64_t ao = (abt * d.Mp + r) * d.Kp;
+    float acc = 0.0f;
+    for (int64_t k = 0; k < d.K; ++k)
+      acc = __fadd_rn(acc, __fmul_rn(__fadd_rn(d.ahi[ao + k], d.alo[ao + k]), __fadd_rn(d.bhi[bo + k], d.blo[bo + k])));
+    out[oo + r * d.som + col * d.son] = acc;
+  }
+}
 
 __global__ void __launch_bounds__(128, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap t_ahi, const __grid_constant__ CUtensorMap t_alo,
@@ -264,6 +318,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap t_ahi, const __grid_constant_
   const int32_t a_row = (int32_t)(abt * d.Mp + tile_m * kTcBM);
   const int32_t b_row = (int32_t)(bbt * d.Np + tile_n * kTcBN);
   const int nk = (int)(d.Kp / kTcBK);
+  // an infinity or NaN among the inputs: the exact chain instead (the flag
+  // is the same for every thread of the grid, so the CTA branches as one)
+  if (*(volatile const int*)d.nonfinite != 0) {
+    tc_exact_tile(d, abt, bbt, oo, tile_m, tile_n);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, kTcCols);
+    return;
+  }
 
   if (threadIdx.x == 0) {  // TMA producer
     for (int kb = 0; kb < nk; ++kb) {
@@ -299,8 +362,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap t_ahi, const __grid_constant_
 #pragma unroll
       for (int k = 0; k < kTcBK / 8; ++k) {
         const uint64_t dk = (uint64_t)(k * 2);  // 8 tf32 = 32 bytes, in 16-byte units
+#if TRS_TC_COLLECTOR
+        // the first two products share A: it is read from shared memory once
+        umma_tf32_fill(tmem, ahi + dk, bhi + dk, kTf32Idesc, (kb > 0 || k > 0) ? 1u : 0u);
+        umma_tf32_lastuse(tmem, ahi + dk, blo + dk, kTf32Idesc, 1u);
+#else
         umma_tf32(tmem, ahi + dk, bhi + dk, kTf32Idesc, (kb > 0 || k > 0) ? 1u : 0u);
         umma_tf32(tmem, ahi + dk, blo + dk, kTf32Idesc, 1u);
+#endif
         umma_tf32(tmem, alo + dk, bhi + dk, kTf32Idesc, 1u);
       }
       umma_commit(&empty[s]);  // the slab is free once these have read it
@@ -465,16 +534,26 @@ Error run_tc_matmul(const trs_view* a, const trs_view* b, const trs_view* out, c
   if (!enc) return e;
   Scratch buf;
   const size_t na = (size_t)(a_batches * Mp * Kp), nbb = (size_t)(b_batches * Np * Kp);
-  e = buf.alloc(sizeof(float) * 2 * (na + nbb), stream);
+  e = buf.alloc(sizeof(float) * 2 * (na + nbb) + 16, stream);
   if (!e.ok()) return e;
   float* ahi = buf.as<float>();
   float* alo = ahi + na;
   float* bhi = alo + na;
   float* blo = bhi + nbb;
+  int* nonfinite = reinterpret_cast<int*>(blo + nbb);
+  cudaError_t ce = cudaMemsetAsync(nonfinite, 0, sizeof(int), stream);
+  if (ce != cudaSuccess) return cuda_error(ce, "cudaMemsetAsync");
+  td.ahi = ahi;
+  td.alo = alo;
+  td.bhi = bhi;
+  td.blo = blo;
+  td.K = K;
+  td.nonfinite = nonfinite;
   // split / pack
   sa.src = static_cast<const float*>(a->data);
   sa.hi = ahi;
   sa.lo = alo;
+  sa.nonfinite = nonfinite;
   sa.rows = M;
   sa.K = K;
   sa.rows_p = Mp;
@@ -488,6 +567,7 @@ Error run_tc_matmul(const trs_view* a, const trs_view* b, const trs_view* out, c
   sb.src = static_cast<const float*>(b->data);
   sb.hi = bhi;
   sb.lo = blo;
+  sb.nonfinite = nonfinite;
   sb.rows = N;
   sb.K = K;
   sb.rows_p = Np;

@@ -87,3 +87,28 @@ def test_tf32x3_no_kernel_gave_up_waiting():
     code = ctypes.c_int32(-1)
     abi.check(abi.load().trs_async_error(ctypes.byref(code)))
     assert code.value == 0
+
+
+def test_tf32x3_non_finite_inputs_follow_the_reference():
+    """An infinity or NaN among the inputs: a split product inf * (a zero lo
+    part) would turn an infinite result into NaN, so such calls take the
+    reference's exact chain and match the oracle bit for bit -- here against
+    partners that are exact TF32 values (small integers), whose lo parts are 0."""
+    import oracle
+    from _util import assert_bit_exact
+    from tensorrs_b200 import device
+    rng = np.random.default_rng(41)
+    a = rng.integers(-4, 5, size=[130, 40]).astype(np.float32)
+    b = rng.integers(-4, 5, size=[40, 140]).astype(np.float32)
+    a[3, 5] = np.inf
+    a[7, 1] = np.nan
+    b[2, 9] = -np.inf
+    da, db = contiguous(a), contiguous(b)
+    got = to_host(device.matmul_tf32x3(da.view, db.view, empty([130, 140], np.float32)))
+    want = oracle.matmul(da.host_view(), db.host_view())
+    assert np.isinf(want).any() and np.isnan(want).any()
+    assert_bit_exact(got, want, "tf32x3 with non-finite inputs")
+    # the same integers, all finite: the tensor-core path, exact for these values
+    a[3, 5] = a[7, 1] = 1.0
+    b[2, 9] = -2.0
+    check(contiguous(a), contiguous(b))
