@@ -763,16 +763,10 @@ ew_tr2d_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc*) {
 // with plain chunk indices instead of the strided row decode; held to 40
 // registers so six CTAs fit on an SM (more warps to cover the loads).
 template <class T, int PROG>
-#ifndef TRS_FLAT1_CTAS
-#define TRS_FLAT1_CTAS 6
-#endif
-#ifndef TRS_FLAT1_U
-#define TRS_FLAT1_U 4
-#endif
-__global__ void __launch_bounds__(kThreads, TRS_FLAT1_CTAS)
+__global__ void __launch_bounds__(kThreads, 6)
 ew_flat1_kernel(const EwDev d, const EwParams p, typename Arith<T>::Acc*) {
   constexpr int V = 16 / (int)sizeof(T);
-  constexpr int U = TRS_FLAT1_U;
+  constexpr int U = 4;
   const T* in = static_cast<const T*>(d.in[0]) + d.off[1];
   T* out = static_cast<T*>(d.out) + d.off[0];
   const uint32_t n = (uint32_t)d.n_chunks;
