@@ -19,16 +19,20 @@
 //      MMA), zero-padded to multiples of 128 rows and 32 k, through 32 x 32
 //      shared-memory tiles so that both the strided reads and the writes are
 //      coalesced (scratch from the stream-ordered pool);
-//   2. tc_gemm_kernel: one CTA of 4 warps per 128 x 128 output tile.  Thread 0
-//      streams 32-deep k slabs of the four operand tiles (16 KiB each) into a
-//      3-stage ring with TMA (cp.async.bulk.tensor.2d, 128-byte swizzle, no
-//      multicast), completing on a `full` mbarrier; thread 32 waits for a slab
-//      and issues, for each of its 4 k-steps of 8, the three tcgen05.mma
-//      kind::tf32 (M 128, N 128) into one f32 accumulator of 128 TMEM columns
-//      (the first two share A, which the collector buffer keeps between them),
-//      then tcgen05.commit frees the slab through its `empty` mbarrier; a final
-//      commit signals `done`, and all 4 warps read their 32 accumulator rows
-//      with tcgen05.ld and write them through the output view.
+//   2. tc_gemm_kernel<BN>: one CTA of 4 warps per 128 x BN output tile, BN =
+//      256 where that still gives six waves of tiles (less shared-memory
+//      traffic per product, the bound of this kernel), 128 otherwise; tiles
+//      in a grouped order (kTcGroup row blocks walked column by column).
+//      Thread 0 streams 32-deep k slabs of the four operand tiles into a ring
+//      of stages (3 x 64 KiB for BN 128, 2 x 96 KiB for BN 256) with TMA
+//      (cp.async.bulk.tensor.2d, 128-byte swizzle, no multicast), completing
+//      on a `full` mbarrier; thread 32 waits for a slab and issues, for each
+//      of its 4 k-steps of 8, the three tcgen05.mma kind::tf32 (M 128, N BN)
+//      into one f32 accumulator of BN TMEM columns (the first two share A,
+//      which the collector buffer keeps between them), then tcgen05.commit
+//      frees the slab through its `empty` mbarrier; a final commit signals
+//      `done`, and all 4 warps read their 32 accumulator rows with
+//      tcgen05.ld and write them through the output view.
 // A call whose inputs hold an infinity or NaN (the split kernels raise a flag)
 // takes the reference's exact chain on the CUDA cores in every CTA instead: a
 // split product inf * (a zero lo part) would turn an infinite result into NaN.
@@ -47,11 +51,23 @@
 namespace trs {
 namespace {
 
-constexpr int kTcBM = 128, kTcBN = 128, kTcBK = 32, kTcStages = 3;
-constexpr uint32_t kTcTile = kTcBM * kTcBK * 4;      // one operand tile of a slab: 16 KiB
-constexpr uint32_t kTcStage = 4 * kTcTile;           // A hi, A lo, B hi, B lo
-constexpr uint32_t kTcSmem = kTcStages * kTcStage + 1024 + 256;  // + alignment slack + barriers
-constexpr uint32_t kTcCols = 128;                    // TMEM columns of the f32 accumulator
+constexpr int kTcBM = 128, kTcBK = 32;
+constexpr uint32_t kTcTile = kTcBM * kTcBK * 4;      // one A tile of a slab: 16 KiB
+
+// An output tile of 128 x BN (BN = 128 or 256): a stage holds A hi, A lo
+// (16 KiB each) and B hi, B lo (BN x 32 each); three stages of 64 KiB for
+// BN = 128, two of 96 KiB for BN = 256; the accumulator takes BN TMEM columns.
+template <int BN>
+struct TcShape {
+  static constexpr uint32_t tile_b = BN * kTcBK * 4;
+  static constexpr uint32_t stage = 2 * kTcTile + 2 * tile_b;
+  static constexpr int stages = BN == 128 ? 3 : 2;
+  static constexpr uint32_t smem = stages * stage + 1024 + 256;  // + alignment slack + barriers
+  static constexpr uint32_t cols = BN;
+  // instruction descriptor: D f32, A and B tf32, both K-major, N = BN, M = 128
+  static constexpr uint32_t idesc =
+      (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kTcBM >> 4) << 24);
+};
 #ifndef TRS_TC_GROUP
 #define TRS_TC_GROUP 8
 #endif
@@ -219,9 +235,6 @@ __device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
   return a | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
 }
 
-// Instruction descriptor: D f32, A and B tf32, both K-major, N 128, M 128.
-constexpr uint32_t kTf32Idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(kTcBN >> 3) << 17) |
-                                ((uint32_t)(kTcBM >> 4) << 24);
 
 struct TcDev {
   int64_t M, N, Kp, Mp, Np;
@@ -241,13 +254,13 @@ struct TcDev {
 // holds an infinity or NaN, where a split product (inf times a zero lo part)
 // would turn an infinite result into NaN.  x = hi + lo exactly (hi = x, lo = 0
 // for a non-finite x), so the result is bit-identical to trs_matmul's.
+template <int BN>
 __device__ void tc_exact_tile(const TcDev& d, int64_t abt, int64_t bbt, int64_t oo, int64_t tile_m, int64_t tile_n) {
-  const int t = threadIdx.x;
-  const int64_t col = tile_n * kTcBN + (t % kTcBN);
-  if (col >= d.N) return;
-  const int64_t bo = (bbt * d.Np + col) * d.Kp;
   float* out = static_cast<float*>(d.out);
-  for (int64_t r = tile_m * kTcBM + t / kTcBN; r < tile_m * kTcBM + kTcBM && r < d.M; r += blockDim.x / kTcBN) {
+  for (int idx = threadIdx.x; idx < kTcBM * BN; idx += blockDim.x) {
+    const int64_t col = tile_n * BN + idx % BN, r = tile_m * kTcBM + idx / BN;
+    if (col >= d.N || r >= d.M) continue;
+    const int64_t bo = (bbt * d.Np + col) * d.Kp;
     const int64_t ao = (abt * d.Mp + r) * d.Kp;
     float acc = 0.0f;
     for (int64_t k = 0; k < d.K; ++k)
@@ -256,22 +269,24 @@ __device__ void tc_exact_tile(const TcDev& d, int64_t abt, int64_t bbt, int64_t 
   }
 }
 
+template <int BN>
 __global__ void __launch_bounds__(128, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap t_ahi, const __grid_constant__ CUtensorMap t_alo,
                const __grid_constant__ CUtensorMap t_bhi, const __grid_constant__ CUtensorMap t_blo,
                const TcDev d) {
+  using S = TcShape<BN>;
   extern __shared__ unsigned char tc_smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTcStages * kTcStage);
-  uint64_t* empty = full + kTcStages;
-  uint64_t* done = empty + kTcStages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::stages * S::stage);
+  uint64_t* empty = full + S::stages;
+  uint64_t* done = empty + S::stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   int* failed = reinterpret_cast<int*>(tmem_slot + 1);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
+    for (int s = 0; s < S::stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -281,7 +296,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap t_ahi, const __grid_constant_
   }
   __syncwarp();  // warp 0 converged for the warp-collective allocation
   if (warp == 0) {
-    tmem_alloc(tmem_slot, kTcCols);
+    tmem_alloc(tmem_slot, S::cols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -316,61 +331,61 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap t_ahi, const __grid_constant_
     tile_n = local / rows;
   }
   const int32_t a_row = (int32_t)(abt * d.Mp + tile_m * kTcBM);
-  const int32_t b_row = (int32_t)(bbt * d.Np + tile_n * kTcBN);
+  const int32_t b_row = (int32_t)(bbt * d.Np + tile_n * BN);
   const int nk = (int)(d.Kp / kTcBK);
   // an infinity or NaN among the inputs: the exact chain instead (the flag
   // is the same for every thread of the grid, so the CTA branches as one)
   if (*(volatile const int*)d.nonfinite != 0) {
-    tc_exact_tile(d, abt, bbt, oo, tile_m, tile_n);
+    tc_exact_tile<BN>(d, abt, bbt, oo, tile_m, tile_n);
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, kTcCols);
+    if (warp == 0) tmem_dealloc(tmem, S::cols);
     return;
   }
 
   if (threadIdx.x == 0) {  // TMA producer
     for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % kTcStages;
-      const uint32_t ph = (uint32_t)(kb / kTcStages) & 1u;
-      if (kb >= kTcStages && !mbar_wait(&empty[s], ph ^ 1u)) {
+      const int s = kb % S::stages;
+      const uint32_t ph = (uint32_t)(kb / S::stages) & 1u;
+      if (kb >= S::stages && !mbar_wait(&empty[s], ph ^ 1u)) {
         atomicExch(failed, 1);
         break;
       }
       if (*(volatile int*)failed) break;
-      unsigned char* st = smem + s * kTcStage;
-      mbar_arrive_expect_tx(&full[s], kTcStage);
+      unsigned char* st = smem + s * S::stage;
+      mbar_arrive_expect_tx(&full[s], S::stage);
       const int32_t kx = kb * kTcBK;
       tma_load_2d(st, &t_ahi, kx, a_row, &full[s]);
       tma_load_2d(st + kTcTile, &t_alo, kx, a_row, &full[s]);
       tma_load_2d(st + 2 * kTcTile, &t_bhi, kx, b_row, &full[s]);
-      tma_load_2d(st + 3 * kTcTile, &t_blo, kx, b_row, &full[s]);
+      tma_load_2d(st + 2 * kTcTile + S::tile_b, &t_blo, kx, b_row, &full[s]);
     }
   } else if (threadIdx.x == 32) {  // MMA issuer
     bool ok = true;
     for (int kb = 0; kb < nk && ok; ++kb) {
-      const int s = kb % kTcStages;
-      const uint32_t ph = (uint32_t)(kb / kTcStages) & 1u;
+      const int s = kb % S::stages;
+      const uint32_t ph = (uint32_t)(kb / S::stages) & 1u;
       if (!mbar_wait(&full[s], ph)) {
         atomicExch(failed, 1);
         ok = false;
         break;
       }
       tc_fence_after();
-      unsigned char* st = smem + s * kTcStage;
+      unsigned char* st = smem + s * S::stage;
       const uint64_t ahi = sw128_desc(st), alo = sw128_desc(st + kTcTile);
-      const uint64_t bhi = sw128_desc(st + 2 * kTcTile), blo = sw128_desc(st + 3 * kTcTile);
+      const uint64_t bhi = sw128_desc(st + 2 * kTcTile), blo = sw128_desc(st + 2 * kTcTile + S::tile_b);
 #pragma unroll
       for (int k = 0; k < kTcBK / 8; ++k) {
         const uint64_t dk = (uint64_t)(k * 2);  // 8 tf32 = 32 bytes, in 16-byte units
 #if TRS_TC_COLLECTOR
         // the first two products share A: it is read from shared memory once
-        umma_tf32_fill(tmem, ahi + dk, bhi + dk, kTf32Idesc, (kb > 0 || k > 0) ? 1u : 0u);
-        umma_tf32_lastuse(tmem, ahi + dk, blo + dk, kTf32Idesc, 1u);
+        umma_tf32_fill(tmem, ahi + dk, bhi + dk, S::idesc, (kb > 0 || k > 0) ? 1u : 0u);
+        umma_tf32_lastuse(tmem, ahi + dk, blo + dk, S::idesc, 1u);
 #else
-        umma_tf32(tmem, ahi + dk, bhi + dk, kTf32Idesc, (kb > 0 || k > 0) ? 1u : 0u);
-        umma_tf32(tmem, ahi + dk, blo + dk, kTf32Idesc, 1u);
+        umma_tf32(tmem, ahi + dk, bhi + dk, S::idesc, (kb > 0 || k > 0) ? 1u : 0u);
+        umma_tf32(tmem, ahi + dk, blo + dk, S::idesc, 1u);
 #endif
-        umma_tf32(tmem, alo + dk, bhi + dk, kTf32Idesc, 1u);
+        umma_tf32(tmem, alo + dk, bhi + dk, S::idesc, 1u);
       }
       umma_commit(&empty[s]);  // the slab is free once these have read it
     }
@@ -388,11 +403,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap t_ahi, const __grid_constant_
     float* out = static_cast<float*>(d.out);
     const int64_t row = tile_m * kTcBM + warp * 32 + lane;
 #pragma unroll 1
-    for (int c = 0; c < kTcBN / 32; ++c) {
+    for (int c = 0; c < BN / 32; ++c) {
       uint32_t v[32];
       tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(c * 32), v);
       if (row < d.M) {
-        const int64_t col0 = tile_n * kTcBN + c * 32;
+        const int64_t col0 = tile_n * BN + c * 32;
 #pragma unroll
         for (int j = 0; j < 32; ++j)
           if (col0 + j < d.N) out[oo + row * d.som + (col0 + j) * d.son] = __uint_as_float(v[j]);
@@ -401,7 +416,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap t_ahi, const __grid_constant_
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, kTcCols);
+  if (warp == 0) tmem_dealloc(tmem, S::cols);
 }
 
 // ---- host side -------------------------------------------------------------------
@@ -428,11 +443,11 @@ EncodeTiled encode_fn(Error* err) {
   return fn;
 }
 
-// [batches * rows_p, Kp] f32, K contiguous, 32 x 128 boxes with 128-byte swizzle.
-Error make_map(EncodeTiled enc, CUtensorMap* map, float* base, int64_t rows_total, int64_t Kp) {
+// [batches * rows_p, Kp] f32, K contiguous, 32 x box_rows boxes with 128-byte swizzle.
+Error make_map(EncodeTiled enc, CUtensorMap* map, float* base, int64_t rows_total, int64_t Kp, int box_rows) {
   const cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)rows_total};
   const cuuint64_t strides[1] = {(cuuint64_t)Kp * 4};
-  const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)kTcBM};
+  const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
@@ -461,6 +476,16 @@ bool views_overlap(const trs_view* a, const trs_view* b) {
 
 int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
+template <int BN>
+Error launch_tc_gemm(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMap& bhi, const CUtensorMap& blo,
+                     const TcDev& td, int64_t batches, cudaStream_t stream) {
+  using S = TcShape<BN>;
+  allow_smem((const void*)tc_gemm_kernel<BN>, (int)S::smem);
+  tc_gemm_kernel<BN><<<dim3((unsigned)(td.Np / BN), (unsigned)(td.Mp / kTcBM), (unsigned)batches), 128, S::smem,
+                       stream>>>(ahi, alo, bhi, blo, td);
+  return check_launch("tcgen05 tf32x3 matmul kernel");
+}
+
 Error run_tc_matmul(const trs_view* a, const trs_view* b, const trs_view* out, cudaStream_t stream) {
   Error e = validate_view(a, "a");
   if (!e.ok()) return e;
@@ -487,7 +512,13 @@ Error run_tc_matmul(const trs_view* a, const trs_view* b, const trs_view* out, c
   int64_t batches = 1;
   for (int i = 0; i < nb; ++i) batches *= batch[i];
   if (M == 0 || N == 0 || batches == 0) return Error{};
-  const int64_t Mp = round_up(M, kTcBM), Np = round_up(N, kTcBN), Kp = round_up(K, kTcBK);
+  // the 128 x 256 tile (less shared-memory traffic per product) where it
+  // still gives at least six waves of tiles, the 128 x 128 tile otherwise
+  const int64_t Mp = round_up(M, kTcBM), Kp = round_up(K, kTcBK);
+  const bool wide =
+      round_up(N, 256) / 256 * (Mp / kTcBM) * batches >= 6 * (int64_t)current_device_info().sm_count;
+  const int BN = wide ? 256 : 128;
+  const int64_t Np = round_up(N, BN);
   // each operand packed over its own batch dimensions
   SplitDev sa, sb;
   std::memset(&sa, 0, sizeof(sa));
@@ -587,15 +618,13 @@ Error run_tc_matmul(const trs_view* a, const trs_view* b, const trs_view* out, c
   e = check_launch("tf32 split kernel (B)");
   if (!e.ok()) return e;
   CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
-  e = make_map(enc, &m_ahi, ahi, a_batches * Mp, Kp);
-  if (e.ok()) e = make_map(enc, &m_alo, alo, a_batches * Mp, Kp);
-  if (e.ok()) e = make_map(enc, &m_bhi, bhi, b_batches * Np, Kp);
-  if (e.ok()) e = make_map(enc, &m_blo, blo, b_batches * Np, Kp);
+  e = make_map(enc, &m_ahi, ahi, a_batches * Mp, Kp, kTcBM);
+  if (e.ok()) e = make_map(enc, &m_alo, alo, a_batches * Mp, Kp, kTcBM);
+  if (e.ok()) e = make_map(enc, &m_bhi, bhi, b_batches * Np, Kp, BN);
+  if (e.ok()) e = make_map(enc, &m_blo, blo, b_batches * Np, Kp, BN);
   if (!e.ok()) return e;
-  allow_smem((const void*)tc_gemm_kernel, (int)kTcSmem);
-  tc_gemm_kernel<<<dim3((unsigned)(Np / kTcBN), (unsigned)(Mp / kTcBM), (unsigned)batches), 128, kTcSmem, stream>>>(
-      m_ahi, m_alo, m_bhi, m_blo, td);
-  return check_launch("tcgen05 tf32x3 matmul kernel");
+  return wide ? launch_tc_gemm<256>(m_ahi, m_alo, m_bhi, m_blo, td, batches, stream)
+              : launch_tc_gemm<128>(m_ahi, m_alo, m_bhi, m_blo, td, batches, stream);
 }
 
 trs_status finish(const Error& e) {

@@ -112,3 +112,20 @@ def test_tf32x3_non_finite_inputs_follow_the_reference():
     a[3, 5] = a[7, 1] = 1.0
     b[2, 9] = -2.0
     check(contiguous(a), contiguous(b))
+
+
+def test_tf32x3_wide_tiles():
+    """Shapes with at least six waves of 128 x 256 tiles take the wide tile:
+    [4096, 40] x [40, 7000] has 32 x 28 such tiles, the last column of tiles
+    88 wide; then the same shape through the exact path (a NaN input)."""
+    import oracle
+    from _util import assert_bit_exact
+    from tensorrs_b200 import device
+    a = rand([4096, 40], 51)
+    b = rand([40, 7000], 52)
+    worst = check(contiguous(a), contiguous(b))
+    print(f"wide tiles: worst |gpu - ref| / sum|ab| = {worst:.2e}")
+    a[100, 3] = np.nan
+    da, db = contiguous(a), contiguous(b)
+    got = to_host(device.matmul_tf32x3(da.view, db.view, empty([4096, 7000], np.float32)))
+    assert_bit_exact(got, oracle.matmul(da.host_view(), db.host_view()), "wide tiles, exact path")
