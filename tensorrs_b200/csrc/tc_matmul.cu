@@ -137,6 +137,49 @@ __global__ void __launch_bounds__(256) tf32_split_kernel(const SplitDev d) {
   }
 }
 
+// The same split for an operand already K-major with 16-byte aligned rows
+// (s_k == 1, s_row and the offset multiples of 4, the base 16-byte aligned):
+// no transpose, one 16-byte load and two 16-byte stores per thread and step.
+// Grid-stride over the padded [batches][rows_p][Kp / 4] chunks (fewer than
+// 2^32: the index decodes with 32-bit fast divisions by rows_p * Kp / 4 and
+// Kp / 4).
+__global__ void __launch_bounds__(256) tf32_split_vec_kernel(const SplitDev d, uint32_t n, FastDiv f_pb, FastDiv f_kq) {
+  bool nonfinite = false;
+  for (uint32_t i = blockIdx.x * 256 + threadIdx.x; i < n; i += gridDim.x * 256) {
+    const uint32_t bt = fdiv(i, f_pb), rem = i - bt * f_pb.d;
+    const uint32_t r32 = fdiv(rem, f_kq);
+    const int64_t r = r32, k = (int64_t)(rem - r32 * f_kq.d) * 4;
+    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (r < d.rows) {
+      int64_t off = d.off;
+      int64_t q = bt;
+      for (int j = d.nb - 1; j >= 0; --j) {
+        off += (q % d.bshape[j]) * d.bst[j];
+        q /= d.bshape[j];
+      }
+      const float* src = d.src + off + r * d.s_row + k;
+      if (k + 4 <= d.K) {
+        const float4 x = __ldcs(reinterpret_cast<const float4*>(src));
+        v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+      } else {
+        for (int j = 0; j < 4; ++j)
+          if (k + j < d.K) v[j] = src[j];
+      }
+    }
+    float4 h, l;
+    float* hp = &h.x;
+    float* lp = &l.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      nonfinite |= (__float_as_uint(v[j]) & 0x7F800000u) == 0x7F800000u;
+      tf32_split(v[j], hp + j, lp + j);
+    }
+    *reinterpret_cast<float4*>(d.hi + (size_t)i * 4) = h;
+    *reinterpret_cast<float4*>(d.lo + (size_t)i * 4) = l;
+  }
+  if (__any_sync(0xffffffffu, nonfinite) && (threadIdx.x & 31) == 0) atomicOr(d.nonfinite, 1);
+}
+
 // +0 into every element of a view (row-major over its shape).
 __global__ void __launch_bounds__(256) zero_view_kernel(const trs_view v, int64_t n) {
   float* o = static_cast<float*>(v.data);
@@ -611,11 +654,27 @@ Error run_tc_matmul(const trs_view* a, const trs_view* b, const trs_view* out, c
   sb.k_fast = sb.s_k == 1 || sb.s_row != 1;
   if (a_batches > 65535 || b_batches > 65535 || batches > 65535)
     return make_error(TRS_ERR_SHAPE, "matmul_tf32x3: more than 65535 batches");
-  tf32_split_kernel<<<dim3((unsigned)(Kp / 32), (unsigned)(Mp / 32), (unsigned)a_batches), dim3(32, 8), 0, stream>>>(sa);
-  e = check_launch("tf32 split kernel (A)");
+  // an operand already K-major with 16-byte aligned rows takes the direct
+  // 16-byte split; any other layout goes through the transposing tiles
+  auto split = [&](const SplitDev& sd, const void* base, int64_t ops_batches, const char* what) {
+    const int64_t chunks = ops_batches * sd.rows_p * (sd.Kp / 4);
+    bool vec = sd.s_k == 1 && sd.s_row % 4 == 0 && sd.off % 4 == 0 && (uintptr_t)base % 16 == 0 &&
+               chunks < (1ll << 32) - 256ll * 65536;
+    for (int i = 0; i < sd.nb && vec; ++i) vec = sd.bst[i] % 4 == 0;
+    if (vec) {
+      const int64_t cap = (int64_t)current_device_info().sm_count * 8;
+      const int64_t g = (chunks + 255) / 256 < cap ? (chunks + 255) / 256 : cap;
+      tf32_split_vec_kernel<<<(unsigned)(g < 1 ? 1 : g), 256, 0, stream>>>(
+          sd, (uint32_t)chunks, make_fastdiv((uint32_t)(sd.rows_p * (sd.Kp / 4))), make_fastdiv((uint32_t)(sd.Kp / 4)));
+    } else {
+      tf32_split_kernel<<<dim3((unsigned)(sd.Kp / 32), (unsigned)(sd.rows_p / 32), (unsigned)ops_batches), dim3(32, 8), 0,
+                          stream>>>(sd);
+    }
+    return check_launch(what);
+  };
+  e = split(sa, a->data, a_batches, "tf32 split kernel (A)");
   if (!e.ok()) return e;
-  tf32_split_kernel<<<dim3((unsigned)(Kp / 32), (unsigned)(Np / 32), (unsigned)b_batches), dim3(32, 8), 0, stream>>>(sb);
-  e = check_launch("tf32 split kernel (B)");
+  e = split(sb, b->data, b_batches, "tf32 split kernel (B)");
   if (!e.ok()) return e;
   CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
   e = make_map(enc, &m_ahi, ahi, a_batches * Mp, Kp, kTcBM);
