@@ -486,7 +486,11 @@ struct FoldTile {
   FastDiv f_seg, f_ty, f_yb, f_cb;
 };
 
-template <class T>
+// WIN > 0: at most WIN x WIN windows cover a pixel (ceil(kh / sh) and
+// ceil(kw / sw) <= WIN), and the window loops are unrolled WIN x WIN with each
+// add predicated on the window existing, so the adds keep their (oh, ow)
+// order; WIN = 0: loops bounded at run time.
+template <class T, int WIN>
 __global__ void __launch_bounds__(kThreads) fold_smem_kernel(const ColsDev d, const FoldTile t) {
   using A = Arith<T>;
   extern __shared__ __align__(16) unsigned char fold_raw[];
@@ -540,9 +544,18 @@ __global__ void __launch_bounds__(kThreads) fold_smem_kernel(const ColsDev d, co
       if (owh > OW - 1) owh = OW - 1;
       T acc = T(0);
       int32_t row_at = ((ohl - oh_a) * OW + owl) * t.segp + (int32_t)cr * kk + (yp - ohl * sh) * kw + (xp - owl * sw);
-      for (int32_t oh = ohl; oh <= ohh; ++oh, row_at += step_oh) {
-        int32_t at = row_at;
-        for (int32_t ow = owl; ow <= owh; ++ow, at += step_ow) acc = A::add(acc, sm[at]);
+      if constexpr (WIN > 0) {
+#pragma unroll
+        for (int dh = 0; dh < WIN; ++dh) {
+#pragma unroll
+          for (int dw = 0; dw < WIN; ++dw)
+            if (ohl + dh <= ohh && owl + dw <= owh) acc = A::add(acc, sm[row_at + dh * step_oh + dw * step_ow]);
+        }
+      } else {
+        for (int32_t oh = ohl; oh <= ohh; ++oh, row_at += step_oh) {
+          int32_t at = row_at;
+          for (int32_t ow = owl; ow <= owh; ++ow, at += step_ow) acc = A::add(acc, sm[at]);
+        }
       }
       out[d.x_off + (int64_t)b * d.xs[0] + (int64_t)c * d.xs[1] + (int64_t)y * d.xs[2] + (int64_t)x * d.xs[3]] = acc;
     }
@@ -755,11 +768,16 @@ Error launch_cols(bool unfold, const ColsDev& d, cudaStream_t stream) {
     FoldTile ft;
     if (pick_fold_tile(d, (int)sizeof(T), &ft)) {
       const int smem = (int)((int64_t)ft.noh * d.OW * ft.segp * (int64_t)sizeof(T));
-      const void* k = (const void*)fold_smem_kernel<T>;
+      // windows covering a pixel, per dimension: the unrolled form up to 3
+      const bool unrolled = (d.kh + d.sh - 1) / d.sh <= 3 && (d.kw + d.sw - 1) / d.sw <= 3;
+      const void* k = unrolled ? (const void*)fold_smem_kernel<T, 3> : (const void*)fold_smem_kernel<T, 0>;
       const uint64_t cap =
           (uint64_t)current_device_info().sm_count * (uint64_t)resident_blocks_smem(k, kThreads, smem);
       const unsigned g = (unsigned)((uint64_t)ft.tiles < cap ? (uint64_t)ft.tiles : cap);
-      fold_smem_kernel<T><<<g, kThreads, smem, stream>>>(d, ft);
+      if (unrolled)
+        fold_smem_kernel<T, 3><<<g, kThreads, smem, stream>>>(d, ft);
+      else
+        fold_smem_kernel<T, 0><<<g, kThreads, smem, stream>>>(d, ft);
       return check_launch("fold_2d kernel");
     }
   }
