@@ -33,6 +33,7 @@
 // increasing (oh, ow) -- starting from +0, so its sums round exactly as the
 // reference's `image[..] += src[..]` loop does.
 #include <cstdlib>
+#include <type_traits>
 #include <cstring>
 #include <string>
 
@@ -222,6 +223,7 @@ struct ColsDev {
   void* dst;
   int64_t B, C, H, W, kh, kw, sh, sw, ph, pw, OH, OW;
   int64_t x_off, xs[4];   // the image ([B, C, H, W] view): unfold's input, fold's output
+  int64_t x_len, c_len;   // storage lengths of the image's and the columns' views
   int64_t c_off, cs[2];   // the columns ([B*OH*OW, C*kh*kw] view): unfold's output, fold's input
   int64_t patch, rows;
   // fold: the columns offset of window (oh, ow) for a fixed pixel is linear,
@@ -278,125 +280,84 @@ __global__ void __launch_bounds__(kThreads) unfold_kernel(const ColsDev d) {
   }
 }
 
-// unfold with a column table.  Each CTA first writes, for every column
-// col = (c, i, j) of a row, the image offset c * xs1 + i * xs2 + j * xs3 and
-// (i, j) into shared memory (patch <= kUnfoldTab columns).  Then it takes
-// groups of `group` rows (b, oh, ow): a pass decodes each row of the group
-// once into shared memory (its image base, top-left corner and output base)
-// and walks the group's group * patch elements flat, so every thread has
-// work whatever the patch.
-//   VEC (contiguous columns, patch a multiple of the 16-byte width EV, table
-//   offsets within 31 bits): a thread takes EV consecutive elements at a
-//   time -- always of one row, since patch % EV == 0 -- with one division,
-//   16-byte reads of the table, unsigned bounds checks, EV gathered loads and
-//   one 16-byte store; kUnfoldVecU such chunks per thread are in flight.
-//   Otherwise: one element at a time, kColsU loads in flight, any strides.
+// Largest patch (columns of a row) whose column table fits a CTA's shared
+// memory in the tile kernel below.
 constexpr int kUnfoldTab = 2048;
-constexpr int kUnfoldGroup = 64;
-constexpr int kUnfoldVecU = 4;
 
-struct UnfoldRow {
-  int64_t base, obase;  // image offset of (b, c=0, y0, x0); output offset of the row
-  int32_t y0, x0;       // top-left corner of the window (may be negative: padding)
-};
+// unfold by tiles of kUtRows output rows x kUtCols columns, transposed
+// through shared memory so both sides are coalesced, with the patch's column
+// table in shared memory (one 8-byte entry per column: its image offset and
+// (i, j), written once per CTA; offsets within 31 bits).  In the gather, lane
+// r of a warp takes output row r0 + r -- consecutive rows are consecutive ow,
+// so consecutive image columns -- for one column at a time, whose table entry
+// is the same for the whole warp (a broadcast read); values go to
+// tile[col][row] (pitch kUtRows + 1: conflict-free both ways).  After a
+// barrier each warp stores whole tile rows, lanes along the columns.
+constexpr int kUtRows = 32;
+constexpr int kUtCols = 64;
 
-template <class T, int N>
-struct alignas(sizeof(T) * N) Pack {
-  T v[N];
-};
-
-template <class T, bool VEC>
-__global__ void __launch_bounds__(kThreads) unfold_tab_kernel(const ColsDev d, const uint32_t group) {
-  constexpr int EV = VEC ? 16 / (int)sizeof(T) : 1;
-  __shared__ __align__(16) unsigned char toff_raw[kUnfoldTab * 8];
-  __shared__ __align__(16) uint32_t tij[kUnfoldTab];
-  __shared__ UnfoldRow rinfo[kUnfoldGroup];
-  int64_t* toff64 = reinterpret_cast<int64_t*>(toff_raw);
-  int32_t* toff32 = reinterpret_cast<int32_t*>(toff_raw);
+// I32: every index the kernel forms (padding offsets included) lies within
+// (-2^31, 2^31), so the index arithmetic runs in 32 bits.
+template <class T, bool I32>
+__global__ void __launch_bounds__(kThreads) unfold_tile_kernel(const ColsDev d) {
+  using Idx = typename std::conditional<I32, int32_t, int64_t>::type;
+  __shared__ T tile[kUtCols][kUtRows + 1];
+  __shared__ int2 tab[kUnfoldTab];  // (image offset of column (c, i, j), i << 16 | j)
+  constexpr int kWarps = kThreads / 32;
   const T* x = static_cast<const T*>(d.src);
   T* out = static_cast<T*>(d.dst);
-  const uint32_t patch = (uint32_t)d.patch;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t rows = (uint32_t)d.rows, patch = (uint32_t)d.patch;
+  const uint32_t H = (uint32_t)d.H, W = (uint32_t)d.W;
   for (uint32_t col = threadIdx.x; col < patch; col += kThreads) {
     const uint32_t c = fdiv(col, d.f_kk), r = col - c * d.f_kk.d;
     const uint32_t i = fdiv(r, d.f_kw), j = r - i * d.f_kw.d;
-    const int64_t off = (int64_t)c * d.xs[1] + (int64_t)i * d.xs[2] + (int64_t)j * d.xs[3];
-    if (VEC)
-      toff32[col] = (int32_t)off;
-    else
-      toff64[col] = off;
-    tij[col] = (i << 16) | j;
+    tab[col] = make_int2((int)((int64_t)c * d.xs[1] + (int64_t)i * d.xs[2] + (int64_t)j * d.xs[3]),
+                         (int)((i << 16) | j));
   }
-  const uint64_t rows = (uint64_t)d.rows;
-  const uint32_t H = (uint32_t)d.H, W = (uint32_t)d.W;
-  for (uint64_t r0 = (uint64_t)blockIdx.x * group; r0 < rows; r0 += (uint64_t)gridDim.x * group) {
-    const uint32_t nr = rows - r0 < group ? (uint32_t)(rows - r0) : group;
-    if (threadIdx.x < nr) {
-      const uint32_t row = (uint32_t)r0 + threadIdx.x;
-      const uint32_t r1 = fdiv(row, d.f_ow), ow = row - r1 * d.f_ow.d;
-      const uint32_t b = fdiv(r1, d.f_oh), oh = r1 - b * d.f_oh.d;
-      UnfoldRow ri;
-      ri.y0 = (int32_t)(oh * (uint32_t)d.sh) - (int32_t)d.ph;
-      ri.x0 = (int32_t)(ow * (uint32_t)d.sw) - (int32_t)d.pw;
-      ri.base = d.x_off + (int64_t)b * d.xs[0] + (int64_t)ri.y0 * d.xs[2] + (int64_t)ri.x0 * d.xs[3];
-      ri.obase = d.c_off + (int64_t)row * d.cs[0];
-      rinfo[threadIdx.x] = ri;
-    }
-    __syncthreads();  // the table (first pass) and this group's rows are written
-    if constexpr (VEC) {
-      // the group's columns are one contiguous run of nr * patch elements
-      T* gout = out + d.c_off + (int64_t)r0 * (int64_t)patch;
-      const uint32_t nv = nr * (patch / EV);
-      for (uint32_t e0 = threadIdx.x; e0 < nv; e0 += kThreads * kUnfoldVecU) {
-        Pack<T, EV> v[kUnfoldVecU];
+  __syncthreads();
+  const uint32_t n_rb = (rows + kUtRows - 1) / kUtRows, n_cb = (patch + kUtCols - 1) / kUtCols;
+  const uint64_t tiles = (uint64_t)n_rb * n_cb;
+  for (uint64_t tl = blockIdx.x; tl < tiles; tl += gridDim.x) {
+    // column blocks fastest: neighbouring CTAs gather from the same image rows
+    const uint32_t rb = (uint32_t)(tl / n_cb), cb = (uint32_t)(tl - (uint64_t)rb * n_cb);
+    const uint32_t r0 = rb * kUtRows, c0 = cb * kUtCols;
+    const uint32_t row = r0 + (uint32_t)lane;  // this lane's output row
+    const bool row_ok = row < rows;
+    const uint32_t r1 = fdiv(row, d.f_ow), ow = row - r1 * d.f_ow.d;
+    const uint32_t b = fdiv(r1, d.f_oh), oh = r1 - b * d.f_oh.d;
+    const int32_t y0 = (int32_t)(oh * (uint32_t)d.sh) - (int32_t)d.ph;
+    const int32_t x0 = (int32_t)(ow * (uint32_t)d.sw) - (int32_t)d.pw;
+    const Idx base = (Idx)d.x_off + (Idx)b * (Idx)d.xs[0] + (Idx)y0 * (Idx)d.xs[2] + (Idx)x0 * (Idx)d.xs[3];
+    T v[kUtCols / kWarps];
 #pragma unroll
-        for (int u = 0; u < kUnfoldVecU; ++u) {
-          const uint32_t ev = e0 + (uint32_t)u * kThreads;
-          if (ev < nv) {
-            const uint32_t e = ev * EV;
-            const uint32_t q = fdiv(e, d.f_patch), col = e - q * patch;
-            const UnfoldRow& ri = rinfo[q];
-            const Pack<uint32_t, EV> ij = *reinterpret_cast<const Pack<uint32_t, EV>*>(&tij[col]);
-            const Pack<int32_t, EV> of = *reinterpret_cast<const Pack<int32_t, EV>*>(&toff32[col]);
-#pragma unroll
-            for (int t = 0; t < EV; ++t) {
-              const uint32_t y = (uint32_t)(ri.y0 + (int32_t)(ij.v[t] >> 16));
-              const uint32_t xx = (uint32_t)(ri.x0 + (int32_t)(ij.v[t] & 0xFFFFu));
-              v[u].v[t] = (y < H && xx < W) ? x[ri.base + of.v[t]] : T(0);
-            }
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < kUnfoldVecU; ++u) {
-          const uint32_t ev = e0 + (uint32_t)u * kThreads;
-          if (ev < nv) *reinterpret_cast<Pack<T, EV>*>(gout + (size_t)ev * EV) = v[u];
-        }
-      }
-    } else {
-      const uint32_t n = nr * patch;  // < 2^32: rows * patch < 2^32
-      for (uint32_t e0 = threadIdx.x; e0 < n; e0 += kThreads * kColsU) {
-        T v[kColsU];
-        int64_t at[kColsU];
-#pragma unroll
-        for (int u = 0; u < kColsU; ++u) {
-          const uint32_t e = e0 + (uint32_t)u * kThreads;
-          v[u] = T(0);
-          at[u] = -1;
-          if (e < n) {
-            const uint32_t q = fdiv(e, d.f_patch), col = e - q * patch;
-            const UnfoldRow& ri = rinfo[q];
-            const uint32_t ij = tij[col];
-            const uint32_t y = (uint32_t)(ri.y0 + (int32_t)(ij >> 16));
-            const uint32_t xx = (uint32_t)(ri.x0 + (int32_t)(ij & 0xFFFFu));
-            if (y < H && xx < W) v[u] = x[ri.base + toff64[col]];
-            at[u] = ri.obase + (int64_t)col * d.cs[1];
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < kColsU; ++u)
-          if (at[u] >= 0) out[at[u]] = v[u];
+    for (int k = 0; k < kUtCols / kWarps; ++k) {
+      const uint32_t col = c0 + (uint32_t)(warp + k * kWarps);
+      v[k] = T(0);
+      if (col < patch) {
+        const int2 e = tab[col];
+        const uint32_t ij = (uint32_t)e.y;
+        const uint32_t y = (uint32_t)(y0 + (int32_t)(ij >> 16)), xx = (uint32_t)(x0 + (int32_t)(ij & 0xFFFFu));
+        if (row_ok && y < H && xx < W) v[k] = x[base + (Idx)e.x];
       }
     }
-    __syncthreads();  // every thread is done with this group's rows
+#pragma unroll
+    for (int k = 0; k < kUtCols / kWarps; ++k) tile[warp + k * kWarps][lane] = v[k];
+    __syncthreads();
+    // store: warp w writes tile rows w, w + 8, ...; lanes along the columns
+#pragma unroll
+    for (int rr = warp; rr < kUtRows; rr += kWarps) {
+      const uint32_t orow = r0 + (uint32_t)rr;
+      if (orow < rows) {
+        const Idx ob = (Idx)d.c_off + (Idx)orow * (Idx)d.cs[0];
+#pragma unroll
+        for (int h = 0; h < kUtCols / 32; ++h) {
+          const uint32_t col = c0 + (uint32_t)(lane + 32 * h);
+          if (col < patch) out[ob + (Idx)col * (Idx)d.cs[1]] = tile[lane + 32 * h][rr];
+        }
+      }
+    }
+    __syncthreads();  // the tile is free for the next one
   }
 }
 
@@ -700,6 +661,7 @@ Error cols_setup(const char* fn, const trs_view* img, int64_t kh, int64_t kw, in
   d->patch = d->C * kh * kw;
   d->rows = d->B * d->OH * d->OW;
   d->x_off = img->offset;
+  d->x_len = img->storage_len;
   for (int i = 0; i < 4; ++i) d->xs[i] = img->strides[i];
   // the kernels decode indices in 32 bits
   const uint64_t lim = 1ull << 32;
@@ -781,43 +743,47 @@ Error launch_cols(bool unfold, const ColsDev& d, cudaStream_t stream) {
       return check_launch("fold_2d kernel");
     }
   }
+  if (unfold) {
+    if (d.rows == 0 || d.patch == 0) return Error{};
+    // the transposed tile when the patch's column table fits (patch <= 2048,
+    // i and j in 16 bits) and every table offset is within 31 bits
+    const uint64_t max_off = (uint64_t)std::llabs(d.xs[1]) * (uint64_t)(d.C > 0 ? d.C - 1 : 0) +
+                             (uint64_t)std::llabs(d.xs[2]) * (uint64_t)(d.kh > 0 ? d.kh - 1 : 0) +
+                             (uint64_t)std::llabs(d.xs[3]) * (uint64_t)(d.kw > 0 ? d.kw - 1 : 0);
+    if (d.patch <= kUnfoldTab && d.kh < 65536 && d.kw < 65536 && max_off < (1ull << 31) &&
+        d.rows < (1ll << 32) - kUtRows) {
+      // 32-bit indices when the image's and the columns' storage, with the
+      // padding's reach before the image, stay below 2^31 elements
+      const uint64_t pad = (uint64_t)std::llabs(d.xs[2]) * (uint64_t)d.ph + (uint64_t)std::llabs(d.xs[3]) * (uint64_t)d.pw;
+      const bool i32 = (uint64_t)d.x_len + max_off + pad < (1ull << 31) && (uint64_t)d.c_len < (1ull << 31);
+      const void* kt = i32 ? (const void*)unfold_tile_kernel<T, true> : (const void*)unfold_tile_kernel<T, false>;
+      const uint64_t tiles =
+          (((uint64_t)d.rows + kUtRows - 1) / kUtRows) * (((uint64_t)d.patch + kUtCols - 1) / kUtCols);
+      const uint64_t cap =
+          (uint64_t)current_device_info().sm_count * (uint64_t)resident_blocks_smem(kt, kThreads, 0);
+      const unsigned g = (unsigned)(tiles < cap ? tiles : cap);
+      if (i32)
+        unfold_tile_kernel<T, true><<<g, kThreads, 0, stream>>>(d);
+      else
+        unfold_tile_kernel<T, false><<<g, kThreads, 0, stream>>>(d);
+      return check_launch("unfold_2d kernel");
+    }
+    const uint64_t items = ((uint64_t)d.rows * (uint64_t)d.patch + kColsU - 1) / kColsU;
+    unfold_kernel<T><<<cols_grid((const void*)unfold_kernel<T>, items), kThreads, 0, stream>>>(d);
+    return check_launch("unfold_2d kernel");
+  }
   // windows that can cover one pixel: ceil(kh / sh) * ceil(kw / sw)
   const int64_t cover = ((d.kh + d.sh - 1) / d.sh) * ((d.kw + d.sw - 1) / d.sw);
   const bool regs = cover <= kFoldRegs;
-  // the table form when a row's columns fit its table (and i, j fit 16 bits)
-  const bool tab = unfold && d.patch <= kUnfoldTab && d.kh < 65536 && d.kw < 65536;
-  // the vector form: contiguous columns, patch % EV == 0, 16-byte aligned
-  // start, every table offset within 31 bits
-  constexpr int EV = 16 / (int)sizeof(T);
-  const uint64_t max_off = (uint64_t)std::llabs(d.xs[1]) * (uint64_t)(d.C > 0 ? d.C - 1 : 0) +
-                           (uint64_t)std::llabs(d.xs[2]) * (uint64_t)(d.kh > 0 ? d.kh - 1 : 0) +
-                           (uint64_t)std::llabs(d.xs[3]) * (uint64_t)(d.kw > 0 ? d.kw - 1 : 0);
-  const bool vec = tab && d.cs[1] == 1 && d.cs[0] == d.patch && d.patch % EV == 0 && d.c_off % EV == 0 &&
-                   ((uintptr_t)d.dst + (uintptr_t)d.c_off * sizeof(T)) % 16 == 0 && max_off < (1ull << 31);
-  const void* k = unfold ? (tab ? (vec ? (const void*)unfold_tab_kernel<T, true> : (const void*)unfold_tab_kernel<T, false>)
-                                : (const void*)unfold_kernel<T>)
-                         : (regs ? (const void*)fold_kernel<T, true> : (const void*)fold_kernel<T, false>);
-  // rows per pass of the table form: about kThreads * kColsU elements; the
-  // vector form, at most one chunk of EV elements per thread and unroll step
-  const uint64_t pt = (uint64_t)(d.patch > 0 ? d.patch : 1);
-  const uint64_t want = vec ? (uint64_t)kThreads * kUnfoldVecU * EV / pt : ((uint64_t)kThreads * kColsU + pt - 1) / pt;
-  const uint32_t group = (uint32_t)(want < 1 ? 1 : (want > (uint64_t)kUnfoldGroup ? kUnfoldGroup : want));
-  const uint64_t items = unfold ? (tab ? ((uint64_t)d.rows + group - 1) / group * kThreads
-                                       : ((uint64_t)d.rows * (uint64_t)d.patch + kColsU - 1) / kColsU)
-                                : (uint64_t)(d.B * d.C * d.H * d.W);
-  if (items == 0 || (unfold && d.patch == 0)) return Error{};
+  const uint64_t items = (uint64_t)(d.B * d.C * d.H * d.W);
+  if (items == 0) return Error{};
+  const void* k = regs ? (const void*)fold_kernel<T, true> : (const void*)fold_kernel<T, false>;
   const unsigned g = cols_grid(k, items);
-  if (unfold && vec)
-    unfold_tab_kernel<T, true><<<g, kThreads, 0, stream>>>(d, group);
-  else if (unfold && tab)
-    unfold_tab_kernel<T, false><<<g, kThreads, 0, stream>>>(d, group);
-  else if (unfold)
-    unfold_kernel<T><<<g, kThreads, 0, stream>>>(d);
-  else if (regs)
+  if (regs)
     fold_kernel<T, true><<<g, kThreads, 0, stream>>>(d);
   else
     fold_kernel<T, false><<<g, kThreads, 0, stream>>>(d);
-  return check_launch(unfold ? "unfold_2d kernel" : "fold_2d kernel");
+  return check_launch("fold_2d kernel");
 }
 
 Error dispatch_cols(bool unfold, int dt, const ColsDev& d, cudaStream_t stream) {
@@ -851,6 +817,7 @@ Error run_unfold(const trs_view* x, int64_t kh, int64_t kw, int64_t sh, int64_t 
   d.src = x->data;
   d.dst = out->data;
   d.c_off = out->offset;
+  d.c_len = out->storage_len;
   d.cs[0] = out->strides[0];
   d.cs[1] = out->strides[1];
   return dispatch_cols(true, x->dtype, d, stream);
@@ -875,6 +842,7 @@ Error run_fold(const trs_view* cols, int64_t kh, int64_t kw, int64_t sh, int64_t
   d.src = cols->data;
   d.dst = out->data;
   d.c_off = cols->offset;
+  d.c_len = cols->storage_len;
   d.cs[0] = cols->strides[0];
   d.cs[1] = cols->strides[1];
   d.step_oh = d.OW * d.cs[0] - d.sh * d.kw * d.cs[1];
