@@ -451,8 +451,11 @@ struct FoldTile {
 // ceil(kw / sw) <= WIN), and the window loops are unrolled WIN x WIN with each
 // add predicated on the window existing, so the adds keep their (oh, ow)
 // order; WIN = 0: loops bounded at run time.
-template <class T, int WIN>
+// I32: the columns' and the image's storage are below 2^31 elements, so the
+// global index arithmetic runs in 32 bits.
+template <class T, int WIN, bool I32>
 __global__ void __launch_bounds__(kThreads) fold_smem_kernel(const ColsDev d, const FoldTile t) {
+  using Idx = typename std::conditional<I32, int32_t, int64_t>::type;
   using A = Arith<T>;
   extern __shared__ __align__(16) unsigned char fold_raw[];
   T* sm = reinterpret_cast<T*>(fold_raw);
@@ -476,13 +479,13 @@ __global__ void __launch_bounds__(kThreads) fold_smem_kernel(const ColsDev d, co
     const int32_t noh = oh_b - oh_a + 1;
     const int32_t seg_eff = ncb * kk;
     if (noh > 0) {
-      const int64_t row0 = ((int64_t)b * OH + oh_a) * OW;  // first window row of the tile
-      const int64_t src0 = d.c_off + row0 * d.cs[0] + (int64_t)c0 * kk * d.cs[1];
+      const Idx row0 = ((Idx)b * OH + oh_a) * OW;  // first window row of the tile
+      const Idx src0 = (Idx)d.c_off + row0 * (Idx)d.cs[0] + (Idx)c0 * kk * (Idx)d.cs[1];
       const uint32_t n_load = (uint32_t)(noh * OW) * (uint32_t)t.seg;
       for (uint32_t i = threadIdx.x; i < n_load; i += kThreads) {
         const uint32_t r = fdiv(i, t.f_seg), e = i - r * t.f_seg.d;
         if ((int32_t)e < seg_eff)
-          cp_async_elem<(int)sizeof(T)>(sm + (size_t)r * t.segp + e, cols + src0 + (int64_t)r * d.cs[0] + (int64_t)e * d.cs[1],
+          cp_async_elem<(int)sizeof(T)>(sm + (size_t)r * t.segp + e, cols + (src0 + (Idx)r * (Idx)d.cs[0] + (Idx)e * (Idx)d.cs[1]),
                                         (int)sizeof(T));
       }
       cp_async_commit();
@@ -518,7 +521,8 @@ __global__ void __launch_bounds__(kThreads) fold_smem_kernel(const ColsDev d, co
           for (int32_t ow = owl; ow <= owh; ++ow, at += step_ow) acc = A::add(acc, sm[at]);
         }
       }
-      out[d.x_off + (int64_t)b * d.xs[0] + (int64_t)c * d.xs[1] + (int64_t)y * d.xs[2] + (int64_t)x * d.xs[3]] = acc;
+      out[(Idx)d.x_off + (Idx)b * (Idx)d.xs[0] + (Idx)c * (Idx)d.xs[1] + (Idx)y * (Idx)d.xs[2] + (Idx)x * (Idx)d.xs[3]] =
+          acc;
     }
     __syncthreads();  // every thread is done with the tile's windows
   }
@@ -732,14 +736,20 @@ Error launch_cols(bool unfold, const ColsDev& d, cudaStream_t stream) {
       const int smem = (int)((int64_t)ft.noh * d.OW * ft.segp * (int64_t)sizeof(T));
       // windows covering a pixel, per dimension: the unrolled form up to 3
       const bool unrolled = (d.kh + d.sh - 1) / d.sh <= 3 && (d.kw + d.sw - 1) / d.sw <= 3;
-      const void* k = unrolled ? (const void*)fold_smem_kernel<T, 3> : (const void*)fold_smem_kernel<T, 0>;
+      const bool i32 = (uint64_t)d.c_len < (1ull << 31) && (uint64_t)d.x_len < (1ull << 31);
+      const void* k = unrolled ? (i32 ? (const void*)fold_smem_kernel<T, 3, true> : (const void*)fold_smem_kernel<T, 3, false>)
+                               : (i32 ? (const void*)fold_smem_kernel<T, 0, true> : (const void*)fold_smem_kernel<T, 0, false>);
       const uint64_t cap =
           (uint64_t)current_device_info().sm_count * (uint64_t)resident_blocks_smem(k, kThreads, smem);
       const unsigned g = (unsigned)((uint64_t)ft.tiles < cap ? (uint64_t)ft.tiles : cap);
-      if (unrolled)
-        fold_smem_kernel<T, 3><<<g, kThreads, smem, stream>>>(d, ft);
+      if (unrolled && i32)
+        fold_smem_kernel<T, 3, true><<<g, kThreads, smem, stream>>>(d, ft);
+      else if (unrolled)
+        fold_smem_kernel<T, 3, false><<<g, kThreads, smem, stream>>>(d, ft);
+      else if (i32)
+        fold_smem_kernel<T, 0, true><<<g, kThreads, smem, stream>>>(d, ft);
       else
-        fold_smem_kernel<T, 0><<<g, kThreads, smem, stream>>>(d, ft);
+        fold_smem_kernel<T, 0, false><<<g, kThreads, smem, stream>>>(d, ft);
       return check_launch("fold_2d kernel");
     }
   }

@@ -214,3 +214,21 @@ def test_conv2d_as_unfold_then_matmul():
     cols = device.unfold_2d(dx.view, (3, 3), (1, 1), (1, 1), empty(cols_ref.shape, np.float32))
     out = device.matmul(device.view_of(cols), dw.view, empty(want.shape, np.float32))
     assert_bit_exact(to_host(out), want, "conv2d as unfold + matmul")
+
+
+def test_unfold_and_fold_at_the_benchmark_size():
+    """unfold_2d / fold_2d of the measured configuration, X f32 [32, 64, 56, 56]
+    ~N(0,1), 3x3 windows, stride 1, padding 1 (57.8 M column elements), bit
+    for bit against the oracle."""
+    import oracle
+    from tensorrs_b200 import device
+    shape = [32, 64, 56, 56]
+    x = oracle.fill_normal(np.float32, int(np.prod(shape)), 7).reshape(shape)
+    dx = contiguous(x)
+    want = oracle.unfold_2d(dx.host_view(), (3, 3), (1, 1), (1, 1))
+    cols = device.unfold_2d(dx.view, (3, 3), (1, 1), (1, 1), empty(want.shape, np.float32))
+    assert_bit_exact(to_host(cols), want, "unfold_2d at the benchmark size")
+    c = oracle.fill_normal(np.float32, want.size, 8).reshape(want.shape)
+    dc = contiguous(c)
+    back = to_host(device.fold_2d(dc.view, (3, 3), (1, 1), (1, 1), empty(shape, np.float32)))
+    assert_bit_exact(back, oracle.fold_2d(dc.host_view(), shape, (3, 3), (1, 1), (1, 1)), "fold_2d at the benchmark size")
