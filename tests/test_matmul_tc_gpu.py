@@ -4,11 +4,13 @@ on the tensor cores (tcgen05, split TF32), through the C ABI.
 Not bit-identical by design (the tensor cores add the products in their own
 order and precision): every output is held to
     |gpu - ref| <= 1e-5 * sum_k |a_ik b_kj|
-against the reference's sequential f32 chain (the oracle), and to
+against the reference's sequential f32 chain (the oracle), and, on these
+shapes and seeds, to
     |gpu - exact| <= 2^-18 * sum_k |a_ik b_kj|
-against the exact product (f64), which the split into hi/lo TF32 parts
-(products kept to about 2^-21) and an f32 accumulation of K terms allow with
-margin.  Shapes cover the padding of every tile edge (M, N not multiples of
+against the exact product (f64) -- a regression bound, not a worst case: the
+split keeps products to about 2^-21, but an f32 accumulation of K terms can
+err by up to (K - 1) 2^-24 sum|ab| (random signs keep it near sqrt(K) 2^-24;
+the benchmark-size test below uses the worst case).  Shapes cover the padding of every tile edge (M, N not multiples of
 128, K not a multiple of 32), batches with broadcasting, transposed and
 offset views, K = 1 and K = 0."""
 from __future__ import annotations
@@ -132,20 +134,27 @@ def test_tf32x3_wide_tiles():
 
 
 def test_tf32x3_at_the_benchmark_size():
-    """[4096, 4096] x [4096, 4096] ~N(0,1), the measured configuration, held to
-    |gpu - exact| <= 2^-18 * sum_k |a_ik b_kj| against the product in f64 on the
-    GPU (the oracle's sequential chain is too slow at this size; the 1e-5 bound
-    against it is checked on the smaller shapes above)."""
+    """[4096, 4096] x [4096, 4096] ~N(0,1), the measured configuration.  The
+    reference's chain at this size comes from trs_matmul, which is bit-identical
+    to it (test_matmul_gpu.py): every output within 1e-5 * sum_k |a_ik b_kj| of
+    it, and within the worst case of an f32 accumulation of K split products,
+    ((K - 1) 2^-24 + 2^-21) * sum_k |a_ik b_kj|, of the exact product (f64)."""
     import torch
     from tensorrs_b200 import device
     n = 4096
     g = torch.Generator(device="cuda").manual_seed(61)
     a = torch.randn(n, n, device="cuda", generator=g)
     b = torch.randn(n, n, device="cuda", generator=g)
+    va, vb = device.view_of(a), device.view_of(b)
     out = torch.empty(n, n, device="cuda")
-    device.matmul_tf32x3(device.view_of(a), device.view_of(b), out)
+    device.matmul_tf32x3(va, vb, out)
+    ref = torch.empty(n, n, device="cuda")
+    device.matmul(va, vb, ref)
     exact = a.double() @ b.double()
     mag = a.double().abs() @ b.double().abs()
-    worst = float(((out.double() - exact).abs() / mag).max())
-    assert worst <= 2.0**-18, worst
-    print(f"4096^3: worst |gpu - exact| / sum|ab| = {worst:.2e}")
+    got = out.double()
+    worst_ref = float(((got - ref.double()).abs() / mag).max())
+    worst_exact = float(((got - exact).abs() / mag).max())
+    assert worst_ref <= 1e-5, worst_ref
+    assert worst_exact <= (n - 1) * 2.0**-24 + 2.0**-21, worst_exact
+    print(f"4096^3: worst / sum|ab|: {worst_ref:.2e} against the reference's chain, {worst_exact:.2e} against exact")
