@@ -539,10 +539,17 @@ Error launch_cluster(K kernel, unsigned grid, unsigned threads, unsigned cluster
 constexpr int kRsConsumerWarps = 8;
 constexpr int kRsThreads = 32 * (1 + kRsConsumerWarps);
 constexpr int kRsTileBytes = 16384;
+// Shared memory per CTA for the stages: 100 KiB (two CTAs per SM, up to 6
+// stages of one input) in general; 64 KiB for max / argmax, whose consumers
+// do more work per byte and gain more from a third CTA per SM (27 warps) than
+// from deeper stages (measured on rows of 64 KiB: 0.83 -> 0.98 of the copy
+// peak, where sum and the two-input gradients lose with it).
 constexpr int kRsBudget = 100 * 1024;
+constexpr int kRsBudgetMax = 64 * 1024;
 
-__host__ __device__ constexpr int rs_stages(int nb) {
-  return kRsBudget / (nb * kRsTileBytes) > 8 ? 8 : (kRsBudget / (nb * kRsTileBytes) < 2 ? 2 : kRsBudget / (nb * kRsTileBytes));
+__host__ __device__ constexpr int rs_stages(int nb, int mode) {
+  const int budget = (mode == kRedMax || mode == kRedArgmax) ? kRsBudgetMax : kRsBudget;
+  return budget / (nb * kRsTileBytes) > 8 ? 8 : (budget / (nb * kRsTileBytes) < 2 ? 2 : budget / (nb * kRsTileBytes));
 }
 
 __device__ __forceinline__ FastDiv fd3(const uint32_t* v) {
@@ -603,7 +610,7 @@ __global__ void __launch_bounds__(kRsThreads) red_stream_kernel(const RedDev d) 
   using Acc = typename A::Acc;
   constexpr int V = 16 / (int)sizeof(T);
   constexpr int TILE = kRsTileBytes / (int)sizeof(T);
-  constexpr int S = rs_stages(NB);
+  constexpr int S = rs_stages(NB, MODE);
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * NB * kRsTileBytes);
   uint64_t* empty = full + S;
@@ -1244,7 +1251,7 @@ Error red_launch(RedDev& d, const RedChoice& c, cudaStream_t stream) {
   if (c.variant == kRedRowStream) {
     const void* k = pick_red_stream<T>(d.mode, c.nb);
     if (!k) return make_error(TRS_ERR_ARG, "no stream reduction kernel for this mode");
-    const int S = rs_stages(c.nb);
+    const int S = rs_stages(c.nb, d.mode);
     const int smem = S * c.nb * kRsTileBytes + 2 * S * 8;
     allow_smem(k, smem);  // once per kernel
     const int per_sm = resident_blocks_smem(k, kRsThreads, smem);
