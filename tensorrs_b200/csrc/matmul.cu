@@ -87,6 +87,41 @@ struct AccTile {
   __device__ __forceinline__ T get(int i, int j) const { return v[i][j]; }
 };
 
+// f32 on sm_100's packed units, two outputs per instruction.  The product is
+// taken as fma(a, b, +0) in f32x2: a * b + 0 rounds exactly as the product
+// alone, except that a -0 product becomes +0 -- which cannot change the chain,
+// since acc starts at +0 and a round-to-nearest sum is -0 only when both of its
+// terms are -0, so acc is never -0 and acc + (+-0) == acc.  The sum is a
+// separate f32x2 add.  (A packed multiply followed by a packed add was
+// contracted into one FMA by the compiler; an FMA followed by an add is not.)
+#ifndef TRS_MM_PACKED
+#define TRS_MM_PACKED 1
+#endif
+#if TRS_MM_PACKED
+template <int TM, int TN>
+struct AccTile<float, TM, TN> {
+  static_assert(TN % 2 == 0, "pairs of columns");
+  float2 v[TM][TN / 2];
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+      for (int j = 0; j < TN / 2; ++j) v[i][j] = make_float2(0.0f, 0.0f);
+  }
+  __device__ __forceinline__ void step(const float (&a)[TM], const float (&b)[TN]) {
+    const float2 zero2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+      const float2 a2 = make_float2(a[i], a[i]);
+#pragma unroll
+      for (int j = 0; j < TN / 2; ++j)
+        v[i][j] = __fadd2_rn(v[i][j], __ffma2_rn(a2, make_float2(b[2 * j], b[2 * j + 1]), zero2));
+    }
+  }
+  __device__ __forceinline__ float get(int i, int j) const { return (j & 1) ? v[i][j >> 1].y : v[i][j >> 1].x; }
+};
+#endif
+
 // Asynchronous global -> shared copy of one element (4 or 8 bytes); src_bytes
 // 0 writes zeros without reading (the slab's padding beyond M, N or K).
 template <int BYTES>
