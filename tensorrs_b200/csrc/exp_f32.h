@@ -189,7 +189,8 @@ __device__ __forceinline__ float sigmoid(float x) {
   return sigmoid_div(x >= 0.0f ? 1.0f : e, d, y0);
 }
 
-// sigmoid of two values at once on sm_100's packed f32x2 add / multiply /
+// exp_nonpos2: `exp_nonpos` of two values at once; sigmoid2: `sigmoid` of two
+// values at once -- both on sm_100's packed f32x2 add / multiply /
 // fused multiply-add (each lane rounded to nearest exactly as the scalar
 // instruction rounds, subnormals kept), so each pair costs one issue slot
 // where `sigmoid` above takes two.  Unlike the scalar __fmul_rn / __fadd_rn,
@@ -207,13 +208,12 @@ __device__ __forceinline__ float sigmoid(float x) {
 // clamp at -104 is max.NaN (a NaN passes through, as the scalar compare
 // lets it); the table loads, the exponent scaling, the reciprocal seed, the
 // reciprocal floor and the numerator choice stay per lane.
-__device__ __forceinline__ float2 sigmoid2(float2 x) {
-  float2 y;
-  asm("max.NaN.f32 %0, %1, 0fC2D00000;" : "=f"(y.x) : "f"(-fabsf(x.x)));  // max(-|x|, -104)
-  asm("max.NaN.f32 %0, %1, 0fC2D00000;" : "=f"(y.y) : "f"(-fabsf(x.y)));
-  const float2 mh = make_float2(kBaseE.mh, kBaseE.mh), ml = make_float2(kBaseE.ml, kBaseE.ml);
+__device__ __forceinline__ float2 exp_nonpos2(float2 y, Base b) {
+  asm("max.NaN.f32 %0, %1, 0fC2D00000;" : "=f"(y.x) : "f"(y.x));  // max(y, -104)
+  asm("max.NaN.f32 %0, %1, 0fC2D00000;" : "=f"(y.y) : "f"(y.y));
+  const float2 mh = make_float2(b.mh, b.mh), ml = make_float2(b.ml, b.ml);
   const float2 shift = make_float2(12582912.0f, 12582912.0f);  // 1.5 * 2^23
-  const float2 m1 = make_float2(-1.0f, -1.0f), one = make_float2(1.0f, 1.0f);
+  const float2 m1 = make_float2(-1.0f, -1.0f);
   const float2 t = __ffma2_rn(y, mh, shift);
   const uint32_t tbx = __float_as_uint(t.x), tby = __float_as_uint(t.y);
   const float2 nkf = __ffma2_rn(t, m1, shift);  // -(t - shift)
@@ -230,7 +230,12 @@ __device__ __forceinline__ float2 sigmoid2(float2 x) {
   // ((t >> 4) << 23) + (191 << 23) modulo 2^32 is its f32 bit pattern
   const float2 p2 = make_float2(__uint_as_float((tbx >> 4) * (1u << 23) + (191u << 23)),
                                 __uint_as_float((tby >> 4) * (1u << 23) + (191u << 23)));
-  const float2 e = __fmul2_rn(__fmul2_rn(s, p2), make_float2(0x1p-64f, 0x1p-64f));
+  return __fmul2_rn(__fmul2_rn(s, p2), make_float2(0x1p-64f, 0x1p-64f));
+}
+
+__device__ __forceinline__ float2 sigmoid2(float2 x) {
+  const float2 m1 = make_float2(-1.0f, -1.0f), one = make_float2(1.0f, 1.0f);
+  const float2 e = exp_nonpos2(make_float2(-fabsf(x.x), -fabsf(x.y)), kBaseE);
   const float2 d = __fadd2_rn(one, e);
   const float2 nd = __ffma2_rn(e, m1, m1);  // -d
   float2 y0;

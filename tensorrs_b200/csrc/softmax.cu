@@ -469,8 +469,15 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
 #pragma unroll
           for (int i = 0; i < V; ++i) {
             if constexpr (kF32) {
-              const float e = expf32::exp_nonpos(__fsub_rn(v.v[i], m), expf32::kBaseEf32);
-              v.v[i] = e;
+              // two lanes at a time on the packed units (exp_nonpos2 is
+              // exp_nonpos lane by lane; x - m is the packed add of -m)
+              if (i % 2 == 0) {
+                const float2 e2 = expf32::exp_nonpos2(
+                    __fadd2_rn(make_float2(v.v[i], v.v[i + 1]), make_float2(-m, -m)), expf32::kBaseEf32);
+                v.v[i] = e2.x;
+                v.v[i + 1] = e2.y;
+              }
+              const float e = v.v[i];
               emin = fminf(emin, e);
               accs[i] = accs[i] + (double)e;
             } else {
@@ -515,11 +522,14 @@ __global__ void __launch_bounds__(kSmThreads, 1) softmax_stream_kernel(const SmD
             const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
             SVec<T, V> r;
 #pragma unroll
-            for (int i = 0; i < V; ++i) {
-              const float e = v.v[i];
-              const float q0 = __fmaf_rn(e, yh, __fmul_rn(e, yl));
-              const float rem = __fmaf_rn(-q0, sum, e);
-              r.v[i] = __fmaf_rn(rem, yh, q0);
+            for (int i = 0; i < V; i += 2) {  // the same steps, two lanes at a time
+              const float2 e = make_float2(v.v[i], v.v[i + 1]);
+              const float2 yh2 = make_float2(yh, yh), yl2 = make_float2(yl, yl);
+              const float2 q0 = __ffma2_rn(e, yh2, __fmul2_rn(e, yl2));
+              const float2 rem = __ffma2_rn(make_float2(-q0.x, -q0.y), make_float2(sum, sum), e);
+              const float2 q = __ffma2_rn(rem, yh2, q0);
+              r.v[i] = q.x;
+              r.v[i + 1] = q.y;
             }
             sstore_stream<T, V>(orow + (size_t)k * V, r);
           }
