@@ -528,10 +528,18 @@ trs_status trs_sharded_elementwise_sum(trs_comm* comm,
                                        trs_view* sum_out, trs_stream stream);
 
 /* sum_axis(0) / max_axis(0) / argmax_axis(0) of a tensor split on axis 0:
- * per-rank partial rows combined with an all-reduce (sum: f64 partials;
- * max: value-and-index pairs gathered and combined in rank order, so ties
- * keep the lowest global index).  `out` is the full [rest...] result on every
- * rank; argmax writes global indices as i64. */
+ * each rank reduces its rows into partials (sum: f64 / wrapping accumulators;
+ * max: value-and-index records), and every rank combines all ranks' partials
+ * in rank order (sums rounded once; ties keep the lowest global index, as the
+ * reference's scan does).  Where every rank mapped every peer's exchange
+ * buffer (trs_comm_peer_exchange) and the partials fit 8 MiB, the combine
+ * reads the peers' partials over NVLink in one kernel after each rank has
+ * published its own (no collective for the sum; max/argmax exchange their row
+ * counts first, for the global indices and the empty-axis check); otherwise
+ * through an NCCL all-reduce / all-gather.  A peer that does not make the call
+ * leaves the combine waiting about 2 s: the results are then NaN (0 for
+ * integers, -1 for argmax) and trs_async_error() reports bit 1.  `out` is the
+ * full [rest...] result on every rank; argmax writes global indices as i64. */
 trs_status trs_sharded_sum_axis0(trs_comm* comm, const trs_view* shard,
                                  trs_view* out, trs_stream stream);
 trs_status trs_sharded_max_axis0(trs_comm* comm, const trs_view* shard,

@@ -47,6 +47,7 @@ struct trs_comm {
   unsigned long long** xpeers = nullptr; // device array: every rank's buffer, mapped here
   std::vector<void*> xopened;            // IPC mappings of the peers' buffers
   unsigned long long xseq = 0;           // sequence number of the last sharded sum
+  unsigned long long xseq_a0 = 0;        // ... and of the last sharded axis-0 exchange
 };
 
 namespace {
@@ -158,7 +159,7 @@ Error setup_exchange(trs_comm* c) {
   cudaError_t ce = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
   if (ce != cudaSuccess) return cuda_error(ce, "cudaStreamCreateWithFlags");
   int ok = wanted ? 1 : 0;
-  const size_t bytes = (size_t)2 * R * 2 * sizeof(unsigned long long);
+  const size_t bytes = x_buffer_bytes(R);  // sum slots, axis-0 flags and arenas
   if (ok && cudaMalloc(&c->xbuf, bytes) != cudaSuccess) ok = 0;
   if (ok && cudaMemset(c->xbuf, 0, bytes) != cudaSuccess) ok = 0;
   cudaIpcMemHandle_t mine;
@@ -280,59 +281,18 @@ Error nccl_call(trs_comm* c, ncclResult_t r, const char* what) {
 
 enum Axis0Op { kAxis0Sum, kAxis0Max, kAxis0Argmax };
 
-// sum_axis(0) / max_axis(0) / argmax_axis(0) of a tensor split on axis 0.
-Error sharded_axis0(trs_comm* c, int op, const trs_view* shard, const trs_view* out, cudaStream_t stream) {
-  if (!c || !c->comm) return make_error(TRS_ERR_ARG, "null communicator");
-  Error e = validate_view(shard, "shard");
-  if (!e.ok()) return e;
-  e = validate_view(out, "output");
-  if (!e.ok()) return e;
-  if (shard->ndim < 1) return make_error(TRS_ERR_AXIS, "!!!Axis index out of range!!!");
-  const int dt = shard->dtype;
-  if (out->dtype != (op == kAxis0Argmax ? (int)TRS_I64 : dt))
-    return make_error(TRS_ERR_DTYPE, op == kAxis0Argmax ? "argmax output must be i64" : "output dtype differs");
-  bool ok = out->ndim == shard->ndim - 1;
-  for (int i = 1; ok && i < shard->ndim; ++i) ok = out->shape[i - 1] == shard->shape[i];
-  if (!ok) return make_error(TRS_ERR_SHAPE, "output shape must be the shard shape without axis 0");
-  Nccl& n = nccl();
-  const int R = c->nranks;
-  // every rank's row count: the global index offset of this shard, and the
-  // empty-axis check of max/argmax
-  Scratch counts;
-  e = counts.alloc(sizeof(int64_t) * (R + 1), stream);
-  if (!e.ok()) return e;
-  int64_t* cnt = counts.as<int64_t>();
-  const int64_t mine = shard->shape[0];
-  cudaError_t ce = cudaMemcpyAsync(cnt + R, &mine, sizeof(int64_t), cudaMemcpyHostToDevice, stream);
-  if (ce != cudaSuccess) return cuda_error(ce, "cudaMemcpyAsync");
-  e = nccl_call(c, n.AllGather(cnt + R, cnt, 1, ncclInt64, c->comm, stream), "ncclAllGather (row counts)");
-  if (!e.ok()) return e;
-  std::vector<int64_t> all(R);
-  ce = cudaMemcpyAsync(all.data(), cnt, sizeof(int64_t) * R, cudaMemcpyDeviceToHost, stream);
-  if (ce == cudaSuccess) ce = cudaStreamSynchronize(stream);
-  if (ce != cudaSuccess) return cuda_error(ce, "reading the row counts");
-  int64_t total = 0, base = 0;
-  int first_rank = -1;
-  for (int r = 0; r < R; ++r) {
-    if (r < c->rank) base += all[r];
-    if (first_rank < 0 && all[r] > 0) first_rank = r;
-    total += all[r];
-  }
-  if (op != kAxis0Sum && total == 0) return make_error(TRS_ERR_EMPTY_AXIS, "!!!Cannot reduce an empty axis!!!");
-  const int64_t nout = numel_of(out->shape, out->ndim);
-  // local partials, unrounded, into a contiguous scratch buffer
-  const size_t rec = op == kAxis0Sum ? (dt == TRS_I32 ? 4 : 8) : max_record_size(dt);
-  const size_t slots = op == kAxis0Sum ? 1 : (size_t)R;
-  Scratch part;
-  e = part.alloc(rec * (size_t)(nout > 0 ? nout : 1) * slots, stream);
-  if (!e.ok()) return e;
-  char* mine_at = part.as<char>() + (op == kAxis0Sum ? 0 : rec * (size_t)nout * (size_t)c->rank);
+// This rank's partials of sum_axis(0) / max_axis(0) / argmax_axis(0) (f64 or
+// wrapping accumulators, or max records with global indices from `base`),
+// unrounded, contiguous at `dst`.
+Error axis0_local(int op, const trs_view* shard, const trs_view* out, int64_t base, void* dst, int64_t nout,
+                  cudaStream_t stream) {
+  if (nout == 0) return Error{};
   trs_view pv;
   std::memset(&pv, 0, sizeof(pv));
-  pv.data = mine_at;
-  pv.dtype = dt;
+  pv.data = dst;
+  pv.dtype = shard->dtype;
   pv.ndim = out->ndim;
-  pv.storage_len = nout > 0 ? nout : 1;
+  pv.storage_len = nout;
   int64_t step = 1;
   for (int i = out->ndim - 1; i >= 0; --i) {
     pv.shape[i] = out->shape[i];
@@ -348,10 +308,24 @@ Error sharded_axis0(trs_comm* c, int op, const trs_view* shard, const trs_view* 
   for (int i = 0; i < shard->ndim; ++i) q.op_strides[0][i] = shard->strides[i];
   q.out[0] = &pv;
   for (int i = 1; i < shard->ndim; ++i) q.out_strides[0][i] = pv.strides[i - 1];
-  if (nout > 0) {
-    e = run_reduce(q, stream);
-    if (!e.ok()) return e;
-  }
+  return run_reduce(q, stream);
+}
+
+// The combine through NCCL: an all-reduce of the f64 partials, or an
+// all-gather of every rank's max records folded in rank order.
+Error axis0_combine_nccl(trs_comm* c, int op, const trs_view* shard, const trs_view* out, int64_t base,
+                         int first_rank, int64_t nout, cudaStream_t stream) {
+  Nccl& n = nccl();
+  const int R = c->nranks;
+  const int dt = shard->dtype;
+  const size_t rec = op == kAxis0Sum ? (dt == TRS_I32 ? 4 : 8) : max_record_size(dt);
+  const size_t slots = op == kAxis0Sum ? 1 : (size_t)R;
+  Scratch part;
+  Error e = part.alloc(rec * (size_t)(nout > 0 ? nout : 1) * slots, stream);
+  if (!e.ok()) return e;
+  char* mine_at = part.as<char>() + (op == kAxis0Sum ? 0 : rec * (size_t)nout * (size_t)c->rank);
+  e = axis0_local(op, shard, out, base, mine_at, nout, stream);
+  if (!e.ok()) return e;
   if (op == kAxis0Sum) {
     e = nccl_call(c, n.AllReduce(part.get(), part.get(), (size_t)nout, acc_type(dt), ncclSum, c->comm, stream),
                   "ncclAllReduce (partial sums)");
@@ -362,6 +336,85 @@ Error sharded_axis0(trs_comm* c, int op, const trs_view* shard, const trs_view* 
                 "ncclAllGather (max records)");
   if (!e.ok()) return e;
   return run_max_records(dt, part.get(), R, first_rank, out, op == kAxis0Argmax, stream);
+}
+
+// The combine over NVLink peer memory: this rank's partials go into its own
+// arena of the call's parity, the publish kernel tells every peer, and the
+// combine kernel reads every rank's partials in rank order (the same order
+// on every rank) once every rank has published.  A rank cannot start call
+// c + 2 (the same parity) before every rank has published call c + 1, which
+// each does only after finishing call c, so no arena is overwritten while a
+// peer still reads it.
+Error axis0_combine_peers(trs_comm* c, int op, const trs_view* shard, const trs_view* out, int64_t base,
+                          int first_rank, int64_t nout, cudaStream_t stream) {
+  Axis0Exchange x;
+  x.peers = c->xpeers;
+  x.world = c->nranks;
+  x.rank = c->rank;
+  x.seq = ++c->xseq_a0;
+  x.parity = (int)(x.seq & 1u);
+  x.flags_off = x_flags_off(c->nranks);
+  x.arena_off = x_arena_off(c->nranks);
+  x.err = async_error_word();
+  char* mine = reinterpret_cast<char*>(c->xbuf) + x.arena_off + (size_t)x.parity * kAxis0Arena;
+  Error e = axis0_local(op, shard, out, base, mine, nout, stream);
+  if (!e.ok()) return e;
+  e = run_axis0_publish(x, stream);
+  if (!e.ok()) return e;
+  if (op == kAxis0Sum) return run_axis0_sum_combine(shard->dtype, x, out, stream);
+  return run_axis0_max_combine(shard->dtype, x, first_rank, out, op == kAxis0Argmax, stream);
+}
+
+// sum_axis(0) / max_axis(0) / argmax_axis(0) of a tensor split on axis 0.
+Error sharded_axis0(trs_comm* c, int op, const trs_view* shard, const trs_view* out, cudaStream_t stream) {
+  if (!c || !c->comm) return make_error(TRS_ERR_ARG, "null communicator");
+  Error e = validate_view(shard, "shard");
+  if (!e.ok()) return e;
+  e = validate_view(out, "output");
+  if (!e.ok()) return e;
+  if (shard->ndim < 1) return make_error(TRS_ERR_AXIS, "!!!Axis index out of range!!!");
+  const int dt = shard->dtype;
+  if (out->dtype != (op == kAxis0Argmax ? (int)TRS_I64 : dt))
+    return make_error(TRS_ERR_DTYPE, op == kAxis0Argmax ? "argmax output must be i64" : "output dtype differs");
+  bool ok = out->ndim == shard->ndim - 1;
+  for (int i = 1; ok && i < shard->ndim; ++i) ok = out->shape[i - 1] == shard->shape[i];
+  if (!ok) return make_error(TRS_ERR_SHAPE, "output shape must be the shard shape without axis 0");
+  const int R = c->nranks;
+  const int64_t nout = numel_of(out->shape, out->ndim);
+  const size_t rec = op == kAxis0Sum ? (dt == TRS_I32 ? 4 : 8) : max_record_size(dt);
+  // the same choice on every rank (it depends on the output's shape only)
+  const bool peers = c->xpeers != nullptr && (size_t)nout * rec <= kAxis0Arena;
+  int64_t base = 0;
+  int first_rank = 0;
+  if (op != kAxis0Sum || !peers) {
+    // every rank's row count: the global index offset of this shard, the
+    // lowest rank holding rows, and the empty-axis check of max/argmax
+    Nccl& n = nccl();
+    Scratch counts;
+    e = counts.alloc(sizeof(int64_t) * (R + 1), stream);
+    if (!e.ok()) return e;
+    int64_t* cnt = counts.as<int64_t>();
+    const int64_t mine = shard->shape[0];
+    cudaError_t ce = cudaMemcpyAsync(cnt + R, &mine, sizeof(int64_t), cudaMemcpyHostToDevice, stream);
+    if (ce != cudaSuccess) return cuda_error(ce, "cudaMemcpyAsync");
+    e = nccl_call(c, n.AllGather(cnt + R, cnt, 1, ncclInt64, c->comm, stream), "ncclAllGather (row counts)");
+    if (!e.ok()) return e;
+    std::vector<int64_t> all(R);
+    ce = cudaMemcpyAsync(all.data(), cnt, sizeof(int64_t) * R, cudaMemcpyDeviceToHost, stream);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(stream);
+    if (ce != cudaSuccess) return cuda_error(ce, "reading the row counts");
+    int64_t total = 0;
+    first_rank = -1;
+    for (int r = 0; r < R; ++r) {
+      if (r < c->rank) base += all[r];
+      if (first_rank < 0 && all[r] > 0) first_rank = r;
+      total += all[r];
+    }
+    if (op != kAxis0Sum && total == 0) return make_error(TRS_ERR_EMPTY_AXIS, "!!!Cannot reduce an empty axis!!!");
+  }
+  if (nout == 0) return Error{};
+  if (peers) return axis0_combine_peers(c, op, shard, out, base, first_rank, nout, stream);
+  return axis0_combine_nccl(c, op, shard, out, base, first_rank, nout, stream);
 }
 
 }  // namespace

@@ -40,6 +40,35 @@ struct SumTarget {
 // Largest communicator the peer exchange serves (one slot per rank).
 constexpr int kMaxExchangeRanks = 64;
 
+// A rank's exchange buffer (one allocation, mapped by every peer through
+// CUDA IPC): the sharded sums' slots (2 sets x world x {accumulator, seq}),
+// then the axis-0 exchange's flags (2 parities x world seq words, written by
+// the peers), then its two arenas of kAxis0Arena bytes (this rank's partial
+// rows of the calls of each parity, read by the peers).
+constexpr size_t kAxis0Arena = (size_t)8 << 20;
+inline size_t x_flags_off(int world) { return ((size_t)2 * world * 2 * 8 + 255) / 256 * 256; }
+inline size_t x_arena_off(int world) { return (x_flags_off(world) + (size_t)2 * world * 8 + 255) / 256 * 256; }
+inline size_t x_buffer_bytes(int world) { return x_arena_off(world) + 2 * kAxis0Arena; }
+
+// One sharded axis-0 reduction's exchange over peer memory: this rank's
+// partials are in its own arena of `parity`; the publish kernel stores `seq`
+// into every peer's flag of (parity, rank), and the combine kernel waits
+// (bounded) for every rank's flag in this rank's buffer, then reads every
+// rank's partials in rank order.
+struct Axis0Exchange {
+  unsigned long long* const* peers = nullptr;  // device array: rank r's exchange buffer
+  int world = 0;
+  int rank = 0;
+  unsigned long long seq = 0;
+  int parity = 0;
+  size_t flags_off = 0, arena_off = 0;         // bytes into every buffer
+  int* err = nullptr;
+};
+Error run_axis0_publish(const Axis0Exchange& x, cudaStream_t stream);
+Error run_axis0_sum_combine(int dtype, const Axis0Exchange& x, const trs_view* out, cudaStream_t stream);
+Error run_axis0_max_combine(int dtype, const Axis0Exchange& x, int first_rank, const trs_view* out, bool argmax,
+                            cudaStream_t stream);
+
 // Element-wise program over `in`; writes `out` unless it is null, and the sum
 // of the results to `sum` when it is non-null.
 Error run_elementwise(const trs_ew_program& prog, const trs_view* in,

@@ -235,6 +235,49 @@ def main(outdir: str) -> int:
 
     run("sums in a row, exchange vs NCCL", case_many)
 
+    def case_axis0_many():
+        """Six axis-0 reductions in a row (each arena parity three times) through
+        the exchange and through a communicator forced onto NCCL: max and argmax
+        identical, sums within one ulp of each other (both the f64 sum of the
+        ranks' partials, rounded once)."""
+        data = []
+        for j, (total, width) in enumerate([(64, 33), (1031, 1000), (4096, 2048)] * 2):
+            counts = counts_for("ragged", total)
+            offs = sharding.row_offsets(counts)
+            x = rand((total, width), np.float32, 500 + j)
+            data.append((dev(x[offs[rank]:offs[rank] + counts[rank]]), width))
+
+        def through(c):
+            res = []
+            for t, width in data:
+                s_ = torch.empty((width,), dtype=t.dtype, device="cuda")
+                m_ = torch.empty((width,), dtype=t.dtype, device="cuda")
+                a_ = torch.empty((width,), dtype=torch.int64, device="cuda")
+                c.sum_axis0(device.view_of(t), device.view_of(s_), sh)
+                c.max_axis0(device.view_of(t), device.view_of(m_), sh)
+                c.argmax_axis0(device.view_of(t), device.view_of(a_), sh)
+                res.append((s_, m_, a_))
+            torch.cuda.synchronize()
+            return [tuple(v.cpu().numpy() for v in r) for r in res]
+
+        got = through(comm)
+        os.environ["TRS_PEER_EXCHANGE"] = "0"
+        try:
+            nc = sharding.Communicator(lib, rank, world, dist, timeout_ms=60000)
+        finally:
+            del os.environ["TRS_PEER_EXCHANGE"]
+        try:
+            assert not nc.peer_exchange
+            ref = through(nc)
+        finally:
+            nc.destroy()
+        for (gs, gm, ga), (rs, rm, ra) in zip(got, ref):
+            assert_bit_exact(gm, rm, "max_axis0, exchange vs NCCL")
+            assert_bit_exact(ga, ra, "argmax_axis0, exchange vs NCCL")
+            assert np.all(np.abs(gs.astype(np.float64) - rs.astype(np.float64)) <= np.spacing(np.abs(rs)))
+
+    run("axis-0 reductions in a row, exchange vs NCCL", case_axis0_many)
+
     def case_peer_timeout():
         """Rank 0 makes a sharded sum that rank 1 skips: its kernel's wait for
         rank 1's partial runs out (about 2 s), it reports bit 1 of the
@@ -257,6 +300,14 @@ def main(outdir: str) -> int:
                 assert code & 2, f"async-error word {code}, waited {waited:.2f} s"
                 assert np.isnan(out.cpu().numpy()[0])
                 assert 0.5 <= waited <= 60, waited
+                # the same for an axis-0 sum: its combine waits on the
+                # exchange's flags, runs out, and writes NaN
+                cols = torch.zeros((8,), dtype=torch.float32, device="cuda")
+                tc.sum_axis0(device.view_of(t), device.view_of(cols), sh)
+                torch.cuda.synchronize()
+                code = ctypes_async_error(lib)
+                assert code & 2, f"axis-0 sum: async-error word {code}"
+                assert np.isnan(cols.cpu().numpy()).all()
             dist.barrier()
         finally:
             tc.destroy()
