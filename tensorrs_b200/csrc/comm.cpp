@@ -386,9 +386,10 @@ Error sharded_axis0(trs_comm* c, int op, const trs_view* shard, const trs_view* 
   const bool peers = c->xpeers != nullptr && (size_t)nout * rec <= kAxis0Arena;
   int64_t base = 0;
   int first_rank = 0;
-  if (op != kAxis0Sum || !peers) {
+  if (op != kAxis0Sum) {
     // every rank's row count: the global index offset of this shard, the
-    // lowest rank holding rows, and the empty-axis check of max/argmax
+    // lowest rank holding rows, and the empty-axis check of max/argmax (a sum
+    // needs none of them)
     Nccl& n = nccl();
     Scratch counts;
     e = counts.alloc(sizeof(int64_t) * (R + 1), stream);
