@@ -38,6 +38,7 @@
 #include <string>
 
 #include "kernels.cuh"
+#include "tma.cuh"
 
 // Tuning knob: CTAs of the matmul kernel an SM keeps resident (its register
 // budget per thread follows); the default is the shipped configuration.
@@ -563,6 +564,229 @@ __global__ void __launch_bounds__(kThreads) fold_smem_kernel(const ColsDev d, co
   }
 }
 
+// V consecutive values of T stored as one 16-byte access (st.global.cs:
+// evict-first, the output is not read again) at a V-aligned address.
+template <class T, int V>
+__device__ __forceinline__ void store_cs(T* p, const T (&v)[V]) {
+  static_assert(sizeof(T) * V == 16 || V == 1, "16-byte vectors or single values");
+  if constexpr (V == 1) {
+    __stcs(p, v[0]);
+  } else {
+    uint32_t w[4];
+    memcpy(w, v, 16);
+    asm volatile("st.global.cs.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+                 : "memory");
+  }
+}
+
+// unfold by output rows.  A tile is (b, oh, a block of CB channels
+// c0 .. c0 + CB - 1): the OW rows (b, oh, 0 .. OW-1) of the columns, entries
+// [c0*kk, (c0 + CB)*kk) of each (kk = kh*kw).  The CTA stages the CB*kh image
+// rows those windows read -- y = oh*sh - ph + i, x = -pw .. (OW-1)*sw + kw-1-pw
+// -- as img_s[(cl*kh + i)*Wp + xq], xq = x + pw, zeros outside the image; then
+// it writes its entries V at a time (16 bytes), consecutive threads on
+// consecutive entries of a row, the rows of a tile one after another.  Entry
+// (cl, i, j) of window ow is img_s[(cl*kh + i)*Wp + ow*sw + j]: the shared
+// offset tab[cl*kk + i*kw + j] + ow*sw, from a table the tile builds once.
+// Each output entry costs a table read shared by V entries, a shared load and
+// 1/V of a store; each image row is staged by about kh/sh tiles, from L2
+// after the first.
+struct UnfoldRows {
+  int32_t CB, n_cb, Wp, tab_pad;  // channels per tile, channel blocks, staged row width, table slots (x4)
+  int64_t tiles;
+  FastDiv f_wp, f_kh;             // staged element -> (row, xq), row -> (cl, i)
+};
+
+// Staged image elements per thread per round: all their loads are issued
+// before the first is stored, so a tile's staging takes about one memory
+// round trip rather than one per row.
+constexpr int kUrStage = 12;
+
+template <class T, int V>
+__global__ void __launch_bounds__(kThreads) unfold_rows_kernel(const ColsDev d, const UnfoldRows u) {
+  extern __shared__ __align__(16) unsigned char ur_raw[];
+  int32_t* tab = reinterpret_cast<int32_t*>(ur_raw);
+  T* img = reinterpret_cast<T*>(ur_raw + (size_t)u.tab_pad * 4);
+  const T* x = static_cast<const T*>(d.src);
+  T* out = static_cast<T*>(d.dst);
+  const int32_t kh = (int32_t)d.kh, kw = (int32_t)d.kw, kk = kh * kw;
+  const int32_t H = (int32_t)d.H, W = (int32_t)d.W, OH = (int32_t)d.OH, OW = (int32_t)d.OW, C = (int32_t)d.C;
+  const int32_t sw = (int32_t)d.sw, pw = (int32_t)d.pw, Wp = u.Wp;
+  for (int64_t tile = blockIdx.x; tile < u.tiles; tile += gridDim.x) {
+    // tile = (b * OH + oh) * n_cb + cb
+    const int64_t r1 = tile / u.n_cb;
+    const int32_t cb = (int32_t)(tile - r1 * u.n_cb);
+    const int64_t b = r1 / OH;
+    const int32_t oh = (int32_t)(r1 - b * OH);
+    const int32_t c0 = cb * u.CB, ncb = C - c0 < u.CB ? C - c0 : u.CB;
+    const int32_t seg = ncb * kk;
+    for (int32_t t = threadIdx.x; t < seg; t += kThreads) {
+      const int32_t cl = t / kk, r = t - cl * kk, i = r / kw, j = r - i * kw;
+      tab[t] = (cl * kh + i) * Wp + j;
+    }
+    // the image rows: element e = (cl*kh + i)*Wp + xq of the staged rows,
+    // consecutive threads on consecutive xq
+    const int32_t ybase = oh * (int32_t)d.sh - (int32_t)d.ph;
+    const T* xb = x + d.x_off + b * d.xs[0] + (int64_t)c0 * d.xs[1];
+    const int32_t n_stage = ncb * kh * Wp;
+    for (int32_t e0 = threadIdx.x; e0 < n_stage; e0 += kThreads * kUrStage) {
+      T v[kUrStage];
+#pragma unroll
+      for (int k = 0; k < kUrStage; ++k) {
+        const int32_t e = e0 + k * kThreads;
+        v[k] = T(0);
+        if (e < n_stage) {
+          const uint32_t rr = fdiv((uint32_t)e, u.f_wp), cl = fdiv(rr, u.f_kh);
+          const int32_t y = ybase + (int32_t)(rr - cl * u.f_kh.d), xx = e - (int32_t)(rr * u.f_wp.d) - pw;
+          if (y >= 0 && y < H && xx >= 0 && xx < W)
+            v[k] = xb[(int64_t)cl * d.xs[1] + (int64_t)y * d.xs[2] + (int64_t)xx * d.xs[3]];
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kUrStage; ++k)
+        if (e0 + k * kThreads < n_stage) img[e0 + k * kThreads] = v[k];
+    }
+    __syncthreads();
+    // entries (ow, g*V .. g*V + V-1): thread t starts at flat index t and
+    // steps by kThreads, carrying (ow, g) along instead of dividing
+    const int32_t G = seg / V, n = OW * G;
+    T* ob = out + d.c_off + (b * OH + oh) * (int64_t)OW * d.cs[0] + (int64_t)c0 * kk;
+    int32_t ow = (int32_t)threadIdx.x / G, g = (int32_t)threadIdx.x - ow * G;
+    const int32_t dow = kThreads / G, dg = kThreads - dow * G;
+    for (int32_t q = threadIdx.x; q < n; q += kThreads) {
+      const int32_t s0 = ow * sw;
+      T v[V];
+      if constexpr (V == 4) {
+        const int4 e = *reinterpret_cast<const int4*>(tab + g * 4);
+        v[0] = img[e.x + s0];
+        v[1] = img[e.y + s0];
+        v[2] = img[e.z + s0];
+        v[3] = img[e.w + s0];
+      } else if constexpr (V == 2) {
+        const int2 e = *reinterpret_cast<const int2*>(tab + g * 2);
+        v[0] = img[e.x + s0];
+        v[1] = img[e.y + s0];
+      } else {
+        v[0] = img[tab[g] + s0];
+      }
+      store_cs<T, V>(ob + (int64_t)ow * d.cs[0] + g * V, v);
+      g += dg;
+      ow += dow;
+      if (g >= G) {
+        g -= G;
+        ++ow;
+      }
+    }
+    __syncthreads();  // the table and the rows are free for the next tile
+  }
+}
+
+// fold for stride 1 from window rows staged by TMA.  A tile is (b, a block of
+// CB channels, a band of TY image rows y0 .. y0+TY-1, a strip of XS image
+// columns x0 .. x0+XS-1).  Pixel (y, x) is covered by the windows
+// (oh, ow) = (y + ph - i, x + pw - j), 0 <= i < kh, 0 <= j < kw, that lie in
+// [0, OH) x [0, OW); the tile's windows are therefore the columns' rows
+// (b, oh, ow) with oh in [y0 + ph - kh + 1, y0 + TY - 1 + ph] and ow in
+// [x0 + pw - kw + 1, x0 + XS - 1 + pw]: R = TY + kh - 1 window rows of
+// Q = XS + kw - 1 windows, of which the tile needs the seg = CB*kk
+// consecutive entries of its channels.  One thread loads each window row
+// with one TMA box [seg, Q, 1, 1] of the columns seen as [B][OH][OW][patch]
+// (windows with ow outside [0, OW) arrive as zeros); window rows outside
+// [0, OH) are written as zeros by the threads.  Window (r, q) entry t sits
+// at r*RS + q*seg + t, so pixel (yy, xx, cl) of the tile finds window (i, j)
+// at base + ii*(RS - kw) + jj*(seg - 1) + kk - 1, with ii = kh-1-i,
+// jj = kw-1-j and base = yy*RS + xx*seg + cl*kk: the same offsets for every
+// pixel, no window bounds.  The adds run ii and jj upward -- windows by
+// increasing (oh, ow), the reference's order -- from +0; a missing window
+// adds +0, which changes no sum (a sum from +0 is never -0, and
+// s + (+0) = s for every other s, NaN and infinities included).
+struct FoldS1 {
+  int32_t CB, TY, XS, R, Q, seg, RS;  // tile; window rows, windows per row, entries per window, row stride
+  int32_t n_cb, n_yb, n_xb;
+  int64_t tiles;
+  FastDiv f_cb, f_xs;
+};
+
+template <class T, int K>
+__global__ void __launch_bounds__(kThreads) fold_s1_kernel(const __grid_constant__ CUtensorMap cmap, const ColsDev d,
+                                                           const FoldS1 f, int* err) {
+  using A = Arith<T>;
+  // the window rows from a 128-byte boundary (each row's start, RS * sizeof(T)
+  // bytes apart, is one too: a TMA destination), the mbarrier after them
+  extern __shared__ unsigned char fs_raw[];
+  unsigned char* base =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(fs_raw) + 127) & ~uintptr_t(127));
+  T* sm = reinterpret_cast<T*>(base);
+  uint64_t& bar = *reinterpret_cast<uint64_t*>(base + (size_t)f.R * f.RS * sizeof(T));
+  T* out = static_cast<T*>(d.dst);
+  const int32_t kh = K ? K : (int32_t)d.kh, kw = K ? K : (int32_t)d.kw, kk = kh * kw;
+  const int32_t H = (int32_t)d.H, W = (int32_t)d.W, C = (int32_t)d.C, OH = (int32_t)d.OH;
+  const int32_t RS = f.RS, seg = f.seg, row_elems = f.Q * f.seg;
+  const uint32_t box_bytes = (uint32_t)row_elems * (uint32_t)sizeof(T);
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  uint32_t phase = 0;
+  for (int64_t tile = blockIdx.x; tile < f.tiles; tile += gridDim.x) {
+    // tile = ((b * n_cb + cb) * n_yb + yb) * n_xb + xb
+    const int64_t t1 = tile / f.n_xb, t2 = t1 / f.n_yb, b = t2 / f.n_cb;
+    const int32_t xb = (int32_t)(tile - t1 * f.n_xb), yb = (int32_t)(t1 - t2 * f.n_yb), cb = (int32_t)(t2 - b * f.n_cb);
+    const int32_t y0 = yb * f.TY, x0 = xb * f.XS, c0 = cb * f.CB;
+    const int32_t ty = H - y0 < f.TY ? H - y0 : f.TY, xs = W - x0 < f.XS ? W - x0 : f.XS;
+    const int32_t ncb = C - c0 < f.CB ? C - c0 : f.CB;
+    const int32_t oh_a = y0 + (int32_t)d.ph - kh + 1, ow_a = x0 + (int32_t)d.pw - kw + 1;
+    if (threadIdx.x == 0) {
+      // the previous tile's reads of these rows (ordered by the barrier that
+      // ended it) come before the copies' writes
+      fence_proxy_async();
+      uint32_t n_in = 0;
+      for (int32_t r = 0; r < f.R; ++r) n_in += (oh_a + r >= 0 && oh_a + r < OH) ? 1u : 0u;
+      mbar_arrive_expect_tx(&bar, n_in * box_bytes);
+      for (int32_t r = 0; r < f.R; ++r)
+        if (oh_a + r >= 0 && oh_a + r < OH) tma_load_4d(sm + r * RS, &cmap, c0 * kk, ow_a, oh_a + r, (int32_t)b, &bar);
+    }
+    for (int32_t r = 0; r < f.R; ++r)
+      if (oh_a + r < 0 || oh_a + r >= OH)
+        for (int32_t e = threadIdx.x; e < row_elems; e += kThreads) sm[r * RS + e] = T(0);
+    const bool ok = mbar_wait(&bar, phase);
+    phase ^= 1u;
+    if (__syncthreads_or(!ok)) {
+      if (threadIdx.x == 0) {
+        atomicOr(err, kAsyncWaitTimeout);
+        mbar_wait(&bar, phase ^ 1u);  // the copies still in flight (bounded)
+      }
+      __syncthreads();
+      return;
+    }
+    const int32_t n_pix = f.CB * f.XS * ty;
+    for (int32_t p = threadIdx.x; p < n_pix; p += kThreads) {
+      // p = (yy * XS + xx) * CB + cl
+      const uint32_t rest = fdiv((uint32_t)p, f.f_cb), cl = (uint32_t)p - rest * f.f_cb.d;
+      const uint32_t yy = fdiv(rest, f.f_xs), xx = rest - yy * f.f_xs.d;
+      if ((int32_t)cl >= ncb || (int32_t)xx >= xs) continue;
+      const T* s = sm + (int32_t)yy * RS + (int32_t)xx * seg + (int32_t)cl * kk + (kk - 1);
+      T acc = T(0);
+      if constexpr (K > 0) {
+        T v[K * K];
+#pragma unroll
+        for (int ii = 0; ii < K; ++ii)
+#pragma unroll
+          for (int jj = 0; jj < K; ++jj) v[ii * K + jj] = s[ii * (RS - K) + jj * (seg - 1)];
+#pragma unroll
+        for (int w = 0; w < K * K; ++w) acc = A::add(acc, v[w]);
+      } else {
+        for (int32_t ii = 0; ii < kh; ++ii)
+          for (int32_t jj = 0; jj < kw; ++jj) acc = A::add(acc, s[ii * (RS - kw) + jj * (seg - 1)]);
+      }
+      out[d.x_off + b * d.xs[0] + (int64_t)(c0 + (int32_t)cl) * d.xs[1] + (int64_t)(y0 + (int32_t)yy) * d.xs[2] +
+          (int64_t)(x0 + (int32_t)xx) * d.xs[3]] = acc;
+    }
+    __syncthreads();  // every thread is done with the tile's windows
+  }
+}
+
 // ---- host side ---------------------------------------------------------------
 
 bool ranges_overlap(const trs_view* a, const trs_view* b) {
@@ -763,8 +987,175 @@ bool pick_fold_tile(const ColsDev& d, int es, FoldTile* t) {
   return false;
 }
 
+// Shared memory an unfold-by-rows tile aims at (eight CTAs of 256 threads per
+// SM) and the most it may take (one channel's kh image rows).
+#ifndef TRS_UNFOLD_ROWS_TARGET
+#define TRS_UNFOLD_ROWS_TARGET (12 * 1024)
+#endif
+constexpr int64_t kUnfoldRowsMax = 48 * 1024;
+
+// The unfold-by-rows tile: the columns' entries contiguous within a row; V
+// entries per store when every row start and every channel block is
+// V-aligned (V = 16 bytes / element), else 1.  False when one channel's
+// image rows do not fit kUnfoldRowsMax or an index leaves 31 bits.
+bool pick_unfold_rows(const ColsDev& d, int es, int* V, UnfoldRows* u) {
+  if (d.cs[1] != 1 || d.rows <= 0 || d.patch <= 0 || d.OW <= 0 || d.kh <= 0 || d.kw <= 0) return false;
+  const int64_t kk = d.kh * d.kw, Wp = (d.OW - 1) * d.sw + d.kw, row_bytes = d.kh * Wp * es;
+  if (row_bytes > kUnfoldRowsMax || d.patch >= (1ll << 30) || d.OW * d.patch >= (1ll << 31)) return false;
+  int v = 16 / es;
+  if (d.patch % v != 0 || d.cs[0] % v != 0 || d.c_off % v != 0 || reinterpret_cast<uintptr_t>(d.dst) % 16 != 0)
+    v = 1;
+  int64_t cb_max = TRS_UNFOLD_ROWS_TARGET / row_bytes;
+  if (cb_max < 1) cb_max = 1;
+  int64_t n_cb = (d.C + cb_max - 1) / cb_max;
+  int64_t CB = (d.C + n_cb - 1) / n_cb;
+  if (v > 1 && n_cb > 1 && (CB * kk) % v != 0) {
+    // channel blocks whose entry count is a multiple of V
+    int64_t m = 1;
+    while ((m * kk) % v != 0) ++m;
+    CB = (CB + m - 1) / m * m;
+    if (CB * row_bytes > kUnfoldRowsMax) v = 1, CB = cb_max < d.C ? cb_max : d.C;
+    n_cb = (d.C + CB - 1) / CB;
+  }
+  *V = v;
+  u->CB = (int32_t)CB;
+  u->n_cb = (int32_t)n_cb;
+  u->Wp = (int32_t)Wp;
+  u->tab_pad = (int32_t)((CB * kk + 3) / 4 * 4);
+  u->tiles = d.B * d.OH * n_cb;
+  u->f_wp = make_fastdiv((uint32_t)Wp);
+  u->f_kh = make_fastdiv((uint32_t)d.kh);
+  return true;
+}
+
+// Shared memory a stride-1 fold tile may take (four CTAs per SM).
+#ifndef TRS_FOLD_S1_BUDGET
+#define TRS_FOLD_S1_BUDGET (52 * 1024)
+#endif
+
+// The stride-1 fold tile: channel blocks whose entries are a whole number of
+// 16-byte units (the TMA box's inner extent and start; m channels, or 2m),
+// at most 256 entries and 256 windows per box; within the budget the widest
+// strip of columns, then the tallest band (8, 4, 2 or 1 rows: the band's
+// window rows are staged (TY + kh - 1) / TY times), then 2m channels.  False
+// when the columns cannot be a TMA tensor (entries not contiguous, a row
+// stride or base not 16-byte aligned) or no tile fits.
+bool pick_fold_s1(const ColsDev& d, int es, FoldS1* f) {
+  if (d.sh != 1 || d.sw != 1 || d.kh < 1 || d.kw < 1 || d.cs[1] != 1) return false;
+  if (d.B <= 0 || d.C <= 0 || d.H <= 0 || d.W <= 0 || d.OH <= 0 || d.OW <= 0) return false;
+  if ((d.cs[0] * es) % 16 != 0 || (reinterpret_cast<uintptr_t>(d.src) + (uintptr_t)(d.c_off * es)) % 16 != 0)
+    return false;
+  if (d.patch >= (1ll << 31) || d.B >= (1ll << 31) || d.H >= (1ll << 30) || d.W >= (1ll << 30)) return false;
+  if ((uint64_t)d.cs[0] * (uint64_t)es * (uint64_t)d.OW * (uint64_t)d.OH >= (1ull << 40)) return false;  // TMA strides
+  const int64_t kk = d.kh * d.kw;
+  int64_t m = 1;
+  while ((m * kk * es) % 16 != 0) ++m;
+  if (m * kk > 256 || d.kw > 128 || m > d.C) return false;
+  const int64_t xs_opts[2] = {d.W + d.kw - 1 <= 256 ? d.W : 256 - (d.kw - 1), d.W < 64 ? d.W : 64};
+  for (const int64_t XS : xs_opts) {
+    for (int ty = 8; ty >= 1; ty /= 2) {
+      if (ty > 1 && ty >= 2 * d.H) continue;
+      for (int64_t CB = 2 * m; CB >= m; CB -= m) {
+        if (CB > m && (CB * kk > 256 || CB > d.C)) continue;
+        const int64_t Q = XS + d.kw - 1, seg = CB * kk, align = 128 / es;
+        const int64_t RS = (Q * seg + align - 1) / align * align, R = ty + d.kh - 1;
+        if (R * RS * es > TRS_FOLD_S1_BUDGET) continue;
+        f->CB = (int32_t)CB;
+        f->TY = ty;
+        f->XS = (int32_t)XS;
+        f->R = (int32_t)R;
+        f->Q = (int32_t)Q;
+        f->seg = (int32_t)seg;
+        f->RS = (int32_t)RS;
+        f->n_cb = (int32_t)((d.C + CB - 1) / CB);
+        f->n_yb = (int32_t)((d.H + ty - 1) / ty);
+        f->n_xb = (int32_t)((d.W + XS - 1) / XS);
+        f->tiles = d.B * f->n_cb * f->n_yb * f->n_xb;
+        f->f_cb = make_fastdiv((uint32_t)CB);
+        f->f_xs = make_fastdiv((uint32_t)XS);
+        return true;
+      }
+    }
+  }
+  return false;
+}
+
+template <class T> constexpr CUtensorMapDataType tma_dtype();
+template <> constexpr CUtensorMapDataType tma_dtype<float>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT32; }
+template <> constexpr CUtensorMapDataType tma_dtype<double>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT64; }
+template <> constexpr CUtensorMapDataType tma_dtype<int32_t>() { return CU_TENSOR_MAP_DATA_TYPE_INT32; }
+template <> constexpr CUtensorMapDataType tma_dtype<int64_t>() { return CU_TENSOR_MAP_DATA_TYPE_INT64; }
+
+// The columns [B*OH*OW, patch] as the 4-D tensor [B][OH][OW][patch] (row
+// stride cs0), boxes [seg, Q, 1, 1], zeros outside.
+template <class T>
+Error make_cols_map(const ColsDev& d, const FoldS1& f, CUtensorMap* map) {
+  Error e;
+  EncodeTiled enc = encode_fn(&e);
+  if (!enc) return e;
+  const cuuint64_t rs = (cuuint64_t)d.cs[0] * sizeof(T);
+  const cuuint64_t dims[4] = {(cuuint64_t)d.patch, (cuuint64_t)d.OW, (cuuint64_t)d.OH, (cuuint64_t)d.B};
+  const cuuint64_t strides[3] = {rs, rs * (cuuint64_t)d.OW, rs * (cuuint64_t)d.OW * (cuuint64_t)d.OH};
+  const cuuint32_t box[4] = {(cuuint32_t)f.seg, (cuuint32_t)f.Q, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  void* base = const_cast<T*>(static_cast<const T*>(d.src) + d.c_off);
+  const CUresult r = enc(map, tma_dtype<T>(), 4, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return make_error(TRS_ERR_CUDA, "fold_2d: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return Error{};
+}
+
+template <class T>
+Error launch_fold_s1(const ColsDev& d, const FoldS1& f, cudaStream_t stream) {
+  CUtensorMap map;
+  Error e = make_cols_map<T>(d, f, &map);
+  if (!e.ok()) return e;
+  const int smem = (int)((int64_t)f.R * f.RS * (int64_t)sizeof(T)) + 8 + 128;  // rows, mbarrier, alignment
+  const bool k3 = d.kh == 3 && d.kw == 3;
+  const void* k = k3 ? (const void*)fold_s1_kernel<T, 3> : (const void*)fold_s1_kernel<T, 0>;
+  allow_smem(k, smem);
+  const uint64_t cap = (uint64_t)current_device_info().sm_count * (uint64_t)resident_blocks_smem(k, kThreads, smem);
+  const unsigned g = (unsigned)((uint64_t)f.tiles < cap * 64 ? (uint64_t)f.tiles : cap * 64);
+  if (k3)
+    fold_s1_kernel<T, 3><<<g, kThreads, smem, stream>>>(map, d, f, async_error_word());
+  else
+    fold_s1_kernel<T, 0><<<g, kThreads, smem, stream>>>(map, d, f, async_error_word());
+  return check_launch("fold_2d kernel");
+}
+
+template <class T>
+Error launch_unfold_rows(const ColsDev& d, int V, const UnfoldRows& u, cudaStream_t stream) {
+  constexpr int kV = (int)(16 / sizeof(T));
+  const int smem = (int)((int64_t)u.tab_pad * 4 + (int64_t)u.CB * d.kh * u.Wp * (int64_t)sizeof(T));
+  const void* k = V > 1 ? (const void*)unfold_rows_kernel<T, kV> : (const void*)unfold_rows_kernel<T, 1>;
+  allow_smem(k, smem);
+  const uint64_t cap = (uint64_t)current_device_info().sm_count * (uint64_t)resident_blocks_smem(k, kThreads, smem);
+  const unsigned g = (unsigned)((uint64_t)u.tiles < cap * 64 ? (uint64_t)u.tiles : cap * 64);
+  if (V > 1)
+    unfold_rows_kernel<T, kV><<<g, kThreads, smem, stream>>>(d, u);
+  else
+    unfold_rows_kernel<T, 1><<<g, kThreads, smem, stream>>>(d, u);
+  return check_launch("unfold_2d kernel");
+}
+
+// Tuning knob: 0 keeps the earlier tile kernels for every geometry.
+#ifndef TRS_COLS_ROWS
+#define TRS_COLS_ROWS 1
+#endif
+
 template <class T>
 Error launch_cols(bool unfold, const ColsDev& d, cudaStream_t stream) {
+  if (TRS_COLS_ROWS && !unfold) {
+    FoldS1 f;
+    if (pick_fold_s1(d, (int)sizeof(T), &f)) return launch_fold_s1<T>(d, f, stream);
+  }
+  if (TRS_COLS_ROWS && unfold) {
+    UnfoldRows u;
+    int V = 1;
+    if (pick_unfold_rows(d, (int)sizeof(T), &V, &u)) return launch_unfold_rows<T>(d, V, u, stream);
+  }
   if (!unfold) {
     FoldTile ft;
     if (pick_fold_tile(d, (int)sizeof(T), &ft)) {

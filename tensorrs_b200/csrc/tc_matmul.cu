@@ -47,6 +47,7 @@
 #include <string>
 
 #include "kernels.cuh"
+#include "tma.cuh"
 
 namespace trs {
 namespace {
@@ -194,14 +195,6 @@ __global__ void __launch_bounds__(256) zero_view_kernel(const trs_view v, int64_
 }
 
 // ---- tcgen05 / TMA primitives ---------------------------------------------------
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
@@ -463,28 +456,6 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap t_ahi, const __grid_constant_
 }
 
 // ---- host side -------------------------------------------------------------------
-
-using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiled encode_fn(Error* err) {
-  static std::once_flag once;
-  static EncodeTiled fn = nullptr;
-  static std::string why;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiled>(p);
-    else
-      why = "cuTensorMapEncodeTiled is not available from the driver";
-    cudaGetLastError();
-  });
-  if (!fn) *err = make_error(TRS_ERR_UNAVAILABLE, why);
-  return fn;
-}
 
 // [batches * rows_p, Kp] f32, K contiguous, 32 x box_rows boxes with 128-byte swizzle.
 Error make_map(EncodeTiled enc, CUtensorMap* map, float* base, int64_t rows_total, int64_t Kp, int box_rows) {

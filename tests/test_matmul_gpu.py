@@ -135,6 +135,13 @@ COL_CASES = [  # shape, kernel, stride, padding
     ([1, 128, 5, 6], (4, 4), (1, 1), (1, 1)), ([1, 240, 6, 7], (3, 3), (1, 1), (1, 1)),
     # fold windows too wide for a shared-memory tile: the per-pixel kernels
     ([1, 1, 6, 1200], (4, 4), (1, 1), (0, 0)), ([1, 1, 12, 20], (11, 11), (1, 1), (0, 0)),
+    # unfold by output rows: a last channel block that is partial (70 = 24 + 24 + 22 channels) and
+    # blocks rounded up to whole 16-byte stores (36 = 12 + 12 + 12)
+    ([2, 70, 6, 40], (3, 3), (1, 1), (1, 1)), ([1, 36, 4, 100], (3, 3), (1, 1), (1, 1)),
+    # stride-1 fold from TMA-staged window rows: strips of 64 columns, a partial channel block,
+    # window rows above the image (no padding) that are zero-filled instead of copied
+    ([1, 8, 5, 300], (3, 3), (1, 1), (1, 1)), ([2, 12, 9, 10], (3, 3), (1, 1), (1, 1)),
+    ([2, 4, 8, 8], (3, 3), (1, 1), (0, 0)),
 ]
 
 
@@ -171,6 +178,30 @@ def test_unfold_into_a_transposed_output(dtype):
     got = device.unfold_2d(dx.view, (3, 3), (1, 1), (1, 1), out)
     assert_bit_exact(to_host(got.contiguous()), want, "unfold into a transposed view")
     assert isinstance(got, torch.Tensor)
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64], ids=lambda d: np.dtype(d).name)
+def test_unfold_and_fold_with_padded_column_rows(dtype):
+    """Columns whose rows are 4 entries longer than a window (row stride
+    patch + 4, still 16-byte aligned): unfold writes only the window entries,
+    fold reads them through the wider rows."""
+    import oracle
+    from tensorrs_b200 import device
+    shape, k, s, p = [2, 8, 9, 10], (3, 3), (1, 1), (1, 1)
+    x = rand(shape, dtype, 15)
+    dx = contiguous(x)
+    want = oracle.unfold_2d(dx.host_view(), k, s, p)
+    rows, patch = want.shape
+    wide = empty([rows, patch + 4], dtype)
+    wide.fill_(7)
+    device.unfold_2d(dx.view, k, s, p, wide[:, :patch])
+    host = to_host(wide)
+    assert_bit_exact(host[:, :patch], want, "unfold into padded rows")
+    assert np.all(host[:, patch:] == 7)
+    c = rand([rows, patch + 4], dtype, 16)
+    dc = DevView(c, [rows, patch], [patch + 4, 1], 0)
+    back = to_host(device.fold_2d(dc.view, k, s, p, empty(shape, dtype)))
+    assert_bit_exact(back, oracle.fold_2d(dc.host_view(), shape, k, s, p), "fold from padded rows")
 
 
 def test_unfold_of_a_strided_image_and_fold_errors():
