@@ -32,7 +32,11 @@
 // values of the windows covering it in the reference's order -- windows by
 // increasing (oh, ow) -- starting from +0, so its sums round exactly as the
 // reference's `image[..] += src[..]` loop does.
+#include <algorithm>
+#include <array>
 #include <cstdlib>
+#include <map>
+#include <mutex>
 #include <type_traits>
 #include <cstring>
 #include <string>
@@ -564,120 +568,154 @@ __global__ void __launch_bounds__(kThreads) fold_smem_kernel(const ColsDev d, co
   }
 }
 
-// V consecutive values of T stored as one 16-byte access (st.global.cs:
-// evict-first, the output is not read again) at a V-aligned address.
+// Tuning knob: 1 stores the unfold's output evict-first (st.global.cs), 0
+// with the default cache policy.
+#ifndef TRS_UNFOLD_CS
+#define TRS_UNFOLD_CS 1
+#endif
+
+// V consecutive values of T stored as one 16-byte access at a V-aligned
+// address (evict-first when TRS_UNFOLD_CS: the output is not read again).
 template <class T, int V>
 __device__ __forceinline__ void store_cs(T* p, const T (&v)[V]) {
   static_assert(sizeof(T) * V == 16 || V == 1, "16-byte vectors or single values");
   if constexpr (V == 1) {
-    __stcs(p, v[0]);
+    if (TRS_UNFOLD_CS) __stcs(p, v[0]); else *p = v[0];
   } else {
     uint32_t w[4];
     memcpy(w, v, 16);
-    asm volatile("st.global.cs.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
-                 : "memory");
+    if (TRS_UNFOLD_CS)
+      asm volatile("st.global.cs.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+                   "r"(w[3])
+                   : "memory");
+    else
+      asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+                   : "memory");
   }
 }
 
 // unfold by output rows.  A tile is (b, oh, a block of CB channels
 // c0 .. c0 + CB - 1): the OW rows (b, oh, 0 .. OW-1) of the columns, entries
 // [c0*kk, (c0 + CB)*kk) of each (kk = kh*kw).  The CTA stages the CB*kh image
-// rows those windows read -- y = oh*sh - ph + i, x = -pw .. (OW-1)*sw + kw-1-pw
-// -- as img_s[(cl*kh + i)*Wp + xq], xq = x + pw, zeros outside the image; then
-// it writes its entries V at a time (16 bytes), consecutive threads on
-// consecutive entries of a row, the rows of a tile one after another.  Entry
-// (cl, i, j) of window ow is img_s[(cl*kh + i)*Wp + ow*sw + j]: the shared
-// offset tab[cl*kk + i*kw + j] + ow*sw, from a table the tile builds once.
-// Each output entry costs a table read shared by V entries, a shared load and
-// 1/V of a store; each image row is staged by about kh/sh tiles, from L2
-// after the first.
+// rows those windows read, y = oh*sh - ph + i, in shared memory as
+// img_s[(cl*kh + i)*Ws + x + xo] for x from -xo to Ws - xo - 1 (zeros outside
+// the image), which covers every x a window reads, -pw .. (OW-1)*sw + kw-1-pw;
+// row (cl, i) starts at cl*CS + i*IS.  With TMA the rows arrive as kh boxes
+// [Ws, 1, CB, 1] of the image seen as [B][C][H][W], one per i (CS = Ws,
+// IS = CB*Ws; xo = pw rounded up to 16 bytes, so each box starts on a 16-byte
+// boundary; rows, columns and channels outside the image read zeros; Ws is
+// the width, among those that fit, whose loads below meet the fewest bank
+// conflicts); otherwise the threads copy them, all their loads in flight at
+// once (CS = kh*Ws, IS = Ws, xo = pw).  Then each thread writes one group g
+// of V consecutive entries (16 bytes) of every step-th row: entry (cl, i, j)
+// of window ow is img_s[e + ow*sw] with e = cl*CS + i*IS + j + xo - pw, so
+// the thread keeps
+// its V offsets e in registers and walks the rows with two increments --
+// V shared loads and one streaming store per V entries.  Each image row is
+// staged by about kh/sh tiles, from L2 after the first.
 struct UnfoldRows {
-  int32_t CB, n_cb, Wp, tab_pad;  // channels per tile, channel blocks, staged row width, table slots (x4)
-  int64_t tiles;
-  FastDiv f_wp, f_kh;             // staged element -> (row, xq), row -> (cl, i)
+  int32_t CB, n_cb, Ws, xo;  // channels per tile, channel blocks, staged row width, staged x offset
+  int32_t CS, IS;            // shared strides of a channel and of a window row i
+  uint32_t tiles;
+  FastDiv f_ncb, f_oh, f_ws, f_kh;
 };
 
-// Staged image elements per thread per round: all their loads are issued
-// before the first is stored, so a tile's staging takes about one memory
-// round trip rather than one per row.
+// Staged image elements per thread per round when the threads copy them: all
+// their loads are issued before the first is stored.
 constexpr int kUrStage = 12;
 
-template <class T, int V>
-__global__ void __launch_bounds__(kThreads) unfold_rows_kernel(const ColsDev d, const UnfoldRows u) {
-  extern __shared__ __align__(16) unsigned char ur_raw[];
-  int32_t* tab = reinterpret_cast<int32_t*>(ur_raw);
-  T* img = reinterpret_cast<T*>(ur_raw + (size_t)u.tab_pad * 4);
-  const T* x = static_cast<const T*>(d.src);
-  T* out = static_cast<T*>(d.dst);
+template <class T, int V, bool TMA>
+__global__ void __launch_bounds__(kThreads) unfold_rows_kernel(const __grid_constant__ CUtensorMap imap,
+                                                               const ColsDev d, const UnfoldRows u, int* err) {
+  extern __shared__ unsigned char ur_raw[];
+  unsigned char* base =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(ur_raw) + 127) & ~uintptr_t(127));
+  T* img = reinterpret_cast<T*>(base);
   const int32_t kh = (int32_t)d.kh, kw = (int32_t)d.kw, kk = kh * kw;
-  const int32_t H = (int32_t)d.H, W = (int32_t)d.W, OH = (int32_t)d.OH, OW = (int32_t)d.OW, C = (int32_t)d.C;
-  const int32_t sw = (int32_t)d.sw, pw = (int32_t)d.pw, Wp = u.Wp;
-  for (int64_t tile = blockIdx.x; tile < u.tiles; tile += gridDim.x) {
-    // tile = (b * OH + oh) * n_cb + cb
-    const int64_t r1 = tile / u.n_cb;
-    const int32_t cb = (int32_t)(tile - r1 * u.n_cb);
-    const int64_t b = r1 / OH;
-    const int32_t oh = (int32_t)(r1 - b * OH);
-    const int32_t c0 = cb * u.CB, ncb = C - c0 < u.CB ? C - c0 : u.CB;
-    const int32_t seg = ncb * kk;
-    for (int32_t t = threadIdx.x; t < seg; t += kThreads) {
-      const int32_t cl = t / kk, r = t - cl * kk, i = r / kw, j = r - i * kw;
-      tab[t] = (cl * kh + i) * Wp + j;
-    }
-    // the image rows: element e = (cl*kh + i)*Wp + xq of the staged rows,
-    // consecutive threads on consecutive xq
-    const int32_t ybase = oh * (int32_t)d.sh - (int32_t)d.ph;
-    const T* xb = x + d.x_off + b * d.xs[0] + (int64_t)c0 * d.xs[1];
-    const int32_t n_stage = ncb * kh * Wp;
-    for (int32_t e0 = threadIdx.x; e0 < n_stage; e0 += kThreads * kUrStage) {
-      T v[kUrStage];
-#pragma unroll
-      for (int k = 0; k < kUrStage; ++k) {
-        const int32_t e = e0 + k * kThreads;
-        v[k] = T(0);
-        if (e < n_stage) {
-          const uint32_t rr = fdiv((uint32_t)e, u.f_wp), cl = fdiv(rr, u.f_kh);
-          const int32_t y = ybase + (int32_t)(rr - cl * u.f_kh.d), xx = e - (int32_t)(rr * u.f_wp.d) - pw;
-          if (y >= 0 && y < H && xx >= 0 && xx < W)
-            v[k] = xb[(int64_t)cl * d.xs[1] + (int64_t)y * d.xs[2] + (int64_t)xx * d.xs[3]];
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < kUrStage; ++k)
-        if (e0 + k * kThreads < n_stage) img[e0 + k * kThreads] = v[k];
+  const int32_t OH = (int32_t)d.OH, OW = (int32_t)d.OW, C = (int32_t)d.C;
+  const int32_t sw = (int32_t)d.sw, Ws = u.Ws;
+  // TMA: kh window rows IS apart; copied: CB channels CS = kh*Ws apart
+  const uint32_t stage_elems = TMA ? (uint32_t)kh * (uint32_t)u.IS : (uint32_t)u.CB * (uint32_t)u.CS;
+  uint64_t& bar = *reinterpret_cast<uint64_t*>(base + ((size_t)stage_elems * sizeof(T) + 7) / 8 * 8);
+  if (TMA) {
+    if (threadIdx.x == 0) {
+      mbar_init(&bar, 1);
+      fence_mbar_init();
     }
     __syncthreads();
-    // entries (ow, g*V .. g*V + V-1): thread t starts at flat index t and
-    // steps by kThreads, carrying (ow, g) along instead of dividing
-    const int32_t G = seg / V, n = OW * G;
-    T* ob = out + d.c_off + (b * OH + oh) * (int64_t)OW * d.cs[0] + (int64_t)c0 * kk;
-    int32_t ow = (int32_t)threadIdx.x / G, g = (int32_t)threadIdx.x - ow * G;
-    const int32_t dow = kThreads / G, dg = kThreads - dow * G;
-    for (int32_t q = threadIdx.x; q < n; q += kThreads) {
-      const int32_t s0 = ow * sw;
-      T v[V];
-      if constexpr (V == 4) {
-        const int4 e = *reinterpret_cast<const int4*>(tab + g * 4);
-        v[0] = img[e.x + s0];
-        v[1] = img[e.y + s0];
-        v[2] = img[e.z + s0];
-        v[3] = img[e.w + s0];
-      } else if constexpr (V == 2) {
-        const int2 e = *reinterpret_cast<const int2*>(tab + g * 2);
-        v[0] = img[e.x + s0];
-        v[1] = img[e.y + s0];
-      } else {
-        v[0] = img[tab[g] + s0];
+  }
+  uint32_t phase = 0;
+  for (uint32_t tile = blockIdx.x; tile < u.tiles; tile += gridDim.x) {
+    // tile = (b * OH + oh) * n_cb + cb
+    const uint32_t r1 = fdiv(tile, u.f_ncb), b = fdiv(r1, u.f_oh);
+    const int32_t cb = (int32_t)(tile - r1 * u.f_ncb.d), oh = (int32_t)(r1 - b * u.f_oh.d);
+    const int32_t c0 = cb * u.CB, ncb = C - c0 < u.CB ? C - c0 : u.CB;
+    const int32_t ybase = oh * (int32_t)d.sh - (int32_t)d.ph;
+    if constexpr (TMA) {
+      if (threadIdx.x == 0) {
+        fence_proxy_async();  // the previous tile's reads (before the barrier that ended it) first
+        mbar_arrive_expect_tx(&bar, (uint32_t)kh * (uint32_t)u.CB * (uint32_t)Ws * (uint32_t)sizeof(T));
+        for (int32_t i = 0; i < kh; ++i) tma_load_4d(img + i * u.IS, &imap, -u.xo, ybase + i, c0, (int32_t)b, &bar);
       }
-      store_cs<T, V>(ob + (int64_t)ow * d.cs[0] + g * V, v);
-      g += dg;
-      ow += dow;
-      if (g >= G) {
-        g -= G;
-        ++ow;
+      const bool ok = mbar_wait(&bar, phase);
+      phase ^= 1u;
+      if (__syncthreads_or(!ok)) {
+        if (threadIdx.x == 0) {
+          atomicOr(err, kAsyncWaitTimeout);
+          mbar_wait(&bar, phase ^ 1u);  // the copy still in flight (bounded)
+        }
+        __syncthreads();
+        return;
+      }
+    } else {
+      const T* x = static_cast<const T*>(d.src);
+      const int32_t H = (int32_t)d.H, W = (int32_t)d.W;
+      const T* xb = x + d.x_off + (int64_t)b * d.xs[0] + (int64_t)c0 * d.xs[1];
+      const int32_t n_stage = ncb * kh * Ws;
+      for (int32_t e0 = threadIdx.x; e0 < n_stage; e0 += kThreads * kUrStage) {
+        T v[kUrStage];
+#pragma unroll
+        for (int k = 0; k < kUrStage; ++k) {
+          const int32_t e = e0 + k * kThreads;
+          v[k] = T(0);
+          if (e < n_stage) {
+            const uint32_t rr = fdiv((uint32_t)e, u.f_ws), cl = fdiv(rr, u.f_kh);
+            const int32_t y = ybase + (int32_t)(rr - cl * u.f_kh.d), xx = e - (int32_t)(rr * u.f_ws.d) - u.xo;
+            if (y >= 0 && y < H && xx >= 0 && xx < W)
+              v[k] = xb[(int64_t)cl * d.xs[1] + (int64_t)y * d.xs[2] + (int64_t)xx * d.xs[3]];
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < kUrStage; ++k)
+          if (e0 + k * kThreads < n_stage) img[e0 + k * kThreads] = v[k];
+      }
+      __syncthreads();
+    }
+    // groups g of V entries; G <= kThreads: step = kThreads / G rows at a
+    // time, thread t on group t % G of rows t / G, t / G + step, ...
+    const int32_t G = ncb * kk / V;
+    const int32_t step = G <= kThreads ? kThreads / G : 1;
+    T* ob = static_cast<T*>(d.dst) + d.c_off + ((int64_t)b * OH + oh) * (int64_t)OW * d.cs[0] + (int64_t)c0 * kk;
+    const int64_t ostep = (int64_t)step * d.cs[0];
+    for (int32_t gi = threadIdx.x; gi < (G <= kThreads ? step * G : G); gi += kThreads) {
+      const int32_t g = G <= kThreads ? gi % G : gi, ow0 = G <= kThreads ? gi / G : 0;
+      int32_t e[V];
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        const uint32_t col = (uint32_t)(g * V + k), cl = fdiv(col, d.f_kk), r = col - cl * d.f_kk.d;
+        const uint32_t i = fdiv(r, d.f_kw), j = r - i * d.f_kw.d;
+        e[k] = (int32_t)cl * u.CS + (int32_t)i * u.IS + (int32_t)j + u.xo - (int32_t)d.pw;
+      }
+      T* op = ob + (int64_t)ow0 * d.cs[0] + g * V;
+      int32_t s = ow0 * sw;
+      for (int32_t ow = ow0; ow < OW; ow += step, s += step * sw, op += ostep) {
+        T v[V];
+#pragma unroll
+        for (int k = 0; k < V; ++k) v[k] = img[e[k] + s];
+        store_cs<T, V>(op, v);
       }
     }
-    __syncthreads();  // the table and the rows are free for the next tile
+    __syncthreads();  // the rows are free for the next tile
   }
 }
 
@@ -696,18 +734,20 @@ __global__ void __launch_bounds__(kThreads) unfold_rows_kernel(const ColsDev d, 
 // at r*RS + q*seg + t, so pixel (yy, xx, cl) of the tile finds window (i, j)
 // at base + ii*(RS - kw) + jj*(seg - 1) + kk - 1, with ii = kh-1-i,
 // jj = kw-1-j and base = yy*RS + xx*seg + cl*kk: the same offsets for every
-// pixel, no window bounds.  The adds run ii and jj upward -- windows by
-// increasing (oh, ow), the reference's order -- from +0; a missing window
-// adds +0, which changes no sum (a sum from +0 is never -0, and
-// s + (+0) = s for every other s, NaN and infinities included).
+// pixel, no window bounds.  Each thread keeps one (cl, xx) and walks the
+// band's rows (RS apart in shared memory, xs2 apart in the image).  The adds
+// run ii and jj upward -- windows by increasing (oh, ow), the reference's
+// order -- from +0; a missing window adds +0, which changes no sum (a sum
+// from +0 is never -0, and s + (+0) = s for every other s, NaN and
+// infinities included).  K > 0: kh = kw = K unrolled; SEG > 0: seg = SEG at
+// compile time (the offsets jj*(seg-1) become immediates).
 struct FoldS1 {
   int32_t CB, TY, XS, R, Q, seg, RS;  // tile; window rows, windows per row, entries per window, row stride
-  int32_t n_cb, n_yb, n_xb;
-  int64_t tiles;
-  FastDiv f_cb, f_xs;
+  uint32_t tiles;
+  FastDiv f_cb, f_nxb, f_nyb, f_ncb;
 };
 
-template <class T, int K>
+template <class T, int K, int SEG>
 __global__ void __launch_bounds__(kThreads) fold_s1_kernel(const __grid_constant__ CUtensorMap cmap, const ColsDev d,
                                                            const FoldS1 f, int* err) {
   using A = Arith<T>;
@@ -718,21 +758,25 @@ __global__ void __launch_bounds__(kThreads) fold_s1_kernel(const __grid_constant
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(fs_raw) + 127) & ~uintptr_t(127));
   T* sm = reinterpret_cast<T*>(base);
   uint64_t& bar = *reinterpret_cast<uint64_t*>(base + (size_t)f.R * f.RS * sizeof(T));
-  T* out = static_cast<T*>(d.dst);
   const int32_t kh = K ? K : (int32_t)d.kh, kw = K ? K : (int32_t)d.kw, kk = kh * kw;
   const int32_t H = (int32_t)d.H, W = (int32_t)d.W, C = (int32_t)d.C, OH = (int32_t)d.OH;
-  const int32_t RS = f.RS, seg = f.seg, row_elems = f.Q * f.seg;
+  const int32_t RS = f.RS, seg = SEG ? SEG : f.seg, row_elems = f.Q * seg;
   const uint32_t box_bytes = (uint32_t)row_elems * (uint32_t)sizeof(T);
+  // this thread's (cl, xx) pairs and first row: pairs = CB * XS
+  const int32_t pairs = f.CB * f.XS;
+  const int32_t ystep = pairs <= kThreads ? kThreads / pairs : 1;
+  const int32_t n_slots = pairs <= kThreads ? ystep * pairs : pairs;
   if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
   }
   __syncthreads();
   uint32_t phase = 0;
-  for (int64_t tile = blockIdx.x; tile < f.tiles; tile += gridDim.x) {
+  for (uint32_t tile = blockIdx.x; tile < f.tiles; tile += gridDim.x) {
     // tile = ((b * n_cb + cb) * n_yb + yb) * n_xb + xb
-    const int64_t t1 = tile / f.n_xb, t2 = t1 / f.n_yb, b = t2 / f.n_cb;
-    const int32_t xb = (int32_t)(tile - t1 * f.n_xb), yb = (int32_t)(t1 - t2 * f.n_yb), cb = (int32_t)(t2 - b * f.n_cb);
+    const uint32_t t1 = fdiv(tile, f.f_nxb), t2 = fdiv(t1, f.f_nyb), b = fdiv(t2, f.f_ncb);
+    const int32_t xb = (int32_t)(tile - t1 * f.f_nxb.d), yb = (int32_t)(t1 - t2 * f.f_nyb.d);
+    const int32_t cb = (int32_t)(t2 - b * f.f_ncb.d);
     const int32_t y0 = yb * f.TY, x0 = xb * f.XS, c0 = cb * f.CB;
     const int32_t ty = H - y0 < f.TY ? H - y0 : f.TY, xs = W - x0 < f.XS ? W - x0 : f.XS;
     const int32_t ncb = C - c0 < f.CB ? C - c0 : f.CB;
@@ -760,28 +804,34 @@ __global__ void __launch_bounds__(kThreads) fold_s1_kernel(const __grid_constant
       __syncthreads();
       return;
     }
-    const int32_t n_pix = f.CB * f.XS * ty;
-    for (int32_t p = threadIdx.x; p < n_pix; p += kThreads) {
-      // p = (yy * XS + xx) * CB + cl
-      const uint32_t rest = fdiv((uint32_t)p, f.f_cb), cl = (uint32_t)p - rest * f.f_cb.d;
-      const uint32_t yy = fdiv(rest, f.f_xs), xx = rest - yy * f.f_xs.d;
+    T* obase = static_cast<T*>(d.dst) + d.x_off + (int64_t)b * d.xs[0] + (int64_t)c0 * d.xs[1] +
+               (int64_t)y0 * d.xs[2] + (int64_t)x0 * d.xs[3];
+    for (int32_t slot = threadIdx.x; slot < n_slots; slot += kThreads) {
+      const int32_t pair = pairs <= kThreads ? slot % pairs : slot, yy0 = pairs <= kThreads ? slot / pairs : 0;
+      // pair = xx * CB + cl
+      const uint32_t xx = fdiv((uint32_t)pair, f.f_cb), cl = (uint32_t)pair - xx * f.f_cb.d;
       if ((int32_t)cl >= ncb || (int32_t)xx >= xs) continue;
-      const T* s = sm + (int32_t)yy * RS + (int32_t)xx * seg + (int32_t)cl * kk + (kk - 1);
-      T acc = T(0);
-      if constexpr (K > 0) {
-        T v[K * K];
+      const T* s = sm + yy0 * RS + (int32_t)xx * seg + (int32_t)cl * kk + (kk - 1);
+      T* o = obase + (int64_t)cl * d.xs[1] + (int64_t)yy0 * d.xs[2] + (int64_t)xx * d.xs[3];
+      const int64_t ostep = (int64_t)ystep * d.xs[2];
+      for (int32_t yy = yy0; yy < ty; yy += ystep, s += ystep * RS, o += ostep) {
+        T acc = T(0);
+        if constexpr (K > 0) {
+          T v[K * K];
 #pragma unroll
-        for (int ii = 0; ii < K; ++ii)
+          for (int ii = 0; ii < K; ++ii) {
+            const T* sr = s + ii * (RS - K);
 #pragma unroll
-          for (int jj = 0; jj < K; ++jj) v[ii * K + jj] = s[ii * (RS - K) + jj * (seg - 1)];
+            for (int jj = 0; jj < K; ++jj) v[ii * K + jj] = sr[jj * (seg - 1)];
+          }
 #pragma unroll
-        for (int w = 0; w < K * K; ++w) acc = A::add(acc, v[w]);
-      } else {
-        for (int32_t ii = 0; ii < kh; ++ii)
-          for (int32_t jj = 0; jj < kw; ++jj) acc = A::add(acc, s[ii * (RS - kw) + jj * (seg - 1)]);
+          for (int w = 0; w < K * K; ++w) acc = A::add(acc, v[w]);
+        } else {
+          for (int32_t ii = 0; ii < kh; ++ii)
+            for (int32_t jj = 0; jj < kw; ++jj) acc = A::add(acc, s[ii * (RS - kw) + jj * (seg - 1)]);
+        }
+        *o = acc;
       }
-      out[d.x_off + b * d.xs[0] + (int64_t)(c0 + (int32_t)cl) * d.xs[1] + (int64_t)(y0 + (int32_t)yy) * d.xs[2] +
-          (int64_t)(x0 + (int32_t)xx) * d.xs[3]] = acc;
     }
     __syncthreads();  // every thread is done with the tile's windows
   }
@@ -990,40 +1040,118 @@ bool pick_fold_tile(const ColsDev& d, int es, FoldTile* t) {
 // Shared memory an unfold-by-rows tile aims at (eight CTAs of 256 threads per
 // SM) and the most it may take (one channel's kh image rows).
 #ifndef TRS_UNFOLD_ROWS_TARGET
-#define TRS_UNFOLD_ROWS_TARGET (12 * 1024)
+#define TRS_UNFOLD_ROWS_TARGET (24 * 1024)
 #endif
 constexpr int64_t kUnfoldRowsMax = 48 * 1024;
 
-// The unfold-by-rows tile: the columns' entries contiguous within a row; V
-// entries per store when every row start and every channel block is
-// V-aligned (V = 16 bytes / element), else 1.  False when one channel's
+// With TMA staging, the shared stride (elements) between window rows i: CB
+// channel rows of ws elements rounded up to 128 bytes, since every TMA
+// destination in shared memory starts on a 128-byte boundary.
+int64_t unfold_row_stride(int64_t CB, int64_t ws, int es) {
+  const int64_t a = 128 / es;
+  return (CB * ws + a - 1) / a * a;
+}
+
+// Bank conflicts of unfold_rows_kernel's shared loads for a full tile of CB
+// channels with strides CS (channel) and IS (window row i): for the first
+// warps and each of the V loads, the most distinct 4-byte words that share a
+// bank, summed.
+int64_t unfold_bank_conflicts(int64_t CB, int64_t kh, int64_t kw, int v, int64_t CS, int64_t IS, int64_t sw, int es) {
+  const int64_t kk = kh * kw, G = CB * kk / v;
+  const int64_t step = G <= kThreads ? kThreads / G : 1, n_slots = G <= kThreads ? step * G : G;
+  int64_t total = 0;
+  for (int64_t w = 0; w < 8 && w * 32 < n_slots; ++w) {
+    for (int k = 0; k < v; ++k) {
+      int64_t words[64];
+      int n = 0;
+      for (int64_t l = 0; l < 32 && w * 32 + l < n_slots; ++l) {
+        const int64_t gi = w * 32 + l, g = G <= kThreads ? gi % G : gi, ow = G <= kThreads ? gi / G : 0;
+        const int64_t col = g * v + k, cl = col / kk, r = col % kk, i = r / kw, j = r % kw;
+        const int64_t a = (cl * CS + i * IS + j + ow * sw) * es / 4;
+        for (int h = 0; h < es / 4; ++h) words[n++] = a + h;
+      }
+      std::sort(words, words + n);
+      n = (int)(std::unique(words, words + n) - words);
+      int per_bank[32] = {0}, worst = 0;
+      for (int x = 0; x < n; ++x) {
+        const int c = ++per_bank[((words[x] % 32) + 32) % 32];
+        worst = c > worst ? c : worst;
+      }
+      total += worst;
+    }
+  }
+  return total;
+}
+
+// The unfold-by-rows tile.  The columns' entries must be contiguous within a
+// row; V entries per store when every row start and every channel block is
+// V-aligned (V = 16 bytes / element), else 1.  *tma: the image is staged by
+// TMA (unit x stride, the other strides positive multiples of 16 bytes, a
+// 16-byte aligned start, box extents within 256).  False when one channel's
 // image rows do not fit kUnfoldRowsMax or an index leaves 31 bits.
-bool pick_unfold_rows(const ColsDev& d, int es, int* V, UnfoldRows* u) {
+bool pick_unfold_rows(const ColsDev& d, int es, int* V, bool* tma, UnfoldRows* u) {
   if (d.cs[1] != 1 || d.rows <= 0 || d.patch <= 0 || d.OW <= 0 || d.kh <= 0 || d.kw <= 0) return false;
-  const int64_t kk = d.kh * d.kw, Wp = (d.OW - 1) * d.sw + d.kw, row_bytes = d.kh * Wp * es;
-  if (row_bytes > kUnfoldRowsMax || d.patch >= (1ll << 30) || d.OW * d.patch >= (1ll << 31)) return false;
-  int v = 16 / es;
+  if (d.B * d.OH * d.C >= (1ll << 32) || d.patch >= (1ll << 30) || d.OW * d.patch >= (1ll << 31)) return false;
+  const int64_t kk = d.kh * d.kw, Wp = (d.OW - 1) * d.sw + d.kw, unit = 16 / es;
+  const int64_t xo_t = (d.pw + unit - 1) / unit * unit, ws_t = (xo_t - d.pw + Wp + unit - 1) / unit * unit;
+  bool t = d.xs[3] == 1 && d.kh <= 256 && ws_t <= 256 && d.H < (1ll << 31) && d.W < (1ll << 31);
+  for (int i = 0; t && i < 3; ++i) t = d.xs[i] > 0 && (d.xs[i] * es) % 16 == 0 && d.xs[i] * es < (1ll << 40);
+  t = t && (reinterpret_cast<uintptr_t>(d.src) + (uintptr_t)(d.x_off * es)) % 16 == 0;
+  const int64_t xo = t ? xo_t : d.pw, Ws = t ? ws_t : Wp, row_bytes = d.kh * Ws * es;
+  if (row_bytes > kUnfoldRowsMax || Ws * d.kh * 256 >= (1ll << 31)) return false;
+  int v = (int)unit;
   if (d.patch % v != 0 || d.cs[0] % v != 0 || d.c_off % v != 0 || reinterpret_cast<uintptr_t>(d.dst) % 16 != 0)
     v = 1;
   int64_t cb_max = TRS_UNFOLD_ROWS_TARGET / row_bytes;
   if (cb_max < 1) cb_max = 1;
+  if (t && cb_max > 256) cb_max = 256;  // the box's channel extent
   int64_t n_cb = (d.C + cb_max - 1) / cb_max;
   int64_t CB = (d.C + n_cb - 1) / n_cb;
   if (v > 1 && n_cb > 1 && (CB * kk) % v != 0) {
     // channel blocks whose entry count is a multiple of V
     int64_t m = 1;
     while ((m * kk) % v != 0) ++m;
-    CB = (CB + m - 1) / m * m;
-    if (CB * row_bytes > kUnfoldRowsMax) v = 1, CB = cb_max < d.C ? cb_max : d.C;
+    const int64_t up = (CB + m - 1) / m * m;
+    if (up * row_bytes <= kUnfoldRowsMax && (!t || up <= 256))
+      CB = up;
+    else
+      v = 1;
     n_cb = (d.C + CB - 1) / CB;
   }
+  int64_t ws = Ws;
+  if (t) {
+    // the staged width (a whole number of 16-byte units, at most 32 words
+    // wider) whose shared loads meet the fewest bank conflicts, found once per
+    // geometry
+    static std::mutex mu;
+    static std::map<std::array<int64_t, 7>, int64_t> chosen;
+    const std::array<int64_t, 7> key = {CB, d.kh, d.kw, (int64_t)v, Ws, d.sw, (int64_t)es};
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = chosen.find(key);
+    if (it != chosen.end()) {
+      ws = it->second;
+    } else {
+      int64_t best = -1;
+      for (int64_t w = Ws; w < Ws + 32 && w <= 256 && d.kh * unfold_row_stride(CB, w, es) * es <= kUnfoldRowsMax;
+           w += unit) {
+        const int64_t c = unfold_bank_conflicts(CB, d.kh, d.kw, v, w, unfold_row_stride(CB, w, es), d.sw, es);
+        if (best < 0 || c < best) best = c, ws = w;
+      }
+      chosen[key] = ws;
+    }
+  }
   *V = v;
+  *tma = t;
   u->CB = (int32_t)CB;
   u->n_cb = (int32_t)n_cb;
-  u->Wp = (int32_t)Wp;
-  u->tab_pad = (int32_t)((CB * kk + 3) / 4 * 4);
-  u->tiles = d.B * d.OH * n_cb;
-  u->f_wp = make_fastdiv((uint32_t)Wp);
+  u->Ws = (int32_t)ws;
+  u->xo = (int32_t)xo;
+  u->CS = (int32_t)(t ? ws : d.kh * ws);
+  u->IS = (int32_t)(t ? unfold_row_stride(CB, ws, es) : ws);
+  u->tiles = (uint32_t)(d.B * d.OH * n_cb);
+  u->f_ncb = make_fastdiv((uint32_t)n_cb);
+  u->f_oh = make_fastdiv((uint32_t)d.OH);
+  u->f_ws = make_fastdiv((uint32_t)ws);
   u->f_kh = make_fastdiv((uint32_t)d.kh);
   return true;
 }
@@ -1043,7 +1171,8 @@ bool pick_unfold_rows(const ColsDev& d, int es, int* V, UnfoldRows* u) {
 bool pick_fold_s1(const ColsDev& d, int es, FoldS1* f) {
   if (d.sh != 1 || d.sw != 1 || d.kh < 1 || d.kw < 1 || d.cs[1] != 1) return false;
   if (d.B <= 0 || d.C <= 0 || d.H <= 0 || d.W <= 0 || d.OH <= 0 || d.OW <= 0) return false;
-  if ((d.cs[0] * es) % 16 != 0 || (reinterpret_cast<uintptr_t>(d.src) + (uintptr_t)(d.c_off * es)) % 16 != 0)
+  if (d.cs[0] <= 0 || (d.cs[0] * es) % 16 != 0 ||
+      (reinterpret_cast<uintptr_t>(d.src) + (uintptr_t)(d.c_off * es)) % 16 != 0)
     return false;
   if (d.patch >= (1ll << 31) || d.B >= (1ll << 31) || d.H >= (1ll << 30) || d.W >= (1ll << 30)) return false;
   if ((uint64_t)d.cs[0] * (uint64_t)es * (uint64_t)d.OW * (uint64_t)d.OH >= (1ull << 40)) return false;  // TMA strides
@@ -1060,6 +1189,8 @@ bool pick_fold_s1(const ColsDev& d, int es, FoldS1* f) {
         const int64_t Q = XS + d.kw - 1, seg = CB * kk, align = 128 / es;
         const int64_t RS = (Q * seg + align - 1) / align * align, R = ty + d.kh - 1;
         if (R * RS * es > TRS_FOLD_S1_BUDGET) continue;
+        const int64_t n_cb = (d.C + CB - 1) / CB, n_yb = (d.H + ty - 1) / ty, n_xb = (d.W + XS - 1) / XS;
+        if (d.B * n_cb * n_yb * n_xb >= (1ll << 32)) return false;
         f->CB = (int32_t)CB;
         f->TY = ty;
         f->XS = (int32_t)XS;
@@ -1067,12 +1198,11 @@ bool pick_fold_s1(const ColsDev& d, int es, FoldS1* f) {
         f->Q = (int32_t)Q;
         f->seg = (int32_t)seg;
         f->RS = (int32_t)RS;
-        f->n_cb = (int32_t)((d.C + CB - 1) / CB);
-        f->n_yb = (int32_t)((d.H + ty - 1) / ty);
-        f->n_xb = (int32_t)((d.W + XS - 1) / XS);
-        f->tiles = d.B * f->n_cb * f->n_yb * f->n_xb;
+        f->tiles = (uint32_t)(d.B * n_cb * n_yb * n_xb);
         f->f_cb = make_fastdiv((uint32_t)CB);
-        f->f_xs = make_fastdiv((uint32_t)XS);
+        f->f_nxb = make_fastdiv((uint32_t)n_xb);
+        f->f_nyb = make_fastdiv((uint32_t)n_yb);
+        f->f_ncb = make_fastdiv((uint32_t)n_cb);
         return true;
       }
     }
@@ -1086,57 +1216,81 @@ template <> constexpr CUtensorMapDataType tma_dtype<double>() { return CU_TENSOR
 template <> constexpr CUtensorMapDataType tma_dtype<int32_t>() { return CU_TENSOR_MAP_DATA_TYPE_INT32; }
 template <> constexpr CUtensorMapDataType tma_dtype<int64_t>() { return CU_TENSOR_MAP_DATA_TYPE_INT64; }
 
-// The columns [B*OH*OW, patch] as the 4-D tensor [B][OH][OW][patch] (row
-// stride cs0), boxes [seg, Q, 1, 1], zeros outside.
+// A 4-D tensor map over `base` (extents innermost first, byte strides of the
+// outer three), boxes `box`, zeros outside.
 template <class T>
-Error make_cols_map(const ColsDev& d, const FoldS1& f, CUtensorMap* map) {
+Error make_map_4d(const char* fn, const void* base, const cuuint64_t (&dims)[4], const cuuint64_t (&strides)[3],
+                  const cuuint32_t (&box)[4], CUtensorMap* map) {
   Error e;
   EncodeTiled enc = encode_fn(&e);
   if (!enc) return e;
-  const cuuint64_t rs = (cuuint64_t)d.cs[0] * sizeof(T);
-  const cuuint64_t dims[4] = {(cuuint64_t)d.patch, (cuuint64_t)d.OW, (cuuint64_t)d.OH, (cuuint64_t)d.B};
-  const cuuint64_t strides[3] = {rs, rs * (cuuint64_t)d.OW, rs * (cuuint64_t)d.OW * (cuuint64_t)d.OH};
-  const cuuint32_t box[4] = {(cuuint32_t)f.seg, (cuuint32_t)f.Q, 1, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
-  void* base = const_cast<T*>(static_cast<const T*>(d.src) + d.c_off);
-  const CUresult r = enc(map, tma_dtype<T>(), 4, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+  const CUresult r = enc(map, tma_dtype<T>(), 4, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
-    return make_error(TRS_ERR_CUDA, "fold_2d: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return make_error(TRS_ERR_CUDA, std::string(fn) + ": cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
   return Error{};
 }
 
 template <class T>
 Error launch_fold_s1(const ColsDev& d, const FoldS1& f, cudaStream_t stream) {
+  // the columns [B*OH*OW, patch] as [B][OH][OW][patch] (row stride cs0)
+  const cuuint64_t rs = (cuuint64_t)d.cs[0] * sizeof(T);
   CUtensorMap map;
-  Error e = make_cols_map<T>(d, f, &map);
+  Error e = make_map_4d<T>("fold_2d", static_cast<const T*>(d.src) + d.c_off,
+                           {(cuuint64_t)d.patch, (cuuint64_t)d.OW, (cuuint64_t)d.OH, (cuuint64_t)d.B},
+                           {rs, rs * (cuuint64_t)d.OW, rs * (cuuint64_t)d.OW * (cuuint64_t)d.OH},
+                           {(cuuint32_t)f.seg, (cuuint32_t)f.Q, 1, 1}, &map);
   if (!e.ok()) return e;
   const int smem = (int)((int64_t)f.R * f.RS * (int64_t)sizeof(T)) + 8 + 128;  // rows, mbarrier, alignment
-  const bool k3 = d.kh == 3 && d.kw == 3;
-  const void* k = k3 ? (const void*)fold_s1_kernel<T, 3> : (const void*)fold_s1_kernel<T, 0>;
+  constexpr int kSeg3 = sizeof(T) == 4 ? 36 : 18;  // 3x3 windows of the fewest channels a TMA box allows
+  const int form = (d.kh == 3 && d.kw == 3) ? (f.seg == kSeg3 ? 2 : 1) : 0;
+  const void* k = form == 2 ? (const void*)fold_s1_kernel<T, 3, kSeg3>
+                : form == 1 ? (const void*)fold_s1_kernel<T, 3, 0> : (const void*)fold_s1_kernel<T, 0, 0>;
   allow_smem(k, smem);
   const uint64_t cap = (uint64_t)current_device_info().sm_count * (uint64_t)resident_blocks_smem(k, kThreads, smem);
   const unsigned g = (unsigned)((uint64_t)f.tiles < cap * 64 ? (uint64_t)f.tiles : cap * 64);
-  if (k3)
-    fold_s1_kernel<T, 3><<<g, kThreads, smem, stream>>>(map, d, f, async_error_word());
+  int* err = async_error_word();
+  if (form == 2)
+    fold_s1_kernel<T, 3, kSeg3><<<g, kThreads, smem, stream>>>(map, d, f, err);
+  else if (form == 1)
+    fold_s1_kernel<T, 3, 0><<<g, kThreads, smem, stream>>>(map, d, f, err);
   else
-    fold_s1_kernel<T, 0><<<g, kThreads, smem, stream>>>(map, d, f, async_error_word());
+    fold_s1_kernel<T, 0, 0><<<g, kThreads, smem, stream>>>(map, d, f, err);
   return check_launch("fold_2d kernel");
 }
 
 template <class T>
-Error launch_unfold_rows(const ColsDev& d, int V, const UnfoldRows& u, cudaStream_t stream) {
+Error launch_unfold_rows(const ColsDev& d, int V, bool tma, const UnfoldRows& u, cudaStream_t stream) {
   constexpr int kV = (int)(16 / sizeof(T));
-  const int smem = (int)((int64_t)u.tab_pad * 4 + (int64_t)u.CB * d.kh * u.Wp * (int64_t)sizeof(T));
-  const void* k = V > 1 ? (const void*)unfold_rows_kernel<T, kV> : (const void*)unfold_rows_kernel<T, 1>;
+  CUtensorMap map;
+  std::memset(&map, 0, sizeof(map));
+  if (tma) {
+    // the image as [B][C][H][W]: boxes [Ws, 1, CB, 1], one per window row
+    const cuuint64_t es = sizeof(T);
+    Error e = make_map_4d<T>("unfold_2d", static_cast<const T*>(d.src) + d.x_off,
+                             {(cuuint64_t)d.W, (cuuint64_t)d.H, (cuuint64_t)d.C, (cuuint64_t)d.B},
+                             {(cuuint64_t)d.xs[2] * es, (cuuint64_t)d.xs[1] * es, (cuuint64_t)d.xs[0] * es},
+                             {(cuuint32_t)u.Ws, 1, (cuuint32_t)u.CB, 1}, &map);
+    if (!e.ok()) return e;
+  }
+  const int64_t stage = tma ? d.kh * (int64_t)u.IS : (int64_t)u.CB * u.CS;
+  const int smem = (int)((stage * (int64_t)sizeof(T) + 7) / 8 * 8) + 8 + 128;  // rows, mbarrier, alignment
+  const void* k = tma ? (V > 1 ? (const void*)unfold_rows_kernel<T, kV, true> : (const void*)unfold_rows_kernel<T, 1, true>)
+                      : (V > 1 ? (const void*)unfold_rows_kernel<T, kV, false> : (const void*)unfold_rows_kernel<T, 1, false>);
   allow_smem(k, smem);
   const uint64_t cap = (uint64_t)current_device_info().sm_count * (uint64_t)resident_blocks_smem(k, kThreads, smem);
   const unsigned g = (unsigned)((uint64_t)u.tiles < cap * 64 ? (uint64_t)u.tiles : cap * 64);
-  if (V > 1)
-    unfold_rows_kernel<T, kV><<<g, kThreads, smem, stream>>>(d, u);
+  int* err = async_error_word();
+  if (tma && V > 1)
+    unfold_rows_kernel<T, kV, true><<<g, kThreads, smem, stream>>>(map, d, u, err);
+  else if (tma)
+    unfold_rows_kernel<T, 1, true><<<g, kThreads, smem, stream>>>(map, d, u, err);
+  else if (V > 1)
+    unfold_rows_kernel<T, kV, false><<<g, kThreads, smem, stream>>>(map, d, u, err);
   else
-    unfold_rows_kernel<T, 1><<<g, kThreads, smem, stream>>>(d, u);
+    unfold_rows_kernel<T, 1, false><<<g, kThreads, smem, stream>>>(map, d, u, err);
   return check_launch("unfold_2d kernel");
 }
 
@@ -1154,7 +1308,8 @@ Error launch_cols(bool unfold, const ColsDev& d, cudaStream_t stream) {
   if (TRS_COLS_ROWS && unfold) {
     UnfoldRows u;
     int V = 1;
-    if (pick_unfold_rows(d, (int)sizeof(T), &V, &u)) return launch_unfold_rows<T>(d, V, u, stream);
+    bool tma = false;
+    if (pick_unfold_rows(d, (int)sizeof(T), &V, &tma, &u)) return launch_unfold_rows<T>(d, V, tma, u, stream);
   }
   if (!unfold) {
     FoldTile ft;
