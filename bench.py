@@ -150,27 +150,86 @@ def run_reference(args) -> None:
 # GPU side
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and throttle reasons sampled during the timed region.
+
+    An NVML thread in this process (the GPU matched to the CUDA device by its
+    UUID) reads the SM clock, its maximum and the active clock-event reasons
+    every 2 ms while `active` is set -- from just before the first timed
+    launch to the synchronisation after the last -- so a timed region of a
+    few tens of milliseconds still gets samples and idle time around it gets
+    none.  Without NVML it falls back to `nvidia-smi -lms 100` over the whole
+    window."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80))
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
         self.file = None
+        self.thread = None
+        self.rows = []
+        self.active = False
+
+    def _nvml_handle(self, nv):
+        import torch
+        try:
+            uuid = str(torch.cuda.get_device_properties(self.gpu).uuid)
+            return nv.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.gpu)
 
     def start(self):
+        import threading
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._nvml_handle(nv)
+            reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.done = threading.Event()
+            probe = (nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM),
+                     reasons(h))
+            del probe  # the calls work on this GPU
+
+            def run():
+                while not self.done.is_set():
+                    if self.active:
+                        try:
+                            self.rows.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                              nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM), int(reasons(h))))
+                        except Exception:
+                            pass
+                    self.done.wait(0.002)
+
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
         except OSError:
             self.proc = None
 
     def stop(self) -> dict:
+        self.active = False
+        if self.thread is not None:
+            self.done.set()
+            self.thread.join(timeout=5)
+            if not self.rows:
+                return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "source": "nvml"}
+            names = sorted({n for _, _, r in self.rows for n, bit in self.REASONS if r & bit})
+            return {"sm_mhz": float(np.median([r[0] for r in self.rows])),
+                    "sm_max_mhz": float(max(r[1] for r in self.rows)), "reasons": names,
+                    "samples": len(self.rows), "source": "nvml, 2 ms, timed region only"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -193,7 +252,7 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvidia-smi, 100 ms"}
 
 
 def measured_peaks() -> tuple[float, str]:
@@ -284,12 +343,12 @@ def run_trs(args) -> None:
 
     clocks = ClockSampler(local)
     clocks.start()
-    time.sleep(0.3)
     launches0 = lib.trs_launch_count()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     barrier()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
+    clocks.active = True
     t_start.record(stream)
     for i in range(args.steps):
         evs[i][0].record(stream)
@@ -297,6 +356,7 @@ def run_trs(args) -> None:
         evs[i][1].record(stream)
     t_end.record(stream)
     barrier()
+    clocks.active = False
     launches = lib.trs_launch_count() - launches0
     clk = clocks.stop()
     ms_total = t_start.elapsed_time(t_end)

@@ -102,6 +102,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+// The whole CTA waits for phase `parity` of `bar`: thread 0 polls (bounded)
+// and the other threads wait at the barrier, where they take no issue slots;
+// the barrier after thread 0's acquiring wait makes the copies' data visible
+// to every thread.  Returns false on every thread when the poll ran out.
+__device__ __forceinline__ bool cta_wait(uint64_t* bar, uint32_t parity) {
+  int failed = 0;
+  if (threadIdx.x == 0) failed = mbar_wait(bar, parity) ? 0 : 1;
+  return __syncthreads_or(failed) == 0;
+}
+
 // Programmatic dependent launch.  launch_dependents: the next grid on the
 // stream, if launched with programmatic stream serialization, may be
 // scheduled now; wait: in that grid, blocks until the previous grid has

@@ -628,8 +628,9 @@ template <class T, int V, bool TMA>
 __global__ void __launch_bounds__(kThreads) unfold_rows_kernel(const __grid_constant__ CUtensorMap imap,
                                                                const ColsDev d, const UnfoldRows u, int* err) {
   extern __shared__ unsigned char ur_raw[];
-  unsigned char* base =
-      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(ur_raw) + 127) & ~uintptr_t(127));
+  // aligned by an offset into the shared array itself (not through an
+  // integer), so the compiler keeps every access a 32-bit shared one
+  unsigned char* base = ur_raw + ((128u - (smem_u32(ur_raw) & 127u)) & 127u);
   T* img = reinterpret_cast<T*>(base);
   const int32_t kh = (int32_t)d.kh, kw = (int32_t)d.kw, kk = kh * kw;
   const int32_t OH = (int32_t)d.OH, OW = (int32_t)d.OW, C = (int32_t)d.C;
@@ -657,9 +658,9 @@ __global__ void __launch_bounds__(kThreads) unfold_rows_kernel(const __grid_cons
         mbar_arrive_expect_tx(&bar, (uint32_t)kh * (uint32_t)u.CB * (uint32_t)Ws * (uint32_t)sizeof(T));
         for (int32_t i = 0; i < kh; ++i) tma_load_4d(img + i * u.IS, &imap, -u.xo, ybase + i, c0, (int32_t)b, &bar);
       }
-      const bool ok = mbar_wait(&bar, phase);
+      const bool ok = cta_wait(&bar, phase);
       phase ^= 1u;
-      if (__syncthreads_or(!ok)) {
+      if (!ok) {
         if (threadIdx.x == 0) {
           atomicOr(err, kAsyncWaitTimeout);
           mbar_wait(&bar, phase ^ 1u);  // the copy still in flight (bounded)
@@ -754,8 +755,9 @@ __global__ void __launch_bounds__(kThreads) fold_s1_kernel(const __grid_constant
   // the window rows from a 128-byte boundary (each row's start, RS * sizeof(T)
   // bytes apart, is one too: a TMA destination), the mbarrier after them
   extern __shared__ unsigned char fs_raw[];
-  unsigned char* base =
-      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(fs_raw) + 127) & ~uintptr_t(127));
+  // aligned by an offset into the shared array itself (not through an
+  // integer), so the compiler keeps every access a 32-bit shared one
+  unsigned char* base = fs_raw + ((128u - (smem_u32(fs_raw) & 127u)) & 127u);
   T* sm = reinterpret_cast<T*>(base);
   uint64_t& bar = *reinterpret_cast<uint64_t*>(base + (size_t)f.R * f.RS * sizeof(T));
   const int32_t kh = K ? K : (int32_t)d.kh, kw = K ? K : (int32_t)d.kw, kk = kh * kw;
@@ -794,9 +796,9 @@ __global__ void __launch_bounds__(kThreads) fold_s1_kernel(const __grid_constant
     for (int32_t r = 0; r < f.R; ++r)
       if (oh_a + r < 0 || oh_a + r >= OH)
         for (int32_t e = threadIdx.x; e < row_elems; e += kThreads) sm[r * RS + e] = T(0);
-    const bool ok = mbar_wait(&bar, phase);
+    const bool ok = cta_wait(&bar, phase);
     phase ^= 1u;
-    if (__syncthreads_or(!ok)) {
+    if (!ok) {
       if (threadIdx.x == 0) {
         atomicOr(err, kAsyncWaitTimeout);
         mbar_wait(&bar, phase ^ 1u);  // the copies still in flight (bounded)
@@ -1208,29 +1210,6 @@ bool pick_fold_s1(const ColsDev& d, int es, FoldS1* f) {
     }
   }
   return false;
-}
-
-template <class T> constexpr CUtensorMapDataType tma_dtype();
-template <> constexpr CUtensorMapDataType tma_dtype<float>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT32; }
-template <> constexpr CUtensorMapDataType tma_dtype<double>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT64; }
-template <> constexpr CUtensorMapDataType tma_dtype<int32_t>() { return CU_TENSOR_MAP_DATA_TYPE_INT32; }
-template <> constexpr CUtensorMapDataType tma_dtype<int64_t>() { return CU_TENSOR_MAP_DATA_TYPE_INT64; }
-
-// A 4-D tensor map over `base` (extents innermost first, byte strides of the
-// outer three), boxes `box`, zeros outside.
-template <class T>
-Error make_map_4d(const char* fn, const void* base, const cuuint64_t (&dims)[4], const cuuint64_t (&strides)[3],
-                  const cuuint32_t (&box)[4], CUtensorMap* map) {
-  Error e;
-  EncodeTiled enc = encode_fn(&e);
-  if (!enc) return e;
-  const cuuint32_t estr[4] = {1, 1, 1, 1};
-  const CUresult r = enc(map, tma_dtype<T>(), 4, const_cast<void*>(base), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return make_error(TRS_ERR_CUDA, std::string(fn) + ": cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
-  return Error{};
 }
 
 template <class T>

@@ -42,6 +42,7 @@
 
 #include "../../include/trs.h"
 #include "kernels.cuh"
+#include "tma.cuh"
 
 namespace trs {
 namespace {
@@ -65,6 +66,7 @@ struct PoolDev {
   int32_t R, P, nblk, full;          // full: whole 16-byte chunks per row
   FastDiv f_blk, f_ow, f_w, f_full;  // blocks per plane, OW, W, full
   int32_t fast;    // items < 2^32: 32-bit index arithmetic
+  int32_t box_rows;  // TMA row kernel: input rows per item's box
   int32_t accumulate;
 };
 
@@ -449,6 +451,158 @@ __global__ void __launch_bounds__(256) pool_tile_fwd_kernel(const PoolDev d) {
   }
 }
 
+// Forward through TMA: an item is a block of R output rows of one plane; its
+// (R-1)*sh + kh input rows (every column, rows past the image never read)
+// arrive as one TMA box [P, rows, 1, 1] of x seen as [N][C][H][W] into shared
+// memory at pitch P (the row width rounded up to 16 bytes).  PAIR (f32, 3x3
+// windows, column stride 2): each thread computes two neighbouring outputs
+// from one 16-byte load and one scalar per window row, a third of the shared
+// loads (stride-2 scalar loads meet two-way bank conflicts).  The CTAs are
+// persistent with two stages: while an item is pooled from one stage, the
+// box of the CTA's next item is in flight into the other.  Each thread owns
+// one output column j and walks every step-th row of the block with two
+// pointer increments, reading its window at fixed shared offsets.  Every wait
+// for a box is bounded: a CTA that runs out records the async error, waits
+// (bounded) for its copies still in flight and returns.
+template <class T, int MODE, int KH = 0, int KW = 0, bool PAIR = false>
+__global__ void __launch_bounds__(256) pool_rows_fwd_kernel(const __grid_constant__ CUtensorMap xmap, const PoolDev d,
+                                                            int* err) {
+  using A = Arith<T>;
+  extern __shared__ unsigned char pool_rows_raw[];
+  // aligned by an offset into the shared array itself (not through an
+  // integer), so the compiler keeps every access a 32-bit shared one
+  unsigned char* base = pool_rows_raw + ((128u - (smem_u32(pool_rows_raw) & 127u)) & 127u);
+  const uint32_t box_bytes = (uint32_t)d.box_rows * (uint32_t)d.P * (uint32_t)sizeof(T);
+  const uint32_t stage_bytes = (box_bytes + 127) / 128 * 128;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(base + 2 * stage_bytes);
+  T* __restrict__ out = static_cast<T*>(d.out);
+  const int kh = KH > 0 ? KH : d.kh, kw = KW > 0 ? KW : d.kw;
+  const int32_t OW = (int32_t)d.OW, P = d.P, sh = d.sh, sw = d.sw;
+  const int32_t step = OW <= 256 ? 256 / OW : 1, n_slots = OW <= 256 ? step * OW : OW;
+  auto issue = [&](uint64_t item, int s) {
+    int64_t n, c, i0;
+    tile_item(d, item, &n, &c, &i0);
+    mbar_arrive_expect_tx(&bar[s], box_bytes);
+    tma_load_4d(base + s * stage_bytes, &xmap, 0, (int32_t)(i0 * sh), (int32_t)c, (int32_t)n, &bar[s]);
+  };
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
+    if (blockIdx.x < (uint64_t)d.items) issue(blockIdx.x, 0);
+  }
+  __syncthreads();
+  uint32_t phase[2] = {0u, 0u};
+  int s = 0;
+  for (uint64_t item = blockIdx.x; item < (uint64_t)d.items; item += gridDim.x, s ^= 1) {
+    const uint64_t next = item + gridDim.x;
+    if (threadIdx.x == 0 && next < (uint64_t)d.items) {
+      // stage s^1 was last read by the item before this one, which ended with
+      // a barrier; order those reads before the copy's writes
+      fence_proxy_async();
+      issue(next, s ^ 1);
+    }
+    const bool ok = cta_wait(&bar[s], phase[s]);
+    phase[s] ^= 1u;
+    if (!ok) {
+      if (threadIdx.x == 0) {
+        atomicOr(err, kAsyncWaitTimeout);
+        mbar_wait(&bar[s], phase[s] ^ 1u);  // the copies still in flight (bounded)
+        if (next < (uint64_t)d.items) mbar_wait(&bar[s ^ 1], phase[s ^ 1]);
+      }
+      __syncthreads();
+      return;
+    }
+    const T* sm = reinterpret_cast<const T*>(base + s * stage_bytes);
+    int64_t n, c, i0;
+    tile_item(d, item, &n, &c, &i0);
+    const int32_t rcnt = (int32_t)(d.OH - i0 < d.R ? d.OH - i0 : d.R);
+    T* oplane = out + d.o_off + n * d.os[0] + c * d.os[1] + i0 * d.os[2];
+    if constexpr (PAIR) {
+      // f32, 3x3 windows at column stride 2: outputs 2q and 2q+1 read columns
+      // 4q .. 4q+4 of each window row, one 16-byte load and one scalar
+      const int32_t QW = (OW + 1) / 2, pstep = 256 / QW;
+      if ((int32_t)threadIdx.x < pstep * QW) {
+        const int32_t q = (int32_t)threadIdx.x % QW, ii = (int32_t)threadIdx.x / QW;
+        const bool second = 2 * q + 1 < OW;
+        const int32_t last = 4 * q + 4 < P ? 4 * q + 4 : P - 1;  // past the row only when unused
+        const T* w = sm + ii * sh * P;
+        T* o = oplane + (int64_t)ii * d.os[2] + (int64_t)(2 * q) * d.os[3];
+        for (int32_t i = ii; i < rcnt; i += pstep, w += pstep * sh * P, o += pstep * d.os[2]) {
+          T v[3][5];
+#pragma unroll
+          for (int u = 0; u < 3; ++u) {
+            const float4 a = *reinterpret_cast<const float4*>(w + u * P + 4 * q);
+            v[u][0] = a.x;
+            v[u][1] = a.y;
+            v[u][2] = a.z;
+            v[u][3] = a.w;
+            v[u][4] = w[u * P + last];
+          }
+          T r0, r1;
+          if constexpr (MODE == kPoolMax) {
+            r0 = v[0][0];
+            r1 = v[0][2];
+#pragma unroll
+            for (int u = 0; u < 3; ++u)
+#pragma unroll
+              for (int k = 0; k < 3; ++k) {
+                if (u > 0 || k > 0) {
+                  if (v[u][k] > r0) r0 = v[u][k];
+                  if (v[u][k + 2] > r1) r1 = v[u][k + 2];
+                }
+              }
+          } else {
+            r0 = T(0);
+            r1 = T(0);
+#pragma unroll
+            for (int u = 0; u < 3; ++u)
+#pragma unroll
+              for (int k = 0; k < 3; ++k) {
+                r0 = A::add(r0, v[u][k]);
+                r1 = A::add(r1, v[u][k + 2]);
+              }
+            r0 = pool_mean<T>(r0, 9);
+            r1 = pool_mean<T>(r1, 9);
+          }
+          o[0] = r0;
+          if (second) o[d.os[3]] = r1;
+        }
+      }
+      __syncthreads();  // every thread is done with stage s
+      continue;
+    }
+    for (int32_t slot = threadIdx.x; slot < n_slots; slot += 256) {
+      const int32_t j = OW <= 256 ? slot % OW : slot, ii = OW <= 256 ? slot / OW : 0;
+      const T* w = sm + ii * sh * P + j * sw;
+      T* o = oplane + (int64_t)ii * d.os[2] + (int64_t)j * d.os[3];
+      for (int32_t i = ii; i < rcnt; i += step, w += step * sh * P, o += step * d.os[2]) {
+        T r;
+        if constexpr (MODE == kPoolMax) {
+          r = w[0];
+#pragma unroll
+          for (int u = 0; u < kh; ++u)
+#pragma unroll
+            for (int v = 0; v < kw; ++v) {
+              if (u == 0 && v == 0) continue;
+              const T val = w[u * P + v];
+              if (val > r) r = val;
+            }
+        } else {
+          r = T(0);
+#pragma unroll
+          for (int u = 0; u < kh; ++u)
+#pragma unroll
+            for (int v = 0; v < kw; ++v) r = A::add(r, w[u * P + v]);
+          r = pool_mean<T>(r, (int64_t)kh * kw);
+        }
+        *o = r;
+      }
+    }
+    __syncthreads();  // every thread is done with stage s
+  }
+}
+
 // MaxPool2d's gradient: an item is a block of R window rows of one plane and
 // owns the input rows from its first window row's start up to the next
 // block's (the last block: to the bottom).  The rows of every window reading
@@ -666,6 +820,80 @@ Error pool_tile_launch(K kernel, const PoolDev& d, size_t smem, cudaStream_t str
   return check_launch(what);
 }
 
+// Shared memory a TMA row item's box may take (a CTA holds two).
+constexpr int64_t kPoolRowsBytes = 24 << 10;
+
+// Tuning knob: 0 never uses the TMA row kernel, 1 uses it wherever it
+// applies, 2 where the strip kernel does not.
+#ifndef TRS_POOL_ROWS
+#define TRS_POOL_ROWS 2
+#endif
+
+// Blocks of R output rows per plane for the TMA row kernel: x must be a TMA
+// tensor (unit-stride rows, positive strides in whole 16-byte units, a
+// 16-byte aligned start), its rows at most 256 wide, the box at most 256 rows
+// and kPoolRowsBytes; false otherwise or when the items overflow 32 bits.
+bool plan_rows(PoolDev* d, int es, int64_t N, int64_t C, size_t* smem) {
+  const int vw = 16 / es;
+  for (int i = 0; i < 3; ++i)
+    if (d->xs[i] <= 0 || d->xs[i] * es >= (1ll << 40)) return false;
+  const int64_t P = (d->W + vw - 1) / vw * vw;
+  auto rows = [&](int64_t R) { return (R - 1) * d->sh + d->kh; };
+  auto fits = [&](int64_t R) { return rows(R) <= 256 && rows(R) * P * es <= kPoolRowsBytes; };
+  if (d->kh < 1 || d->kw < 1 || P > 256 || !fits(1) || N >= (1ll << 31) || C >= (1ll << 31) ||
+      d->H >= (1ll << 31))
+    return false;
+  int64_t R = 1;
+  while (R < d->OH && fits(R + 1)) ++R;
+  const int64_t nblk = (d->OH + R - 1) / R, items = N * C * nblk;
+  if (items >= (1ll << 32)) return false;
+  d->R = (int32_t)R;
+  d->P = (int32_t)P;
+  d->nblk = (int32_t)nblk;
+  d->items = items;
+  d->box_rows = (int32_t)rows(R);
+  d->f_blk = make_fastdiv((uint32_t)nblk);
+  d->f_c = make_fastdiv((uint32_t)(C < 1 ? 1 : C));
+  *smem = (size_t)(2 * ((rows(R) * P * es + 127) / 128 * 128) + 16 + 128);  // two boxes, mbarriers, alignment
+  return true;
+}
+
+template <class T, int MODE, int KH, int KW, bool PAIR = false>
+Error pool_rows_launch(const PoolDev& d, const CUtensorMap& map, size_t smem, cudaStream_t stream) {
+  const void* k = (const void*)pool_rows_fwd_kernel<T, MODE, KH, KW, PAIR>;
+  allow_smem(k, (int)smem);
+  const uint64_t cap = (uint64_t)current_device_info().sm_count * (uint64_t)resident_blocks_smem(k, 256, (int)smem);
+  const uint64_t grid = (uint64_t)d.items < cap ? (uint64_t)d.items : cap;  // persistent
+  pool_rows_fwd_kernel<T, MODE, KH, KW, PAIR><<<(unsigned)grid, 256, smem, stream>>>(map, d, async_error_word());
+  return check_launch("pool rows");
+}
+
+template <class T>
+Error launch_pool_rows(const PoolDev& d, int mode, int64_t N, int64_t C, size_t smem, cudaStream_t stream) {
+  // x as [N][C][H][W]: boxes [P, box_rows, 1, 1]
+  const cuuint64_t es = sizeof(T);
+  CUtensorMap map;
+  Error e = make_map_4d<T>("pool", static_cast<const T*>(d.x) + d.x_off,
+                           {(cuuint64_t)d.W, (cuuint64_t)d.H, (cuuint64_t)C, (cuuint64_t)N},
+                           {(cuuint64_t)d.xs[2] * es, (cuuint64_t)d.xs[1] * es, (cuuint64_t)d.xs[0] * es},
+                           {(cuuint32_t)d.P, (cuuint32_t)d.box_rows, 1, 1}, &map);
+  if (!e.ok()) return e;
+  const bool max = mode == kPoolMax;
+  if constexpr (sizeof(T) == 4) {
+    if (d.kh == 3 && d.kw == 3 && d.sw == 2 && (d.OW + 1) / 2 <= 256)
+      return max ? pool_rows_launch<T, kPoolMax, 3, 3, true>(d, map, smem, stream)
+                 : pool_rows_launch<T, kPoolAvg, 3, 3, true>(d, map, smem, stream);
+  }
+  if (d.kh == 3 && d.kw == 3)
+    return max ? pool_rows_launch<T, kPoolMax, 3, 3>(d, map, smem, stream)
+               : pool_rows_launch<T, kPoolAvg, 3, 3>(d, map, smem, stream);
+  if (d.kh == 2 && d.kw == 2)
+    return max ? pool_rows_launch<T, kPoolMax, 2, 2>(d, map, smem, stream)
+               : pool_rows_launch<T, kPoolAvg, 2, 2>(d, map, smem, stream);
+  return max ? pool_rows_launch<T, kPoolMax, 0, 0>(d, map, smem, stream)
+             : pool_rows_launch<T, kPoolAvg, 0, 0>(d, map, smem, stream);
+}
+
 template <class T>
 Error launch_pool_fwd(PoolDev d, int mode, int64_t N, int64_t C, cudaStream_t stream) {
   constexpr int VW = 16 / sizeof(T);
@@ -673,6 +901,10 @@ Error launch_pool_fwd(PoolDev d, int mode, int64_t N, int64_t C, cudaStream_t st
   const bool aligned = rows_aligned(d.x, d.x_off, d.xs, sizeof(T));
   const bool strip = d.kw == d.sw && d.kw > 0 && VW % d.kw == 0 && d.kh <= 4 && aligned;
   size_t smem = 0;
+  if (TRS_POOL_ROWS && (TRS_POOL_ROWS == 1 || !strip) && aligned) {
+    PoolDev r = d;
+    if (plan_rows(&r, sizeof(T), N, C, &smem)) return launch_pool_rows<T>(r, mode, N, C, smem, stream);
+  }
   if ((!strip || TRS_POOL_TILE_FIRST) && aligned && plan_tile(&d, false, sizeof(T), N, C, &smem)) {
     // the common square windows with their loops unrolled
     if (d.kh == 3 && d.kw == 3)

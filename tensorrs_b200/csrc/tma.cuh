@@ -42,6 +42,29 @@ inline EncodeTiled encode_fn(Error* err) {
   return fn;
 }
 
+template <class T> constexpr CUtensorMapDataType tma_dtype();
+template <> constexpr CUtensorMapDataType tma_dtype<float>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT32; }
+template <> constexpr CUtensorMapDataType tma_dtype<double>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT64; }
+template <> constexpr CUtensorMapDataType tma_dtype<int32_t>() { return CU_TENSOR_MAP_DATA_TYPE_INT32; }
+template <> constexpr CUtensorMapDataType tma_dtype<int64_t>() { return CU_TENSOR_MAP_DATA_TYPE_INT64; }
+
+// A 4-D tensor map over `base` (extents innermost first, byte strides of the
+// outer three), boxes `box`, zeros outside.
+template <class T>
+inline Error make_map_4d(const char* fn, const void* base, const cuuint64_t (&dims)[4], const cuuint64_t (&strides)[3],
+                  const cuuint32_t (&box)[4], CUtensorMap* map) {
+  Error e;
+  EncodeTiled enc = encode_fn(&e);
+  if (!enc) return e;
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(map, tma_dtype<T>(), 4, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return make_error(TRS_ERR_CUDA, std::string(fn) + ": cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return Error{};
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(

@@ -71,6 +71,7 @@ FWD = [
     ([2, 2, 11, 8], (3, 1), (2, 3)),
     ([1, 3, 32, 36], (5, 3), (3, 2)),
     ([1, 2, 64, 1024], (3, 3), (2, 2)),   # several blocks of rows per plane
+    ([1, 2, 600, 40], (3, 3), (2, 2)),    # several TMA boxes of rows per plane
     ([1, 1, 4, 8192], (1, 3), (1, 2)),    # rows too wide for a tile: the general kernel
 ]
 
