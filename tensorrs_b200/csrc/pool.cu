@@ -29,6 +29,9 @@
 //       `current + grad` of autodiff/traits.rs:141-150).
 //       pool_max_bwd_strip_kernel serves windows that tile the image (stride
 //       == window, kw dividing 16 bytes) with 16-byte strips;
+//       pool_max_bwd_rows_kernel serves f32 2x2 windows at stride 2 tiling
+//       an image of even height and a width that is a multiple of 8, from TMA
+//       boxes of x and grad_out;
 //       pool_tile_bwd_kernel stages the rows of a block of window rows in
 //       shared memory, finds each window's winner once, then lets each owned
 //       pixel add the gradients of the covering windows it wins.
@@ -603,6 +606,105 @@ __global__ void __launch_bounds__(256) pool_rows_fwd_kernel(const __grid_constan
   }
 }
 
+// MaxPool2d's gradient for f32 2x2 windows at stride 2 that tile the image
+// (H even, W a multiple of 8, so every pixel lies in exactly one window and
+// the gradient's rows are whole 16-byte units): an item is a block of R window
+// rows of one plane; its 2R rows of x and R rows of grad_out arrive as two TMA
+// boxes into one of two stages of a persistent CTA (the next item's boxes in
+// flight while the current one is done).  Each thread takes two neighbouring
+// windows of a window row: two 16-byte loads of x and one 8-byte load of
+// grad_out from shared memory, each window's winner found as the first of
+// its largest elements in row-major order (a NaN first element wins), then
+// two 16-byte stores of grad_x: RN(0 + g) at the winner, +0 elsewhere (with
+// ACC, added to the gradient already held, pixel by pixel).
+template <bool ACC>
+__global__ void __launch_bounds__(256) pool_max_bwd_rows_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                                const __grid_constant__ CUtensorMap gmap,
+                                                                const PoolDev d, int* err) {
+  using A = Arith<float>;
+  extern __shared__ unsigned char pool_bwd_raw[];
+  // aligned by an offset into the shared array itself, so every access stays
+  // a 32-bit shared one
+  unsigned char* base = pool_bwd_raw + ((128u - (smem_u32(pool_bwd_raw) & 127u)) & 127u);
+  const int32_t W = (int32_t)d.W, OW = (int32_t)d.OW;
+  const uint32_t xbytes = (uint32_t)(2 * d.R) * (uint32_t)W * 4u, gbytes = (uint32_t)d.R * (uint32_t)OW * 4u;
+  const uint32_t xpart = (xbytes + 127) / 128 * 128, stage_bytes = xpart + (gbytes + 127) / 128 * 128;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(base + 2 * stage_bytes);
+  float* __restrict__ out = static_cast<float*>(d.out);
+  const int32_t QP = OW / 2, pstep = 256 / QP;
+  const bool active = (int32_t)threadIdx.x < pstep * QP;
+  const int32_t q = (int32_t)threadIdx.x % QP, ii = (int32_t)threadIdx.x / QP;
+  auto issue = [&](uint64_t item, int s) {
+    int64_t n, c, i0;
+    tile_item(d, item, &n, &c, &i0);
+    mbar_arrive_expect_tx(&bar[s], xbytes + gbytes);
+    tma_load_4d(base + s * stage_bytes, &xmap, 0, (int32_t)(2 * i0), (int32_t)c, (int32_t)n, &bar[s]);
+    tma_load_4d(base + s * stage_bytes + xpart, &gmap, 0, (int32_t)i0, (int32_t)c, (int32_t)n, &bar[s]);
+  };
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
+    if (blockIdx.x < (uint64_t)d.items) issue(blockIdx.x, 0);
+  }
+  __syncthreads();
+  uint32_t phase[2] = {0u, 0u};
+  int s = 0;
+  for (uint64_t item = blockIdx.x; item < (uint64_t)d.items; item += gridDim.x, s ^= 1) {
+    const uint64_t next = item + gridDim.x;
+    if (threadIdx.x == 0 && next < (uint64_t)d.items) {
+      fence_proxy_async();  // stage s^1's reads ended with the barrier of the item before
+      issue(next, s ^ 1);
+    }
+    const bool ok = cta_wait(&bar[s], phase[s]);
+    phase[s] ^= 1u;
+    if (!ok) {
+      if (threadIdx.x == 0) {
+        atomicOr(err, kAsyncWaitTimeout);
+        mbar_wait(&bar[s], phase[s] ^ 1u);  // the copies still in flight (bounded)
+        if (next < (uint64_t)d.items) mbar_wait(&bar[s ^ 1], phase[s ^ 1]);
+      }
+      __syncthreads();
+      return;
+    }
+    if (active) {
+      int64_t n, c, i0;
+      tile_item(d, item, &n, &c, &i0);
+      const int32_t rcnt = (int32_t)(d.OH - i0 < d.R ? d.OH - i0 : d.R);
+      const float* sx = reinterpret_cast<const float*>(base + s * stage_bytes);
+      const float* sg = reinterpret_cast<const float*>(base + s * stage_bytes + xpart);
+      float* o = out + d.o_off + n * d.os[0] + c * d.os[1] + (2 * i0 + 2 * ii) * d.os[2] + 4 * q;
+      for (int32_t i = ii; i < rcnt; i += pstep, o += 2 * pstep * d.os[2]) {
+        const float4 a = *reinterpret_cast<const float4*>(sx + (2 * i) * W + 4 * q);
+        const float4 b = *reinterpret_cast<const float4*>(sx + (2 * i + 1) * W + 4 * q);
+        const float2 gv = *reinterpret_cast<const float2*>(sg + i * OW + 2 * q);
+        // window 0: a.x a.y / b.x b.y; window 1: a.z a.w / b.z b.w (row-major)
+        int w0 = 0, w1 = 0;
+        float m0 = a.x, m1 = a.z;
+        if (a.y > m0) { m0 = a.y; w0 = 1; }
+        if (b.x > m0) { m0 = b.x; w0 = 2; }
+        if (b.y > m0) { w0 = 3; }
+        if (a.w > m1) { m1 = a.w; w1 = 1; }
+        if (b.z > m1) { m1 = b.z; w1 = 2; }
+        if (b.w > m1) { w1 = 3; }
+        const float g0 = A::add(0.0f, gv.x), g1 = A::add(0.0f, gv.y);
+        float4 r0 = make_float4(w0 == 0 ? g0 : 0.0f, w0 == 1 ? g0 : 0.0f, w1 == 0 ? g1 : 0.0f, w1 == 1 ? g1 : 0.0f);
+        float4 r1 = make_float4(w0 == 2 ? g0 : 0.0f, w0 == 3 ? g0 : 0.0f, w1 == 2 ? g1 : 0.0f, w1 == 3 ? g1 : 0.0f);
+        float4* o0 = reinterpret_cast<float4*>(o);
+        float4* o1 = reinterpret_cast<float4*>(o + d.os[2]);
+        if constexpr (ACC) {
+          const float4 c0 = *o0, c1 = *o1;
+          r0 = make_float4(A::add(c0.x, r0.x), A::add(c0.y, r0.y), A::add(c0.z, r0.z), A::add(c0.w, r0.w));
+          r1 = make_float4(A::add(c1.x, r1.x), A::add(c1.y, r1.y), A::add(c1.z, r1.z), A::add(c1.w, r1.w));
+        }
+        *o0 = r0;
+        *o1 = r1;
+      }
+    }
+    __syncthreads();  // every thread is done with stage s
+  }
+}
+
 // MaxPool2d's gradient: an item is a block of R window rows of one plane and
 // owns the input rows from its first window row's start up to the next
 // block's (the last block: to the bottom).  The rows of every window reading
@@ -894,6 +996,63 @@ Error launch_pool_rows(const PoolDev& d, int mode, int64_t N, int64_t C, size_t 
              : pool_rows_launch<T, kPoolAvg, 0, 0>(d, map, smem, stream);
 }
 
+// Tuning knob: 0 keeps MaxPool2d's gradient off the TMA row kernel.
+#ifndef TRS_POOL_BWD_ROWS
+#define TRS_POOL_BWD_ROWS 1
+#endif
+
+// The TMA row kernel of MaxPool2d's gradient (f32, 2x2 windows at stride 2
+// tiling the image, W a multiple of 8 and at most 256): x and grad_out as TMA
+// tensors, grad_x in unit-stride 16-byte aligned rows; blocks of R window rows
+// whose two boxes fit kPoolRowsBytes.  False otherwise.
+bool plan_bwd_rows(PoolDev* d, const trs_view* x, const trs_view* g, const trs_view* gx, int64_t N, int64_t C,
+                   size_t* smem) {
+  if (x->dtype != TRS_F32 || d->kh != 2 || d->kw != 2 || d->sh != 2 || d->sw != 2) return false;
+  if (d->H % 2 != 0 || d->W % 8 != 0 || d->W > 256 || d->OH * 2 != d->H || d->OW * 2 != d->W) return false;
+  if (!rows_aligned(x->data, x->offset, x->strides, 4) || !rows_aligned(g->data, g->offset, g->strides, 4) ||
+      !rows_aligned(gx->data, gx->offset, gx->strides, 4))
+    return false;
+  for (int i = 0; i < 3; ++i)
+    if (x->strides[i] <= 0 || g->strides[i] <= 0 || x->strides[i] * 4 >= (1ll << 40) || g->strides[i] * 4 >= (1ll << 40))
+      return false;
+  if (N >= (1ll << 31) || C >= (1ll << 31)) return false;
+  auto bytes = [&](int64_t R) { return ((2 * R * d->W * 4 + 127) / 128 + (R * d->OW * 4 + 127) / 128) * 128; };
+  int64_t R = 1;
+  while (R < d->OH && 2 * (R + 1) <= 256 && bytes(R + 1) <= kPoolRowsBytes) ++R;
+  const int64_t nblk = (d->OH + R - 1) / R, items = N * C * nblk;
+  if (items >= (1ll << 32)) return false;
+  d->R = (int32_t)R;
+  d->nblk = (int32_t)nblk;
+  d->items = items;
+  d->f_blk = make_fastdiv((uint32_t)nblk);
+  d->f_c = make_fastdiv((uint32_t)(C < 1 ? 1 : C));
+  *smem = (size_t)(2 * bytes(R) + 16 + 128);  // two stages, mbarriers, alignment
+  return true;
+}
+
+Error launch_pool_bwd_rows(const PoolDev& d, int64_t N, int64_t C, size_t smem, cudaStream_t stream) {
+  CUtensorMap xmap, gmap;
+  Error e = make_map_4d<float>("pool backward", static_cast<const float*>(d.x) + d.x_off,
+                               {(cuuint64_t)d.W, (cuuint64_t)d.H, (cuuint64_t)C, (cuuint64_t)N},
+                               {(cuuint64_t)d.xs[2] * 4, (cuuint64_t)d.xs[1] * 4, (cuuint64_t)d.xs[0] * 4},
+                               {(cuuint32_t)d.W, (cuuint32_t)(2 * d.R), 1, 1}, &xmap);
+  if (e.ok())
+    e = make_map_4d<float>("pool backward", static_cast<const float*>(d.g) + d.g_off,
+                           {(cuuint64_t)d.OW, (cuuint64_t)d.OH, (cuuint64_t)C, (cuuint64_t)N},
+                           {(cuuint64_t)d.gs[2] * 4, (cuuint64_t)d.gs[1] * 4, (cuuint64_t)d.gs[0] * 4},
+                           {(cuuint32_t)d.OW, (cuuint32_t)d.R, 1, 1}, &gmap);
+  if (!e.ok()) return e;
+  const void* k = d.accumulate ? (const void*)pool_max_bwd_rows_kernel<true> : (const void*)pool_max_bwd_rows_kernel<false>;
+  allow_smem(k, (int)smem);
+  const uint64_t cap = (uint64_t)current_device_info().sm_count * (uint64_t)resident_blocks_smem(k, 256, (int)smem);
+  const unsigned grid = (unsigned)((uint64_t)d.items < cap ? (uint64_t)d.items : cap);  // persistent
+  if (d.accumulate)
+    pool_max_bwd_rows_kernel<true><<<grid, 256, smem, stream>>>(xmap, gmap, d, async_error_word());
+  else
+    pool_max_bwd_rows_kernel<false><<<grid, 256, smem, stream>>>(xmap, gmap, d, async_error_word());
+  return check_launch("max pool backward rows");
+}
+
 template <class T>
 Error launch_pool_fwd(PoolDev d, int mode, int64_t N, int64_t C, cudaStream_t stream) {
   constexpr int VW = 16 / sizeof(T);
@@ -1015,6 +1174,11 @@ Error run_max_pool_backward(const trs_view* x, const trs_view* g, int64_t kh, in
     d.os[i] = gx->strides[i];
   }
   d.accumulate = accumulate ? 1 : 0;
+  {
+    PoolDev r = d;
+    size_t smem = 0;
+    if (TRS_POOL_BWD_ROWS && plan_bwd_rows(&r, x, g, gx, N, C, &smem)) return launch_pool_bwd_rows(r, N, C, smem, stream);
+  }
   if (x->dtype == TRS_F32) return launch_pool_bwd<float>(d, N, C, stream);
   return launch_pool_bwd<double>(d, N, C, stream);
 }

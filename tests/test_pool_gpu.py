@@ -154,6 +154,7 @@ BWD = [
     ([1, 2, 4, 8], (1, 2), (1, 1)),
     ([2, 2, 11, 8], (2, 1), (3, 3)),
     ([1, 2, 40, 1024], (3, 3), (2, 2)),  # blocks that take windows from the block above
+    ([1, 2, 600, 16], (2, 2), (2, 2)),   # several TMA row blocks per plane
     ([1, 2, 13, 16], (5, 2), (1, 2)),    # windows five rows high at stride 1
 ]
 
