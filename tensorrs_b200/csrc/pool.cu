@@ -458,9 +458,10 @@ __global__ void __launch_bounds__(256) pool_tile_fwd_kernel(const PoolDev d) {
 // (R-1)*sh + kh input rows (every column, rows past the image never read)
 // arrive as one TMA box [P, rows, 1, 1] of x seen as [N][C][H][W] into shared
 // memory at pitch P (the row width rounded up to 16 bytes).  PAIR (f32, 3x3
-// windows, column stride 2): each thread computes two neighbouring outputs
-// from one 16-byte load and one scalar per window row, a third of the shared
-// loads (stride-2 scalar loads meet two-way bank conflicts).  The CTAs are
+// or 2x2 windows, column stride 2): each thread computes two neighbouring
+// outputs from one 16-byte load (and, for 3x3, one scalar) per window row, a
+// third of the shared loads (stride-2 scalar loads meet two-way bank
+// conflicts).  The CTAs are
 // persistent with two stages: while an item is pooled from one stage, the
 // box of the CTA's next item is in flight into the other.  Each thread owns
 // one output column j and walks every step-th row of the block with two
@@ -522,8 +523,9 @@ __global__ void __launch_bounds__(256) pool_rows_fwd_kernel(const __grid_constan
     const int32_t rcnt = (int32_t)(d.OH - i0 < d.R ? d.OH - i0 : d.R);
     T* oplane = out + d.o_off + n * d.os[0] + c * d.os[1] + i0 * d.os[2];
     if constexpr (PAIR) {
-      // f32, 3x3 windows at column stride 2: outputs 2q and 2q+1 read columns
-      // 4q .. 4q+4 of each window row, one 16-byte load and one scalar
+      // f32, 3x3 (2x2) windows at column stride 2: outputs 2q and 2q+1 read
+      // columns 4q .. 4q+4 (4q .. 4q+3) of each window row, one 16-byte load
+      // and one scalar (one 16-byte load)
       const int32_t QW = (OW + 1) / 2, pstep = 256 / QW;
       if ((int32_t)threadIdx.x < pstep * QW) {
         const int32_t q = (int32_t)threadIdx.x % QW, ii = (int32_t)threadIdx.x / QW;
@@ -531,25 +533,29 @@ __global__ void __launch_bounds__(256) pool_rows_fwd_kernel(const __grid_constan
         const int32_t last = 4 * q + 4 < P ? 4 * q + 4 : P - 1;  // past the row only when unused
         const T* w = sm + ii * sh * P;
         T* o = oplane + (int64_t)ii * d.os[2] + (int64_t)(2 * q) * d.os[3];
+        // window columns: output 2q starts at column 4q, output 2q+1 at
+        // 4q + KW - 1 (3x3: 4q+2; 2x2: 4q+2 as well, the window one column
+        // narrower); KW == 2 needs no fifth column
+        constexpr int K = KW;
         for (int32_t i = ii; i < rcnt; i += pstep, w += pstep * sh * P, o += pstep * d.os[2]) {
-          T v[3][5];
+          T v[K][5];
 #pragma unroll
-          for (int u = 0; u < 3; ++u) {
+          for (int u = 0; u < K; ++u) {
             const float4 a = *reinterpret_cast<const float4*>(w + u * P + 4 * q);
             v[u][0] = a.x;
             v[u][1] = a.y;
             v[u][2] = a.z;
             v[u][3] = a.w;
-            v[u][4] = w[u * P + last];
+            v[u][4] = K == 3 ? w[u * P + last] : T(0);
           }
           T r0, r1;
           if constexpr (MODE == kPoolMax) {
             r0 = v[0][0];
             r1 = v[0][2];
 #pragma unroll
-            for (int u = 0; u < 3; ++u)
+            for (int u = 0; u < K; ++u)
 #pragma unroll
-              for (int k = 0; k < 3; ++k) {
+              for (int k = 0; k < K; ++k) {
                 if (u > 0 || k > 0) {
                   if (v[u][k] > r0) r0 = v[u][k];
                   if (v[u][k + 2] > r1) r1 = v[u][k + 2];
@@ -559,14 +565,14 @@ __global__ void __launch_bounds__(256) pool_rows_fwd_kernel(const __grid_constan
             r0 = T(0);
             r1 = T(0);
 #pragma unroll
-            for (int u = 0; u < 3; ++u)
+            for (int u = 0; u < K; ++u)
 #pragma unroll
-              for (int k = 0; k < 3; ++k) {
+              for (int k = 0; k < K; ++k) {
                 r0 = A::add(r0, v[u][k]);
                 r1 = A::add(r1, v[u][k + 2]);
               }
-            r0 = pool_mean<T>(r0, 9);
-            r1 = pool_mean<T>(r1, 9);
+            r0 = pool_mean<T>(r0, K * K);
+            r1 = pool_mean<T>(r1, K * K);
           }
           o[0] = r0;
           if (second) o[d.os[3]] = r1;
@@ -985,6 +991,9 @@ Error launch_pool_rows(const PoolDev& d, int mode, int64_t N, int64_t C, size_t 
     if (d.kh == 3 && d.kw == 3 && d.sw == 2 && (d.OW + 1) / 2 <= 256)
       return max ? pool_rows_launch<T, kPoolMax, 3, 3, true>(d, map, smem, stream)
                  : pool_rows_launch<T, kPoolAvg, 3, 3, true>(d, map, smem, stream);
+    if (d.kh == 2 && d.kw == 2 && d.sw == 2 && (d.OW + 1) / 2 <= 256)
+      return max ? pool_rows_launch<T, kPoolMax, 2, 2, true>(d, map, smem, stream)
+                 : pool_rows_launch<T, kPoolAvg, 2, 2, true>(d, map, smem, stream);
   }
   if (d.kh == 3 && d.kw == 3)
     return max ? pool_rows_launch<T, kPoolMax, 3, 3>(d, map, smem, stream)
@@ -1060,7 +1069,9 @@ Error launch_pool_fwd(PoolDev d, int mode, int64_t N, int64_t C, cudaStream_t st
   const bool aligned = rows_aligned(d.x, d.x_off, d.xs, sizeof(T));
   const bool strip = d.kw == d.sw && d.kw > 0 && VW % d.kw == 0 && d.kh <= 4 && aligned;
   size_t smem = 0;
-  if (TRS_POOL_ROWS && (TRS_POOL_ROWS == 1 || !strip) && aligned) {
+  // f32 2x2 windows at stride 2: the row kernel's paired outputs beat the strips
+  const bool pair2 = sizeof(T) == 4 && d.kh == 2 && d.kw == 2 && d.sw == 2;
+  if (TRS_POOL_ROWS && (TRS_POOL_ROWS == 1 || !strip || pair2) && aligned) {
     PoolDev r = d;
     if (plan_rows(&r, sizeof(T), N, C, &smem)) return launch_pool_rows<T>(r, mode, N, C, smem, stream);
   }
