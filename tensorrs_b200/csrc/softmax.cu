@@ -289,8 +289,9 @@ __device__ __forceinline__ Acc consumer_sum(Acc acc, Acc* red, int cw, int lane,
 #ifndef TRS_LN_NACC
 #define TRS_LN_NACC 1
 #endif
-// Tuning knob: chunks of the normalising pass unrolled for f32 rows (their
-// gamma and beta loads in flight together; 8 against 4: 2.5 % at [8192, 16384]).
+// Tuning knob: chunks of the normalising pass unrolled (their gamma and beta
+// loads in flight together; 8 against 4: 2.5 % at [8192, 16384] in f32, where
+// 4 spilled 20 bytes of registers and 8 spills none).
 #ifndef TRS_LN_U3
 #define TRS_LN_U3 8
 #endif
@@ -359,7 +360,7 @@ __device__ __forceinline__ void layer_norm_row(const SmDev& d, const unsigned ch
   T* orow = static_cast<T*>(d.out) + bo;
   const T* gm = static_cast<const T*>(d.gamma) + d.g_off;
   const T* bt = static_cast<const T*>(d.beta) + d.b_off;
-  constexpr int kU3 = sizeof(T) == 4 ? TRS_LN_U3 : 4;  // f64 rows: 4 (8 spills its registers)
+  constexpr int kU3 = TRS_LN_U3;
 #pragma unroll kU3
   for (uint32_t k = (uint32_t)ct; k < nchunk; k += kSmGroupThreads) {
     const SVec<T, V> v = *reinterpret_cast<const SVec<T, V>*>(stage + k * 16);
