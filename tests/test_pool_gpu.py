@@ -2,12 +2,15 @@
 oracle's restatement of the reference (reshape -> unfold_2d -> max_axis, or
 sum_axis / (kh * kw); max_axis's backward -> fold_2d):
 
-* the forward kernels: the 16-byte strip kernel (kw == stride_w dividing 16
-  bytes, its ragged row ends), the shared-memory tile kernel (rows of a
-  multiple of 16 bytes, any window: overlapping, gapped, planes split into
-  several blocks of rows) and the general one (other views, strided outputs);
+* the forward kernels: the TMA row-box kernel (rows of a multiple of 16 bytes
+  and at most 256 elements, any window: overlapping, gapped, planes split into
+  several boxes of rows; f32 3x3 and 2x2 windows at stride 2 two outputs per
+  thread), the 16-byte strip kernel (kw == stride_w dividing 16 bytes, its
+  ragged row ends), the shared-memory tile kernel (wider rows) and the general
+  one (other views, strided outputs);
 * NaN as a window's first element and elsewhere, +-inf, -0 / +0 ties;
-* MaxPool2d's gradient through the strip, tile and general kernels with
+* MaxPool2d's gradient through the TMA row-box kernel (f32 2x2 windows at
+  stride 2 tiling the image), the strip, tile and general kernels with
   ties, overlapping windows (a pixel collecting from several windows, blocks
   taking windows from the block above), uncovered edge pixels, and the
   accumulation onto a held gradient;
