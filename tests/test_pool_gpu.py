@@ -96,7 +96,8 @@ def test_pool_forward_ties_and_signed_zeros(kind):
     import oracle
     x = _ties([3, 4, 12, 16], np.float32, 1)
     dv = contiguous(x)
-    for kernel, stride in [((2, 2), (2, 2)), ((3, 3), (1, 1)), ((2, 4), (2, 4))]:
+    # 2x2 / 3x3 at stride 2: two outputs per thread (3x3: an odd OW, the last thread's second one skipped)
+    for kernel, stride in [((2, 2), (2, 2)), ((3, 3), (2, 2)), ((3, 3), (1, 1)), ((2, 4), (2, 4))]:
         got = _fwd(kind, dv, kernel, stride, np.float32)
         want = oracle.pool2d(kind, dv.host_view(), kernel, stride)
         assert_bit_exact(got, want, f"{kind} ties {kernel}")
