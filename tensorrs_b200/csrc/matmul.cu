@@ -1042,7 +1042,7 @@ bool pick_fold_tile(const ColsDev& d, int es, FoldTile* t) {
 // Shared memory an unfold-by-rows tile aims at (eight CTAs of 256 threads per
 // SM) and the most it may take (one channel's kh image rows).
 #ifndef TRS_UNFOLD_ROWS_TARGET
-#define TRS_UNFOLD_ROWS_TARGET (24 * 1024)
+#define TRS_UNFOLD_ROWS_TARGET (12 * 1024)
 #endif
 constexpr int64_t kUnfoldRowsMax = 48 * 1024;
 
