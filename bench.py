@@ -195,15 +195,19 @@ class ClockSampler:
                      reasons(h))
             del probe  # the calls work on this GPU
 
+            def sample():
+                try:
+                    self.rows.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                      nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM), int(reasons(h))))
+                except Exception:
+                    pass
+
             def run():
                 while not self.done.is_set():
                     if self.active:
-                        try:
-                            self.rows.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
-                                              nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM), int(reasons(h))))
-                        except Exception:
-                            pass
+                        sample()
                     self.done.wait(0.002)
+            self.sample_now = sample
 
             self.thread = threading.Thread(target=run, daemon=True)
             self.thread.start()
@@ -224,12 +228,17 @@ class ClockSampler:
         if self.thread is not None:
             self.done.set()
             self.thread.join(timeout=5)
+            source = "nvml, 2 ms, timed region only"
+            if not self.rows:
+                # a region shorter than the sampling interval: one sample just after it
+                self.sample_now()
+                source = "nvml, one sample at the end of a region shorter than 2 ms"
             if not self.rows:
                 return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "source": "nvml"}
             names = sorted({n for _, _, r in self.rows for n, bit in self.REASONS if r & bit})
             return {"sm_mhz": float(np.median([r[0] for r in self.rows])),
                     "sm_max_mhz": float(max(r[1] for r in self.rows)), "reasons": names,
-                    "samples": len(self.rows), "source": "nvml, 2 ms, timed region only"}
+                    "samples": len(self.rows), "source": source}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
