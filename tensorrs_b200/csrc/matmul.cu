@@ -1158,7 +1158,14 @@ bool pick_unfold_rows(const ColsDev& d, int es, int* V, bool* tma, UnfoldRows* u
   return true;
 }
 
-// Shared memory a stride-1 fold tile may take (four CTAs per SM).
+// Widest strip of image columns a stride-1 fold tile takes: narrower strips
+// let taller bands fit (fewer window rows staged twice) and more CTAs share an
+// SM, for a few more windows staged twice at the strips' edges.
+#ifndef TRS_FOLD_XS_MAX
+#define TRS_FOLD_XS_MAX 32
+#endif
+
+// Shared memory a stride-1 fold tile may take.
 #ifndef TRS_FOLD_S1_BUDGET
 #define TRS_FOLD_S1_BUDGET (52 * 1024)
 #endif
@@ -1182,7 +1189,11 @@ bool pick_fold_s1(const ColsDev& d, int es, FoldS1* f) {
   int64_t m = 1;
   while ((m * kk * es) % 16 != 0) ++m;
   if (m * kk > 256 || d.kw > 128 || m > d.C) return false;
-  const int64_t xs_opts[2] = {d.W + d.kw - 1 <= 256 ? d.W : 256 - (d.kw - 1), d.W < 64 ? d.W : 64};
+  // strips of at most TRS_FOLD_XS_MAX columns, of equal widths
+  const int64_t xs_cap = d.W + d.kw - 1 <= 256 ? d.W : 256 - (d.kw - 1);
+  const int64_t xs_max = xs_cap < TRS_FOLD_XS_MAX ? xs_cap : TRS_FOLD_XS_MAX;
+  const int64_t n_strips = (d.W + xs_max - 1) / xs_max;
+  const int64_t xs_opts[2] = {(d.W + n_strips - 1) / n_strips, d.W < 64 ? d.W : 64};
   for (const int64_t XS : xs_opts) {
     for (int ty = 8; ty >= 1; ty /= 2) {
       if (ty > 1 && ty >= 2 * d.H) continue;
